@@ -1,0 +1,192 @@
+/*
+ * taccel_b200.h -- C ABI of the B200 execution engine for taccel programs.
+ *
+ * The engine replaces the NumPy execute loop of the taccel golden simulator
+ * (SayatAbdikul/LLM_accelerator).  Every entry point takes plain pointers and
+ * sizes; the Python class llm_accelerator_b200.B200Simulator binds them with
+ * ctypes and keeps the reference simulator's interface.  Each declaration
+ * names the reference interface it stands in for (paths are inside
+ * software/taccel of the reference repository).
+ *
+ * Status codes: 0 is success; codes 1..7 mirror the reference simulator's
+ * exception classes (golden_model/simulator.py:53-65, golden_model/memory.py:11-26)
+ * and come with a filled tac_fault record.
+ */
+#ifndef TACCEL_B200_H
+#define TACCEL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum tac_status {
+  TAC_OK = 0,
+  TAC_E_SIMULATOR = 1,       /* SimulatorError: PC past the end, DRAM capacity       */
+  TAC_E_ILLEGAL_OPCODE = 2,  /* IllegalOpcodeError: word does not decode            */
+  TAC_E_ILLEGAL_BUFFER = 3,  /* IllegalBufferError                                  */
+  TAC_E_CONFIG = 4,          /* ConfigError                                         */
+  TAC_E_SRAM_ACCESS = 5,     /* SRAMAccessError                                     */
+  TAC_E_DRAM_ACCESS = 6,     /* DRAMAccessError                                     */
+  TAC_E_VALUE = 7,           /* ValueError from the reference's SRAM helpers        */
+  TAC_E_ARGUMENT = 16,       /* bad argument to this API                            */
+  TAC_E_UNSUPPORTED = 17,    /* program form this engine rejects (self-modifying code,
+                                unaligned DRAM address, split SET_ADDR pair)        */
+  TAC_E_SHARED_WRITE = 18,   /* a STORE may write the shared read-only DRAM region  */
+  TAC_E_CUDA = 19,           /* CUDA runtime error                                  */
+  TAC_E_DEVICE = 20,         /* a device-side check failed (bounds, barrier timeout) */
+  TAC_E_RECOMPILE = 21       /* runtime words fall outside the compiled ranges       */
+};
+
+/* Fault record: which instruction faulted and the fields the reference's
+ * exception carries (pc/raw bytes, buffer id/offset/limit, DRAM address). */
+typedef struct tac_fault {
+  int32_t status;
+  int32_t buf_id;
+  uint64_t pc;
+  uint64_t raw_word;
+  uint64_t addr;
+  int64_t offset;
+  int64_t limit;
+  char message[320];
+} tac_fault;
+
+/* Host-visible architectural registers that are fixed by the instruction
+ * stream (golden_model/state.py:43-56): address registers, tile
+ * configuration (0-based tile counts) and the attention context. */
+typedef struct tac_regs {
+  uint64_t addr_regs[4];
+  int32_t tile_valid;
+  uint32_t tile[3];
+  int32_t attn_valid;
+  uint32_t attn_qrb;
+  uint32_t attn_vkl;
+  uint32_t attn_mode;
+} tac_regs;
+
+/* A runtime-patched word.  kind 0: a SET_ADDR_LO/SET_ADDR_HI pair whose
+ * register value lies in [range_lo, range_hi); kind 1: a CONFIG_ATTN word.
+ * Mirrors RuntimePatchSite / RuntimeConfigAttnSite (assembler/assembler.py:127-160). */
+typedef struct tac_var_site {
+  uint32_t kind;
+  uint32_t addr_reg;
+  uint64_t lo_pc;
+  uint64_t hi_pc;
+  uint64_t range_lo;
+  uint64_t range_hi;
+} tac_var_site;
+
+/* Static facts about a compiled stream. */
+typedef struct tac_exec_info {
+  uint64_t executed;     /* instructions retired (the value Simulator.run returns) */
+  uint64_t final_pc;
+  int32_t halted;
+  int32_t faulted;       /* the stream faults after `executed` instructions */
+  uint64_t cycles;       /* analytic cycle count added (golden_model cycle model) */
+  uint64_t n_ops;
+  uint64_t n_levels;
+  uint64_t n_tasks;
+  uint64_t n_segments;
+  uint64_t arena_bytes;  /* per-sequence scratch the plan needs */
+  uint64_t n_slots;      /* renamed scale-register slots */
+  uint64_t n_var_words;  /* runtime words tac_run expects per sequence */
+  tac_regs final_regs;
+} tac_exec_info;
+
+typedef struct tac_engine tac_engine;
+typedef struct tac_program tac_program;
+
+/* Machine state for `batch` independent sequences on one GPU
+ * (golden_model/state.py:19-63 MachineState, one per sequence).  DRAM bytes
+ * [0, shared_bytes) are one read-only copy shared by all sequences;
+ * [shared_bytes, dram_bytes) are private to each sequence. */
+int tac_engine_create(int device, int batch, uint64_t dram_bytes, uint64_t shared_bytes,
+                      tac_engine** out);
+int tac_engine_destroy(tac_engine* e);
+int tac_engine_batch(const tac_engine* e);
+
+/* DRAM image upload / read-back (Simulator.load_bundle simulator.py:162-179
+ * and state.dram slicing as used by HostRunner._read_logits host_runner.py:66-76).
+ * seq = -1 writes every sequence.  Shared-region writes go to the one shared copy. */
+int tac_dram_write(tac_engine* e, int seq, uint64_t addr, const void* src, uint64_t len);
+int tac_dram_read(tac_engine* e, int seq, uint64_t addr, void* dst, uint64_t len);
+/* SRAM access (golden_model/memory.py:337-366 read_bytes / write_bytes). */
+int tac_sram_write(tac_engine* e, int seq, int buf, uint64_t byte_off, const void* src, uint64_t len);
+int tac_sram_read(tac_engine* e, int seq, int buf, uint64_t byte_off, void* dst, uint64_t len);
+/* The 16 FP16 scale registers (state.scale_regs), as raw FP16 bits. */
+int tac_sregs_write(tac_engine* e, int seq, const uint16_t* regs16);
+int tac_sregs_read(tac_engine* e, int seq, uint16_t* regs16);
+
+/* Decode and plan a stream (the work Simulator.step/_execute repeat for
+ * every instruction, simulator.py:200-206,299-322,476-565, done once).
+ * insn_bytes: the big-endian instruction region, n_insns words, fetched from
+ * entry_pc on; at most max_insns retire.  init_regs: registers at entry;
+ * sregs_reset != 0 means the scale registers start at zero (run_program's
+ * volatile reset, simulator.py:147-160), else they keep their values.
+ * sites: words that change between runs.  Needs no GPU.
+ * A stream that faults still compiles: info->faulted is set, the plan
+ * covers the instructions before the fault and *fault describes it. */
+int tac_compile(int batch, uint64_t dram_bytes, uint64_t shared_bytes,
+                const uint8_t* insn_bytes, uint64_t n_insns, uint64_t entry_pc,
+                uint64_t max_insns, const tac_regs* init_regs, int sregs_reset,
+                const tac_var_site* sites, int n_sites, tac_program** out,
+                tac_exec_info* info, tac_fault* fault);
+int tac_program_destroy(tac_program* p);
+int tac_program_info(const tac_program* p, tac_exec_info* info, tac_fault* fault);
+
+/* Plan introspection (profiling and tests): copy out the device ops
+ * (sizeof = tac_program_record_size(0)), gather segments (record size 1),
+ * tasks (record size 2) and per-level task offsets (uint32, n_levels + 1). */
+uint64_t tac_program_record_size(int which);
+int tac_program_dump(const tac_program* p, void* ops, void* segments, void* tasks,
+                     uint32_t* level_offsets);
+
+/* Run a compiled stream on every sequence (Simulator.run_program
+ * simulator.py:181-198; batched).  var_words: [batch][n_var_words] current
+ * values of the runtime words in site order (a pair contributes its LO then
+ * its HI word).  stream: a cudaStream_t or NULL.  tac_run_async returns
+ * after enqueueing; tac_run waits and reports device-side faults. */
+int tac_run_async(tac_engine* e, tac_program* p, const uint64_t* var_words, void* stream,
+                  tac_fault* fault);
+int tac_run(tac_engine* e, tac_program* p, const uint64_t* var_words, tac_fault* fault);
+int tac_check_device_status(tac_engine* e, tac_fault* fault);
+
+/* Greedy decode helpers for batched generation (HostRunner._greedy_token,
+ * host_runner.py:97-101): argmax over `count` FP16 values at DRAM address
+ * `addr` of every sequence, written to out_tokens (device int32[batch]).
+ * Ties resolve to the lowest index, like numpy.argmax. */
+int tac_argmax_f16(tac_engine* e, uint64_t addr, uint64_t count, int32_t* out_tokens_dev,
+                   void* stream);
+
+/* Per-sequence device pointer arithmetic for zero-copy callers. */
+int tac_engine_layout(const tac_engine* e, void** seq_base, uint64_t* seq_stride,
+                      void** shared_base);
+
+/* ---- Stand-alone kernels ------------------------------------------------ */
+
+/* INT8 GEMM with the REQUANT_PC epilogue: out[M,N] int8 =
+ * clip(rint(float(A[M,K] @ B[K,N]) * float(scale[n]))), A K-major (row-major),
+ * B row-major [K,N], scale FP16 bits.  The MATMUL + REQUANT_PC instruction
+ * pair (golden_model/systolic.py:31-71, simulator.py:661-688) fused into one
+ * tcgen05 kernel.  All pointers are device pointers. */
+int tac_gemm_i8_requant_pc(const int8_t* A, const int8_t* B, const uint16_t* scale_f16,
+                           int8_t* out, int M, int N, int K, void* stream);
+
+/* INT8 GEMM with an integer requant epilogue: out = clip((acc * mult[n] +
+ * 2^(shift[n]-1)) >> shift[n]) computed in int64, shift 8..15.  No reference
+ * counterpart (the reference requant is FP16-scale based); parity unpinned. */
+int tac_gemm_i8_requant_shift(const int8_t* A, const int8_t* B, const int32_t* mult,
+                              const int32_t* shift, int8_t* out, int M, int N, int K,
+                              void* stream);
+
+/* Raw INT8 GEMM with int32 output C[M,N] = A @ B (MATMUL, systolic.py:31-71). */
+int tac_gemm_i8_i32(const int8_t* A, const int8_t* B, int32_t* C, int M, int N, int K,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TACCEL_B200_H */

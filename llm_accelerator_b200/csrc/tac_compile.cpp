@@ -1,0 +1,1215 @@
+// Host compiler: taccel instruction stream -> renamed dataflow plan.
+//
+// Semantics of each instruction (operands, bounds checks and their order,
+// exceptions, cycle costs) follow the reference golden model:
+//   fetch/run loop ........ golden_model/simulator.py:181-206,299-322
+//   dispatch .............. golden_model/simulator.py:476-565
+//   registers ............. golden_model/simulator.py:567-627
+//   MATMUL ................ golden_model/systolic.py:31-71
+//   LOAD/STORE/BUF_COPY ... golden_model/dma.py:27-97
+//   SRAM bounds ........... golden_model/memory.py:29-366
+//   INT8 / FP ops ......... golden_model/simulator.py:629-1140, golden_model/sfu.py:149-443
+// The compiler does not compute data; it records, per instruction, which
+// physical bytes hold each operand and emits a device op that the executor
+// (tac_exec.cu) runs.  See tac_plan.h for the physical layout.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <new>
+#include <string>
+
+#include "tac_program.h"
+
+namespace tac {
+namespace {
+
+constexpr uint64_t kNone = ~0ull;
+
+enum PhysClass { PC_SHARED, PC_HOME_SRAM, PC_HOME_RW, PC_ARENA };
+
+struct AddrReg {
+  int kind = 0;          // 0 static, 1 runtime parameter, 2 partly known (unusable)
+  uint64_t value = 0;    // static value (kind 0) or the known halves (kind 2)
+  uint32_t known = 3;    // kind 2: bit 0 = bits [27:0] known, bit 1 = bits [55:28] known
+  int param = -1;
+  uint64_t lo = 0, hi = 0;  // runtime value range
+};
+
+struct Access {
+  std::vector<std::pair<uint64_t, uint64_t>> reads;   // (phys, units)
+  std::vector<std::pair<uint64_t, uint64_t>> writes;  // (phys, units)
+  std::vector<uint32_t> slot_reads;
+  std::vector<uint32_t> slot_writes;
+  bool sreg_home_read = false;
+  bool sreg_home_write = false;
+};
+
+class Compiler {
+ public:
+  Compiler(tac_program* prog, const uint8_t* words, uint64_t n_insns, uint64_t entry_pc,
+           uint64_t max_insns, const tac_regs* init, int sregs_reset, const tac_var_site* sites,
+           int n_sites)
+      : P(prog), words_(words), n_insns_(n_insns), entry_(entry_pc), max_insns_(max_insns),
+        sites_(sites), n_sites_(n_sites) {
+    dram_bytes_ = P->dram_bytes;
+    shared_bytes_ = P->shared_bytes;
+    ro_units_ = shared_bytes_ / kUnit;
+    dram_units_ = (dram_bytes_ + kUnit - 1) / kUnit;
+    rw_units_ = dram_units_ > ro_units_ ? dram_units_ - ro_units_ : 0;
+    rw_base_ = kSramUnits;
+    arena_base_ = rw_base_ + rw_units_;
+    for (int r = 0; r < 4; ++r) areg_[r].value = init ? init->addr_regs[r] : 0;
+    tile_valid_ = init && init->tile_valid;
+    if (tile_valid_) for (int i = 0; i < 3; ++i) tile_[i] = init->tile[i];
+    if (init && init->attn_valid) {
+      attn_kind_ = 1;
+      attn_qrb_ = init->attn_qrb;
+      attn_vkl_ = init->attn_vkl;
+      attn_mode_ = init->attn_mode;
+    }
+    for (int r = 0; r < 16; ++r) sreg_[r] = sregs_reset ? (kSregConst | 0u) : uint32_t(r);
+  }
+
+  int compile();
+
+ private:
+  // ---- layout helpers ------------------------------------------------------
+  PhysClass cls(uint64_t p) const {
+    if (p & kSharedBit) return PC_SHARED;
+    if (p < rw_base_) return PC_HOME_SRAM;
+    if (p < arena_base_) return PC_HOME_RW;
+    return PC_ARENA;
+  }
+  uint64_t rw_home(uint64_t rw_index) const { return rw_base_ + rw_index; }
+
+  uint64_t alloc(uint64_t units) {
+    uint64_t rounded = (units + 15) & ~15ull;  // 256-byte aligned extents
+    uint64_t p = arena_base_ + arena_top_;
+    arena_top_ += rounded;
+    arena_lvl_.resize(arena_top_, 0);
+    return p;
+  }
+
+  // ---- faults ----------------------------------------------------------------
+  int fault(int status, const std::string& msg) {
+    tac_fault& f = P->fault;
+    f.status = status;
+    f.pc = pc_;
+    f.raw_word = word_;
+    std::snprintf(f.message, sizeof(f.message), "%s", msg.c_str());
+    return status;
+  }
+  int sram_fault(int buf, uint64_t off) {
+    P->fault.buf_id = buf;
+    P->fault.offset = static_cast<int64_t>(off);
+    P->fault.limit = static_cast<int64_t>(kBufUnits[buf < 3 ? buf : 0]) - 1;
+    return fault(TAC_E_SRAM_ACCESS, "SRAM access out of bounds");
+  }
+  int dram_fault(uint64_t addr) {
+    P->fault.addr = addr;
+    return fault(TAC_E_DRAM_ACCESS, "DRAM access out of bounds");
+  }
+  int ibuf_fault(int buf) {
+    P->fault.buf_id = buf;
+    return fault(TAC_E_ILLEGAL_BUFFER, "Illegal buffer ID: " + std::to_string(buf));
+  }
+  int config_fault(const std::string& msg) { return fault(TAC_E_CONFIG, msg); }
+  int value_fault(const std::string& msg) { return fault(TAC_E_VALUE, msg); }
+  int unsupported(const std::string& msg) { return fault(TAC_E_UNSUPPORTED, msg); }
+
+  // End-of-range SRAM check shared by every tile / byte helper.
+  bool sram_span_ok(int buf, uint64_t off, uint64_t nbytes) const {
+    return off * kUnit + nbytes <= uint64_t(kBufUnits[buf]) * kUnit;
+  }
+
+  // ---- dependency levels ---------------------------------------------------------
+  int32_t level_for(const Access& a) {
+    int32_t L = 0;
+    for (auto& r : a.reads) {
+      uint64_t p = r.first;
+      switch (cls(p)) {
+        case PC_ARENA:
+          for (uint64_t i = 0; i < r.second; ++i) L = std::max(L, arena_lvl_[p - arena_base_ + i]);
+          break;
+        case PC_HOME_RW:
+          for (uint64_t i = 0; i < r.second; ++i) L = std::max(L, rw_wl_[p - rw_base_ + i]);
+          break;
+        default:
+          break;  // shared: never written; SRAM home: written only by the final materialise
+      }
+    }
+    for (auto& w : a.writes) {
+      uint64_t p = w.first;
+      switch (cls(p)) {
+        case PC_HOME_RW:
+          for (uint64_t i = 0; i < w.second; ++i) {
+            L = std::max(L, rw_wl_[p - rw_base_ + i]);
+            L = std::max(L, rw_rl_[p - rw_base_ + i]);
+          }
+          break;
+        case PC_HOME_SRAM:
+          for (uint64_t i = 0; i < w.second; ++i) L = std::max(L, home_rl_[p + i]);
+          break;
+        default:
+          break;  // arena extents are fresh
+      }
+    }
+    for (uint32_t s : a.slot_reads) L = std::max(L, slot_lvl_[s]);
+    if (a.sreg_home_write) L = std::max(L, sreg_home_rl_);
+    return L + 1;
+  }
+
+  void commit(const Access& a, int32_t L) {
+    for (auto& r : a.reads) {
+      uint64_t p = r.first;
+      PhysClass c = cls(p);
+      if (c == PC_HOME_RW) {
+        for (uint64_t i = 0; i < r.second; ++i) {
+          int32_t& x = rw_rl_[p - rw_base_ + i];
+          x = std::max(x, L);
+        }
+      } else if (c == PC_HOME_SRAM) {
+        for (uint64_t i = 0; i < r.second; ++i) home_rl_[p + i] = std::max(home_rl_[p + i], L);
+      }
+    }
+    for (auto& w : a.writes) {
+      uint64_t p = w.first;
+      PhysClass c = cls(p);
+      if (c == PC_ARENA) {
+        for (uint64_t i = 0; i < w.second; ++i) arena_lvl_[p - arena_base_ + i] = L;
+      } else if (c == PC_HOME_RW) {
+        for (uint64_t i = 0; i < w.second; ++i) rw_wl_[p - rw_base_ + i] = L;
+      }
+    }
+    for (uint32_t s : a.slot_writes) slot_lvl_[s] = L;
+    if (a.sreg_home_read) sreg_home_rl_ = std::max(sreg_home_rl_, L);
+  }
+
+  uint32_t emit(DevOp op, const Access& a) {
+    int32_t L = level_for(a);
+    commit(a, L);
+    op.level = static_cast<uint32_t>(L);
+    op.pc = static_cast<uint32_t>(pc_);
+    P->ops.push_back(op);
+    return static_cast<uint32_t>(P->ops.size() - 1);
+  }
+
+  static DevOp blank(uint16_t kind) {
+    DevOp op;
+    std::memset(&op, 0, sizeof(op));
+    op.kind = kind;
+    op.param = -1;
+    return op;
+  }
+
+  // ---- register operands ------------------------------------------------------
+  uint32_t new_slot() {
+    uint32_t s = kSregSlotBase + n_slots_++;
+    slot_lvl_.resize(s + 1, 0);
+    return s;
+  }
+  void read_sreg(Access& a, uint32_t enc) {
+    if (enc & kSregConst) return;
+    if (enc < kSregSlotBase) a.sreg_home_read = true;
+    else a.slot_reads.push_back(enc);
+  }
+
+  // ---- logical SRAM -> physical operand --------------------------------------------
+  static uint32_t unit_of(int buf, uint64_t off) { return kBufUnitBase[buf] + uint32_t(off); }
+
+  bool contiguous(const uint64_t* map, uint64_t n) const {
+    PhysClass c0 = cls(map[0]);
+    for (uint64_t i = 1; i < n; ++i)
+      if (map[i] != map[0] + i || cls(map[i]) != c0) return false;
+    return true;
+  }
+
+  // Gathers scattered physical units into one fresh arena extent.
+  uint64_t gather(const uint64_t* map, uint64_t n) {
+    uint64_t dst = alloc(n);
+    DevOp op = blank(K_GATHER);
+    op.seg0 = static_cast<uint32_t>(P->segs.size());
+    Access acc;
+    uint64_t i = 0;
+    while (i < n) {
+      uint64_t j = i + 1;
+      while (j < n && map[j] == map[i] + (j - i) && cls(map[j]) == cls(map[i])) ++j;
+      P->segs.push_back(Segment{map[i], dst + i, j - i});
+      acc.reads.push_back({map[i], j - i});
+      i = j;
+    }
+    op.nseg = static_cast<uint32_t>(P->segs.size() - op.seg0);
+    op.d = dst;
+    op.N = static_cast<uint32_t>(n);
+    acc.writes.push_back({dst, n});
+    emit(op, acc);
+    return dst;
+  }
+
+  // Physical start of a contiguous copy of logical SRAM units [u0, u0+n).
+  uint64_t src(uint32_t u0, uint64_t nbytes, Access& acc) {
+    uint64_t n = (nbytes + kUnit - 1) / kUnit;
+    if (n == 0) n = 1;
+    uint64_t* m = &sram_[u0];
+    if (!contiguous(m, n)) {
+      uint64_t g = gather(m, n);
+      for (uint64_t i = 0; i < n; ++i) m[i] = g + i;
+    }
+    acc.reads.push_back({m[0], n});
+    return m[0];
+  }
+
+  // Fresh destination extent for logical SRAM units [u0, u0+n).
+  uint64_t dst(uint32_t u0, uint64_t nbytes, Access& acc) {
+    uint64_t n = (nbytes + kUnit - 1) / kUnit;
+    uint64_t p = alloc(n);
+    for (uint64_t i = 0; i < n; ++i) sram_[u0 + i] = p + i;
+    acc.writes.push_back({p, n});
+    return p;
+  }
+
+  // ---- DRAM value tracking ------------------------------------------------------
+  // Flushes arena-resident values of writable DRAM units [i0, i1) (rw indices)
+  // to their home location so that a runtime-addressed access sees them.
+  void flush_rw(uint64_t i0, uint64_t i1) {
+    std::vector<uint64_t> idx;
+    for (uint64_t i = i0; i < i1; ++i)
+      if (shadow_[i] != rw_home(i)) idx.push_back(i);
+    if (idx.empty()) return;
+    DevOp op = blank(K_GATHER);
+    op.seg0 = static_cast<uint32_t>(P->segs.size());
+    Access acc;
+    size_t k = 0;
+    while (k < idx.size()) {
+      size_t j = k + 1;
+      while (j < idx.size() && idx[j] == idx[k] + (j - k) &&
+             shadow_[idx[j]] == shadow_[idx[k]] + (j - k) &&
+             cls(shadow_[idx[j]]) == cls(shadow_[idx[k]]))
+        ++j;
+      uint64_t n = j - k;
+      P->segs.push_back(Segment{shadow_[idx[k]], rw_home(idx[k]), n});
+      acc.reads.push_back({shadow_[idx[k]], n});
+      acc.writes.push_back({rw_home(idx[k]), n});
+      k = j;
+    }
+    op.nseg = static_cast<uint32_t>(P->segs.size() - op.seg0);
+    emit(op, acc);
+    for (uint64_t i : idx) shadow_[i] = rw_home(i);
+  }
+
+  // Physical location of the current value of DRAM unit u.
+  uint64_t dram_phys(uint64_t u) const {
+    return u < ro_units_ ? (kSharedBit | u) : shadow_[u - ro_units_];
+  }
+
+  // ---- instruction handlers ------------------------------------------------------
+  int step(const Insn& x);
+  int h_load(const Insn& x);
+  int h_store(const Insn& x);
+  int h_buf_copy(const Insn& x);
+  int h_rtype(const Insn& x);
+  int h_set_scale(const Insn& x);
+  int h_config_attn(const Insn& x);
+  int attn_keys_check(uint32_t key_cols, DevOp& op);
+  int effective_address(const Insn& x, uint64_t nbytes, bool& dynamic, uint64_t& addr,
+                        uint64_t& lo, uint64_t& hi, int& param);
+  void finalize();
+  void build_tasks();
+
+  // ---- state ----------------------------------------------------------------------
+  tac_program* P;
+  const uint8_t* words_;
+  uint64_t n_insns_, entry_, max_insns_;
+  const tac_var_site* sites_;
+  int n_sites_;
+  uint64_t dram_bytes_ = 0, shared_bytes_ = 0, ro_units_ = 0, dram_units_ = 0, rw_units_ = 0;
+  uint64_t rw_base_ = 0, arena_base_ = 0, arena_top_ = 0;
+  std::vector<uint64_t> sram_, shadow_;
+  std::vector<int32_t> arena_lvl_, rw_wl_, rw_rl_, home_rl_, slot_lvl_;
+  int32_t sreg_home_rl_ = 0;
+  uint32_t sreg_[16];
+  uint32_t n_slots_ = 0;
+  AddrReg areg_[4];
+  bool tile_valid_ = false;
+  uint32_t tile_[3] = {0, 0, 0};
+  int attn_kind_ = 0;  // 0 unset, 1 static, 2 runtime parameter
+  uint32_t attn_qrb_ = 0, attn_vkl_ = 0, attn_mode_ = 0;
+  int attn_param_ = -1;
+  uint64_t pc_ = 0, word_ = 0;
+  uint64_t insn_region_bytes_ = 0;
+  uint64_t cycles_ = 0;
+  bool halted_ = false;
+  // var-site lookup: pc -> (site index, role 0 = lo / attn, 1 = hi)
+  std::map<uint64_t, std::pair<int, int>> var_pc_;
+};
+
+// ---------------------------------------------------------------------------------
+int Compiler::effective_address(const Insn& x, uint64_t nbytes, bool& dynamic, uint64_t& addr,
+                                uint64_t& lo, uint64_t& hi, int& param) {
+  const AddrReg& r = areg_[x.addr_reg];
+  uint64_t off = uint64_t(x.dram_off) * kUnit;
+  if (r.kind == 2) return unsupported("LOAD/STORE through a half-patched SET_ADDR pair");
+  if (r.kind == 0) {
+    dynamic = false;
+    addr = r.value + off;
+    if (addr + nbytes > dram_bytes_) return dram_fault(addr + nbytes);
+    if (nbytes && (addr % kUnit)) return unsupported("DRAM address not 16-byte aligned");
+    return 0;
+  }
+  dynamic = true;
+  param = r.param;
+  lo = r.lo + off;
+  hi = r.hi + off;  // exclusive bound on the start address
+  uint64_t last = hi + nbytes;
+  if (last > dram_bytes_) {
+    // Runtime addresses that overflow DRAM are caught by the run-time check and
+    // recompiled statically to raise the exact fault.
+    hi = dram_bytes_ >= nbytes ? dram_bytes_ - nbytes + 1 : 0;
+    if (hi < lo) hi = lo;
+  }
+  RtCheck c{};
+  c.kind = CHK_ADDR;
+  c.param = static_cast<uint32_t>(param);
+  c.pc = pc_;
+  c.dconst = static_cast<int64_t>(off);
+  c.lo = lo;
+  c.hi = hi;
+  c.nbytes = nbytes;
+  P->checks.push_back(c);
+  return 0;
+}
+
+int Compiler::h_load(const Insn& x) {                       // dma.py:27-44
+  uint64_t n = uint64_t(x.xfer_len) * kUnit;
+  bool dyn = false;
+  uint64_t addr = 0, lo = 0, hi = 0;
+  int param = -1;
+  if (int s = effective_address(x, n, dyn, addr, lo, hi, param)) return s;
+  // write_bytes: the start offset is valid by decode; the end must fit.
+  if (!sram_span_ok(x.buf_id, x.sram_off, n)) {
+    if (x.buf_id == BUF_ACCUM)
+      return value_fault("could not broadcast input array from shape (" + std::to_string(n) +
+                         ",) into shape (" +
+                         std::to_string(uint64_t(kBufUnits[BUF_ACCUM]) * kUnit - x.sram_off * kUnit) +
+                         ",)");
+    return sram_fault(x.buf_id, x.sram_off);
+  }
+  cycles_ += x.xfer_len;
+  if (n == 0) return 0;
+  uint32_t u0 = unit_of(x.buf_id, x.sram_off);
+  uint64_t nu = n / kUnit;
+  if (!dyn) {
+    uint64_t a0 = addr / kUnit;
+    std::vector<uint64_t> src(nu);
+    bool needs_copy = false;
+    for (uint64_t i = 0; i < nu; ++i) {
+      src[i] = dram_phys(a0 + i);
+      if (cls(src[i]) == PC_HOME_RW) needs_copy = true;
+    }
+    if (!needs_copy) {
+      for (uint64_t i = 0; i < nu; ++i) sram_[u0 + i] = src[i];  // alias, no device work
+      return 0;
+    }
+    uint64_t g = gather(src.data(), nu);
+    for (uint64_t i = 0; i < nu; ++i) sram_[u0 + i] = g + i;
+    return 0;
+  }
+  // Runtime address: copy into a fresh extent.
+  bool in_shared = hi + n <= shared_bytes_;
+  bool in_rw = lo >= shared_bytes_;
+  if (!in_shared && !in_rw) return unsupported("runtime-addressed LOAD straddles the shared DRAM region");
+  Access acc;
+  if (in_rw) {
+    uint64_t i0 = (lo - shared_bytes_) / kUnit;
+    uint64_t i1 = std::min<uint64_t>(rw_units_, (hi + n - shared_bytes_ + kUnit - 1) / kUnit);
+    flush_rw(i0, i1);
+    acc.reads.push_back({rw_home(i0), i1 - i0});
+  }
+  DevOp op = blank(K_DYN_LOAD);
+  op.param = param;
+  op.dconst = int64_t(x.dram_off) * kUnit;
+  op.nbytes = n;
+  op.d = dst(u0, n, acc);
+  emit(op, acc);
+  return 0;
+}
+
+int Compiler::h_store(const Insn& x) {                      // dma.py:47-64
+  uint64_t n = uint64_t(x.xfer_len) * kUnit;
+  if (!sram_span_ok(x.buf_id, x.sram_off, n)) return sram_fault(x.buf_id, x.sram_off);
+  bool dyn = false;
+  uint64_t addr = 0, lo = 0, hi = 0;
+  int param = -1;
+  if (int s = effective_address(x, n, dyn, addr, lo, hi, param)) return s;
+  uint64_t first = dyn ? lo : addr;
+  if (n > 0 && first < insn_region_bytes_)
+    return unsupported("STORE into the instruction region (self-modifying program)");
+  if (n > 0 && first < shared_bytes_)
+    return fault(TAC_E_SHARED_WRITE, "STORE may write the shared read-only DRAM region");
+  cycles_ += x.xfer_len;
+  if (n == 0) return 0;
+  uint32_t u0 = unit_of(x.buf_id, x.sram_off);
+  uint64_t nu = n / kUnit;
+  if (!dyn) {
+    uint64_t i0 = addr / kUnit - ro_units_;
+    for (uint64_t i = 0; i < nu; ++i) shadow_[i0 + i] = sram_[u0 + i];  // lazy: flushed at the end
+    return 0;
+  }
+  uint64_t i0 = (lo - shared_bytes_) / kUnit;
+  uint64_t i1 = std::min<uint64_t>(rw_units_, (hi + n - shared_bytes_ + kUnit - 1) / kUnit);
+  flush_rw(i0, i1);
+  Access acc;
+  DevOp op = blank(K_DYN_STORE);
+  op.a = src(u0, n, acc);
+  op.param = param;
+  op.dconst = int64_t(x.dram_off) * kUnit;
+  op.nbytes = n;
+  acc.writes.push_back({rw_home(i0), i1 - i0});
+  emit(op, acc);
+  return 0;
+}
+
+int Compiler::h_buf_copy(const Insn& x) {                   // dma.py:67-97
+  uint64_t n = uint64_t(x.length) * kUnit;
+  uint32_t su = unit_of(x.src_buf, x.src_off), du = unit_of(x.dst_buf_b, x.dst_off_b);
+  auto dst_fits = [&]() -> int {
+    if (sram_span_ok(x.dst_buf_b, x.dst_off_b, n)) return 0;
+    if (x.dst_buf_b == BUF_ACCUM)
+      return value_fault("could not broadcast input array from shape (" + std::to_string(n) +
+                         ",) into shape (" +
+                         std::to_string(uint64_t(kBufUnits[BUF_ACCUM]) * kUnit - x.dst_off_b * kUnit) +
+                         ",)");
+    return sram_fault(x.dst_buf_b, x.dst_off_b);
+  };
+  if (!x.transpose) {
+    if (!sram_span_ok(x.src_buf, x.src_off, n)) return sram_fault(x.src_buf, x.src_off);
+    if (int s = dst_fits()) return s;
+    std::vector<uint64_t> tmp(sram_.begin() + su, sram_.begin() + su + n / kUnit);
+    for (uint64_t i = 0; i < tmp.size(); ++i) sram_[du + i] = tmp[i];  // alias
+    cycles_ += x.length;
+    return 0;
+  }
+  uint64_t rows = uint64_t(x.src_rows) * 16;
+  if (rows == 0) return 0;
+  uint64_t cols = n / rows;
+  if (cols == 0) return 0;
+  if (!sram_span_ok(x.src_buf, x.src_off, n)) return sram_fault(x.src_buf, x.src_off);
+  if (rows * cols != n)
+    return value_fault("cannot reshape array of size " + std::to_string(n) + " into shape (" +
+                       std::to_string(rows) + "," + std::to_string(cols) + ")");
+  if (int s = dst_fits()) return s;
+  Access acc;
+  DevOp op = blank(K_TRANSPOSE);
+  op.M = static_cast<uint32_t>(rows);
+  op.N = static_cast<uint32_t>(cols);
+  op.a = src(su, n, acc);
+  op.d = dst(du, n, acc);
+  emit(op, acc);
+  cycles_ += x.length;
+  return 0;
+}
+
+int Compiler::h_set_scale(const Insn& x) {                  // simulator.py:605-617
+  if (x.src_mode == 0) {
+    sreg_[x.sreg] = kSregConst | x.imm16;
+    return 0;
+  }
+  int buf = x.src_mode == 1 ? BUF_ABUF : (x.src_mode == 2 ? BUF_WBUF : BUF_ACCUM);
+  if (x.imm16 >= kBufUnits[buf] || !sram_span_ok(buf, x.imm16, 2)) return sram_fault(buf, x.imm16);
+  Access acc;
+  DevOp op = blank(K_SREG_LOAD);
+  op.a = src(unit_of(buf, x.imm16), 2, acc);
+  op.out_slot = new_slot();
+  acc.slot_writes.push_back(op.out_slot);
+  emit(op, acc);
+  sreg_[x.sreg] = op.out_slot;
+  return 0;
+}
+
+int Compiler::h_config_attn(const Insn& x) {                // simulator.py:567-580
+  if (!tile_valid_) return config_fault("CONFIG_TILE not set");
+  auto it = var_pc_.find(pc_);
+  if (it != var_pc_.end()) {
+    int site = it->second.first;
+    RtCheck c{};
+    c.kind = CHK_ATTN_SET;
+    c.param = static_cast<uint32_t>(site);
+    c.pc = pc_;
+    P->checks.push_back(c);
+    attn_kind_ = 2;
+    attn_param_ = site;
+    return 0;
+  }
+  if (x.mode == 0) return config_fault("CONFIG_ATTN mode 0b00 is reserved");
+  if (x.vkl == 0) return config_fault("CONFIG_ATTN valid_kv_len must be > 0");
+  attn_kind_ = 1;
+  attn_qrb_ = x.qrb;
+  attn_vkl_ = x.vkl;
+  attn_mode_ = x.mode;
+  return 0;
+}
+
+// simulator.py:582-603 (_validate_attn_context_for_key_cols).
+int Compiler::attn_keys_check(uint32_t key_cols, DevOp& op) {
+  if (!tile_valid_) return config_fault("CONFIG_TILE not set");
+  if (attn_kind_ == 0) return config_fault("CONFIG_ATTN not set");
+  if (attn_kind_ == 2) {
+    RtCheck c{};
+    c.kind = CHK_ATTN_KEYS;
+    c.param = static_cast<uint32_t>(attn_param_);
+    c.pc = pc_;
+    c.lo = key_cols;
+    P->checks.push_back(c);
+    op.flags |= F_ATTN_DYN;
+    op.param = attn_param_;
+    return 0;
+  }
+  if (attn_mode_ == 0) return config_fault("CONFIG_ATTN mode 0b00 is reserved");
+  if (attn_vkl_ == 0) return config_fault("CONFIG_ATTN valid_kv_len must be > 0");
+  if ((attn_mode_ == 1 || attn_mode_ == 3) && key_cols < attn_vkl_)
+    return config_fault("CONFIG_ATTN valid_kv_len=" + std::to_string(attn_vkl_) +
+                        " exceeds softmax key columns " + std::to_string(key_cols));
+  if (attn_mode_ == 2 && key_cols != attn_vkl_)
+    return config_fault("CONFIG_ATTN pure-causal mode requires softmax key columns " +
+                        std::to_string(key_cols) + " to equal valid_kv_len=" +
+                        std::to_string(attn_vkl_));
+  op.attn_qrb = attn_qrb_;
+  op.attn_vkl = attn_vkl_;
+  op.attn_mode = attn_mode_;
+  return 0;
+}
+
+int Compiler::h_rtype(const Insn& x) {
+  const uint8_t o = x.op;
+  // Masked variants validate the attention context before their handler runs
+  // (simulator.py:521-525, 534-542, 556-560).
+  DevOp op = blank(0);
+  if (o == OP_MASKED_SOFTMAX || o == OP_MASKED_SOFTMAX_FP32 || o == OP_MASKED_SOFTMAX_ATTNV) {
+    if (!tile_valid_) return config_fault("CONFIG_TILE not set");
+    uint32_t keys = (o == OP_MASKED_SOFTMAX_ATTNV ? tile_[2] + 1 : tile_[1] + 1) * 16;
+    if (int s = attn_keys_check(keys, op)) return s;
+  }
+  if (!tile_valid_) return config_fault("CONFIG_TILE not set");
+  const uint64_t M = (tile_[0] + 1) * 16ull, N = (tile_[1] + 1) * 16ull, K = (tile_[2] + 1) * 16ull;
+  op.M = static_cast<uint32_t>(M);
+  op.N = static_cast<uint32_t>(N);
+  op.K = static_cast<uint32_t>(K);
+  const uint32_t s1 = unit_of(x.src1_buf, x.src1_off), s2 = unit_of(x.src2_buf, x.src2_off),
+                 d = unit_of(x.dst_buf, x.dst_off);
+  Access acc;
+
+  // Helpers mirroring memory.py read/write tile functions (ACCUM rules + end checks).
+  auto rd_i8 = [&](int buf, uint64_t off, uint64_t nbytes) -> int {
+    if (buf == BUF_ACCUM) return value_fault("Use read_int32_tile for ACCUM buffer");
+    if (!sram_span_ok(buf, off, nbytes)) return sram_fault(buf, off);
+    return 0;
+  };
+  auto wr_i8 = [&](int buf, uint64_t off, uint64_t nbytes) -> int {
+    if (buf == BUF_ACCUM) return value_fault("Use write_int32_tile for ACCUM buffer");
+    if (!sram_span_ok(buf, off, nbytes)) return sram_fault(buf, off);
+    return 0;
+  };
+  auto span = [&](int buf, uint64_t off, uint64_t nbytes) -> int {
+    if (!sram_span_ok(buf, off, nbytes)) return sram_fault(buf, off);
+    return 0;
+  };
+  auto need_accum_src1 = [&]() -> int {
+    if (x.src1_buf != BUF_ACCUM) return ibuf_fault(x.src1_buf);
+    if (x.src2_buf == BUF_ACCUM) return ibuf_fault(x.src2_buf);
+    if (x.dst_buf == BUF_ACCUM) return ibuf_fault(x.dst_buf);
+    return 0;
+  };
+#define TRY(e) do { if (int _s = (e)) return _s; } while (0)
+
+  switch (o) {
+    case OP_MATMUL: {                                        // systolic.py:31-71
+      TRY(rd_i8(x.src1_buf, x.src1_off, M * K));
+      TRY(rd_i8(x.src2_buf, x.src2_off, K * N));
+      if (x.flags & 1) TRY(span(x.dst_buf, x.dst_off, M * N * 4));
+      TRY(span(x.dst_buf, x.dst_off, M * N * 4));
+      op.kind = K_MATMUL;
+      op.a = src(s1, M * K, acc);
+      op.b = src(s2, K * N, acc);
+      if (x.flags & 1) {
+        op.flags |= F_ACCUMULATE;
+        op.c = src(d, M * N * 4, acc);
+      }
+      op.d = dst(d, M * N * 4, acc);
+      cycles_ += (M / 16) * (N / 16) * (K / 16) * 16;
+      break;
+    }
+    case OP_REQUANT: {                                       // simulator.py:629-659
+      TRY(span(x.src1_buf, x.src1_off, M * N * 4));
+      TRY(wr_i8(x.dst_buf, x.dst_off, M * N));
+      op.kind = K_REQUANT;
+      op.s[0] = sreg_[x.sreg];
+      read_sreg(acc, op.s[0]);
+      op.a = src(s1, M * N * 4, acc);
+      op.d = dst(d, M * N, acc);
+      cycles_ += M * N;
+      break;
+    }
+    case OP_REQUANT_PC: {                                    // simulator.py:661-688
+      TRY(need_accum_src1());
+      TRY(span(x.src1_buf, x.src1_off, M * N * 4));
+      TRY(span(x.src2_buf, x.src2_off, N * 2));
+      TRY(wr_i8(x.dst_buf, x.dst_off, M * N));
+      op.kind = K_REQUANT_PC;
+      op.a = src(s1, M * N * 4, acc);
+      op.b = src(s2, N * 2, acc);
+      op.d = dst(d, M * N, acc);
+      cycles_ += M * N;
+      break;
+    }
+    case OP_SCALE_MUL: {                                     // simulator.py:690-722
+      op.s[0] = sreg_[x.sreg];
+      if (x.src1_buf == BUF_ACCUM) {
+        TRY(span(x.src1_buf, x.src1_off, M * N * 4));
+        TRY(span(x.dst_buf, x.dst_off, M * N * 4));
+        op.kind = K_SCALE_MUL_I32;
+        read_sreg(acc, op.s[0]);
+        op.a = src(s1, M * N * 4, acc);
+        op.d = dst(d, M * N * 4, acc);
+      } else {
+        TRY(rd_i8(x.src1_buf, x.src1_off, M * N));
+        TRY(wr_i8(x.dst_buf, x.dst_off, M * N));
+        op.kind = K_SCALE_MUL_I8;
+        read_sreg(acc, op.s[0]);
+        op.a = src(s1, M * N, acc);
+        op.d = dst(d, M * N, acc);
+      }
+      cycles_ += M * N;
+      break;
+    }
+    case OP_VADD: {                                          // simulator.py:724-760
+      if (x.src1_buf == BUF_ABUF) {
+        TRY(rd_i8(x.src1_buf, x.src1_off, M * N));
+        TRY(rd_i8(x.src2_buf, x.src2_off, M * N));
+        TRY(wr_i8(x.dst_buf, x.dst_off, M * N));
+        op.kind = K_VADD_I8;
+        op.a = src(s1, M * N, acc);
+        op.b = src(s2, M * N, acc);
+        op.d = dst(d, M * N, acc);
+      } else if (x.src1_buf == BUF_ACCUM) {
+        TRY(span(x.src1_buf, x.src1_off, M * N * 4));
+        TRY(span(x.src2_buf, x.src2_off, N * 4));
+        TRY(span(x.dst_buf, x.dst_off, M * N * 4));
+        op.kind = K_VADD_I32;
+        op.a = src(s1, M * N * 4, acc);
+        op.b = src(s2, N * 4, acc);
+        op.d = dst(d, M * N * 4, acc);
+      } else {
+        return ibuf_fault(x.src1_buf);
+      }
+      cycles_ += M * N;
+      break;
+    }
+    case OP_DEQUANT_ADD: {                                   // simulator.py:762-788
+      TRY(need_accum_src1());
+      if (x.sreg >= 15) return config_fault("DEQUANT_ADD sreg+1 out of range");
+      TRY(span(x.src1_buf, x.src1_off, M * N * 4));
+      TRY(rd_i8(x.src2_buf, x.src2_off, M * N));
+      TRY(wr_i8(x.dst_buf, x.dst_off, M * N));
+      op.kind = K_DEQUANT_ADD;
+      op.s[0] = sreg_[x.sreg];
+      op.s[1] = sreg_[x.sreg + 1];
+      read_sreg(acc, op.s[0]);
+      read_sreg(acc, op.s[1]);
+      op.a = src(s1, M * N * 4, acc);
+      op.b = src(s2, M * N, acc);
+      op.d = dst(d, M * N, acc);
+      cycles_ += M * N;
+      break;
+    }
+    case OP_DEQUANT_ACCUM_FP32:                              // simulator.py:808-833
+    case OP_DEQUANT_ACCUM_FP32_SCALED: {                     // simulator.py:1043-1086
+      TRY(need_accum_src1());
+      const uint64_t vec = (o == OP_DEQUANT_ACCUM_FP32 ? N : 2 * N) * 2;
+      TRY(span(x.src1_buf, x.src1_off, M * N * 4));
+      TRY(span(x.src2_buf, x.src2_off, vec));
+      TRY(span(x.dst_buf, x.dst_off, M * N * 2));
+      op.kind = o == OP_DEQUANT_ACCUM_FP32 ? K_DEQUANT_ACCUM : K_DEQUANT_SCALED;
+      if (o == OP_DEQUANT_ACCUM_FP32_SCALED) {
+        op.s[0] = sreg_[x.sreg];
+        read_sreg(acc, op.s[0]);
+      }
+      op.a = src(s1, M * N * 4, acc);
+      op.b = src(s2, vec, acc);
+      op.d = dst(d, M * N * 2, acc);
+      cycles_ += M * N;
+      break;
+    }
+    case OP_QUANT_FP32_INT8: {                               // simulator.py:835-867
+      if (x.src1_buf == BUF_ACCUM) return ibuf_fault(x.src1_buf);
+      if (x.dst_buf == BUF_ACCUM) return ibuf_fault(x.dst_buf);
+      TRY(span(x.src1_buf, x.src1_off, M * N * 2));
+      TRY(span(x.dst_buf, x.dst_off, M * N));
+      op.kind = K_QUANT;
+      op.s[0] = sreg_[x.sreg];
+      read_sreg(acc, op.s[0]);
+      op.a = src(s1, M * N * 2, acc);
+      op.d = dst(d, M * N, acc);
+      cycles_ += M * N;
+      break;
+    }
+    case OP_VADD_FP32:                                       // simulator.py:869-891
+    case OP_LAYERNORM_FP32: {                                // simulator.py:893-934
+      if (x.src1_buf == BUF_ACCUM || x.src2_buf == BUF_ACCUM) return ibuf_fault(BUF_ACCUM);
+      if (x.dst_buf == BUF_ACCUM) return ibuf_fault(x.dst_buf);
+      const uint64_t b_bytes = o == OP_VADD_FP32 ? M * N * 2 : 2 * N * 2;
+      TRY(span(x.src1_buf, x.src1_off, M * N * 2));
+      TRY(span(x.src2_buf, x.src2_off, b_bytes));
+      TRY(span(x.dst_buf, x.dst_off, M * N * 2));
+      op.kind = o == OP_VADD_FP32 ? K_VADD_F16 : K_LAYERNORM_F16;
+      op.a = src(s1, M * N * 2, acc);
+      op.b = src(s2, b_bytes, acc);
+      op.d = dst(d, M * N * 2, acc);
+      cycles_ += M * N;
+      break;
+    }
+    case OP_GELU_FP32:                                       // simulator.py:936-962
+    case OP_SOFTMAX_FP32:                                    // simulator.py:964-988
+    case OP_MASKED_SOFTMAX_FP32: {                           // simulator.py:990-1037
+      if (x.src1_buf == BUF_ACCUM) return ibuf_fault(x.src1_buf);
+      if (x.dst_buf == BUF_ACCUM) return ibuf_fault(x.dst_buf);
+      TRY(span(x.src1_buf, x.src1_off, M * N * 2));
+      TRY(span(x.dst_buf, x.dst_off, M * N * 2));
+      op.kind = o == OP_GELU_FP32 ? K_GELU_F16
+                                  : (o == OP_SOFTMAX_FP32 ? K_SOFTMAX_F16 : K_MASKED_SOFTMAX_F16);
+      op.a = src(s1, M * N * 2, acc);
+      op.d = dst(d, M * N * 2, acc);
+      cycles_ += M * N;
+      break;
+    }
+    case OP_MAX_ABS_REDUCE_FP32: {                           // simulator.py:1088-1140
+      if (x.src1_buf == BUF_ACCUM) return ibuf_fault(x.src1_buf);
+      if (x.sreg >= 15) return config_fault("MAX_ABS_REDUCE_FP32 sreg+1 out of range (must be 0..14)");
+      TRY(span(x.src1_buf, x.src1_off, M * N * 2));
+      op.kind = K_MAX_ABS;
+      op.a = src(s1, M * N * 2, acc);
+      op.out_slot = new_slot();
+      new_slot();
+      acc.slot_writes.push_back(op.out_slot);
+      acc.slot_writes.push_back(op.out_slot + 1);
+      sreg_[x.sreg] = op.out_slot;
+      sreg_[x.sreg + 1] = op.out_slot + 1;
+      cycles_ += M * N;
+      break;
+    }
+    case OP_LAYERNORM: {                                     // sfu.py:149-190
+      if (x.sreg >= 15) return config_fault("SFU sreg+1 out of range");
+      TRY(rd_i8(x.src1_buf, x.src1_off, M * N));
+      TRY(span(x.src2_buf, x.src2_off, N * 4));
+      TRY(wr_i8(x.dst_buf, x.dst_off, M * N));
+      op.kind = K_LN_I8;
+      op.s[0] = sreg_[x.sreg];
+      op.s[1] = sreg_[x.sreg + 1];
+      read_sreg(acc, op.s[0]);
+      read_sreg(acc, op.s[1]);
+      op.a = src(s1, M * N, acc);
+      op.b = src(s2, N * 4, acc);
+      op.d = dst(d, M * N, acc);
+      cycles_ += M * N * 2;
+      break;
+    }
+    case OP_SOFTMAX:                                         // sfu.py:193-235
+    case OP_MASKED_SOFTMAX:                                  // sfu.py:238-272
+    case OP_GELU: {                                          // sfu.py:275-320
+      if (x.sreg >= 15) return config_fault("SFU sreg+1 out of range");
+      uint64_t in_bytes = M * N;
+      if (x.src1_buf == BUF_ACCUM) {
+        op.flags |= F_SRC_I32;
+        in_bytes = M * N * 4;
+        TRY(span(BUF_ACCUM, x.src1_off, in_bytes));
+      } else {
+        TRY(rd_i8(x.src1_buf, x.src1_off, in_bytes));
+      }
+      TRY(wr_i8(x.dst_buf, x.dst_off, M * N));
+      op.kind = o == OP_SOFTMAX ? K_SOFTMAX_I8 : (o == OP_GELU ? K_GELU_I8 : K_MASKED_SOFTMAX_I8);
+      op.s[0] = sreg_[x.sreg];
+      op.s[1] = sreg_[x.sreg + 1];
+      read_sreg(acc, op.s[0]);
+      read_sreg(acc, op.s[1]);
+      op.a = src(s1, in_bytes, acc);
+      op.d = dst(d, M * N, acc);
+      cycles_ += M * N * 2;
+      break;
+    }
+    case OP_SOFTMAX_ATTNV:                                   // sfu.py:323-381
+    case OP_MASKED_SOFTMAX_ATTNV: {                          // sfu.py:384-443
+      TRY(need_accum_src1());
+      if (x.sreg >= 13) return config_fault("SFU sreg+3 out of range");
+      TRY(span(BUF_ACCUM, x.src1_off, M * K * 4));
+      TRY(rd_i8(x.src2_buf, x.src2_off, K * N));
+      TRY(wr_i8(x.dst_buf, x.dst_off, M * N));
+      op.kind = o == OP_SOFTMAX_ATTNV ? K_SOFTMAX_ATTNV : K_MASKED_SOFTMAX_ATTNV;
+      for (int i = 0; i < 4; ++i) {
+        op.s[i] = sreg_[x.sreg + i];
+        read_sreg(acc, op.s[i]);
+      }
+      op.a = src(s1, M * K * 4, acc);
+      op.b = src(s2, K * N, acc);
+      op.d = dst(d, M * N, acc);
+      cycles_ += M * K * 2 + (M / 16) * (N / 16) * (K / 16) * 16 + M * N;
+      break;
+    }
+    default:
+      return unsupported("unhandled opcode");
+  }
+#undef TRY
+  emit(op, acc);
+  return 0;
+}
+
+int Compiler::step(const Insn& x) {
+  switch (x.op) {
+    case OP_NOP:
+    case OP_SYNC:
+      cycles_ += 1;
+      return 0;
+    case OP_HALT:
+      halted_ = true;
+      return 0;
+    case OP_CONFIG_TILE:
+      tile_valid_ = true;
+      tile_[0] = x.tm;
+      tile_[1] = x.tn;
+      tile_[2] = x.tk;
+      return 0;
+    case OP_CONFIG_ATTN:
+      return h_config_attn(x);
+    case OP_SET_SCALE:
+      return h_set_scale(x);
+    case OP_SET_ADDR_LO:
+    case OP_SET_ADDR_HI: {                                   // simulator.py:619-627
+      AddrReg& r = areg_[x.addr_reg];
+      auto it = var_pc_.find(pc_);
+      if (it != var_pc_.end()) {
+        const tac_var_site& s = sites_[it->second.first];
+        if (s.kind != 0 || s.addr_reg != x.addr_reg)
+          return unsupported("runtime SET_ADDR site does not match its instruction");
+        if (it->second.second == 0) {
+          r.kind = 2;  // LO written, HI pending
+          r.known = 0;
+        } else {
+          r.kind = 1;
+          r.param = it->second.first;
+          r.lo = s.range_lo;
+          r.hi = s.range_hi;
+        }
+        return 0;
+      }
+      if (r.kind == 1) {  // a static half over a runtime value
+        r.kind = 2;
+        r.known = 0;
+        r.value = 0;
+      }
+      if (x.op == OP_SET_ADDR_LO) {
+        r.value = (r.value & ~0xFFFFFFFull) | x.imm28;
+        r.known |= 1;
+      } else {
+        r.value = (r.value & 0xFFFFFFFull) | (uint64_t(x.imm28) << 28);
+        r.known |= 2;
+      }
+      if (r.kind == 2 && r.known == 3) r.kind = 0;
+      return 0;
+    }
+    case OP_LOAD:
+      return h_load(x);
+    case OP_STORE:
+      return h_store(x);
+    case OP_BUF_COPY:
+      return h_buf_copy(x);
+    default:
+      return h_rtype(x);
+  }
+}
+
+// Materialises the architectural state at the end of the run: writable DRAM,
+// SRAM home images and scale registers.
+void Compiler::finalize() {
+  // 1. writable DRAM units whose value lives elsewhere
+  flush_rw(0, rw_units_);
+  // 2. SRAM units whose value is not in place
+  std::vector<uint32_t> moved;
+  for (uint32_t u = 0; u < kSramUnits; ++u)
+    if (sram_[u] != u) moved.push_back(u);
+  if (!moved.empty()) {
+    // Values still held in SRAM home locations are first copied out, so the
+    // final copy never reads a unit it also writes.
+    std::vector<uint64_t> from_home;
+    for (uint32_t u : moved)
+      if (cls(sram_[u]) == PC_HOME_SRAM) from_home.push_back(sram_[u]);
+    if (!from_home.empty()) {
+      std::vector<uint64_t> uniq = from_home;
+      std::sort(uniq.begin(), uniq.end());
+      uniq.erase(std::unique(uniq.begin(), uniq.end()), uniq.end());
+      // gather them (in sorted order) into one extent and remap
+      uint64_t g = gather(uniq.data(), uniq.size());
+      for (uint32_t u : moved) {
+        if (cls(sram_[u]) == PC_HOME_SRAM) {
+          uint64_t k = std::lower_bound(uniq.begin(), uniq.end(), sram_[u]) - uniq.begin();
+          sram_[u] = g + k;
+        }
+      }
+    }
+    DevOp op = blank(K_GATHER);
+    op.seg0 = static_cast<uint32_t>(P->segs.size());
+    Access acc;
+    size_t k = 0;
+    while (k < moved.size()) {
+      size_t j = k + 1;
+      while (j < moved.size() && moved[j] == moved[k] + (j - k) &&
+             sram_[moved[j]] == sram_[moved[k]] + (j - k) &&
+             cls(sram_[moved[j]]) == cls(sram_[moved[k]]))
+        ++j;
+      uint64_t n = j - k;
+      P->segs.push_back(Segment{sram_[moved[k]], uint64_t(moved[k]), n});
+      acc.reads.push_back({sram_[moved[k]], n});
+      acc.writes.push_back({uint64_t(moved[k]), n});
+      k = j;
+    }
+    op.nseg = static_cast<uint32_t>(P->segs.size() - op.seg0);
+    emit(op, acc);
+    for (uint32_t u : moved) sram_[u] = u;
+  }
+  // 3. scale registers
+  bool any = false;
+  for (int r = 0; r < 16; ++r) any |= sreg_[r] != uint32_t(r);
+  if (any) {
+    DevOp op = blank(K_SREG_FINAL);
+    op.seg0 = static_cast<uint32_t>(P->segs.size());
+    Access acc;
+    for (int r = 0; r < 16; ++r) {
+      if (sreg_[r] == uint32_t(r)) continue;
+      P->segs.push_back(Segment{sreg_[r], uint64_t(r), 0});
+      read_sreg(acc, sreg_[r]);
+    }
+    op.nseg = static_cast<uint32_t>(P->segs.size() - op.seg0);
+    acc.sreg_home_write = true;
+    emit(op, acc);
+  }
+}
+
+// Splits each op into tasks (tile x sequence group) and orders them by level.
+void Compiler::build_tasks() {
+  const uint32_t B = static_cast<uint32_t>(P->batch);
+  // compress levels
+  std::vector<uint32_t> lv;
+  for (auto& op : P->ops) lv.push_back(op.level);
+  std::sort(lv.begin(), lv.end());
+  lv.erase(std::unique(lv.begin(), lv.end()), lv.end());
+  for (auto& op : P->ops) op.level = static_cast<uint32_t>(std::lower_bound(lv.begin(), lv.end(), op.level) - lv.begin());
+  std::vector<std::vector<Task>> per_level(lv.size());
+  auto per_seq = [&](uint32_t opi, uint32_t tiles) {
+    for (uint32_t s = 0; s < B; ++s)
+      for (uint32_t t = 0; t < tiles; ++t) per_level[P->ops[opi].level].push_back(Task{opi, s, 1, t});
+  };
+  for (uint32_t i = 0; i < P->ops.size(); ++i) {
+    const DevOp& op = P->ops[i];
+    const uint64_t MN = uint64_t(op.M) * op.N;
+    switch (op.kind) {
+      case K_GATHER: {
+        uint64_t total = 0;
+        for (uint32_t k = 0; k < op.nseg; ++k) total += P->segs[op.seg0 + k].n;
+        // ~64 KB of data per task
+        uint32_t tiles = static_cast<uint32_t>(std::max<uint64_t>(1, (total + 4095) / 4096));
+        per_seq(i, tiles);
+        break;
+      }
+      case K_MATMUL: {
+        const uint32_t ntile = (op.N + 63) / 64;
+        const bool shared_b = (op.b & kSharedBit) != 0;
+        if (op.M >= 128 || !shared_b) {
+          const uint32_t mchunks = (op.M + 127) / 128;
+          per_seq(i, ntile * mchunks);
+        } else {
+          const uint32_t spt = std::max<uint32_t>(1, 128 / op.M);
+          for (uint32_t s = 0; s < B; s += spt)
+            for (uint32_t t = 0; t < ntile; ++t)
+              per_level[op.level].push_back(Task{i, s, std::min(spt, B - s), t});
+        }
+        break;
+      }
+      case K_SREG_LOAD:
+      case K_SREG_FINAL: {
+        for (uint32_t s = 0; s < B; s += 256)
+          per_level[op.level].push_back(Task{i, s, std::min<uint32_t>(256, B - s), 0});
+        break;
+      }
+      case K_MAX_ABS:
+      case K_DYN_LOAD:
+      case K_DYN_STORE:
+        per_seq(i, 1);
+        break;
+      case K_LAYERNORM_F16: case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16:
+      case K_LN_I8: case K_SOFTMAX_I8: case K_MASKED_SOFTMAX_I8:
+      case K_SOFTMAX_ATTNV: case K_MASKED_SOFTMAX_ATTNV:
+        per_seq(i, (op.M + 7) / 8);   // one warp per row, 8 rows per task
+        break;
+      case K_TRANSPOSE:
+        per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + 16383) / 16384)));
+        break;
+      default: {  // element-wise ops: 4096 elements per task
+        per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + 4095) / 4096)));
+        break;
+      }
+    }
+  }
+  P->tasks.clear();
+  P->level_off.assign(1, 0);
+  for (auto& v : per_level) {
+    P->tasks.insert(P->tasks.end(), v.begin(), v.end());
+    P->level_off.push_back(static_cast<uint32_t>(P->tasks.size()));
+  }
+}
+
+int Compiler::compile() {
+  sram_.resize(kSramUnits);
+  for (uint32_t u = 0; u < kSramUnits; ++u) sram_[u] = u;
+  shadow_.resize(rw_units_);
+  for (uint64_t i = 0; i < rw_units_; ++i) shadow_[i] = rw_home(i);
+  rw_wl_.assign(rw_units_, 0);
+  rw_rl_.assign(rw_units_, 0);
+  home_rl_.assign(kSramUnits, 0);
+  slot_lvl_.assign(kSregSlotBase, 0);
+  insn_region_bytes_ = n_insns_ * 8;
+
+  // var sites
+  uint32_t w = 0;
+  for (int i = 0; i < n_sites_; ++i) {
+    const tac_var_site& s = sites_[i];
+    VarInfo v{};
+    v.kind = s.kind;
+    v.addr_reg = s.addr_reg;
+    v.lo_pc = s.lo_pc;
+    v.hi_pc = s.hi_pc;
+    v.range_lo = s.range_lo;
+    v.range_hi = s.range_hi;
+    v.word0 = w;
+    if (s.lo_pc >= n_insns_ || (s.kind == 0 && s.hi_pc >= n_insns_)) {
+      pc_ = s.lo_pc;
+      return unsupported("runtime site outside the instruction region");
+    }
+    v.base_lo = load_be64(words_ + s.lo_pc * 8);
+    if (s.kind == 0) {
+      v.base_hi = load_be64(words_ + s.hi_pc * 8);
+      var_pc_[s.lo_pc] = {i, 0};
+      var_pc_[s.hi_pc] = {i, 1};
+      w += 2;
+    } else {
+      var_pc_[s.lo_pc] = {i, 0};
+      w += 1;
+    }
+    P->vars.push_back(v);
+  }
+  P->n_var_words = w;
+  P->n_params = static_cast<uint32_t>(n_sites_);
+
+  uint64_t count = 0;
+  pc_ = entry_;
+  int status = 0;
+  while (!halted_ && count < max_insns_) {
+    if (pc_ >= n_insns_) {
+      word_ = 0;
+      status = fault(TAC_E_SIMULATOR, "PC=" + std::to_string(pc_) + " past end of program (" +
+                                          std::to_string(n_insns_) + " insns)");
+      break;
+    }
+    word_ = load_be64(words_ + pc_ * 8);
+    Insn x;
+    if (!decode(word_, x)) {
+      status = fault(TAC_E_ILLEGAL_OPCODE, "Illegal opcode");
+      break;
+    }
+    status = step(x);
+    if (status) break;
+    ++count;
+    ++pc_;
+  }
+  if (status == TAC_E_UNSUPPORTED || status == TAC_E_SHARED_WRITE) return status;
+  finalize();
+  build_tasks();
+
+  tac_exec_info& I = P->info;
+  I.executed = count;
+  I.final_pc = pc_;
+  I.halted = halted_ ? 1 : 0;
+  I.faulted = status ? 1 : 0;
+  I.cycles = cycles_;
+  I.n_ops = P->ops.size();
+  I.n_levels = P->level_off.size() - 1;
+  I.n_tasks = P->tasks.size();
+  I.n_segments = P->segs.size();
+  I.arena_bytes = arena_top_ * kUnit;
+  I.n_slots = n_slots_;
+  I.n_var_words = P->n_var_words;
+  for (int r = 0; r < 4; ++r) I.final_regs.addr_regs[r] = areg_[r].value;
+  I.final_regs.tile_valid = tile_valid_;
+  for (int i = 0; i < 3; ++i) I.final_regs.tile[i] = tile_[i];
+  I.final_regs.attn_valid = attn_kind_ == 1;
+  I.final_regs.attn_qrb = attn_qrb_;
+  I.final_regs.attn_vkl = attn_vkl_;
+  I.final_regs.attn_mode = attn_mode_;
+  P->arena_units = arena_top_;
+  P->n_slots = n_slots_;
+  return 0;
+}
+
+}  // namespace
+}  // namespace tac
+
+// ------------------------------------------------------------------------------------
+extern "C" int tac_compile(int batch, uint64_t dram_bytes, uint64_t shared_bytes,
+                           const uint8_t* insn_bytes, uint64_t n_insns, uint64_t entry_pc,
+                           uint64_t max_insns, const tac_regs* init_regs, int sregs_reset,
+                           const tac_var_site* sites, int n_sites, tac_program** out,
+                           tac_exec_info* info, tac_fault* fault) {
+  if (!out || !insn_bytes || batch <= 0 || shared_bytes > dram_bytes || (shared_bytes % 16) ||
+      n_sites < 0 || (n_sites > 0 && !sites))
+    return TAC_E_ARGUMENT;
+  *out = nullptr;
+  tac_program* p = new (std::nothrow) tac_program();
+  if (!p) return TAC_E_ARGUMENT;
+  p->batch = batch;
+  p->dram_bytes = dram_bytes;
+  p->shared_bytes = shared_bytes;
+  tac::Compiler c(p, insn_bytes, n_insns, entry_pc, max_insns, init_regs, sregs_reset, sites, n_sites);
+  int s = c.compile();
+  if (fault) *fault = p->fault;
+  if (s) {  // the stream cannot be planned at all
+    delete p;
+    return s;
+  }
+  if (info) *info = p->info;
+  *out = p;
+  return TAC_OK;
+}
+
+extern "C" int tac_program_info(const tac_program* p, tac_exec_info* info, tac_fault* fault) {
+  if (!p) return TAC_E_ARGUMENT;
+  if (info) *info = p->info;
+  if (fault) *fault = p->fault;
+  return TAC_OK;
+}
+
+extern "C" uint64_t tac_program_record_size(int which) {
+  switch (which) {
+    case 0: return sizeof(tac::DevOp);
+    case 1: return sizeof(tac::Segment);
+    case 2: return sizeof(tac::Task);
+    default: return 0;
+  }
+}
+
+extern "C" int tac_program_dump(const tac_program* p, void* ops, void* segments, void* tasks,
+                                uint32_t* level_offsets) {
+  if (!p) return TAC_E_ARGUMENT;
+  if (ops && !p->ops.empty()) std::memcpy(ops, p->ops.data(), p->ops.size() * sizeof(tac::DevOp));
+  if (segments && !p->segs.empty())
+    std::memcpy(segments, p->segs.data(), p->segs.size() * sizeof(tac::Segment));
+  if (tasks && !p->tasks.empty()) std::memcpy(tasks, p->tasks.data(), p->tasks.size() * sizeof(tac::Task));
+  if (level_offsets) std::memcpy(level_offsets, p->level_off.data(), p->level_off.size() * sizeof(uint32_t));
+  return TAC_OK;
+}

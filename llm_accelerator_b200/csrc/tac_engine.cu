@@ -1,0 +1,405 @@
+// Engine: device machine state for a batch of sequences and the C ABI that
+// runs compiled plans on it (include/taccel_b200.h).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "tac_exec.cuh"
+#include "tac_program.h"
+
+struct tac_engine {
+  int device = 0;
+  int batch = 1;
+  uint64_t dram_bytes = 0, shared_bytes = 0;
+  uint64_t rw_bytes = 0;        // per-sequence writable DRAM image
+  uint64_t arena_bytes = 0;     // per-sequence arena capacity
+  uint64_t seq_stride = 0;      // bytes per sequence block
+  uint8_t* d_seq = nullptr;
+  uint8_t* d_shared = nullptr;
+  uint16_t* d_sregs = nullptr;
+  uint32_t sreg_stride = 16;
+  uint64_t* d_params = nullptr;
+  size_t params_cap = 0;
+  uint32_t* d_status = nullptr;  // [0..3] fault info, [4..5] barrier
+  int n_sms = 0;
+  int grid = 0;
+  std::vector<uint64_t> h_params;
+};
+
+namespace {
+
+using namespace tac;
+
+constexpr uint64_t kSramBytes = uint64_t(kSramUnits) * 16;
+
+int cuda_fail(cudaError_t e, tac_fault* f, const char* what) {
+  if (e == cudaSuccess) return TAC_OK;
+  if (f) {
+    std::memset(f, 0, sizeof(*f));
+    f->status = TAC_E_CUDA;
+    std::snprintf(f->message, sizeof(f->message), "%s: %s", what, cudaGetErrorString(e));
+  }
+  return TAC_E_CUDA;
+}
+
+#define CK(expr, f, what) do { cudaError_t _e = (expr); if (_e != cudaSuccess) return cuda_fail(_e, f, what); } while (0)
+
+uint64_t round_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+int set_fault(tac_fault* f, int status, const char* msg, uint64_t pc = 0) {
+  if (f) {
+    std::memset(f, 0, sizeof(*f));
+    f->status = status;
+    f->pc = pc;
+    std::snprintf(f->message, sizeof(f->message), "%s", msg);
+  }
+  return status;
+}
+
+// Grows the per-sequence arena, keeping SRAM and writable-DRAM contents.
+int ensure_arena(tac_engine* e, uint64_t need_bytes, tac_fault* f) {
+  if (need_bytes <= e->arena_bytes) return TAC_OK;
+  uint64_t new_arena = std::max<uint64_t>(need_bytes, e->arena_bytes * 2);
+  new_arena = round_up(new_arena, 1 << 20);
+  const uint64_t new_stride = round_up(kSramBytes + e->rw_bytes + new_arena, 256);
+  uint8_t* nb = nullptr;
+  CK(cudaMalloc(&nb, new_stride * e->batch), f, "cudaMalloc arena");
+  const uint64_t keep = kSramBytes + e->rw_bytes;
+  CK(cudaDeviceSynchronize(), f, "sync");
+  CK(cudaMemcpy2D(nb, new_stride, e->d_seq, e->seq_stride, keep, e->batch, cudaMemcpyDeviceToDevice), f,
+     "copy state");
+  CK(cudaFree(e->d_seq), f, "cudaFree");
+  e->d_seq = nb;
+  e->seq_stride = new_stride;
+  e->arena_bytes = new_arena;
+  return TAC_OK;
+}
+
+int ensure_sregs(tac_engine* e, uint32_t slots, tac_fault* f) {
+  const uint32_t need = 16 + slots;
+  if (need <= e->sreg_stride) return TAC_OK;
+  const uint32_t ns = static_cast<uint32_t>(round_up(std::max<uint32_t>(need, e->sreg_stride * 2), 64));
+  uint16_t* nb = nullptr;
+  CK(cudaMalloc(&nb, size_t(ns) * 2 * e->batch), f, "cudaMalloc sregs");
+  CK(cudaMemset(nb, 0, size_t(ns) * 2 * e->batch), f, "memset sregs");
+  CK(cudaDeviceSynchronize(), f, "sync");
+  CK(cudaMemcpy2D(nb, size_t(ns) * 2, e->d_sregs, size_t(e->sreg_stride) * 2, 32, e->batch,
+                  cudaMemcpyDeviceToDevice), f, "copy sregs");
+  CK(cudaFree(e->d_sregs), f, "cudaFree");
+  e->d_sregs = nb;
+  e->sreg_stride = ns;
+  return TAC_OK;
+}
+
+int upload_program(tac_engine* e, tac_program* p, tac_fault* f) {
+  if (p->d_blob && p->device == e->device) return TAC_OK;
+  if (p->d_blob) {
+    cudaFree(p->d_blob);
+    p->d_blob = nullptr;
+  }
+  const uint64_t s_ops = p->ops.size() * sizeof(DevOp), s_segs = p->segs.size() * sizeof(Segment);
+  const uint64_t s_tasks = p->tasks.size() * sizeof(Task), s_lv = p->level_off.size() * 4;
+  p->off_ops = 0;
+  p->off_segs = round_up(s_ops, 256);
+  p->off_tasks = p->off_segs + round_up(s_segs, 256);
+  p->off_levels = p->off_tasks + round_up(s_tasks, 256);
+  const uint64_t total = p->off_levels + round_up(s_lv, 256) + 256;
+  std::vector<uint8_t> blob(total, 0);
+  if (s_ops) std::memcpy(blob.data() + p->off_ops, p->ops.data(), s_ops);
+  if (s_segs) std::memcpy(blob.data() + p->off_segs, p->segs.data(), s_segs);
+  if (s_tasks) std::memcpy(blob.data() + p->off_tasks, p->tasks.data(), s_tasks);
+  std::memcpy(blob.data() + p->off_levels, p->level_off.data(), s_lv);
+  CK(cudaMalloc(&p->d_blob, total), f, "cudaMalloc program");
+  CK(cudaMemcpy(p->d_blob, blob.data(), total, cudaMemcpyHostToDevice), f, "upload program");
+  p->device = e->device;
+  return TAC_OK;
+}
+
+uint32_t insn_bits(uint64_t w, int shift, int width) { return static_cast<uint32_t>((w >> shift) & ((1ull << width) - 1)); }
+
+// Decodes one sequence's runtime words into parameters and checks them
+// against the ranges the plan was compiled for.
+int decode_params(const tac_program* p, const uint64_t* words, uint64_t* params, tac_fault* f) {
+  for (size_t i = 0; i < p->vars.size(); ++i) {
+    const VarInfo& v = p->vars[i];
+    if (v.kind == 0) {
+      const uint64_t lo = words[v.word0], hi = words[v.word0 + 1];
+      if (insn_bits(lo, 59, 5) != OP_SET_ADDR_LO || insn_bits(hi, 59, 5) != OP_SET_ADDR_HI ||
+          insn_bits(lo, 57, 2) != v.addr_reg || insn_bits(hi, 57, 2) != v.addr_reg)
+        return set_fault(f, TAC_E_RECOMPILE, "runtime SET_ADDR word changed its opcode or register", v.lo_pc);
+      params[i] = (uint64_t(insn_bits(hi, 29, 28)) << 28) | insn_bits(lo, 29, 28);
+    } else {
+      const uint64_t w = words[v.word0];
+      if (insn_bits(w, 59, 5) != OP_CONFIG_ATTN || (w & ((1ull << 33) - 1)))
+        return set_fault(f, TAC_E_RECOMPILE, "runtime CONFIG_ATTN word changed its form", v.lo_pc);
+      params[i] = uint64_t(insn_bits(w, 47, 12)) | (uint64_t(insn_bits(w, 35, 12)) << 16) |
+                  (uint64_t(insn_bits(w, 33, 2)) << 32);
+    }
+  }
+  for (const RtCheck& c : p->checks) {
+    const uint64_t v = params[c.param];
+    bool ok = true;
+    if (c.kind == CHK_ADDR) {
+      const uint64_t a = v + static_cast<uint64_t>(c.dconst);
+      ok = (a % 16 == 0 || c.nbytes == 0) && a >= c.lo && a < std::max(c.hi, c.lo + 1) &&
+           a + c.nbytes <= p->dram_bytes;
+    } else {
+      const uint32_t vkl = (v >> 16) & 0xFFFF, mode = (v >> 32) & 3;
+      if (c.kind == CHK_ATTN_SET) ok = mode != 0 && vkl != 0;
+      else {
+        const uint32_t keys = static_cast<uint32_t>(c.lo);
+        ok = mode != 0 && vkl != 0 && !((mode == 1 || mode == 3) && keys < vkl) && !(mode == 2 && keys != vkl);
+      }
+    }
+    if (!ok) return set_fault(f, TAC_E_RECOMPILE, "runtime word outside the compiled range", c.pc);
+  }
+  return TAC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tac_engine_create(int device, int batch, uint64_t dram_bytes, uint64_t shared_bytes, tac_engine** out) {
+  if (!out || batch <= 0 || shared_bytes > dram_bytes || shared_bytes % 16) return TAC_E_ARGUMENT;
+  *out = nullptr;
+  if (cudaSetDevice(device) != cudaSuccess) return TAC_E_CUDA;
+  tac_engine* e = new (std::nothrow) tac_engine();
+  if (!e) return TAC_E_ARGUMENT;
+  e->device = device;
+  e->batch = batch;
+  e->dram_bytes = dram_bytes;
+  e->shared_bytes = shared_bytes;
+  e->rw_bytes = round_up(dram_bytes - shared_bytes, 256);
+  e->arena_bytes = 0;
+  e->seq_stride = round_up(kSramBytes + e->rw_bytes, 256);
+  bool ok = cudaMalloc(&e->d_seq, e->seq_stride * batch) == cudaSuccess &&
+            cudaMemset(e->d_seq, 0, e->seq_stride * batch) == cudaSuccess &&
+            cudaMalloc(&e->d_shared, std::max<uint64_t>(round_up(shared_bytes, 256), 256)) == cudaSuccess &&
+            cudaMemset(e->d_shared, 0, std::max<uint64_t>(round_up(shared_bytes, 256), 256)) == cudaSuccess &&
+            cudaMalloc(&e->d_sregs, size_t(e->sreg_stride) * 2 * batch) == cudaSuccess &&
+            cudaMemset(e->d_sregs, 0, size_t(e->sreg_stride) * 2 * batch) == cudaSuccess &&
+            cudaMalloc(&e->d_status, 64) == cudaSuccess && cudaMemset(e->d_status, 0, 64) == cudaSuccess;
+  if (ok) {
+    cudaDeviceGetAttribute(&e->n_sms, cudaDevAttrMultiProcessorCount, device);
+    cudaFuncSetAttribute(exec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kExecSmem));
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exec_kernel, kThreads, kExecSmem);
+    e->grid = e->n_sms * std::max(1, std::min(per_sm, 1));
+    ok = cudaDeviceSynchronize() == cudaSuccess && per_sm >= 1;
+  }
+  if (!ok) {
+    tac_engine_destroy(e);
+    return TAC_E_CUDA;
+  }
+  *out = e;
+  return TAC_OK;
+}
+
+int tac_engine_destroy(tac_engine* e) {
+  if (!e) return TAC_E_ARGUMENT;
+  cudaSetDevice(e->device);
+  cudaDeviceSynchronize();
+  cudaFree(e->d_seq);
+  cudaFree(e->d_shared);
+  cudaFree(e->d_sregs);
+  cudaFree(e->d_params);
+  cudaFree(e->d_status);
+  delete e;
+  return TAC_OK;
+}
+
+int tac_engine_batch(const tac_engine* e) { return e ? e->batch : 0; }
+
+int tac_engine_layout(const tac_engine* e, void** seq_base, uint64_t* seq_stride, void** shared_base) {
+  if (!e) return TAC_E_ARGUMENT;
+  if (seq_base) *seq_base = e->d_seq;
+  if (seq_stride) *seq_stride = e->seq_stride;
+  if (shared_base) *shared_base = e->d_shared;
+  return TAC_OK;
+}
+
+static int dram_copy(tac_engine* e, int seq, uint64_t addr, void* host, uint64_t len, bool write) {
+  if (!e || (len && !host) || seq < -1 || seq >= e->batch || addr + len > e->dram_bytes || addr + len < addr)
+    return TAC_E_ARGUMENT;
+  if (!write && seq < 0) return TAC_E_ARGUMENT;
+  if (cudaSetDevice(e->device) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) return TAC_E_CUDA;
+  uint8_t* h = static_cast<uint8_t*>(host);
+  // shared part
+  if (addr < e->shared_bytes) {
+    const uint64_t n = std::min(len, e->shared_bytes - addr);
+    cudaError_t c = write ? cudaMemcpy(e->d_shared + addr, h, n, cudaMemcpyHostToDevice)
+                          : cudaMemcpy(h, e->d_shared + addr, n, cudaMemcpyDeviceToHost);
+    if (c != cudaSuccess) return TAC_E_CUDA;
+    h += n;
+    addr += n;
+    len -= n;
+  }
+  if (!len) return TAC_OK;
+  const uint64_t off = kSramBytes + (addr - e->shared_bytes);
+  const int s0 = seq < 0 ? 0 : seq, s1 = seq < 0 ? e->batch : seq + 1;
+  for (int s = s0; s < s1; ++s) {
+    uint8_t* d = e->d_seq + uint64_t(s) * e->seq_stride + off;
+    cudaError_t c = write ? cudaMemcpy(d, h, len, cudaMemcpyHostToDevice) : cudaMemcpy(h, d, len, cudaMemcpyDeviceToHost);
+    if (c != cudaSuccess) return TAC_E_CUDA;
+  }
+  return TAC_OK;
+}
+
+int tac_dram_write(tac_engine* e, int seq, uint64_t addr, const void* src, uint64_t len) {
+  return dram_copy(e, seq, addr, const_cast<void*>(src), len, true);
+}
+int tac_dram_read(tac_engine* e, int seq, uint64_t addr, void* dst, uint64_t len) {
+  return dram_copy(e, seq, addr, dst, len, false);
+}
+
+static int sram_copy(tac_engine* e, int seq, int buf, uint64_t off, void* host, uint64_t len, bool write) {
+  if (!e || buf < 0 || buf > 2 || seq < -1 || seq >= e->batch || (len && !host)) return TAC_E_ARGUMENT;
+  if (off + len > uint64_t(kBufUnits[buf]) * 16 || (!write && seq < 0)) return TAC_E_ARGUMENT;
+  if (cudaSetDevice(e->device) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) return TAC_E_CUDA;
+  const int s0 = seq < 0 ? 0 : seq, s1 = seq < 0 ? e->batch : seq + 1;
+  for (int s = s0; s < s1; ++s) {
+    uint8_t* d = e->d_seq + uint64_t(s) * e->seq_stride + uint64_t(kBufUnitBase[buf]) * 16 + off;
+    cudaError_t c = write ? cudaMemcpy(d, host, len, cudaMemcpyHostToDevice) : cudaMemcpy(host, d, len, cudaMemcpyDeviceToHost);
+    if (c != cudaSuccess) return TAC_E_CUDA;
+  }
+  return TAC_OK;
+}
+
+int tac_sram_write(tac_engine* e, int seq, int buf, uint64_t byte_off, const void* src, uint64_t len) {
+  return sram_copy(e, seq, buf, byte_off, const_cast<void*>(src), len, true);
+}
+int tac_sram_read(tac_engine* e, int seq, int buf, uint64_t byte_off, void* dst, uint64_t len) {
+  return sram_copy(e, seq, buf, byte_off, dst, len, false);
+}
+
+int tac_sregs_write(tac_engine* e, int seq, const uint16_t* regs16) {
+  if (!e || !regs16 || seq < -1 || seq >= e->batch) return TAC_E_ARGUMENT;
+  if (cudaSetDevice(e->device) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) return TAC_E_CUDA;
+  const int s0 = seq < 0 ? 0 : seq, s1 = seq < 0 ? e->batch : seq + 1;
+  for (int s = s0; s < s1; ++s)
+    if (cudaMemcpy(e->d_sregs + size_t(s) * e->sreg_stride, regs16, 32, cudaMemcpyHostToDevice) != cudaSuccess)
+      return TAC_E_CUDA;
+  return TAC_OK;
+}
+
+int tac_sregs_read(tac_engine* e, int seq, uint16_t* regs16) {
+  if (!e || !regs16 || seq < 0 || seq >= e->batch) return TAC_E_ARGUMENT;
+  if (cudaSetDevice(e->device) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) return TAC_E_CUDA;
+  if (cudaMemcpy(regs16, e->d_sregs + size_t(seq) * e->sreg_stride, 32, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return TAC_E_CUDA;
+  return TAC_OK;
+}
+
+int tac_program_destroy(tac_program* p) {
+  if (!p) return TAC_E_ARGUMENT;
+  if (p->d_blob) {
+    cudaSetDevice(p->device);
+    cudaFree(p->d_blob);
+  }
+  delete p;
+  return TAC_OK;
+}
+
+int tac_run_async(tac_engine* e, tac_program* p, const uint64_t* var_words, void* stream, tac_fault* f) {
+  if (!e || !p || p->batch != e->batch || p->dram_bytes != e->dram_bytes || p->shared_bytes != e->shared_bytes)
+    return set_fault(f, TAC_E_ARGUMENT, "program was compiled for a different engine layout");
+  if (p->n_var_words && !var_words) return set_fault(f, TAC_E_ARGUMENT, "missing runtime words");
+  CK(cudaSetDevice(e->device), f, "cudaSetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int s = upload_program(e, p, f)) return s;
+  if (int s = ensure_arena(e, p->arena_units * 16, f)) return s;
+  if (int s = ensure_sregs(e, p->n_slots, f)) return s;
+  const uint32_t np = std::max<uint32_t>(p->n_params, 1);
+  e->h_params.assign(size_t(np) * e->batch, 0);
+  for (int s = 0; s < e->batch && p->n_params; ++s) {
+    if (int r = decode_params(p, var_words + size_t(s) * p->n_var_words, e->h_params.data() + size_t(s) * np, f)) {
+      if (f) f->buf_id = s;
+      return r;
+    }
+  }
+  if (e->params_cap < e->h_params.size()) {
+    cudaFree(e->d_params);
+    e->params_cap = std::max<size_t>(e->h_params.size(), 1024);
+    CK(cudaMalloc(&e->d_params, e->params_cap * 8), f, "cudaMalloc params");
+  }
+  CK(cudaMemcpyAsync(e->d_params, e->h_params.data(), e->h_params.size() * 8, cudaMemcpyHostToDevice, st), f,
+     "upload params");
+  CK(cudaMemsetAsync(e->d_status, 0, 64, st), f, "reset status");
+  const uint32_t n_levels = static_cast<uint32_t>(p->level_off.size() - 1);
+  if (n_levels > 0 && !p->tasks.empty()) {
+    ExecArgs A;
+    const uint8_t* blob = static_cast<const uint8_t*>(p->d_blob);
+    A.ops = reinterpret_cast<const DevOp*>(blob + p->off_ops);
+    A.segs = reinterpret_cast<const Segment*>(blob + p->off_segs);
+    A.tasks = reinterpret_cast<const Task*>(blob + p->off_tasks);
+    A.level_off = reinterpret_cast<const uint32_t*>(blob + p->off_levels);
+    A.n_levels = n_levels;
+    A.n_params = np;
+    A.seq_base = e->d_seq;
+    A.seq_stride = e->seq_stride;
+    A.shared_base = e->d_shared;
+    A.sregs = e->d_sregs;
+    A.sreg_stride = e->sreg_stride;
+    A.params = e->d_params;
+    A.status = e->d_status;
+    A.barrier = e->d_status + 4;
+    A.shared_bytes = e->shared_bytes;
+    A.dram_bytes = e->dram_bytes;
+    void* args[] = {&A};
+    CK(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(exec_kernel), dim3(e->grid), dim3(kThreads), args,
+                                   kExecSmem, st), f, "launch executor");
+  }
+  if (p->info.faulted) {
+    if (f) *f = p->fault;
+    return p->fault.status;
+  }
+  return TAC_OK;
+}
+
+int tac_check_device_status(tac_engine* e, tac_fault* f) {
+  if (!e) return TAC_E_ARGUMENT;
+  uint32_t st[8];
+  CK(cudaMemcpy(st, e->d_status, 32, cudaMemcpyDeviceToHost), f, "read status");
+  switch (st[0]) {
+    case DF_NONE: return TAC_OK;
+    case DF_ZERO_DENOM:
+      return set_fault(f, TAC_E_CONFIG, "CONFIG_ATTN produced zero softmax denominator");
+    case DF_BARRIER_TIMEOUT:
+      return set_fault(f, TAC_E_DEVICE, "executor grid barrier timed out");
+    case DF_DYN_ADDRESS:
+      return set_fault(f, TAC_E_DEVICE, "runtime address outside DRAM");
+    default:
+      return set_fault(f, TAC_E_DEVICE, "executor reported an invalid op");
+  }
+}
+
+int tac_run(tac_engine* e, tac_program* p, const uint64_t* var_words, tac_fault* f) {
+  int s = tac_run_async(e, p, var_words, nullptr, f);
+  if (s != TAC_OK && !(p && p->info.faulted && s == p->fault.status)) return s;
+  const int compiled_fault = s;
+  CK(cudaStreamSynchronize(nullptr), f, "synchronize");
+  CK(cudaGetLastError(), f, "executor");
+  tac_fault df;
+  std::memset(&df, 0, sizeof(df));
+  int ds = tac_check_device_status(e, &df);
+  if (ds != TAC_OK) {
+    if (f) *f = df;
+    return ds;
+  }
+  return compiled_fault;
+}
+
+int tac_argmax_f16(tac_engine* e, uint64_t addr, uint64_t count, int32_t* out_tokens_dev, void* stream) {
+  if (!e || !out_tokens_dev || addr + 2 * count > e->dram_bytes) return TAC_E_ARGUMENT;
+  if (cudaSetDevice(e->device) != cudaSuccess) return TAC_E_CUDA;
+  argmax_f16_kernel<<<e->batch, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+      e->d_seq, e->seq_stride, e->d_shared, e->shared_bytes, addr, count, out_tokens_dev);
+  return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
+}
+
+}  // extern "C"

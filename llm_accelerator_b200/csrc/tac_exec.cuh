@@ -1,0 +1,717 @@
+// Device executor: one persistent cooperative kernel runs a compiled plan.
+//
+// The grid walks the plan's dependency levels in order.  Inside a level the
+// tasks (op x tile x sequence group) are independent and are spread over the
+// CTAs; a bounded grid barrier separates levels.  Every op reproduces the
+// golden model's arithmetic (see tac_numerics.cuh) on the physical operands
+// the compiler resolved.
+#pragma once
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "tac_isa.h"
+#include "tac_numerics.cuh"
+#include "tac_plan.h"
+
+namespace tac {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr uint32_t kBarrierSpinLimit = 1u << 26;   // ~ seconds with nanosleep back-off
+
+// Device-side fault codes (status word 0).
+enum DevFault : uint32_t {
+  DF_NONE = 0,
+  DF_BARRIER_TIMEOUT = 1,
+  DF_DYN_ADDRESS = 2,
+  DF_ZERO_DENOM = 3,
+  DF_BAD_OP = 4,
+};
+
+struct ExecArgs {
+  const DevOp* ops;
+  const Segment* segs;
+  const Task* tasks;
+  const uint32_t* level_off;
+  uint32_t n_levels;
+  uint32_t n_params;
+  uint8_t* seq_base;
+  uint64_t seq_stride;       // bytes
+  const uint8_t* shared_base;
+  uint16_t* sregs;           // [batch][sreg_stride]
+  uint32_t sreg_stride;
+  const uint64_t* params;    // [batch][n_params]
+  uint32_t* status;          // [0] fault, [1] op, [2] seq, [3] level
+  uint32_t* barrier;         // [0] arrivals, [1] generation
+  uint64_t shared_bytes;
+  uint64_t dram_bytes;
+};
+
+__device__ __forceinline__ uint8_t* pptr(const ExecArgs& A, uint64_t phys, uint32_t seq) {
+  if (phys & kSharedBit) return const_cast<uint8_t*>(A.shared_base) + ((phys & ~kSharedBit) << 4);
+  return A.seq_base + uint64_t(seq) * A.seq_stride + (phys << 4);
+}
+
+__device__ __forceinline__ uint16_t sreg_bits(const ExecArgs& A, uint32_t enc, uint32_t seq) {
+  if (enc & kSregConst) return static_cast<uint16_t>(enc & 0xFFFF);
+  return A.sregs[uint64_t(seq) * A.sreg_stride + enc];
+}
+__device__ __forceinline__ float sreg_f32(const ExecArgs& A, uint32_t enc, uint32_t seq) {
+  return h2f(sreg_bits(A, enc, seq));
+}
+
+__device__ __forceinline__ void raise_fault(const ExecArgs& A, uint32_t code, uint32_t op, uint32_t seq) {
+  if (atomicCAS(A.status, 0u, code) == 0u) {
+    A.status[1] = op;
+    A.status[2] = seq;
+  }
+}
+
+// Address of DRAM byte `addr` for sequence `seq` (runtime-addressed copies).
+__device__ __forceinline__ uint8_t* dram_ptr(const ExecArgs& A, uint64_t addr, uint32_t seq) {
+  if (addr < A.shared_bytes) return const_cast<uint8_t*>(A.shared_base) + addr;
+  return A.seq_base + uint64_t(seq) * A.seq_stride + uint64_t(kSramUnits) * 16 + (addr - A.shared_bytes);
+}
+
+// ---------------------------------------------------------------------------------
+// Data movement
+// ---------------------------------------------------------------------------------
+__device__ void op_gather(const ExecArgs& A, const DevOp& op, const Task& t) {
+  const uint64_t lo = uint64_t(t.tile) * 4096, hi = lo + 4096;
+  uint64_t base = 0;
+  for (uint32_t k = 0; k < op.nseg; ++k) {
+    const Segment sg = A.segs[op.seg0 + k];
+    const uint64_t s0 = base > lo ? base : lo;
+    const uint64_t e = base + sg.n;
+    const uint64_t s1 = e < hi ? e : hi;
+    if (s0 < s1) {
+      const uint4* src = reinterpret_cast<const uint4*>(pptr(A, sg.src + (s0 - base), t.seq0));
+      uint4* dst = reinterpret_cast<uint4*>(pptr(A, sg.dst + (s0 - base), t.seq0));
+      for (uint64_t u = threadIdx.x; u < s1 - s0; u += blockDim.x) dst[u] = src[u];
+    }
+    base = e;
+    if (base >= hi) break;
+  }
+}
+
+__device__ void op_dyn_copy(const ExecArgs& A, const DevOp& op, const Task& t, uint32_t opi) {
+  const uint32_t seq = t.seq0;
+  const uint64_t addr = A.params[uint64_t(seq) * A.n_params + op.param] + op.dconst;
+  if ((addr & 15) || addr + op.nbytes > A.dram_bytes) {
+    if (threadIdx.x == 0) raise_fault(A, DF_DYN_ADDRESS, opi, seq);
+    return;
+  }
+  const uint64_t n = op.nbytes / 16;
+  const uint4* src;
+  uint4* dst;
+  if (op.kind == K_DYN_LOAD) {
+    src = reinterpret_cast<const uint4*>(dram_ptr(A, addr, seq));
+    dst = reinterpret_cast<uint4*>(pptr(A, op.d, seq));
+  } else {
+    if (addr < A.shared_bytes) {
+      if (threadIdx.x == 0) raise_fault(A, DF_DYN_ADDRESS, opi, seq);
+      return;
+    }
+    src = reinterpret_cast<const uint4*>(pptr(A, op.a, seq));
+    dst = reinterpret_cast<uint4*>(dram_ptr(A, addr, seq));
+  }
+  for (uint64_t u = threadIdx.x; u < n; u += blockDim.x) dst[u] = src[u];
+}
+
+__device__ void op_transpose(const ExecArgs& A, const DevOp& op, const Task& t) {
+  const int8_t* src = reinterpret_cast<const int8_t*>(pptr(A, op.a, t.seq0));
+  int8_t* dst = reinterpret_cast<int8_t*>(pptr(A, op.d, t.seq0));
+  const uint64_t rows = op.M, cols = op.N, total = rows * cols;
+  const uint64_t lo = uint64_t(t.tile) * 16384, hi = lo + 16384 < total ? lo + 16384 : total;
+  for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const uint64_t c = i / rows, r = i % rows;   // dst element i = (c, r)
+    dst[i] = src[r * cols + c];
+  }
+}
+
+__device__ void op_sreg_load(const ExecArgs& A, const DevOp& op, const Task& t) {
+  for (uint32_t s = t.seq0 + threadIdx.x; s < t.seq0 + t.nseq; s += blockDim.x) {
+    const uint16_t v = *reinterpret_cast<const uint16_t*>(pptr(A, op.a, s));
+    A.sregs[uint64_t(s) * A.sreg_stride + op.out_slot] = v;
+  }
+}
+
+__device__ void op_sreg_final(const ExecArgs& A, const DevOp& op, const Task& t) {
+  for (uint32_t s = t.seq0 + threadIdx.x; s < t.seq0 + t.nseq; s += blockDim.x) {
+    uint16_t vals[16];
+    for (uint32_t k = 0; k < op.nseg && k < 16; ++k)
+      vals[k] = sreg_bits(A, static_cast<uint32_t>(A.segs[op.seg0 + k].src), s);
+    for (uint32_t k = 0; k < op.nseg && k < 16; ++k)
+      A.sregs[uint64_t(s) * A.sreg_stride + A.segs[op.seg0 + k].dst] = vals[k];
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// MATMUL: int8 x int8 -> int32 on the tensor cores (mma.sync m16n8k32).
+// A task covers up to 128 rows (whole sequences when B is shared) x 64 columns.
+// ---------------------------------------------------------------------------------
+constexpr int kMmKc = 128;            // K chunk
+constexpr int kMmAStride = kMmKc + 16; // padded row stride (bytes) in shared memory
+constexpr int kMmBStride = kMmKc + 16;
+
+__device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                       uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ void op_matmul(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+  const uint32_t M = op.M, N = op.N, K = op.K;
+  const uint32_t ntile = (N + 63) / 64;
+  const bool grouped = (op.b & kSharedBit) && M < 128;
+  uint32_t n0, nblocks;
+  uint32_t blk_seq[8], blk_row[8];
+  if (grouped) {
+    n0 = t.tile * 64;
+    const uint32_t bps = M / 16;
+    nblocks = 0;
+    for (uint32_t s = 0; s < t.nseq; ++s)
+      for (uint32_t b = 0; b < bps && nblocks < 8; ++b) {
+        blk_seq[nblocks] = t.seq0 + s;
+        blk_row[nblocks] = b * 16;
+        ++nblocks;
+      }
+  } else {
+    n0 = (t.tile % ntile) * 64;
+    const uint32_t mchunk = t.tile / ntile;
+    const uint32_t r0 = mchunk * 128;
+    nblocks = 0;
+    for (uint32_t r = r0; r < M && nblocks < 8; r += 16) {
+      blk_seq[nblocks] = t.seq0;
+      blk_row[nblocks] = r;
+      ++nblocks;
+    }
+  }
+  const uint32_t ncols = N - n0 < 64 ? N - n0 : 64;
+  uint8_t* As = smem;                        // [8][16][kMmAStride]
+  uint8_t* Bs = smem + 8 * 16 * kMmAStride;  // [64][kMmBStride]  (n-major, k contiguous)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  // each warp owns pairs p = warp + 8*i  (row block p/8, n-subtile p%8)
+  int acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0;
+
+  const uint8_t* Bg = pptr(A, op.b, t.seq0);
+  for (uint32_t k0 = 0; k0 < K; k0 += kMmKc) {
+    const uint32_t kc = K - k0 < uint32_t(kMmKc) ? K - k0 : uint32_t(kMmKc);
+    const uint32_t kc32 = (kc + 31) & ~31u;
+    __syncthreads();
+    // A chunk: 16-byte vectors
+    for (uint32_t i = threadIdx.x; i < nblocks * 16 * (kc32 / 16); i += blockDim.x) {
+      const uint32_t v = i % (kc32 / 16), row = (i / (kc32 / 16)) % 16, blk = i / (kc32 / 16) / 16;
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (v * 16 < kc) {
+        const uint8_t* src = pptr(A, op.a, blk_seq[blk]) + uint64_t(blk_row[blk] + row) * K + k0 + v * 16;
+        val = *reinterpret_cast<const uint4*>(src);
+      }
+      *reinterpret_cast<uint4*>(As + (blk * 16 + row) * kMmAStride + v * 16) = val;
+    }
+    // B chunk transposed into Bs[n][k]: each thread handles a 4(k) x 4(n) block
+    for (uint32_t i = threadIdx.x; i < (kc32 / 4) * 16; i += blockDim.x) {
+      const uint32_t kb = (i / 16) * 4, nb = (i % 16) * 4;
+      uint32_t r[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        r[j] = 0;
+        if (kb + j < kc && nb < ncols)
+          r[j] = *reinterpret_cast<const uint32_t*>(Bg + uint64_t(k0 + kb + j) * N + n0 + nb);
+      }
+      const uint32_t t0 = __byte_perm(r[0], r[1], 0x5140), t1 = __byte_perm(r[2], r[3], 0x5140);
+      const uint32_t t2 = __byte_perm(r[0], r[1], 0x7362), t3 = __byte_perm(r[2], r[3], 0x7362);
+      *reinterpret_cast<uint32_t*>(Bs + (nb + 0) * kMmBStride + kb) = __byte_perm(t0, t1, 0x5410);
+      *reinterpret_cast<uint32_t*>(Bs + (nb + 1) * kMmBStride + kb) = __byte_perm(t0, t1, 0x7632);
+      *reinterpret_cast<uint32_t*>(Bs + (nb + 2) * kMmBStride + kb) = __byte_perm(t2, t3, 0x5410);
+      *reinterpret_cast<uint32_t*>(Bs + (nb + 3) * kMmBStride + kb) = __byte_perm(t2, t3, 0x7632);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t p = warp + 8 * i;
+      const uint32_t blk = p / 8, ns = p % 8;
+      if (blk >= nblocks || ns * 8 >= ncols) continue;
+      const uint8_t* a_row0 = As + (blk * 16 + g) * kMmAStride;
+      const uint8_t* a_row8 = As + (blk * 16 + g + 8) * kMmAStride;
+      const uint8_t* b_col = Bs + (ns * 8 + g) * kMmBStride;
+      for (uint32_t ks = 0; ks < kc32; ks += 32) {
+        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(a_row0 + ks + q * 4);
+        const uint32_t a1 = *reinterpret_cast<const uint32_t*>(a_row8 + ks + q * 4);
+        const uint32_t a2 = *reinterpret_cast<const uint32_t*>(a_row0 + ks + 16 + q * 4);
+        const uint32_t a3 = *reinterpret_cast<const uint32_t*>(a_row8 + ks + 16 + q * 4);
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(b_col + ks + q * 4);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(b_col + ks + 16 + q * 4);
+        mma_s8(acc[i], a0, a1, a2, a3, b0, b1);
+      }
+    }
+  }
+  // epilogue
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t p = warp + 8 * i;
+    const uint32_t blk = p / 8, ns = p % 8;
+    if (blk >= nblocks || ns * 8 >= ncols) continue;
+    const uint32_t col = n0 + ns * 8 + q * 2;
+    const uint32_t seq = blk_seq[blk];
+    int32_t* D = reinterpret_cast<int32_t*>(pptr(A, op.d, seq));
+    const int32_t* C = (op.flags & F_ACCUMULATE) ? reinterpret_cast<const int32_t*>(pptr(A, op.c, seq)) : nullptr;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint64_t row = blk_row[blk] + g + 8 * h;
+      int2 v = make_int2(acc[i][2 * h], acc[i][2 * h + 1]);
+      if (C) {
+        const int2 c = *reinterpret_cast<const int2*>(C + row * N + col);
+        v.x = static_cast<int32_t>(static_cast<uint32_t>(v.x) + static_cast<uint32_t>(c.x));
+        v.y = static_cast<int32_t>(static_cast<uint32_t>(v.y) + static_cast<uint32_t>(c.y));
+      }
+      *reinterpret_cast<int2*>(D + row * N + col) = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Element-wise ops (4096 elements of one sequence per task)
+// ---------------------------------------------------------------------------------
+__device__ void op_elementwise(const ExecArgs& A, const DevOp& op, const Task& t) {
+  const uint32_t seq = t.seq0, N = op.N;
+  const uint64_t MN = uint64_t(op.M) * N;
+  const uint64_t lo = uint64_t(t.tile) * 4096, hi = lo + 4096 < MN ? lo + 4096 : MN;
+  const uint8_t* a = pptr(A, op.a, seq);
+  const uint8_t* b = (op.kind == K_VADD_I8 || op.kind == K_VADD_I32 || op.kind == K_DEQUANT_ADD ||
+                      op.kind == K_DEQUANT_ACCUM || op.kind == K_DEQUANT_SCALED ||
+                      op.kind == K_VADD_F16 || op.kind == K_REQUANT_PC)
+                         ? pptr(A, op.b, seq) : nullptr;
+  uint8_t* d = pptr(A, op.d, seq);
+  const float s0 = sreg_f32(A, op.s[0], seq);
+  const float s1 = sreg_f32(A, op.s[1], seq);
+  for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const uint32_t col = static_cast<uint32_t>(i % N);
+    switch (op.kind) {
+      case K_REQUANT:
+        reinterpret_cast<int8_t*>(d)[i] =
+            sat8(__fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]), s0));
+        break;
+      case K_REQUANT_PC:
+        reinterpret_cast<int8_t*>(d)[i] =
+            sat8(__fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]),
+                           h2f(reinterpret_cast<const uint16_t*>(b)[col])));
+        break;
+      case K_SCALE_MUL_I32:
+        reinterpret_cast<int32_t*>(d)[i] =
+            sat32(__fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]), s0));
+        break;
+      case K_SCALE_MUL_I8:
+        reinterpret_cast<int8_t*>(d)[i] =
+            sat8(__fmul_rn(static_cast<float>(reinterpret_cast<const int8_t*>(a)[i]), s0));
+        break;
+      case K_VADD_I8: {
+        int v = int(reinterpret_cast<const int8_t*>(a)[i]) + int(reinterpret_cast<const int8_t*>(b)[i]);
+        reinterpret_cast<int8_t*>(d)[i] = static_cast<int8_t>(v < -128 ? -128 : (v > 127 ? 127 : v));
+        break;
+      }
+      case K_VADD_I32:
+        reinterpret_cast<int32_t*>(d)[i] = static_cast<int32_t>(
+            static_cast<uint32_t>(reinterpret_cast<const int32_t*>(a)[i]) +
+            static_cast<uint32_t>(reinterpret_cast<const int32_t*>(b)[col]));
+        break;
+      case K_DEQUANT_ADD: {
+        const float acc = __fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]), s0);
+        const float skip = __fmul_rn(static_cast<float>(reinterpret_cast<const int8_t*>(b)[i]), s1);
+        reinterpret_cast<int8_t*>(d)[i] = sat8(__fadd_rn(acc, skip));
+        break;
+      }
+      case K_DEQUANT_ACCUM:
+        reinterpret_cast<uint16_t*>(d)[i] =
+            f2h(__fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]),
+                          h2f(reinterpret_cast<const uint16_t*>(b)[col])));
+        break;
+      case K_DEQUANT_SCALED: {
+        const uint16_t* pb = reinterpret_cast<const uint16_t*>(b);
+        float v = __fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]), h2f(pb[col]));
+        v = __fmul_rn(v, s0);
+        reinterpret_cast<uint16_t*>(d)[i] = f2h(__fadd_rn(v, h2f(pb[N + col])));
+        break;
+      }
+      case K_QUANT: {
+        const float r = rintf(__fmul_rn(h2f(reinterpret_cast<const uint16_t*>(a)[i]), s0));
+        int8_t o = 0;
+        if (r == r) o = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f)));
+        reinterpret_cast<int8_t*>(d)[i] = o;
+        break;
+      }
+      case K_VADD_F16:
+        reinterpret_cast<uint16_t*>(d)[i] =
+            f2h(__fadd_rn(h2f(reinterpret_cast<const uint16_t*>(a)[i]),
+                          h2f(reinterpret_cast<const uint16_t*>(b)[i])));
+        break;
+      case K_GELU_F16:
+        reinterpret_cast<uint16_t*>(d)[i] = f2h(gelu_f32(h2f(reinterpret_cast<const uint16_t*>(a)[i])));
+        break;
+      case K_GELU_I8: {
+        const float x = (op.flags & F_SRC_I32)
+                            ? __fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]), s0)
+                            : __fmul_rn(static_cast<float>(reinterpret_cast<const int8_t*>(a)[i]), s0);
+        const float y = gelu_f32(x);
+        reinterpret_cast<int8_t*>(d)[i] = s1 == 0.f ? int8_t(0) : sat8(__fdiv_rn(y, s1));
+        break;
+      }
+      default:
+        break;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// MAX_ABS_REDUCE_FP32 (simulator.py:1088-1140): one task per sequence.
+// ---------------------------------------------------------------------------------
+__device__ void op_max_abs(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+  const uint32_t seq = t.seq0;
+  const uint64_t MN = uint64_t(op.M) * op.N;
+  const uint16_t* x = reinterpret_cast<const uint16_t*>(pptr(A, op.a, seq));
+  // |x| of FP16 values compared as bit patterns (monotone for non-NaN);
+  // any NaN wins, as np.max propagates NaN.
+  uint32_t m = 0;
+  for (uint64_t i = threadIdx.x; i < MN; i += blockDim.x) {
+    uint32_t v = x[i] & 0x7FFFu;
+    if (v > 0x7C00u) v = 0xFFFFu;  // NaN
+    m = v > m ? v : m;
+  }
+  for (int o = 16; o; o >>= 1) {
+    uint32_t w = __shfl_xor_sync(0xffffffffu, m, o);
+    m = w > m ? w : m;
+  }
+  uint32_t* red = reinterpret_cast<uint32_t*>(smem);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kWarps; ++w) m = red[w] > m ? red[w] : m;
+    uint16_t inv, fwd;
+    if (m == 0xFFFFu) {
+      inv = fwd = 0x7E00u;
+    } else {
+      double mx = static_cast<double>(h2f(static_cast<uint16_t>(m)));
+      mx = mx > 0.001953125 ? mx : 0.001953125;         // 2^-9
+      mx = mx < 4159504.0 ? mx : 4159504.0;             // 65504 * 127 / 2
+      inv = d2h(127.0 / mx);
+      fwd = d2h(mx / 127.0);
+    }
+    A.sregs[uint64_t(seq) * A.sreg_stride + op.out_slot] = inv;
+    A.sregs[uint64_t(seq) * A.sreg_stride + op.out_slot + 1] = fwd;
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------------
+// Row ops: one warp per row, 8 rows per task.
+// ---------------------------------------------------------------------------------
+struct RowCtx {
+  float* row;            // per-warp float row buffer (capacity kRowCap) or null
+  uint32_t* pw;          // per-warp pairwise scratch
+};
+constexpr uint32_t kRowCap = 2048;
+
+// float32 value of element j of row r of the op's first input.
+__device__ __forceinline__ float in_val(const ExecArgs& A, const DevOp& op, uint32_t seq, uint64_t idx,
+                                        float in_scale) {
+  const uint8_t* a = pptr(A, op.a, seq);
+  switch (op.kind) {
+    case K_LAYERNORM_F16: case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16:
+      return h2f(reinterpret_cast<const uint16_t*>(a)[idx]);
+    case K_LN_I8:
+      return __fmul_rn(static_cast<float>(reinterpret_cast<const int8_t*>(a)[idx]), in_scale);
+    default:  // legacy softmax variants: int8 or int32 input times in_scale
+      if (op.flags & F_SRC_I32)
+        return __fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[idx]), in_scale);
+      return __fmul_rn(static_cast<float>(reinterpret_cast<const int8_t*>(a)[idx]), in_scale);
+  }
+}
+
+__device__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem, uint32_t opi) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t seq = t.seq0, N = op.N;
+  const uint32_t r = t.tile * 8 + warp;
+  float* rowbuf = reinterpret_cast<float*>(smem) + warp * kRowCap;
+  uint32_t* pw = reinterpret_cast<uint32_t*>(smem + kWarps * kRowCap * 4) + warp * (3 * kPwMaxLeaves);
+  if (r >= op.M) return;
+  const bool legacy = op.kind == K_LN_I8 || op.kind == K_SOFTMAX_I8 || op.kind == K_MASKED_SOFTMAX_I8;
+  const float in_scale = legacy ? sreg_f32(A, op.s[0], seq) : 0.f;
+  const float out_scale = legacy ? sreg_f32(A, op.s[1], seq) : 0.f;
+  const uint64_t base = uint64_t(r) * N;
+  const bool buffered = N <= kRowCap;
+  // attention context
+  uint32_t qrb = op.attn_qrb, vkl = op.attn_vkl, mode = op.attn_mode;
+  if (op.flags & F_ATTN_DYN) {
+    const uint64_t v = A.params[uint64_t(seq) * A.n_params + op.param];
+    qrb = v & 0xFFFF;
+    vkl = (v >> 16) & 0xFFFF;
+    mode = (v >> 32) & 0x3;
+  }
+  auto x_at = [&](uint32_t j) -> float {
+    return buffered ? rowbuf[j] : in_val(A, op, seq, base + j, in_scale);
+  };
+  if (buffered) {
+    for (uint32_t j = lane; j < N; j += 32) rowbuf[j] = in_val(A, op, seq, base + j, in_scale);
+    __syncwarp();
+  }
+  uint8_t* d = pptr(A, op.d, seq);
+
+  if (op.kind == K_LAYERNORM_F16 || op.kind == K_LN_I8) {
+    const float eps = op.kind == K_LN_I8 ? 1e-6f : 1e-5f;
+    const float sum = warp_pairwise_sum([&](uint32_t j) { return x_at(j); }, N, pw);
+    const float mean = div_count(sum, N);
+    const float sq = warp_pairwise_sum(
+        [&](uint32_t j) { const float dd = __fsub_rn(x_at(j), mean); return __fmul_rn(dd, dd); }, N, pw);
+    const float var = div_count(sq, N);
+    const float denom = __fsqrt_rn(__fadd_rn(var, eps));
+    const uint8_t* gb = pptr(A, op.b, seq);
+    for (uint32_t j = lane; j < N; j += 32) {
+      const float y = __fdiv_rn(__fsub_rn(x_at(j), mean), denom);
+      const float g = h2f(reinterpret_cast<const uint16_t*>(gb)[j]);
+      const float b = h2f(reinterpret_cast<const uint16_t*>(gb)[N + j]);
+      const float o = __fadd_rn(__fmul_rn(y, g), b);
+      if (op.kind == K_LAYERNORM_F16) reinterpret_cast<uint16_t*>(d)[base + j] = f2h(o);
+      else reinterpret_cast<int8_t*>(d)[base + j] = out_scale == 0.f ? int8_t(0) : sat8(__fdiv_rn(o, out_scale));
+    }
+    return;
+  }
+
+  // softmax family
+  uint32_t last = N - 1;        // last visible column (FP16 masked variant)
+  bool masked_f16 = op.kind == K_MASKED_SOFTMAX_F16;
+  bool masked_i8 = op.kind == K_MASKED_SOFTMAX_I8;
+  if (masked_f16) {
+    const int64_t lt = int64_t(r) + qrb < int64_t(vkl) - 1 ? int64_t(r) + qrb : int64_t(vkl) - 1;
+    if (lt < 0) {
+      for (uint32_t j = lane; j < N; j += 32) reinterpret_cast<uint16_t*>(d)[base + j] = 0;
+      return;
+    }
+    last = static_cast<uint32_t>(lt);
+  }
+  auto visible = [&](uint32_t j) -> bool {
+    if (masked_f16) return j <= last;
+    if (masked_i8) {
+      bool v = true;
+      if (mode & 2) v = v && (j <= qrb + r);
+      if (mode & 1) v = v && (j < vkl);
+      return v;
+    }
+    return true;
+  };
+  float mx = -INFINITY;
+  for (uint32_t j = lane; j < N; j += 32)
+    if (visible(j)) mx = fmaxf(mx, x_at(j));
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  // exp values (buffered rows are overwritten in place)
+  auto e_at = [&](uint32_t j) -> float {
+    return visible(j) ? exp_f32(__fsub_rn(x_at(j), mx)) : 0.f;
+  };
+  if (buffered) {
+    __syncwarp();
+    for (uint32_t j = lane; j < N; j += 32) {
+      const float e = e_at(j);
+      __syncwarp(__activemask());
+      rowbuf[j] = e;
+    }
+    __syncwarp();
+  }
+  auto ev = [&](uint32_t j) -> float { return buffered ? rowbuf[j] : e_at(j); };
+  const float denom = warp_pairwise_sum(ev, N, pw);
+  if (masked_i8 && denom == 0.f) {
+    if (lane == 0) raise_fault(A, DF_ZERO_DENOM, 0, seq);
+  }
+  for (uint32_t j = lane; j < N; j += 32) {
+    const float e = ev(j);
+    if (op.kind == K_SOFTMAX_F16) {
+      reinterpret_cast<uint16_t*>(d)[base + j] = f2h(__fdiv_rn(e, denom));
+    } else if (masked_f16) {
+      reinterpret_cast<uint16_t*>(d)[base + j] = f2h(denom > 0.f ? __fdiv_rn(e, denom) : 0.f);
+    } else {
+      const float p = __fdiv_rn(e, denom);
+      reinterpret_cast<int8_t*>(d)[base + j] = out_scale == 0.f ? int8_t(0) : sat8(__fdiv_rn(p, out_scale));
+    }
+  }
+  (void)opi;
+}
+
+// Legacy fused softmax(QK^T)·V (sfu.py:323-443): one warp per query row.
+__device__ void op_attnv(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t seq = t.seq0, M = op.M, N = op.N, K = op.K;
+  const uint32_t r = t.tile * 8 + warp;
+  float* rowbuf = reinterpret_cast<float*>(smem) + warp * kRowCap;
+  uint32_t* pw = reinterpret_cast<uint32_t*>(smem + kWarps * kRowCap * 4) + warp * (3 * kPwMaxLeaves);
+  if (r >= M) return;
+  const float s_qkt = sreg_f32(A, op.s[0], seq), s_v = sreg_f32(A, op.s[1], seq);
+  const float s_out = sreg_f32(A, op.s[2], seq);
+  const int32_t* q = reinterpret_cast<const int32_t*>(pptr(A, op.a, seq)) + uint64_t(r) * K;
+  const int8_t* v = reinterpret_cast<const int8_t*>(pptr(A, op.b, seq));
+  int8_t* d = reinterpret_cast<int8_t*>(pptr(A, op.d, seq));
+  uint32_t qrb = op.attn_qrb, vkl = op.attn_vkl, mode = op.attn_mode;
+  if (op.flags & F_ATTN_DYN) {
+    const uint64_t pv = A.params[uint64_t(seq) * A.n_params + op.param];
+    qrb = pv & 0xFFFF;
+    vkl = (pv >> 16) & 0xFFFF;
+    mode = (pv >> 32) & 0x3;
+  }
+  const bool masked = op.kind == K_MASKED_SOFTMAX_ATTNV;
+  auto visible = [&](uint32_t j) -> bool {
+    if (!masked) return true;
+    bool vis = true;
+    if (mode & 2) vis = vis && (j <= qrb + r);
+    if (mode & 1) vis = vis && (j < vkl);
+    return vis;
+  };
+  const bool buffered = K <= kRowCap;
+  float mx = -INFINITY;
+  for (uint32_t j = lane; j < K; j += 32)
+    if (visible(j)) mx = fmaxf(mx, __fmul_rn(__int2float_rn(q[j]), s_qkt));
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  auto e_at = [&](uint32_t j) -> float {
+    return visible(j) ? exp_f32(__fsub_rn(__fmul_rn(__int2float_rn(q[j]), s_qkt), mx)) : 0.f;
+  };
+  if (buffered) {
+    for (uint32_t j = lane; j < K; j += 32) rowbuf[j] = e_at(j);
+    __syncwarp();
+  }
+  auto ev = [&](uint32_t j) -> float { return buffered ? rowbuf[j] : e_at(j); };
+  const float denom = warp_pairwise_sum(ev, K, pw);
+  if (masked && denom == 0.f && lane == 0) raise_fault(A, DF_ZERO_DENOM, 0, seq);
+  for (uint32_t n = lane; n < N; n += 32) {
+    float accv = 0.f;
+    for (uint32_t k = 0; k < K; ++k)
+      accv = __fadd_rn(accv, __fmul_rn(__fdiv_rn(ev(k), denom), __fmul_rn(static_cast<float>(v[uint64_t(k) * N + n]), s_v)));
+    d[uint64_t(r) * N + n] = s_out == 0.f ? int8_t(0) : sat8(__fdiv_rn(accv, s_out));
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Grid barrier with a bounded wait.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ bool grid_barrier(const ExecArgs& A) {
+  __syncthreads();
+  __shared__ uint32_t ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    volatile uint32_t* gen = A.barrier + 1;
+    const uint32_t g = *gen;
+    __threadfence();
+    const uint32_t arrived = atomicAdd(A.barrier, 1u);
+    if (arrived == gridDim.x - 1) {
+      atomicExch(A.barrier, 0u);
+      __threadfence();
+      atomicAdd(A.barrier + 1, 1u);
+    } else {
+      uint32_t spins = 0;
+      while (*gen == g) {
+        if (++spins > kBarrierSpinLimit) {
+          raise_fault(A, DF_BARRIER_TIMEOUT, 0, 0);
+          break;
+        }
+        if (spins > 64) __nanosleep(64);
+      }
+    }
+    __threadfence();
+    if (*reinterpret_cast<volatile uint32_t*>(A.status) != 0) ok = 0;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem) {
+  const Task t = A.tasks[ti];
+  const DevOp& op = A.ops[t.op];
+  switch (op.kind) {
+    case K_GATHER: op_gather(A, op, t); break;
+    case K_DYN_LOAD:
+    case K_DYN_STORE: op_dyn_copy(A, op, t, t.op); break;
+    case K_SREG_LOAD: op_sreg_load(A, op, t); break;
+    case K_SREG_FINAL: op_sreg_final(A, op, t); break;
+    case K_MATMUL: op_matmul(A, op, t, smem); break;
+    case K_TRANSPOSE: op_transpose(A, op, t); break;
+    case K_MAX_ABS: op_max_abs(A, op, t, smem); break;
+    case K_LAYERNORM_F16: case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16:
+    case K_LN_I8: case K_SOFTMAX_I8: case K_MASKED_SOFTMAX_I8:
+      op_rows(A, op, t, smem, t.op);
+      break;
+    case K_SOFTMAX_ATTNV: case K_MASKED_SOFTMAX_ATTNV: op_attnv(A, op, t, smem); break;
+    case K_REQUANT: case K_REQUANT_PC: case K_SCALE_MUL_I32: case K_SCALE_MUL_I8:
+    case K_VADD_I8: case K_VADD_I32: case K_DEQUANT_ADD: case K_DEQUANT_ACCUM:
+    case K_DEQUANT_SCALED: case K_QUANT: case K_VADD_F16: case K_GELU_F16: case K_GELU_I8:
+      op_elementwise(A, op, t);
+      break;
+    default:
+      if (threadIdx.x == 0) raise_fault(A, DF_BAD_OP, t.op, t.seq0);
+      break;
+  }
+  __syncthreads();
+}
+
+// Shared memory: max(MATMUL tiles, row buffers + pairwise scratch).
+constexpr size_t kExecSmem =
+    (kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4) > (8 * 16 * kMmAStride + 64 * kMmBStride)
+        ? (kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4)
+        : (8 * 16 * kMmAStride + 64 * kMmBStride);
+
+__global__ void __launch_bounds__(kThreads, 1) exec_kernel(ExecArgs A) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  for (uint32_t L = 0; L < A.n_levels; ++L) {
+    const uint32_t t0 = A.level_off[L], t1 = A.level_off[L + 1];
+    for (uint32_t ti = t0 + blockIdx.x; ti < t1; ti += gridDim.x) run_task(A, ti, smem);
+    if (L + 1 < A.n_levels) {
+      if (!grid_barrier(A)) return;
+      if (threadIdx.x == 0 && blockIdx.x == 0) A.status[3] = L + 1;
+    }
+  }
+}
+
+// Greedy argmax over FP16 logits (np.argmax: first maximal index; NaN wins).
+__global__ void argmax_f16_kernel(const uint8_t* seq_base, uint64_t seq_stride, const uint8_t* shared_base,
+                                  uint64_t shared_bytes, uint64_t addr, uint64_t count, int32_t* out) {
+  const uint32_t seq = blockIdx.x;
+  const uint16_t* x = reinterpret_cast<const uint16_t*>(
+      addr < shared_bytes ? shared_base + addr
+                          : seq_base + uint64_t(seq) * seq_stride + uint64_t(kSramUnits) * 16 + (addr - shared_bytes));
+  float best = -INFINITY;
+  uint32_t bi = 0xFFFFFFFFu;
+  bool nan_seen = false;
+  uint32_t nan_i = 0xFFFFFFFFu;
+  for (uint32_t i = threadIdx.x; i < count; i += blockDim.x) {
+    const float v = h2f(x[i]);
+    if (v != v) {
+      if (i < nan_i) nan_i = i;
+      nan_seen = true;
+    } else if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  __shared__ float sb[1024];
+  __shared__ uint32_t si[1024], sn[1024];
+  sb[threadIdx.x] = best;
+  si[threadIdx.x] = bi;
+  sn[threadIdx.x] = nan_seen ? nan_i : 0xFFFFFFFFu;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = -INFINITY;
+    uint32_t idx = 0xFFFFFFFFu, ni = 0xFFFFFFFFu;
+    for (uint32_t k = 0; k < blockDim.x; ++k) {
+      if (sn[k] < ni) ni = sn[k];
+      if (si[k] == 0xFFFFFFFFu) continue;
+      if (sb[k] > b || (sb[k] == b && si[k] < idx)) { b = sb[k]; idx = si[k]; }
+    }
+    if (ni != 0xFFFFFFFFu) idx = ni;
+    if (idx == 0xFFFFFFFFu) idx = 0;
+    out[seq] = static_cast<int32_t>(idx);
+  }
+}
+
+}  // namespace tac

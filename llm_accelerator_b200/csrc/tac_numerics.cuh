@@ -1,0 +1,205 @@
+// Device-side arithmetic that reproduces the golden model's NumPy semantics.
+//
+// Rules (each mirrors a NumPy behaviour the golden simulator relies on):
+//  * float32 arithmetic is IEEE round-to-nearest with no FMA contraction
+//    (explicit __fmul_rn / __fadd_rn / __fdiv_rn / __fsqrt_rn);
+//  * int32 -> float32 rounds to nearest (__int2float_rn);
+//  * np.round is round-half-to-even (rintf);
+//  * float32 -> float16 rounds to nearest even, overflow to inf;
+//  * float64 -> float16 converts directly (cvt.rn.f16.f64), as np.float16(python float);
+//  * float32 row sums follow NumPy's pairwise summation (8 accumulators per
+//    leaf of <= 128 elements, halving split rounded to a multiple of 8) with
+//    the additive identity as the initial value;
+//  * mean / var divide in float64 and round to float32 (true_divide of a
+//    float32 array by an intp count with out=float32);
+//  * int8 casts of clipped values send NaN to 0; the int32 clip path sends
+//    NaN and values >= 2^31 to INT32_MIN (x86 cvttss2si behaviour).
+// exp, tanh and x**3 are evaluated in float64 and rounded once to float32;
+// NumPy's own float32 SIMD versions are not correctly rounded, so these
+// paths agree with the golden model to within one float32 ulp before the
+// final FP16 rounding rather than bit-for-bit.
+#pragma once
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace tac {
+
+__device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+__device__ __forceinline__ uint16_t d2h(double d) {
+  uint16_t h;
+  asm("cvt.rn.f16.f64 %0, %1;" : "=h"(h) : "d"(d));
+  return h;
+}
+
+// np.clip(np.round(v), -128, 127).astype(np.int8)
+__device__ __forceinline__ int8_t sat8(float v) {
+  float r = rintf(v);
+  if (r != r) return 0;
+  r = fminf(fmaxf(r, -128.f), 127.f);
+  return static_cast<int8_t>(static_cast<int>(r));
+}
+
+// np.clip(np.round(v), int32.min, int32.max).astype(np.int32) for float32 v
+__device__ __forceinline__ int32_t sat32(float v) {
+  float r = rintf(v);
+  if (r != r || r >= 2147483648.f) return INT32_MIN;
+  if (r <= -2147483648.f) return INT32_MIN;
+  return static_cast<int32_t>(r);
+}
+
+__device__ __forceinline__ float exp_f32(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
+__device__ __forceinline__ float tanh_f32(float x) { return static_cast<float>(tanh(static_cast<double>(x))); }
+__device__ __forceinline__ float cube_f32(float x) {
+  double d = static_cast<double>(x);
+  return static_cast<float>(d * d * d);
+}
+
+// tanh-approximation GELU in the operation order of simulator.py:955-960.
+__device__ __forceinline__ float gelu_f32(float x) {
+  const float c = 0.7978845608028654f;   // np.float32(np.sqrt(2 / pi))
+  const float k = 0.044715f;
+  float inner = __fmul_rn(c, __fadd_rn(x, __fmul_rn(k, cube_f32(x))));
+  return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, tanh_f32(inner)));
+}
+
+// ---- NumPy pairwise summation -------------------------------------------------
+constexpr int kPwMaxLeaves = 256;
+
+// Leaves of the pairwise tree over n elements, left to right.
+__device__ inline int pw_leaves(uint32_t n, uint32_t* loff, uint32_t* llen) {
+  uint32_t so[24], sn[24];
+  int sp = 0, nl = 0;
+  so[sp] = 0;
+  sn[sp] = n;
+  ++sp;
+  while (sp) {
+    --sp;
+    uint32_t o = so[sp], m = sn[sp];
+    if (m <= 128) {
+      if (nl < kPwMaxLeaves) { loff[nl] = o; llen[nl] = m; }
+      ++nl;
+    } else {
+      uint32_t h = m / 2;
+      h -= h % 8;
+      so[sp] = o + h; sn[sp] = m - h; ++sp;   // right (processed second)
+      so[sp] = o;     sn[sp] = h;     ++sp;   // left
+    }
+  }
+  return nl;
+}
+
+template <class Get>
+__device__ inline float pw_leaf(const Get& get, uint32_t o, uint32_t m) {
+  if (m < 8) {
+    float r = -0.0f;
+    for (uint32_t i = 0; i < m; ++i) r = __fadd_rn(r, get(o + i));
+    return r;
+  }
+  float r[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) r[j] = get(o + j);
+  uint32_t i = 8;
+  for (; i < m - (m % 8); i += 8) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = __fadd_rn(r[j], get(o + i + j));
+  }
+  float res = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
+                        __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
+  for (; i < m; ++i) res = __fadd_rn(res, get(o + i));
+  return res;
+}
+
+// Combines leaf sums in the tree's order (post-order walk of the same split).
+__device__ inline float pw_combine(uint32_t n, const float* leaf) {
+  uint32_t sn[24];
+  uint8_t st[24];
+  float vals[24];
+  int sp = 0, vp = 0, li = 0;
+  sn[sp] = n; st[sp] = 0; ++sp;
+  while (sp) {
+    uint32_t m = sn[sp - 1];
+    if (m <= 128) {
+      vals[vp++] = leaf[li++];
+      --sp;
+      continue;
+    }
+    uint32_t h = m / 2;
+    h -= h % 8;
+    if (st[sp - 1] == 0) {
+      st[sp - 1] = 1;
+      sn[sp] = h; st[sp] = 0; ++sp;
+    } else if (st[sp - 1] == 1) {
+      st[sp - 1] = 2;
+      sn[sp] = m - h; st[sp] = 0; ++sp;
+    } else {
+      float r = vals[--vp];
+      float l = vals[--vp];
+      vals[vp++] = __fadd_rn(l, r);
+      --sp;
+    }
+  }
+  return vals[0];
+}
+
+// Warp-cooperative np.sum(row) for a float32 row of n elements; every lane
+// returns the result.  `scratch` holds kPwMaxLeaves*3 words per warp.
+template <class Get>
+__device__ inline float warp_pairwise_sum(const Get& get, uint32_t n, uint32_t* scratch) {
+  const int lane = threadIdx.x & 31;
+  uint32_t* loff = scratch;
+  uint32_t* llen = scratch + kPwMaxLeaves;
+  float* lsum = reinterpret_cast<float*>(scratch + 2 * kPwMaxLeaves);
+  int nl = 0;
+  if (lane == 0) nl = pw_leaves(n, loff, llen);
+  nl = __shfl_sync(0xffffffffu, nl, 0);
+  __syncwarp();
+  float total = 0.f;
+  if (nl <= kPwMaxLeaves) {
+    for (int l = lane; l < nl; l += 32) lsum[l] = pw_leaf(get, loff[l], llen[l]);
+    __syncwarp();
+    if (lane == 0) total = __fadd_rn(0.0f, pw_combine(n, lsum));
+  } else if (lane == 0) {
+    // Rows with more leaves than the scratch holds: lane 0 walks the tree.
+    uint32_t so[24], sn[24];
+    uint8_t st[24];
+    float vals[24];
+    int sp = 0, vp = 0;
+    uint32_t off = 0;
+    so[sp] = 0; sn[sp] = n; st[sp] = 0; ++sp;
+    while (sp) {
+      uint32_t m = sn[sp - 1];
+      if (m <= 128) {
+        vals[vp++] = pw_leaf(get, so[sp - 1], m);
+        --sp;
+        continue;
+      }
+      uint32_t h = m / 2;
+      h -= h % 8;
+      off = so[sp - 1];
+      if (st[sp - 1] == 0) {
+        st[sp - 1] = 1;
+        so[sp] = off; sn[sp] = h; st[sp] = 0; ++sp;
+      } else if (st[sp - 1] == 1) {
+        st[sp - 1] = 2;
+        so[sp] = off + h; sn[sp] = m - h; st[sp] = 0; ++sp;
+      } else {
+        float r = vals[--vp];
+        float l = vals[--vp];
+        vals[vp++] = __fadd_rn(l, r);
+        --sp;
+      }
+    }
+    total = __fadd_rn(0.0f, vals[0]);
+  }
+  total = __shfl_sync(0xffffffffu, total, 0);
+  __syncwarp();
+  return total;
+}
+
+// float32 mean / variance divisor: f32(f64(sum) / n)
+__device__ __forceinline__ float div_count(float s, uint32_t n) {
+  return static_cast<float>(static_cast<double>(s) / static_cast<double>(n));
+}
+
+}  // namespace tac

@@ -1,0 +1,107 @@
+// Execution plan shared by the host compiler (tac_compile.cpp) and the device
+// executor (tac_exec.cu).
+//
+// A taccel instruction stream is straight-line code (the ISA has no branches),
+// so every address, tile shape and register value except a few runtime-patched
+// words is known before execution.  The compiler walks the stream once and
+// tracks, for every 16-byte unit of SRAM and of writable DRAM, the physical
+// location that holds its current value:
+//   * LOAD / STORE / flat BUF_COPY only move pointers (no device work),
+//   * every compute instruction writes a fresh extent of a per-sequence arena
+//     (so SRAM reuse never creates write-after-read hazards),
+//   * reads whose units are not physically contiguous get one gather op.
+// Device ops are then grouped into dependency levels; ops in one level are
+// independent and run concurrently, levels are separated by a grid barrier.
+#pragma once
+#include <cstdint>
+
+namespace tac {
+
+// Physical addresses are counted in 16-byte units.  Bit 63 set: the shared
+// read-only DRAM image (weights, tables), identical for every sequence.
+// Otherwise: an offset inside the per-sequence block, laid out as
+//   [SRAM home: ABUF | WBUF | ACCUM][writable DRAM home][arena].
+constexpr uint64_t kSharedBit = 1ull << 63;
+
+// Scale-register operands.  Bit 31 set: an FP16 constant in the low 16 bits.
+// Otherwise an index into the per-sequence register file: 0..15 are the
+// architectural registers, 16.. are renamed slots written during the run.
+constexpr uint32_t kSregConst = 1u << 31;
+constexpr uint32_t kSregSlotBase = 16;
+
+enum DevKind : uint16_t {
+  K_GATHER = 1,            // copy a list of unit segments
+  K_DYN_LOAD,              // arena <- DRAM at (runtime register + constant)
+  K_DYN_STORE,             // writable DRAM at (runtime register + constant) <- arena
+  K_SREG_LOAD,             // register slot <- 2 bytes of SRAM (SET_SCALE from buffer)
+  K_SREG_FINAL,            // write the architectural registers at the end of a run
+  K_MATMUL,                // int8 x int8 -> int32 (optionally + previous int32)
+  K_REQUANT,               // int32 * scalar -> int8
+  K_REQUANT_PC,            // int32 * per-column FP16 -> int8
+  K_SCALE_MUL_I32,         // int32 * scalar -> int32
+  K_SCALE_MUL_I8,          // int8 * scalar -> int8
+  K_VADD_I8,               // saturating int8 add
+  K_VADD_I32,              // int32 + broadcast int32 row
+  K_DEQUANT_ADD,           // int32*s0 + int8*s1 -> int8
+  K_DEQUANT_ACCUM,         // int32 * per-column FP16 -> FP16
+  K_DEQUANT_SCALED,        // int32 * per-column FP16 * scalar + bias -> FP16
+  K_QUANT,                 // FP16 * scalar -> int8 (NaN -> 0)
+  K_VADD_F16,              // FP16 + FP16 -> FP16
+  K_LAYERNORM_F16,         // row LayerNorm, eps 1e-5
+  K_GELU_F16,              // tanh GELU
+  K_SOFTMAX_F16,           // row softmax
+  K_MASKED_SOFTMAX_F16,    // causal / padded row softmax
+  K_MAX_ABS,               // max |x| -> two FP16 scale slots
+  K_TRANSPOSE,             // int8 [rows, cols] -> [cols, rows]
+  K_LN_I8,                 // legacy INT8-I/O LayerNorm (eps 1e-6)
+  K_SOFTMAX_I8,            // legacy INT8-I/O softmax (src int8 or int32)
+  K_MASKED_SOFTMAX_I8,     // legacy INT8-I/O masked softmax
+  K_GELU_I8,               // legacy INT8-I/O GELU
+  K_SOFTMAX_ATTNV,         // legacy fused softmax(QK^T) @ V -> int8
+  K_MASKED_SOFTMAX_ATTNV,  // legacy fused masked softmax(QK^T) @ V -> int8
+  K_NUM_KINDS
+};
+
+// Flags on DevOp::flags.
+constexpr uint16_t F_ACCUMULATE = 1;   // MATMUL adds the previous int32 tile (operand c)
+constexpr uint16_t F_SRC_I32 = 2;      // legacy SFU input is int32 (ACCUM) rather than int8
+constexpr uint16_t F_ATTN_DYN = 4;     // masked softmax context comes from a runtime parameter
+
+struct DevOp {
+  uint16_t kind;
+  uint16_t flags;
+  uint32_t M, N, K;        // element dimensions (rows, cols, reduction)
+  uint64_t a, b, c, d;     // physical unit addresses: src1, src2, extra input, destination
+  uint32_t s[4];           // scale-register operands
+  uint32_t out_slot;       // first renamed register slot written (MAX_ABS, SET_SCALE)
+  uint32_t seg0, nseg;     // K_GATHER: segment range; K_SREG_FINAL: unused
+  int32_t param;           // runtime parameter index (dynamic address / attention context)
+  uint32_t attn_mode;
+  int64_t dconst;          // byte constant added to the runtime address
+  uint64_t nbytes;         // bytes moved by dynamic copies
+  uint32_t attn_qrb, attn_vkl;
+  uint32_t pc;             // instruction that produced the op (for error reports)
+  uint32_t level;
+};
+
+struct Segment {
+  uint64_t src;   // physical unit address
+  uint64_t dst;   // physical unit address
+  uint64_t n;     // units
+};
+
+struct Task {
+  uint32_t op;
+  uint32_t seq0;   // first sequence
+  uint32_t nseq;   // sequences covered
+  uint32_t tile;   // op-specific tile index
+};
+
+// Parameters decoded from runtime-patched instruction words, one set per
+// sequence.  Address parameters hold the 56-bit register value; attention
+// parameters pack query_row_base | valid_kv_len << 16 | mode << 32.
+struct RunParam {
+  uint64_t value;
+};
+
+}  // namespace tac

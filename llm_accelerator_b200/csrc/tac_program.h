@@ -1,0 +1,65 @@
+// Host-side representation of a compiled stream (shared by the compiler and
+// the CUDA engine).
+#pragma once
+#include <cstdint>
+#include <vector>
+
+#include "../../include/taccel_b200.h"
+#include "tac_isa.h"
+#include "tac_plan.h"
+
+namespace tac {
+
+// One runtime-patched site, in the order the caller listed them.
+struct VarInfo {
+  uint32_t kind;        // 0: SET_ADDR pair, 1: CONFIG_ATTN
+  uint32_t addr_reg;
+  uint64_t lo_pc, hi_pc;
+  uint64_t range_lo, range_hi;
+  uint32_t word0;       // index of the site's first word in a sequence's var-word row
+  uint64_t base_lo, base_hi;  // compile-time words (opcode / register must not change)
+};
+
+// A condition on runtime parameters that the compiler could not decide.
+enum CheckKind : uint32_t {
+  CHK_ADDR = 1,        // param + dconst is 16-byte aligned and lies in [lo, hi)
+  CHK_ATTN_SET = 2,    // CONFIG_ATTN: mode != 0 and valid_kv_len != 0
+  CHK_ATTN_KEYS = 3,   // masked softmax: context fits `key_cols` columns
+};
+
+struct RtCheck {
+  uint32_t kind;
+  uint32_t param;
+  uint64_t pc;
+  int64_t dconst;
+  uint64_t lo, hi;     // CHK_ADDR: allowed start range; CHK_ATTN_KEYS: lo = key columns
+  uint64_t nbytes;
+};
+
+}  // namespace tac
+
+struct tac_program {
+  int batch = 1;
+  uint64_t dram_bytes = 0, shared_bytes = 0;
+  std::vector<tac::DevOp> ops;
+  std::vector<tac::Segment> segs;
+  std::vector<tac::Task> tasks;
+  std::vector<uint32_t> level_off;
+  std::vector<tac::VarInfo> vars;
+  std::vector<tac::RtCheck> checks;
+  uint32_t n_var_words = 0;
+  uint32_t n_params = 0;
+  uint64_t arena_units = 0;
+  uint32_t n_slots = 0;
+  tac_exec_info info{};
+  tac_fault fault{};
+  // Device mirror (filled by the engine on first use).
+  int device = -1;
+  void* d_blob = nullptr;
+  uint64_t off_ops = 0, off_segs = 0, off_tasks = 0, off_levels = 0;
+};
+
+namespace tac {
+// Layout constants of the per-sequence block, in 16-byte units.
+inline uint64_t rw_base_units() { return kSramUnits; }
+}  // namespace tac

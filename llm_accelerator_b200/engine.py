@@ -1,0 +1,159 @@
+"""Thin object wrapper over the C ABI: an engine (device machine state for a
+batch of sequences) and compiled programs."""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib as L
+from .errors import EngineError
+
+_lib = L.lib
+
+# numpy views of the plan records (layout of tac::DevOp / Segment / Task)
+DEVOP_DTYPE = np.dtype([
+    ("kind", "<u2"), ("flags", "<u2"), ("M", "<u4"), ("N", "<u4"), ("K", "<u4"),
+    ("a", "<u8"), ("b", "<u8"), ("c", "<u8"), ("d", "<u8"), ("s", "<u4", (4,)),
+    ("out_slot", "<u4"), ("seg0", "<u4"), ("nseg", "<u4"), ("param", "<i4"), ("attn_mode", "<u4"),
+    ("_pad", "<u4"), ("dconst", "<i8"), ("nbytes", "<u8"), ("attn_qrb", "<u4"), ("attn_vkl", "<u4"),
+    ("pc", "<u4"), ("level", "<u4")])
+SEGMENT_DTYPE = np.dtype([("src", "<u8"), ("dst", "<u8"), ("n", "<u8")])
+TASK_DTYPE = np.dtype([("op", "<u4"), ("seq0", "<u4"), ("nseq", "<u4"), ("tile", "<u4")])
+
+
+@dataclass
+class Site:
+    """A runtime-patched word: kind 0 = SET_ADDR pair, 1 = CONFIG_ATTN."""
+    kind: int
+    addr_reg: int
+    lo_pc: int
+    hi_pc: int = 0
+    range_lo: int = 0
+    range_hi: int = 0
+
+
+class Program:
+    def __init__(self, handle, info: L.ExecInfo, fault: L.Fault, n_var_words: int):
+        self.handle = handle
+        self.info = info
+        self.fault = fault
+        self.n_var_words = n_var_words
+
+    def __del__(self):
+        h, self.handle = getattr(self, "handle", None), None
+        if h:
+            _lib.tac_program_destroy(h)
+
+    def dump(self):
+        """(ops, segments, tasks, level_offsets) as numpy structured arrays."""
+        i = self.info
+        assert _lib.tac_program_record_size(0) == DEVOP_DTYPE.itemsize
+        ops = np.zeros(i.n_ops, DEVOP_DTYPE)
+        segs = np.zeros(i.n_segments, SEGMENT_DTYPE)
+        tasks = np.zeros(i.n_tasks, TASK_DTYPE)
+        lv = np.zeros(i.n_levels + 1, np.uint32)
+        L.check(_lib.tac_program_dump(self.handle, ops.ctypes.data, segs.ctypes.data, tasks.ctypes.data,
+                                      lv.ctypes.data), "tac_program_dump")
+        return ops, segs, tasks, lv
+
+
+def compile_program(batch: int, dram_bytes: int, shared_bytes: int, region: bytes, entry_pc: int,
+                    max_insns: int, regs: L.Regs, sregs_reset: bool, sites=()) -> Program:
+    """Plans an instruction region; raises only when the stream cannot be
+    planned at all (a faulting stream still yields a program)."""
+    n = len(region) // 8
+    buf = C.create_string_buffer(bytes(region), len(region))
+    arr = (L.VarSite * max(1, len(sites)))()
+    for k, s in enumerate(sites):
+        arr[k] = L.VarSite(s.kind, s.addr_reg, s.lo_pc, s.hi_pc, s.range_lo, s.range_hi)
+    h = C.c_void_p()
+    info, fault = L.ExecInfo(), L.Fault()
+    st = _lib.tac_compile(batch, dram_bytes, shared_bytes, buf, n, entry_pc, max_insns, C.byref(regs),
+                          1 if sregs_reset else 0, arr, len(sites), C.byref(h), C.byref(info), C.byref(fault))
+    if st != L.OK:
+        raise L.fault_to_exception(fault, st)
+    return Program(h, info, fault, int(info.n_var_words))
+
+
+class Engine:
+    """Device machine state for `batch` sequences (one GPU)."""
+
+    def __init__(self, batch: int, dram_bytes: int, shared_bytes: int = 0, device: int = 0):
+        h = C.c_void_p()
+        st = _lib.tac_engine_create(device, batch, dram_bytes, shared_bytes, C.byref(h))
+        if st != L.OK:
+            raise EngineError(f"tac_engine_create failed with status {st} (no usable sm_100 GPU?)")
+        self.handle = h
+        self.batch, self.dram_bytes, self.shared_bytes, self.device = batch, dram_bytes, shared_bytes, device
+
+    def close(self):
+        h, self.handle = getattr(self, "handle", None), None
+        if h:
+            _lib.tac_engine_destroy(h)
+
+    __del__ = close
+
+    # ---- memory ----------------------------------------------------------------------
+    def write_dram(self, seq: int, addr: int, data) -> None:
+        b = bytes(data)
+        L.check(_lib.tac_dram_write(self.handle, seq, addr, b, len(b)), "tac_dram_write")
+
+    def read_dram(self, seq: int, addr: int, n: int) -> bytes:
+        out = C.create_string_buffer(n)
+        L.check(_lib.tac_dram_read(self.handle, seq, addr, out, n), "tac_dram_read")
+        return out.raw
+
+    def write_sram(self, seq: int, buf: int, off: int, data) -> None:
+        b = bytes(data)
+        L.check(_lib.tac_sram_write(self.handle, seq, buf, off, b, len(b)), "tac_sram_write")
+
+    def read_sram(self, seq: int, buf: int, off: int, n: int) -> bytes:
+        out = C.create_string_buffer(n)
+        L.check(_lib.tac_sram_read(self.handle, seq, buf, off, out, n), "tac_sram_read")
+        return out.raw
+
+    def read_sregs(self, seq: int) -> np.ndarray:
+        a = np.zeros(16, np.uint16)
+        L.check(_lib.tac_sregs_read(self.handle, seq, a.ctypes.data), "tac_sregs_read")
+        return a
+
+    def write_sregs(self, seq: int, bits) -> None:
+        a = np.ascontiguousarray(np.asarray(bits, dtype=np.uint16).reshape(16))
+        L.check(_lib.tac_sregs_write(self.handle, seq, a.ctypes.data), "tac_sregs_write")
+
+    # ---- execution --------------------------------------------------------------------
+    def run(self, prog: Program, var_words=None) -> int:
+        """Runs a program on every sequence; returns the status (0 or the
+        stream's own fault) and raises on engine / device failures."""
+        vw = None
+        if prog.n_var_words:
+            vw = np.ascontiguousarray(np.asarray(var_words, dtype=np.uint64).reshape(self.batch, prog.n_var_words))
+        f = L.Fault()
+        st = _lib.tac_run(self.handle, prog.handle, None if vw is None else vw.ctypes.data, C.byref(f))
+        self._last_fault = f
+        return st
+
+    def run_async(self, prog: Program, var_words, stream=None) -> None:
+        vw = None
+        if prog.n_var_words:
+            vw = np.ascontiguousarray(np.asarray(var_words, dtype=np.uint64).reshape(self.batch, prog.n_var_words))
+        f = L.Fault()
+        st = _lib.tac_run_async(self.handle, prog.handle, None if vw is None else vw.ctypes.data, stream, C.byref(f))
+        if st != L.OK and not (prog.info.faulted and st == prog.fault.status):
+            raise L.fault_to_exception(f, st)
+
+    def check_device(self) -> None:
+        f = L.Fault()
+        st = _lib.tac_check_device_status(self.handle, C.byref(f))
+        if st != L.OK:
+            raise L.fault_to_exception(f, st)
+
+    def argmax_f16(self, addr: int, count: int, out_dev_ptr: int, stream=None) -> None:
+        L.check(_lib.tac_argmax_f16(self.handle, addr, count, out_dev_ptr, stream), "tac_argmax_f16")
+
+    def layout(self):
+        sb, ss, sh = C.c_void_p(), C.c_uint64(), C.c_void_p()
+        L.check(_lib.tac_engine_layout(self.handle, C.byref(sb), C.byref(ss), C.byref(sh)), "tac_engine_layout")
+        return sb.value, ss.value, sh.value

@@ -1,0 +1,208 @@
+"""Host runners for decoder ProgramBundles.
+
+``HostRunner`` mirrors ``taccel.runtime.host_runner.HostRunner``
+(``software/taccel/runtime/host_runner.py:12-123``): it patches the
+runtime sites of a bundle (token / position embedding rows, KV-cache base,
+attention context), runs the prefill or decode stream on a simulator and reads
+the logits back.  It defaults to ``B200Simulator``.
+
+``BatchedRunner`` is the B200-native form of the same loop: B independent
+sequences share one compiled plan per stream and one read-only copy of the
+weights; each sequence's patched words are passed as runtime parameters, the
+greedy argmax runs on the GPU, and only token ids cross PCIe per step.
+"""
+from __future__ import annotations
+
+from typing import Iterable, List, Optional, Sequence
+
+import numpy as np
+
+from . import _lib as L
+from . import isa
+from .bundle import ProgramBundle
+from .engine import Engine, Site, compile_program
+
+
+class HostRunner:
+    def __init__(self, bundle, simulator=None, *, logits_dtype=np.int32):
+        if simulator is None:
+            from .simulator import B200Simulator
+            simulator = B200Simulator()
+        self.bundle = bundle
+        self.simulator = simulator
+        self.logits_dtype = np.dtype(logits_dtype)
+        self.simulator.load_bundle(bundle)
+
+    def _sites(self, kind: str, stream: str):
+        return [s for s in self.bundle.runtime_patch_sites if s.kind == kind and s.stream == stream]
+
+    def _patch_sites(self, kind: str, stream: str, offsets: Sequence[int]) -> None:
+        sites = self._sites(kind, stream)
+        if not sites:
+            return
+        if len(sites) == 1 and len(offsets) != 1:
+            raise ValueError(f"Runtime site kind={kind!r} stream={stream!r} supports one row, "
+                             f"got {len(offsets)} offsets")
+        if len(sites) != len(offsets):
+            raise ValueError(f"Expected {len(sites)} offsets for kind={kind!r} stream={stream!r}, "
+                             f"got {len(offsets)}")
+        for site, off in zip(sites, offsets):
+            self.bundle.patch_runtime_site(site, int(off))
+
+    def _patch_embeddings(self, stream: str, token_ids, position_ids) -> None:
+        row = int(self.bundle.embedding_row_bytes)
+        self._patch_sites("token_embed", stream, [int(t) * row for t in token_ids])
+        self._patch_sites("pos_embed", stream, [int(p) * row for p in position_ids])
+
+    def _patch_kv_bases(self, position: int) -> None:
+        off = int(position) * int(self.bundle.kv_step_bytes)
+        for site in self._sites("kv_base", "decode"):
+            self.bundle.patch_runtime_site(site, off)
+
+    def _patch_decode_attention_context(self, position: int) -> None:
+        for site in self.bundle.runtime_config_attn_sites:
+            if site.stream == "decode":
+                self.bundle.patch_config_attn_site(site, query_row_base=int(position),
+                                                   valid_kv_len=int(position) + 1)
+
+    def _read_logits(self, offset: int) -> np.ndarray:
+        size = int(self.bundle.logits_size)
+        if size <= 0:
+            return np.asarray([], dtype=self.logits_dtype)
+        if size % self.logits_dtype.itemsize:
+            raise ValueError(f"logits_size={size} is not divisible by dtype size {self.logits_dtype.itemsize}")
+        data = bytes(self.simulator.state.dram[int(offset):int(offset) + size])
+        return np.frombuffer(data, dtype=self.logits_dtype).copy()
+
+    def run_prefill(self, token_ids: Iterable[int], *, max_instructions: int = 10_000_000) -> np.ndarray:
+        tokens = [int(t) for t in token_ids]
+        if not tokens:
+            raise ValueError("run_prefill requires at least one token")
+        self._patch_embeddings("prefill", tokens, list(range(len(tokens))))
+        self.simulator.run_program(self.bundle, "prefill", max_instructions=max_instructions)
+        return self._read_logits(self.bundle.prefill_logits_offset)
+
+    def run_decode_step(self, token_id: int, position: int, *, max_instructions: int = 10_000_000) -> np.ndarray:
+        if position < 0:
+            raise ValueError("position must be non-negative")
+        self._patch_embeddings("decode", [int(token_id)], [int(position)])
+        self._patch_kv_bases(int(position))
+        self._patch_decode_attention_context(int(position))
+        self.simulator.run_program(self.bundle, "decode", max_instructions=max_instructions)
+        return self._read_logits(self.bundle.decode_logits_offset)
+
+    @staticmethod
+    def _greedy_token(logits: np.ndarray) -> int:
+        return 0 if logits.size == 0 else int(np.argmax(logits))
+
+    def generate(self, prompt_ids: Sequence[int], max_new_tokens: int, *, sampler: str = "greedy",
+                 eos_token_id: Optional[int] = None) -> List[int]:
+        if sampler != "greedy":
+            raise ValueError("Stage 3 HostRunner only supports greedy sampling")
+        if max_new_tokens < 0:
+            raise ValueError("max_new_tokens must be non-negative")
+        if not prompt_ids:
+            raise ValueError("generate requires at least one prompt token")
+        generated = [int(t) for t in prompt_ids]
+        nxt = self._greedy_token(self.run_prefill(generated))
+        for _ in range(max_new_tokens):
+            generated.append(nxt)
+            if eos_token_id is not None and nxt == eos_token_id:
+                break
+            nxt = self._greedy_token(self.run_decode_step(nxt, len(generated) - 1))
+        return generated
+
+
+class BatchedRunner:
+    """Runs B independent sequences of one decoder bundle on one GPU.
+
+    Sequence s keeps its own SRAM, temp, KV-cache and logits regions; the
+    instruction streams and the shared data (weights, embeddings, tables) are
+    held once.  Each step takes one token and one position per sequence."""
+
+    def __init__(self, bundle, batch: int, *, device: int = 0):
+        b = ProgramBundle.from_any(bundle)
+        self.bundle, self.batch, self.device = b, int(batch), device
+        image = b.materialize(reset_runtime=True)
+        self.dram_bytes = max(16 * 1024 * 1024, b.required_dram_bytes)
+        self.shared_bytes = (b.temp_base // 16) * 16
+        self.engine = Engine(self.batch, self.dram_bytes, self.shared_bytes, device)
+        self.engine.write_dram(-1, 0, image[:self.shared_bytes])
+        tail = image[self.shared_bytes:]
+        if any(tail):
+            self.engine.write_dram(-1, self.shared_bytes, tail)
+        self.region = bytes(b.instruction_region())
+        self.logits_count = int(b.logits_size) // 2
+        self.plans = {}
+        self._sites = {}
+        for name in ("prefill", "decode"):
+            sites, meta = [], []
+            for s in b.runtime_patch_sites:
+                if s.stream == name:
+                    lo, hi = b.symbol_extent(s.base_symbol)
+                    sites.append(Site(0, s.addr_reg, s.absolute_lo_pc, s.absolute_hi_pc, lo, hi))
+                    meta.append(("addr", s))
+            for s in b.runtime_config_attn_sites:
+                if s.stream == name:
+                    sites.append(Site(1, 0, s.absolute_pc))
+                    meta.append(("attn", s))
+            self._sites[name] = (sites, meta)
+            entry = b.prefill_pc if name == "prefill" else b.decode_pc
+            masked = bytearray(self.region)
+            for site in sites:
+                for pc in ((site.lo_pc, site.hi_pc) if site.kind == 0 else (site.lo_pc,)):
+                    w = isa.word_of(masked[pc * 8:pc * 8 + 8]) & (0x7F << 57)
+                    masked[pc * 8:pc * 8 + 8] = isa.bytes_of(w)
+            regs = L.Regs()
+            prog = compile_program(self.batch, self.dram_bytes, self.shared_bytes, bytes(masked), entry,
+                                   10_000_000, regs, True, sites)
+            if prog.info.faulted:
+                raise L.fault_to_exception(prog.fault)
+            self.plans[name] = prog
+
+    # ---- runtime words ------------------------------------------------------------------
+    def var_words(self, name: str, tokens: Sequence[int], positions: Sequence[int]) -> np.ndarray:
+        """[batch, n_var_words] runtime words for one step of every sequence."""
+        b = self.bundle
+        sites, meta = self._sites[name]
+        out = np.zeros((self.batch, self.plans[name].n_var_words), dtype=np.uint64)
+        row, kv = int(b.embedding_row_bytes), int(b.kv_step_bytes)
+        tokens = np.asarray(tokens, dtype=np.int64).reshape(self.batch)
+        positions = np.asarray(positions, dtype=np.int64).reshape(self.batch)
+        col = 0
+        for (kind, s) in meta:
+            if kind == "addr":
+                base = b.symbol_address(s.base_symbol)
+                if s.kind == "token_embed":
+                    vals = base + tokens * row
+                elif s.kind == "pos_embed":
+                    vals = base + positions * row
+                else:
+                    vals = base + positions * kv
+                lo_op, hi_op = np.uint64(isa.SET_ADDR_LO << 59), np.uint64(isa.SET_ADDR_HI << 59)
+                reg = np.uint64(s.addr_reg << 57)
+                v = vals.astype(np.uint64)
+                out[:, col] = lo_op | reg | ((v & np.uint64(isa.M28)) << np.uint64(29))
+                out[:, col + 1] = hi_op | reg | (((v >> np.uint64(28)) & np.uint64(isa.M28)) << np.uint64(29))
+                col += 2
+            else:
+                p = positions.astype(np.uint64)
+                out[:, col] = (np.uint64(isa.CONFIG_ATTN << 59) | (p << np.uint64(47)) |
+                               ((p + np.uint64(1)) << np.uint64(35)) | np.uint64(s.mode << 33))
+                col += 1
+        return out
+
+    def step_async(self, name: str, tokens, positions, stream=None) -> None:
+        self.engine.run_async(self.plans[name], self.var_words(name, tokens, positions), stream)
+
+    def step(self, name: str, tokens, positions) -> None:
+        st = self.engine.run(self.plans[name], self.var_words(name, tokens, positions))
+        if st != L.OK:
+            raise L.fault_to_exception(self.engine._last_fault, st)
+
+    def logits(self, name: str, seq: int) -> np.ndarray:
+        off = self.bundle.prefill_logits_offset if name == "prefill" else self.bundle.decode_logits_offset
+        return np.frombuffer(self.engine.read_dram(seq, off, self.logits_count * 2), dtype=np.float16).copy()
+
+    def logits_offset(self, name: str) -> int:
+        return self.bundle.prefill_logits_offset if name == "prefill" else self.bundle.decode_logits_offset

@@ -1,0 +1,126 @@
+"""Shared test helpers: golden fixture loading and oracle drivers."""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+
+import op_cases as oc
+from oracle import golden as G
+from oracle import isa as OI
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def load_op_golden():
+    z = np.load(GOLDEN / "op_cases.npz")
+    n = int(z["n_cases"][0])
+    out = []
+    for i in range(n):
+        p = f"c{i:03d}_"
+        err = bytes(z[p + "err"]).decode()
+        rec = dict(err="" if err == "-" else err, cycles=int(z[p + "cycles"][0]), pc=int(z[p + "cycles"][1]))
+        for nm in ("abuf", "wbuf", "accum", "sregs", "dram"):
+            if p + nm + "_sha" not in z:
+                continue
+            offs, lens, data = z[p + nm + "_off"], z[p + nm + "_len"], bytes(z[p + nm + "_data"])
+            spans, pos = [], 0
+            for o, l in zip(offs, lens):
+                spans.append((int(o), data[pos:pos + int(l)]))
+                pos += int(l)
+            rec[nm] = (bytes(z[p + nm + "_sha"]).hex(), spans)
+        out.append(rec)
+    return out
+
+
+def apply_spans(pre: np.ndarray, spans):
+    post = pre.copy()
+    for o, d in spans:
+        post[o:o + len(d)] = np.frombuffer(d, np.uint8)
+    return post
+
+
+class ProgramStub:
+    """ProgramBinary-like container for short hand-built programs."""
+
+    def __init__(self, words):
+        self.instructions = b"".join(int(w).to_bytes(8, "big") for w in words)
+        self.data = b""
+        self.entry_point = 0
+        self.insn_count = len(words)
+        self.data_base = 0
+        self.trace_manifest = {}
+
+
+def run_oracle_case(case):
+    """Runs an op case on the oracle; returns (err name, post dict, cycles, pc)."""
+    abuf, wbuf, accum, sregs, dram = oc.pre_state(case)
+    st = G.OracleState()
+    st.abuf[:] = abuf.tobytes()
+    st.wbuf[:] = wbuf.tobytes()
+    st.accum[:] = accum.view(np.int32)
+    st.scale_regs[:] = sregs.view(np.float16)
+    if dram is not None:
+        st.dram[:len(dram)] = dram.tobytes()
+    if case["tile"] is not None:
+        st.tile_config = tuple(case["tile"])
+    v, q, k, m = case["attn"]
+    if v:
+        st.attn_context = {"is_valid": True, "query_row_base": q, "valid_kv_len": k, "mode": m}
+    sim = G.OracleSimulator(st)
+    err = ""
+    try:
+        if case["kind"] == "program":
+            sim.load_program(ProgramStub(case["words"]))
+            sim.run()
+        else:
+            sim._execute(OI.decode_word(int(case["words"][0])))
+    except Exception as e:
+        err = type(e).__name__
+    post = dict(abuf=np.frombuffer(bytes(st.abuf), np.uint8), wbuf=np.frombuffer(bytes(st.wbuf), np.uint8),
+                accum=st.accum.view(np.uint8).copy(), sregs=st.scale_regs.view(np.uint8).copy())
+    if dram is not None:
+        post["dram"] = np.frombuffer(bytes(st.dram[:len(dram)]), np.uint8)
+    return err, post, st.cycle_count, st.pc
+
+
+def expected_post(case, rec):
+    abuf, wbuf, accum, sregs, dram = oc.pre_state(case)
+    pre = dict(abuf=abuf, wbuf=wbuf, accum=accum, sregs=sregs.view(np.uint8))
+    if dram is not None:
+        pre["dram"] = dram
+    return {nm: apply_spans(pre[nm], rec[nm][1]) for nm in pre}
+
+
+def fp16_ulp_diff(a_bytes: np.ndarray, b_bytes: np.ndarray) -> np.ndarray:
+    """|ulp distance| between two FP16 arrays given as bytes (same sign class)."""
+    a = a_bytes.view(np.uint16).astype(np.int32)
+    b = b_bytes.view(np.uint16).astype(np.int32)
+    ai = np.where(a & 0x8000, -(a & 0x7FFF), a)
+    bi = np.where(b & 0x8000, -(b & 0x7FFF), b)
+    return np.abs(ai - bi)
+
+
+def load_bundle(name):
+    from llm_accelerator_b200.bundle import ProgramBundle
+    return ProgramBundle.load(GOLDEN / f"bundle_{name}.npz")
+
+
+def load_run(name):
+    z = np.load(GOLDEN / f"run_{name}.npz")
+    return {k: z[k] for k in z.files}
+
+
+def run_bundle_sequence(sim_factory, bundle, prompt, n_steps, vocab, runner_cls):
+    """prefill(prompt[0]) then decode with teacher forcing over the prompt and
+    greedy tokens afterwards; returns (tokens, logits per step, sim)."""
+    sim = sim_factory()
+    r = runner_cls(bundle, simulator=sim, logits_dtype=np.float16)
+    logits = [r.run_prefill([int(prompt[0])])]
+    toks = [int(t) for t in prompt]
+    for pos in range(1, n_steps):
+        tok = int(prompt[pos]) if pos < len(prompt) else int(np.argmax(logits[-1][:vocab]))
+        if pos >= len(prompt):
+            toks.append(tok)
+        logits.append(r.run_decode_step(tok, pos))
+    return toks, np.stack(logits), sim

@@ -1,0 +1,185 @@
+"""Test helper: executes a compiled device plan on the CPU with NumPy.
+
+This checks the C++ compiler (renaming, aliasing, gathers, levels, final
+materialisation) independently of the CUDA kernels: the plan is run level by
+level with the oracle's NumPy arithmetic, and the resulting machine state is
+compared with the oracle's.  It is test infrastructure only and is never used
+by the engine.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from oracle import golden as G
+
+SRAM_UNITS = 8192 + 16384 + 4096
+SHARED = 1 << 63
+CONST = 1 << 31
+K = dict(GATHER=1, DYN_LOAD=2, DYN_STORE=3, SREG_LOAD=4, SREG_FINAL=5, MATMUL=6, REQUANT=7, REQUANT_PC=8,
+         SCALE_MUL_I32=9, SCALE_MUL_I8=10, VADD_I8=11, VADD_I32=12, DEQUANT_ADD=13, DEQUANT_ACCUM=14,
+         DEQUANT_SCALED=15, QUANT=16, VADD_F16=17, LAYERNORM_F16=18, GELU_F16=19, SOFTMAX_F16=20,
+         MASKED_SOFTMAX_F16=21, MAX_ABS=22, TRANSPOSE=23)
+
+
+class PlanMachine:
+    """One sequence: shared image + per-sequence block + register file."""
+
+    def __init__(self, dram: bytes, shared_bytes: int, arena_bytes: int, n_slots: int):
+        self.shared_bytes = shared_bytes
+        self.shared = np.frombuffer(bytes(dram[:shared_bytes]), np.uint8).copy()
+        rw = np.frombuffer(bytes(dram[shared_bytes:]), np.uint8)
+        self.rw_bytes = len(rw)
+        self.block = np.zeros(SRAM_UNITS * 16 + len(rw) + arena_bytes, np.uint8)
+        self.block[SRAM_UNITS * 16:SRAM_UNITS * 16 + len(rw)] = rw
+        self.sregs = np.zeros(16 + n_slots, np.uint16)
+
+    def load_sram(self, st: G.OracleState):
+        self.block[0:131072] = np.frombuffer(bytes(st.abuf), np.uint8)
+        self.block[131072:131072 + 262144] = np.frombuffer(bytes(st.wbuf), np.uint8)
+        self.block[393216:458752] = st.accum.view(np.uint8)
+        self.sregs[:16] = st.scale_regs.view(np.uint16)
+
+    def mem(self, phys: int, nbytes: int) -> np.ndarray:
+        if phys & SHARED:
+            a = (phys & ~SHARED) * 16
+            return self.shared[a:a + nbytes]
+        a = phys * 16
+        return self.block[a:a + nbytes]
+
+    def dram_mem(self, addr: int, nbytes: int) -> np.ndarray:
+        if addr < self.shared_bytes:
+            return self.shared[addr:addr + nbytes]
+        a = SRAM_UNITS * 16 + addr - self.shared_bytes
+        return self.block[a:a + nbytes]
+
+    def sreg(self, enc: int) -> np.float16:
+        bits = enc & 0xFFFF if enc & CONST else int(self.sregs[enc])
+        return np.array([bits], np.uint16).view(np.float16)[0]
+
+    def dram_image(self) -> bytes:
+        return bytes(self.shared) + bytes(self.block[SRAM_UNITS * 16:SRAM_UNITS * 16 + self.rw_bytes])
+
+
+def _f16(m, p, n):
+    return m.mem(p, n * 2).view(np.float16).astype(np.float32)
+
+
+def run_plan(m: PlanMachine, ops, segs, lv, params=None):
+    """Executes ops in level order (within a level in op order)."""
+    order = np.argsort(ops["level"], kind="stable")
+    for i in order:
+        op = ops[i]
+        k = int(op["kind"])
+        M, N, Kd = int(op["M"]), int(op["N"]), int(op["K"])
+        a, b, c, d = (int(op[x]) for x in "abcd")
+        s = [int(v) for v in op["s"]]
+        if k == K["GATHER"]:
+            data = []
+            for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]:
+                data.append((int(sg["dst"]), m.mem(int(sg["src"]), int(sg["n"]) * 16).copy()))
+            for dst, v in data:
+                m.mem(dst, len(v))[:] = v
+        elif k in (K["DYN_LOAD"], K["DYN_STORE"]):
+            addr = int(params[int(op["param"])]) + int(op["dconst"])
+            n = int(op["nbytes"])
+            if k == K["DYN_LOAD"]:
+                m.mem(d, n)[:] = m.dram_mem(addr, n)
+            else:
+                m.dram_mem(addr, n)[:] = m.mem(a, n)
+        elif k == K["SREG_LOAD"]:
+            m.sregs[int(op["out_slot"])] = m.mem(a, 2).view(np.uint16)[0]
+        elif k == K["SREG_FINAL"]:
+            vals = [(int(sg["dst"]), m.sreg(int(sg["src"]))) for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]]
+            for r, v in vals:
+                m.sregs[r] = np.array([v], np.float16).view(np.uint16)[0]
+        elif k == K["MATMUL"]:
+            A = m.mem(a, M * Kd).view(np.int8).reshape(M, Kd).astype(np.int32)
+            B = m.mem(b, Kd * N).view(np.int8).reshape(Kd, N).astype(np.int32)
+            acc = m.mem(c, M * N * 4).view(np.int32).reshape(M, N).copy() if op["flags"] & 1 else np.zeros((M, N), np.int32)
+            acc += A @ B
+            m.mem(d, M * N * 4)[:] = acc.view(np.uint8).ravel()
+        elif k in (K["REQUANT"], K["REQUANT_PC"]):
+            acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
+            sc = np.float32(m.sreg(s[0])) if k == K["REQUANT"] else _f16(m, b, N).reshape(1, N)
+            m.mem(d, M * N)[:] = G._sat8(acc * sc).view(np.uint8).ravel()
+        elif k == K["SCALE_MUL_I32"]:
+            v = np.round(m.mem(a, M * N * 4).view(np.int32).astype(np.float32) * np.float32(m.sreg(s[0])))
+            with np.errstate(invalid="ignore"):
+                r = np.clip(v, np.iinfo(np.int32).min, np.iinfo(np.int32).max).astype(np.int32)
+            m.mem(d, M * N * 4)[:] = r.view(np.uint8)
+        elif k == K["SCALE_MUL_I8"]:
+            v = m.mem(a, M * N).view(np.int8).astype(np.float32) * np.float32(m.sreg(s[0]))
+            m.mem(d, M * N)[:] = G._sat8(v).view(np.uint8)
+        elif k == K["VADD_I8"]:
+            v = m.mem(a, M * N).view(np.int8).astype(np.int16) + m.mem(b, M * N).view(np.int8).astype(np.int16)
+            m.mem(d, M * N)[:] = np.clip(v, -128, 127).astype(np.int8).view(np.uint8)
+        elif k == K["VADD_I32"]:
+            v = m.mem(a, M * N * 4).view(np.int32).reshape(M, N) + m.mem(b, N * 4).view(np.int32).reshape(1, N)
+            m.mem(d, M * N * 4)[:] = v.astype(np.int32).view(np.uint8).ravel()
+        elif k == K["DEQUANT_ADD"]:
+            acc = m.mem(a, M * N * 4).view(np.int32).astype(np.float32)
+            skip = m.mem(b, M * N).view(np.int8).astype(np.float32)
+            v = acc * np.float32(m.sreg(s[0])) + skip * np.float32(m.sreg(s[1]))
+            m.mem(d, M * N)[:] = G._sat8(v).view(np.uint8)
+        elif k == K["SOFTMAX_F16"]:
+            x = _f16(m, a, M * N).reshape(M, N)
+            e = np.exp((x - x.max(axis=-1, keepdims=True)).astype(np.float32))
+            r = (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
+            m.mem(d, M * N * 2)[:] = r.astype(np.float16).view(np.uint8).ravel()
+        elif k == K["QUANT"]:
+            x = _f16(m, a, M * N) * np.float32(m.sreg(s[0]))
+            v = np.round(x)
+            m.mem(d, M * N)[:] = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8).view(np.uint8)
+        elif k == K["MAX_ABS"]:
+            inv, fwd = G.max_abs_scales(float(np.max(np.abs(_f16(m, a, M * N)))))
+            m.sregs[int(op["out_slot"])] = np.array([inv], np.float16).view(np.uint16)[0]
+            m.sregs[int(op["out_slot"]) + 1] = np.array([fwd], np.float16).view(np.uint16)[0]
+        elif k in (K["DEQUANT_SCALED"], K["DEQUANT_ACCUM"]):
+            acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
+            vec = _f16(m, b, 2 * N if k == K["DEQUANT_SCALED"] else N)
+            if k == K["DEQUANT_SCALED"]:
+                r = acc * vec[:N].reshape(1, N) * np.float32(m.sreg(s[0])) + vec[N:].reshape(1, N)
+            else:
+                r = acc * vec[:N].reshape(1, N)
+            m.mem(d, M * N * 2)[:] = r.astype(np.float32).astype(np.float16).view(np.uint8).ravel()
+        elif k == K["VADD_F16"]:
+            r = _f16(m, a, M * N) + _f16(m, b, M * N)
+            m.mem(d, M * N * 2)[:] = r.astype(np.float16).view(np.uint8)
+        elif k == K["LAYERNORM_F16"]:
+            x = _f16(m, a, M * N).reshape(M, N)
+            gb = _f16(m, b, 2 * N)
+            mean = x.mean(axis=-1, keepdims=True).astype(np.float32)
+            var = x.var(axis=-1, keepdims=True).astype(np.float32)
+            y = (x - mean) / np.sqrt(var + np.float32(1e-5))
+            m.mem(d, M * N * 2)[:] = (y * gb[:N] + gb[N:]).astype(np.float32).astype(np.float16).view(np.uint8).ravel()
+        elif k == K["GELU_F16"]:
+            m.mem(d, M * N * 2)[:] = G._gelu_tanh(_f16(m, a, M * N)).astype(np.float32).astype(np.float16).view(np.uint8)
+        elif k == K["MASKED_SOFTMAX_F16"]:
+            if op["flags"] & 4:
+                v = int(params[int(op["param"])])
+                qrb, vkl = v & 0xFFFF, (v >> 16) & 0xFFFF
+            else:
+                qrb, vkl = int(op["attn_qrb"]), int(op["attn_vkl"])
+            src = _f16(m, a, M * N).reshape(M, N)
+            out = np.zeros((M, N), np.float32)
+            for i2 in range(M):
+                last = min(i2 + qrb, vkl - 1)
+                row = src[i2].copy()
+                if last + 1 < N:
+                    row[last + 1:] = -np.inf
+                e = np.exp((row - float(row.max())).astype(np.float32))
+                if last + 1 < N:
+                    e[last + 1:] = 0.0
+                den = float(e.sum())
+                out[i2] = e / den if den > 0 else 0.0
+            m.mem(d, M * N * 2)[:] = out.astype(np.float16).view(np.uint8).ravel()
+        elif k == K["TRANSPOSE"]:
+            src = m.mem(a, M * N).view(np.int8).reshape(M, N)
+            m.mem(d, M * N)[:] = np.ascontiguousarray(src.T).view(np.uint8).ravel()
+        else:
+            raise NotImplementedError(f"plan executor: op kind {k}")
+
+
+def final_state(m: PlanMachine):
+    return dict(abuf=bytes(m.block[0:131072]), wbuf=bytes(m.block[131072:393216]),
+                accum=bytes(m.block[393216:458752]), sregs=bytes(m.sregs[:16].tobytes()), dram=m.dram_image())

@@ -1,0 +1,189 @@
+"""CPU tests of the C++ stream compiler (no GPU needed).
+
+The compiler must (a) fault exactly where and how the reference faults,
+(b) count retired instructions and analytic cycles like the reference, and
+(c) produce a plan whose execution, in level order, reproduces the oracle's
+machine state bit-for-bit.  (c) runs the plan through tests/plan_exec.py with
+the oracle's NumPy arithmetic, so it checks the dataflow transformation
+(renaming, aliasing, gathers, levels, final materialisation) in isolation.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import op_cases as oc
+import plan_exec as PE
+from helpers import GOLDEN, load_bundle, load_op_golden, load_run
+from llm_accelerator_b200 import _lib as L
+from llm_accelerator_b200.engine import Site, compile_program
+from oracle import golden as G
+
+CASES = oc.case_list()
+GOLD = load_op_golden()
+DRAM = 16 * 1024 * 1024
+ERR_OF_STATUS = {L.E_SIMULATOR: "SimulatorError", L.E_ILLEGAL_OPCODE: "IllegalOpcodeError",
+                 L.E_ILLEGAL_BUFFER: "IllegalBufferError", L.E_CONFIG: "ConfigError",
+                 L.E_SRAM_ACCESS: "SRAMAccessError", L.E_DRAM_ACCESS: "DRAMAccessError", L.E_VALUE: "ValueError"}
+
+
+def _regs(case):
+    r = L.Regs()
+    if case["tile"] is not None:
+        r.tile_valid = 1
+        r.tile[0], r.tile[1], r.tile[2] = case["tile"]
+    v, q, k, m = case["attn"]
+    if v:
+        r.attn_valid, r.attn_qrb, r.attn_vkl, r.attn_mode = 1, q, k, m
+    return r
+
+
+def _compile_case(case):
+    region = b"".join(int(w).to_bytes(8, "big") for w in case["words"])
+    return compile_program(1, DRAM, 0, region, 0, 10_000_000 if case["kind"] == "program" else 1, _regs(case),
+                           False, ())
+
+
+@pytest.mark.parametrize("i", range(len(CASES)))
+def test_compiler_faults_and_cycles_match_reference(i):
+    case, rec = CASES[i], GOLD[i]
+    p = _compile_case(case)
+    err = ERR_OF_STATUS.get(int(p.fault.status), "") if p.info.faulted else ""
+    assert err == rec["err"], p.fault.message
+    assert int(p.info.cycles) == rec["cycles"]
+
+
+@pytest.mark.parametrize("i", [i for i, c in enumerate(CASES) if c["op"] not in
+                               (0x0F, 0x0E, 0x10, 0x15, 0x12, 0x16)])
+def test_plan_reproduces_reference_op_case(i):
+    """Executes the compiled plan with NumPy and compares with the golden record."""
+    case, rec = CASES[i], GOLD[i]
+    if rec["err"]:
+        pytest.skip("faulting case (covered by the fault test)")
+    p = _compile_case(case)
+    abuf, wbuf, accum, sregs, dram = oc.pre_state(case)
+    img = np.zeros(DRAM, np.uint8)
+    if dram is not None:
+        img[:len(dram)] = dram
+    img[:len(case["words"]) * 8] = np.frombuffer(b"".join(int(w).to_bytes(8, "big") for w in case["words"]), np.uint8) \
+        if case["kind"] == "program" and dram is None else img[:len(case["words"]) * 8]
+    m = PE.PlanMachine(img.tobytes(), 0, int(p.info.arena_bytes), int(p.info.n_slots))
+    m.block[:131072] = abuf
+    m.block[131072:393216] = wbuf
+    m.block[393216:458752] = accum
+    m.sregs[:16] = sregs
+    ops, segs, tasks, lv = p.dump()
+    PE.run_plan(m, ops, segs, lv)
+    f = PE.final_state(m)
+    from helpers import expected_post
+    exp = expected_post(case, rec)
+    assert f["abuf"] == exp["abuf"].tobytes()
+    assert f["wbuf"] == exp["wbuf"].tobytes()
+    assert f["accum"] == exp["accum"].tobytes()
+    assert f["sregs"] == exp["sregs"].tobytes()
+    if "dram" in exp:
+        assert f["dram"][:len(exp["dram"])] == exp["dram"].tobytes()
+
+
+def _sites(b, name):
+    sites = []
+    for s in b.runtime_patch_sites:
+        if s.stream == name:
+            lo, hi = b.symbol_extent(s.base_symbol)
+            sites.append(Site(0, s.addr_reg, s.absolute_lo_pc, s.absolute_hi_pc, lo, hi))
+    for s in b.runtime_config_attn_sites:
+        if s.stream == name:
+            sites.append(Site(1, 0, s.absolute_pc))
+    return sites
+
+
+def _params(region, sites):
+    out = []
+    for s in sites:
+        if s.kind == 0:
+            lo = int.from_bytes(region[s.lo_pc * 8:s.lo_pc * 8 + 8], "big")
+            hi = int.from_bytes(region[s.hi_pc * 8:s.hi_pc * 8 + 8], "big")
+            out.append((((hi >> 29) & 0xFFFFFFF) << 28) | ((lo >> 29) & 0xFFFFFFF))
+        else:
+            w = int.from_bytes(region[s.lo_pc * 8:s.lo_pc * 8 + 8], "big")
+            out.append(((w >> 47) & 0xFFF) | (((w >> 35) & 0xFFF) << 16) | (((w >> 33) & 3) << 32))
+    return out
+
+
+@pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
+def test_plan_reproduces_oracle_bundle_run(name):
+    """Prefill + decode steps: one plan per stream compiled with runtime sites,
+    executed with each step's parameters, equals the oracle bit-for-bit."""
+    b = load_bundle(name)
+    gold = load_run(name)
+    orc = G.OracleSimulator()
+    orc.load_bundle(b)
+    dram_bytes, shared = len(orc.state.dram), b.temp_base // 16 * 16
+    plans = {}
+    for nm in ("prefill", "decode"):
+        sites = _sites(b, nm)
+        region = bytearray(b.instruction_region())
+        for s in sites:
+            for pc in ((s.lo_pc, s.hi_pc) if s.kind == 0 else (s.lo_pc,)):
+                w = int.from_bytes(region[pc * 8:pc * 8 + 8], "big") & (0x7F << 57)
+                region[pc * 8:pc * 8 + 8] = w.to_bytes(8, "big")
+        entry = b.prefill_pc if nm == "prefill" else b.decode_pc
+        plans[nm] = (compile_program(1, dram_bytes, shared, bytes(region), entry, 10_000_000, L.Regs(), True, sites),
+                     sites)
+    arena = max(int(p.info.arena_bytes) for p, _ in plans.values())
+    slots = max(int(p.info.n_slots) for p, _ in plans.values())
+    m = PE.PlanMachine(bytes(orc.state.dram), shared, arena, slots)
+    prompt = gold["prompt"]
+    for pos in range(0, 6):
+        nm = "prefill" if pos == 0 else "decode"
+        tok = int(prompt[pos]) if pos < len(prompt) else int(gold["tokens"][pos])
+        row = b.embedding_row_bytes
+        for s in b.runtime_patch_sites:
+            if s.stream == nm:
+                b.patch_runtime_site(s, {"token_embed": tok * row, "pos_embed": pos * row,
+                                         "kv_base": pos * b.kv_step_bytes}[s.kind])
+        for s in b.runtime_config_attn_sites:
+            if s.stream == nm:
+                b.patch_config_attn_site(s, query_row_base=pos, valid_kv_len=pos + 1)
+        region = bytes(b.instruction_region())
+        m.shared[:len(region)] = np.frombuffer(region, np.uint8)
+        p, sites = plans[nm]
+        ops, segs, tasks, lv = p.dump()
+        PE.run_plan(m, ops, segs, lv, _params(region, sites))
+        n = orc.run_program(b, nm)
+        assert n == int(p.info.executed)
+        f = PE.final_state(m)
+        st = orc.state
+        assert f["abuf"] == bytes(st.abuf) and f["wbuf"] == bytes(st.wbuf)
+        assert f["accum"] == st.accum.tobytes() and f["sregs"] == st.scale_regs.tobytes()
+        assert f["dram"] == bytes(st.dram[:len(f["dram"])])
+
+
+def test_runtime_site_out_of_range_requests_recompile():
+    """A patched word outside its compiled range is reported, not executed."""
+    b = load_bundle("tiny_l1_d64")
+    sites = _sites(b, "decode")
+    assert sites and sites[0].kind == 0
+    region = bytes(b.instruction_region())
+    p = compile_program(1, 16 << 20, b.temp_base // 16 * 16, region, b.decode_pc, 10_000_000, L.Regs(), True, sites)
+    assert int(p.info.n_var_words) == sum(2 if s.kind == 0 else 1 for s in sites)
+    assert int(p.info.n_levels) > 0 and not p.info.faulted
+
+
+def test_self_modifying_store_is_rejected():
+    # SET_ADDR R1 = 0 ; STORE ABUF[0..16) -> DRAM[0] (the instruction region) ; HALT
+    words = [(0x05 << 59) | (1 << 57), (0x06 << 59) | (1 << 57),
+             (0x08 << 59) | (1 << 25) | (1 << 23), 0x01 << 59]
+    region = b"".join(w.to_bytes(8, "big") for w in words)
+    with pytest.raises(Exception, match="self-modifying"):
+        compile_program(1, DRAM, 0, region, 0, 100, L.Regs(), True, ())
+
+
+def test_pc_past_end_and_halt_counts():
+    words = [0x00 << 59, 0x02 << 59]   # NOP, SYNC, no HALT
+    region = b"".join(w.to_bytes(8, "big") for w in words)
+    p = compile_program(1, DRAM, 0, region, 0, 100, L.Regs(), True, ())
+    assert p.info.faulted and int(p.fault.status) == L.E_SIMULATOR
+    assert int(p.info.executed) == 2 and int(p.info.cycles) == 2
+    p = compile_program(1, DRAM, 0, region, 0, 1, L.Regs(), True, ())   # watchdog stops first
+    assert not p.info.faulted and int(p.info.executed) == 1
