@@ -16,18 +16,15 @@ from .errors import (ConfigError, DRAMAccessError, EngineError, IllegalBufferErr
                      IllegalOpcodeError, SimulatorError, SRAMAccessError)
 
 
+_LAZY = {"B200Simulator": "simulator", "B200State": "simulator", "HostRunner": "runner",
+         "BatchedRunner": "runner", "Engine": "engine", "compile_program": "engine"}
+
+
 def __getattr__(name):
     # CUDA-backed classes load libtaccel_b200.so on first use.
-    if name in ("B200Simulator", "B200State"):
-        from . import simulator
-        return getattr(simulator, name)
-    if name in ("HostRunner", "BatchedRunner"):
-        from . import runner
-        return getattr(runner, name)
-    if name in ("Engine", "compile_program"):
-        from . import engine
-        return getattr(engine, name)
+    import importlib
+    if name in _LAZY:
+        return getattr(importlib.import_module(f".{_LAZY[name]}", __name__), name)
     if name == "gemm":
-        from . import gemm
-        return gemm
+        return importlib.import_module(".gemm", __name__)
     raise AttributeError(name)

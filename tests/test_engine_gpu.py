@@ -3,9 +3,11 @@
 Integer / byte work (MATMUL, REQUANT*, QUANT, MAX_ABS, DMA, transposes,
 DEQUANT*, VADD*, LayerNorm) must be bit-exact against the reference goldens.
 GELU and softmax use exp / tanh / x**3 that NumPy's float32 SIMD code does not
-round correctly; the engine evaluates them in float64 and rounds once, so those
-outputs are held to at most 1 FP16 ulp (1 int8 step for the legacy INT8-I/O
-ops) against the golden values.
+round correctly; the engine evaluates them in float64 and rounds once.  Their
+FP16 outputs are held to FP16_TOL: at most 2 FP16 ulp where |ref| >= 2^-6 and
+at most 2^-14 absolute below that (GELU's 1 + tanh(x) cancels for large
+negative x, which magnifies a one-ulp float32 tanh difference there); legacy
+INT8-I/O outputs to one int8 step.
 """
 from __future__ import annotations
 
@@ -22,6 +24,21 @@ pytestmark = pytest.mark.gpu
 CASES = oc.case_list()
 GOLD = load_op_golden()
 FP16_OUT = {0x1B, 0x1C, 0x1D}
+FP16_TOL_ULP, FP16_TOL_SMALL, FP16_TOL_ABS = 2, 2.0 ** -6, 2.0 ** -14
+
+
+def assert_fp16_close(got: np.ndarray, want: np.ndarray, what: str = ""):
+    """FP16_TOL check on two byte arrays holding FP16 values."""
+    g = got.view(np.float16).astype(np.float32)
+    w = want.view(np.float16).astype(np.float32)
+    ulp = fp16_ulp_diff(got, want)
+    small = np.abs(w) < FP16_TOL_SMALL
+    bad = np.where(small, np.abs(g - w) > FP16_TOL_ABS, ulp > FP16_TOL_ULP)
+    assert not bad.any(), f"{what}: {int(bad.sum())} values out of tolerance, max ulp {int(ulp.max())}, " \
+                          f"max abs {float(np.max(np.abs(g - w))):.3g}"
+    return float(np.mean(ulp == 0))
+
+
 I8_OUT_TRANSC = {0x0E, 0x10, 0x15, 0x12, 0x16}
 
 
@@ -73,11 +90,7 @@ def test_engine_op_case(i):
     for nm, got in post.items():
         want = exp[nm]
         if op in FP16_OUT and nm == "abuf":
-            diff = np.flatnonzero(got != want)
-            if diff.size:
-                lo, hi = diff[0] & ~1, (diff[-1] | 1) + 1
-                ulp = fp16_ulp_diff(got[lo:hi].copy(), want[lo:hi].copy())
-                assert ulp.max() <= 1, f"{nm}: max ulp {ulp.max()}"
+            assert_fp16_close(got.copy(), want.copy(), nm)
         elif op in I8_OUT_TRANSC and nm == "abuf":
             d = np.abs(got.view(np.int8).astype(np.int16) - want.view(np.int8).astype(np.int16))
             assert d.max() <= 1, f"{nm}: max int8 step {d.max()}"
@@ -120,19 +133,18 @@ def test_batched_runner_matches_single_sequence_runs():
 
 
 def test_batched_runner_ragged_positions():
-    """Sequences at different positions in one step (per-sequence runtime words)."""
+    """Sequences at different positions in one step (per-sequence runtime words):
+    sequence 1 re-runs position 1 while sequences 0 and 2 move to position 2."""
     from llm_accelerator_b200.runner import BatchedRunner, HostRunner
     b = load_bundle("tiny_l1_d64")
-    B, vocab = 3, 128
+    B = 3
     br = BatchedRunner(b, B)
-    toks = np.array([5, 6, 7])
-    br.step("prefill", toks, np.zeros(B, int))
+    br.step("prefill", np.array([5, 6, 7]), np.zeros(B, int))
     br.step("decode", np.array([9, 10, 11]), np.array([1, 1, 1]))
-    br.step("decode", np.array([12, 13, 14]), np.array([2, 2, 2]))
-    got = br.logits("decode", 1)
-    b2 = load_bundle("tiny_l1_d64")
-    r = HostRunner(b2, simulator=_sim(), logits_dtype=np.float16)
-    r.run_prefill([6])
-    r.run_decode_step(10, 1)
-    want = r.run_decode_step(13, 2)
-    np.testing.assert_array_equal(got.view(np.uint16), want.view(np.uint16))
+    br.step("decode", np.array([12, 13, 14]), np.array([2, 1, 2]))
+    for seq, (t0, t1, t2, p2) in enumerate([(5, 9, 12, 2), (6, 10, 13, 1), (7, 11, 14, 2)]):
+        r = HostRunner(load_bundle("tiny_l1_d64"), simulator=_sim(), logits_dtype=np.float16)
+        r.run_prefill([t0])
+        r.run_decode_step(t1, 1)
+        want = r.run_decode_step(t2, p2)
+        np.testing.assert_array_equal(br.logits("decode", seq).view(np.uint16), want.view(np.uint16))
