@@ -136,6 +136,33 @@ int tac_compile(int batch, uint64_t dram_bytes, uint64_t shared_bytes,
 int tac_program_destroy(tac_program* p);
 int tac_program_info(const tac_program* p, tac_exec_info* info, tac_fault* fault);
 
+/* Compile options.  By default a run leaves the complete architectural state
+ * behind (every SRAM byte, every DRAM byte, the scale registers), as the
+ * golden simulator does.  A caller that only needs part of it (a batched
+ * generation loop reads logits and keeps the KV cache) lists the DRAM byte
+ * ranges that stay live after the run; values the run leaves in other
+ * writable DRAM bytes, in SRAM (sram_live = 0) or in the scale registers
+ * (sregs_live = 0) may then be dropped.  n_live = 0 keeps everything. */
+typedef struct tac_compile_opts {
+  uint32_t n_live;
+  int32_t sram_live;
+  int32_t sregs_live;
+  int32_t reserved;
+  const uint64_t* live;   /* [n_live][2] byte ranges [lo, hi) */
+} tac_compile_opts;
+
+int tac_compile_ex(int batch, uint64_t dram_bytes, uint64_t shared_bytes,
+                   const uint8_t* insn_bytes, uint64_t n_insns, uint64_t entry_pc,
+                   uint64_t max_insns, const tac_regs* init_regs, int sregs_reset,
+                   const tac_var_site* sites, int n_sites, const tac_compile_opts* opts,
+                   tac_program** out, tac_exec_info* info, tac_fault* fault);
+
+/* What a compiled run reads that an earlier run may have left behind:
+ * writable-DRAM byte ranges (up to max_ranges, [lo, hi) pairs), and whether it
+ * reads SRAM or scale registers it did not write itself. */
+int tac_program_home_reads(const tac_program* p, uint64_t* ranges, uint32_t max_ranges, uint32_t* n_ranges,
+                           int32_t* sram_read, int32_t* sregs_read);
+
 /* Plan introspection (profiling and tests): copy out the device ops
  * (sizeof = tac_program_record_size(0)), gather segments (record size 1),
  * tasks (record size 2) and per-level task offsets (uint32, n_levels + 1). */
@@ -153,12 +180,29 @@ int tac_run_async(tac_engine* e, tac_program* p, const uint64_t* var_words, void
 int tac_run(tac_engine* e, tac_program* p, const uint64_t* var_words, tac_fault* fault);
 int tac_check_device_status(tac_engine* e, tac_fault* fault);
 
+/* Split form of tac_run_async for callers that stage inputs ahead of time:
+ * tac_encode_params decodes and range-checks one run's runtime words on the
+ * host into params_out[batch][tac_program_param_count(p)] (no GPU needed);
+ * tac_run_async_params runs with those parameters already in device memory. */
+uint64_t tac_program_param_count(const tac_program* p);
+int tac_encode_params(const tac_program* p, int batch, const uint64_t* var_words, uint64_t* params_out,
+                      tac_fault* fault);
+int tac_run_async_params(tac_engine* e, tac_program* p, const uint64_t* params_dev, void* stream,
+                         tac_fault* fault);
+
 /* Greedy decode helpers for batched generation (HostRunner._greedy_token,
  * host_runner.py:97-101): argmax over `count` FP16 values at DRAM address
  * `addr` of every sequence, written to out_tokens (device int32[batch]).
  * Ties resolve to the lowest index, like numpy.argmax. */
 int tac_argmax_f16(tac_engine* e, uint64_t addr, uint64_t count, int32_t* out_tokens_dev,
                    void* stream);
+
+/* Profiling (the golden model's analytic cycle_count has no wall-clock
+ * counterpart, golden_model/simulator.py:208-236 trace hooks): when enabled,
+ * each run records the device time at the end of every plan level;
+ * tac_read_profile copies the n_levels + 1 timestamps (ns) of the last run. */
+int tac_set_profiling(tac_engine* e, int enable);
+int tac_read_profile(tac_engine* e, uint64_t* out_ns, uint32_t max_entries, uint32_t* n_entries);
 
 /* Per-sequence device pointer arithmetic for zero-copy callers. */
 int tac_engine_layout(const tac_engine* e, void** seq_base, uint64_t* seq_stride,

@@ -43,6 +43,11 @@ class ExecInfo(C.Structure):
                 ("final_regs", Regs)]
 
 
+class CompileOpts(C.Structure):
+    _fields_ = [("n_live", C.c_uint32), ("sram_live", C.c_int32), ("sregs_live", C.c_int32),
+                ("reserved", C.c_int32), ("live", C.c_void_p)]
+
+
 _P = C.c_void_p
 _U64 = C.c_uint64
 _I = C.c_int
@@ -60,6 +65,9 @@ SIGNATURES = {
     "tac_sregs_read": (_I, [_P, _I, _P]),
     "tac_compile": (_I, [_I, _U64, _U64, _P, _U64, _U64, _U64, C.POINTER(Regs), _I, C.POINTER(VarSite), _I,
                          C.POINTER(_P), C.POINTER(ExecInfo), C.POINTER(Fault)]),
+    "tac_compile_ex": (_I, [_I, _U64, _U64, _P, _U64, _U64, _U64, C.POINTER(Regs), _I, C.POINTER(VarSite), _I,
+                            C.POINTER(CompileOpts), C.POINTER(_P), C.POINTER(ExecInfo), C.POINTER(Fault)]),
+    "tac_program_home_reads": (_I, [_P, _P, C.c_uint32, _P, _P, _P]),
     "tac_program_destroy": (_I, [_P]),
     "tac_program_info": (_I, [_P, C.POINTER(ExecInfo), C.POINTER(Fault)]),
     "tac_program_record_size": (_U64, [_I]),
@@ -67,7 +75,12 @@ SIGNATURES = {
     "tac_run_async": (_I, [_P, _P, _P, _P, C.POINTER(Fault)]),
     "tac_run": (_I, [_P, _P, _P, C.POINTER(Fault)]),
     "tac_check_device_status": (_I, [_P, C.POINTER(Fault)]),
+    "tac_program_param_count": (_U64, [_P]),
+    "tac_encode_params": (_I, [_P, _I, _P, _P, C.POINTER(Fault)]),
+    "tac_run_async_params": (_I, [_P, _P, _P, _P, C.POINTER(Fault)]),
     "tac_argmax_f16": (_I, [_P, _U64, _U64, _P, _P]),
+    "tac_set_profiling": (_I, [_P, _I]),
+    "tac_read_profile": (_I, [_P, _P, C.c_uint32, _P]),
     "tac_engine_layout": (_I, [_P, C.POINTER(_P), C.POINTER(_U64), C.POINTER(_P)]),
     "tac_gemm_i8_requant_pc": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
     "tac_gemm_i8_requant_shift": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),

@@ -16,6 +16,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <unordered_map>
 #include <new>
 #include <string>
 
@@ -168,9 +169,11 @@ class Compiler {
         for (uint64_t i = 0; i < r.second; ++i) {
           int32_t& x = rw_rl_[p - rw_base_ + i];
           x = std::max(x, L);
+          rw_home_read_[p - rw_base_ + i] = 1;
         }
       } else if (c == PC_HOME_SRAM) {
         for (uint64_t i = 0; i < r.second; ++i) home_rl_[p + i] = std::max(home_rl_[p + i], L);
+        sram_home_read_ = true;
       }
     }
     for (auto& w : a.writes) {
@@ -183,7 +186,10 @@ class Compiler {
       }
     }
     for (uint32_t s : a.slot_writes) slot_lvl_[s] = L;
-    if (a.sreg_home_read) sreg_home_rl_ = std::max(sreg_home_rl_, L);
+    if (a.sreg_home_read) {
+      sreg_home_rl_ = std::max(sreg_home_rl_, L);
+      sreg_home_read_ = true;
+    }
   }
 
   uint32_t emit(DevOp op, const Access& a) {
@@ -225,26 +231,94 @@ class Compiler {
     return true;
   }
 
-  // Gathers scattered physical units into one fresh arena extent.
+  // Appends a copy segment, split into pieces of at most kGatherChunkUnits.
+  void push_seg(uint64_t src, uint64_t dst, uint64_t n) {
+    while (n > kGatherChunkUnits) {
+      P->segs.push_back(Segment{src, dst, kGatherChunkUnits});
+      src += kGatherChunkUnits;
+      dst += kGatherChunkUnits;
+      n -= kGatherChunkUnits;
+    }
+    P->segs.push_back(Segment{src, dst, n});
+  }
+
+  // Gathers scattered physical units into one fresh arena extent.  Two gathers
+  // of the same immutable sources share one extent.
   uint64_t gather(const uint64_t* map, uint64_t n) {
-    uint64_t dst = alloc(n);
-    DevOp op = blank(K_GATHER);
-    op.seg0 = static_cast<uint32_t>(P->segs.size());
-    Access acc;
+    std::vector<std::pair<uint64_t, uint64_t>> runs;
+    bool mutable_src = false;
     uint64_t i = 0;
     while (i < n) {
       uint64_t j = i + 1;
       while (j < n && map[j] == map[i] + (j - i) && cls(map[j]) == cls(map[i])) ++j;
-      P->segs.push_back(Segment{map[i], dst + i, j - i});
-      acc.reads.push_back({map[i], j - i});
+      runs.push_back({map[i], j - i});
+      mutable_src |= cls(map[i]) == PC_HOME_RW;
       i = j;
+    }
+    std::string key;
+    if (!mutable_src) {
+      key.assign("G", 1);
+      key.append(reinterpret_cast<const char*>(runs.data()), runs.size() * sizeof(runs[0]));
+      auto it = cse_.find(key);
+      if (it != cse_.end()) return P->ops[it->second].d;
+    }
+    uint64_t dst = alloc(n);
+    DevOp op = blank(K_GATHER);
+    op.seg0 = static_cast<uint32_t>(P->segs.size());
+    Access acc;
+    uint64_t off = 0;
+    for (auto& r : runs) {
+      push_seg(r.first, dst + off, r.second);
+      acc.reads.push_back(r);
+      off += r.second;
     }
     op.nseg = static_cast<uint32_t>(P->segs.size() - op.seg0);
     op.d = dst;
     op.N = static_cast<uint32_t>(n);
     acc.writes.push_back({dst, n});
-    emit(op, acc);
+    uint32_t idx = emit(op, acc);
+    if (!mutable_src) cse_[key] = idx;
     return dst;
+  }
+
+  // Emits a compute op unless an identical op (same kind, shape and
+  // immutable operands) already produced the value; then the destination
+  // logical units (and scale-register slots) alias that op's output.
+  void emit_compute(DevOp& op, Access& acc, uint32_t dst_u0, int sreg_idx) {
+    bool mutable_src = false;
+    for (auto& r : acc.reads) mutable_src |= cls(r.first) == PC_HOME_RW;
+    std::string key;
+    if (!mutable_src && op.kind != K_DYN_LOAD && op.kind != K_DYN_STORE && op.kind != K_SREG_FINAL) {
+      DevOp k = op;
+      k.d = 0;
+      k.out_slot = 0;
+      k.pc = 0;
+      k.level = 0;
+      key.assign(reinterpret_cast<const char*>(&k), sizeof(k));
+      auto it = cse_.find(key);
+      if (it != cse_.end()) {
+        const DevOp& prev = P->ops[it->second];
+        if (op.kind == K_MAX_ABS) {
+          sreg_[sreg_idx] = prev.out_slot;
+          sreg_[sreg_idx + 1] = prev.out_slot + 1;
+          if (op.out_slot + 2 == kSregSlotBase + n_slots_) n_slots_ -= 2;
+        } else if (op.kind == K_SREG_LOAD) {
+          sreg_[sreg_idx] = prev.out_slot;
+          if (op.out_slot + 1 == kSregSlotBase + n_slots_) n_slots_ -= 1;
+        } else {
+          for (uint64_t i = 0; i < last_dst_units_; ++i) sram_[dst_u0 + i] = prev.d + i;
+          const uint64_t rounded = (last_dst_units_ + 15) & ~15ull;
+          if (op.d + rounded == arena_base_ + arena_top_) {
+            arena_top_ -= rounded;
+            arena_lvl_.resize(arena_top_);
+          }
+        }
+        ++cse_hits_;
+        return;
+      }
+    }
+    uint32_t idx = emit(op, acc);
+    if (!key.empty()) cse_[key] = idx;
   }
 
   // Physical start of a contiguous copy of logical SRAM units [u0, u0+n).
@@ -263,6 +337,7 @@ class Compiler {
   // Fresh destination extent for logical SRAM units [u0, u0+n).
   uint64_t dst(uint32_t u0, uint64_t nbytes, Access& acc) {
     uint64_t n = (nbytes + kUnit - 1) / kUnit;
+    last_dst_units_ = n;
     uint64_t p = alloc(n);
     for (uint64_t i = 0; i < n; ++i) sram_[u0 + i] = p + i;
     acc.writes.push_back({p, n});
@@ -288,7 +363,7 @@ class Compiler {
              cls(shadow_[idx[j]]) == cls(shadow_[idx[k]]))
         ++j;
       uint64_t n = j - k;
-      P->segs.push_back(Segment{shadow_[idx[k]], rw_home(idx[k]), n});
+      push_seg(shadow_[idx[k]], rw_home(idx[k]), n);
       acc.reads.push_back({shadow_[idx[k]], n});
       acc.writes.push_back({rw_home(idx[k]), n});
       k = j;
@@ -296,6 +371,21 @@ class Compiler {
     op.nseg = static_cast<uint32_t>(P->segs.size() - op.seg0);
     emit(op, acc);
     for (uint64_t i : idx) shadow_[i] = rw_home(i);
+  }
+
+  // Flushes only the units of [i0, i1) that lie in the caller's live-out ranges.
+  void flush_live(uint64_t i0, uint64_t i1) {
+    if (!opts_ || opts_->n_live == 0) {
+      flush_rw(i0, i1);
+      return;
+    }
+    for (uint32_t r = 0; r < opts_->n_live; ++r) {
+      uint64_t lo = opts_->live[2 * r], hi = opts_->live[2 * r + 1];
+      if (hi <= shared_bytes_) continue;
+      lo = lo < shared_bytes_ ? 0 : (lo - shared_bytes_) / kUnit;
+      hi = std::min<uint64_t>(rw_units_, (hi - shared_bytes_ + kUnit - 1) / kUnit);
+      if (lo < hi) flush_rw(std::max(lo, i0), std::min(hi, i1));
+    }
   }
 
   // Physical location of the current value of DRAM unit u.
@@ -342,6 +432,15 @@ class Compiler {
   bool halted_ = false;
   // var-site lookup: pc -> (site index, role 0 = lo / attn, 1 = hi)
   std::map<uint64_t, std::pair<int, int>> var_pc_;
+  // common-subexpression table: op signature -> op index
+  std::unordered_map<std::string, uint32_t> cse_;
+  uint64_t cse_hits_ = 0;
+  uint64_t last_dst_units_ = 0;
+  // what the run reads that it did not produce
+  std::vector<uint8_t> rw_home_read_;
+  bool sram_home_read_ = false, sreg_home_read_ = false;
+ public:
+  const tac_compile_opts* opts_ = nullptr;
 };
 
 // ---------------------------------------------------------------------------------
@@ -505,7 +604,7 @@ int Compiler::h_buf_copy(const Insn& x) {                   // dma.py:67-97
   op.N = static_cast<uint32_t>(cols);
   op.a = src(su, n, acc);
   op.d = dst(du, n, acc);
-  emit(op, acc);
+  emit_compute(op, acc, du, -1);
   cycles_ += x.length;
   return 0;
 }
@@ -522,8 +621,8 @@ int Compiler::h_set_scale(const Insn& x) {                  // simulator.py:605-
   op.a = src(unit_of(buf, x.imm16), 2, acc);
   op.out_slot = new_slot();
   acc.slot_writes.push_back(op.out_slot);
-  emit(op, acc);
   sreg_[x.sreg] = op.out_slot;
+  emit_compute(op, acc, 0, x.sreg);
   return 0;
 }
 
@@ -858,7 +957,7 @@ int Compiler::h_rtype(const Insn& x) {
       return unsupported("unhandled opcode");
   }
 #undef TRY
-  emit(op, acc);
+  emit_compute(op, acc, d, x.sreg);
   return 0;
 }
 
@@ -930,10 +1029,11 @@ int Compiler::step(const Insn& x) {
 // SRAM home images and scale registers.
 void Compiler::finalize() {
   // 1. writable DRAM units whose value lives elsewhere
-  flush_rw(0, rw_units_);
+  flush_live(0, rw_units_);
   // 2. SRAM units whose value is not in place
   std::vector<uint32_t> moved;
-  for (uint32_t u = 0; u < kSramUnits; ++u)
+  const bool sram_live = !opts_ || opts_->sram_live;
+  for (uint32_t u = 0; sram_live && u < kSramUnits; ++u)
     if (sram_[u] != u) moved.push_back(u);
   if (!moved.empty()) {
     // Values still held in SRAM home locations are first copied out, so the
@@ -965,7 +1065,7 @@ void Compiler::finalize() {
              cls(sram_[moved[j]]) == cls(sram_[moved[k]]))
         ++j;
       uint64_t n = j - k;
-      P->segs.push_back(Segment{sram_[moved[k]], uint64_t(moved[k]), n});
+      push_seg(sram_[moved[k]], uint64_t(moved[k]), n);
       acc.reads.push_back({sram_[moved[k]], n});
       acc.writes.push_back({uint64_t(moved[k]), n});
       k = j;
@@ -975,6 +1075,7 @@ void Compiler::finalize() {
     for (uint32_t u : moved) sram_[u] = u;
   }
   // 3. scale registers
+  if (opts_ && !opts_->sregs_live) return;
   bool any = false;
   for (int r = 0; r < 16; ++r) any |= sreg_[r] != uint32_t(r);
   if (any) {
@@ -1004,18 +1105,27 @@ void Compiler::build_tasks() {
   std::vector<std::vector<Task>> per_level(lv.size());
   auto per_seq = [&](uint32_t opi, uint32_t tiles) {
     for (uint32_t s = 0; s < B; ++s)
-      for (uint32_t t = 0; t < tiles; ++t) per_level[P->ops[opi].level].push_back(Task{opi, s, 1, t});
+      for (uint32_t t = 0; t < tiles; ++t) per_level[P->ops[opi].level].push_back(Task{opi, s, 1, t, 0});
   };
   for (uint32_t i = 0; i < P->ops.size(); ++i) {
     const DevOp& op = P->ops[i];
     const uint64_t MN = uint64_t(op.M) * op.N;
     switch (op.kind) {
       case K_GATHER: {
-        uint64_t total = 0;
-        for (uint32_t k = 0; k < op.nseg; ++k) total += P->segs[op.seg0 + k].n;
-        // ~64 KB of data per task
-        uint32_t tiles = static_cast<uint32_t>(std::max<uint64_t>(1, (total + 4095) / 4096));
-        per_seq(i, tiles);
+        // runs of whole segments of about kGatherChunkUnits units per task
+        uint32_t first = 0;
+        uint64_t acc_units = 0;
+        for (uint32_t k = 0; k < op.nseg; ++k) {
+          const uint64_t n = P->segs[op.seg0 + k].n;
+          if (k > first && acc_units + n > kGatherChunkUnits) {
+            for (uint32_t s = 0; s < B; ++s) per_level[op.level].push_back(Task{i, s, 1, first, k});
+            first = k;
+            acc_units = 0;
+          }
+          acc_units += n;
+        }
+        if (op.nseg > first)
+          for (uint32_t s = 0; s < B; ++s) per_level[op.level].push_back(Task{i, s, 1, first, op.nseg});
         break;
       }
       case K_MATMUL: {
@@ -1028,14 +1138,14 @@ void Compiler::build_tasks() {
           const uint32_t spt = std::max<uint32_t>(1, 128 / op.M);
           for (uint32_t s = 0; s < B; s += spt)
             for (uint32_t t = 0; t < ntile; ++t)
-              per_level[op.level].push_back(Task{i, s, std::min(spt, B - s), t});
+              per_level[op.level].push_back(Task{i, s, std::min(spt, B - s), t, 0});
         }
         break;
       }
       case K_SREG_LOAD:
       case K_SREG_FINAL: {
         for (uint32_t s = 0; s < B; s += 256)
-          per_level[op.level].push_back(Task{i, s, std::min<uint32_t>(256, B - s), 0});
+          per_level[op.level].push_back(Task{i, s, std::min<uint32_t>(256, B - s), 0, 0});
         break;
       }
       case K_MAX_ABS:
@@ -1051,8 +1161,8 @@ void Compiler::build_tasks() {
       case K_TRANSPOSE:
         per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + 16383) / 16384)));
         break;
-      default: {  // element-wise ops: 4096 elements per task
-        per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + 4095) / 4096)));
+      default: {  // element-wise ops: kEwTaskElems elements per task
+        per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + kEwTaskElems - 1) / kEwTaskElems)));
         break;
       }
     }
@@ -1074,6 +1184,7 @@ int Compiler::compile() {
   rw_rl_.assign(rw_units_, 0);
   home_rl_.assign(kSramUnits, 0);
   slot_lvl_.assign(kSregSlotBase, 0);
+  rw_home_read_.assign(rw_units_, 0);
   insn_region_bytes_ = n_insns_ * 8;
 
   // var sites
@@ -1154,6 +1265,17 @@ int Compiler::compile() {
   I.final_regs.attn_mode = attn_mode_;
   P->arena_units = arena_top_;
   P->n_slots = n_slots_;
+  P->cse_hits = cse_hits_;
+  P->sram_home_read = sram_home_read_;
+  P->sreg_home_read = sreg_home_read_;
+  P->home_read_ranges.clear();
+  for (uint64_t i = 0; i < rw_units_;) {
+    if (!rw_home_read_[i]) { ++i; continue; }
+    uint64_t j = i;
+    while (j < rw_units_ && rw_home_read_[j]) ++j;
+    P->home_read_ranges.push_back({shared_bytes_ + i * kUnit, shared_bytes_ + j * kUnit});
+    i = j;
+  }
   return 0;
 }
 
@@ -1161,13 +1283,13 @@ int Compiler::compile() {
 }  // namespace tac
 
 // ------------------------------------------------------------------------------------
-extern "C" int tac_compile(int batch, uint64_t dram_bytes, uint64_t shared_bytes,
-                           const uint8_t* insn_bytes, uint64_t n_insns, uint64_t entry_pc,
-                           uint64_t max_insns, const tac_regs* init_regs, int sregs_reset,
-                           const tac_var_site* sites, int n_sites, tac_program** out,
-                           tac_exec_info* info, tac_fault* fault) {
+extern "C" int tac_compile_ex(int batch, uint64_t dram_bytes, uint64_t shared_bytes,
+                              const uint8_t* insn_bytes, uint64_t n_insns, uint64_t entry_pc,
+                              uint64_t max_insns, const tac_regs* init_regs, int sregs_reset,
+                              const tac_var_site* sites, int n_sites, const tac_compile_opts* opts,
+                              tac_program** out, tac_exec_info* info, tac_fault* fault) {
   if (!out || !insn_bytes || batch <= 0 || shared_bytes > dram_bytes || (shared_bytes % 16) ||
-      n_sites < 0 || (n_sites > 0 && !sites))
+      n_sites < 0 || (n_sites > 0 && !sites) || (opts && opts->n_live && !opts->live))
     return TAC_E_ARGUMENT;
   *out = nullptr;
   tac_program* p = new (std::nothrow) tac_program();
@@ -1176,6 +1298,7 @@ extern "C" int tac_compile(int batch, uint64_t dram_bytes, uint64_t shared_bytes
   p->dram_bytes = dram_bytes;
   p->shared_bytes = shared_bytes;
   tac::Compiler c(p, insn_bytes, n_insns, entry_pc, max_insns, init_regs, sregs_reset, sites, n_sites);
+  c.opts_ = opts;
   int s = c.compile();
   if (fault) *fault = p->fault;
   if (s) {  // the stream cannot be planned at all
@@ -1184,6 +1307,29 @@ extern "C" int tac_compile(int batch, uint64_t dram_bytes, uint64_t shared_bytes
   }
   if (info) *info = p->info;
   *out = p;
+  return TAC_OK;
+}
+
+extern "C" int tac_compile(int batch, uint64_t dram_bytes, uint64_t shared_bytes,
+                           const uint8_t* insn_bytes, uint64_t n_insns, uint64_t entry_pc,
+                           uint64_t max_insns, const tac_regs* init_regs, int sregs_reset,
+                           const tac_var_site* sites, int n_sites, tac_program** out,
+                           tac_exec_info* info, tac_fault* fault) {
+  return tac_compile_ex(batch, dram_bytes, shared_bytes, insn_bytes, n_insns, entry_pc, max_insns, init_regs,
+                        sregs_reset, sites, n_sites, nullptr, out, info, fault);
+}
+
+extern "C" int tac_program_home_reads(const tac_program* p, uint64_t* ranges, uint32_t max_ranges,
+                                      uint32_t* n_ranges, int32_t* sram_read, int32_t* sregs_read) {
+  if (!p) return TAC_E_ARGUMENT;
+  const uint32_t n = static_cast<uint32_t>(p->home_read_ranges.size());
+  if (n_ranges) *n_ranges = n;
+  for (uint32_t i = 0; ranges && i < n && i < max_ranges; ++i) {
+    ranges[2 * i] = p->home_read_ranges[i].first;
+    ranges[2 * i + 1] = p->home_read_ranges[i].second;
+  }
+  if (sram_read) *sram_read = p->sram_home_read ? 1 : 0;
+  if (sregs_read) *sregs_read = p->sreg_home_read ? 1 : 0;
   return TAC_OK;
 }
 

@@ -28,6 +28,18 @@ struct tac_engine {
   int n_sms = 0;
   int grid = 0;
   std::vector<uint64_t> h_params;
+  // pinned staging ring for parameter uploads: slot i is reusable once its
+  // copy (event i) has completed, so several runs can be in flight
+  static constexpr int kRing = 4;
+  uint64_t* h_pinned = nullptr;
+  size_t pinned_cap = 0;        // words per slot
+  cudaEvent_t ring_ev[kRing] = {};
+  uint64_t* d_prof = nullptr;     // per-level timestamps when profiling is on
+  size_t prof_cap = 0;
+  bool profiling = false;
+  uint32_t prof_levels = 0;
+  bool ring_used[kRing] = {};
+  int ring_next = 0;
 };
 
 namespace {
@@ -209,6 +221,10 @@ int tac_engine_destroy(tac_engine* e) {
   cudaFree(e->d_sregs);
   cudaFree(e->d_params);
   cudaFree(e->d_status);
+  cudaFree(e->d_prof);
+  if (e->h_pinned) cudaFreeHost(e->h_pinned);
+  for (int i = 0; i < tac_engine::kRing; ++i)
+    if (e->ring_ev[i]) cudaEventDestroy(e->ring_ev[i]);
   delete e;
   return TAC_OK;
 }
@@ -305,30 +321,17 @@ int tac_program_destroy(tac_program* p) {
   return TAC_OK;
 }
 
-int tac_run_async(tac_engine* e, tac_program* p, const uint64_t* var_words, void* stream, tac_fault* f) {
+static int prepare(tac_engine* e, tac_program* p, tac_fault* f) {
   if (!e || !p || p->batch != e->batch || p->dram_bytes != e->dram_bytes || p->shared_bytes != e->shared_bytes)
     return set_fault(f, TAC_E_ARGUMENT, "program was compiled for a different engine layout");
-  if (p->n_var_words && !var_words) return set_fault(f, TAC_E_ARGUMENT, "missing runtime words");
   CK(cudaSetDevice(e->device), f, "cudaSetDevice");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (int s = upload_program(e, p, f)) return s;
   if (int s = ensure_arena(e, p->arena_units * 16, f)) return s;
   if (int s = ensure_sregs(e, p->n_slots, f)) return s;
-  const uint32_t np = std::max<uint32_t>(p->n_params, 1);
-  e->h_params.assign(size_t(np) * e->batch, 0);
-  for (int s = 0; s < e->batch && p->n_params; ++s) {
-    if (int r = decode_params(p, var_words + size_t(s) * p->n_var_words, e->h_params.data() + size_t(s) * np, f)) {
-      if (f) f->buf_id = s;
-      return r;
-    }
-  }
-  if (e->params_cap < e->h_params.size()) {
-    cudaFree(e->d_params);
-    e->params_cap = std::max<size_t>(e->h_params.size(), 1024);
-    CK(cudaMalloc(&e->d_params, e->params_cap * 8), f, "cudaMalloc params");
-  }
-  CK(cudaMemcpyAsync(e->d_params, e->h_params.data(), e->h_params.size() * 8, cudaMemcpyHostToDevice, st), f,
-     "upload params");
+  return TAC_OK;
+}
+
+static int launch(tac_engine* e, tac_program* p, const uint64_t* d_params, cudaStream_t st, tac_fault* f) {
   CK(cudaMemsetAsync(e->d_status, 0, 64, st), f, "reset status");
   const uint32_t n_levels = static_cast<uint32_t>(p->level_off.size() - 1);
   if (n_levels > 0 && !p->tasks.empty()) {
@@ -339,17 +342,28 @@ int tac_run_async(tac_engine* e, tac_program* p, const uint64_t* var_words, void
     A.tasks = reinterpret_cast<const Task*>(blob + p->off_tasks);
     A.level_off = reinterpret_cast<const uint32_t*>(blob + p->off_levels);
     A.n_levels = n_levels;
-    A.n_params = np;
+    A.n_params = std::max<uint32_t>(p->n_params, 1);
     A.seq_base = e->d_seq;
     A.seq_stride = e->seq_stride;
     A.shared_base = e->d_shared;
     A.sregs = e->d_sregs;
     A.sreg_stride = e->sreg_stride;
-    A.params = e->d_params;
+    A.params = d_params;
     A.status = e->d_status;
     A.barrier = e->d_status + 4;
     A.shared_bytes = e->shared_bytes;
     A.dram_bytes = e->dram_bytes;
+    A.prof = nullptr;
+    if (e->profiling) {
+      if (e->prof_cap < n_levels + 1) {
+        cudaFree(e->d_prof);
+        e->prof_cap = n_levels + 1024;
+        CK(cudaMalloc(&e->d_prof, e->prof_cap * 8), f, "cudaMalloc profile");
+      }
+      CK(cudaMemsetAsync(e->d_prof, 0, (n_levels + 1) * 8, st), f, "reset profile");
+      A.prof = e->d_prof;
+      e->prof_levels = n_levels;
+    }
     void* args[] = {&A};
     CK(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(exec_kernel), dim3(e->grid), dim3(kThreads), args,
                                    kExecSmem, st), f, "launch executor");
@@ -359,6 +373,59 @@ int tac_run_async(tac_engine* e, tac_program* p, const uint64_t* var_words, void
     return p->fault.status;
   }
   return TAC_OK;
+}
+
+uint64_t tac_program_param_count(const tac_program* p) { return p ? std::max<uint32_t>(p->n_params, 1) : 0; }
+
+int tac_encode_params(const tac_program* p, int batch, const uint64_t* var_words, uint64_t* out, tac_fault* f) {
+  if (!p || !out || batch <= 0 || (p->n_var_words && !var_words)) return set_fault(f, TAC_E_ARGUMENT, "bad arguments");
+  const uint32_t np = std::max<uint32_t>(p->n_params, 1);
+  std::memset(out, 0, sizeof(uint64_t) * np * batch);
+  for (int s = 0; s < batch && p->n_params; ++s) {
+    if (int r = decode_params(p, var_words + size_t(s) * p->n_var_words, out + size_t(s) * np, f)) {
+      if (f) f->buf_id = s;
+      return r;
+    }
+  }
+  return TAC_OK;
+}
+
+int tac_run_async_params(tac_engine* e, tac_program* p, const uint64_t* params_dev, void* stream, tac_fault* f) {
+  if (int s = prepare(e, p, f)) return s;
+  if (p->n_params && !params_dev) return set_fault(f, TAC_E_ARGUMENT, "missing parameters");
+  return launch(e, p, p->n_params ? params_dev : reinterpret_cast<const uint64_t*>(e->d_status + 8), static_cast<cudaStream_t>(stream), f);
+}
+
+int tac_run_async(tac_engine* e, tac_program* p, const uint64_t* var_words, void* stream, tac_fault* f) {
+  if (int s = prepare(e, p, f)) return s;
+  if (p->n_var_words && !var_words) return set_fault(f, TAC_E_ARGUMENT, "missing runtime words");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint32_t np = std::max<uint32_t>(p->n_params, 1);
+  const size_t n = size_t(np) * e->batch;
+  if (e->pinned_cap < n || e->params_cap < n) {
+    CK(cudaDeviceSynchronize(), f, "sync");
+    if (e->h_pinned) cudaFreeHost(e->h_pinned);
+    e->h_pinned = nullptr;
+    e->pinned_cap = std::max<size_t>(n, 4096);
+    CK(cudaMallocHost(&e->h_pinned, e->pinned_cap * 8 * tac_engine::kRing), f, "cudaMallocHost");
+    cudaFree(e->d_params);
+    e->params_cap = e->pinned_cap;
+    CK(cudaMalloc(&e->d_params, e->params_cap * 8 * tac_engine::kRing), f, "cudaMalloc params");
+    for (int i = 0; i < tac_engine::kRing; ++i) {
+      if (!e->ring_ev[i]) CK(cudaEventCreateWithFlags(&e->ring_ev[i], cudaEventDisableTiming), f, "event");
+      e->ring_used[i] = false;
+    }
+  }
+  const int slot = e->ring_next;
+  e->ring_next = (slot + 1) % tac_engine::kRing;
+  if (e->ring_used[slot]) CK(cudaEventSynchronize(e->ring_ev[slot]), f, "staging slot");
+  uint64_t* h = e->h_pinned + size_t(slot) * e->pinned_cap;
+  uint64_t* d = e->d_params + size_t(slot) * e->params_cap;
+  if (int r = tac_encode_params(p, e->batch, var_words, h, f)) return r;
+  CK(cudaMemcpyAsync(d, h, n * 8, cudaMemcpyHostToDevice, st), f, "upload params");
+  CK(cudaEventRecord(e->ring_ev[slot], st), f, "record staging event");
+  e->ring_used[slot] = true;
+  return launch(e, p, d, st, f);
 }
 
 int tac_check_device_status(tac_engine* e, tac_fault* f) {
@@ -392,6 +459,22 @@ int tac_run(tac_engine* e, tac_program* p, const uint64_t* var_words, tac_fault*
     return ds;
   }
   return compiled_fault;
+}
+
+int tac_set_profiling(tac_engine* e, int enable) {
+  if (!e) return TAC_E_ARGUMENT;
+  e->profiling = enable != 0;
+  return TAC_OK;
+}
+
+int tac_read_profile(tac_engine* e, uint64_t* out_ns, uint32_t max_entries, uint32_t* n_entries) {
+  if (!e || !n_entries) return TAC_E_ARGUMENT;
+  *n_entries = e->prof_levels ? e->prof_levels + 1 : 0;
+  if (!out_ns || !e->d_prof || !e->prof_levels) return TAC_OK;
+  if (cudaSetDevice(e->device) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) return TAC_E_CUDA;
+  const uint32_t n = std::min<uint32_t>(max_entries, e->prof_levels + 1);
+  if (cudaMemcpy(out_ns, e->d_prof, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return TAC_E_CUDA;
+  return TAC_OK;
 }
 
 int tac_argmax_f16(tac_engine* e, uint64_t addr, uint64_t count, int32_t* out_tokens_dev, void* stream) {

@@ -45,7 +45,14 @@ struct ExecArgs {
   uint32_t* barrier;         // [0] arrivals, [1] generation
   uint64_t shared_bytes;
   uint64_t dram_bytes;
+  uint64_t* prof;            // optional: globaltimer at the end of each level (n_levels + 1)
 };
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint8_t* pptr(const ExecArgs& A, uint64_t phys, uint32_t seq) {
   if (phys & kSharedBit) return const_cast<uint8_t*>(A.shared_base) + ((phys & ~kSharedBit) << 4);
@@ -76,25 +83,18 @@ __device__ __forceinline__ uint8_t* dram_ptr(const ExecArgs& A, uint64_t addr, u
 // ---------------------------------------------------------------------------------
 // Data movement
 // ---------------------------------------------------------------------------------
-__device__ void op_gather(const ExecArgs& A, const DevOp& op, const Task& t) {
-  const uint64_t lo = uint64_t(t.tile) * 4096, hi = lo + 4096;
-  uint64_t base = 0;
-  for (uint32_t k = 0; k < op.nseg; ++k) {
+__device__ __noinline__ void op_gather(const ExecArgs& A, const DevOp& op, const Task& t) {
+  // segments [t.tile, t.aux) of the op; one warp per segment
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (uint32_t k = t.tile + warp; k < t.aux; k += kWarps) {
     const Segment sg = A.segs[op.seg0 + k];
-    const uint64_t s0 = base > lo ? base : lo;
-    const uint64_t e = base + sg.n;
-    const uint64_t s1 = e < hi ? e : hi;
-    if (s0 < s1) {
-      const uint4* src = reinterpret_cast<const uint4*>(pptr(A, sg.src + (s0 - base), t.seq0));
-      uint4* dst = reinterpret_cast<uint4*>(pptr(A, sg.dst + (s0 - base), t.seq0));
-      for (uint64_t u = threadIdx.x; u < s1 - s0; u += blockDim.x) dst[u] = src[u];
-    }
-    base = e;
-    if (base >= hi) break;
+    const uint4* src = reinterpret_cast<const uint4*>(pptr(A, sg.src, t.seq0));
+    uint4* dst = reinterpret_cast<uint4*>(pptr(A, sg.dst, t.seq0));
+    for (uint64_t u = lane; u < sg.n; u += 32) dst[u] = src[u];
   }
 }
 
-__device__ void op_dyn_copy(const ExecArgs& A, const DevOp& op, const Task& t, uint32_t opi) {
+__device__ __noinline__ void op_dyn_copy(const ExecArgs& A, const DevOp& op, const Task& t, uint32_t opi) {
   const uint32_t seq = t.seq0;
   const uint64_t addr = A.params[uint64_t(seq) * A.n_params + op.param] + op.dconst;
   if ((addr & 15) || addr + op.nbytes > A.dram_bytes) {
@@ -118,7 +118,7 @@ __device__ void op_dyn_copy(const ExecArgs& A, const DevOp& op, const Task& t, u
   for (uint64_t u = threadIdx.x; u < n; u += blockDim.x) dst[u] = src[u];
 }
 
-__device__ void op_transpose(const ExecArgs& A, const DevOp& op, const Task& t) {
+__device__ __noinline__ void op_transpose(const ExecArgs& A, const DevOp& op, const Task& t) {
   const int8_t* src = reinterpret_cast<const int8_t*>(pptr(A, op.a, t.seq0));
   int8_t* dst = reinterpret_cast<int8_t*>(pptr(A, op.d, t.seq0));
   const uint64_t rows = op.M, cols = op.N, total = rows * cols;
@@ -129,14 +129,14 @@ __device__ void op_transpose(const ExecArgs& A, const DevOp& op, const Task& t) 
   }
 }
 
-__device__ void op_sreg_load(const ExecArgs& A, const DevOp& op, const Task& t) {
+__device__ __noinline__ void op_sreg_load(const ExecArgs& A, const DevOp& op, const Task& t) {
   for (uint32_t s = t.seq0 + threadIdx.x; s < t.seq0 + t.nseq; s += blockDim.x) {
     const uint16_t v = *reinterpret_cast<const uint16_t*>(pptr(A, op.a, s));
     A.sregs[uint64_t(s) * A.sreg_stride + op.out_slot] = v;
   }
 }
 
-__device__ void op_sreg_final(const ExecArgs& A, const DevOp& op, const Task& t) {
+__device__ __noinline__ void op_sreg_final(const ExecArgs& A, const DevOp& op, const Task& t) {
   for (uint32_t s = t.seq0 + threadIdx.x; s < t.seq0 + t.nseq; s += blockDim.x) {
     uint16_t vals[16];
     for (uint32_t k = 0; k < op.nseg && k < 16; ++k)
@@ -150,9 +150,12 @@ __device__ void op_sreg_final(const ExecArgs& A, const DevOp& op, const Task& t)
 // MATMUL: int8 x int8 -> int32 on the tensor cores (mma.sync m16n8k32).
 // A task covers up to 128 rows (whole sequences when B is shared) x 64 columns.
 // ---------------------------------------------------------------------------------
-constexpr int kMmKc = 128;            // K chunk
-constexpr int kMmAStride = kMmKc + 16; // padded row stride (bytes) in shared memory
-constexpr int kMmBStride = kMmKc + 16;
+constexpr int kMmKc = 128;             // K chunk (bytes of A rows / rows of B)
+constexpr int kMmStages = 3;           // cp.async pipeline depth
+constexpr int kMmAStage = 128 * kMmKc; // 8 row blocks x 16 rows x K chunk
+constexpr int kMmBStage = kMmKc * 64;  // K chunk x 64 columns, raw [k][n]
+constexpr int kMmBStride = kMmKc + 16; // transposed B row stride [n][k] (bytes)
+constexpr size_t kMmSmem = size_t(kMmStages) * (kMmAStage + kMmBStage) + 64 * kMmBStride;
 
 __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                        uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -163,7 +166,15 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, ui
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ void op_matmul(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, uint32_t src_bytes) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gsrc), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
   const uint32_t M = op.M, N = op.N, K = op.K;
   const uint32_t ntile = (N + 63) / 64;
   const bool grouped = (op.b & kSharedBit) && M < 128;
@@ -181,8 +192,7 @@ __device__ void op_matmul(const ExecArgs& A, const DevOp& op, const Task& t, uin
       }
   } else {
     n0 = (t.tile % ntile) * 64;
-    const uint32_t mchunk = t.tile / ntile;
-    const uint32_t r0 = mchunk * 128;
+    const uint32_t r0 = (t.tile / ntile) * 128;
     nblocks = 0;
     for (uint32_t r = r0; r < M && nblocks < 8; r += 16) {
       blk_seq[nblocks] = t.seq0;
@@ -191,11 +201,11 @@ __device__ void op_matmul(const ExecArgs& A, const DevOp& op, const Task& t, uin
     }
   }
   const uint32_t ncols = N - n0 < 64 ? N - n0 : 64;
-  uint8_t* As = smem;                        // [8][16][kMmAStride]
-  uint8_t* Bs = smem + 8 * 16 * kMmAStride;  // [64][kMmBStride]  (n-major, k contiguous)
+  uint8_t* As = smem;                                    // [stage][blk*16 + row][kMmKc]
+  uint8_t* Bs = smem + kMmStages * kMmAStage;            // [stage][k][64] raw
+  uint8_t* Bt = Bs + kMmStages * kMmBStage;              // [n][kMmBStride] transposed
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
-  // each warp owns pairs p = warp + 8*i  (row block p/8, n-subtile p%8)
   int acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -203,36 +213,60 @@ __device__ void op_matmul(const ExecArgs& A, const DevOp& op, const Task& t, uin
     for (int j = 0; j < 4; ++j) acc[i][j] = 0;
 
   const uint8_t* Bg = pptr(A, op.b, t.seq0);
-  for (uint32_t k0 = 0; k0 < K; k0 += kMmKc) {
+  const uint8_t* Ag[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) Ag[i] = i < int(nblocks) ? pptr(A, op.a, blk_seq[i]) + uint64_t(blk_row[i]) * K : nullptr;
+  const uint32_t nchunks = (K + kMmKc - 1) / kMmKc;
+
+  // issues the cp.async copies of chunk c into pipeline slot c % kMmStages
+  auto issue = [&](uint32_t c) {
+    const uint32_t k0 = c * kMmKc;
+    const uint32_t kc = K - k0 < uint32_t(kMmKc) ? K - k0 : uint32_t(kMmKc);
+    uint8_t* as = As + (c % kMmStages) * kMmAStage;
+    uint8_t* bs = Bs + (c % kMmStages) * kMmBStage;
+    // A: nblocks*16 rows x 8 vectors of 16 bytes
+    for (uint32_t i = threadIdx.x; i < nblocks * 16 * (kMmKc / 16); i += blockDim.x) {
+      const uint32_t v = i % (kMmKc / 16), row = i / (kMmKc / 16);
+      const bool in = v * 16 < kc;
+      const uint8_t* src = Ag[row / 16] + uint64_t(row % 16) * K + k0 + (in ? v * 16 : 0);
+      cp_async16(as + row * kMmKc + v * 16, src, in ? 16u : 0u);
+    }
+    // B: kMmKc rows x 4 vectors of 16 bytes (64 columns)
+    for (uint32_t i = threadIdx.x; i < uint32_t(kMmKc) * 4; i += blockDim.x) {
+      const uint32_t v = i % 4, kk = i / 4;
+      const bool in = kk < kc && v * 16 < ncols;
+      const uint8_t* src = Bg + (in ? uint64_t(k0 + kk) * N + n0 + v * 16 : 0);
+      cp_async16(bs + kk * 64 + v * 16, src, in ? 16u : 0u);
+    }
+  };
+
+#pragma unroll
+  for (int sidx = 0; sidx < kMmStages - 1; ++sidx) {
+    if (uint32_t(sidx) < nchunks) issue(sidx);
+    cp_async_commit();
+  }
+  for (uint32_t c = 0; c < nchunks; ++c) {
+    cp_async_wait<kMmStages - 2>();
+    __syncthreads();   // chunk c landed; every warp finished chunk c-1 (slot and Bt free)
+    if (c + kMmStages - 1 < nchunks) issue(c + kMmStages - 1);
+    cp_async_commit();
+    const uint32_t k0 = c * kMmKc;
     const uint32_t kc = K - k0 < uint32_t(kMmKc) ? K - k0 : uint32_t(kMmKc);
     const uint32_t kc32 = (kc + 31) & ~31u;
-    __syncthreads();
-    // A chunk: 16-byte vectors
-    for (uint32_t i = threadIdx.x; i < nblocks * 16 * (kc32 / 16); i += blockDim.x) {
-      const uint32_t v = i % (kc32 / 16), row = (i / (kc32 / 16)) % 16, blk = i / (kc32 / 16) / 16;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      if (v * 16 < kc) {
-        const uint8_t* src = pptr(A, op.a, blk_seq[blk]) + uint64_t(blk_row[blk] + row) * K + k0 + v * 16;
-        val = *reinterpret_cast<const uint4*>(src);
-      }
-      *reinterpret_cast<uint4*>(As + (blk * 16 + row) * kMmAStride + v * 16) = val;
-    }
-    // B chunk transposed into Bs[n][k]: each thread handles a 4(k) x 4(n) block
+    const uint8_t* as = As + (c % kMmStages) * kMmAStage;
+    const uint8_t* bs = Bs + (c % kMmStages) * kMmBStage;
+    // transpose B [k][n] -> Bt [n][k], 4x4 byte blocks
     for (uint32_t i = threadIdx.x; i < (kc32 / 4) * 16; i += blockDim.x) {
       const uint32_t kb = (i / 16) * 4, nb = (i % 16) * 4;
       uint32_t r[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        r[j] = 0;
-        if (kb + j < kc && nb < ncols)
-          r[j] = *reinterpret_cast<const uint32_t*>(Bg + uint64_t(k0 + kb + j) * N + n0 + nb);
-      }
+      for (int j = 0; j < 4; ++j) r[j] = *reinterpret_cast<const uint32_t*>(bs + (kb + j) * 64 + nb);
       const uint32_t t0 = __byte_perm(r[0], r[1], 0x5140), t1 = __byte_perm(r[2], r[3], 0x5140);
       const uint32_t t2 = __byte_perm(r[0], r[1], 0x7362), t3 = __byte_perm(r[2], r[3], 0x7362);
-      *reinterpret_cast<uint32_t*>(Bs + (nb + 0) * kMmBStride + kb) = __byte_perm(t0, t1, 0x5410);
-      *reinterpret_cast<uint32_t*>(Bs + (nb + 1) * kMmBStride + kb) = __byte_perm(t0, t1, 0x7632);
-      *reinterpret_cast<uint32_t*>(Bs + (nb + 2) * kMmBStride + kb) = __byte_perm(t2, t3, 0x5410);
-      *reinterpret_cast<uint32_t*>(Bs + (nb + 3) * kMmBStride + kb) = __byte_perm(t2, t3, 0x7632);
+      *reinterpret_cast<uint32_t*>(Bt + (nb + 0) * kMmBStride + kb) = __byte_perm(t0, t1, 0x5410);
+      *reinterpret_cast<uint32_t*>(Bt + (nb + 1) * kMmBStride + kb) = __byte_perm(t0, t1, 0x7632);
+      *reinterpret_cast<uint32_t*>(Bt + (nb + 2) * kMmBStride + kb) = __byte_perm(t2, t3, 0x5410);
+      *reinterpret_cast<uint32_t*>(Bt + (nb + 3) * kMmBStride + kb) = __byte_perm(t2, t3, 0x7632);
     }
     __syncthreads();
 #pragma unroll
@@ -240,10 +274,11 @@ __device__ void op_matmul(const ExecArgs& A, const DevOp& op, const Task& t, uin
       const uint32_t p = warp + 8 * i;
       const uint32_t blk = p / 8, ns = p % 8;
       if (blk >= nblocks || ns * 8 >= ncols) continue;
-      const uint8_t* a_row0 = As + (blk * 16 + g) * kMmAStride;
-      const uint8_t* a_row8 = As + (blk * 16 + g + 8) * kMmAStride;
-      const uint8_t* b_col = Bs + (ns * 8 + g) * kMmBStride;
+      const uint8_t* a_row0 = as + (blk * 16 + g) * kMmKc;
+      const uint8_t* a_row8 = as + (blk * 16 + g + 8) * kMmKc;
+      const uint8_t* b_col = Bt + (ns * 8 + g) * kMmBStride;
       for (uint32_t ks = 0; ks < kc32; ks += 32) {
+        // A rows are kMmKc = 128 bytes apart: rotate the 16-byte quad by row to spread banks
         const uint32_t a0 = *reinterpret_cast<const uint32_t*>(a_row0 + ks + q * 4);
         const uint32_t a1 = *reinterpret_cast<const uint32_t*>(a_row8 + ks + q * 4);
         const uint32_t a2 = *reinterpret_cast<const uint32_t*>(a_row0 + ks + 16 + q * 4);
@@ -254,6 +289,7 @@ __device__ void op_matmul(const ExecArgs& A, const DevOp& op, const Task& t, uin
       }
     }
   }
+  cp_async_wait<0>();
   // epilogue
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -269,121 +305,258 @@ __device__ void op_matmul(const ExecArgs& A, const DevOp& op, const Task& t, uin
       const uint64_t row = blk_row[blk] + g + 8 * h;
       int2 v = make_int2(acc[i][2 * h], acc[i][2 * h + 1]);
       if (C) {
-        const int2 c = *reinterpret_cast<const int2*>(C + row * N + col);
+        const int2 c = __ldcg(reinterpret_cast<const int2*>(C + row * N + col));
         v.x = static_cast<int32_t>(static_cast<uint32_t>(v.x) + static_cast<uint32_t>(c.x));
         v.y = static_cast<int32_t>(static_cast<uint32_t>(v.y) + static_cast<uint32_t>(c.y));
       }
       *reinterpret_cast<int2*>(D + row * N + col) = v;
     }
   }
+  __syncthreads();
 }
 
 // ---------------------------------------------------------------------------------
-// Element-wise ops (4096 elements of one sequence per task)
+// Element-wise ops.  A task covers kEwTask elements of one sequence; each
+// thread owns groups of 8 consecutive elements (8 never straddle a row: N is
+// a multiple of 16) and issues every load of its groups before computing, so
+// the memory latency is paid once per task rather than once per element.
 // ---------------------------------------------------------------------------------
-__device__ void op_elementwise(const ExecArgs& A, const DevOp& op, const Task& t) {
+constexpr uint32_t kEwGroups = 4;                       // groups of 8 per thread
+constexpr uint32_t kEwTask = kThreads * kEwGroups * 8;   // 8192 elements per task
+static_assert(kEwTask == kEwTaskElems, "host and device element-wise task sizes differ");
+
+struct V8 { uint4 lo, hi; };   // 8 x 32-bit values
+
+// Operands are written by other CTAs in earlier levels of the same launch, so
+// loads go through L2 (ld.global.cg), never the non-coherent read-only path.
+__device__ __forceinline__ uint4 ld16(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ uint2 ld8(const void* p) { return __ldcg(reinterpret_cast<const uint2*>(p)); }
+__device__ __forceinline__ V8 ld32(const void* p) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+  return V8{__ldcg(q), __ldcg(q + 1)};
+}
+__device__ __forceinline__ uint16_t h_at(const uint4& v, int j) {
+  const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
+  return static_cast<uint16_t>(j & 1 ? w >> 16 : w & 0xFFFF);
+}
+__device__ __forceinline__ int32_t i_at(const V8& v, int j) {
+  const uint4& q = j < 4 ? v.lo : v.hi;
+  const int k = j & 3;
+  return static_cast<int32_t>(k == 0 ? q.x : k == 1 ? q.y : k == 2 ? q.z : q.w);
+}
+__device__ __forceinline__ int8_t b_at(const uint2& v, int j) {
+  const uint32_t w = j < 4 ? v.x : v.y;
+  return static_cast<int8_t>((w >> (8 * (j & 3))) & 0xFF);
+}
+__device__ __forceinline__ uint4 pack_h(const uint16_t (&h)[8]) {
+  return make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                    h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+}
+__device__ __forceinline__ uint2 pack_b(const int8_t (&q)[8]) {
+  uint32_t x = 0, y = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    x |= uint32_t(uint8_t(q[j])) << (8 * j);
+    y |= uint32_t(uint8_t(q[j + 4])) << (8 * j);
+  }
+  return make_uint2(x, y);
+}
+
+template <int KIND>
+__device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const Task& t) {
   const uint32_t seq = t.seq0, N = op.N;
   const uint64_t MN = uint64_t(op.M) * N;
-  const uint64_t lo = uint64_t(t.tile) * 4096, hi = lo + 4096 < MN ? lo + 4096 : MN;
-  const uint8_t* a = pptr(A, op.a, seq);
-  const uint8_t* b = (op.kind == K_VADD_I8 || op.kind == K_VADD_I32 || op.kind == K_DEQUANT_ADD ||
-                      op.kind == K_DEQUANT_ACCUM || op.kind == K_DEQUANT_SCALED ||
-                      op.kind == K_VADD_F16 || op.kind == K_REQUANT_PC)
-                         ? pptr(A, op.b, seq) : nullptr;
-  uint8_t* d = pptr(A, op.d, seq);
+  const uint64_t base = uint64_t(t.tile) * kEwTask;
+  const uint8_t* __restrict__ a = pptr(A, op.a, seq);
+  const uint8_t* __restrict__ b = pptr(A, op.b, seq);
+  uint8_t* __restrict__ d = pptr(A, op.d, seq);
   const float s0 = sreg_f32(A, op.s[0], seq);
   const float s1 = sreg_f32(A, op.s[1], seq);
-  for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-    const uint32_t col = static_cast<uint32_t>(i % N);
-    switch (op.kind) {
-      case K_REQUANT:
-        reinterpret_cast<int8_t*>(d)[i] =
-            sat8(__fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]), s0));
-        break;
-      case K_REQUANT_PC:
-        reinterpret_cast<int8_t*>(d)[i] =
-            sat8(__fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]),
-                           h2f(reinterpret_cast<const uint16_t*>(b)[col])));
-        break;
-      case K_SCALE_MUL_I32:
-        reinterpret_cast<int32_t*>(d)[i] =
-            sat32(__fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]), s0));
-        break;
-      case K_SCALE_MUL_I8:
-        reinterpret_cast<int8_t*>(d)[i] =
-            sat8(__fmul_rn(static_cast<float>(reinterpret_cast<const int8_t*>(a)[i]), s0));
-        break;
-      case K_VADD_I8: {
-        int v = int(reinterpret_cast<const int8_t*>(a)[i]) + int(reinterpret_cast<const int8_t*>(b)[i]);
-        reinterpret_cast<int8_t*>(d)[i] = static_cast<int8_t>(v < -128 ? -128 : (v > 127 ? 127 : v));
-        break;
-      }
-      case K_VADD_I32:
-        reinterpret_cast<int32_t*>(d)[i] = static_cast<int32_t>(
-            static_cast<uint32_t>(reinterpret_cast<const int32_t*>(a)[i]) +
-            static_cast<uint32_t>(reinterpret_cast<const int32_t*>(b)[col]));
-        break;
-      case K_DEQUANT_ADD: {
-        const float acc = __fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]), s0);
-        const float skip = __fmul_rn(static_cast<float>(reinterpret_cast<const int8_t*>(b)[i]), s1);
-        reinterpret_cast<int8_t*>(d)[i] = sat8(__fadd_rn(acc, skip));
-        break;
-      }
-      case K_DEQUANT_ACCUM:
-        reinterpret_cast<uint16_t*>(d)[i] =
-            f2h(__fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]),
-                          h2f(reinterpret_cast<const uint16_t*>(b)[col])));
-        break;
-      case K_DEQUANT_SCALED: {
-        const uint16_t* pb = reinterpret_cast<const uint16_t*>(b);
-        float v = __fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]), h2f(pb[col]));
-        v = __fmul_rn(v, s0);
-        reinterpret_cast<uint16_t*>(d)[i] = f2h(__fadd_rn(v, h2f(pb[N + col])));
-        break;
-      }
-      case K_QUANT: {
-        const float r = rintf(__fmul_rn(h2f(reinterpret_cast<const uint16_t*>(a)[i]), s0));
-        int8_t o = 0;
-        if (r == r) o = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f)));
-        reinterpret_cast<int8_t*>(d)[i] = o;
-        break;
-      }
-      case K_VADD_F16:
-        reinterpret_cast<uint16_t*>(d)[i] =
-            f2h(__fadd_rn(h2f(reinterpret_cast<const uint16_t*>(a)[i]),
-                          h2f(reinterpret_cast<const uint16_t*>(b)[i])));
-        break;
-      case K_GELU_F16:
-        reinterpret_cast<uint16_t*>(d)[i] = f2h(gelu_f32(h2f(reinterpret_cast<const uint16_t*>(a)[i])));
-        break;
-      case K_GELU_I8: {
-        const float x = (op.flags & F_SRC_I32)
-                            ? __fmul_rn(__int2float_rn(reinterpret_cast<const int32_t*>(a)[i]), s0)
-                            : __fmul_rn(static_cast<float>(reinterpret_cast<const int8_t*>(a)[i]), s0);
-        const float y = gelu_f32(x);
-        reinterpret_cast<int8_t*>(d)[i] = s1 == 0.f ? int8_t(0) : sat8(__fdiv_rn(y, s1));
-        break;
-      }
-      default:
-        break;
+  // phase 1: loads
+  uint4 ra[kEwGroups], rb[kEwGroups], rc[kEwGroups];
+  V8 ia[kEwGroups];
+  uint2 qa[kEwGroups], qb[kEwGroups];
+  uint64_t e0[kEwGroups];
+#pragma unroll
+  for (uint32_t g = 0; g < kEwGroups; ++g) {
+    e0[g] = base + (uint64_t(g) * kThreads + threadIdx.x) * 8;
+    if (e0[g] >= MN) continue;
+    const uint32_t col = static_cast<uint32_t>(e0[g] % N);
+    if constexpr (KIND == K_QUANT || KIND == K_GELU_F16) {
+      ra[g] = ld16(a + e0[g] * 2);
+    } else if constexpr (KIND == K_VADD_F16) {
+      ra[g] = ld16(a + e0[g] * 2);
+      rb[g] = ld16(b + e0[g] * 2);
+    } else if constexpr (KIND == K_DEQUANT_SCALED) {
+      ia[g] = ld32(a + e0[g] * 4);
+      rb[g] = ld16(b + uint64_t(col) * 2);
+      rc[g] = ld16(b + uint64_t(N + col) * 2);
+    } else if constexpr (KIND == K_DEQUANT_ACCUM || KIND == K_REQUANT_PC) {
+      ia[g] = ld32(a + e0[g] * 4);
+      rb[g] = ld16(b + uint64_t(col) * 2);
+    } else if constexpr (KIND == K_REQUANT || KIND == K_SCALE_MUL_I32) {
+      ia[g] = ld32(a + e0[g] * 4);
+    } else if constexpr (KIND == K_VADD_I32) {
+      ia[g] = ld32(a + e0[g] * 4);
+      const uint4* q = reinterpret_cast<const uint4*>(b + uint64_t(col) * 4);
+      rb[g] = __ldcg(q);
+      rc[g] = __ldcg(q + 1);
+    } else if constexpr (KIND == K_SCALE_MUL_I8) {
+      qa[g] = ld8(a + e0[g]);
+    } else if constexpr (KIND == K_VADD_I8) {
+      qa[g] = ld8(a + e0[g]);
+      qb[g] = ld8(b + e0[g]);
+    } else if constexpr (KIND == K_DEQUANT_ADD) {
+      ia[g] = ld32(a + e0[g] * 4);
+      qb[g] = ld8(b + e0[g]);
+    } else if constexpr (KIND == K_GELU_I8) {
+      if (op.flags & F_SRC_I32) ia[g] = ld32(a + e0[g] * 4);
+      else qa[g] = ld8(a + e0[g]);
     }
+  }
+  // phase 2: compute and store
+#pragma unroll
+  for (uint32_t g = 0; g < kEwGroups; ++g) {
+    if (e0[g] >= MN) continue;
+    if constexpr (KIND == K_QUANT) {
+      int8_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float r = rintf(__fmul_rn(h2f(h_at(ra[g], j)), s0));
+        q[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+      }
+      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+    } else if constexpr (KIND == K_GELU_F16) {
+      uint16_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = f2h(gelu_f32(h2f(h_at(ra[g], j))));
+      *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
+    } else if constexpr (KIND == K_VADD_F16) {
+      uint16_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = f2h(__fadd_rn(h2f(h_at(ra[g], j)), h2f(h_at(rb[g], j))));
+      *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
+    } else if constexpr (KIND == K_DEQUANT_SCALED) {
+      uint16_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float v = __fmul_rn(__int2float_rn(i_at(ia[g], j)), h2f(h_at(rb[g], j)));
+        v = __fmul_rn(v, s0);
+        h[j] = f2h(__fadd_rn(v, h2f(h_at(rc[g], j))));
+      }
+      *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
+    } else if constexpr (KIND == K_DEQUANT_ACCUM) {
+      uint16_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = f2h(__fmul_rn(__int2float_rn(i_at(ia[g], j)), h2f(h_at(rb[g], j))));
+      *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
+    } else if constexpr (KIND == K_REQUANT_PC) {
+      int8_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = sat8(__fmul_rn(__int2float_rn(i_at(ia[g], j)), h2f(h_at(rb[g], j))));
+      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+    } else if constexpr (KIND == K_REQUANT) {
+      int8_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = sat8(__fmul_rn(__int2float_rn(i_at(ia[g], j)), s0));
+      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+    } else if constexpr (KIND == K_SCALE_MUL_I32) {
+      int32_t o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = sat32(__fmul_rn(__int2float_rn(i_at(ia[g], j)), s0));
+      uint4* q = reinterpret_cast<uint4*>(d + e0[g] * 4);
+      q[0] = make_uint4(o[0], o[1], o[2], o[3]);
+      q[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    } else if constexpr (KIND == K_VADD_I32) {
+      const V8 rv{rb[g], rc[g]};
+      uint32_t o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = static_cast<uint32_t>(i_at(ia[g], j)) + static_cast<uint32_t>(i_at(rv, j));
+      uint4* q = reinterpret_cast<uint4*>(d + e0[g] * 4);
+      q[0] = make_uint4(o[0], o[1], o[2], o[3]);
+      q[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    } else if constexpr (KIND == K_SCALE_MUL_I8) {
+      int8_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = sat8(__fmul_rn(static_cast<float>(b_at(qa[g], j)), s0));
+      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+    } else if constexpr (KIND == K_VADD_I8) {
+      int8_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int v = int(b_at(qa[g], j)) + int(b_at(qb[g], j));
+        q[j] = static_cast<int8_t>(v < -128 ? -128 : (v > 127 ? 127 : v));
+      }
+      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+    } else if constexpr (KIND == K_DEQUANT_ADD) {
+      int8_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float accv = __fmul_rn(__int2float_rn(i_at(ia[g], j)), s0);
+        const float skip = __fmul_rn(static_cast<float>(b_at(qb[g], j)), s1);
+        q[j] = sat8(__fadd_rn(accv, skip));
+      }
+      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+    } else if constexpr (KIND == K_GELU_I8) {
+      int8_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float x = (op.flags & F_SRC_I32) ? __fmul_rn(__int2float_rn(i_at(ia[g], j)), s0)
+                                               : __fmul_rn(static_cast<float>(b_at(qa[g], j)), s0);
+        const float y = gelu_f32(x);
+        q[j] = s1 == 0.f ? int8_t(0) : sat8(__fdiv_rn(y, s1));
+      }
+      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+    }
+  }
+}
+
+__device__ __noinline__ void op_elementwise(const ExecArgs& A, const DevOp& op, const Task& t) {
+  switch (op.kind) {
+    case K_QUANT: ew_kernel<K_QUANT>(A, op, t); break;
+    case K_GELU_F16: ew_kernel<K_GELU_F16>(A, op, t); break;
+    case K_VADD_F16: ew_kernel<K_VADD_F16>(A, op, t); break;
+    case K_DEQUANT_SCALED: ew_kernel<K_DEQUANT_SCALED>(A, op, t); break;
+    case K_DEQUANT_ACCUM: ew_kernel<K_DEQUANT_ACCUM>(A, op, t); break;
+    case K_REQUANT_PC: ew_kernel<K_REQUANT_PC>(A, op, t); break;
+    case K_REQUANT: ew_kernel<K_REQUANT>(A, op, t); break;
+    case K_SCALE_MUL_I32: ew_kernel<K_SCALE_MUL_I32>(A, op, t); break;
+    case K_VADD_I32: ew_kernel<K_VADD_I32>(A, op, t); break;
+    case K_SCALE_MUL_I8: ew_kernel<K_SCALE_MUL_I8>(A, op, t); break;
+    case K_VADD_I8: ew_kernel<K_VADD_I8>(A, op, t); break;
+    case K_DEQUANT_ADD: ew_kernel<K_DEQUANT_ADD>(A, op, t); break;
+    case K_GELU_I8: ew_kernel<K_GELU_I8>(A, op, t); break;
+    default: break;
   }
 }
 
 // ---------------------------------------------------------------------------------
 // MAX_ABS_REDUCE_FP32 (simulator.py:1088-1140): one task per sequence.
 // ---------------------------------------------------------------------------------
-__device__ void op_max_abs(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+__device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
   const uint32_t seq = t.seq0;
   const uint64_t MN = uint64_t(op.M) * op.N;
   const uint16_t* x = reinterpret_cast<const uint16_t*>(pptr(A, op.a, seq));
   // |x| of FP16 values compared as bit patterns (monotone for non-NaN);
   // any NaN wins, as np.max propagates NaN.
   uint32_t m = 0;
-  for (uint64_t i = threadIdx.x; i < MN; i += blockDim.x) {
-    uint32_t v = x[i] & 0x7FFFu;
-    if (v > 0x7C00u) v = 0xFFFFu;  // NaN
-    m = v > m ? v : m;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  const uint64_t ng = MN / 8;   // MN is a multiple of 256
+  for (uint64_t g0 = threadIdx.x; g0 < ng; g0 += uint64_t(blockDim.x) * 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint64_t g = g0 + uint64_t(k) * blockDim.x;
+      v[k] = g < ng ? __ldcg(xv + g) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t h = h_at(v[k], j) & 0x7FFFu;
+        if (h > 0x7C00u) h = 0xFFFFu;  // NaN
+        m = h > m ? h : m;
+      }
   }
   for (int o = 16; o; o >>= 1) {
     uint32_t w = __shfl_xor_sync(0xffffffffu, m, o);
@@ -435,7 +608,7 @@ __device__ __forceinline__ float in_val(const ExecArgs& A, const DevOp& op, uint
   }
 }
 
-__device__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem, uint32_t opi) {
+__device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem, uint32_t opi) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t seq = t.seq0, N = op.N;
   const uint32_t r = t.tile * 8 + warp;
@@ -458,7 +631,28 @@ __device__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8
   auto x_at = [&](uint32_t j) -> float {
     return buffered ? rowbuf[j] : in_val(A, op, seq, base + j, in_scale);
   };
-  if (buffered) {
+  const bool fp16_in = op.kind == K_LAYERNORM_F16 || op.kind == K_SOFTMAX_F16 || op.kind == K_MASKED_SOFTMAX_F16;
+  if (buffered && fp16_in) {
+    // 8 FP16 per lane per load, all loads issued before any conversion
+    const uint4* src = reinterpret_cast<const uint4*>(pptr(A, op.a, seq) + base * 2);
+    const uint32_t ng = N / 8;
+    for (uint32_t half = 0; half < kRowCap / 256; half += 4) {
+      uint4 v[4];
+#pragma unroll
+      for (uint32_t k = 0; k < 4; ++k) {
+        const uint32_t g = lane + 32 * (half + k);
+        if (g < ng) v[k] = __ldcg(src + g);
+      }
+#pragma unroll
+      for (uint32_t k = 0; k < 4; ++k) {
+        const uint32_t g = lane + 32 * (half + k);
+        if (g < ng)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) rowbuf[g * 8 + j] = h2f(h_at(v[k], j));
+      }
+    }
+    __syncwarp();
+  } else if (buffered) {
     for (uint32_t j = lane; j < N; j += 32) rowbuf[j] = in_val(A, op, seq, base + j, in_scale);
     __syncwarp();
   }
@@ -473,6 +667,33 @@ __device__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8
     const float var = div_count(sq, N);
     const float denom = __fsqrt_rn(__fadd_rn(var, eps));
     const uint8_t* gb = pptr(A, op.b, seq);
+    if (op.kind == K_LAYERNORM_F16 && buffered) {
+      const uint32_t ng = N / 8;
+      for (uint32_t half = 0; half < kRowCap / 256; half += 4) {
+      uint4 gv[4], bv[4];
+#pragma unroll
+      for (uint32_t k = 0; k < 4; ++k) {
+        const uint32_t g = lane + 32 * (half + k);
+        if (g < ng) {
+          gv[k] = __ldcg(reinterpret_cast<const uint4*>(gb) + g);
+          bv[k] = __ldcg(reinterpret_cast<const uint4*>(gb + uint64_t(N) * 2) + g);
+        }
+      }
+#pragma unroll
+      for (uint32_t k = 0; k < 4; ++k) {
+        const uint32_t g = lane + 32 * (half + k);
+        if (g >= ng) continue;
+        uint16_t h[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float y = __fdiv_rn(__fsub_rn(rowbuf[g * 8 + j], mean), denom);
+          h[j] = f2h(__fadd_rn(__fmul_rn(y, h2f(h_at(gv[k], j))), h2f(h_at(bv[k], j))));
+        }
+        *reinterpret_cast<uint4*>(d + (base + uint64_t(g) * 8) * 2) = pack_h(h);
+      }
+      }
+      return;
+    }
     for (uint32_t j = lane; j < N; j += 32) {
       const float y = __fdiv_rn(__fsub_rn(x_at(j), mean), denom);
       const float g = h2f(reinterpret_cast<const uint16_t*>(gb)[j]);
@@ -516,17 +737,25 @@ __device__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8
   };
   if (buffered) {
     __syncwarp();
-    for (uint32_t j = lane; j < N; j += 32) {
-      const float e = e_at(j);
-      __syncwarp(__activemask());
-      rowbuf[j] = e;
-    }
+    for (uint32_t j = lane; j < N; j += 32) rowbuf[j] = e_at(j);
     __syncwarp();
   }
   auto ev = [&](uint32_t j) -> float { return buffered ? rowbuf[j] : e_at(j); };
   const float denom = warp_pairwise_sum(ev, N, pw);
   if (masked_i8 && denom == 0.f) {
     if (lane == 0) raise_fault(A, DF_ZERO_DENOM, 0, seq);
+  }
+  if ((op.kind == K_SOFTMAX_F16 || masked_f16) && buffered) {
+    for (uint32_t g = lane; g < N / 8; g += 32) {
+      uint16_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float e = rowbuf[g * 8 + j];
+        h[j] = f2h(op.kind == K_SOFTMAX_F16 ? __fdiv_rn(e, denom) : (denom > 0.f ? __fdiv_rn(e, denom) : 0.f));
+      }
+      *reinterpret_cast<uint4*>(d + (base + uint64_t(g) * 8) * 2) = pack_h(h);
+    }
+    return;
   }
   for (uint32_t j = lane; j < N; j += 32) {
     const float e = ev(j);
@@ -543,7 +772,7 @@ __device__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8
 }
 
 // Legacy fused softmax(QK^T)·V (sfu.py:323-443): one warp per query row.
-__device__ void op_attnv(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+__device__ __noinline__ void op_attnv(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t seq = t.seq0, M = op.M, N = op.N, K = op.K;
   const uint32_t r = t.tile * 8 + warp;
@@ -656,20 +885,28 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem) {
 }
 
 // Shared memory: max(MATMUL tiles, row buffers + pairwise scratch).
-constexpr size_t kExecSmem =
-    (kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4) > (8 * 16 * kMmAStride + 64 * kMmBStride)
-        ? (kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4)
-        : (8 * 16 * kMmAStride + 64 * kMmBStride);
+constexpr size_t kRowSmem = kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4;
+constexpr size_t kExecSmem = kRowSmem > kMmSmem ? kRowSmem : kMmSmem;
 
 __global__ void __launch_bounds__(kThreads, 1) exec_kernel(ExecArgs A) {
   extern __shared__ __align__(16) uint8_t smem[];
+  if (A.prof && blockIdx.x == 0 && threadIdx.x == 0) A.prof[0] = global_ns();
   for (uint32_t L = 0; L < A.n_levels; ++L) {
     const uint32_t t0 = A.level_off[L], t1 = A.level_off[L + 1];
     for (uint32_t ti = t0 + blockIdx.x; ti < t1; ti += gridDim.x) run_task(A, ti, smem);
     if (L + 1 < A.n_levels) {
       if (!grid_barrier(A)) return;
-      if (threadIdx.x == 0 && blockIdx.x == 0) A.status[3] = L + 1;
+      if (threadIdx.x == 0 && blockIdx.x == 0) {
+        A.status[3] = L + 1;
+        if (A.prof) A.prof[L + 1] = global_ns();
+      }
     }
+  }
+  if (A.prof) {
+    // the last level ends when every CTA has finished it
+    __syncthreads();
+    if (threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned long long*>(&A.prof[A.n_levels]),
+                                    static_cast<unsigned long long>(global_ns()));
   }
 }
 

@@ -94,8 +94,16 @@ struct Task {
   uint32_t op;
   uint32_t seq0;   // first sequence
   uint32_t nseq;   // sequences covered
-  uint32_t tile;   // op-specific tile index
+  uint32_t tile;   // op-specific tile index (K_GATHER: first segment, relative to seg0)
+  uint32_t aux;    // K_GATHER: one past the last segment (relative to seg0)
 };
+
+// Gathers split their segments into pieces of at most this many units, and a
+// gather task copies a run of whole segments of about this size.
+constexpr uint64_t kGatherChunkUnits = 4096;
+
+// Elements of one sequence an element-wise task covers (256 threads x 4 groups of 8).
+constexpr uint64_t kEwTaskElems = 8192;
 
 // Parameters decoded from runtime-patched instruction words, one set per
 // sequence.  Address parameters hold the 56-bit register value; attention

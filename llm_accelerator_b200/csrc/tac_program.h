@@ -2,6 +2,7 @@
 // the CUDA engine).
 #pragma once
 #include <cstdint>
+#include <utility>
 #include <vector>
 
 #include "../../include/taccel_b200.h"
@@ -53,6 +54,10 @@ struct tac_program {
   uint32_t n_slots = 0;
   tac_exec_info info{};
   tac_fault fault{};
+  uint64_t cse_hits = 0;                 // ops removed as repeats of earlier ones
+  bool sram_home_read = false;           // reads SRAM bytes an earlier run left
+  bool sreg_home_read = false;           // reads scale registers an earlier run left
+  std::vector<std::pair<uint64_t, uint64_t>> home_read_ranges;  // writable DRAM read before written
   // Device mirror (filled by the engine on first use).
   int device = -1;
   void* d_blob = nullptr;

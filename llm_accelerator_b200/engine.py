@@ -20,7 +20,7 @@ DEVOP_DTYPE = np.dtype([
     ("_pad", "<u4"), ("dconst", "<i8"), ("nbytes", "<u8"), ("attn_qrb", "<u4"), ("attn_vkl", "<u4"),
     ("pc", "<u4"), ("level", "<u4")])
 SEGMENT_DTYPE = np.dtype([("src", "<u8"), ("dst", "<u8"), ("n", "<u8")])
-TASK_DTYPE = np.dtype([("op", "<u4"), ("seq0", "<u4"), ("nseq", "<u4"), ("tile", "<u4")])
+TASK_DTYPE = np.dtype([("op", "<u4"), ("seq0", "<u4"), ("nseq", "<u4"), ("tile", "<u4"), ("aux", "<u4")])
 
 
 @dataclass
@@ -60,9 +60,12 @@ class Program:
 
 
 def compile_program(batch: int, dram_bytes: int, shared_bytes: int, region: bytes, entry_pc: int,
-                    max_insns: int, regs: L.Regs, sregs_reset: bool, sites=()) -> Program:
+                    max_insns: int, regs: L.Regs, sregs_reset: bool, sites=(), *, live=None,
+                    sram_live: bool = True, sregs_live: bool = True) -> Program:
     """Plans an instruction region; raises only when the stream cannot be
-    planned at all (a faulting stream still yields a program)."""
+    planned at all (a faulting stream still yields a program).  ``live``:
+    DRAM byte ranges that must hold their final values after a run (None =
+    all of DRAM); ``sram_live`` / ``sregs_live``: keep SRAM / scale registers."""
     n = len(region) // 8
     buf = C.create_string_buffer(bytes(region), len(region))
     arr = (L.VarSite * max(1, len(sites)))()
@@ -70,11 +73,33 @@ def compile_program(batch: int, dram_bytes: int, shared_bytes: int, region: byte
         arr[k] = L.VarSite(s.kind, s.addr_reg, s.lo_pc, s.hi_pc, s.range_lo, s.range_hi)
     h = C.c_void_p()
     info, fault = L.ExecInfo(), L.Fault()
-    st = _lib.tac_compile(batch, dram_bytes, shared_bytes, buf, n, entry_pc, max_insns, C.byref(regs),
-                          1 if sregs_reset else 0, arr, len(sites), C.byref(h), C.byref(info), C.byref(fault))
+    opts = None
+    if live is not None or not sram_live or not sregs_live:
+        rng = np.asarray(list(live or []), dtype=np.uint64).reshape(-1, 2)
+        if live is not None and len(rng) == 0:
+            rng = np.zeros((1, 2), np.uint64)   # nothing in DRAM stays live
+        rng = np.ascontiguousarray(rng)
+        opts = L.CompileOpts(len(rng), int(sram_live), int(sregs_live), 0, rng.ctypes.data)
+        opts._keep = rng
+    st = _lib.tac_compile_ex(batch, dram_bytes, shared_bytes, buf, n, entry_pc, max_insns, C.byref(regs),
+                             1 if sregs_reset else 0, arr, len(sites), None if opts is None else C.byref(opts),
+                             C.byref(h), C.byref(info), C.byref(fault))
     if st != L.OK:
         raise L.fault_to_exception(fault, st)
     return Program(h, info, fault, int(info.n_var_words))
+
+
+def home_reads(prog: Program):
+    """(DRAM byte ranges, reads SRAM, reads scale registers) that a run of
+    ``prog`` reads before writing them, i.e. state an earlier run left."""
+    n = C.c_uint32()
+    sr, gr = C.c_int32(), C.c_int32()
+    L.check(_lib.tac_program_home_reads(prog.handle, None, 0, C.byref(n), C.byref(sr), C.byref(gr)),
+            "tac_program_home_reads")
+    arr = np.zeros((max(1, n.value), 2), np.uint64)
+    L.check(_lib.tac_program_home_reads(prog.handle, arr.ctypes.data, n.value, C.byref(n), C.byref(sr),
+                                        C.byref(gr)), "tac_program_home_reads")
+    return [tuple(int(v) for v in r) for r in arr[:n.value]], bool(sr.value), bool(gr.value)
 
 
 class Engine:
@@ -144,6 +169,28 @@ class Engine:
         if st != L.OK and not (prog.info.faulted and st == prog.fault.status):
             raise L.fault_to_exception(f, st)
 
+    def encode_params(self, prog: Program, var_words) -> np.ndarray:
+        """Decodes and range-checks runtime words into the [batch, n_params]
+        parameter block a run consumes (host only)."""
+        n = int(_lib.tac_program_param_count(prog.handle))
+        out = np.zeros((self.batch, n), np.uint64)
+        vw = None
+        if prog.n_var_words:
+            vw = np.ascontiguousarray(np.asarray(var_words, dtype=np.uint64).reshape(self.batch, prog.n_var_words))
+        f = L.Fault()
+        st = _lib.tac_encode_params(prog.handle, self.batch, None if vw is None else vw.ctypes.data,
+                                    out.ctypes.data, C.byref(f))
+        if st != L.OK:
+            raise L.fault_to_exception(f, st)
+        return out
+
+    def run_async_params(self, prog: Program, params_dev_ptr: int, stream=None) -> None:
+        """Runs with a parameter block already in device memory."""
+        f = L.Fault()
+        st = _lib.tac_run_async_params(self.handle, prog.handle, params_dev_ptr, stream, C.byref(f))
+        if st != L.OK and not (prog.info.faulted and st == prog.fault.status):
+            raise L.fault_to_exception(f, st)
+
     def check_device(self) -> None:
         f = L.Fault()
         st = _lib.tac_check_device_status(self.handle, C.byref(f))
@@ -152,6 +199,18 @@ class Engine:
 
     def argmax_f16(self, addr: int, count: int, out_dev_ptr: int, stream=None) -> None:
         L.check(_lib.tac_argmax_f16(self.handle, addr, count, out_dev_ptr, stream), "tac_argmax_f16")
+
+    def set_profiling(self, on: bool) -> None:
+        L.check(_lib.tac_set_profiling(self.handle, 1 if on else 0), "tac_set_profiling")
+
+    def read_profile(self) -> np.ndarray:
+        """Device time (ns) at the end of each level of the last run; entry 0 is the start."""
+        n = C.c_uint32()
+        L.check(_lib.tac_read_profile(self.handle, None, 0, C.byref(n)), "tac_read_profile")
+        out = np.zeros(n.value, np.uint64)
+        if n.value:
+            L.check(_lib.tac_read_profile(self.handle, out.ctypes.data, n.value, C.byref(n)), "tac_read_profile")
+        return out
 
     def layout(self):
         sb, ss, sh = C.c_void_p(), C.c_uint64(), C.c_void_p()

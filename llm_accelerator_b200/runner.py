@@ -20,7 +20,7 @@ import numpy as np
 from . import _lib as L
 from . import isa
 from .bundle import ProgramBundle
-from .engine import Engine, Site, compile_program
+from .engine import Engine, Site, compile_program, home_reads
 
 
 class HostRunner:
@@ -153,12 +153,26 @@ class BatchedRunner:
                 for pc in ((site.lo_pc, site.hi_pc) if site.kind == 0 else (site.lo_pc,)):
                     w = isa.word_of(masked[pc * 8:pc * 8 + 8]) & (0x7F << 57)
                     masked[pc * 8:pc * 8 + 8] = isa.bytes_of(w)
-            regs = L.Regs()
-            prog = compile_program(self.batch, self.dram_bytes, self.shared_bytes, bytes(masked), entry,
-                                   10_000_000, regs, True, sites)
-            if prog.info.faulted:
-                raise L.fault_to_exception(prog.fault)
-            self.plans[name] = prog
+            self._masked = getattr(self, "_masked", {})
+            self._masked[name] = (bytes(masked), entry, sites)
+        # State a step must leave behind: logits, the KV cache, and whatever a
+        # later step reads before writing (found from the full-state plans).
+        live = [(b.logits_base, b.kv_cache_base), (b.kv_cache_base, b.required_dram_bytes)]
+        sram_live = sregs_live = False
+        for name, (masked, entry, sites) in self._masked.items():
+            full = compile_program(self.batch, self.dram_bytes, self.shared_bytes, masked, entry, 10_000_000,
+                                   L.Regs(), True, sites)
+            if full.info.faulted:
+                raise L.fault_to_exception(full.fault)
+            ranges, sr, gr = home_reads(full)
+            live += ranges
+            sram_live |= sr
+            sregs_live |= gr
+        self.live = live
+        for name, (masked, entry, sites) in self._masked.items():
+            self.plans[name] = compile_program(self.batch, self.dram_bytes, self.shared_bytes, masked, entry,
+                                               10_000_000, L.Regs(), True, sites, live=live,
+                                               sram_live=sram_live, sregs_live=sregs_live)
 
     # ---- runtime words ------------------------------------------------------------------
     def var_words(self, name: str, tokens: Sequence[int], positions: Sequence[int]) -> np.ndarray:
@@ -191,6 +205,18 @@ class BatchedRunner:
                                ((p + np.uint64(1)) << np.uint64(35)) | np.uint64(s.mode << 33))
                 col += 1
         return out
+
+    def params(self, name: str, tokens, positions) -> np.ndarray:
+        """Host parameter block for one step (see Engine.encode_params)."""
+        return self.engine.encode_params(self.plans[name], self.var_words(name, tokens, positions))
+
+    def step_params_async(self, name: str, params_dev_ptr: int, stream=None) -> None:
+        """One step with its parameter block already on the device."""
+        self.engine.run_async_params(self.plans[name], params_dev_ptr, stream)
+
+    def argmax_async(self, name: str, out_dev_ptr: int, vocab: int, stream=None) -> None:
+        """Greedy token of every sequence (device int32[batch]) from this step's logits."""
+        self.engine.argmax_f16(self.logits_offset(name), vocab, out_dev_ptr, stream)
 
     def step_async(self, name: str, tokens, positions, stream=None) -> None:
         self.engine.run_async(self.plans[name], self.var_words(name, tokens, positions), stream)
