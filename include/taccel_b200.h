@@ -229,6 +229,15 @@ int tac_gemm_i8_requant_shift(const int8_t* A, const int8_t* B, const int32_t* m
 int tac_gemm_i8_i32(const int8_t* A, const int8_t* B, int32_t* C, int M, int N, int K,
                     void* stream);
 
+/* The stand-alone GEMMs run on the tcgen05 kernel when K and N are
+ * multiples of 16 and A, B and the output are 16-byte aligned, otherwise on
+ * an mma.sync kernel; both are exact.  Every wait inside the tcgen05 kernel
+ * is bounded: one that runs out sets a device fault code and the kernel
+ * returns.  tac_gemm_status synchronizes the current device, returns
+ * TAC_E_DEVICE (code in *fault_code, then cleared) if any launch since the
+ * last call recorded one, else TAC_OK.  No reference counterpart. */
+int tac_gemm_status(int* fault_code);
+
 #ifdef __cplusplus
 }
 #endif

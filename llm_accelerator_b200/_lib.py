@@ -85,6 +85,7 @@ SIGNATURES = {
     "tac_gemm_i8_requant_pc": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
     "tac_gemm_i8_requant_shift": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "tac_gemm_i8_i32": (_I, [_P, _P, _P, _I, _I, _I, _P]),
+    "tac_gemm_status": (_I, [_P]),
 }
 
 

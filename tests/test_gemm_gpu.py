@@ -9,6 +9,8 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
+from llm_accelerator_b200 import _lib as L
+
 pytestmark = pytest.mark.gpu
 
 
@@ -24,8 +26,18 @@ def _requant_shift_ref(acc, mult, shift):
     return np.clip(v, -128, 127).astype(np.int8)
 
 
+# K and N multiples of 16 run on the tcgen05 kernel, the rest on the mma.sync
+# tile.  Covered: partial 128-row / 128- and 256-column tiles, K not a multiple
+# of the 128-byte K block, a single K block, the decode GEMV (M=1), and a
+# 256-column-tile case with ragged M, N and K (1936 x 2064 x 784).
 SHAPES = [(64, 64, 64), (64, 768, 768), (768, 64, 3072), (1, 3072, 768), (16, 48, 64), (100, 200, 48),
-          (768, 768, 768), (256, 4096, 512), (4096, 64, 768)]
+          (768, 768, 768), (256, 4096, 512), (4096, 64, 768), (130, 272, 144), (1, 16, 16), (300, 208, 4096),
+          (1936, 2064, 784), (3072, 3072, 64)]
+
+
+def _exact_matmul(A, B):
+    # float64 BLAS is exact here: |A @ B| <= K * 2^14 < 2^53
+    return (A.astype(np.float64) @ B.astype(np.float64)).astype(np.int64)
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -35,7 +47,7 @@ def test_gemm_exact(M, N, K):
     rng = np.random.default_rng(M * 7 + N * 3 + K)
     A = rng.integers(-128, 128, (M, K), dtype=np.int8)
     B = rng.integers(-128, 128, (K, N), dtype=np.int8)
-    ref = A.astype(np.int64) @ B.astype(np.int64)
+    ref = _exact_matmul(A, B)
     dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
     got = gemm.gemm_i8_i32(dA, dB).cpu().numpy()
     np.testing.assert_array_equal(got, ref.astype(np.int32))
@@ -46,6 +58,7 @@ def test_gemm_exact(M, N, K):
     shift = rng.integers(8, 16, N, dtype=np.int32)
     q2 = gemm.gemm_i8_requant_shift(dA, dB, torch.from_numpy(mult).cuda(), torch.from_numpy(shift).cuda()).cpu().numpy()
     np.testing.assert_array_equal(q2, _requant_shift_ref(ref, mult, shift))
+    assert L.lib.tac_gemm_status(None) == L.OK
 
 
 def test_gemm_4096_cubed_sampled():
@@ -66,3 +79,9 @@ def test_gemm_4096_cubed_sampled():
         np.testing.assert_array_equal(Cn[i], (A[i] @ B).astype(np.int32))
     # checksum of checksums: (1^T A) B == 1^T C
     np.testing.assert_array_equal(Cn.astype(np.int64).sum(axis=0), A.sum(axis=0) @ B)
+    # fused requant epilogue at full size: equal to requantising the int32 result
+    scale = torch.full((N,), 1.0 / 4096, dtype=torch.float16, device="cuda")
+    scale[::7] = 3e-4
+    q = gemm.gemm_i8_requant_pc(dA, dB, scale).cpu().numpy()
+    np.testing.assert_array_equal(q, _requant_pc_ref(Cn, scale.cpu().numpy()))
+    assert L.lib.tac_gemm_status(None) == L.OK
