@@ -229,6 +229,30 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
+INT8_DENSE_PEAK_TOPS = 4500.0   # nominal dense INT8 tensor peak of one B200
+
+
+def int8_gemm_line():
+    """Second half of the metric: the stand-alone MATMUL + REQUANT_PC kernel at
+    4096^3 against the dense INT8 tensor peak, with cuBLASLt INT8 timed beside it."""
+    from llm_accelerator_b200.gemm import time_gemm
+    r = time_gemm(4096, 4096, 4096, epilogue="requant_pc", iters=20, warmup=5)
+    bf16 = None
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        bf16 = float(json.loads(p.read_text()).get("bf16_tflops", 0.0)) or None
+    out = {"shape": r["shape"], "epilogue": "MATMUL + REQUANT_PC (int8 out)", "ms": round(r["ms"], 4),
+           "tops": round(r["tops"], 1), "peak_tops": INT8_DENSE_PEAK_TOPS, "peak_kind": "nominal dense INT8",
+           "frac": round(r["tops"] / INT8_DENSE_PEAK_TOPS, 4),
+           "timing": "median of 20 launches, CUDA events, L2 flushed between launches"}
+    if bf16:
+        out["frac_of_2x_measured_bf16"] = round(r["tops"] / (2 * bf16), 4)
+    if "cublas_tops" in r:
+        out["cublas_int_mm_tops"] = round(r["cublas_tops"], 1)
+        out["vs_cublas"] = round(r["tops"] / r["cublas_tops"], 3)
+    return out
+
+
 def traffic_per_launch(workload, batch):
     """DRAM bytes per executor launch from the committed ncu summary (or None)."""
     f = ROOT / "profiles" / f"exec_kernel_{workload}.txt"
@@ -358,6 +382,11 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     e2e = B_total * K / float(t.item())
     runner.engine.check_device()
 
+    gemm_line = None
+    if rank == 0 and not args.no_gemm:
+        gemm_line = int8_gemm_line()
+    barrier()
+
     plan = runner.plans["decode"]
     algo, shared_b, per_seq_b = algorithmic_bytes(plan, B, bundle)
     per_launch_s = ms / 1000.0 / K
@@ -387,6 +416,8 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
         }
         if cpu_baseline is not None:
             line["cpu_baseline"] = cpu_baseline
+        if gemm_line is not None:
+            line["int8_gemm"] = gemm_line
         print(json.dumps(line), flush=True)
 
 
@@ -399,6 +430,7 @@ def main():
     ap.add_argument("--workload", default="gpt2-medium", choices=sorted(WORKLOADS))
     ap.add_argument("--batch", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the stand-alone 4096^3 INT8 GEMM measurement")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -152,7 +152,9 @@ __device__ __noinline__ void op_sreg_final(const ExecArgs& A, const DevOp& op, c
 // ---------------------------------------------------------------------------------
 constexpr int kMmKc = 128;             // K chunk (bytes of A rows / rows of B)
 constexpr int kMmStages = 3;           // cp.async pipeline depth
-constexpr int kMmAStage = 128 * kMmKc; // 8 row blocks x 16 rows x K chunk
+constexpr int kMmAStride = kMmKc + 16; // A row stride in shared memory: 144 B keeps the 8 rows
+                                       // of an mma fragment load on distinct banks
+constexpr int kMmAStage = 128 * kMmAStride; // 8 row blocks x 16 rows x K chunk
 constexpr int kMmBStage = kMmKc * 64;  // K chunk x 64 columns, raw [k][n]
 constexpr int kMmBStride = kMmKc + 16; // transposed B row stride [n][k] (bytes)
 constexpr size_t kMmSmem = size_t(kMmStages) * (kMmAStage + kMmBStage) + 64 * kMmBStride;
@@ -201,7 +203,7 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
     }
   }
   const uint32_t ncols = N - n0 < 64 ? N - n0 : 64;
-  uint8_t* As = smem;                                    // [stage][blk*16 + row][kMmKc]
+  uint8_t* As = smem;                                    // [stage][blk*16 + row][kMmAStride]
   uint8_t* Bs = smem + kMmStages * kMmAStage;            // [stage][k][64] raw
   uint8_t* Bt = Bs + kMmStages * kMmBStage;              // [n][kMmBStride] transposed
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -229,7 +231,7 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
       const uint32_t v = i % (kMmKc / 16), row = i / (kMmKc / 16);
       const bool in = v * 16 < kc;
       const uint8_t* src = Ag[row / 16] + uint64_t(row % 16) * K + k0 + (in ? v * 16 : 0);
-      cp_async16(as + row * kMmKc + v * 16, src, in ? 16u : 0u);
+      cp_async16(as + row * kMmAStride + v * 16, src, in ? 16u : 0u);
     }
     // B: kMmKc rows x 4 vectors of 16 bytes (64 columns)
     for (uint32_t i = threadIdx.x; i < uint32_t(kMmKc) * 4; i += blockDim.x) {
@@ -274,11 +276,10 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
       const uint32_t p = warp + 8 * i;
       const uint32_t blk = p / 8, ns = p % 8;
       if (blk >= nblocks || ns * 8 >= ncols) continue;
-      const uint8_t* a_row0 = as + (blk * 16 + g) * kMmKc;
-      const uint8_t* a_row8 = as + (blk * 16 + g + 8) * kMmKc;
+      const uint8_t* a_row0 = as + (blk * 16 + g) * kMmAStride;
+      const uint8_t* a_row8 = as + (blk * 16 + g + 8) * kMmAStride;
       const uint8_t* b_col = Bt + (ns * 8 + g) * kMmBStride;
       for (uint32_t ks = 0; ks < kc32; ks += 32) {
-        // A rows are kMmKc = 128 bytes apart: rotate the 16-byte quad by row to spread banks
         const uint32_t a0 = *reinterpret_cast<const uint32_t*>(a_row0 + ks + q * 4);
         const uint32_t a1 = *reinterpret_cast<const uint32_t*>(a_row8 + ks + q * 4);
         const uint32_t a2 = *reinterpret_cast<const uint32_t*>(a_row0 + ks + 16 + q * 4);

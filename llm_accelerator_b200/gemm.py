@@ -59,3 +59,67 @@ def gemm_i8_requant_shift(A, B, mult, shift, out=None):
     L.check(L.lib.tac_gemm_i8_requant_shift(_ptr(A), _ptr(B), _ptr(mult.contiguous()), _ptr(shift.contiguous()),
                                             _ptr(out), M, N, K, _stream()), "tac_gemm_i8_requant_shift")
     return out
+
+
+def time_gemm(M: int, N: int, K: int, *, epilogue: str = "requant_pc", iters: int = 20, warmup: int = 5,
+              seed: int = 0, compare_cublas: bool = True) -> dict:
+    """Device time of one stand-alone GEMM (median over `iters` launches, CUDA
+    events on the launching stream, L2 flushed between launches by writing a
+    256 MB buffer) and, for comparison, torch._int_mm (cuBLASLt INT8) on the
+    same operands."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    A = torch.randint(-128, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+    B = torch.randint(-128, 128, (K, N), dtype=torch.int8, device="cuda", generator=g)
+    scale = torch.full((N,), 1e-3, dtype=torch.float16, device="cuda")
+    if epilogue == "i32":
+        out = torch.empty((M, N), dtype=torch.int32, device="cuda")
+        fn = lambda: gemm_i8_i32(A, B, out)  # noqa: E731
+    else:
+        out = torch.empty((M, N), dtype=torch.int8, device="cuda")
+        fn = lambda: gemm_i8_requant_pc(A, B, scale, out)  # noqa: E731
+    flush = torch.empty(256 << 20, dtype=torch.int8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def med(f):
+        for _ in range(warmup):
+            f()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            f()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sorted(ts)[len(ts) // 2]
+
+    ms = med(fn)
+    st = L.lib.tac_gemm_status(None)
+    if st != L.OK:
+        raise RuntimeError(f"GEMM kernel reported device fault status {st}")
+    ops = 2.0 * M * N * K
+    res = {"shape": [M, N, K], "epilogue": epilogue, "ms": ms, "tops": ops / ms / 1e9}
+    if compare_cublas and M > 16:
+        Bc = B.t().contiguous().t()   # column-major operand for cuBLASLt
+        cms = med(lambda: torch._int_mm(A, Bc))
+        res.update({"cublas_int_mm_ms": cms, "cublas_tops": ops / cms / 1e9})
+    return res
+
+
+if __name__ == "__main__":
+    import argparse
+    import json
+    ap = argparse.ArgumentParser(description="time the stand-alone INT8 GEMM")
+    ap.add_argument("M", type=int)
+    ap.add_argument("N", type=int)
+    ap.add_argument("K", type=int)
+    ap.add_argument("--epilogue", default="requant_pc", choices=["requant_pc", "i32"])
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--no-cublas", action="store_true")
+    a = ap.parse_args()
+    print(json.dumps(time_gemm(a.M, a.N, a.K, epilogue=a.epilogue, iters=a.iters, warmup=a.warmup,
+                               compare_cublas=not a.no_cublas)))

@@ -85,3 +85,4 @@ def test_gemm_4096_cubed_sampled():
     q = gemm.gemm_i8_requant_pc(dA, dB, scale).cpu().numpy()
     np.testing.assert_array_equal(q, _requant_pc_ref(Cn, scale.cpu().numpy()))
     assert L.lib.tac_gemm_status(None) == L.OK
+
