@@ -229,6 +229,20 @@ int tac_gemm_i8_requant_shift(const int8_t* A, const int8_t* B, const int32_t* m
 int tac_gemm_i8_i32(const int8_t* A, const int8_t* B, int32_t* C, int M, int N, int K,
                     void* stream);
 
+/* Decode GEMV with the REQUANT_PC epilogue that allocates nothing: out[M,N]
+ * int8 = the same result as tac_gemm_i8_requant_pc, for M <= 16 rows, computed
+ * split-K over about two CTAs per SM.  Its int32 partial sums and per-column-
+ * block arrival counters live in a static device workspace of 8 MiB
+ * (requires M * N * 4 <= 8 MiB, N <= 65536; TAC_E_ARGUMENT otherwise).
+ * The first call on each device does the set-up (looks up the workspace,
+ * clears the counters, synchronizes the device), so make it once before any
+ * stream capture or latency-critical loop; later calls only launch.  The
+ * counters return to zero at the end of every call.  Calls that overlap in
+ * time on one device share the workspace and race: issue them on one stream.
+ * No counterpart in the reference. */
+int tac_gemv_i8_requant_pc_static(const int8_t* A, const int8_t* B, const uint16_t* scale_f16,
+                                  int8_t* out, int M, int N, int K, void* stream);
+
 /* The stand-alone GEMMs run on the tcgen05 kernel when K and N are
  * multiples of 16 and A, B and the output are 16-byte aligned, otherwise on
  * an mma.sync kernel; both are exact.  Every wait inside the tcgen05 kernel

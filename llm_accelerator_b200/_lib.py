@@ -86,6 +86,7 @@ SIGNATURES = {
     "tac_gemm_i8_requant_shift": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "tac_gemm_i8_i32": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "tac_gemm_status": (_I, [_P]),
+    "tac_gemv_i8_requant_pc_static": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
 }
 
 
