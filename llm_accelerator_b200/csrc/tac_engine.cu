@@ -201,7 +201,7 @@ int tac_engine_create(int device, int batch, uint64_t dram_bytes, uint64_t share
     cudaFuncSetAttribute(exec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kExecSmem));
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exec_kernel, kThreads, kExecSmem);
-    e->grid = e->n_sms * std::max(1, std::min(per_sm, 1));
+    e->grid = e->n_sms * std::max(1, std::min(per_sm, 2));
     ok = cudaDeviceSynchronize() == cudaSuccess && per_sm >= 1;
   }
   if (!ok) {

@@ -17,7 +17,7 @@ namespace tac {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr uint32_t kBarrierSpinLimit = 1u << 26;   // ~ seconds with nanosleep back-off
+constexpr uint32_t kBarrierSpinLimit = 1u << 22;   // polls of L2 (~0.5 us each): a few seconds
 
 // Device-side fault codes (status word 0).
 enum DevFault : uint32_t {
@@ -826,37 +826,49 @@ __device__ __noinline__ void op_attnv(const ExecArgs& A, const DevOp& op, const 
 // ---------------------------------------------------------------------------------
 // Grid barrier with a bounded wait.
 // ---------------------------------------------------------------------------------
-__device__ __forceinline__ bool grid_barrier(const ExecArgs& A) {
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];\n" ::"l"(p));
+}
+
+// Grid-wide barrier between levels.  The arrival counter only grows during a
+// launch (the host zeroes it before each launch): a CTA arrives with a release
+// add and waits, with acquire loads, until all gridDim.x CTAs of this level
+// have arrived (target = (level + 1) * gridDim.x).  The same poll watches the
+// fault word, so a fault anywhere stops every CTA at its next barrier.  The
+// wait is bounded: running out raises DF_BARRIER_TIMEOUT.  Meanwhile warp 1
+// pulls this CTA's first task of the next level and its op record into L1.
+__device__ __forceinline__ bool grid_barrier(const ExecArgs& A, uint32_t target, uint32_t next_level) {
   __syncthreads();
   __shared__ uint32_t ok;
   if (threadIdx.x == 0) {
-    ok = 1;
-    volatile uint32_t* gen = A.barrier + 1;
-    const uint32_t g = *gen;
-    __threadfence();
-    const uint32_t arrived = atomicAdd(A.barrier, 1u);
-    if (arrived == gridDim.x - 1) {
-      atomicExch(A.barrier, 0u);
-      __threadfence();
-      atomicAdd(A.barrier + 1, 1u);
-    } else {
-      uint32_t spins = 0;
-      while (*gen == g) {
-        if (++spins > kBarrierSpinLimit) {
-          raise_fault(A, DF_BARRIER_TIMEOUT, 0, 0);
-          break;
-        }
-        if (spins > 64) __nanosleep(64);
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;\n" ::"l"(A.barrier) : "memory");
+    uint32_t spins = 0, v = 0, st = 0;
+    for (;;) {
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(A.barrier) : "memory");
+      st = *reinterpret_cast<volatile uint32_t*>(A.status);
+      if (v >= target || st != 0) break;
+      if (++spins > kBarrierSpinLimit) {
+        raise_fault(A, DF_BARRIER_TIMEOUT, 0, 0);
+        st = 1;
+        break;
       }
+      if (spins > 256) __nanosleep(32);
     }
-    __threadfence();
-    if (*reinterpret_cast<volatile uint32_t*>(A.status) != 0) ok = 0;
+    ok = st == 0;
+  } else if (threadIdx.x == 32 && next_level < A.n_levels) {
+    const uint32_t ti = A.level_off[next_level] + blockIdx.x;
+    if (ti < A.level_off[next_level + 1]) {
+      const uint32_t op = A.tasks[ti].op;
+      prefetch_l1(A.ops + op);
+      prefetch_l1(reinterpret_cast<const uint8_t*>(A.ops + op) + sizeof(DevOp) - 1);
+    }
   }
   __syncthreads();
   return ok != 0;
 }
 
-__device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem) {
+__device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t next_ti) {
+  if (threadIdx.x == 32 && next_ti != 0xFFFFFFFFu) prefetch_l1(A.tasks + next_ti);
   const Task t = A.tasks[ti];
   const DevOp& op = A.ops[t.op];
   switch (op.kind) {
@@ -889,14 +901,15 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem) {
 constexpr size_t kRowSmem = kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4;
 constexpr size_t kExecSmem = kRowSmem > kMmSmem ? kRowSmem : kMmSmem;
 
-__global__ void __launch_bounds__(kThreads, 1) exec_kernel(ExecArgs A) {
+__global__ void __launch_bounds__(kThreads, 2) exec_kernel(ExecArgs A) {
   extern __shared__ __align__(16) uint8_t smem[];
   if (A.prof && blockIdx.x == 0 && threadIdx.x == 0) A.prof[0] = global_ns();
   for (uint32_t L = 0; L < A.n_levels; ++L) {
     const uint32_t t0 = A.level_off[L], t1 = A.level_off[L + 1];
-    for (uint32_t ti = t0 + blockIdx.x; ti < t1; ti += gridDim.x) run_task(A, ti, smem);
+    for (uint32_t ti = t0 + blockIdx.x; ti < t1; ti += gridDim.x)
+      run_task(A, ti, smem, ti + gridDim.x < t1 ? ti + gridDim.x : 0xFFFFFFFFu);
     if (L + 1 < A.n_levels) {
-      if (!grid_barrier(A)) return;
+      if (!grid_barrier(A, (L + 1) * gridDim.x, L + 1)) return;
       if (threadIdx.x == 0 && blockIdx.x == 0) {
         A.status[3] = L + 1;
         if (A.prof) A.prof[L + 1] = global_ns();

@@ -144,9 +144,45 @@ __device__ inline float pw_combine(uint32_t n, const float* leaf) {
 
 // Warp-cooperative np.sum(row) for a float32 row of n elements; every lane
 // returns the result.  `scratch` holds kPwMaxLeaves*3 words per warp.
+// True when the pairwise tree over n elements is perfectly balanced: every
+// split halves exactly (n % 16 == 0 above the leaf size), leaving nl <= 8
+// leaves of L elements with L a multiple of 8 in [8, 128].
+__device__ inline bool pw_balanced(uint32_t n, uint32_t& nl, uint32_t& L) {
+  nl = 1;
+  L = n;
+  while (L > 128) {
+    if (L % 16) return false;
+    L /= 2;
+    nl *= 2;
+  }
+  return L >= 8 && L % 8 == 0 && nl <= 8;
+}
+
 template <class Get>
 __device__ inline float warp_pairwise_sum(const Get& get, uint32_t n, uint32_t* scratch) {
   const int lane = threadIdx.x & 31;
+  uint32_t bnl, bL;
+  if (pw_balanced(n, bnl, bL)) {
+    // Lanes 4l..4l+3 own leaf l; lane 4l+p runs the leaf's accumulators 2p and
+    // 2p+1 in order.  The xor-shuffle butterfly then adds exactly the pairs
+    // the tree adds: (r0+r1)+(r2+r3), then the two halves of the leaf, then
+    // neighbouring leaves, then neighbouring pairs of leaves.
+    const uint32_t leaf = uint32_t(lane) >> 2, p = uint32_t(lane) & 3;
+    float v = 0.f;
+    if (leaf < bnl) {
+      const uint32_t o = leaf * bL + 2 * p;
+      float r0 = get(o), r1 = get(o + 1);
+      for (uint32_t i = 8; i < bL; i += 8) {
+        r0 = __fadd_rn(r0, get(o + i));
+        r1 = __fadd_rn(r1, get(o + i + 1));
+      }
+      v = __fadd_rn(r0, r1);
+    }
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    for (uint32_t s = 4; s < 4 * bnl; s <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
+    return __fadd_rn(0.0f, __shfl_sync(0xffffffffu, v, 0));
+  }
   uint32_t* loff = scratch;
   uint32_t* llen = scratch + kPwMaxLeaves;
   float* lsum = reinterpret_cast<float*>(scratch + 2 * kPwMaxLeaves);
