@@ -1162,7 +1162,14 @@ void Compiler::build_tasks() {
         per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + 16383) / 16384)));
         break;
       default: {  // element-wise ops: kEwTaskElems elements per task
-        per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + kEwTaskElems - 1) / kEwTaskElems)));
+        if (B > 1 && MN > 0 && MN * 2 <= kEwTaskElems) {
+          // small ops: one task takes several whole sequences
+          const uint32_t spt = static_cast<uint32_t>(kEwTaskElems / MN);
+          for (uint32_t s = 0; s < B; s += spt)
+            per_level[op.level].push_back(Task{i, s, std::min(spt, B - s), 0, 0});
+        } else {
+          per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + kEwTaskElems - 1) / kEwTaskElems)));
+        }
         break;
       }
     }

@@ -61,7 +61,8 @@ __device__ __forceinline__ uint8_t* pptr(const ExecArgs& A, uint64_t phys, uint3
 
 __device__ __forceinline__ uint16_t sreg_bits(const ExecArgs& A, uint32_t enc, uint32_t seq) {
   if (enc & kSregConst) return static_cast<uint16_t>(enc & 0xFFFF);
-  return A.sregs[uint64_t(seq) * A.sreg_stride + enc];
+  // slots are written by other CTAs earlier in the launch: read through L2
+  return __ldcg(&A.sregs[uint64_t(seq) * A.sreg_stride + enc]);
 }
 __device__ __forceinline__ float sreg_f32(const ExecArgs& A, uint32_t enc, uint32_t seq) {
   return h2f(sreg_bits(A, enc, seq));
@@ -363,26 +364,44 @@ __device__ __forceinline__ uint2 pack_b(const int8_t (&q)[8]) {
   return make_uint2(x, y);
 }
 
+// A task covers kEwTask elements of one sequence (t.nseq == 1, chunk t.tile)
+// or, for small ops, t.nseq whole sequences (t.nseq * M * N <= kEwTask) whose
+// elements are numbered consecutively.  Operands of sequence seq0 + k sit
+// k * seq_stride bytes after those of seq0 (0 for the shared region).
 template <int KIND>
 __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const Task& t) {
-  const uint32_t seq = t.seq0, N = op.N;
-  const uint64_t MN = uint64_t(op.M) * N;
-  const uint64_t base = uint64_t(t.tile) * kEwTask;
-  const uint8_t* __restrict__ a = pptr(A, op.a, seq);
-  const uint8_t* __restrict__ b = pptr(A, op.b, seq);
-  uint8_t* __restrict__ d = pptr(A, op.d, seq);
-  const float s0 = sreg_f32(A, op.s[0], seq);
-  const float s1 = sreg_f32(A, op.s[1], seq);
+  const uint32_t N = op.N;
+  const uint32_t MN = op.M * N;
+  const bool packed = t.nseq > 1;
+  const uint32_t base = packed ? 0u : t.tile * kEwTask;
+  const uint32_t span = packed ? t.nseq * MN : MN;
+  const uint8_t* __restrict__ a0 = pptr(A, op.a, t.seq0);
+  const uint8_t* __restrict__ b0 = pptr(A, op.b, t.seq0);
+  uint8_t* __restrict__ d0 = pptr(A, op.d, t.seq0);
+  const uint64_t sa = (op.a & kSharedBit) ? 0 : A.seq_stride;
+  const uint64_t sb = (op.b & kSharedBit) ? 0 : A.seq_stride;
+  const uint64_t sd = (op.d & kSharedBit) ? 0 : A.seq_stride;
   // phase 1: loads
   uint4 ra[kEwGroups], rb[kEwGroups], rc[kEwGroups];
   V8 ia[kEwGroups];
   uint2 qa[kEwGroups], qb[kEwGroups];
-  uint64_t e0[kEwGroups];
+  uint32_t e0[kEwGroups], sq[kEwGroups];
+  float s0v[kEwGroups], s1v[kEwGroups];
 #pragma unroll
   for (uint32_t g = 0; g < kEwGroups; ++g) {
-    e0[g] = base + (uint64_t(g) * kThreads + threadIdx.x) * 8;
-    if (e0[g] >= MN) continue;
-    const uint32_t col = static_cast<uint32_t>(e0[g] % N);
+    const uint32_t e = base + (g * kThreads + threadIdx.x) * 8;
+    sq[g] = packed ? e / MN : 0u;
+    e0[g] = e - sq[g] * MN;
+    if (e >= span || e0[g] >= MN) {
+      e0[g] = MN;   // marks the group empty
+      continue;
+    }
+    const uint32_t seq = t.seq0 + sq[g];
+    s0v[g] = sreg_f32(A, op.s[0], seq);
+    s1v[g] = sreg_f32(A, op.s[1], seq);
+    const uint8_t* __restrict__ a = a0 + sq[g] * sa;
+    const uint8_t* __restrict__ b = b0 + sq[g] * sb;
+    const uint32_t col = e0[g] % N;
     if constexpr (KIND == K_QUANT || KIND == K_GELU_F16) {
       ra[g] = ld16(a + e0[g] * 2);
     } else if constexpr (KIND == K_VADD_F16) {
@@ -419,6 +438,8 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
 #pragma unroll
   for (uint32_t g = 0; g < kEwGroups; ++g) {
     if (e0[g] >= MN) continue;
+    uint8_t* __restrict__ d = d0 + sq[g] * sd;
+    const float s0 = s0v[g], s1 = s1v[g];
     if constexpr (KIND == K_QUANT) {
       int8_t q[8];
 #pragma unroll

@@ -187,3 +187,34 @@ def test_pc_past_end_and_halt_counts():
     assert int(p.info.executed) == 2 and int(p.info.cycles) == 2
     p = compile_program(1, DRAM, 0, region, 0, 1, L.Regs(), True, ())   # watchdog stops first
     assert not p.info.faulted and int(p.info.executed) == 1
+
+
+@pytest.mark.parametrize("batch", [1, 3, 5, 8])
+def test_tasks_cover_every_sequence_and_element_once(batch):
+    """Element-wise tasks either take one chunk of one sequence or pack whole
+    sequences; across an op's tasks every (sequence, element) appears once."""
+    b = load_bundle("tiny_l2_d128")
+    region = bytes(b.instruction_region())
+    p = compile_program(batch, 16 << 20, b.temp_base // 16 * 16, region, b.decode_pc, 10_000_000, L.Regs(), True,
+                        _sites(b, "decode"))
+    ops, segs, tasks, lv = p.dump()
+    EW_TASK = 8192
+    ew_kinds = set(range(7, 18)) | {19, 27}
+    seen = {}
+    for t in tasks:
+        op = ops[t["op"]]
+        if int(op["kind"]) not in ew_kinds:
+            continue
+        MN = int(op["M"]) * int(op["N"])
+        cov = seen.setdefault(int(t["op"]), np.zeros((batch, MN), np.int32))
+        s0, n = int(t["seq0"]), int(t["nseq"])
+        assert s0 + n <= batch
+        if n > 1:
+            assert n * MN <= EW_TASK and int(t["tile"]) == 0
+            cov[s0:s0 + n] += 1
+        else:
+            lo = int(t["tile"]) * EW_TASK
+            cov[s0, lo:lo + EW_TASK] += 1
+    assert seen, "no element-wise ops in the plan"
+    for opi, cov in seen.items():
+        assert (cov == 1).all(), f"op {opi}: coverage {np.unique(cov)}"
