@@ -84,14 +84,31 @@ __device__ __forceinline__ uint8_t* dram_ptr(const ExecArgs& A, uint64_t addr, u
 // ---------------------------------------------------------------------------------
 // Data movement
 // ---------------------------------------------------------------------------------
+// Copies segments [t.tile, t.aux) of the op.  A task with fewer segments
+// than warps gives each segment several warps; every lane keeps four 16-byte
+// loads in flight before it stores.
 __device__ __noinline__ void op_gather(const ExecArgs& A, const DevOp& op, const Task& t) {
-  // segments [t.tile, t.aux) of the op; one warp per segment
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (uint32_t k = t.tile + warp; k < t.aux; k += kWarps) {
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t nseg = t.aux - t.tile;
+  const uint32_t wps = nseg >= uint32_t(kWarps) ? 1u : uint32_t(kWarps) / nseg;   // warps per segment
+  const uint32_t groups = uint32_t(kWarps) / wps;
+  const uint32_t gi = warp / wps;
+  if (gi >= groups) return;
+  const uint32_t stride = wps * 32, start = (warp % wps) * 32 + lane;
+  for (uint32_t k = t.tile + gi; k < t.aux; k += groups) {
     const Segment sg = A.segs[op.seg0 + k];
-    const uint4* src = reinterpret_cast<const uint4*>(pptr(A, sg.src, t.seq0));
-    uint4* dst = reinterpret_cast<uint4*>(pptr(A, sg.dst, t.seq0));
-    for (uint64_t u = lane; u < sg.n; u += 32) dst[u] = src[u];
+    const uint4* __restrict__ src = reinterpret_cast<const uint4*>(pptr(A, sg.src, t.seq0));
+    uint4* __restrict__ dst = reinterpret_cast<uint4*>(pptr(A, sg.dst, t.seq0));
+    const uint64_t n = sg.n;
+    for (uint64_t u0 = start; u0 < n; u0 += 4 * stride) {
+      uint4 v[4];
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j)
+        if (u0 + j * stride < n) v[j] = __ldcg(src + u0 + j * stride);
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j)
+        if (u0 + j * stride < n) dst[u0 + j * stride] = v[j];
+    }
   }
 }
 
@@ -116,17 +133,60 @@ __device__ __noinline__ void op_dyn_copy(const ExecArgs& A, const DevOp& op, con
     src = reinterpret_cast<const uint4*>(pptr(A, op.a, seq));
     dst = reinterpret_cast<uint4*>(dram_ptr(A, addr, seq));
   }
-  for (uint64_t u = threadIdx.x; u < n; u += blockDim.x) dst[u] = src[u];
+  for (uint64_t u = threadIdx.x; u < n; u += blockDim.x) dst[u] = __ldcg(src + u);
 }
 
-__device__ __noinline__ void op_transpose(const ExecArgs& A, const DevOp& op, const Task& t) {
-  const int8_t* src = reinterpret_cast<const int8_t*>(pptr(A, op.a, t.seq0));
-  int8_t* dst = reinterpret_cast<int8_t*>(pptr(A, op.d, t.seq0));
-  const uint64_t rows = op.M, cols = op.N, total = rows * cols;
+// int8 [rows, cols] -> [cols, rows].  A matrix of at most kTransposeSmem bytes
+// (one task) is staged in shared memory: 16-byte coalesced loads, then each
+// thread gathers 16 consecutive output bytes of one column.  Larger matrices
+// take the element loop, 16384 output bytes per task.
+constexpr uint32_t kTransposeSmem = 16384;
+
+__device__ __noinline__ void op_transpose(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+  const int8_t* __restrict__ src = reinterpret_cast<const int8_t*>(pptr(A, op.a, t.seq0));
+  int8_t* __restrict__ dst = reinterpret_cast<int8_t*>(pptr(A, op.d, t.seq0));
+  const uint32_t rows = op.M, cols = op.N, total = rows * cols;
+  if (t.tile == 0 && total <= kTransposeSmem && rows % 16 == 0 && cols % 16 == 0) {
+    const uint32_t nv = total / 16;
+    const uint4* __restrict__ s4 = reinterpret_cast<const uint4*>(src);
+    uint4* sm4 = reinterpret_cast<uint4*>(smem);
+    for (uint32_t i0 = threadIdx.x; i0 < nv; i0 += 4 * kThreads) {
+      uint4 v[4];
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j)
+        if (i0 + j * kThreads < nv) v[j] = __ldcg(s4 + i0 + j * kThreads);
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j)
+        if (i0 + j * kThreads < nv) sm4[i0 + j * kThreads] = v[j];
+    }
+    __syncthreads();
+    const uint32_t rchunks = rows / 16;
+    uint4* __restrict__ d4 = reinterpret_cast<uint4*>(dst);
+    for (uint32_t o = threadIdx.x; o < nv; o += kThreads) {
+      const uint32_t c = o % cols, r0 = (o / cols) * 16;   // output column c, rows r0 .. r0+15
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t x = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x |= uint32_t(smem[(r0 + 4 * q + j) * cols + c]) << (8 * j);
+        w[q] = x;
+      }
+      d4[c * rchunks + r0 / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    return;
+  }
   const uint64_t lo = uint64_t(t.tile) * 16384, hi = lo + 16384 < total ? lo + 16384 : total;
-  for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-    const uint64_t c = i / rows, r = i % rows;   // dst element i = (c, r)
-    dst[i] = src[r * cols + c];
+  for (uint64_t i0 = lo + threadIdx.x; i0 < hi; i0 += 4 * kThreads) {
+    int8_t v[4];
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      const uint64_t i = i0 + j * kThreads;
+      if (i < hi) v[j] = src[(i % rows) * cols + i / rows];   // dst element i = (i / rows, i % rows)
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j)
+      if (i0 + j * kThreads < hi) dst[i0 + j * kThreads] = v[j];
   }
 }
 
@@ -899,7 +959,7 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_SREG_LOAD: op_sreg_load(A, op, t); break;
     case K_SREG_FINAL: op_sreg_final(A, op, t); break;
     case K_MATMUL: op_matmul(A, op, t, smem); break;
-    case K_TRANSPOSE: op_transpose(A, op, t); break;
+    case K_TRANSPOSE: op_transpose(A, op, t, smem); break;
     case K_MAX_ABS: op_max_abs(A, op, t, smem); break;
     case K_LAYERNORM_F16: case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16:
     case K_LN_I8: case K_SOFTMAX_I8: case K_MASKED_SOFTMAX_I8:
