@@ -204,6 +204,10 @@ int tac_argmax_f16(tac_engine* e, uint64_t addr, uint64_t count, int32_t* out_to
 int tac_set_profiling(tac_engine* e, int enable);
 int tac_read_profile(tac_engine* e, uint64_t* out_ns, uint32_t max_entries, uint32_t* n_entries);
 
+/* CTAs of the persistent executor (SMs x resident CTAs per SM); no
+ * reference counterpart. */
+int tac_engine_grid(const tac_engine* e);
+
 /* Per-sequence device pointer arithmetic for zero-copy callers. */
 int tac_engine_layout(const tac_engine* e, void** seq_base, uint64_t* seq_stride,
                       void** shared_base);

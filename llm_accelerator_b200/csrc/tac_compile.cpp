@@ -1103,6 +1103,18 @@ void Compiler::build_tasks() {
   lv.erase(std::unique(lv.begin(), lv.end()), lv.end());
   for (auto& op : P->ops) op.level = static_cast<uint32_t>(std::lower_bound(lv.begin(), lv.end(), op.level) - lv.begin());
   std::vector<std::vector<Task>> per_level(lv.size());
+  // MATMULs whose weights (B) are shared and whose A rows of up to 128/M
+  // sequences fill one 128-row tensor-core tile run on tcgen05, fed by TMA;
+  // seg0 numbers their pair of tensor maps.
+  P->n_tc = 0;
+  for (auto& op : P->ops) {
+    if (op.kind == K_MATMUL && (op.b & kSharedBit) && !(op.a & kSharedBit) && op.M < 128 && op.M % 16 == 0 &&
+        op.N % 16 == 0 && op.K % 16 == 0 && op.M > 0 && op.N > 0 && op.K > 0) {
+      op.flags |= F_TC;
+      op.seg0 = P->n_tc++;
+      op.nseg = 0;
+    }
+  }
   auto per_seq = [&](uint32_t opi, uint32_t tiles) {
     for (uint32_t s = 0; s < B; ++s)
       for (uint32_t t = 0; t < tiles; ++t) per_level[P->ops[opi].level].push_back(Task{opi, s, 1, t, 0});

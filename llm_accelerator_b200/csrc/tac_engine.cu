@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "tac_exec.cuh"
+#include "tac_tmap.h"
 #include "tac_program.h"
 
 struct tac_engine {
@@ -131,6 +132,38 @@ int upload_program(tac_engine* e, tac_program* p, tac_fault* f) {
   return TAC_OK;
 }
 
+// TMA maps of the tcgen05 MATMULs for this engine's memory layout: A as
+// [batch][M][K] over the sequences' blocks (128-byte swizzle, box 128 B x M rows
+// x 128/M sequences), the shared weights B as [K][N] (64-byte swizzle, box 64 x
+// 128).  Rebuilt when the layout changes (arena growth, another engine).
+int ensure_maps(tac_engine* e, tac_program* p, tac_fault* f) {
+  if (!p->n_tc) return TAC_OK;
+  const uint64_t key[4] = {reinterpret_cast<uint64_t>(e->d_seq), e->seq_stride,
+                           reinterpret_cast<uint64_t>(e->d_shared), uint64_t(e->batch)};
+  if (p->d_maps && std::memcmp(key, p->maps_key, sizeof(key)) == 0) return TAC_OK;
+  std::vector<CUtensorMap> maps(2 * size_t(p->n_tc));
+  for (const DevOp& op : p->ops) {
+    if (!(op.kind == K_MATMUL && (op.flags & F_TC))) continue;
+    const uint8_t* a = static_cast<const uint8_t*>(e->d_seq) + (op.a << 4);
+    const uint8_t* b = static_cast<const uint8_t*>(e->d_shared) + ((op.b & ~kSharedBit) << 4);
+    const cuuint64_t adims[3] = {op.K, op.M, cuuint64_t(e->batch)};
+    const cuuint64_t astr[2] = {op.K, e->seq_stride};
+    const cuuint32_t abox[3] = {128, op.M, 128 / op.M};
+    const cuuint64_t bdims[2] = {op.N, op.K};
+    const cuuint64_t bstr[1] = {op.N};
+    const cuuint32_t bbox[2] = {64, 128};
+    if (!tmap_encode_u8(&maps[2 * op.seg0], a, 3, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !tmap_encode_u8(&maps[2 * op.seg0 + 1], b, 2, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_64B))
+      return set_fault(f, TAC_E_CUDA, "cuTensorMapEncodeTiled rejected a MATMUL operand map");
+  }
+  if (!p->d_maps) CK(cudaMalloc(&p->d_maps, maps.size() * sizeof(CUtensorMap)), f, "cudaMalloc tensor maps");
+  else CK(cudaDeviceSynchronize(), f, "wait for runs using the old maps");
+  CK(cudaMemcpy(p->d_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice), f,
+     "upload tensor maps");
+  std::memcpy(p->maps_key, key, sizeof(key));
+  return TAC_OK;
+}
+
 uint32_t insn_bits(uint64_t w, int shift, int width) { return static_cast<uint32_t>((w >> shift) & ((1ull << width) - 1)); }
 
 // Decodes one sequence's runtime words into parameters and checks them
@@ -200,8 +233,8 @@ int tac_engine_create(int device, int batch, uint64_t dram_bytes, uint64_t share
     cudaDeviceGetAttribute(&e->n_sms, cudaDevAttrMultiProcessorCount, device);
     cudaFuncSetAttribute(exec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kExecSmem));
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exec_kernel, kThreads, kExecSmem);
-    e->grid = e->n_sms * std::max(1, std::min(per_sm, 2));
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exec_kernel, kCtaThreads, kExecSmem);
+    e->grid = e->n_sms * std::max(1, std::min(per_sm, 1));
     ok = cudaDeviceSynchronize() == cudaSuccess && per_sm >= 1;
   }
   if (!ok) {
@@ -230,6 +263,8 @@ int tac_engine_destroy(tac_engine* e) {
 }
 
 int tac_engine_batch(const tac_engine* e) { return e ? e->batch : 0; }
+
+int tac_engine_grid(const tac_engine* e) { return e ? e->grid : 0; }
 
 int tac_engine_layout(const tac_engine* e, void** seq_base, uint64_t* seq_stride, void** shared_base) {
   if (!e) return TAC_E_ARGUMENT;
@@ -313,10 +348,9 @@ int tac_sregs_read(tac_engine* e, int seq, uint16_t* regs16) {
 
 int tac_program_destroy(tac_program* p) {
   if (!p) return TAC_E_ARGUMENT;
-  if (p->d_blob) {
-    cudaSetDevice(p->device);
-    cudaFree(p->d_blob);
-  }
+  if (p->d_blob || p->d_maps) cudaSetDevice(p->device);
+  if (p->d_maps) cudaFree(p->d_maps);
+  if (p->d_blob) cudaFree(p->d_blob);
   delete p;
   return TAC_OK;
 }
@@ -328,6 +362,7 @@ static int prepare(tac_engine* e, tac_program* p, tac_fault* f) {
   if (int s = upload_program(e, p, f)) return s;
   if (int s = ensure_arena(e, p->arena_units * 16, f)) return s;
   if (int s = ensure_sregs(e, p->n_slots, f)) return s;
+  if (int s = ensure_maps(e, p, f)) return s;
   return TAC_OK;
 }
 
@@ -351,6 +386,7 @@ static int launch(tac_engine* e, tac_program* p, const uint64_t* d_params, cudaS
     A.params = d_params;
     A.status = e->d_status;
     A.barrier = e->d_status + 4;
+    A.tmaps = static_cast<const CUtensorMap*>(p->d_maps);
     A.shared_bytes = e->shared_bytes;
     A.dram_bytes = e->dram_bytes;
     A.prof = nullptr;
@@ -365,7 +401,7 @@ static int launch(tac_engine* e, tac_program* p, const uint64_t* d_params, cudaS
       e->prof_levels = n_levels;
     }
     void* args[] = {&A};
-    CK(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(exec_kernel), dim3(e->grid), dim3(kThreads), args,
+    CK(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(exec_kernel), dim3(e->grid), dim3(kCtaThreads), args,
                                    kExecSmem, st), f, "launch executor");
   }
   if (p->info.faulted) {
@@ -440,6 +476,8 @@ int tac_check_device_status(tac_engine* e, tac_fault* f) {
       return set_fault(f, TAC_E_DEVICE, "executor grid barrier timed out");
     case DF_DYN_ADDRESS:
       return set_fault(f, TAC_E_DEVICE, "runtime address outside DRAM");
+    case DF_MMA_TIMEOUT:
+      return set_fault(f, TAC_E_DEVICE, "executor tensor-core MATMUL wait timed out");
     default:
       return set_fault(f, TAC_E_DEVICE, "executor reported an invalid op");
   }

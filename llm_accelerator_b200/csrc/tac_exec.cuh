@@ -11,13 +11,28 @@
 
 #include "tac_isa.h"
 #include "tac_numerics.cuh"
+#include "tac_sm100.cuh"
 #include "tac_plan.h"
 
 namespace tac {
 
-constexpr int kThreads = 256;
+// The executor runs one 512-thread CTA per SM made of two independent halves
+// of 256 threads.  Each half walks its own share of a level's tasks with its
+// own shared memory, TMEM columns and mbarriers, and synchronizes on its own
+// named barrier; the halves meet only at the grid barrier between levels.
+// (A kernel that issues tcgen05 instructions gets one CTA per SM, so the
+// halves provide the task concurrency that two CTAs per SM would.)
+constexpr int kThreads = 256;                    // threads of one half
 constexpr int kWarps = kThreads / 32;
+constexpr int kHalves = 2;
+constexpr int kCtaThreads = kThreads * kHalves;
 constexpr uint32_t kBarrierSpinLimit = 1u << 22;   // polls of L2 (~0.5 us each): a few seconds
+
+__device__ __forceinline__ uint32_t htid() { return threadIdx.x & (kThreads - 1); }   // thread in its half
+__device__ __forceinline__ uint32_t hidx() { return threadIdx.x / kThreads; }         // which half
+__device__ __forceinline__ void hsync() {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(1 + hidx()), "n"(kThreads) : "memory");
+}
 
 // Device-side fault codes (status word 0).
 enum DevFault : uint32_t {
@@ -26,9 +41,11 @@ enum DevFault : uint32_t {
   DF_DYN_ADDRESS = 2,
   DF_ZERO_DENOM = 3,
   DF_BAD_OP = 4,
+  DF_MMA_TIMEOUT = 5,
 };
 
 struct ExecArgs {
+  const CUtensorMap* tmaps;  // two per F_TC MATMUL (A, B), indexed by op.seg0
   const DevOp* ops;
   const Segment* segs;
   const Task* tasks;
@@ -88,7 +105,7 @@ __device__ __forceinline__ uint8_t* dram_ptr(const ExecArgs& A, uint64_t addr, u
 // than warps gives each segment several warps; every lane keeps four 16-byte
 // loads in flight before it stores.
 __device__ __noinline__ void op_gather(const ExecArgs& A, const DevOp& op, const Task& t) {
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t warp = htid() >> 5, lane = htid() & 31;
   const uint32_t nseg = t.aux - t.tile;
   const uint32_t wps = nseg >= uint32_t(kWarps) ? 1u : uint32_t(kWarps) / nseg;   // warps per segment
   const uint32_t groups = uint32_t(kWarps) / wps;
@@ -116,7 +133,7 @@ __device__ __noinline__ void op_dyn_copy(const ExecArgs& A, const DevOp& op, con
   const uint32_t seq = t.seq0;
   const uint64_t addr = A.params[uint64_t(seq) * A.n_params + op.param] + op.dconst;
   if ((addr & 15) || addr + op.nbytes > A.dram_bytes) {
-    if (threadIdx.x == 0) raise_fault(A, DF_DYN_ADDRESS, opi, seq);
+    if (htid() == 0) raise_fault(A, DF_DYN_ADDRESS, opi, seq);
     return;
   }
   const uint64_t n = op.nbytes / 16;
@@ -127,13 +144,13 @@ __device__ __noinline__ void op_dyn_copy(const ExecArgs& A, const DevOp& op, con
     dst = reinterpret_cast<uint4*>(pptr(A, op.d, seq));
   } else {
     if (addr < A.shared_bytes) {
-      if (threadIdx.x == 0) raise_fault(A, DF_DYN_ADDRESS, opi, seq);
+      if (htid() == 0) raise_fault(A, DF_DYN_ADDRESS, opi, seq);
       return;
     }
     src = reinterpret_cast<const uint4*>(pptr(A, op.a, seq));
     dst = reinterpret_cast<uint4*>(dram_ptr(A, addr, seq));
   }
-  for (uint64_t u = threadIdx.x; u < n; u += blockDim.x) dst[u] = __ldcg(src + u);
+  for (uint64_t u = htid(); u < n; u += kThreads) dst[u] = __ldcg(src + u);
 }
 
 // int8 [rows, cols] -> [cols, rows].  A matrix of at most kTransposeSmem bytes
@@ -150,7 +167,7 @@ __device__ __noinline__ void op_transpose(const ExecArgs& A, const DevOp& op, co
     const uint32_t nv = total / 16;
     const uint4* __restrict__ s4 = reinterpret_cast<const uint4*>(src);
     uint4* sm4 = reinterpret_cast<uint4*>(smem);
-    for (uint32_t i0 = threadIdx.x; i0 < nv; i0 += 4 * kThreads) {
+    for (uint32_t i0 = htid(); i0 < nv; i0 += 4 * kThreads) {
       uint4 v[4];
 #pragma unroll
       for (uint32_t j = 0; j < 4; ++j)
@@ -159,10 +176,10 @@ __device__ __noinline__ void op_transpose(const ExecArgs& A, const DevOp& op, co
       for (uint32_t j = 0; j < 4; ++j)
         if (i0 + j * kThreads < nv) sm4[i0 + j * kThreads] = v[j];
     }
-    __syncthreads();
+    hsync();
     const uint32_t rchunks = rows / 16;
     uint4* __restrict__ d4 = reinterpret_cast<uint4*>(dst);
-    for (uint32_t o = threadIdx.x; o < nv; o += kThreads) {
+    for (uint32_t o = htid(); o < nv; o += kThreads) {
       const uint32_t c = o % cols, r0 = (o / cols) * 16;   // output column c, rows r0 .. r0+15
       uint32_t w[4];
 #pragma unroll
@@ -177,7 +194,7 @@ __device__ __noinline__ void op_transpose(const ExecArgs& A, const DevOp& op, co
     return;
   }
   const uint64_t lo = uint64_t(t.tile) * 16384, hi = lo + 16384 < total ? lo + 16384 : total;
-  for (uint64_t i0 = lo + threadIdx.x; i0 < hi; i0 += 4 * kThreads) {
+  for (uint64_t i0 = lo + htid(); i0 < hi; i0 += 4 * kThreads) {
     int8_t v[4];
 #pragma unroll
     for (uint32_t j = 0; j < 4; ++j) {
@@ -191,14 +208,14 @@ __device__ __noinline__ void op_transpose(const ExecArgs& A, const DevOp& op, co
 }
 
 __device__ __noinline__ void op_sreg_load(const ExecArgs& A, const DevOp& op, const Task& t) {
-  for (uint32_t s = t.seq0 + threadIdx.x; s < t.seq0 + t.nseq; s += blockDim.x) {
+  for (uint32_t s = t.seq0 + htid(); s < t.seq0 + t.nseq; s += kThreads) {
     const uint16_t v = *reinterpret_cast<const uint16_t*>(pptr(A, op.a, s));
     A.sregs[uint64_t(s) * A.sreg_stride + op.out_slot] = v;
   }
 }
 
 __device__ __noinline__ void op_sreg_final(const ExecArgs& A, const DevOp& op, const Task& t) {
-  for (uint32_t s = t.seq0 + threadIdx.x; s < t.seq0 + t.nseq; s += blockDim.x) {
+  for (uint32_t s = t.seq0 + htid(); s < t.seq0 + t.nseq; s += kThreads) {
     uint16_t vals[16];
     for (uint32_t k = 0; k < op.nseg && k < 16; ++k)
       vals[k] = sreg_bits(A, static_cast<uint32_t>(A.segs[op.seg0 + k].src), s);
@@ -212,7 +229,7 @@ __device__ __noinline__ void op_sreg_final(const ExecArgs& A, const DevOp& op, c
 // A task covers up to 128 rows (whole sequences when B is shared) x 64 columns.
 // ---------------------------------------------------------------------------------
 constexpr int kMmKc = 128;             // K chunk (bytes of A rows / rows of B)
-constexpr int kMmStages = 3;           // cp.async pipeline depth
+constexpr int kMmStages = 2;           // cp.async pipeline depth (per-sequence operands: K <= 256 in decoder programs)
 constexpr int kMmAStride = kMmKc + 16; // A row stride in shared memory: 144 B keeps the 8 rows
                                        // of an mma fragment load on distinct banks
 constexpr int kMmAStage = 128 * kMmAStride; // 8 row blocks x 16 rows x K chunk
@@ -267,7 +284,7 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
   uint8_t* As = smem;                                    // [stage][blk*16 + row][kMmAStride]
   uint8_t* Bs = smem + kMmStages * kMmAStage;            // [stage][k][64] raw
   uint8_t* Bt = Bs + kMmStages * kMmBStage;              // [n][kMmBStride] transposed
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = htid() >> 5, lane = htid() & 31;
   const int g = lane >> 2, q = lane & 3;
   int acc[8][4];
 #pragma unroll
@@ -288,14 +305,14 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
     uint8_t* as = As + (c % kMmStages) * kMmAStage;
     uint8_t* bs = Bs + (c % kMmStages) * kMmBStage;
     // A: nblocks*16 rows x 8 vectors of 16 bytes
-    for (uint32_t i = threadIdx.x; i < nblocks * 16 * (kMmKc / 16); i += blockDim.x) {
+    for (uint32_t i = htid(); i < nblocks * 16 * (kMmKc / 16); i += kThreads) {
       const uint32_t v = i % (kMmKc / 16), row = i / (kMmKc / 16);
       const bool in = v * 16 < kc;
       const uint8_t* src = Ag[row / 16] + uint64_t(row % 16) * K + k0 + (in ? v * 16 : 0);
       cp_async16(as + row * kMmAStride + v * 16, src, in ? 16u : 0u);
     }
     // B: kMmKc rows x 4 vectors of 16 bytes (64 columns)
-    for (uint32_t i = threadIdx.x; i < uint32_t(kMmKc) * 4; i += blockDim.x) {
+    for (uint32_t i = htid(); i < uint32_t(kMmKc) * 4; i += kThreads) {
       const uint32_t v = i % 4, kk = i / 4;
       const bool in = kk < kc && v * 16 < ncols;
       const uint8_t* src = Bg + (in ? uint64_t(k0 + kk) * N + n0 + v * 16 : 0);
@@ -310,7 +327,7 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
   }
   for (uint32_t c = 0; c < nchunks; ++c) {
     cp_async_wait<kMmStages - 2>();
-    __syncthreads();   // chunk c landed; every warp finished chunk c-1 (slot and Bt free)
+    hsync();   // chunk c landed; every warp finished chunk c-1 (slot and Bt free)
     if (c + kMmStages - 1 < nchunks) issue(c + kMmStages - 1);
     cp_async_commit();
     const uint32_t k0 = c * kMmKc;
@@ -319,7 +336,7 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
     const uint8_t* as = As + (c % kMmStages) * kMmAStage;
     const uint8_t* bs = Bs + (c % kMmStages) * kMmBStage;
     // transpose B [k][n] -> Bt [n][k], 4x4 byte blocks
-    for (uint32_t i = threadIdx.x; i < (kc32 / 4) * 16; i += blockDim.x) {
+    for (uint32_t i = htid(); i < (kc32 / 4) * 16; i += kThreads) {
       const uint32_t kb = (i / 16) * 4, nb = (i % 16) * 4;
       uint32_t r[4];
 #pragma unroll
@@ -331,7 +348,7 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
       *reinterpret_cast<uint32_t*>(Bt + (nb + 2) * kMmBStride + kb) = __byte_perm(t2, t3, 0x5410);
       *reinterpret_cast<uint32_t*>(Bt + (nb + 3) * kMmBStride + kb) = __byte_perm(t2, t3, 0x7632);
     }
-    __syncthreads();
+    hsync();
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const uint32_t p = warp + 8 * i;
@@ -374,7 +391,124 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
       *reinterpret_cast<int2*>(D + row * N + col) = v;
     }
   }
-  __syncthreads();
+  hsync();
+}
+
+// ---------------------------------------------------------------------------------
+// MATMUL with shared weights on the 5th-generation tensor cores (ops flagged
+// F_TC).  A task is up to 128 rows (the M rows of up to 128/M sequences) x 64
+// columns.  Per 128-byte K block, TMA brings A as one [128/M sequences][M
+// rows][128 B] box (128-byte swizzle, K-major) and the weights as a [128 K
+// rows][64 B] box (64-byte swizzle, MN-major) into one of three
+// shared-memory stages; thread 0 issues tcgen05.mma.kind::i8 (M 128, N 64,
+// K 32) into this CTA's 64 TMEM columns and recycles a stage once the MMAs
+// that read it have committed.  The eight warps read the int32 accumulator
+// back with tcgen05.ld.  Waits are bounded (DF_MMA_TIMEOUT).
+// ---------------------------------------------------------------------------------
+constexpr int kTcStages = 3;
+constexpr uint32_t kTcAStage = 128 * 128;
+constexpr uint32_t kTcBStage = 128 * 64;
+constexpr uint32_t kTcStage = kTcAStage + kTcBStage;   // a multiple of 1024
+constexpr uint32_t kTcCols = 64;
+constexpr uint32_t kTcIdesc = sm100::idesc_i8(128, 64, 1);
+
+struct TcShared {
+  uint64_t full[kTcStages];    // TMA bytes of a stage landed
+  uint64_t empty[kTcStages];   // the MMAs reading a stage completed
+  uint32_t tmem;
+  uint32_t phase_full;         // bit s: parity of the next phase of full[s]
+  uint32_t phase_empty;
+};
+
+// shared-memory descriptor, 64-byte swizzle (layout type 4)
+__device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return uint64_t((saddr >> 4) & 0x3FFF) | (uint64_t((lbo >> 4) & 0x3FFF) << 16) |
+         (uint64_t((sbo >> 4) & 0x3FFF) << 32) | (uint64_t(1) << 46) | (uint64_t(4) << 61);
+}
+
+__device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
+                                          TcShared* tc, uint32_t opi) {
+  const uint32_t M = op.M, N = op.N, K = op.K;
+  const uint32_t n0 = t.tile * 64;
+  const uint32_t ncols = N - n0 < 64 ? N - n0 : 64;
+  const uint32_t rows = t.nseq * M;                       // <= 128
+  const uint32_t nchunks = (K + 127) / 128;
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023));
+  if (htid() == 0) {
+    const CUtensorMap* ma = A.tmaps + 2 * op.seg0;
+    const CUtensorMap* mb = ma + 1;
+    const uint32_t bytes = (128 / M) * M * 128 + kTcBStage;
+    uint32_t pf = tc->phase_full, pe = tc->phase_empty;
+    bool ok = true;
+    auto load = [&](uint32_t c) {
+      const uint32_t st = c % kTcStages;
+      uint8_t* as = base + st * kTcStage;
+      sm100::mbar_arrive_expect_tx(&tc->full[st], bytes);
+      sm100::tma_load_3d(as, ma, int32_t(c * 128), 0, int32_t(t.seq0), &tc->full[st]);
+      sm100::tma_load_2d(as + kTcAStage, mb, int32_t(n0), int32_t(c * 128), &tc->full[st]);
+    };
+    auto wait = [&](uint64_t* bar, uint32_t& ph, uint32_t st) {
+      if (!sm100::mbar_wait(&bar[st], (ph >> st) & 1u, nullptr, 0)) ok = false;
+      ph ^= 1u << st;
+    };
+    for (uint32_t c = 0; c < nchunks && c < uint32_t(kTcStages); ++c) load(c);
+    for (uint32_t c = 0; c < nchunks; ++c) {
+      const uint32_t st = c % kTcStages;
+      wait(tc->full, pf, st);
+      sm100::tc_fence_after();
+      const uint32_t a_addr = sm100::smem_u32(base + st * kTcStage), b_addr = a_addr + kTcAStage;
+      const uint32_t kc = K - c * 128 < 128 ? K - c * 128 : 128;
+      for (uint32_t ks = 0; ks * 32 < kc; ++ks)
+        sm100::mma_i8(tc->tmem, sm100::smem_desc_sw128(a_addr + ks * 32, 16, 1024),
+                      desc_sw64(b_addr + ks * 2048, 16, 512), kTcIdesc, (c | ks) != 0);
+      sm100::mma_commit(&tc->empty[st]);
+      if (c + kTcStages < nchunks) {   // refill this stage once its MMAs are done
+        wait(tc->empty, pe, st);
+        load(c + kTcStages);
+      }
+    }
+    // the commits not yet waited: every MMA of the task is done after these
+    for (uint32_t j = nchunks > uint32_t(kTcStages) ? nchunks - kTcStages : 0; j < nchunks; ++j)
+      wait(tc->empty, pe, j % kTcStages);
+    tc->phase_full = pf;
+    tc->phase_empty = pe;
+    if (!ok) raise_fault(A, DF_MMA_TIMEOUT, opi, t.seq0);
+  }
+  hsync();
+  sm100::tc_fence_after();
+
+  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31, columns 32 (w / 4) .. +31
+  const uint32_t warp = htid() >> 5, lane = htid() & 31, q = warp & 3, h = warp >> 2;
+  uint32_t v[32];
+  __syncwarp();
+  sm100::tmem_ld32(tc->tmem + ((q * 32) << 16) + h * 32, v);
+  const uint32_t r = q * 32 + lane;
+  if (r < rows && h * 32 < ncols) {
+    const uint32_t seq = t.seq0 + r / M, row = r % M;
+    const uint32_t col0 = n0 + h * 32;
+    const uint32_t nc = ncols - h * 32 < 32 ? ncols - h * 32 : 32;
+    int32_t* D = reinterpret_cast<int32_t*>(pptr(A, op.d, seq)) + uint64_t(row) * N + col0;
+    const int32_t* C = (op.flags & F_ACCUMULATE)
+                           ? reinterpret_cast<const int32_t*>(pptr(A, op.c, seq)) + uint64_t(row) * N + col0
+                           : nullptr;
+#pragma unroll
+    for (uint32_t j = 0; j < 32; j += 4) {
+      if (j < nc) {
+        int4 val = make_int4(int(v[j]), int(v[j + 1]), int(v[j + 2]), int(v[j + 3]));
+        if (C) {
+          const int4 cv = __ldcg(reinterpret_cast<const int4*>(C + j));
+          val.x = int32_t(uint32_t(val.x) + uint32_t(cv.x));
+          val.y = int32_t(uint32_t(val.y) + uint32_t(cv.y));
+          val.z = int32_t(uint32_t(val.z) + uint32_t(cv.z));
+          val.w = int32_t(uint32_t(val.w) + uint32_t(cv.w));
+        }
+        *reinterpret_cast<int4*>(D + j) = val;
+      }
+    }
+  }
+  // the next tcgen05 MATMUL overwrites the accumulator only after every warp read it
+  sm100::tc_fence_before();
+  hsync();
 }
 
 // ---------------------------------------------------------------------------------
@@ -449,7 +583,7 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
   float s0v[kEwGroups], s1v[kEwGroups];
 #pragma unroll
   for (uint32_t g = 0; g < kEwGroups; ++g) {
-    const uint32_t e = base + (g * kThreads + threadIdx.x) * 8;
+    const uint32_t e = base + (g * kThreads + htid()) * 8;
     sq[g] = packed ? e / MN : 0u;
     e0[g] = e - sq[g] * MN;
     if (e >= span || e0[g] >= MN) {
@@ -624,11 +758,11 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
   uint32_t m = 0;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
   const uint64_t ng = MN / 8;   // MN is a multiple of 256
-  for (uint64_t g0 = threadIdx.x; g0 < ng; g0 += uint64_t(blockDim.x) * 8) {
+  for (uint64_t g0 = htid(); g0 < ng; g0 += uint64_t(kThreads) * 8) {
     uint4 v[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const uint64_t g = g0 + uint64_t(k) * blockDim.x;
+      const uint64_t g = g0 + uint64_t(k) * kThreads;
       v[k] = g < ng ? __ldcg(xv + g) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
@@ -645,9 +779,9 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
     m = w > m ? w : m;
   }
   uint32_t* red = reinterpret_cast<uint32_t*>(smem);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-  __syncthreads();
-  if (threadIdx.x == 0) {
+  if ((htid() & 31) == 0) red[htid() >> 5] = m;
+  hsync();
+  if (htid() == 0) {
     for (int w = 1; w < kWarps; ++w) m = red[w] > m ? red[w] : m;
     uint16_t inv, fwd;
     if (m == 0xFFFFu) {
@@ -662,7 +796,7 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
     A.sregs[uint64_t(seq) * A.sreg_stride + op.out_slot] = inv;
     A.sregs[uint64_t(seq) * A.sreg_stride + op.out_slot + 1] = fwd;
   }
-  __syncthreads();
+  hsync();
 }
 
 // ---------------------------------------------------------------------------------
@@ -691,7 +825,7 @@ __device__ __forceinline__ float in_val(const ExecArgs& A, const DevOp& op, uint
 }
 
 __device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem, uint32_t opi) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = htid() >> 5, lane = htid() & 31;
   const uint32_t seq = t.seq0, N = op.N;
   const uint32_t r = t.tile * 8 + warp;
   float* rowbuf = reinterpret_cast<float*>(smem) + warp * kRowCap;
@@ -855,7 +989,7 @@ __device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const T
 
 // Legacy fused softmax(QK^T)·V (sfu.py:323-443): one warp per query row.
 __device__ __noinline__ void op_attnv(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = htid() >> 5, lane = htid() & 31;
   const uint32_t seq = t.seq0, M = op.M, N = op.N, K = op.K;
   const uint32_t r = t.tile * 8 + warp;
   float* rowbuf = reinterpret_cast<float*>(smem) + warp * kRowCap;
@@ -916,8 +1050,9 @@ __device__ __forceinline__ void prefetch_l1(const void* p) {
 // add and waits, with acquire loads, until all gridDim.x CTAs of this level
 // have arrived (target = (level + 1) * gridDim.x).  The same poll watches the
 // fault word, so a fault anywhere stops every CTA at its next barrier.  The
-// wait is bounded: running out raises DF_BARRIER_TIMEOUT.  Meanwhile warp 1
-// pulls this CTA's first task of the next level and its op record into L1.
+// wait is bounded: running out raises DF_BARRIER_TIMEOUT.  Meanwhile warp 1 of
+// each half pulls that half's first task of the next level and its op record
+// into L1.
 __device__ __forceinline__ bool grid_barrier(const ExecArgs& A, uint32_t target, uint32_t next_level) {
   __syncthreads();
   __shared__ uint32_t ok;
@@ -936,8 +1071,8 @@ __device__ __forceinline__ bool grid_barrier(const ExecArgs& A, uint32_t target,
       if (spins > 256) __nanosleep(32);
     }
     ok = st == 0;
-  } else if (threadIdx.x == 32 && next_level < A.n_levels) {
-    const uint32_t ti = A.level_off[next_level] + blockIdx.x;
+  } else if (htid() == 32 && next_level < A.n_levels) {
+    const uint32_t ti = A.level_off[next_level] + blockIdx.x * kHalves + hidx();
     if (ti < A.level_off[next_level + 1]) {
       const uint32_t op = A.tasks[ti].op;
       prefetch_l1(A.ops + op);
@@ -948,8 +1083,9 @@ __device__ __forceinline__ bool grid_barrier(const ExecArgs& A, uint32_t target,
   return ok != 0;
 }
 
-__device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t next_ti) {
-  if (threadIdx.x == 32 && next_ti != 0xFFFFFFFFu) prefetch_l1(A.tasks + next_ti);
+// Runs one task on the calling half.
+__device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t next_ti, TcShared* tc) {
+  if (htid() == 32 && next_ti != 0xFFFFFFFFu) prefetch_l1(A.tasks + next_ti);
   const Task t = A.tasks[ti];
   const DevOp& op = A.ops[t.op];
   switch (op.kind) {
@@ -958,7 +1094,10 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_DYN_STORE: op_dyn_copy(A, op, t, t.op); break;
     case K_SREG_LOAD: op_sreg_load(A, op, t); break;
     case K_SREG_FINAL: op_sreg_final(A, op, t); break;
-    case K_MATMUL: op_matmul(A, op, t, smem); break;
+    case K_MATMUL:
+      if (op.flags & F_TC) op_matmul_tc(A, op, t, smem, tc, t.op);
+      else op_matmul(A, op, t, smem);
+      break;
     case K_TRANSPOSE: op_transpose(A, op, t, smem); break;
     case K_MAX_ABS: op_max_abs(A, op, t, smem); break;
     case K_LAYERNORM_F16: case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16:
@@ -972,25 +1111,54 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
       op_elementwise(A, op, t);
       break;
     default:
-      if (threadIdx.x == 0) raise_fault(A, DF_BAD_OP, t.op, t.seq0);
+      if (htid() == 0) raise_fault(A, DF_BAD_OP, t.op, t.seq0);
       break;
   }
-  __syncthreads();
+  hsync();
 }
 
-// Shared memory: max(MATMUL tiles, row buffers + pairwise scratch).
+// Shared memory of one half: max(MATMUL tiles, row buffers + pairwise scratch,
+// tcgen05 stages); the two halves' regions are followed by their TcShared slots.
 constexpr size_t kRowSmem = kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4;
-constexpr size_t kExecSmem = kRowSmem > kMmSmem ? kRowSmem : kMmSmem;
+constexpr size_t kTcSmem = kTcStages * kTcStage + 1024;   // + alignment of the swizzled stages
+constexpr size_t kExecOpSmem0 = kRowSmem > kMmSmem ? kRowSmem : kMmSmem;
+constexpr size_t kExecOpSmem = kExecOpSmem0 > kTcSmem ? kExecOpSmem0 : kTcSmem;
+constexpr size_t kExecSmem = kHalves * kExecOpSmem + kHalves * 64;
+static_assert(sizeof(TcShared) <= 64, "TcShared outgrew its slot");
+static_assert(kExecOpSmem % 1024 == 0 || kTcSmem <= kExecOpSmem, "half regions must keep the stage alignment slack");
+static_assert(kExecSmem <= 227 * 1024, "executor shared memory exceeds one CTA's limit");
 
-__global__ void __launch_bounds__(kThreads, 2) exec_kernel(ExecArgs A) {
-  extern __shared__ __align__(16) uint8_t smem[];
+__global__ void __launch_bounds__(kCtaThreads, 1) exec_kernel(ExecArgs A) {
+  extern __shared__ __align__(16) uint8_t smem_all[];
+  uint8_t* smem = smem_all + hidx() * kExecOpSmem;
+  TcShared* tcs = reinterpret_cast<TcShared*>(smem_all + kHalves * kExecOpSmem);
+  TcShared* tc = tcs + hidx();
+  if (threadIdx.x == 0) {
+    for (int h = 0; h < kHalves; ++h) {
+      for (int st = 0; st < kTcStages; ++st) {
+        sm100::mbar_init(&tcs[h].full[st], 1);
+        sm100::mbar_init(&tcs[h].empty[st], 1);
+      }
+      tcs[h].phase_full = 0;
+      tcs[h].phase_empty = 0;
+    }
+    sm100::mbar_fence_init();
+  }
+  if (threadIdx.x < 32) sm100::tmem_alloc(&tcs[0].tmem, kHalves * kTcCols);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  if (threadIdx.x == 0)
+    for (int h = 1; h < kHalves; ++h) tcs[h].tmem = tcs[0].tmem + h * kTcCols;   // column offset
+  __syncthreads();
   if (A.prof && blockIdx.x == 0 && threadIdx.x == 0) A.prof[0] = global_ns();
+  const uint32_t vid = blockIdx.x * kHalves + hidx(), vgrid = gridDim.x * kHalves;
   for (uint32_t L = 0; L < A.n_levels; ++L) {
     const uint32_t t0 = A.level_off[L], t1 = A.level_off[L + 1];
-    for (uint32_t ti = t0 + blockIdx.x; ti < t1; ti += gridDim.x)
-      run_task(A, ti, smem, ti + gridDim.x < t1 ? ti + gridDim.x : 0xFFFFFFFFu);
+    for (uint32_t ti = t0 + vid; ti < t1; ti += vgrid)
+      run_task(A, ti, smem, ti + vgrid < t1 ? ti + vgrid : 0xFFFFFFFFu, tc);
     if (L + 1 < A.n_levels) {
-      if (!grid_barrier(A, (L + 1) * gridDim.x, L + 1)) return;
+      if (!grid_barrier(A, (L + 1) * gridDim.x, L + 1)) break;
       if (threadIdx.x == 0 && blockIdx.x == 0) {
         A.status[3] = L + 1;
         if (A.prof) A.prof[L + 1] = global_ns();
@@ -1002,6 +1170,14 @@ __global__ void __launch_bounds__(kThreads, 2) exec_kernel(ExecArgs A) {
     __syncthreads();
     if (threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned long long*>(&A.prof[A.n_levels]),
                                     static_cast<unsigned long long>(global_ns()));
+  }
+  // every MMA completed inside its task; release this CTA's TMEM columns
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tcs[0].tmem, kHalves * kTcCols);
   }
 }
 

@@ -64,7 +64,7 @@ __device__ __forceinline__ float gelu_f32(float x) {
 }
 
 // ---- NumPy pairwise summation -------------------------------------------------
-constexpr int kPwMaxLeaves = 256;
+constexpr int kPwMaxLeaves = 64;
 
 // Leaves of the pairwise tree over n elements, left to right.
 __device__ inline int pw_leaves(uint32_t n, uint32_t* loff, uint32_t* llen) {

@@ -66,6 +66,7 @@ enum DevKind : uint16_t {
 constexpr uint16_t F_ACCUMULATE = 1;   // MATMUL adds the previous int32 tile (operand c)
 constexpr uint16_t F_SRC_I32 = 2;      // legacy SFU input is int32 (ACCUM) rather than int8
 constexpr uint16_t F_ATTN_DYN = 4;     // masked softmax context comes from a runtime parameter
+constexpr uint16_t F_TC = 8;           // MATMUL with shared weights on tcgen05, TMA maps pair seg0
 
 struct DevOp {
   uint16_t kind;

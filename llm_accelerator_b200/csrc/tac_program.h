@@ -61,6 +61,9 @@ struct tac_program {
   // Device mirror (filled by the engine on first use).
   int device = -1;
   void* d_blob = nullptr;
+  uint32_t n_tc = 0;                     // MATMULs flagged F_TC (two TMA maps each)
+  void* d_maps = nullptr;                // their maps, encoded for one engine layout
+  uint64_t maps_key[4] = {0, 0, 0, 0};   // seq_base, seq_stride, shared_base, batch
   uint64_t off_ops = 0, off_segs = 0, off_tasks = 0, off_levels = 0;
 };
 

@@ -212,6 +212,10 @@ class Engine:
             L.check(_lib.tac_read_profile(self.handle, out.ctypes.data, n.value, C.byref(n)), "tac_read_profile")
         return out
 
+    def grid(self) -> int:
+        """CTAs of the persistent executor launch."""
+        return int(_lib.tac_engine_grid(self.handle))
+
     def layout(self):
         sb, ss, sh = C.c_void_p(), C.c_uint64(), C.c_void_p()
         L.check(_lib.tac_engine_layout(self.handle, C.byref(sb), C.byref(ss), C.byref(sh)), "tac_engine_layout")
