@@ -308,6 +308,7 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     import torch.distributed as dist
     from llm_accelerator_b200.runner import BatchedRunner
 
+    from llm_accelerator_b200.shard import gather_tokens, shard
     B_total = args.batch or w["batch"]
     if B_total % world:
         raise SystemExit(f"batch {B_total} does not split over {world} GPUs")
@@ -316,7 +317,7 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     dev = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(dev)
     runner = BatchedRunner(bundle, B, device=local_rank)
-    seqs = np.arange(rank * B, rank * B + B)
+    seqs = np.asarray(shard(B_total, world, rank))
     K, W = args.steps, args.warmup
     if 1 + W + 2 * K >= w["kv_len"]:
         raise SystemExit("steps + warmup exceed the KV length of the workload")
@@ -358,7 +359,6 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     # e2e: K greedy steps through the runner API with host buffers each step
     tok_dev = torch.zeros(B, dtype=torch.int32, device=dev)
     tok_host = torch.zeros(B, dtype=torch.int32).pin_memory()
-    gathered = [torch.zeros(B, dtype=torch.int32, device=dev) for _ in range(world)]
     tokens = prompts[:, p0 + K - 1].copy()
     runner.argmax_async("decode", tok_dev.data_ptr(), VOCAB, stream.cuda_stream)
     tok_host.copy_(tok_dev)
@@ -369,8 +369,7 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     for i in range(K):
         runner.step_async("decode", tokens, np.full(B, pos0 + i), stream.cuda_stream)
         runner.argmax_async("decode", tok_dev.data_ptr(), VOCAB, stream.cuda_stream)
-        if world > 1:
-            dist.all_gather(gathered, tok_dev)
+        gather_tokens(tok_dev, world)   # every rank sees the whole batch's tokens (NCCL all-gather)
         tok_host.copy_(tok_dev, non_blocking=True)
         stream.synchronize()
         tokens = tok_host.numpy().astype(np.int64)
