@@ -253,6 +253,20 @@ def int8_gemm_line():
     return out
 
 
+def quarot_line():
+    """The QuaRot W8A16 layer workload (1024 x 768 activations = 8 x 128
+    tokens, 768 x 3072 INT8 weights, block Hadamard 3 x 256): device time of
+    rotation + quantisation + INT8 GEMM with the dequant epilogue."""
+    from llm_accelerator_b200.quarot import time_layer
+    r = time_layer(1024, 768, 3072, block=256)
+    peak_gbs, _ = measured_peak()
+    return {"shape": r["shape"], "block": r["block"], "ms": round(r["ms"], 4), "tops": round(r["tflops"], 1),
+            "frac_of_nominal_int8": round(r["tflops"] / INT8_DENSE_PEAK_TOPS, 4),
+            "gbs": round(r["gbs"], 1), "frac_of_measured_hbm": round(r["gbs"] / peak_gbs, 4),
+            "algorithmic_bytes": r["bytes"],
+            "timing": "median of 20 calls (4 stream-ordered launches), CUDA events, L2 flushed"}
+
+
 def traffic_per_launch(workload, batch):
     """DRAM bytes per executor launch from the committed ncu summary (or None)."""
     f = ROOT / "profiles" / f"exec_kernel_{workload}.txt"
@@ -381,9 +395,10 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     e2e = B_total * K / float(t.item())
     runner.engine.check_device()
 
-    gemm_line = None
+    gemm_line = quarot = None
     if rank == 0 and not args.no_gemm:
         gemm_line = int8_gemm_line()
+        quarot = quarot_line()
     barrier()
 
     plan = runner.plans["decode"]
@@ -417,6 +432,8 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
             line["cpu_baseline"] = cpu_baseline
         if gemm_line is not None:
             line["int8_gemm"] = gemm_line
+        if quarot is not None:
+            line["quarot_w8a16"] = quarot
         print(json.dumps(line), flush=True)
 
 
@@ -429,7 +446,8 @@ def main():
     ap.add_argument("--workload", default="gpt2-medium", choices=sorted(WORKLOADS))
     ap.add_argument("--batch", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-gemm", action="store_true", help="skip the stand-alone 4096^3 INT8 GEMM measurement")
+    ap.add_argument("--no-gemm", action="store_true",
+                    help="skip the stand-alone 4096^3 INT8 GEMM and QuaRot layer measurements")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -247,6 +247,34 @@ int tac_gemm_i8_i32(const int8_t* A, const int8_t* B, int32_t* C, int M, int N, 
 int tac_gemv_i8_requant_pc_static(const int8_t* A, const int8_t* B, const uint16_t* scale_f16,
                                   int8_t* out, int M, int N, int K, void* stream);
 
+/* ---- QuaRot W8A16 layer ----------------------------------------------------
+ * The reference folds QuaRot's rotation into the weights offline
+ * (quantizer/rotation.py:51-135) and has no runtime Hadamard; these entry
+ * points add one.  All pointers are device pointers; FP16 values as bits. */
+
+/* Y[M,K] = rows of X rotated by the normalised block Walsh-Hadamard
+ * I (x) H_block / sqrt(block) (H the Sylvester matrix of rotation.py:108-114):
+ * float32 butterflies, one rounding to FP16.  block: a power of two in
+ * [32, 1024] dividing K; X and Y 16-byte aligned. */
+int tac_fwht_f16(const uint16_t* X, uint16_t* Y, int M, int K, int block, void* stream);
+
+/* Bytes of workspace tac_quarot_w8a16 needs (rotated FP16 rows, their INT8
+ * quantisation, scale words). */
+uint64_t tac_quarot_workspace_bytes(int M, int K);
+
+/* Y[M,N] FP16 = the W8A16 dynamic matmul (runtime/w8a16_simulator_reference.py:96-135:
+ * per-tensor max|x| floored at 2^-9, FP16 inverse / forward scales, INT8
+ * round-half-even activations, INT8 x INT8 -> int32, then
+ * fp16((f32(acc) * f32(w_scale[n])) * f32(fwd) + f32(bias[n]))) applied to the
+ * block-Hadamard-rotated rows of X.  W int8 [K,N] row-major; bias may be null;
+ * workspace >= tac_quarot_workspace_bytes(M, K), 256-byte aligned.  Four
+ * stream-ordered launches: rotation (+ max|x|), activation quantisation,
+ * tcgen05 GEMM with the dequant epilogue.  Calls sharing a workspace must not
+ * overlap. */
+int tac_quarot_w8a16(const uint16_t* X, const int8_t* W, const uint16_t* w_scale, const uint16_t* bias,
+                     uint16_t* Y, void* workspace, uint64_t workspace_bytes, int M, int N, int K,
+                     int block, void* stream);
+
 /* The stand-alone GEMMs run on the tcgen05 kernel when K and N are
  * multiples of 16 and A, B and the output are 16-byte aligned, otherwise on
  * an mma.sync kernel; both are exact.  Every wait inside the tcgen05 kernel

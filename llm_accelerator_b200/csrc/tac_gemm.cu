@@ -98,10 +98,17 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, tac::TcGemmParams p,
   return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
 }
 
-int launch_gemm(const int8_t* A, const int8_t* B, void* out, const uint16_t* scale, const int32_t* mult,
-                const int32_t* shift, int M, int N, int K, int epi, void* stream) {
+}  // namespace
+
+namespace tac {
+
+// The stand-alone GEMM dispatcher (also used by the QuaRot layer).
+int gemm_launch(const int8_t* A, const int8_t* B, void* out, const uint16_t* scale, const int32_t* mult,
+                const int32_t* shift, int M, int N, int K, int epi, void* stream, const uint16_t* act_scale,
+                const uint16_t* bias) {
   if (!A || !B || !out || M <= 0 || N <= 0 || K <= 0) return TAC_E_ARGUMENT;
-  if (epi == tac::EPI_REQUANT_PC && !scale) return TAC_E_ARGUMENT;
+  if ((epi == tac::EPI_REQUANT_PC || epi == tac::EPI_DEQUANT_SCALED) && !scale) return TAC_E_ARGUMENT;
+  if (epi == tac::EPI_DEQUANT_SCALED && !act_scale) return TAC_E_ARGUMENT;
   if (epi == tac::EPI_REQUANT_SHIFT && (!mult || !shift)) return TAC_E_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (K % 16 == 0 && N % 16 == 0 && aligned16(A) && aligned16(B) && aligned16(out)) {
@@ -112,14 +119,23 @@ int launch_gemm(const int8_t* A, const int8_t* B, void* out, const uint16_t* sca
       DeviceInfo& di = device_info(dev);
       int* fault = nullptr;
       if (cudaGetSymbolAddress(reinterpret_cast<void**>(&fault), g_tc_gemm_fault) != cudaSuccess) return TAC_E_CUDA;
-      tac::TcGemmParams p{out, scale, mult, shift, M, N, K, epi, 0, 0, 0, fault};
+      tac::TcGemmParams p{out, scale, mult, shift, M, N, K, epi, 0, 0, 0, fault, act_scale, bias};
       return pick_bn(M, N, di.sms) == 256 ? launch_tc<256>(ma, mb, p, di, st) : launch_tc<128>(ma, mb, p, di, st);
     }
   }
-  tac::GemmArgs g{A, B, out, scale, mult, shift, M, N, K, epi};
+  tac::GemmArgs g{A, B, out, scale, mult, shift, M, N, K, epi, act_scale, bias};
   dim3 grid((N + tac::kSgBN - 1) / tac::kSgBN, (M + tac::kSgBM - 1) / tac::kSgBM);
   tac::gemm_sync_kernel<<<grid, 256, 0, st>>>(g);
   return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
+}
+
+}  // namespace tac
+
+namespace {
+
+int launch_gemm(const int8_t* A, const int8_t* B, void* out, const uint16_t* scale, const int32_t* mult,
+                const int32_t* shift, int M, int N, int K, int epi, void* stream) {
+  return tac::gemm_launch(A, B, out, scale, mult, shift, M, N, K, epi, stream, nullptr, nullptr);
 }
 
 }  // namespace

@@ -5,11 +5,11 @@
 #pragma once
 #include <cstdint>
 
+#include "tac_gemm_epi.h"
 #include "tac_numerics.cuh"
 
 namespace tac {
 
-enum GemmEpilogue : int { EPI_I32 = 0, EPI_REQUANT_PC = 1, EPI_REQUANT_SHIFT = 2 };
 
 struct GemmArgs {
   const int8_t* A;
@@ -20,7 +20,16 @@ struct GemmArgs {
   const int32_t* shift;
   int M, N, K;
   int epi;
+  const uint16_t* act_scale;   // EPI_DEQUANT_SCALED: one FP16 activation scale (device memory)
+  const uint16_t* bias;        // EPI_DEQUANT_SCALED: per-column FP16 bias or null
 };
+
+// DEQUANT_ACCUM_FP32_SCALED arithmetic: fp16((f32(acc) * f32(pc)) * f32(act) [+ f32(bias)])
+__device__ __forceinline__ uint16_t dequant_scaled(int32_t acc, float pc, float act, const uint16_t* bias, int col) {
+  float y = __fmul_rn(__fmul_rn(__int2float_rn(acc), pc), act);
+  if (bias) y = __fadd_rn(y, h2f(bias[col]));
+  return f2h(y);
+}
 
 // clip((acc * mult + 2^(shift-1)) >> shift) in int64, floor shift; shift 0 = no rounding term.
 __device__ __forceinline__ int8_t requant_shift(int32_t acc, int32_t mult, int32_t shift) {
@@ -39,6 +48,9 @@ __device__ __forceinline__ void gemm_store(const GemmArgs& g, int row, int col, 
       break;
     case EPI_REQUANT_PC:
       static_cast<int8_t*>(g.out)[idx] = sat8(__fmul_rn(__int2float_rn(acc), h2f(g.scale_f16[col])));
+      break;
+    case EPI_DEQUANT_SCALED:
+      static_cast<uint16_t*>(g.out)[idx] = dequant_scaled(acc, h2f(g.scale_f16[col]), h2f(*g.act_scale), g.bias, col);
       break;
     default:
       static_cast<int8_t*>(g.out)[idx] = requant_shift(acc, g.mult[col], g.shift[col]);

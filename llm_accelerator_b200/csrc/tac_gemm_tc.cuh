@@ -37,6 +37,8 @@ struct TcGemmParams {
   int epi;
   int m_tiles, n_tiles, k_blocks;
   int* fault;
+  const uint16_t* act_scale;   // EPI_DEQUANT_SCALED
+  const uint16_t* bias;
 };
 
 template <int BN>
@@ -69,6 +71,37 @@ __device__ __forceinline__ void tc_store_chunk(const TcGemmParams& p, int row, i
     } else {
       for (int j = 0; j < 32; ++j)
         if (col0 + j < p.N) dst[j] = int(v[j]);
+    }
+    return;
+  }
+  if (p.epi == EPI_DEQUANT_SCALED) {
+    const int c = col0 + lane;
+    const float pc_mine = c < p.N ? h2f(p.scale_f16[c]) : 0.f;
+    const float b_mine = (p.bias && c < p.N) ? h2f(p.bias[c]) : 0.f;
+    const float act = h2f(*p.act_scale);
+    uint32_t h2[16];
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      uint32_t w = 0;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const float pc = __shfl_sync(0xffffffffu, pc_mine, j + t);
+        const float bb = __shfl_sync(0xffffffffu, b_mine, j + t);
+        float y = __fmul_rn(__fmul_rn(__int2float_rn(int(v[j + t])), pc), act);
+        if (p.bias) y = __fadd_rn(y, bb);
+        w |= uint32_t(f2h(y)) << (16 * t);
+      }
+      h2[j / 2] = w;
+    }
+    if (!row_ok) return;
+    uint16_t* dst = static_cast<uint16_t*>(p.out) + uint64_t(row) * p.N + col0;
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        reinterpret_cast<uint4*>(dst)[q] = make_uint4(h2[4 * q], h2[4 * q + 1], h2[4 * q + 2], h2[4 * q + 3]);
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) dst[j] = uint16_t(h2[j / 2] >> (16 * (j % 2)));
     }
     return;
   }
