@@ -334,6 +334,23 @@ class Compiler {
     return m[0];
   }
 
+  // A [first half | second half] vector operand (2 x half_bytes): when the
+  // halves are each contiguous but not adjacent (two LOADs from different
+  // places), the op reads them through b and c (F_SPLIT) instead of a gather.
+  void src_pair(uint32_t u0, uint64_t half_bytes, Access& acc, DevOp& op) {
+    const uint64_t h = half_bytes / kUnit;
+    uint64_t* m = &sram_[u0];
+    if (half_bytes % kUnit == 0 && h > 0 && !contiguous(m, 2 * h) && contiguous(m, h) && contiguous(m + h, h)) {
+      acc.reads.push_back({m[0], h});
+      acc.reads.push_back({m[h], h});
+      op.b = m[0];
+      op.c = m[h];
+      op.flags |= F_SPLIT;
+      return;
+    }
+    op.b = src(u0, 2 * half_bytes, acc);
+  }
+
   // Fresh destination extent for logical SRAM units [u0, u0+n).
   uint64_t dst(uint32_t u0, uint64_t nbytes, Access& acc) {
     uint64_t n = (nbytes + kUnit - 1) / kUnit;
@@ -834,7 +851,8 @@ int Compiler::h_rtype(const Insn& x) {
         read_sreg(acc, op.s[0]);
       }
       op.a = src(s1, M * N * 4, acc);
-      op.b = src(s2, vec, acc);
+      if (o == OP_DEQUANT_ACCUM_FP32_SCALED) src_pair(s2, N * 2, acc, op);
+      else op.b = src(s2, vec, acc);
       op.d = dst(d, M * N * 2, acc);
       cycles_ += M * N;
       break;
@@ -862,7 +880,8 @@ int Compiler::h_rtype(const Insn& x) {
       TRY(span(x.dst_buf, x.dst_off, M * N * 2));
       op.kind = o == OP_VADD_FP32 ? K_VADD_F16 : K_LAYERNORM_F16;
       op.a = src(s1, M * N * 2, acc);
-      op.b = src(s2, b_bytes, acc);
+      if (o == OP_LAYERNORM_FP32) src_pair(s2, N * 2, acc, op);
+      else op.b = src(s2, b_bytes, acc);
       op.d = dst(d, M * N * 2, acc);
       cycles_ += M * N;
       break;
@@ -1173,14 +1192,15 @@ void Compiler::build_tasks() {
       case K_TRANSPOSE:
         per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + 16383) / 16384)));
         break;
-      default: {  // element-wise ops: kEwTaskElems elements per task
-        if (B > 1 && MN > 0 && MN * 2 <= kEwTaskElems) {
+      default: {  // element-wise ops: ew_task_elems(kind) elements per task
+        const uint64_t te = ew_task_elems(op.kind);
+        if (B > 1 && MN > 0 && MN * 2 <= te) {
           // small ops: one task takes several whole sequences
-          const uint32_t spt = static_cast<uint32_t>(kEwTaskElems / MN);
+          const uint32_t spt = static_cast<uint32_t>(te / MN);
           for (uint32_t s = 0; s < B; s += spt)
             per_level[op.level].push_back(Task{i, s, std::min(spt, B - s), 0, 0});
         } else {
-          per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + kEwTaskElems - 1) / kEwTaskElems)));
+          per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + te - 1) / te)));
         }
         break;
       }

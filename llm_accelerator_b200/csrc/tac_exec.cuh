@@ -566,8 +566,11 @@ template <int KIND>
 __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const Task& t) {
   const uint32_t N = op.N;
   const uint32_t MN = op.M * N;
+  constexpr uint32_t kTask = ew_task_elems(KIND);
+  constexpr uint32_t kGroups = kTask / (kThreads * 8);   // groups of 8 per thread
+  static_assert(kGroups >= 1 && kGroups <= kEwGroups, "element-wise task size");
   const bool packed = t.nseq > 1;
-  const uint32_t base = packed ? 0u : t.tile * kEwTask;
+  const uint32_t base = packed ? 0u : t.tile * kTask;
   const uint32_t span = packed ? t.nseq * MN : MN;
   const uint8_t* __restrict__ a0 = pptr(A, op.a, t.seq0);
   const uint8_t* __restrict__ b0 = pptr(A, op.b, t.seq0);
@@ -582,7 +585,7 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
   uint32_t e0[kEwGroups], sq[kEwGroups];
   float s0v[kEwGroups], s1v[kEwGroups];
 #pragma unroll
-  for (uint32_t g = 0; g < kEwGroups; ++g) {
+  for (uint32_t g = 0; g < kGroups; ++g) {
     const uint32_t e = base + (g * kThreads + htid()) * 8;
     sq[g] = packed ? e / MN : 0u;
     e0[g] = e - sq[g] * MN;
@@ -604,7 +607,7 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
     } else if constexpr (KIND == K_DEQUANT_SCALED) {
       ia[g] = ld32(a + e0[g] * 4);
       rb[g] = ld16(b + uint64_t(col) * 2);
-      rc[g] = ld16(b + uint64_t(N + col) * 2);
+      rc[g] = (op.flags & F_SPLIT) ? ld16(pptr(A, op.c, seq) + uint64_t(col) * 2) : ld16(b + uint64_t(N + col) * 2);
     } else if constexpr (KIND == K_DEQUANT_ACCUM || KIND == K_REQUANT_PC) {
       ia[g] = ld32(a + e0[g] * 4);
       rb[g] = ld16(b + uint64_t(col) * 2);
@@ -630,7 +633,7 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
   }
   // phase 2: compute and store
 #pragma unroll
-  for (uint32_t g = 0; g < kEwGroups; ++g) {
+  for (uint32_t g = 0; g < kGroups; ++g) {
     if (e0[g] >= MN) continue;
     uint8_t* __restrict__ d = d0 + sq[g] * sd;
     const float s0 = s0v[g], s1 = s1v[g];
@@ -876,13 +879,17 @@ __device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const T
 
   if (op.kind == K_LAYERNORM_F16 || op.kind == K_LN_I8) {
     const float eps = op.kind == K_LN_I8 ? 1e-6f : 1e-5f;
-    const float sum = warp_pairwise_sum([&](uint32_t j) { return x_at(j); }, N, pw);
+    const float sum = buffered ? warp_pairwise_sum_smem(rowbuf, N, pw)
+                               : warp_pairwise_sum([&](uint32_t j) { return x_at(j); }, N, pw);
     const float mean = div_count(sum, N);
-    const float sq = warp_pairwise_sum(
-        [&](uint32_t j) { const float dd = __fsub_rn(x_at(j), mean); return __fmul_rn(dd, dd); }, N, pw);
+    const float sq =
+        buffered ? warp_pairwise_sum_smem(rowbuf, N, pw, true, mean)
+                 : warp_pairwise_sum(
+                       [&](uint32_t j) { const float dd = __fsub_rn(x_at(j), mean); return __fmul_rn(dd, dd); }, N, pw);
     const float var = div_count(sq, N);
     const float denom = __fsqrt_rn(__fadd_rn(var, eps));
     const uint8_t* gb = pptr(A, op.b, seq);
+    const uint8_t* be = (op.flags & F_SPLIT) ? pptr(A, op.c, seq) : gb + uint64_t(N) * 2;   // beta
     if (op.kind == K_LAYERNORM_F16 && buffered) {
       const uint32_t ng = N / 8;
       for (uint32_t half = 0; half < kRowCap / 256; half += 4) {
@@ -892,7 +899,7 @@ __device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const T
         const uint32_t g = lane + 32 * (half + k);
         if (g < ng) {
           gv[k] = __ldcg(reinterpret_cast<const uint4*>(gb) + g);
-          bv[k] = __ldcg(reinterpret_cast<const uint4*>(gb + uint64_t(N) * 2) + g);
+          bv[k] = __ldcg(reinterpret_cast<const uint4*>(be) + g);
         }
       }
 #pragma unroll
@@ -913,7 +920,7 @@ __device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const T
     for (uint32_t j = lane; j < N; j += 32) {
       const float y = __fdiv_rn(__fsub_rn(x_at(j), mean), denom);
       const float g = h2f(reinterpret_cast<const uint16_t*>(gb)[j]);
-      const float b = h2f(reinterpret_cast<const uint16_t*>(gb)[N + j]);
+      const float b = h2f(reinterpret_cast<const uint16_t*>(be)[j]);
       const float o = __fadd_rn(__fmul_rn(y, g), b);
       if (op.kind == K_LAYERNORM_F16) reinterpret_cast<uint16_t*>(d)[base + j] = f2h(o);
       else reinterpret_cast<int8_t*>(d)[base + j] = out_scale == 0.f ? int8_t(0) : sat8(__fdiv_rn(o, out_scale));
@@ -957,7 +964,7 @@ __device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const T
     __syncwarp();
   }
   auto ev = [&](uint32_t j) -> float { return buffered ? rowbuf[j] : e_at(j); };
-  const float denom = warp_pairwise_sum(ev, N, pw);
+  const float denom = buffered ? warp_pairwise_sum_smem(rowbuf, N, pw) : warp_pairwise_sum(ev, N, pw);
   if (masked_i8 && denom == 0.f) {
     if (lane == 0) raise_fault(A, DF_ZERO_DENOM, 0, seq);
   }

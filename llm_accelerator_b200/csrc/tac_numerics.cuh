@@ -158,6 +158,51 @@ __device__ inline bool pw_balanced(uint32_t n, uint32_t& nl, uint32_t& L) {
   return L >= 8 && L % 8 == 0 && nl <= 8;
 }
 
+// np.sum of x[0..n) held in shared memory (every lane returns it), or of
+// (x[i] - mean)^2 when sq is set.  Balanced trees take the butterfly of
+// warp_pairwise_sum without a gather callback; others fall back to it.
+template <class Get>
+__device__ inline float warp_pairwise_sum(const Get& get, uint32_t n, uint32_t* scratch);
+
+__device__ __forceinline__ float warp_pairwise_sum_smem(const float* x, uint32_t n, uint32_t* scratch,
+                                                        bool sq = false, float mean = 0.f) {
+  uint32_t bnl, bL;
+  if (pw_balanced(n, bnl, bL)) {
+    const uint32_t lane = threadIdx.x & 31, leaf = lane >> 2, p = lane & 3;
+    float v = 0.f;
+    if (leaf < bnl) {
+      const float* q = x + leaf * bL + 2 * p;
+      float r0, r1;
+      if (sq) {
+        const float d0 = __fsub_rn(q[0], mean), d1 = __fsub_rn(q[1], mean);
+        r0 = __fmul_rn(d0, d0);
+        r1 = __fmul_rn(d1, d1);
+        for (uint32_t i = 8; i < bL; i += 8) {
+          const float e0 = __fsub_rn(q[i], mean), e1 = __fsub_rn(q[i + 1], mean);
+          r0 = __fadd_rn(r0, __fmul_rn(e0, e0));
+          r1 = __fadd_rn(r1, __fmul_rn(e1, e1));
+        }
+      } else {
+        r0 = q[0];
+        r1 = q[1];
+        for (uint32_t i = 8; i < bL; i += 8) {
+          r0 = __fadd_rn(r0, q[i]);
+          r1 = __fadd_rn(r1, q[i + 1]);
+        }
+      }
+      v = __fadd_rn(r0, r1);
+    }
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    for (uint32_t s = 4; s < 4 * bnl; s <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, s));
+    return __fadd_rn(0.0f, __shfl_sync(0xffffffffu, v, 0));
+  }
+  if (sq)
+    return warp_pairwise_sum([&](uint32_t j) { const float d = __fsub_rn(x[j], mean); return __fmul_rn(d, d); }, n,
+                             scratch);
+  return warp_pairwise_sum([&](uint32_t j) { return x[j]; }, n, scratch);
+}
+
 template <class Get>
 __device__ inline float warp_pairwise_sum(const Get& get, uint32_t n, uint32_t* scratch) {
   const int lane = threadIdx.x & 31;

@@ -67,6 +67,8 @@ constexpr uint16_t F_ACCUMULATE = 1;   // MATMUL adds the previous int32 tile (o
 constexpr uint16_t F_SRC_I32 = 2;      // legacy SFU input is int32 (ACCUM) rather than int8
 constexpr uint16_t F_ATTN_DYN = 4;     // masked softmax context comes from a runtime parameter
 constexpr uint16_t F_TC = 8;           // MATMUL with shared weights on tcgen05, TMA maps pair seg0
+constexpr uint16_t F_SPLIT = 16;       // DEQUANT_SCALED / LAYERNORM: second half of the [scale|bias]
+                                       // ([gamma|beta]) vector at operand c instead of b + N
 
 struct DevOp {
   uint16_t kind;
@@ -105,6 +107,19 @@ constexpr uint64_t kGatherChunkUnits = 4096;
 
 // Elements of one sequence an element-wise task covers (256 threads x 4 groups of 8).
 constexpr uint64_t kEwTaskElems = 8192;
+
+#ifdef __CUDACC__
+#define TAC_HD __host__ __device__
+#else
+#define TAC_HD
+#endif
+
+// Element-wise task size by op kind: GELU (float64 tanh per element) takes
+// 2048-element tasks (one group of 8 per thread) so its work spreads over
+// more SMs; the rest take kEwTaskElems.
+TAC_HD constexpr uint32_t ew_task_elems(uint32_t kind) {
+  return (kind == K_GELU_F16 || kind == K_GELU_I8) ? 2048u : uint32_t(kEwTaskElems);
+}
 
 // Parameters decoded from runtime-patched instruction words, one set per
 // sequence.  Address parameters hold the 56-bit register value; attention

@@ -136,7 +136,10 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None):
             m.sregs[int(op["out_slot"]) + 1] = np.array([fwd], np.float16).view(np.uint16)[0]
         elif k in (K["DEQUANT_SCALED"], K["DEQUANT_ACCUM"]):
             acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
-            vec = _f16(m, b, 2 * N if k == K["DEQUANT_SCALED"] else N)
+            if op["flags"] & 16:   # F_SPLIT: second half of the vector at c
+                vec = np.concatenate([_f16(m, b, N), _f16(m, c, N)])
+            else:
+                vec = _f16(m, b, 2 * N if k == K["DEQUANT_SCALED"] else N)
             if k == K["DEQUANT_SCALED"]:
                 r = acc * vec[:N].reshape(1, N) * np.float32(m.sreg(s[0])) + vec[N:].reshape(1, N)
             else:
@@ -147,7 +150,7 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None):
             m.mem(d, M * N * 2)[:] = r.astype(np.float16).view(np.uint8)
         elif k == K["LAYERNORM_F16"]:
             x = _f16(m, a, M * N).reshape(M, N)
-            gb = _f16(m, b, 2 * N)
+            gb = np.concatenate([_f16(m, b, N), _f16(m, c, N)]) if op["flags"] & 16 else _f16(m, b, 2 * N)
             mean = x.mean(axis=-1, keepdims=True).astype(np.float32)
             var = x.var(axis=-1, keepdims=True).astype(np.float32)
             y = (x - mean) / np.sqrt(var + np.float32(1e-5))

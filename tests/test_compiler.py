@@ -200,6 +200,7 @@ def test_tasks_cover_every_sequence_and_element_once(batch):
     ops, segs, tasks, lv = p.dump()
     EW_TASK = 8192
     ew_kinds = set(range(7, 18)) | {19, 27}
+    task_elems = lambda kind: 2048 if kind in (19, 27) else EW_TASK  # noqa: E731
     seen = {}
     for t in tasks:
         op = ops[t["op"]]
@@ -209,12 +210,13 @@ def test_tasks_cover_every_sequence_and_element_once(batch):
         cov = seen.setdefault(int(t["op"]), np.zeros((batch, MN), np.int32))
         s0, n = int(t["seq0"]), int(t["nseq"])
         assert s0 + n <= batch
+        te = task_elems(int(op["kind"]))
         if n > 1:
-            assert n * MN <= EW_TASK and int(t["tile"]) == 0
+            assert n * MN <= te and int(t["tile"]) == 0
             cov[s0:s0 + n] += 1
         else:
-            lo = int(t["tile"]) * EW_TASK
-            cov[s0, lo:lo + EW_TASK] += 1
+            lo = int(t["tile"]) * te
+            cov[s0, lo:lo + te] += 1
     assert seen, "no element-wise ops in the plan"
     for opi, cov in seen.items():
         assert (cov == 1).all(), f"op {opi}: coverage {np.unique(cov)}"
