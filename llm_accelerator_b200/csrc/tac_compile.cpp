@@ -14,6 +14,7 @@
 // (tac_exec.cu) runs.  See tac_plan.h for the physical layout.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <unordered_map>
@@ -44,6 +45,22 @@ struct Access {
   std::vector<uint32_t> slot_writes;
   bool sreg_home_read = false;
   bool sreg_home_write = false;
+  // a runtime-addressed DRAM access (the single writable-DRAM entry of reads,
+  // or of writes when dyn_write): its parameter and its byte range relative
+  // to the parameter's value
+  int dyn_param = -1;
+  bool dyn_write = false;
+  int64_t dyn_c0 = 0, dyn_c1 = 0;
+};
+
+// A runtime-addressed store: kept out of the per-unit write levels so that two
+// stores whose parameters hold one value and whose offsets do not overlap
+// (the per-head KV-cache appends of a layer) stay unordered.
+struct DynWrite {
+  int param;
+  int64_t c0, c1;       // bytes written, relative to the parameter's value
+  uint64_t i0, i1;      // every writable-DRAM unit it may write
+  int32_t level;
 };
 
 class Compiler {
@@ -70,7 +87,13 @@ class Compiler {
       attn_mode_ = init->attn_mode;
     }
     for (int r = 0; r < 16; ++r) sreg_[r] = sregs_reset ? (kSregConst | 0u) : uint32_t(r);
+    if (const char* path = std::getenv("TAC_LEVEL_TRACE")) trace_ = std::fopen(path, "a");
   }
+  ~Compiler() {
+    if (trace_) std::fclose(trace_);
+  }
+  Compiler(const Compiler&) = delete;
+  Compiler& operator=(const Compiler&) = delete;
 
   int compile();
 
@@ -125,16 +148,48 @@ class Compiler {
   }
 
   // ---- dependency levels ---------------------------------------------------------
+  // Latest level of a runtime-addressed store that may touch writable-DRAM
+  // units [i0, i1).  For a runtime-addressed access (param >= 0, bytes
+  // [c0, c1) relative to the parameter's value), a store whose parameter is in
+  // the same site group and whose relative bytes are disjoint cannot touch the
+  // same bytes: it is skipped, and the equality of the two parameters becomes
+  // a run-time check.
+  int32_t dyn_level(uint64_t i0, uint64_t i1, int param, int64_t c0, int64_t c1) {
+    int32_t L = 0;
+    for (const DynWrite& d : dyn_w_) {
+      if (d.i1 <= i0 || d.i0 >= i1 || d.level <= L) continue;
+      if (param >= 0 && site_group_[d.param] == site_group_[param] && (d.c1 <= c0 || c1 <= d.c0)) {
+        pending_same_.push_back(d.param);
+        pending_same_.push_back(param);
+        continue;
+      }
+      L = d.level;
+    }
+    return L;
+  }
+
   int32_t level_for(const Access& a) {
     int32_t L = 0;
+    why_ = "none";
+    auto bump = [&](int32_t v, const char* tag) {
+      if (v > L) {
+        L = v;
+        why_ = tag;
+      }
+    };
     for (auto& r : a.reads) {
       uint64_t p = r.first;
       switch (cls(p)) {
         case PC_ARENA:
-          for (uint64_t i = 0; i < r.second; ++i) L = std::max(L, arena_lvl_[p - arena_base_ + i]);
+          for (uint64_t i = 0; i < r.second; ++i) bump(arena_lvl_[p - arena_base_ + i], "arena-raw");
           break;
         case PC_HOME_RW:
-          for (uint64_t i = 0; i < r.second; ++i) L = std::max(L, rw_wl_[p - rw_base_ + i]);
+          for (uint64_t i = 0; i < r.second; ++i) bump(rw_wl_[p - rw_base_ + i], "home-raw");
+          if (!dyn_w_.empty()) {
+            const bool dyn = a.dyn_param >= 0 && !a.dyn_write;
+            bump(dyn_level(p - rw_base_, p - rw_base_ + r.second, dyn ? a.dyn_param : -1, a.dyn_c0, a.dyn_c1),
+                 "home-dyn-raw");
+          }
           break;
         default:
           break;  // shared: never written; SRAM home: written only by the final materialise
@@ -145,19 +200,24 @@ class Compiler {
       switch (cls(p)) {
         case PC_HOME_RW:
           for (uint64_t i = 0; i < w.second; ++i) {
-            L = std::max(L, rw_wl_[p - rw_base_ + i]);
-            L = std::max(L, rw_rl_[p - rw_base_ + i]);
+            bump(rw_wl_[p - rw_base_ + i], "home-waw");
+            bump(rw_rl_[p - rw_base_ + i], "home-war");
+          }
+          if (!dyn_w_.empty()) {
+            const bool dyn = a.dyn_param >= 0 && a.dyn_write;
+            bump(dyn_level(p - rw_base_, p - rw_base_ + w.second, dyn ? a.dyn_param : -1, a.dyn_c0, a.dyn_c1),
+                 "home-dyn-waw");
           }
           break;
         case PC_HOME_SRAM:
-          for (uint64_t i = 0; i < w.second; ++i) L = std::max(L, home_rl_[p + i]);
+          for (uint64_t i = 0; i < w.second; ++i) bump(home_rl_[p + i], "sram-war");
           break;
         default:
           break;  // arena extents are fresh
       }
     }
-    for (uint32_t s : a.slot_reads) L = std::max(L, slot_lvl_[s]);
-    if (a.sreg_home_write) L = std::max(L, sreg_home_rl_);
+    for (uint32_t s : a.slot_reads) bump(slot_lvl_[s], "slot-raw");
+    if (a.sreg_home_write) bump(sreg_home_rl_, "sreg-war");
     return L + 1;
   }
 
@@ -182,7 +242,11 @@ class Compiler {
       if (c == PC_ARENA) {
         for (uint64_t i = 0; i < w.second; ++i) arena_lvl_[p - arena_base_ + i] = L;
       } else if (c == PC_HOME_RW) {
-        for (uint64_t i = 0; i < w.second; ++i) rw_wl_[p - rw_base_ + i] = L;
+        if (a.dyn_param >= 0 && a.dyn_write) {
+          dyn_w_.push_back(DynWrite{a.dyn_param, a.dyn_c0, a.dyn_c1, p - rw_base_, p - rw_base_ + w.second, L});
+        } else {
+          for (uint64_t i = 0; i < w.second; ++i) rw_wl_[p - rw_base_ + i] = L;
+        }
       }
     }
     for (uint32_t s : a.slot_writes) slot_lvl_[s] = L;
@@ -193,10 +257,37 @@ class Compiler {
   }
 
   uint32_t emit(DevOp op, const Access& a) {
+    pending_same_.clear();
     int32_t L = level_for(a);
     commit(a, L);
+    for (int prm : pending_same_) {   // equalities the level relied on
+      const int g = site_group_[prm];
+      if (prm == g || same_checked_[prm]) continue;
+      same_checked_[prm] = 1;
+      RtCheck c{};
+      c.kind = CHK_SAME;
+      c.param = static_cast<uint32_t>(prm);
+      c.pc = pc_;
+      c.lo = static_cast<uint64_t>(g);
+      P->checks.push_back(c);
+    }
     op.level = static_cast<uint32_t>(L);
     op.pc = static_cast<uint32_t>(pc_);
+    if (trace_) {
+      std::fprintf(trace_, "%llu %u %d %s", static_cast<unsigned long long>(pc_), op.kind, L, why_);
+      for (auto& r : a.reads)
+        if (cls(r.first) == PC_HOME_RW)
+          std::fprintf(trace_, " r:%llu+%llu", static_cast<unsigned long long>(r.first - rw_base_),
+                       static_cast<unsigned long long>(r.second));
+      for (auto& w : a.writes)
+        if (cls(w.first) == PC_HOME_RW)
+          std::fprintf(trace_, " w:%llu+%llu", static_cast<unsigned long long>(w.first - rw_base_),
+                       static_cast<unsigned long long>(w.second));
+      if (op.kind == K_DYN_STORE || op.kind == K_DYN_LOAD)
+        std::fprintf(trace_, " p:%d c:%lld n:%llu", op.param, static_cast<long long>(op.dconst),
+                     static_cast<unsigned long long>(op.nbytes));
+      std::fputc('\n', trace_);
+    }
     P->ops.push_back(op);
     return static_cast<uint32_t>(P->ops.size() - 1);
   }
@@ -294,10 +385,14 @@ class Compiler {
       k.out_slot = 0;
       k.pc = 0;
       k.level = 0;
+      if (op.flags & F_SEGA) k.seg0 = 0;   // a segment list is keyed by its contents
       key.assign(reinterpret_cast<const char*>(&k), sizeof(k));
+      if (op.flags & F_SEGA)
+        key.append(reinterpret_cast<const char*>(&P->segs[op.seg0]), op.nseg * sizeof(Segment));
       auto it = cse_.find(key);
       if (it != cse_.end()) {
         const DevOp& prev = P->ops[it->second];
+        if ((op.flags & F_SEGA) && op.seg0 + op.nseg == P->segs.size()) P->segs.resize(op.seg0);
         if (op.kind == K_MAX_ABS) {
           sreg_[sreg_idx] = prev.out_slot;
           sreg_[sreg_idx + 1] = prev.out_slot + 1;
@@ -349,6 +444,39 @@ class Compiler {
       return;
     }
     op.b = src(u0, 2 * half_bytes, acc);
+  }
+
+  // Operand a of a MAX_ABS / QUANT / VADD_F16 read straight from scattered
+  // units through a segment list (F_SEGA) rather than gathered first: the
+  // gather would be a dependency level of its own.  Returns false (nothing
+  // emitted) when the units are contiguous or form too many runs.
+  bool src_segments(uint32_t u0, uint64_t nbytes, Access& acc, DevOp& op) {
+    const uint64_t n = (nbytes + kUnit - 1) / kUnit;
+    const uint64_t* m = &sram_[u0];
+    if (n < 2 || contiguous(m, n)) return false;
+    std::vector<std::pair<uint64_t, uint64_t>> runs;   // (first unit, length)
+    for (uint64_t i = 0; i < n;) {
+      uint64_t j = i + 1;
+      while (j < n && m[j] == m[i] + (j - i) && cls(m[j]) == cls(m[i])) ++j;
+      runs.push_back({i, j - i});
+      i = j;
+    }
+    if (runs.size() > kMaxSegRuns) return false;
+    op.seg0 = static_cast<uint32_t>(P->segs.size());
+    for (auto& r : runs) {
+      push_seg(m[r.first], r.first, r.second);
+      acc.reads.push_back({m[r.first], r.second});
+    }
+    op.nseg = static_cast<uint32_t>(P->segs.size() - op.seg0);
+    if (op.nseg > kMaxSegRuns) {   // long runs were split: fall back to a gather
+      P->segs.resize(op.seg0);
+      acc.reads.resize(acc.reads.size() - runs.size());
+      op.seg0 = op.nseg = 0;
+      return false;
+    }
+    op.a = 0;
+    op.flags |= F_SEGA;
+    return true;
   }
 
   // Fresh destination extent for logical SRAM units [u0, u0+n).
@@ -434,6 +562,12 @@ class Compiler {
   uint64_t rw_base_ = 0, arena_base_ = 0, arena_top_ = 0;
   std::vector<uint64_t> sram_, shadow_;
   std::vector<int32_t> arena_lvl_, rw_wl_, rw_rl_, home_rl_, slot_lvl_;
+  std::vector<DynWrite> dyn_w_;
+  // site i's group: the first address site with the same value range; sites of
+  // one group are assumed (and checked at run time) to carry one value
+  std::vector<int> site_group_;
+  std::vector<int> pending_same_;          // parameters a disambiguation relied on
+  std::vector<uint8_t> same_checked_;      // per parameter: CHK_SAME emitted
   int32_t sreg_home_rl_ = 0;
   uint32_t sreg_[16];
   uint32_t n_slots_ = 0;
@@ -444,6 +578,10 @@ class Compiler {
   uint32_t attn_qrb_ = 0, attn_vkl_ = 0, attn_mode_ = 0;
   int attn_param_ = -1;
   uint64_t pc_ = 0, word_ = 0;
+  // TAC_LEVEL_TRACE=<file>: one line per emitted op, "pc kind level cause", the
+  // cause naming the access class that set the level (a diagnostic of the plan).
+  FILE* trace_ = nullptr;
+  const char* why_ = "none";
   uint64_t insn_region_bytes_ = 0;
   uint64_t cycles_ = 0;
   bool halted_ = false;
@@ -541,6 +679,9 @@ int Compiler::h_load(const Insn& x) {                       // dma.py:27-44
     uint64_t i1 = std::min<uint64_t>(rw_units_, (hi + n - shared_bytes_ + kUnit - 1) / kUnit);
     flush_rw(i0, i1);
     acc.reads.push_back({rw_home(i0), i1 - i0});
+    acc.dyn_param = param;
+    acc.dyn_c0 = int64_t(x.dram_off) * kUnit;
+    acc.dyn_c1 = acc.dyn_c0 + int64_t(n);
   }
   DevOp op = blank(K_DYN_LOAD);
   op.param = param;
@@ -582,6 +723,10 @@ int Compiler::h_store(const Insn& x) {                      // dma.py:47-64
   op.dconst = int64_t(x.dram_off) * kUnit;
   op.nbytes = n;
   acc.writes.push_back({rw_home(i0), i1 - i0});
+  acc.dyn_param = param;
+  acc.dyn_write = true;
+  acc.dyn_c0 = op.dconst;
+  acc.dyn_c1 = op.dconst + int64_t(n);
   emit(op, acc);
   return 0;
 }
@@ -865,7 +1010,7 @@ int Compiler::h_rtype(const Insn& x) {
       op.kind = K_QUANT;
       op.s[0] = sreg_[x.sreg];
       read_sreg(acc, op.s[0]);
-      op.a = src(s1, M * N * 2, acc);
+      if (!src_segments(s1, M * N * 2, acc, op)) op.a = src(s1, M * N * 2, acc);
       op.d = dst(d, M * N, acc);
       cycles_ += M * N;
       break;
@@ -879,9 +1024,17 @@ int Compiler::h_rtype(const Insn& x) {
       TRY(span(x.src2_buf, x.src2_off, b_bytes));
       TRY(span(x.dst_buf, x.dst_off, M * N * 2));
       op.kind = o == OP_VADD_FP32 ? K_VADD_F16 : K_LAYERNORM_F16;
-      op.a = src(s1, M * N * 2, acc);
-      if (o == OP_LAYERNORM_FP32) src_pair(s2, N * 2, acc, op);
-      else op.b = src(s2, b_bytes, acc);
+      if (o == OP_LAYERNORM_FP32) {
+        op.a = src(s1, M * N * 2, acc);
+        src_pair(s2, N * 2, acc, op);
+      } else if (src_segments(s1, M * N * 2, acc, op)) {
+        op.b = src(s2, b_bytes, acc);
+      } else if (src_segments(s2, b_bytes, acc, op)) {   // a + b == b + a exactly: read b as the list
+        op.b = src(s1, M * N * 2, acc);
+      } else {
+        op.a = src(s1, M * N * 2, acc);
+        op.b = src(s2, b_bytes, acc);
+      }
       op.d = dst(d, M * N * 2, acc);
       cycles_ += M * N;
       break;
@@ -905,7 +1058,7 @@ int Compiler::h_rtype(const Insn& x) {
       if (x.sreg >= 15) return config_fault("MAX_ABS_REDUCE_FP32 sreg+1 out of range (must be 0..14)");
       TRY(span(x.src1_buf, x.src1_off, M * N * 2));
       op.kind = K_MAX_ABS;
-      op.a = src(s1, M * N * 2, acc);
+      if (!src_segments(s1, M * N * 2, acc, op)) op.a = src(s1, M * N * 2, acc);
       op.out_slot = new_slot();
       new_slot();
       acc.slot_writes.push_back(op.out_slot);
@@ -1193,6 +1346,10 @@ void Compiler::build_tasks() {
         per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + 16383) / 16384)));
         break;
       default: {  // element-wise ops: ew_task_elems(kind) elements per task
+        if (op.flags & F_SEGA) {   // segment-list operand: one task per sequence
+          per_seq(i, 1);
+          break;
+        }
         const uint64_t te = ew_task_elems(op.kind);
         if (B > 1 && MN > 0 && MN * 2 <= te) {
           // small ops: one task takes several whole sequences
@@ -1256,6 +1413,17 @@ int Compiler::compile() {
   }
   P->n_var_words = w;
   P->n_params = static_cast<uint32_t>(n_sites_);
+  site_group_.resize(n_sites_);
+  same_checked_.assign(n_sites_, 0);
+  for (int i = 0; i < n_sites_; ++i) {
+    site_group_[i] = i;
+    if (sites_[i].kind != 0) continue;
+    for (int j = 0; j < i; ++j)
+      if (sites_[j].kind == 0 && sites_[j].range_lo == sites_[i].range_lo && sites_[j].range_hi == sites_[i].range_hi) {
+        site_group_[i] = j;
+        break;
+      }
+  }
 
   uint64_t count = 0;
   pc_ = entry_;

@@ -192,6 +192,8 @@ int decode_params(const tac_program* p, const uint64_t* words, uint64_t* params,
       const uint64_t a = v + static_cast<uint64_t>(c.dconst);
       ok = (a % 16 == 0 || c.nbytes == 0) && a >= c.lo && a < std::max(c.hi, c.lo + 1) &&
            a + c.nbytes <= p->dram_bytes;
+    } else if (c.kind == CHK_SAME) {
+      ok = c.lo < p->vars.size() && v == params[c.lo];
     } else {
       const uint32_t vkl = (v >> 16) & 0xFFFF, mode = (v >> 32) & 3;
       if (c.kind == CHK_ATTN_SET) ok = mode != 0 && vkl != 0;

@@ -752,6 +752,78 @@ __device__ __noinline__ void op_elementwise(const ExecArgs& A, const DevOp& op, 
 // ---------------------------------------------------------------------------------
 // MAX_ABS_REDUCE_FP32 (simulator.py:1088-1140): one task per sequence.
 // ---------------------------------------------------------------------------------
+// Operands read through a segment list (F_SEGA): the op's segments give, in
+// order, runs of physically contiguous 16-byte units; Segment.dst is the run's
+// offset in the operand.  The table is staged in shared memory past the first
+// kSegTableOff bytes and each unit found by binary search, so every thread
+// keeps four 16-byte loads in flight however the runs are sized.
+constexpr uint32_t kSegTableOff = 4096;
+
+__device__ __forceinline__ void seg_stage(const ExecArgs& A, const DevOp& op, uint8_t* smem) {
+  uint32_t* ofs = reinterpret_cast<uint32_t*>(smem + kSegTableOff);
+  uint64_t* src = reinterpret_cast<uint64_t*>(smem + kSegTableOff + kMaxSegRuns * 4);
+  for (uint32_t k = htid(); k < op.nseg; k += kThreads) {
+    const Segment sg = A.segs[op.seg0 + k];
+    ofs[k] = static_cast<uint32_t>(sg.dst);
+    src[k] = sg.src;
+  }
+  hsync();
+}
+
+// Address of operand unit u (segments staged by seg_stage).
+__device__ __forceinline__ const uint4* seg_unit(const ExecArgs& A, const DevOp& op, const uint8_t* smem,
+                                                 uint32_t seq, uint32_t u) {
+  const uint32_t* ofs = reinterpret_cast<const uint32_t*>(smem + kSegTableOff);
+  const uint64_t* src = reinterpret_cast<const uint64_t*>(smem + kSegTableOff + kMaxSegRuns * 4);
+  uint32_t lo = 0, hi = op.nseg;   // last k with ofs[k] <= u
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (ofs[mid] <= u) lo = mid;
+    else hi = mid;
+  }
+  return reinterpret_cast<const uint4*>(pptr(A, src[lo], seq)) + (u - ofs[lo]);
+}
+
+// QUANT / VADD_F16 with a segment-list first operand; one sequence per task.
+__device__ __noinline__ void op_seg_ew(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+  const uint32_t seq = t.seq0;
+  const uint32_t units = op.M * op.N / 8;   // FP16 operand: 8 elements per 16-byte unit
+  seg_stage(A, op, smem);
+  const float s0 = op.kind == K_QUANT ? sreg_f32(A, op.s[0], seq) : 0.f;
+  const uint4* b = reinterpret_cast<const uint4*>(pptr(A, op.b, seq));
+  uint8_t* d = pptr(A, op.d, seq);
+  for (uint32_t u0 = htid(); u0 < units; u0 += 4 * kThreads) {
+    uint4 va[4], vb[4];
+#pragma unroll
+    for (uint32_t q = 0; q < 4; ++q) {
+      const uint32_t u = u0 + q * kThreads;
+      if (u < units) {
+        va[q] = __ldcg(seg_unit(A, op, smem, seq, u));
+        if (op.kind == K_VADD_F16) vb[q] = __ldcg(b + u);
+      }
+    }
+#pragma unroll
+    for (uint32_t q = 0; q < 4; ++q) {
+      const uint32_t u = u0 + q * kThreads;
+      if (u >= units) continue;
+      if (op.kind == K_QUANT) {
+        int8_t o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float r = rintf(__fmul_rn(h2f(h_at(va[q], j)), s0));
+          o[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+        }
+        *reinterpret_cast<uint2*>(d + uint64_t(u) * 8) = pack_b(o);
+      } else {
+        uint16_t h[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = f2h(__fadd_rn(h2f(h_at(va[q], j)), h2f(h_at(vb[q], j))));
+        *reinterpret_cast<uint4*>(d + uint64_t(u) * 16) = pack_h(h);
+      }
+    }
+  }
+}
+
 __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
   const uint32_t seq = t.seq0;
   const uint64_t MN = uint64_t(op.M) * op.N;
@@ -761,12 +833,14 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
   uint32_t m = 0;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
   const uint64_t ng = MN / 8;   // MN is a multiple of 256
+  const bool seg = op.flags & F_SEGA;
+  if (seg) seg_stage(A, op, smem);
   for (uint64_t g0 = htid(); g0 < ng; g0 += uint64_t(kThreads) * 8) {
     uint4 v[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const uint64_t g = g0 + uint64_t(k) * kThreads;
-      v[k] = g < ng ? __ldcg(xv + g) : make_uint4(0, 0, 0, 0);
+      v[k] = g < ng ? __ldcg(seg ? seg_unit(A, op, smem, seq, uint32_t(g)) : xv + g) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int k = 0; k < 8; ++k)
@@ -1115,7 +1189,8 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_REQUANT: case K_REQUANT_PC: case K_SCALE_MUL_I32: case K_SCALE_MUL_I8:
     case K_VADD_I8: case K_VADD_I32: case K_DEQUANT_ADD: case K_DEQUANT_ACCUM:
     case K_DEQUANT_SCALED: case K_QUANT: case K_VADD_F16: case K_GELU_F16: case K_GELU_I8:
-      op_elementwise(A, op, t);
+      if (op.flags & F_SEGA) op_seg_ew(A, op, t, smem);
+      else op_elementwise(A, op, t);
       break;
     default:
       if (htid() == 0) raise_fault(A, DF_BAD_OP, t.op, t.seq0);
@@ -1132,6 +1207,7 @@ constexpr size_t kExecOpSmem0 = kRowSmem > kMmSmem ? kRowSmem : kMmSmem;
 constexpr size_t kExecOpSmem = kExecOpSmem0 > kTcSmem ? kExecOpSmem0 : kTcSmem;
 constexpr size_t kExecSmem = kHalves * kExecOpSmem + kHalves * 64;
 static_assert(sizeof(TcShared) <= 64, "TcShared outgrew its slot");
+static_assert(kSegTableOff + kMaxSegRuns * 12 <= kExecOpSmem, "segment table exceeds the op shared memory");
 static_assert(kExecOpSmem % 1024 == 0 || kTcSmem <= kExecOpSmem, "half regions must keep the stage alignment slack");
 static_assert(kExecSmem <= 227 * 1024, "executor shared memory exceeds one CTA's limit");
 

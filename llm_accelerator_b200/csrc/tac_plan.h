@@ -69,6 +69,11 @@ constexpr uint16_t F_ATTN_DYN = 4;     // masked softmax context comes from a ru
 constexpr uint16_t F_TC = 8;           // MATMUL with shared weights on tcgen05, TMA maps pair seg0
 constexpr uint16_t F_SPLIT = 16;       // DEQUANT_SCALED / LAYERNORM: second half of the [scale|bias]
                                        // ([gamma|beta]) vector at operand c instead of b + N
+constexpr uint16_t F_SEGA = 32;        // MAX_ABS / QUANT / VADD_F16: operand a is the segment list
+                                       // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
+
+// Most runs an operand read through a segment list may have (longer lists are gathered).
+constexpr uint32_t kMaxSegRuns = 256;
 
 struct DevOp {
   uint16_t kind;

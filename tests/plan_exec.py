@@ -64,9 +64,24 @@ def _f16(m, p, n):
     return m.mem(p, n * 2).view(np.float16).astype(np.float32)
 
 
-def run_plan(m: PlanMachine, ops, segs, lv, params=None):
-    """Executes ops in level order (within a level in op order)."""
-    order = np.argsort(ops["level"], kind="stable")
+def _seg_read(m: PlanMachine, op, segs, nbytes: int) -> np.ndarray:
+    """Operand a of an F_SEGA op: the runs of its segment list, in order."""
+    out = np.zeros(nbytes, np.uint8)
+    for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]:
+        o, n = int(sg["dst"]) * 16, int(sg["n"]) * 16
+        out[o:o + n] = m.mem(int(sg["src"]), n)
+    return out
+
+
+def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
+    """Executes ops in level order, within a level in op order (reverse=True:
+    the opposite order; ops of one level must not depend on one another, so
+    both orders give the same state)."""
+    if reverse:
+        idx = np.arange(len(ops))
+        order = np.lexsort((-idx, ops["level"]))
+    else:
+        order = np.argsort(ops["level"], kind="stable")
     for i in order:
         op = ops[i]
         k = int(op["kind"])
@@ -127,11 +142,15 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None):
             r = (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
             m.mem(d, M * N * 2)[:] = r.astype(np.float16).view(np.uint8).ravel()
         elif k == K["QUANT"]:
-            x = _f16(m, a, M * N) * np.float32(m.sreg(s[0]))
+            xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
+                else _f16(m, a, M * N)
+            x = xa * np.float32(m.sreg(s[0]))
             v = np.round(x)
             m.mem(d, M * N)[:] = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8).view(np.uint8)
         elif k == K["MAX_ABS"]:
-            inv, fwd = G.max_abs_scales(float(np.max(np.abs(_f16(m, a, M * N)))))
+            xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
+                else _f16(m, a, M * N)
+            inv, fwd = G.max_abs_scales(float(np.max(np.abs(xa))))
             m.sregs[int(op["out_slot"])] = np.array([inv], np.float16).view(np.uint16)[0]
             m.sregs[int(op["out_slot"]) + 1] = np.array([fwd], np.float16).view(np.uint16)[0]
         elif k in (K["DEQUANT_SCALED"], K["DEQUANT_ACCUM"]):
@@ -146,7 +165,9 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None):
                 r = acc * vec[:N].reshape(1, N)
             m.mem(d, M * N * 2)[:] = r.astype(np.float32).astype(np.float16).view(np.uint8).ravel()
         elif k == K["VADD_F16"]:
-            r = _f16(m, a, M * N) + _f16(m, b, M * N)
+            xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
+                else _f16(m, a, M * N)
+            r = xa + _f16(m, b, M * N)
             m.mem(d, M * N * 2)[:] = r.astype(np.float16).view(np.uint8)
         elif k == K["LAYERNORM_F16"]:
             x = _f16(m, a, M * N).reshape(M, N)

@@ -110,10 +110,13 @@ def _params(region, sites):
     return out
 
 
+@pytest.mark.parametrize("reverse", [False, True], ids=["level-order", "level-reversed"])
 @pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
-def test_plan_reproduces_oracle_bundle_run(name):
+def test_plan_reproduces_oracle_bundle_run(name, reverse):
     """Prefill + decode steps: one plan per stream compiled with runtime sites,
-    executed with each step's parameters, equals the oracle bit-for-bit."""
+    executed with each step's parameters, equals the oracle bit-for-bit, also
+    with every level's ops run in reverse order (no hidden intra-level
+    dependency, e.g. between the KV-cache appends of one step)."""
     b = load_bundle(name)
     gold = load_run(name)
     orc = G.OracleSimulator()
@@ -149,7 +152,7 @@ def test_plan_reproduces_oracle_bundle_run(name):
         m.shared[:len(region)] = np.frombuffer(region, np.uint8)
         p, sites = plans[nm]
         ops, segs, tasks, lv = p.dump()
-        PE.run_plan(m, ops, segs, lv, _params(region, sites))
+        PE.run_plan(m, ops, segs, lv, _params(region, sites), reverse=reverse)
         n = orc.run_program(b, nm)
         assert n == int(p.info.executed)
         f = PE.final_state(m)
@@ -168,6 +171,43 @@ def test_runtime_site_out_of_range_requests_recompile():
     p = compile_program(1, 16 << 20, b.temp_base // 16 * 16, region, b.decode_pc, 10_000_000, L.Regs(), True, sites)
     assert int(p.info.n_var_words) == sum(2 if s.kind == 0 else 1 for s in sites)
     assert int(p.info.n_levels) > 0 and not p.info.faulted
+
+
+def _var_words(region, sites):
+    words = []
+    for s in sites:
+        pcs = (s.lo_pc, s.hi_pc) if s.kind == 0 else (s.lo_pc,)
+        words += [int.from_bytes(region[pc * 8:pc * 8 + 8], "big") for pc in pcs]
+    return np.array(words, np.uint64)
+
+
+def test_sites_over_one_symbol_must_carry_one_value():
+    """The KV-cache appends of a decode step go through runtime sites over one
+    symbol (kv_bank0) at different static offsets; the plan leaves them
+    unordered on the assumption that those sites hold one value, and checks
+    it: unequal values are reported (TAC_E_RECOMPILE), not executed."""
+    import ctypes as C
+    b = load_bundle("tiny_l2_d128")
+    sites = _sites(b, "decode")
+    kv = [i for i, (s, m) in enumerate(zip(sites, [x for x in b.runtime_patch_sites if x.stream == "decode"]))
+          if s.kind == 0 and m.kind == "kv_base"]
+    assert len(kv) >= 4
+    p = compile_program(1, 16 << 20, b.temp_base // 16 * 16, bytes(b.instruction_region()), b.decode_pc,
+                        10_000_000, L.Regs(), True, sites)
+    for s in b.runtime_patch_sites:
+        if s.stream == "decode":
+            b.patch_runtime_site(s, {"token_embed": 3 * b.embedding_row_bytes, "pos_embed": 2 * b.embedding_row_bytes,
+                                     "kv_base": 2 * b.kv_step_bytes}[s.kind])
+    words = _var_words(bytes(b.instruction_region()), sites)
+    out = np.zeros(len(sites), np.uint64)
+    f = L.Fault()
+    assert L.lib.tac_encode_params(p.handle, 1, words.ctypes.data, out.ctypes.data, C.byref(f)) == L.OK
+    # move one KV site by one row (still inside its range and aligned)
+    site = b.runtime_patch_sites[[x for x in b.runtime_patch_sites if x.stream == "decode"].index(
+        [x for x in b.runtime_patch_sites if x.stream == "decode"][kv[-1]])]
+    b.patch_runtime_site(site, 3 * b.kv_step_bytes)
+    words = _var_words(bytes(b.instruction_region()), sites)
+    assert L.lib.tac_encode_params(p.handle, 1, words.ctypes.data, out.ctypes.data, C.byref(f)) == L.E_RECOMPILE
 
 
 def test_self_modifying_store_is_rejected():
