@@ -198,11 +198,15 @@ int tac_argmax_f16(tac_engine* e, uint64_t addr, uint64_t count, int32_t* out_to
                    void* stream);
 
 /* Profiling (the golden model's analytic cycle_count has no wall-clock
- * counterpart, golden_model/simulator.py:208-236 trace hooks): when enabled,
- * each run records the device time at the end of every plan level;
- * tac_read_profile copies the n_levels + 1 timestamps (ns) of the last run. */
+ * counterpart, golden_model/simulator.py:208-236 trace hooks): when enabled
+ * (enable = 1), each run records the device time at the end of every plan
+ * level; tac_read_profile copies the n_levels + 1 timestamps (ns) of the last
+ * run.  enable = 2 also records each task's duration in SM cycles, read with
+ * tac_read_task_profile (entry i = task i in level order; no reference
+ * counterpart). */
 int tac_set_profiling(tac_engine* e, int enable);
 int tac_read_profile(tac_engine* e, uint64_t* out_ns, uint32_t max_entries, uint32_t* n_entries);
+int tac_read_task_profile(tac_engine* e, uint32_t* out_cycles, uint64_t max_entries, uint64_t* n_entries);
 
 /* CTAs of the persistent executor (SMs x resident CTAs per SM); no
  * reference counterpart. */

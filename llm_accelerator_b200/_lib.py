@@ -81,6 +81,7 @@ SIGNATURES = {
     "tac_argmax_f16": (_I, [_P, _U64, _U64, _P, _P]),
     "tac_set_profiling": (_I, [_P, _I]),
     "tac_read_profile": (_I, [_P, _P, C.c_uint32, _P]),
+    "tac_read_task_profile": (_I, [_P, _P, _U64, _P]),
     "tac_engine_layout": (_I, [_P, C.POINTER(_P), C.POINTER(_U64), C.POINTER(_P)]),
     "tac_engine_grid": (_I, [_P]),
     "tac_gemm_i8_requant_pc": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),

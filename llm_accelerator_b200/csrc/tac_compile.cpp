@@ -497,6 +497,7 @@ class Compiler {
     for (uint64_t i = i0; i < i1; ++i)
       if (shadow_[i] != rw_home(i)) idx.push_back(i);
     if (idx.empty()) return;
+    break_aliases(idx.front(), idx.back() + 1);
     DevOp op = blank(K_GATHER);
     op.seg0 = static_cast<uint32_t>(P->segs.size());
     Access acc;
@@ -516,6 +517,65 @@ class Compiler {
     op.nseg = static_cast<uint32_t>(P->segs.size() - op.seg0);
     emit(op, acc);
     for (uint64_t i : idx) shadow_[i] = rw_home(i);
+  }
+
+  // Writable-DRAM units that SRAM may alias in place, as disjoint intervals
+  // [first, end) of rw indices.
+  void note_alias(uint64_t i) {
+    auto it = alias_iv_.upper_bound(i);
+    if (it != alias_iv_.begin()) {
+      auto pv = std::prev(it);
+      if (pv->second >= i) {   // inside, or extends the interval ending at i
+        if (pv->second == i) {
+          pv->second = i + 1;
+          if (it != alias_iv_.end() && it->first == i + 1) {
+            pv->second = it->second;
+            alias_iv_.erase(it);
+          }
+        }
+        return;
+      }
+    }
+    if (it != alias_iv_.end() && it->first == i + 1) {
+      const uint64_t end = it->second;
+      alias_iv_.erase(it);
+      alias_iv_[i] = end;
+      return;
+    }
+    alias_iv_[i] = i + 1;
+  }
+
+  // Before writable-DRAM units [i0, i1) are written: SRAM units that still
+  // alias any of them are given a copy of the old value first (one gather,
+  // which the write then orders after as a read of those units).
+  void break_aliases(uint64_t i0, uint64_t i1) {
+    auto it = alias_iv_.upper_bound(i0);
+    if (it != alias_iv_.begin() && std::prev(it)->second > i0) --it;
+    if (it == alias_iv_.end() || it->first >= i1) return;
+    std::vector<uint32_t> us;
+    std::vector<uint64_t> src;
+    const uint64_t p0 = rw_home(i0), p1 = rw_home(i1);
+    for (uint32_t u = 0; u < kSramUnits; ++u)
+      if (sram_[u] >= p0 && sram_[u] < p1 && cls(sram_[u]) == PC_HOME_RW) {
+        us.push_back(u);
+        src.push_back(sram_[u]);
+      }
+    if (!us.empty()) {
+      std::vector<uint64_t> uniq = src;
+      std::sort(uniq.begin(), uniq.end());
+      uniq.erase(std::unique(uniq.begin(), uniq.end()), uniq.end());
+      const uint64_t g = gather(uniq.data(), uniq.size());
+      for (size_t k = 0; k < us.size(); ++k)
+        sram_[us[k]] = g + (std::lower_bound(uniq.begin(), uniq.end(), src[k]) - uniq.begin());
+    }
+    // drop [i0, i1) from the alias intervals
+    std::vector<std::pair<uint64_t, uint64_t>> keep;
+    while (it != alias_iv_.end() && it->first < i1) {
+      if (it->first < i0) keep.push_back({it->first, i0});
+      if (it->second > i1) keep.push_back({i1, it->second});
+      it = alias_iv_.erase(it);
+    }
+    for (auto& kv : keep) alias_iv_[kv.first] = kv.second;
   }
 
   // Flushes only the units of [i0, i1) that lie in the caller's live-out ranges.
@@ -563,6 +623,7 @@ class Compiler {
   std::vector<uint64_t> sram_, shadow_;
   std::vector<int32_t> arena_lvl_, rw_wl_, rw_rl_, home_rl_, slot_lvl_;
   std::vector<DynWrite> dyn_w_;
+  std::map<uint64_t, uint64_t> alias_iv_;   // see note_alias
   // site i's group: the first address site with the same value range; sites of
   // one group are assumed (and checked at run time) to carry one value
   std::vector<int> site_group_;
@@ -654,19 +715,14 @@ int Compiler::h_load(const Insn& x) {                       // dma.py:27-44
   uint32_t u0 = unit_of(x.buf_id, x.sram_off);
   uint64_t nu = n / kUnit;
   if (!dyn) {
+    // The SRAM units alias the value's physical location, no device work.  A
+    // unit that aliases writable DRAM in place is copied out only if a later
+    // write reaches that DRAM unit while the alias lives (break_aliases).
     uint64_t a0 = addr / kUnit;
-    std::vector<uint64_t> src(nu);
-    bool needs_copy = false;
     for (uint64_t i = 0; i < nu; ++i) {
-      src[i] = dram_phys(a0 + i);
-      if (cls(src[i]) == PC_HOME_RW) needs_copy = true;
+      sram_[u0 + i] = dram_phys(a0 + i);
+      if (cls(sram_[u0 + i]) == PC_HOME_RW) note_alias(sram_[u0 + i] - rw_base_);
     }
-    if (!needs_copy) {
-      for (uint64_t i = 0; i < nu; ++i) sram_[u0 + i] = src[i];  // alias, no device work
-      return 0;
-    }
-    uint64_t g = gather(src.data(), nu);
-    for (uint64_t i = 0; i < nu; ++i) sram_[u0 + i] = g + i;
     return 0;
   }
   // Runtime address: copy into a fresh extent.
@@ -716,6 +772,7 @@ int Compiler::h_store(const Insn& x) {                      // dma.py:47-64
   uint64_t i0 = (lo - shared_bytes_) / kUnit;
   uint64_t i1 = std::min<uint64_t>(rw_units_, (hi + n - shared_bytes_ + kUnit - 1) / kUnit);
   flush_rw(i0, i1);
+  break_aliases(i0, i1);
   Access acc;
   DevOp op = blank(K_DYN_STORE);
   op.a = src(u0, n, acc);

@@ -37,8 +37,11 @@ struct tac_engine {
   cudaEvent_t ring_ev[kRing] = {};
   uint64_t* d_prof = nullptr;     // per-level timestamps when profiling is on
   size_t prof_cap = 0;
-  bool profiling = false;
+  int profiling = 0;              // 0 off, 1 levels, 2 levels + task cycles
   uint32_t prof_levels = 0;
+  uint32_t* d_task_prof = nullptr;   // per-task SM cycles (profiling mode 2)
+  size_t task_prof_cap = 0;
+  uint64_t prof_tasks = 0;
   bool ring_used[kRing] = {};
   int ring_next = 0;
 };
@@ -257,6 +260,7 @@ int tac_engine_destroy(tac_engine* e) {
   cudaFree(e->d_params);
   cudaFree(e->d_status);
   cudaFree(e->d_prof);
+  cudaFree(e->d_task_prof);
   if (e->h_pinned) cudaFreeHost(e->h_pinned);
   for (int i = 0; i < tac_engine::kRing; ++i)
     if (e->ring_ev[i]) cudaEventDestroy(e->ring_ev[i]);
@@ -392,6 +396,7 @@ static int launch(tac_engine* e, tac_program* p, const uint64_t* d_params, cudaS
     A.shared_bytes = e->shared_bytes;
     A.dram_bytes = e->dram_bytes;
     A.prof = nullptr;
+    A.task_prof = nullptr;
     if (e->profiling) {
       if (e->prof_cap < n_levels + 1) {
         cudaFree(e->d_prof);
@@ -401,6 +406,16 @@ static int launch(tac_engine* e, tac_program* p, const uint64_t* d_params, cudaS
       CK(cudaMemsetAsync(e->d_prof, 0, (n_levels + 1) * 8, st), f, "reset profile");
       A.prof = e->d_prof;
       e->prof_levels = n_levels;
+      const uint64_t n_tasks = p->tasks.size();
+      if (e->profiling == 2 && n_tasks) {
+        if (e->task_prof_cap < n_tasks) {
+          cudaFree(e->d_task_prof);
+          e->task_prof_cap = n_tasks;
+          CK(cudaMalloc(&e->d_task_prof, n_tasks * 4), f, "cudaMalloc task profile");
+        }
+        A.task_prof = e->d_task_prof;
+        e->prof_tasks = n_tasks;
+      }
     }
     void* args[] = {&A};
     CK(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(exec_kernel), dim3(e->grid), dim3(kCtaThreads), args,
@@ -502,8 +517,18 @@ int tac_run(tac_engine* e, tac_program* p, const uint64_t* var_words, tac_fault*
 }
 
 int tac_set_profiling(tac_engine* e, int enable) {
-  if (!e) return TAC_E_ARGUMENT;
-  e->profiling = enable != 0;
+  if (!e || enable < 0 || enable > 2) return TAC_E_ARGUMENT;
+  e->profiling = enable;
+  return TAC_OK;
+}
+
+int tac_read_task_profile(tac_engine* e, uint32_t* out_cycles, uint64_t max_entries, uint64_t* n_entries) {
+  if (!e || !n_entries) return TAC_E_ARGUMENT;
+  *n_entries = e->prof_tasks;
+  if (!out_cycles || !e->d_task_prof || !e->prof_tasks) return TAC_OK;
+  if (cudaSetDevice(e->device) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) return TAC_E_CUDA;
+  const uint64_t n = std::min<uint64_t>(max_entries, e->prof_tasks);
+  if (cudaMemcpy(out_cycles, e->d_task_prof, n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return TAC_E_CUDA;
   return TAC_OK;
 }
 

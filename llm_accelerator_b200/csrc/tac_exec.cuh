@@ -63,6 +63,7 @@ struct ExecArgs {
   uint64_t shared_bytes;
   uint64_t dram_bytes;
   uint64_t* prof;            // optional: globaltimer at the end of each level (n_levels + 1)
+  uint32_t* task_prof;       // optional: SM cycles of each task
 };
 
 __device__ __forceinline__ uint64_t global_ns() {
@@ -1238,8 +1239,11 @@ __global__ void __launch_bounds__(kCtaThreads, 1) exec_kernel(ExecArgs A) {
   const uint32_t vid = blockIdx.x * kHalves + hidx(), vgrid = gridDim.x * kHalves;
   for (uint32_t L = 0; L < A.n_levels; ++L) {
     const uint32_t t0 = A.level_off[L], t1 = A.level_off[L + 1];
-    for (uint32_t ti = t0 + vid; ti < t1; ti += vgrid)
+    for (uint32_t ti = t0 + vid; ti < t1; ti += vgrid) {
+      const long long c0 = A.task_prof ? clock64() : 0;
       run_task(A, ti, smem, ti + vgrid < t1 ? ti + vgrid : 0xFFFFFFFFu, tc);
+      if (A.task_prof && htid() == 0) A.task_prof[ti] = static_cast<uint32_t>(clock64() - c0);
+    }
     if (L + 1 < A.n_levels) {
       if (!grid_barrier(A, (L + 1) * gridDim.x, L + 1)) break;
       if (threadIdx.x == 0 && blockIdx.x == 0) {

@@ -200,8 +200,20 @@ class Engine:
     def argmax_f16(self, addr: int, count: int, out_dev_ptr: int, stream=None) -> None:
         L.check(_lib.tac_argmax_f16(self.handle, addr, count, out_dev_ptr, stream), "tac_argmax_f16")
 
-    def set_profiling(self, on: bool) -> None:
-        L.check(_lib.tac_set_profiling(self.handle, 1 if on else 0), "tac_set_profiling")
+    def set_profiling(self, on, tasks: bool = False) -> None:
+        """Level timestamps (on); with tasks=True also each task's SM cycles."""
+        mode = (2 if tasks else 1) if on else 0
+        L.check(_lib.tac_set_profiling(self.handle, mode), "tac_set_profiling")
+
+    def read_task_profile(self) -> np.ndarray:
+        """SM cycles of each task of the last run (tasks in level order)."""
+        n = C.c_uint64()
+        L.check(_lib.tac_read_task_profile(self.handle, None, 0, C.byref(n)), "tac_read_task_profile")
+        out = np.zeros(n.value, np.uint32)
+        if n.value:
+            L.check(_lib.tac_read_task_profile(self.handle, out.ctypes.data, n.value, C.byref(n)),
+                    "tac_read_task_profile")
+        return out
 
     def read_profile(self) -> np.ndarray:
         """Device time (ns) at the end of each level of the last run; entry 0 is the start."""

@@ -210,6 +210,45 @@ def test_sites_over_one_symbol_must_carry_one_value():
     assert L.lib.tac_encode_params(p.handle, 1, words.ctypes.data, out.ctypes.data, C.byref(f)) == L.E_RECOMPILE
 
 
+def _words(*insns):
+    from types import SimpleNamespace
+    from llm_accelerator_b200 import isa
+    return b"".join(isa.encode(SimpleNamespace(**d)) for d in insns)
+
+
+@pytest.mark.parametrize("reverse", [False, True], ids=["level-order", "level-reversed"])
+@pytest.mark.parametrize("then", ["halt", "overwrite-then-read"])
+def test_load_aliases_dram_until_it_is_overwritten(then, reverse):
+    """A LOAD from writable DRAM reads the DRAM bytes in place; a later write
+    of those bytes (here the end-of-run flush of a STORE, or a STORE followed
+    by a LOAD of the same bytes) must not change what the LOAD saw."""
+    X = 8192 // 16   # DRAM unit of the data
+    prog = [dict(opcode=0x05, addr_reg=0, imm28=0), dict(opcode=0x06, addr_reg=0, imm28=0),
+            dict(opcode=0x07, buf_id=0, sram_off=0, xfer_len=4, addr_reg=0, dram_off=X),     # ABUF[0:64] <- X
+            dict(opcode=0x08, buf_id=1, sram_off=0, xfer_len=4, addr_reg=0, dram_off=X)]     # X <- WBUF[0:64]
+    if then == "overwrite-then-read":
+        prog.append(dict(opcode=0x07, buf_id=2, sram_off=0, xfer_len=4, addr_reg=0, dram_off=X))  # ACCUM <- X
+    prog.append(dict(opcode=0x01))
+    region = _words(*prog)
+    p = compile_program(1, DRAM, 0, region, 0, 100, L.Regs(), True, ())
+    assert not p.info.faulted
+    rng = np.random.default_rng(7)
+    img = np.zeros(DRAM, np.uint8)
+    img[:len(region)] = np.frombuffer(region, np.uint8)
+    old = rng.integers(0, 256, 64, dtype=np.uint8)
+    new = rng.integers(0, 256, 64, dtype=np.uint8)
+    img[8192:8256] = old
+    m = PE.PlanMachine(img.tobytes(), 0, int(p.info.arena_bytes), int(p.info.n_slots))
+    m.block[131072:131072 + 64] = new
+    ops, segs, tasks, lv = p.dump()
+    PE.run_plan(m, ops, segs, lv, reverse=reverse)
+    f = PE.final_state(m)
+    assert f["abuf"][:64] == old.tobytes()
+    assert f["dram"][8192:8256] == new.tobytes()
+    if then == "overwrite-then-read":
+        assert f["accum"][:64] == new.tobytes()
+
+
 def test_self_modifying_store_is_rejected():
     # SET_ADDR R1 = 0 ; STORE ABUF[0..16) -> DRAM[0] (the instruction region) ; HALT
     words = [(0x05 << 59) | (1 << 57), (0x06 << 59) | (1 << 57),
