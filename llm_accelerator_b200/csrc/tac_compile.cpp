@@ -96,6 +96,7 @@ class Compiler {
   Compiler& operator=(const Compiler&) = delete;
 
   int compile();
+  void prefetch_hint(const DevOp& op, Task& t) const;
 
  private:
   // ---- layout helpers ------------------------------------------------------
@@ -1423,9 +1424,96 @@ void Compiler::build_tasks() {
   P->tasks.clear();
   P->level_off.assign(1, 0);
   for (auto& v : per_level) {
+    for (Task& t : v) prefetch_hint(P->ops[t.op], t);
     P->tasks.insert(P->tasks.end(), v.begin(), v.end());
     P->level_off.push_back(static_cast<uint32_t>(P->tasks.size()));
   }
+}
+
+// The operand bytes a task reads first, for the executor to pull into L2
+// while the task before it runs.  A hint never exceeds what the task itself
+// reads; ops without a cheap contiguous estimate get none.
+void Compiler::prefetch_hint(const DevOp& op, Task& t) const {
+  constexpr uint64_t kMaxUnits = 4096;   // 64 KB
+  uint64_t phys = 0, units = 0;
+  const uint64_t MN = uint64_t(op.M) * op.N;
+  auto elem_bytes = [&](uint32_t kind) -> uint64_t {
+    switch (kind) {
+      case K_QUANT: case K_GELU_F16: case K_VADD_F16: case K_LAYERNORM_F16: case K_SOFTMAX_F16:
+      case K_MASKED_SOFTMAX_F16: case K_MAX_ABS:
+        return 2;
+      case K_DEQUANT_SCALED: case K_DEQUANT_ACCUM: case K_REQUANT_PC: case K_REQUANT: case K_SCALE_MUL_I32:
+      case K_VADD_I32: case K_DEQUANT_ADD:
+        return 4;
+      default:
+        return 1;
+    }
+  };
+  if (op.flags & F_SEGA) {
+    if (op.nseg) {
+      phys = P->segs[op.seg0].src;
+      units = P->segs[op.seg0].n;
+    }
+  } else {
+    switch (op.kind) {
+      case K_GATHER:
+        if (t.tile < op.nseg) {
+          phys = P->segs[op.seg0 + t.tile].src;
+          units = P->segs[op.seg0 + t.tile].n;
+        }
+        break;
+      case K_DYN_STORE:
+        phys = op.a;
+        units = op.nbytes / kUnit;
+        break;
+      case K_MATMUL:
+        if (op.flags & F_TC) break;
+        if (!(op.b & kSharedBit)) {   // per-sequence B: the whole matrix
+          phys = op.b;
+          units = uint64_t(op.K) * op.N / kUnit;
+        } else {
+          phys = op.a;
+          units = uint64_t(std::min<uint32_t>(op.M, 128)) * op.K / kUnit;
+        }
+        break;
+      case K_TRANSPOSE:
+      case K_MAX_ABS:
+        phys = op.a;
+        units = MN * elem_bytes(op.kind) / kUnit;
+        break;
+      case K_LAYERNORM_F16: case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16: {
+        const uint64_t row_units = uint64_t(op.N) * 2 / kUnit;
+        const uint64_t r0 = uint64_t(t.tile) * 8;
+        if (r0 < op.M && op.N % 8 == 0) {
+          phys = op.a + r0 * row_units;
+          units = std::min<uint64_t>(8, op.M - r0) * row_units;
+        }
+        break;
+      }
+      case K_REQUANT: case K_REQUANT_PC: case K_SCALE_MUL_I32: case K_SCALE_MUL_I8: case K_VADD_I8:
+      case K_VADD_I32: case K_DEQUANT_ADD: case K_DEQUANT_ACCUM: case K_DEQUANT_SCALED: case K_QUANT:
+      case K_VADD_F16: case K_GELU_F16: {
+        const uint64_t eb = elem_bytes(op.kind);
+        if (t.nseq > 1) {
+          units = MN * eb / kUnit;
+          phys = op.a;
+        } else {
+          const uint64_t te = ew_task_elems(op.kind);
+          const uint64_t e0 = uint64_t(t.tile) * te;
+          if (e0 < MN && (e0 * eb) % kUnit == 0) {
+            phys = op.a + e0 * eb / kUnit;
+            units = std::min<uint64_t>(te, MN - e0) * eb / kUnit;
+          }
+        }
+        break;
+      }
+      default:
+        break;
+    }
+  }
+  if (units == 0) return;
+  t.pf_phys = phys;
+  t.pf_units = static_cast<uint32_t>(std::min<uint64_t>(units, kMaxUnits));
 }
 
 int Compiler::compile() {

@@ -1127,6 +1127,14 @@ __device__ __forceinline__ void prefetch_l1(const void* p) {
   asm volatile("prefetch.global.L1 [%0];\n" ::"l"(p));
 }
 
+// L2 prefetch of a task's hinted operand bytes.  L2 is the point of
+// coherence, so a prefetch can never expose a stale value.
+__device__ __forceinline__ void prefetch_task_operand(const ExecArgs& A, const Task& t) {
+  if (!t.pf_units) return;
+  const uint8_t* p = pptr(A, t.pf_phys, t.seq0);
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(t.pf_units * 16u) : "memory");
+}
+
 // Grid-wide barrier between levels.  The arrival counter only grows during a
 // launch (the host zeroes it before each launch): a CTA arrives with a release
 // add and waits, with acquire loads, until all gridDim.x CTAs of this level
@@ -1156,18 +1164,31 @@ __device__ __forceinline__ bool grid_barrier(const ExecArgs& A, uint32_t target,
   } else if (htid() == 32 && next_level < A.n_levels) {
     const uint32_t ti = A.level_off[next_level] + blockIdx.x * kHalves + hidx();
     if (ti < A.level_off[next_level + 1]) {
-      const uint32_t op = A.tasks[ti].op;
-      prefetch_l1(A.ops + op);
-      prefetch_l1(reinterpret_cast<const uint8_t*>(A.ops + op) + sizeof(DevOp) - 1);
+      const Task tn = A.tasks[ti];
+      prefetch_l1(A.ops + tn.op);
+      prefetch_l1(reinterpret_cast<const uint8_t*>(A.ops + tn.op) + sizeof(DevOp) - 1);
+      prefetch_task_operand(A, tn);
+      const uint32_t t2 = ti + gridDim.x * kHalves;
+      if (t2 < A.level_off[next_level + 1]) prefetch_l1(A.tasks + t2);
     }
   }
   __syncthreads();
   return ok != 0;
 }
 
-// Runs one task on the calling half.
-__device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t next_ti, TcShared* tc) {
-  if (htid() == 32 && next_ti != 0xFFFFFFFFu) prefetch_l1(A.tasks + next_ti);
+// Runs one task on the calling half.  Meanwhile lane 0 of warp 1 pulls the
+// next task's op record into L1 (op records never change during a launch)
+// and its hinted operand bytes into L2, and the record of the task after it
+// into L1.
+__device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t next_ti, uint32_t next2_ti,
+                         TcShared* tc) {
+  if (htid() == 32 && next_ti != 0xFFFFFFFFu) {
+    const Task tn = A.tasks[next_ti];
+    prefetch_l1(A.ops + tn.op);
+    prefetch_l1(reinterpret_cast<const uint8_t*>(A.ops + tn.op) + sizeof(DevOp) - 1);
+    prefetch_task_operand(A, tn);
+    if (next2_ti != 0xFFFFFFFFu) prefetch_l1(A.tasks + next2_ti);
+  }
   const Task t = A.tasks[ti];
   const DevOp& op = A.ops[t.op];
   switch (op.kind) {
@@ -1241,7 +1262,8 @@ __global__ void __launch_bounds__(kCtaThreads, 1) exec_kernel(ExecArgs A) {
     const uint32_t t0 = A.level_off[L], t1 = A.level_off[L + 1];
     for (uint32_t ti = t0 + vid; ti < t1; ti += vgrid) {
       const long long c0 = A.task_prof ? clock64() : 0;
-      run_task(A, ti, smem, ti + vgrid < t1 ? ti + vgrid : 0xFFFFFFFFu, tc);
+      run_task(A, ti, smem, ti + vgrid < t1 ? ti + vgrid : 0xFFFFFFFFu,
+               ti + 2 * vgrid < t1 ? ti + 2 * vgrid : 0xFFFFFFFFu, tc);
       if (A.task_prof && htid() == 0) A.task_prof[ti] = static_cast<uint32_t>(clock64() - c0);
     }
     if (L + 1 < A.n_levels) {

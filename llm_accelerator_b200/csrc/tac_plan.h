@@ -104,7 +104,10 @@ struct Task {
   uint32_t nseq;   // sequences covered
   uint32_t tile;   // op-specific tile index (K_GATHER: first segment, relative to seg0)
   uint32_t aux;    // K_GATHER: one past the last segment (relative to seg0)
+  uint32_t pf_units;   // prefetch hint: 16-byte units the task reads first (0 = none)
+  uint64_t pf_phys;    // prefetch hint: their physical start (sequence seq0)
 };
+static_assert(sizeof(Task) == 32, "Task is a 32-byte record");
 
 // Gathers split their segments into pieces of at most this many units, and a
 // gather task copies a run of whole segments of about this size.

@@ -20,7 +20,8 @@ DEVOP_DTYPE = np.dtype([
     ("_pad", "<u4"), ("dconst", "<i8"), ("nbytes", "<u8"), ("attn_qrb", "<u4"), ("attn_vkl", "<u4"),
     ("pc", "<u4"), ("level", "<u4")])
 SEGMENT_DTYPE = np.dtype([("src", "<u8"), ("dst", "<u8"), ("n", "<u8")])
-TASK_DTYPE = np.dtype([("op", "<u4"), ("seq0", "<u4"), ("nseq", "<u4"), ("tile", "<u4"), ("aux", "<u4")])
+TASK_DTYPE = np.dtype([("op", "<u4"), ("seq0", "<u4"), ("nseq", "<u4"), ("tile", "<u4"), ("aux", "<u4"),
+                       ("pf_units", "<u4"), ("pf_phys", "<u8")])
 
 
 @dataclass

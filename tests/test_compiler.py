@@ -173,6 +173,35 @@ def test_runtime_site_out_of_range_requests_recompile():
     assert int(p.info.n_levels) > 0 and not p.info.faulted
 
 
+def _check_prefetch_hints(p, dram_bytes, shared_bytes):
+    """Every task's L2 prefetch range lies inside the memory its op reads:
+    the per-sequence block [SRAM | writable DRAM | arena] or the shared image."""
+    ops, segs, tasks, lv = p.dump()
+    block_units = PE.SRAM_UNITS + (dram_bytes - shared_bytes + 15) // 16 + int(p.info.arena_bytes) // 16
+    hinted = tasks[tasks["pf_units"] > 0]
+    assert len(hinted) > 0
+    phys = hinted["pf_phys"].astype(np.uint64)
+    units = hinted["pf_units"].astype(np.uint64)
+    shared = (phys >> np.uint64(63)) == 1
+    off = phys & np.uint64((1 << 63) - 1)
+    end = off + units
+    assert np.all(end[shared] <= np.uint64(shared_bytes // 16))
+    assert np.all(end[~shared] <= np.uint64(block_units))
+    assert np.all(units <= 4096)
+
+
+@pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
+@pytest.mark.parametrize("batch", [1, 4])
+def test_prefetch_hints_stay_inside_operands(name, batch):
+    b = load_bundle(name)
+    shared = b.temp_base // 16 * 16
+    for nm in ("prefill", "decode"):
+        entry = b.prefill_pc if nm == "prefill" else b.decode_pc
+        p = compile_program(batch, 16 << 20, shared, bytes(b.instruction_region()), entry, 10_000_000, L.Regs(),
+                            True, _sites(b, nm))
+        _check_prefetch_hints(p, 16 << 20, shared)
+
+
 def _var_words(region, sites):
     words = []
     for s in sites:
