@@ -495,6 +495,8 @@ int tac_check_device_status(tac_engine* e, tac_fault* f) {
       return set_fault(f, TAC_E_DEVICE, "runtime address outside DRAM");
     case DF_MMA_TIMEOUT:
       return set_fault(f, TAC_E_DEVICE, "executor tensor-core MATMUL wait timed out");
+    case DF_STAGE_TIMEOUT:
+      return set_fault(f, TAC_E_DEVICE, "executor operand bulk copy wait timed out");
     default:
       return set_fault(f, TAC_E_DEVICE, "executor reported an invalid op");
   }

@@ -42,6 +42,7 @@ enum DevFault : uint32_t {
   DF_ZERO_DENOM = 3,
   DF_BAD_OP = 4,
   DF_MMA_TIMEOUT = 5,
+  DF_STAGE_TIMEOUT = 6,
 };
 
 struct ExecArgs {
@@ -416,9 +417,11 @@ constexpr uint32_t kTcIdesc = sm100::idesc_i8(128, 64, 1);
 struct TcShared {
   uint64_t full[kTcStages];    // TMA bytes of a stage landed
   uint64_t empty[kTcStages];   // the MMAs reading a stage completed
+  uint64_t stage;              // bulk-copied element-wise operands landed
   uint32_t tmem;
   uint32_t phase_full;         // bit s: parity of the next phase of full[s]
   uint32_t phase_empty;
+  uint32_t phase_stage;        // parity of the next phase of `stage`
 };
 
 // shared-memory descriptor, 64-byte swizzle (layout type 4)
@@ -452,6 +455,7 @@ __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, co
       if (!sm100::mbar_wait(&bar[st], (ph >> st) & 1u, nullptr, 0)) ok = false;
       ph ^= 1u << st;
     };
+    sm100::fence_proxy_async();   // A was written by generic stores in earlier levels
     for (uint32_t c = 0; c < nchunks && c < uint32_t(kTcStages); ++c) load(c);
     for (uint32_t c = 0; c < nchunks; ++c) {
       const uint32_t st = c % kTcStages;
@@ -584,7 +588,9 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
   V8 ia[kEwGroups];
   uint2 qa[kEwGroups], qb[kEwGroups];
   uint32_t e0[kEwGroups], sq[kEwGroups];
-  float s0v[kEwGroups], s1v[kEwGroups];
+  // raw FP16 register bits: converted only in phase 2, so no load of phase 1
+  // waits for another
+  uint16_t s0b[kEwGroups], s1b[kEwGroups];
 #pragma unroll
   for (uint32_t g = 0; g < kGroups; ++g) {
     const uint32_t e = base + (g * kThreads + htid()) * 8;
@@ -595,8 +601,8 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
       continue;
     }
     const uint32_t seq = t.seq0 + sq[g];
-    s0v[g] = sreg_f32(A, op.s[0], seq);
-    s1v[g] = sreg_f32(A, op.s[1], seq);
+    s0b[g] = sreg_bits(A, op.s[0], seq);
+    s1b[g] = sreg_bits(A, op.s[1], seq);
     const uint8_t* __restrict__ a = a0 + sq[g] * sa;
     const uint8_t* __restrict__ b = b0 + sq[g] * sb;
     const uint32_t col = e0[g] % N;
@@ -637,7 +643,7 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
   for (uint32_t g = 0; g < kGroups; ++g) {
     if (e0[g] >= MN) continue;
     uint8_t* __restrict__ d = d0 + sq[g] * sd;
-    const float s0 = s0v[g], s1 = s1v[g];
+    const float s0 = h2f(s0b[g]), s1 = h2f(s1b[g]);
     if constexpr (KIND == K_QUANT) {
       int8_t q[8];
 #pragma unroll
@@ -731,6 +737,135 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
   }
 }
 
+// ---------------------------------------------------------------------------------
+// QUANT, GELU_F16, VADD_F16 and DEQUANT_SCALED with their operands staged in
+// shared memory: one thread bulk-copies the task's slice of a (and of b for
+// VADD, the [scale | bias] rows for DEQUANT_SCALED) for every sequence of the
+// task, the half waits once on an mbarrier, then computes from shared memory.
+// No operand register is held across the memory latency, and the latency is
+// paid once per task.  Requires MN and N multiples of 8 (every copy is whole
+// 16-byte units) and a staged size of at most kStageBytes.
+// ---------------------------------------------------------------------------------
+constexpr uint32_t kStageBytes = 64 * 1024;
+
+template <int KIND>
+__device__ __forceinline__ uint32_t staged_bytes(const DevOp& op, const Task& t) {
+  const uint32_t N = op.N, MN = op.M * N;
+  constexpr uint32_t kTask = ew_task_elems(KIND);
+  constexpr uint32_t ea = KIND == K_DEQUANT_SCALED ? 4 : 2;
+  const uint32_t nseq = t.nseq > 1 ? t.nseq : 1;
+  const uint32_t e_begin = t.nseq > 1 ? 0 : t.tile * kTask;
+  const uint32_t e_count = t.nseq > 1 ? MN : min(kTask, MN - e_begin);
+  uint32_t bytes = nseq * e_count * ea;
+  if (KIND == K_VADD_F16) bytes += nseq * e_count * 2;
+  if (KIND == K_DEQUANT_SCALED) bytes += ((op.b & kSharedBit) ? 1u : nseq) * N * 4;
+  return bytes;
+}
+
+template <int KIND>
+__device__ __noinline__ void ew_staged(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
+                                       TcShared* tc, uint32_t opi) {
+  const uint32_t N = op.N, MN = op.M * N;
+  constexpr uint32_t kTask = ew_task_elems(KIND);
+  constexpr uint32_t ea = KIND == K_DEQUANT_SCALED ? 4 : 2;   // bytes of an a element
+  const uint32_t nseq = t.nseq > 1 ? t.nseq : 1;
+  const uint32_t e_begin = t.nseq > 1 ? 0 : t.tile * kTask;
+  const uint32_t e_count = t.nseq > 1 ? MN : min(kTask, MN - e_begin);   // elements per sequence
+  const bool row_shared = (op.b & kSharedBit) != 0;
+  uint8_t* sa = smem;                                   // [nseq][e_count] a
+  uint8_t* sb = sa + nseq * e_count * ea;               // VADD: [nseq][e_count] b; DEQ: [seq][scale N | bias N]
+  const uint32_t par = tc->phase_stage;
+  hsync();   // every thread has the parity before it flips
+  if (htid() == 0) {
+    tc->phase_stage = par ^ 1u;
+    sm100::fence_proxy_async();
+    sm100::mbar_arrive_expect_tx(&tc->stage, staged_bytes<KIND>(op, t));
+    for (uint32_t s = 0; s < nseq; ++s) {
+      const uint32_t seq = t.seq0 + s;
+      sm100::bulk_g2s(sa + s * e_count * ea, pptr(A, op.a, seq) + uint64_t(e_begin) * ea, e_count * ea, &tc->stage);
+      if (KIND == K_VADD_F16)
+        sm100::bulk_g2s(sb + s * e_count * 2, pptr(A, op.b, seq) + uint64_t(e_begin) * 2, e_count * 2, &tc->stage);
+      if (KIND == K_DEQUANT_SCALED && (s == 0 || !row_shared)) {
+        uint8_t* rows = sb + s * N * 4;
+        const uint8_t* scale = pptr(A, op.b, seq);
+        const uint8_t* bias = (op.flags & F_SPLIT) ? pptr(A, op.c, seq) : scale + uint64_t(N) * 2;
+        sm100::bulk_g2s(rows, scale, N * 2, &tc->stage);
+        sm100::bulk_g2s(rows + N * 2, bias, N * 2, &tc->stage);
+      }
+    }
+  }
+  // the registers' raw bits load while the copies are in flight
+  uint16_t s0b = 0;
+  if (KIND == K_QUANT || KIND == K_DEQUANT_SCALED) s0b = sreg_bits(A, op.s[0], t.seq0);
+  if (!sm100::mbar_wait(&tc->stage, par, nullptr, 0)) {
+    // the copies did not land in time: wait (bounded) for them once more, then fault
+    sm100::mbar_wait(&tc->stage, par, nullptr, 0);
+    if (htid() == 0) raise_fault(A, DF_STAGE_TIMEOUT, opi, t.seq0);
+    return;
+  }
+  const uint32_t total = nseq * e_count;
+  uint32_t cur_seq = 0xFFFFFFFFu;
+  float s0 = 0.f;
+  for (uint32_t i = htid() * 8; i < total; i += kThreads * 8) {
+    const uint32_t s = i / e_count, e = e_begin + (i - s * e_count);
+    const uint32_t seq = t.seq0 + s;
+    if (KIND == K_QUANT || KIND == K_DEQUANT_SCALED) {
+      if (seq != cur_seq) {
+        s0 = h2f(seq == t.seq0 ? s0b : sreg_bits(A, op.s[0], seq));
+        cur_seq = seq;
+      }
+    }
+    uint8_t* d = pptr(A, op.d, seq);
+    if constexpr (KIND == K_QUANT) {
+      const uint4 x = *reinterpret_cast<const uint4*>(sa + uint64_t(i) * 2);
+      int8_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float r = rintf(__fmul_rn(h2f(h_at(x, j)), s0));
+        q[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+      }
+      *reinterpret_cast<uint2*>(d + e) = pack_b(q);
+    } else if constexpr (KIND == K_GELU_F16) {
+      const uint4 x = *reinterpret_cast<const uint4*>(sa + uint64_t(i) * 2);
+      uint16_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = f2h(gelu_f32(h2f(h_at(x, j))));
+      *reinterpret_cast<uint4*>(d + uint64_t(e) * 2) = pack_h(h);
+    } else if constexpr (KIND == K_VADD_F16) {
+      const uint4 x = *reinterpret_cast<const uint4*>(sa + uint64_t(i) * 2);
+      const uint4 y = *reinterpret_cast<const uint4*>(sb + uint64_t(i) * 2);
+      uint16_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = f2h(__fadd_rn(h2f(h_at(x, j)), h2f(h_at(y, j))));
+      *reinterpret_cast<uint4*>(d + uint64_t(e) * 2) = pack_h(h);
+    } else {   // K_DEQUANT_SCALED
+      const uint4 lo = *reinterpret_cast<const uint4*>(sa + uint64_t(i) * 4);
+      const uint4 hi = *reinterpret_cast<const uint4*>(sa + uint64_t(i) * 4 + 16);
+      const uint32_t col = e % N;
+      const uint8_t* rows = sb + (row_shared ? 0u : s) * N * 4;
+      const uint4 sc = *reinterpret_cast<const uint4*>(rows + col * 2);
+      const uint4 bi = *reinterpret_cast<const uint4*>(rows + N * 2 + col * 2);
+      const int32_t acc[8] = {int32_t(lo.x), int32_t(lo.y), int32_t(lo.z), int32_t(lo.w),
+                              int32_t(hi.x), int32_t(hi.y), int32_t(hi.z), int32_t(hi.w)};
+      uint16_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float v = __fmul_rn(__int2float_rn(acc[j]), h2f(h_at(sc, j)));
+        v = __fmul_rn(v, s0);
+        h[j] = f2h(__fadd_rn(v, h2f(h_at(bi, j))));
+      }
+      *reinterpret_cast<uint4*>(d + uint64_t(e) * 2) = pack_h(h);
+    }
+  }
+}
+
+// Whether a task can take the staged path.
+template <int KIND>
+__device__ __forceinline__ bool can_stage(const DevOp& op, const Task& t) {
+  if (op.N % 8 || (op.M * op.N) % 8) return false;
+  return staged_bytes<KIND>(op, t) <= kStageBytes;
+}
+
 __device__ __noinline__ void op_elementwise(const ExecArgs& A, const DevOp& op, const Task& t) {
   switch (op.kind) {
     case K_QUANT: ew_kernel<K_QUANT>(A, op, t); break;
@@ -789,8 +924,10 @@ __device__ __forceinline__ const uint4* seg_unit(const ExecArgs& A, const DevOp&
 __device__ __noinline__ void op_seg_ew(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
   const uint32_t seq = t.seq0;
   const uint32_t units = op.M * op.N / 8;   // FP16 operand: 8 elements per 16-byte unit
+  // the register's raw bits load while the segment table is staged; they are
+  // converted at their first use, after the operand loads are in flight
+  const uint16_t s0b = op.kind == K_QUANT ? sreg_bits(A, op.s[0], seq) : uint16_t(0);
   seg_stage(A, op, smem);
-  const float s0 = op.kind == K_QUANT ? sreg_f32(A, op.s[0], seq) : 0.f;
   const uint4* b = reinterpret_cast<const uint4*>(pptr(A, op.b, seq));
   uint8_t* d = pptr(A, op.d, seq);
   for (uint32_t u0 = htid(); u0 < units; u0 += 4 * kThreads) {
@@ -808,6 +945,7 @@ __device__ __noinline__ void op_seg_ew(const ExecArgs& A, const DevOp& op, const
       const uint32_t u = u0 + q * kThreads;
       if (u >= units) continue;
       if (op.kind == K_QUANT) {
+        const float s0 = h2f(s0b);
         int8_t o[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -1189,7 +1327,7 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     prefetch_task_operand(A, tn);
     if (next2_ti != 0xFFFFFFFFu) prefetch_l1(A.tasks + next2_ti);
   }
-  const Task t = A.tasks[ti];
+  const Task& t = A.tasks[ti];   // read in place (L1), not copied to local memory
   const DevOp& op = A.ops[t.op];
   switch (op.kind) {
     case K_GATHER: op_gather(A, op, t); break;
@@ -1211,8 +1349,19 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_REQUANT: case K_REQUANT_PC: case K_SCALE_MUL_I32: case K_SCALE_MUL_I8:
     case K_VADD_I8: case K_VADD_I32: case K_DEQUANT_ADD: case K_DEQUANT_ACCUM:
     case K_DEQUANT_SCALED: case K_QUANT: case K_VADD_F16: case K_GELU_F16: case K_GELU_I8:
-      if (op.flags & F_SEGA) op_seg_ew(A, op, t, smem);
-      else op_elementwise(A, op, t);
+      if (op.flags & F_SEGA) {
+        op_seg_ew(A, op, t, smem);
+      } else if (op.kind == K_QUANT && can_stage<K_QUANT>(op, t)) {
+        ew_staged<K_QUANT>(A, op, t, smem, tc, t.op);
+      } else if (op.kind == K_DEQUANT_SCALED && can_stage<K_DEQUANT_SCALED>(op, t)) {
+        ew_staged<K_DEQUANT_SCALED>(A, op, t, smem, tc, t.op);
+      } else if (op.kind == K_VADD_F16 && can_stage<K_VADD_F16>(op, t)) {
+        ew_staged<K_VADD_F16>(A, op, t, smem, tc, t.op);
+      } else if (op.kind == K_GELU_F16 && can_stage<K_GELU_F16>(op, t)) {
+        ew_staged<K_GELU_F16>(A, op, t, smem, tc, t.op);
+      } else {
+        op_elementwise(A, op, t);
+      }
       break;
     default:
       if (htid() == 0) raise_fault(A, DF_BAD_OP, t.op, t.seq0);
@@ -1227,13 +1376,16 @@ constexpr size_t kRowSmem = kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4
 constexpr size_t kTcSmem = kTcStages * kTcStage + 1024;   // + alignment of the swizzled stages
 constexpr size_t kExecOpSmem0 = kRowSmem > kMmSmem ? kRowSmem : kMmSmem;
 constexpr size_t kExecOpSmem = kExecOpSmem0 > kTcSmem ? kExecOpSmem0 : kTcSmem;
-constexpr size_t kExecSmem = kHalves * kExecOpSmem + kHalves * 64;
-static_assert(sizeof(TcShared) <= 64, "TcShared outgrew its slot");
+constexpr size_t kExecSmem = kHalves * kExecOpSmem + kHalves * 128;
+static_assert(sizeof(TcShared) <= 128, "TcShared outgrew its slot");
+static_assert(kStageBytes <= kExecOpSmem, "element-wise staging exceeds the op shared memory");
 static_assert(kSegTableOff + kMaxSegRuns * 12 <= kExecOpSmem, "segment table exceeds the op shared memory");
 static_assert(kExecOpSmem % 1024 == 0 || kTcSmem <= kExecOpSmem, "half regions must keep the stage alignment slack");
 static_assert(kExecSmem <= 227 * 1024, "executor shared memory exceeds one CTA's limit");
 
-__global__ void __launch_bounds__(kCtaThreads, 1) exec_kernel(ExecArgs A) {
+// A is a __grid_constant__ parameter: the op functions take its address
+// without a per-thread copy in local memory.
+__global__ void __launch_bounds__(kCtaThreads, 1) exec_kernel(const __grid_constant__ ExecArgs A) {
   extern __shared__ __align__(16) uint8_t smem_all[];
   uint8_t* smem = smem_all + hidx() * kExecOpSmem;
   TcShared* tcs = reinterpret_cast<TcShared*>(smem_all + kHalves * kExecOpSmem);
@@ -1244,8 +1396,10 @@ __global__ void __launch_bounds__(kCtaThreads, 1) exec_kernel(ExecArgs A) {
         sm100::mbar_init(&tcs[h].full[st], 1);
         sm100::mbar_init(&tcs[h].empty[st], 1);
       }
+      sm100::mbar_init(&tcs[h].stage, 1);
       tcs[h].phase_full = 0;
       tcs[h].phase_empty = 0;
+      tcs[h].phase_stage = 0;
     }
     sm100::mbar_fence_init();
   }
