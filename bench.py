@@ -3,15 +3,19 @@
 
 Workload (default ``gpt2-medium``): GPT-2 medium (24 layers, d_model 1024,
 16 heads, vocab 50257) compiled by the reference toolchain to a W8A16
-ProgramBundle with a 256-position KV cache; 64 independent sequences sharded
-by sequence over the GPUs.  A step runs the decode stream once for every
-sequence (one token each).  ``value`` times K teacher-forced prompt steps with
+ProgramBundle with a 256-position KV cache; 64 independent sequences per GPU
+(weak scaling: N GPUs run 64 x N sequences, each rank its own shard of the
+sequence ids, no collective on the data path; ``--strong`` splits a fixed
+global batch instead).  A step runs the decode stream once for every sequence
+(one token each).  ``value`` times K teacher-forced prompt steps with
 their runtime parameters already in device memory; ``e2e`` times K greedy
 steps through the public runner API with host buffers (runtime words in,
 argmax token ids out, every step).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gpt2-medium|gpt2-small] [--batch B]
+                    [--workload gpt2-medium|gpt2-small] [--batch B] [--strong]
+
+``--batch`` is the per-GPU batch (the global batch with ``--strong``).
 
 ``--impl reference`` times the CPU oracle port of the golden simulator on the
 host cores (rank 0 only) with the same metric.
@@ -268,21 +272,27 @@ def quarot_line():
 
 
 def traffic_per_launch(workload, batch):
-    """DRAM bytes per executor launch from the committed ncu summary (or None)."""
+    """DRAM bytes per executor launch from the committed ncu summary: the
+    measured line for this batch, else a least-squares line through the
+    measured batches (None without a summary)."""
     f = ROOT / "profiles" / f"exec_kernel_{workload}.txt"
     if not f.exists():
         return None
-    vals = {}
+    pts = {}
     for line in f.read_text().splitlines():
-        if "=" in line and not line.startswith("#"):
+        if line.startswith("dram_bytes_batch_") and "=" in line:
             k, v = line.split("=", 1)
-            vals[k.strip()] = v.strip()
-    try:
-        per_seq = float(vals["dram_bytes_per_sequence"])
-        fixed = float(vals["dram_bytes_fixed"])
-        return fixed + per_seq * batch
-    except KeyError:
+            pts[int(k.strip()[len("dram_bytes_batch_"):])] = float(v.strip())
+    if not pts:
         return None
+    if batch in pts:
+        return pts[batch]
+    if len(pts) == 1:
+        (b0, v0), = pts.items()
+        return v0 * batch / b0
+    xs, ys = np.array(list(pts)), np.array(list(pts.values()))
+    slope, icpt = np.polyfit(xs, ys, 1)
+    return float(icpt + slope * batch)
 
 
 # ----------------------------------------------------------------------------------------
@@ -309,8 +319,10 @@ def run_reference(args, w, bundle, rank, world):
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": min(args.warmup, 1), "ms_per_step": round(1000 * secs / args.steps, 1),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic", "config": {"workload": w["desc"], "global_batch": w["batch"]},
+        "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": w["desc"],
+                   "global_batch": (args.batch or w["batch"]) * (1 if args.strong else max(args.gpus, world))},
         "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": workers, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -323,9 +335,12 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     from llm_accelerator_b200.runner import BatchedRunner
 
     from llm_accelerator_b200.shard import gather_tokens, shard
-    B_total = args.batch or w["batch"]
-    if B_total % world:
-        raise SystemExit(f"batch {B_total} does not split over {world} GPUs")
+    if args.strong:
+        B_total = args.batch or w["batch"]
+        if B_total % world:
+            raise SystemExit(f"batch {B_total} does not split over {world} GPUs")
+    else:
+        B_total = (args.batch or w["batch"]) * world
     B = B_total // world
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -410,7 +425,8 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K,
-            "warmup": W, "ms_per_step": round(ms / K, 3), "higher_is_better": True, "scaling": "strong",
+            "warmup": W, "ms_per_step": round(ms / K, 3), "higher_is_better": True,
+            "scaling": "strong" if args.strong else "weak",
             "vs_baseline": None, "dtype": "int8",
             "data": "synthetic: seeded random-init weights in the reference-compiled program",
             "config": {"workload": w["desc"], "global_batch": B_total, "per_gpu_batch": B,
@@ -444,7 +460,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="gpt2-medium", choices=sorted(WORKLOADS))
-    ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--batch", type=int, default=0, help="per-GPU batch (global batch with --strong)")
+    ap.add_argument("--strong", action="store_true", help="split one global batch over the GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true",
                     help="skip the stand-alone 4096^3 INT8 GEMM and QuaRot layer measurements")

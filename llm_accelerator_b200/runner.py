@@ -175,35 +175,55 @@ class BatchedRunner:
                                                sram_live=sram_live, sregs_live=sregs_live)
 
     # ---- runtime words ------------------------------------------------------------------
-    def var_words(self, name: str, tokens: Sequence[int], positions: Sequence[int]) -> np.ndarray:
-        """[batch, n_var_words] runtime words for one step of every sequence."""
+    def _var_layout(self, name: str):
+        """Per-stream coefficients of the runtime words, built once: address
+        site i holds base_i + token * tok_mul_i + position * pos_mul_i."""
+        cache = self.__dict__.setdefault("_var_layout_cache", {})
+        if name in cache:
+            return cache[name]
         b = self.bundle
         sites, meta = self._sites[name]
-        out = np.zeros((self.batch, self.plans[name].n_var_words), dtype=np.uint64)
         row, kv = int(b.embedding_row_bytes), int(b.kv_step_bytes)
-        tokens = np.asarray(tokens, dtype=np.int64).reshape(self.batch)
-        positions = np.asarray(positions, dtype=np.int64).reshape(self.batch)
+        a_col, a_base, a_tok, a_pos, a_reg, t_col, t_mode = [], [], [], [], [], [], []
         col = 0
         for (kind, s) in meta:
             if kind == "addr":
-                base = b.symbol_address(s.base_symbol)
-                if s.kind == "token_embed":
-                    vals = base + tokens * row
-                elif s.kind == "pos_embed":
-                    vals = base + positions * row
-                else:
-                    vals = base + positions * kv
-                lo_op, hi_op = np.uint64(isa.SET_ADDR_LO << 59), np.uint64(isa.SET_ADDR_HI << 59)
-                reg = np.uint64(s.addr_reg << 57)
-                v = vals.astype(np.uint64)
-                out[:, col] = lo_op | reg | ((v & np.uint64(isa.M28)) << np.uint64(29))
-                out[:, col + 1] = hi_op | reg | (((v >> np.uint64(28)) & np.uint64(isa.M28)) << np.uint64(29))
+                a_col.append(col)
+                a_base.append(b.symbol_address(s.base_symbol))
+                a_tok.append(row if s.kind == "token_embed" else 0)
+                a_pos.append(row if s.kind == "pos_embed" else (0 if s.kind == "token_embed" else kv))
+                a_reg.append(s.addr_reg)
                 col += 2
             else:
-                p = positions.astype(np.uint64)
-                out[:, col] = (np.uint64(isa.CONFIG_ATTN << 59) | (p << np.uint64(47)) |
-                               ((p + np.uint64(1)) << np.uint64(35)) | np.uint64(s.mode << 33))
+                t_col.append(col)
+                t_mode.append(s.mode)
                 col += 1
+        u = lambda v: np.asarray(v, dtype=np.uint64)  # noqa: E731
+        lay = dict(a_col=np.asarray(a_col, np.int64), a_base=u(a_base), a_tok=u(a_tok), a_pos=u(a_pos),
+                   a_reg=u(a_reg) << np.uint64(57), t_col=np.asarray(t_col, np.int64),
+                   t_mode=u(t_mode) << np.uint64(33), n=col)
+        cache[name] = lay
+        return lay
+
+    def var_words(self, name: str, tokens: Sequence[int], positions: Sequence[int]) -> np.ndarray:
+        """[batch, n_var_words] runtime words for one step of every sequence:
+        SET_ADDR_LO/HI pairs of symbol + token * row, symbol + position * row
+        or symbol + position * kv_step_bytes, and CONFIG_ATTN words with
+        query_row_base = position, valid_kv_len = position + 1."""
+        lay = self._var_layout(name)
+        out = np.zeros((self.batch, self.plans[name].n_var_words), dtype=np.uint64)
+        tok = np.asarray(tokens, dtype=np.int64).reshape(self.batch, 1).astype(np.uint64)
+        pos = np.asarray(positions, dtype=np.int64).reshape(self.batch, 1).astype(np.uint64)
+        if len(lay["a_col"]):
+            v = lay["a_base"][None, :] + tok * lay["a_tok"][None, :] + pos * lay["a_pos"][None, :]
+            m28 = np.uint64(isa.M28)
+            out[:, lay["a_col"]] = (np.uint64(isa.SET_ADDR_LO << 59) | lay["a_reg"][None, :] |
+                                    ((v & m28) << np.uint64(29)))
+            out[:, lay["a_col"] + 1] = (np.uint64(isa.SET_ADDR_HI << 59) | lay["a_reg"][None, :] |
+                                        (((v >> np.uint64(28)) & m28) << np.uint64(29)))
+        if len(lay["t_col"]):
+            out[:, lay["t_col"]] = (np.uint64(isa.CONFIG_ATTN << 59) | (pos << np.uint64(47)) |
+                                    ((pos + np.uint64(1)) << np.uint64(35)) | lay["t_mode"][None, :])
         return out
 
     def params(self, name: str, tokens, positions) -> np.ndarray:
