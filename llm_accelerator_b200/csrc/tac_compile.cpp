@@ -97,6 +97,8 @@ class Compiler {
 
   int compile();
   void prefetch_hint(const DevOp& op, Task& t) const;
+  void drop_dead_ops();
+  uint64_t dead_ops_ = 0;
 
  private:
   // ---- layout helpers ------------------------------------------------------
@@ -258,6 +260,18 @@ class Compiler {
   }
 
   uint32_t emit(DevOp op, const Access& a) {
+    std::vector<std::pair<uint64_t, uint64_t>> ar, aw;
+    for (auto& r : a.reads)
+      if (cls(r.first) == PC_ARENA) ar.push_back(r);
+    bool pure = a.slot_writes.empty() && !a.sreg_home_write && op.kind != K_DYN_STORE && op.kind != K_SREG_FINAL;
+    for (auto& w : a.writes) {
+      pure = pure && cls(w.first) == PC_ARENA;
+      if (cls(w.first) == PC_ARENA) aw.push_back(w);
+    }
+    pure = pure && !aw.empty();
+    op_arena_reads_.push_back(std::move(ar));
+    op_arena_writes_.push_back(std::move(aw));
+    op_pure_.push_back(pure ? 1 : 0);
     pending_same_.clear();
     int32_t L = level_for(a);
     commit(a, L);
@@ -415,6 +429,22 @@ class Compiler {
     }
     uint32_t idx = emit(op, acc);
     if (!key.empty()) cse_[key] = idx;
+  }
+
+  // Operand B of a small per-sequence MATMUL that is the transpose of an
+  // immutable [N][K] extent: read that extent directly (F_BT), so the MATMUL
+  // needs neither the TRANSPOSE's output nor a transpose of its own.
+  bool bt_source(uint32_t u0, uint32_t M, uint32_t N, uint32_t K, Access& acc, DevOp& op) {
+    if (M == 0 || M > 32 || K == 0 || K > 128 || N == 0 || N > 256 || M % 16 || K % 16 || N % 16) return false;
+    const uint64_t n = uint64_t(K) * N / kUnit;
+    const uint64_t* m = &sram_[u0];
+    if (!contiguous(m, n)) return false;
+    auto it = transposed_.find(m[0]);
+    if (it == transposed_.end() || it->second.rows != N || it->second.cols != K) return false;
+    op.b = it->second.src;
+    op.flags |= F_BT | F_WIDE;   // only the wide MATMUL reads B^T
+    acc.reads.push_back({op.b, n});
+    return true;
   }
 
   // Physical start of a contiguous copy of logical SRAM units [u0, u0+n).
@@ -625,6 +655,15 @@ class Compiler {
   std::vector<int32_t> arena_lvl_, rw_wl_, rw_rl_, home_rl_, slot_lvl_;
   std::vector<DynWrite> dyn_w_;
   std::map<uint64_t, uint64_t> alias_iv_;   // see note_alias
+  // arena extents written by TRANSPOSE ops -> their immutable [rows][cols] source
+  struct TransposeOf {
+    uint64_t src;
+    uint64_t rows, cols;
+  };
+  std::unordered_map<uint64_t, TransposeOf> transposed_;
+  // per emitted op: its arena reads and writes, and whether arena writes are its only effect
+  std::vector<std::vector<std::pair<uint64_t, uint64_t>>> op_arena_reads_, op_arena_writes_;
+  std::vector<uint8_t> op_pure_;
   // site i's group: the first address site with the same value range; sites of
   // one group are assumed (and checked at run time) to carry one value
   std::vector<int> site_group_;
@@ -825,6 +864,9 @@ int Compiler::h_buf_copy(const Insn& x) {                   // dma.py:67-97
   op.a = src(su, n, acc);
   op.d = dst(du, n, acc);
   emit_compute(op, acc, du, -1);
+  // a MATMUL may later read the source with F_BT instead (immutable sources only)
+  const uint64_t out = sram_[du];
+  if (cls(op.a) == PC_ARENA && cls(out) == PC_ARENA) transposed_[out] = TransposeOf{op.a, rows, cols};
   cycles_ += x.length;
   return 0;
 }
@@ -949,7 +991,7 @@ int Compiler::h_rtype(const Insn& x) {
       TRY(span(x.dst_buf, x.dst_off, M * N * 4));
       op.kind = K_MATMUL;
       op.a = src(s1, M * K, acc);
-      op.b = src(s2, K * N, acc);
+      if (!bt_source(s2, M, N, K, acc, op)) op.b = src(s2, K * N, acc);
       if (x.flags & 1) {
         op.flags |= F_ACCUMULATE;
         op.c = src(d, M * N * 4, acc);
@@ -1323,6 +1365,42 @@ void Compiler::finalize() {
   }
 }
 
+// Removes ops whose only effect is arena extents no kept op reads (a
+// TRANSPOSE whose MATMUL reads its source instead, a value overwritten before
+// use).  Walks the ops backwards, keeping an op when it has another effect or
+// a kept op reads any unit it writes.
+void Compiler::drop_dead_ops() {
+  const size_t n = P->ops.size();
+  if (op_arena_reads_.size() != n || op_arena_writes_.size() != n || op_pure_.size() != n) return;
+  std::vector<uint8_t> read(arena_top_, 0);
+  std::vector<uint8_t> keep(n, 0);
+  auto mark = [&](uint64_t phys, uint64_t units) {
+    for (uint64_t u = 0; u < units; ++u) {
+      const uint64_t k = phys - arena_base_ + u;
+      if (k < read.size()) read[k] = 1;
+    }
+  };
+  auto any_read = [&](uint64_t phys, uint64_t units) {
+    for (uint64_t u = 0; u < units; ++u) {
+      const uint64_t k = phys - arena_base_ + u;
+      if (k >= read.size() || read[k]) return true;
+    }
+    return false;
+  };
+  for (size_t i = n; i-- > 0;) {
+    bool live = !op_pure_[i];
+    for (auto& w : op_arena_writes_[i]) live = live || any_read(w.first, w.second);
+    if (!live) continue;
+    keep[i] = 1;
+    for (auto& r : op_arena_reads_[i]) mark(r.first, r.second);
+  }
+  size_t j = 0;
+  for (size_t i = 0; i < n; ++i)
+    if (keep[i]) P->ops[j++] = P->ops[i];
+  dead_ops_ = n - j;
+  P->ops.resize(j);
+}
+
 // Splits each op into tasks (tile x sequence group) and orders them by level.
 void Compiler::build_tasks() {
   const uint32_t B = static_cast<uint32_t>(P->batch);
@@ -1373,6 +1451,12 @@ void Compiler::build_tasks() {
       case K_MATMUL: {
         const uint32_t ntile = (op.N + 63) / 64;
         const bool shared_b = (op.b & kSharedBit) != 0;
+        if ((op.flags & F_WIDE) || (!(op.flags & F_TC) && !shared_b && op.M <= 32 && op.K <= 128 &&
+                                    op.N <= 256 && op.M % 16 == 0 && op.K % 16 == 0 && op.N % 16 == 0)) {
+          P->ops[i].flags |= F_WIDE;   // one task per sequence, every column
+          per_seq(i, 1);
+          break;
+        }
         if (op.M >= 128 || !shared_b) {
           const uint32_t mchunks = (op.M + 127) / 128;
           per_seq(i, ntile * mchunks);
@@ -1593,6 +1677,7 @@ int Compiler::compile() {
   }
   if (status == TAC_E_UNSUPPORTED || status == TAC_E_SHARED_WRITE) return status;
   finalize();
+  drop_dead_ops();
   build_tasks();
 
   tac_exec_info& I = P->info;

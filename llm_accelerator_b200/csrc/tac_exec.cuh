@@ -397,6 +397,114 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
 }
 
 // ---------------------------------------------------------------------------------
+// MATMUL with per-sequence operands, M <= 32, K <= 128, N <= 256 (F_WIDE): one
+// task computes every column of one sequence (QK^T and P.V of a head).  A and
+// B^T land in shared memory as rows of K bytes padded to the MMA's 32 plus 16
+// (so the eight rows of a fragment load sit on distinct banks); B^T is copied
+// row by row when the op holds it (F_BT), else B [K][N] is loaded and
+// transposed in 4 x 4 byte blocks.  Padding bytes are zero-filled by cp.async.
+// ---------------------------------------------------------------------------------
+__device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+  const uint32_t M = op.M, N = op.N, K = op.K, seq = t.seq0;
+  const uint32_t kc32 = (K + 31) & ~31u;
+  const uint32_t bts = kc32 + 16;
+  const uint32_t nblocks = (M + 15) / 16, n8 = (N + 7) / 8;
+  uint8_t* As = smem;                               // [nblocks * 16][bts]
+  uint8_t* Bt = As + nblocks * 16 * bts;            // [n8 * 8][bts]
+  uint8_t* Braw = Bt + n8 * 8 * bts;                // [kc32][N]
+  const uint8_t* Ag = pptr(A, op.a, seq);
+  const uint8_t* Bg = pptr(A, op.b, seq);
+  const bool bt = (op.flags & F_BT) != 0;
+  const uint32_t kv = kc32 / 16;                    // 16-byte vectors per padded row
+  for (uint32_t i = htid(); i < nblocks * 16 * kv; i += kThreads) {
+    const uint32_t r = i / kv, v = i % kv;
+    const bool in = r < M && v * 16 < K;
+    cp_async16(As + r * bts + v * 16, Ag + (in ? uint64_t(r) * K + v * 16 : 0), in ? 16u : 0u);
+  }
+  if (bt) {
+    for (uint32_t i = htid(); i < n8 * 8 * kv; i += kThreads) {
+      const uint32_t n = i / kv, v = i % kv;
+      const bool in = n < N && v * 16 < K;
+      cp_async16(Bt + n * bts + v * 16, Bg + (in ? uint64_t(n) * K + v * 16 : 0), in ? 16u : 0u);
+    }
+  } else {
+    const uint32_t nv = N / 16;
+    for (uint32_t i = htid(); i < kc32 * nv; i += kThreads) {
+      const uint32_t k = i / nv, v = i % nv;
+      const bool in = k < K;
+      cp_async16(Braw + k * N + v * 16, Bg + (in ? uint64_t(k) * N + v * 16 : 0), in ? 16u : 0u);
+    }
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  hsync();
+  if (!bt) {
+    const uint32_t nb4 = N / 4;
+    for (uint32_t i = htid(); i < (kc32 / 4) * nb4; i += kThreads) {
+      const uint32_t kb = (i / nb4) * 4, nb = (i % nb4) * 4;
+      uint32_t r[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = *reinterpret_cast<const uint32_t*>(Braw + (kb + j) * N + nb);
+      const uint32_t t0 = __byte_perm(r[0], r[1], 0x5140), t1 = __byte_perm(r[2], r[3], 0x5140);
+      const uint32_t t2 = __byte_perm(r[0], r[1], 0x7362), t3 = __byte_perm(r[2], r[3], 0x7362);
+      *reinterpret_cast<uint32_t*>(Bt + (nb + 0) * bts + kb) = __byte_perm(t0, t1, 0x5410);
+      *reinterpret_cast<uint32_t*>(Bt + (nb + 1) * bts + kb) = __byte_perm(t0, t1, 0x7632);
+      *reinterpret_cast<uint32_t*>(Bt + (nb + 2) * bts + kb) = __byte_perm(t2, t3, 0x5410);
+      *reinterpret_cast<uint32_t*>(Bt + (nb + 3) * bts + kb) = __byte_perm(t2, t3, 0x7632);
+    }
+    hsync();
+  }
+  const int warp = htid() >> 5, lane = htid() & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const uint32_t pairs = nblocks * n8;
+  int acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t p = warp + 8 * i;
+    if (p >= pairs) continue;
+    const uint32_t blk = p / n8, ns = p % n8;
+    const uint8_t* a_row0 = As + (blk * 16 + g) * bts;
+    const uint8_t* a_row8 = a_row0 + 8 * bts;
+    const uint8_t* b_col = Bt + (ns * 8 + g) * bts;
+    for (uint32_t ks = 0; ks < kc32; ks += 32) {
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(a_row0 + ks + q * 4);
+      const uint32_t a1 = *reinterpret_cast<const uint32_t*>(a_row8 + ks + q * 4);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(a_row0 + ks + 16 + q * 4);
+      const uint32_t a3 = *reinterpret_cast<const uint32_t*>(a_row8 + ks + 16 + q * 4);
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(b_col + ks + q * 4);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(b_col + ks + 16 + q * 4);
+      mma_s8(acc[i], a0, a1, a2, a3, b0, b1);
+    }
+  }
+  int32_t* D = reinterpret_cast<int32_t*>(pptr(A, op.d, seq));
+  const int32_t* C = (op.flags & F_ACCUMULATE) ? reinterpret_cast<const int32_t*>(pptr(A, op.c, seq)) : nullptr;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t p = warp + 8 * i;
+    if (p >= pairs) continue;
+    const uint32_t blk = p / n8, ns = p % n8;
+    const uint32_t col = ns * 8 + q * 2;
+    if (col >= N) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint64_t row = blk * 16 + g + 8 * h;
+      if (row >= M) continue;
+      int2 v = make_int2(acc[i][2 * h], acc[i][2 * h + 1]);
+      if (C) {
+        const int2 c = __ldcg(reinterpret_cast<const int2*>(C + row * N + col));
+        v.x = static_cast<int32_t>(static_cast<uint32_t>(v.x) + static_cast<uint32_t>(c.x));
+        v.y = static_cast<int32_t>(static_cast<uint32_t>(v.y) + static_cast<uint32_t>(c.y));
+      }
+      *reinterpret_cast<int2*>(D + row * N + col) = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
 // MATMUL with shared weights on the 5th-generation tensor cores (ops flagged
 // F_TC).  A task is up to 128 rows (the M rows of up to 128/M sequences) x 64
 // columns.  Per 128-byte K block, TMA brings A as one [128/M sequences][M
@@ -1337,6 +1445,7 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_SREG_FINAL: op_sreg_final(A, op, t); break;
     case K_MATMUL:
       if (op.flags & F_TC) op_matmul_tc(A, op, t, smem, tc, t.op);
+      else if (op.flags & F_WIDE) op_matmul_wide(A, op, t, smem);
       else op_matmul(A, op, t, smem);
       break;
     case K_TRANSPOSE: op_transpose(A, op, t, smem); break;
@@ -1379,6 +1488,8 @@ constexpr size_t kExecOpSmem = kExecOpSmem0 > kTcSmem ? kExecOpSmem0 : kTcSmem;
 constexpr size_t kExecSmem = kHalves * kExecOpSmem + kHalves * 128;
 static_assert(sizeof(TcShared) <= 128, "TcShared outgrew its slot");
 static_assert(kStageBytes <= kExecOpSmem, "element-wise staging exceeds the op shared memory");
+// op_matmul_wide at its limits (M 32, K 128, N 256): A + B^T rows + raw B
+static_assert(32 * 144 + 256 * 144 + 128 * 256 <= kExecOpSmem, "wide MATMUL exceeds the op shared memory");
 static_assert(kSegTableOff + kMaxSegRuns * 12 <= kExecOpSmem, "segment table exceeds the op shared memory");
 static_assert(kExecOpSmem % 1024 == 0 || kTcSmem <= kExecOpSmem, "half regions must keep the stage alignment slack");
 static_assert(kExecSmem <= 227 * 1024, "executor shared memory exceeds one CTA's limit");

@@ -70,6 +70,9 @@ constexpr uint16_t F_TC = 8;           // MATMUL with shared weights on tcgen05,
 constexpr uint16_t F_SPLIT = 16;       // DEQUANT_SCALED / LAYERNORM: second half of the [scale|bias]
                                        // ([gamma|beta]) vector at operand c instead of b + N
 constexpr uint16_t F_SEGA = 32;        // MAX_ABS / QUANT / VADD_F16: operand a is the segment list
+constexpr uint16_t F_WIDE = 64;        // MATMUL (per-sequence operands, M <= 32, K <= 128, N <= 256):
+                                       // one task per sequence covers every column
+constexpr uint16_t F_BT = 128;         // MATMUL: operand b holds B transposed, [N][K] row-major
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 
 // Most runs an operand read through a segment list may have (longer lists are gathered).
