@@ -185,6 +185,12 @@ int tac_check_device_status(tac_engine* e, tac_fault* fault);
  * host into params_out[batch][tac_program_param_count(p)] (no GPU needed);
  * tac_run_async_params runs with those parameters already in device memory. */
 uint64_t tac_program_param_count(const tac_program* p);
+
+/* The fewest softmax key columns any runtime-configured masked softmax of the
+ * stream has (0 when none): a valid_kv_len, and so a decode position, must
+ * fit them.  A runner uses it to bound the runtime KV-cache addresses it
+ * declares (no reference counterpart; no GPU needed). */
+uint32_t tac_program_attn_key_cols(const tac_program* p);
 int tac_encode_params(const tac_program* p, int batch, const uint64_t* var_words, uint64_t* params_out,
                       tac_fault* fault);
 int tac_run_async_params(tac_engine* e, tac_program* p, const uint64_t* params_dev, void* stream,

@@ -76,6 +76,7 @@ SIGNATURES = {
     "tac_run": (_I, [_P, _P, _P, C.POINTER(Fault)]),
     "tac_check_device_status": (_I, [_P, C.POINTER(Fault)]),
     "tac_program_param_count": (_U64, [_P]),
+    "tac_program_attn_key_cols": (C.c_uint32, [_P]),
     "tac_encode_params": (_I, [_P, _I, _P, _P, C.POINTER(Fault)]),
     "tac_run_async_params": (_I, [_P, _P, _P, _P, C.POINTER(Fault)]),
     "tac_argmax_f16": (_I, [_P, _U64, _U64, _P, _P]),

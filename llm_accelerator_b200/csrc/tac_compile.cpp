@@ -272,6 +272,11 @@ class Compiler {
     op_arena_reads_.push_back(std::move(ar));
     op_arena_writes_.push_back(std::move(aw));
     op_pure_.push_back(pure ? 1 : 0);
+    for (auto& w : a.writes)
+      if (cls(w.first) == PC_HOME_RW) {
+        ++home_writes_;
+        break;
+      }
     pending_same_.clear();
     int32_t L = level_for(a);
     commit(a, L);
@@ -431,17 +436,36 @@ class Compiler {
     if (!key.empty()) cse_[key] = idx;
   }
 
-  // Operand B of a small per-sequence MATMUL that is the transpose of an
-  // immutable [N][K] extent: read that extent directly (F_BT), so the MATMUL
-  // needs neither the TRANSPOSE's output nor a transpose of its own.
-  bool bt_source(uint32_t u0, uint32_t M, uint32_t N, uint32_t K, Access& acc, DevOp& op) {
-    if (M == 0 || M > 32 || K == 0 || K > 128 || N == 0 || N > 256 || M % 16 || K % 16 || N % 16) return false;
+  // Operand B of a small per-sequence MATMUL (the wide task shape).  When B
+  // is the transpose of an immutable [N][K] extent, that extent is read
+  // directly (F_BT); when B (or that extent) is the output of a QUANT whose
+  // FP16 source still holds the same bytes, the MATMUL quantises the source
+  // itself (F_QB, register in s[1]).  The TRANSPOSE and QUANT outputs then go
+  // unread and their ops are dropped.  Returns false for an ordinary operand.
+  bool mm_b_source(uint32_t u0, uint32_t M, uint32_t N, uint32_t K, Access& acc, DevOp& op) {
+    if (!wide_mm_ok(M, N, K, true, false)) return false;
     const uint64_t n = uint64_t(K) * N / kUnit;
     const uint64_t* m = &sram_[u0];
     if (!contiguous(m, n)) return false;
-    auto it = transposed_.find(m[0]);
-    if (it == transposed_.end() || it->second.rows != N || it->second.cols != K) return false;
-    op.b = it->second.src;
+    uint64_t key = m[0];
+    bool bt = false;
+    auto it = transposed_.find(key);
+    if (it != transposed_.end() && it->second.rows == N && it->second.cols == K) {
+      key = it->second.src;
+      bt = true;
+    }
+    auto q = quantized_.find(key);
+    if (q != quantized_.end() && q->second.rows * q->second.cols == uint64_t(K) * N &&
+        (cls(q->second.src) != PC_HOME_RW || q->second.epoch == home_writes_) && wide_mm_ok(M, N, K, bt, true)) {
+      op.b = q->second.src;
+      op.s[1] = q->second.scale;
+      read_sreg(acc, op.s[1]);
+      op.flags |= F_QB | F_WIDE | (bt ? F_BT : 0);
+      acc.reads.push_back({op.b, 2 * n});
+      return true;
+    }
+    if (!bt) return false;
+    op.b = key;
     op.flags |= F_BT | F_WIDE;   // only the wide MATMUL reads B^T
     acc.reads.push_back({op.b, n});
     return true;
@@ -661,6 +685,16 @@ class Compiler {
     uint64_t rows, cols;
   };
   std::unordered_map<uint64_t, TransposeOf> transposed_;
+  // arena extents written by (non-segmented) QUANT ops -> FP16 source, register, shape,
+  // and the count of writable-DRAM writes emitted before it (a source there must be unchanged)
+  struct QuantOf {
+    uint64_t src;
+    uint32_t scale;
+    uint64_t rows, cols;
+    uint64_t epoch;
+  };
+  std::unordered_map<uint64_t, QuantOf> quantized_;
+  uint64_t home_writes_ = 0;
   // per emitted op: its arena reads and writes, and whether arena writes are its only effect
   std::vector<std::vector<std::pair<uint64_t, uint64_t>>> op_arena_reads_, op_arena_writes_;
   std::vector<uint8_t> op_pure_;
@@ -714,15 +748,15 @@ int Compiler::effective_address(const Insn& x, uint64_t nbytes, bool& dynamic, u
   }
   dynamic = true;
   param = r.param;
+  // [lo, hi): the bytes the access may touch.  The site's value lies in its
+  // symbol's extent [range_lo, range_hi) and the whole access must stay in
+  // that extent shifted by the instruction's offset; the run-time check
+  // enforces it (a value outside asks for a recompile).  Runtime addresses
+  // that overflow DRAM fail the same check and are recompiled statically to
+  // raise the exact fault.
   lo = r.lo + off;
-  hi = r.hi + off;  // exclusive bound on the start address
-  uint64_t last = hi + nbytes;
-  if (last > dram_bytes_) {
-    // Runtime addresses that overflow DRAM are caught by the run-time check and
-    // recompiled statically to raise the exact fault.
-    hi = dram_bytes_ >= nbytes ? dram_bytes_ - nbytes + 1 : 0;
-    if (hi < lo) hi = lo;
-  }
+  hi = std::max(r.hi + off, lo + nbytes);
+  if (hi > dram_bytes_) hi = std::max<uint64_t>(dram_bytes_, lo + nbytes);
   RtCheck c{};
   c.kind = CHK_ADDR;
   c.param = static_cast<uint32_t>(param);
@@ -766,13 +800,13 @@ int Compiler::h_load(const Insn& x) {                       // dma.py:27-44
     return 0;
   }
   // Runtime address: copy into a fresh extent.
-  bool in_shared = hi + n <= shared_bytes_;
+  bool in_shared = hi <= shared_bytes_;
   bool in_rw = lo >= shared_bytes_;
   if (!in_shared && !in_rw) return unsupported("runtime-addressed LOAD straddles the shared DRAM region");
   Access acc;
   if (in_rw) {
     uint64_t i0 = (lo - shared_bytes_) / kUnit;
-    uint64_t i1 = std::min<uint64_t>(rw_units_, (hi + n - shared_bytes_ + kUnit - 1) / kUnit);
+    uint64_t i1 = std::min<uint64_t>(rw_units_, (hi - shared_bytes_ + kUnit - 1) / kUnit);
     flush_rw(i0, i1);
     acc.reads.push_back({rw_home(i0), i1 - i0});
     acc.dyn_param = param;
@@ -810,7 +844,7 @@ int Compiler::h_store(const Insn& x) {                      // dma.py:47-64
     return 0;
   }
   uint64_t i0 = (lo - shared_bytes_) / kUnit;
-  uint64_t i1 = std::min<uint64_t>(rw_units_, (hi + n - shared_bytes_ + kUnit - 1) / kUnit);
+  uint64_t i1 = std::min<uint64_t>(rw_units_, (hi - shared_bytes_ + kUnit - 1) / kUnit);
   flush_rw(i0, i1);
   break_aliases(i0, i1);
   Access acc;
@@ -991,7 +1025,7 @@ int Compiler::h_rtype(const Insn& x) {
       TRY(span(x.dst_buf, x.dst_off, M * N * 4));
       op.kind = K_MATMUL;
       op.a = src(s1, M * K, acc);
-      if (!bt_source(s2, M, N, K, acc, op)) op.b = src(s2, K * N, acc);
+      if (!mm_b_source(s2, M, N, K, acc, op)) op.b = src(s2, K * N, acc);
       if (x.flags & 1) {
         op.flags |= F_ACCUMULATE;
         op.c = src(d, M * N * 4, acc);
@@ -1230,6 +1264,8 @@ int Compiler::h_rtype(const Insn& x) {
   }
 #undef TRY
   emit_compute(op, acc, d, x.sreg);
+  if (op.kind == K_QUANT && !(op.flags & F_SEGA) && cls(sram_[d]) == PC_ARENA)
+    quantized_[sram_[d]] = QuantOf{op.a, op.s[0], M, N, home_writes_};
   return 0;
 }
 
@@ -1419,6 +1455,7 @@ void Compiler::build_tasks() {
     if (op.kind == K_MATMUL && (op.b & kSharedBit) && !(op.a & kSharedBit) && op.M < 128 && op.M % 16 == 0 &&
         op.N % 16 == 0 && op.K % 16 == 0 && op.M > 0 && op.N > 0 && op.K > 0) {
       op.flags |= F_TC;
+      if (op.N >= 128) op.flags |= F_TC128;
       op.seg0 = P->n_tc++;
       op.nseg = 0;
     }
@@ -1451,8 +1488,7 @@ void Compiler::build_tasks() {
       case K_MATMUL: {
         const uint32_t ntile = (op.N + 63) / 64;
         const bool shared_b = (op.b & kSharedBit) != 0;
-        if ((op.flags & F_WIDE) || (!(op.flags & F_TC) && !shared_b && op.M <= 32 && op.K <= 128 &&
-                                    op.N <= 256 && op.M % 16 == 0 && op.K % 16 == 0 && op.N % 16 == 0)) {
+        if ((op.flags & F_WIDE) || (!(op.flags & F_TC) && !shared_b && wide_mm_ok(op.M, op.N, op.K, false, false))) {
           P->ops[i].flags |= F_WIDE;   // one task per sequence, every column
           per_seq(i, 1);
           break;
@@ -1462,8 +1498,9 @@ void Compiler::build_tasks() {
           per_seq(i, ntile * mchunks);
         } else {
           const uint32_t spt = std::max<uint32_t>(1, 128 / op.M);
+          const uint32_t nt = (op.flags & F_TC128) ? (op.N + 127) / 128 : ntile;
           for (uint32_t s = 0; s < B; s += spt)
-            for (uint32_t t = 0; t < ntile; ++t)
+            for (uint32_t t = 0; t < nt; ++t)
               per_level[op.level].push_back(Task{i, s, std::min(spt, B - s), t, 0});
         }
         break;
@@ -1481,9 +1518,11 @@ void Compiler::build_tasks() {
         break;
       case K_LAYERNORM_F16: case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16:
       case K_LN_I8: case K_SOFTMAX_I8: case K_MASKED_SOFTMAX_I8:
-      case K_SOFTMAX_ATTNV: case K_MASKED_SOFTMAX_ATTNV:
-        per_seq(i, (op.M + 7) / 8);   // one warp per row, 8 rows per task
+      case K_SOFTMAX_ATTNV: case K_MASKED_SOFTMAX_ATTNV: {
+        const uint32_t rpt = row_task_rows(op.kind, op.N);   // one warp per row, 8 or 16 rows per task
+        per_seq(i, (op.M + rpt - 1) / rpt);
         break;
+      }
       case K_TRANSPOSE:
         per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + 16383) / 16384)));
         break;
@@ -1567,10 +1606,11 @@ void Compiler::prefetch_hint(const DevOp& op, Task& t) const {
         break;
       case K_LAYERNORM_F16: case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16: {
         const uint64_t row_units = uint64_t(op.N) * 2 / kUnit;
-        const uint64_t r0 = uint64_t(t.tile) * 8;
+        const uint64_t rpt = row_task_rows(op.kind, op.N);
+        const uint64_t r0 = uint64_t(t.tile) * rpt;
         if (r0 < op.M && op.N % 8 == 0) {
           phys = op.a + r0 * row_units;
-          units = std::min<uint64_t>(8, op.M - r0) * row_units;
+          units = std::min<uint64_t>(rpt, op.M - r0) * row_units;
         }
         break;
       }

@@ -152,11 +152,13 @@ int ensure_maps(tac_engine* e, tac_program* p, tac_fault* f) {
     const cuuint64_t adims[3] = {op.K, op.M, cuuint64_t(e->batch)};
     const cuuint64_t astr[2] = {op.K, e->seq_stride};
     const cuuint32_t abox[3] = {128, op.M, 128 / op.M};
+    const bool wide = (op.flags & F_TC128) != 0;   // 128-column tiles: 128-byte swizzle, else 64
     const cuuint64_t bdims[2] = {op.N, op.K};
     const cuuint64_t bstr[1] = {op.N};
-    const cuuint32_t bbox[2] = {64, 128};
+    const cuuint32_t bbox[2] = {wide ? 128u : 64u, 128};
     if (!tmap_encode_u8(&maps[2 * op.seg0], a, 3, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !tmap_encode_u8(&maps[2 * op.seg0 + 1], b, 2, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_64B))
+        !tmap_encode_u8(&maps[2 * op.seg0 + 1], b, 2, bdims, bstr, bbox,
+                        wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
       return set_fault(f, TAC_E_CUDA, "cuTensorMapEncodeTiled rejected a MATMUL operand map");
   }
   if (!p->d_maps) CK(cudaMalloc(&p->d_maps, maps.size() * sizeof(CUtensorMap)), f, "cudaMalloc tensor maps");
@@ -193,8 +195,7 @@ int decode_params(const tac_program* p, const uint64_t* words, uint64_t* params,
     bool ok = true;
     if (c.kind == CHK_ADDR) {
       const uint64_t a = v + static_cast<uint64_t>(c.dconst);
-      ok = (a % 16 == 0 || c.nbytes == 0) && a >= c.lo && a < std::max(c.hi, c.lo + 1) &&
-           a + c.nbytes <= p->dram_bytes;
+      ok = (a % 16 == 0 || c.nbytes == 0) && a >= c.lo && a + c.nbytes <= c.hi && a + c.nbytes <= p->dram_bytes;
     } else if (c.kind == CHK_SAME) {
       ok = c.lo < p->vars.size() && v == params[c.lo];
     } else {
@@ -429,6 +430,14 @@ static int launch(tac_engine* e, tac_program* p, const uint64_t* d_params, cudaS
 }
 
 uint64_t tac_program_param_count(const tac_program* p) { return p ? std::max<uint32_t>(p->n_params, 1) : 0; }
+
+uint32_t tac_program_attn_key_cols(const tac_program* p) {
+  if (!p) return 0;
+  uint64_t keys = 0;
+  for (const RtCheck& c : p->checks)
+    if (c.kind == CHK_ATTN_KEYS && (keys == 0 || c.lo < keys)) keys = c.lo;
+  return static_cast<uint32_t>(keys);
+}
 
 int tac_encode_params(const tac_program* p, int batch, const uint64_t* var_words, uint64_t* out, tac_fault* f) {
   if (!p || !out || batch <= 0 || (p->n_var_words && !var_words)) return set_fault(f, TAC_E_ARGUMENT, "bad arguments");

@@ -397,31 +397,76 @@ __device__ __noinline__ void op_matmul(const ExecArgs& A, const DevOp& op, const
 }
 
 // ---------------------------------------------------------------------------------
-// MATMUL with per-sequence operands, M <= 32, K <= 128, N <= 256 (F_WIDE): one
-// task computes every column of one sequence (QK^T and P.V of a head).  A and
-// B^T land in shared memory as rows of K bytes padded to the MMA's 32 plus 16
-// (so the eight rows of a fragment load sit on distinct banks); B^T is copied
-// row by row when the op holds it (F_BT), else B [K][N] is loaded and
-// transposed in 4 x 4 byte blocks.  Padding bytes are zero-filled by cp.async.
+// Small vector helpers: 16-byte loads through L2 and lane views of packed values.
+// ---------------------------------------------------------------------------------
+struct V8 { uint4 lo, hi; };   // 8 x 32-bit values
+
+// Operands are written by other CTAs in earlier levels of the same launch, so
+// loads go through L2 (ld.global.cg), never the non-coherent read-only path.
+__device__ __forceinline__ uint4 ld16(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ uint2 ld8(const void* p) { return __ldcg(reinterpret_cast<const uint2*>(p)); }
+__device__ __forceinline__ V8 ld32(const void* p) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+  return V8{__ldcg(q), __ldcg(q + 1)};
+}
+__device__ __forceinline__ uint16_t h_at(const uint4& v, int j) {
+  const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
+  return static_cast<uint16_t>(j & 1 ? w >> 16 : w & 0xFFFF);
+}
+__device__ __forceinline__ int32_t i_at(const V8& v, int j) {
+  const uint4& q = j < 4 ? v.lo : v.hi;
+  const int k = j & 3;
+  return static_cast<int32_t>(k == 0 ? q.x : k == 1 ? q.y : k == 2 ? q.z : q.w);
+}
+__device__ __forceinline__ int8_t b_at(const uint2& v, int j) {
+  const uint32_t w = j < 4 ? v.x : v.y;
+  return static_cast<int8_t>((w >> (8 * (j & 3))) & 0xFF);
+}
+__device__ __forceinline__ uint4 pack_h(const uint16_t (&h)[8]) {
+  return make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                    h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+}
+__device__ __forceinline__ uint2 pack_b(const int8_t (&q)[8]) {
+  uint32_t x = 0, y = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    x |= uint32_t(uint8_t(q[j])) << (8 * j);
+    y |= uint32_t(uint8_t(q[j + 4])) << (8 * j);
+  }
+  return make_uint2(x, y);
+}
+
+// ---------------------------------------------------------------------------------
+// MATMUL with per-sequence operands in the wide shape (F_WIDE: M <= 32,
+// K <= 256, N <= 256, shared memory by wide_mm_smem): one task computes every
+// column of one sequence (QK^T and P.V of a head).  A and B^T land in shared
+// memory as rows of K bytes padded to the MMA's 32 plus 16 (so the eight rows
+// of a fragment load sit on distinct banks).  B^T is copied row by row when
+// the op holds it (F_BT), else B [K][N] is loaded and transposed in 4 x 4 byte
+// blocks.  With F_QB, B arrives as FP16 and is quantised on the way in, with
+// QUANT's rule.  Padding bytes are zero.
 // ---------------------------------------------------------------------------------
 __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
   const uint32_t M = op.M, N = op.N, K = op.K, seq = t.seq0;
   const uint32_t kc32 = (K + 31) & ~31u;
   const uint32_t bts = kc32 + 16;
   const uint32_t nblocks = (M + 15) / 16, n8 = (N + 7) / 8;
+  const bool bt = (op.flags & F_BT) != 0, qb = (op.flags & F_QB) != 0;
   uint8_t* As = smem;                               // [nblocks * 16][bts]
   uint8_t* Bt = As + nblocks * 16 * bts;            // [n8 * 8][bts]
-  uint8_t* Braw = Bt + n8 * 8 * bts;                // [kc32][N]
+  uint8_t* Braw = Bt + n8 * 8 * bts;                // [kc32][N] (not F_BT)
+  uint8_t* Bh = Braw + (bt ? 0u : kc32 * N);        // FP16 B (F_QB)
   const uint8_t* Ag = pptr(A, op.a, seq);
   const uint8_t* Bg = pptr(A, op.b, seq);
-  const bool bt = (op.flags & F_BT) != 0;
   const uint32_t kv = kc32 / 16;                    // 16-byte vectors per padded row
   for (uint32_t i = htid(); i < nblocks * 16 * kv; i += kThreads) {
     const uint32_t r = i / kv, v = i % kv;
     const bool in = r < M && v * 16 < K;
     cp_async16(As + r * bts + v * 16, Ag + (in ? uint64_t(r) * K + v * 16 : 0), in ? 16u : 0u);
   }
-  if (bt) {
+  if (qb) {
+    for (uint32_t i = htid(); i < K * N / 8; i += kThreads) cp_async16(Bh + i * 16, Bg + uint64_t(i) * 16, 16u);
+  } else if (bt) {
     for (uint32_t i = htid(); i < n8 * 8 * kv; i += kThreads) {
       const uint32_t n = i / kv, v = i % kv;
       const bool in = n < N && v * 16 < K;
@@ -436,8 +481,38 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
     }
   }
   cp_async_commit();
+  const uint16_t sb = qb ? sreg_bits(A, op.s[1], seq) : uint16_t(0);
   cp_async_wait<0>();
   hsync();
+  if (qb) {
+    // QUANT's rule: rint(x * s), NaN -> 0, clipped to int8; 8 elements per step
+    const float s1 = h2f(sb);
+    for (uint32_t i = htid(); i < K * N / 8; i += kThreads) {
+      const uint4 x = *reinterpret_cast<const uint4*>(Bh + i * 16);
+      int8_t q8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float r = rintf(__fmul_rn(h2f(h_at(x, j)), s1));
+        q8[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+      }
+      const uint32_t e = i * 8;
+      uint8_t* dst = bt ? Bt + (e / K) * bts + (e % K) : Braw + e;   // [N][K] rows or [K][N]
+      *reinterpret_cast<uint2*>(dst) = pack_b(q8);
+    }
+    // zero padding: B^T columns K .. kc32 of every row, or raw rows K .. kc32
+    if (kc32 > K) {
+      if (bt) {
+        for (uint32_t i = htid(); i < n8 * 8 * ((kc32 - K) / 16); i += kThreads) {
+          const uint32_t n = i / ((kc32 - K) / 16), v = i % ((kc32 - K) / 16);
+          *reinterpret_cast<uint4*>(Bt + n * bts + K + v * 16) = make_uint4(0, 0, 0, 0);
+        }
+      } else {
+        for (uint32_t i = htid(); i < (kc32 - K) * N / 16; i += kThreads)
+          *reinterpret_cast<uint4*>(Braw + K * N + i * 16) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    hsync();
+  }
   if (!bt) {
     const uint32_t nb4 = N / 4;
     for (uint32_t i = htid(); i < (kc32 / 4) * nb4; i += kThreads) {
@@ -515,12 +590,15 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
 // that read it have committed.  The eight warps read the int32 accumulator
 // back with tcgen05.ld.  Waits are bounded (DF_MMA_TIMEOUT).
 // ---------------------------------------------------------------------------------
-constexpr int kTcStages = 3;
+constexpr int kTcStages = 3;                            // stage slots (64-column tasks use 3, 128-column 2)
 constexpr uint32_t kTcAStage = 128 * 128;
-constexpr uint32_t kTcBStage = 128 * 64;
-constexpr uint32_t kTcStage = kTcAStage + kTcBStage;   // a multiple of 1024
-constexpr uint32_t kTcCols = 64;
+constexpr uint32_t kTcBStage = 128 * 64;                // 64 columns x 128 K rows
+constexpr uint32_t kTcStage = kTcAStage + kTcBStage;    // a multiple of 1024
+constexpr uint32_t kTcStage128 = kTcAStage + 128 * 128; // 128-column stage
+constexpr uint32_t kTcCols = 128;                       // TMEM columns per half
 constexpr uint32_t kTcIdesc = sm100::idesc_i8(128, 64, 1);
+constexpr uint32_t kTcIdesc128 = sm100::idesc_i8(128, 128, 1);
+
 
 struct TcShared {
   uint64_t full[kTcStages];    // TMA bytes of a stage landed
@@ -538,60 +616,13 @@ __device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr, uint32_t lbo, uint
          (uint64_t((sbo >> 4) & 0x3FFF) << 32) | (uint64_t(1) << 46) | (uint64_t(4) << 61);
 }
 
-__device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
-                                          TcShared* tc, uint32_t opi) {
-  const uint32_t M = op.M, N = op.N, K = op.K;
-  const uint32_t n0 = t.tile * 64;
-  const uint32_t ncols = N - n0 < 64 ? N - n0 : 64;
-  const uint32_t rows = t.nseq * M;                       // <= 128
-  const uint32_t nchunks = (K + 127) / 128;
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023));
-  if (htid() == 0) {
-    const CUtensorMap* ma = A.tmaps + 2 * op.seg0;
-    const CUtensorMap* mb = ma + 1;
-    const uint32_t bytes = (128 / M) * M * 128 + kTcBStage;
-    uint32_t pf = tc->phase_full, pe = tc->phase_empty;
-    bool ok = true;
-    auto load = [&](uint32_t c) {
-      const uint32_t st = c % kTcStages;
-      uint8_t* as = base + st * kTcStage;
-      sm100::mbar_arrive_expect_tx(&tc->full[st], bytes);
-      sm100::tma_load_3d(as, ma, int32_t(c * 128), 0, int32_t(t.seq0), &tc->full[st]);
-      sm100::tma_load_2d(as + kTcAStage, mb, int32_t(n0), int32_t(c * 128), &tc->full[st]);
-    };
-    auto wait = [&](uint64_t* bar, uint32_t& ph, uint32_t st) {
-      if (!sm100::mbar_wait(&bar[st], (ph >> st) & 1u, nullptr, 0)) ok = false;
-      ph ^= 1u << st;
-    };
-    sm100::fence_proxy_async();   // A was written by generic stores in earlier levels
-    for (uint32_t c = 0; c < nchunks && c < uint32_t(kTcStages); ++c) load(c);
-    for (uint32_t c = 0; c < nchunks; ++c) {
-      const uint32_t st = c % kTcStages;
-      wait(tc->full, pf, st);
-      sm100::tc_fence_after();
-      const uint32_t a_addr = sm100::smem_u32(base + st * kTcStage), b_addr = a_addr + kTcAStage;
-      const uint32_t kc = K - c * 128 < 128 ? K - c * 128 : 128;
-      for (uint32_t ks = 0; ks * 32 < kc; ++ks)
-        sm100::mma_i8(tc->tmem, sm100::smem_desc_sw128(a_addr + ks * 32, 16, 1024),
-                      desc_sw64(b_addr + ks * 2048, 16, 512), kTcIdesc, (c | ks) != 0);
-      sm100::mma_commit(&tc->empty[st]);
-      if (c + kTcStages < nchunks) {   // refill this stage once its MMAs are done
-        wait(tc->empty, pe, st);
-        load(c + kTcStages);
-      }
-    }
-    // the commits not yet waited: every MMA of the task is done after these
-    for (uint32_t j = nchunks > uint32_t(kTcStages) ? nchunks - kTcStages : 0; j < nchunks; ++j)
-      wait(tc->empty, pe, j % kTcStages);
-    tc->phase_full = pf;
-    tc->phase_empty = pe;
-    if (!ok) raise_fault(A, DF_MMA_TIMEOUT, opi, t.seq0);
-  }
-  hsync();
-  sm100::tc_fence_after();
-
-  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31, columns 32 (w / 4) .. +31
-  const uint32_t warp = htid() >> 5, lane = htid() & 31, q = warp & 3, h = warp >> 2;
+// One warp's slice of the tcgen05 MATMUL epilogue: TMEM lanes 32q..32q+31,
+// columns 32h..32h+31 of the task's tile, to int32 rows (plus the previous
+// int32 tile when F_ACCUMULATE).
+__device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp& op, const Task& t, TcShared* tc,
+                                                  uint32_t q, uint32_t lane, uint32_t h, uint32_t n0,
+                                                  uint32_t ncols, uint32_t rows) {
+  const uint32_t M = op.M, N = op.N;
   uint32_t v[32];
   __syncwarp();
   sm100::tmem_ld32(tc->tmem + ((q * 32) << 16) + h * 32, v);
@@ -619,10 +650,80 @@ __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, co
       }
     }
   }
+}
+
+__device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
+                                          TcShared* tc, uint32_t opi) {
+  const uint32_t M = op.M, N = op.N, K = op.K;
+  // tile width: 128 columns (B box 128 x 128, 128-byte swizzle, two 32 KB
+  // stages) or 64 (B box 64 x 128, 64-byte swizzle, three 24 KB stages)
+  const bool w128 = (op.flags & F_TC128) != 0;
+  const uint32_t tn = w128 ? 128u : 64u;
+  const uint32_t nst = w128 ? 2u : uint32_t(kTcStages);
+  const uint32_t stage_bytes = w128 ? kTcStage128 : kTcStage;
+  const uint32_t n0 = t.tile * tn;
+  const uint32_t ncols = N - n0 < tn ? N - n0 : tn;
+  const uint32_t rows = t.nseq * M;                       // <= 128
+  const uint32_t nchunks = (K + 127) / 128;
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023));
+  if (htid() == 0) {
+    const CUtensorMap* ma = A.tmaps + 2 * op.seg0;
+    const CUtensorMap* mb = ma + 1;
+    const uint32_t bytes = (128 / M) * M * 128 + tn * 128;
+    uint32_t pf = tc->phase_full, pe = tc->phase_empty;
+    bool ok = true;
+    auto load = [&](uint32_t c) {
+      const uint32_t st = c % nst;
+      uint8_t* as = base + st * stage_bytes;
+      sm100::mbar_arrive_expect_tx(&tc->full[st], bytes);
+      sm100::tma_load_3d(as, ma, int32_t(c * 128), 0, int32_t(t.seq0), &tc->full[st]);
+      sm100::tma_load_2d(as + kTcAStage, mb, int32_t(n0), int32_t(c * 128), &tc->full[st]);
+    };
+    auto wait = [&](uint64_t* bar, uint32_t& ph, uint32_t st) {
+      if (!sm100::mbar_wait(&bar[st], (ph >> st) & 1u, nullptr, 0)) ok = false;
+      ph ^= 1u << st;
+    };
+    sm100::fence_proxy_async();   // A was written by generic stores in earlier levels
+    for (uint32_t c = 0; c < nchunks && c < nst; ++c) load(c);
+    for (uint32_t c = 0; c < nchunks; ++c) {
+      const uint32_t st = c % nst;
+      wait(tc->full, pf, st);
+      sm100::tc_fence_after();
+      const uint32_t a_addr = sm100::smem_u32(base + st * stage_bytes), b_addr = a_addr + kTcAStage;
+      const uint32_t kc = K - c * 128 < 128 ? K - c * 128 : 128;
+      for (uint32_t ks = 0; ks * 32 < kc; ++ks) {
+        // B: MN-major rows (one per K) of 64 or 128 bytes, 8-K groups of 512 or 1024 B;
+        // a step of 32 K rows is 2 or 4 KB
+        const uint64_t db = w128 ? sm100::smem_desc_sw128(b_addr + ks * 4096, 16384, 1024)
+                                 : desc_sw64(b_addr + ks * 2048, 16, 512);
+        sm100::mma_i8(tc->tmem, sm100::smem_desc_sw128(a_addr + ks * 32, 16, 1024), db,
+                      w128 ? kTcIdesc128 : kTcIdesc, (c | ks) != 0);
+      }
+      sm100::mma_commit(&tc->empty[st]);
+      if (c + nst < nchunks) {   // refill this stage once its MMAs are done
+        wait(tc->empty, pe, st);
+        load(c + nst);
+      }
+    }
+    // the commits not yet waited: every MMA of the task is done after these
+    for (uint32_t j = nchunks > nst ? nchunks - nst : 0; j < nchunks; ++j) wait(tc->empty, pe, j % nst);
+    tc->phase_full = pf;
+    tc->phase_empty = pe;
+    if (!ok) raise_fault(A, DF_MMA_TIMEOUT, opi, t.seq0);
+  }
+  hsync();
+  sm100::tc_fence_after();
+
+  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31; with 64 columns it
+  // takes columns 32 (w / 4) .. +31, with 128 columns two such slices
+  const uint32_t warp = htid() >> 5, lane = htid() & 31, q = warp & 3;
+  for (uint32_t hh = warp >> 2; hh * 32 < tn; hh += 2)
+    tc_epilogue_slice(A, op, t, tc, q, lane, hh, n0, ncols, rows);
   // the next tcgen05 MATMUL overwrites the accumulator only after every warp read it
   sm100::tc_fence_before();
   hsync();
 }
+
 
 // ---------------------------------------------------------------------------------
 // Element-wise ops.  A task covers kEwTask elements of one sequence; each
@@ -634,42 +735,7 @@ constexpr uint32_t kEwGroups = 4;                       // groups of 8 per threa
 constexpr uint32_t kEwTask = kThreads * kEwGroups * 8;   // 8192 elements per task
 static_assert(kEwTask == kEwTaskElems, "host and device element-wise task sizes differ");
 
-struct V8 { uint4 lo, hi; };   // 8 x 32-bit values
 
-// Operands are written by other CTAs in earlier levels of the same launch, so
-// loads go through L2 (ld.global.cg), never the non-coherent read-only path.
-__device__ __forceinline__ uint4 ld16(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
-__device__ __forceinline__ uint2 ld8(const void* p) { return __ldcg(reinterpret_cast<const uint2*>(p)); }
-__device__ __forceinline__ V8 ld32(const void* p) {
-  const uint4* q = reinterpret_cast<const uint4*>(p);
-  return V8{__ldcg(q), __ldcg(q + 1)};
-}
-__device__ __forceinline__ uint16_t h_at(const uint4& v, int j) {
-  const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
-  return static_cast<uint16_t>(j & 1 ? w >> 16 : w & 0xFFFF);
-}
-__device__ __forceinline__ int32_t i_at(const V8& v, int j) {
-  const uint4& q = j < 4 ? v.lo : v.hi;
-  const int k = j & 3;
-  return static_cast<int32_t>(k == 0 ? q.x : k == 1 ? q.y : k == 2 ? q.z : q.w);
-}
-__device__ __forceinline__ int8_t b_at(const uint2& v, int j) {
-  const uint32_t w = j < 4 ? v.x : v.y;
-  return static_cast<int8_t>((w >> (8 * (j & 3))) & 0xFF);
-}
-__device__ __forceinline__ uint4 pack_h(const uint16_t (&h)[8]) {
-  return make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
-                    h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
-}
-__device__ __forceinline__ uint2 pack_b(const int8_t (&q)[8]) {
-  uint32_t x = 0, y = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    x |= uint32_t(uint8_t(q[j])) << (8 * j);
-    y |= uint32_t(uint8_t(q[j + 4])) << (8 * j);
-  }
-  return make_uint2(x, y);
-}
 
 // A task covers kEwTask elements of one sequence (t.nseq == 1, chunk t.tile)
 // or, for small ops, t.nseq whole sequences (t.nseq * M * N <= kEwTask) whose
@@ -680,10 +746,12 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
   const uint32_t N = op.N;
   const uint32_t MN = op.M * N;
   constexpr uint32_t kTask = ew_task_elems(KIND);
-  constexpr uint32_t kGroups = kTask / (kThreads * 8);   // groups of 8 per thread
-  static_assert(kGroups >= 1 && kGroups <= kEwGroups, "element-wise task size");
+  // a task larger than kEwTask runs as consecutive chunks of kEwTask elements
+  constexpr uint32_t kChunk = kTask < kEwTask ? kTask : kEwTask;
+  constexpr uint32_t kGroups = kChunk / (kThreads * 8);   // groups of 8 per thread
+  static_assert(kGroups >= 1 && kGroups <= kEwGroups && kTask % kChunk == 0, "element-wise task size");
   const bool packed = t.nseq > 1;
-  const uint32_t base = packed ? 0u : t.tile * kTask;
+  const uint32_t task_base = packed ? 0u : t.tile * kTask;
   const uint32_t span = packed ? t.nseq * MN : MN;
   const uint8_t* __restrict__ a0 = pptr(A, op.a, t.seq0);
   const uint8_t* __restrict__ b0 = pptr(A, op.b, t.seq0);
@@ -691,156 +759,158 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
   const uint64_t sa = (op.a & kSharedBit) ? 0 : A.seq_stride;
   const uint64_t sb = (op.b & kSharedBit) ? 0 : A.seq_stride;
   const uint64_t sd = (op.d & kSharedBit) ? 0 : A.seq_stride;
-  // phase 1: loads
-  uint4 ra[kEwGroups], rb[kEwGroups], rc[kEwGroups];
-  V8 ia[kEwGroups];
-  uint2 qa[kEwGroups], qb[kEwGroups];
-  uint32_t e0[kEwGroups], sq[kEwGroups];
-  // raw FP16 register bits: converted only in phase 2, so no load of phase 1
-  // waits for another
-  uint16_t s0b[kEwGroups], s1b[kEwGroups];
-#pragma unroll
-  for (uint32_t g = 0; g < kGroups; ++g) {
-    const uint32_t e = base + (g * kThreads + htid()) * 8;
-    sq[g] = packed ? e / MN : 0u;
-    e0[g] = e - sq[g] * MN;
-    if (e >= span || e0[g] >= MN) {
-      e0[g] = MN;   // marks the group empty
-      continue;
+  for (uint32_t base = task_base; base < task_base + kTask && base < span; base += kChunk) {
+    // phase 1: loads
+    uint4 ra[kEwGroups], rb[kEwGroups], rc[kEwGroups];
+    V8 ia[kEwGroups];
+    uint2 qa[kEwGroups], qb[kEwGroups];
+    uint32_t e0[kEwGroups], sq[kEwGroups];
+    // raw FP16 register bits: converted only in phase 2, so no load of phase 1
+    // waits for another
+    uint16_t s0b[kEwGroups], s1b[kEwGroups];
+  #pragma unroll
+    for (uint32_t g = 0; g < kGroups; ++g) {
+      const uint32_t e = base + (g * kThreads + htid()) * 8;
+      sq[g] = packed ? e / MN : 0u;
+      e0[g] = e - sq[g] * MN;
+      if (e >= span || e0[g] >= MN) {
+        e0[g] = MN;   // marks the group empty
+        continue;
+      }
+      const uint32_t seq = t.seq0 + sq[g];
+      s0b[g] = sreg_bits(A, op.s[0], seq);
+      s1b[g] = sreg_bits(A, op.s[1], seq);
+      const uint8_t* __restrict__ a = a0 + sq[g] * sa;
+      const uint8_t* __restrict__ b = b0 + sq[g] * sb;
+      const uint32_t col = e0[g] % N;
+      if constexpr (KIND == K_QUANT || KIND == K_GELU_F16) {
+        ra[g] = ld16(a + e0[g] * 2);
+      } else if constexpr (KIND == K_VADD_F16) {
+        ra[g] = ld16(a + e0[g] * 2);
+        rb[g] = ld16(b + e0[g] * 2);
+      } else if constexpr (KIND == K_DEQUANT_SCALED) {
+        ia[g] = ld32(a + e0[g] * 4);
+        rb[g] = ld16(b + uint64_t(col) * 2);
+        rc[g] = (op.flags & F_SPLIT) ? ld16(pptr(A, op.c, seq) + uint64_t(col) * 2) : ld16(b + uint64_t(N + col) * 2);
+      } else if constexpr (KIND == K_DEQUANT_ACCUM || KIND == K_REQUANT_PC) {
+        ia[g] = ld32(a + e0[g] * 4);
+        rb[g] = ld16(b + uint64_t(col) * 2);
+      } else if constexpr (KIND == K_REQUANT || KIND == K_SCALE_MUL_I32) {
+        ia[g] = ld32(a + e0[g] * 4);
+      } else if constexpr (KIND == K_VADD_I32) {
+        ia[g] = ld32(a + e0[g] * 4);
+        const uint4* q = reinterpret_cast<const uint4*>(b + uint64_t(col) * 4);
+        rb[g] = __ldcg(q);
+        rc[g] = __ldcg(q + 1);
+      } else if constexpr (KIND == K_SCALE_MUL_I8) {
+        qa[g] = ld8(a + e0[g]);
+      } else if constexpr (KIND == K_VADD_I8) {
+        qa[g] = ld8(a + e0[g]);
+        qb[g] = ld8(b + e0[g]);
+      } else if constexpr (KIND == K_DEQUANT_ADD) {
+        ia[g] = ld32(a + e0[g] * 4);
+        qb[g] = ld8(b + e0[g]);
+      } else if constexpr (KIND == K_GELU_I8) {
+        if (op.flags & F_SRC_I32) ia[g] = ld32(a + e0[g] * 4);
+        else qa[g] = ld8(a + e0[g]);
+      }
     }
-    const uint32_t seq = t.seq0 + sq[g];
-    s0b[g] = sreg_bits(A, op.s[0], seq);
-    s1b[g] = sreg_bits(A, op.s[1], seq);
-    const uint8_t* __restrict__ a = a0 + sq[g] * sa;
-    const uint8_t* __restrict__ b = b0 + sq[g] * sb;
-    const uint32_t col = e0[g] % N;
-    if constexpr (KIND == K_QUANT || KIND == K_GELU_F16) {
-      ra[g] = ld16(a + e0[g] * 2);
-    } else if constexpr (KIND == K_VADD_F16) {
-      ra[g] = ld16(a + e0[g] * 2);
-      rb[g] = ld16(b + e0[g] * 2);
-    } else if constexpr (KIND == K_DEQUANT_SCALED) {
-      ia[g] = ld32(a + e0[g] * 4);
-      rb[g] = ld16(b + uint64_t(col) * 2);
-      rc[g] = (op.flags & F_SPLIT) ? ld16(pptr(A, op.c, seq) + uint64_t(col) * 2) : ld16(b + uint64_t(N + col) * 2);
-    } else if constexpr (KIND == K_DEQUANT_ACCUM || KIND == K_REQUANT_PC) {
-      ia[g] = ld32(a + e0[g] * 4);
-      rb[g] = ld16(b + uint64_t(col) * 2);
-    } else if constexpr (KIND == K_REQUANT || KIND == K_SCALE_MUL_I32) {
-      ia[g] = ld32(a + e0[g] * 4);
-    } else if constexpr (KIND == K_VADD_I32) {
-      ia[g] = ld32(a + e0[g] * 4);
-      const uint4* q = reinterpret_cast<const uint4*>(b + uint64_t(col) * 4);
-      rb[g] = __ldcg(q);
-      rc[g] = __ldcg(q + 1);
-    } else if constexpr (KIND == K_SCALE_MUL_I8) {
-      qa[g] = ld8(a + e0[g]);
-    } else if constexpr (KIND == K_VADD_I8) {
-      qa[g] = ld8(a + e0[g]);
-      qb[g] = ld8(b + e0[g]);
-    } else if constexpr (KIND == K_DEQUANT_ADD) {
-      ia[g] = ld32(a + e0[g] * 4);
-      qb[g] = ld8(b + e0[g]);
-    } else if constexpr (KIND == K_GELU_I8) {
-      if (op.flags & F_SRC_I32) ia[g] = ld32(a + e0[g] * 4);
-      else qa[g] = ld8(a + e0[g]);
-    }
-  }
-  // phase 2: compute and store
-#pragma unroll
-  for (uint32_t g = 0; g < kGroups; ++g) {
-    if (e0[g] >= MN) continue;
-    uint8_t* __restrict__ d = d0 + sq[g] * sd;
-    const float s0 = h2f(s0b[g]), s1 = h2f(s1b[g]);
-    if constexpr (KIND == K_QUANT) {
-      int8_t q[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float r = rintf(__fmul_rn(h2f(h_at(ra[g], j)), s0));
-        q[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+    // phase 2: compute and store
+  #pragma unroll
+    for (uint32_t g = 0; g < kGroups; ++g) {
+      if (e0[g] >= MN) continue;
+      uint8_t* __restrict__ d = d0 + sq[g] * sd;
+      const float s0 = h2f(s0b[g]), s1 = h2f(s1b[g]);
+      if constexpr (KIND == K_QUANT) {
+        int8_t q[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float r = rintf(__fmul_rn(h2f(h_at(ra[g], j)), s0));
+          q[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+        }
+        *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+      } else if constexpr (KIND == K_GELU_F16) {
+        uint16_t h[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = f2h(gelu_f32(h2f(h_at(ra[g], j))));
+        *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
+      } else if constexpr (KIND == K_VADD_F16) {
+        uint16_t h[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = f2h(__fadd_rn(h2f(h_at(ra[g], j)), h2f(h_at(rb[g], j))));
+        *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
+      } else if constexpr (KIND == K_DEQUANT_SCALED) {
+        uint16_t h[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float v = __fmul_rn(__int2float_rn(i_at(ia[g], j)), h2f(h_at(rb[g], j)));
+          v = __fmul_rn(v, s0);
+          h[j] = f2h(__fadd_rn(v, h2f(h_at(rc[g], j))));
+        }
+        *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
+      } else if constexpr (KIND == K_DEQUANT_ACCUM) {
+        uint16_t h[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = f2h(__fmul_rn(__int2float_rn(i_at(ia[g], j)), h2f(h_at(rb[g], j))));
+        *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
+      } else if constexpr (KIND == K_REQUANT_PC) {
+        int8_t q[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = sat8(__fmul_rn(__int2float_rn(i_at(ia[g], j)), h2f(h_at(rb[g], j))));
+        *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+      } else if constexpr (KIND == K_REQUANT) {
+        int8_t q[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = sat8(__fmul_rn(__int2float_rn(i_at(ia[g], j)), s0));
+        *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+      } else if constexpr (KIND == K_SCALE_MUL_I32) {
+        int32_t o[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = sat32(__fmul_rn(__int2float_rn(i_at(ia[g], j)), s0));
+        uint4* q = reinterpret_cast<uint4*>(d + e0[g] * 4);
+        q[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        q[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      } else if constexpr (KIND == K_VADD_I32) {
+        const V8 rv{rb[g], rc[g]};
+        uint32_t o[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = static_cast<uint32_t>(i_at(ia[g], j)) + static_cast<uint32_t>(i_at(rv, j));
+        uint4* q = reinterpret_cast<uint4*>(d + e0[g] * 4);
+        q[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        q[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      } else if constexpr (KIND == K_SCALE_MUL_I8) {
+        int8_t q[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = sat8(__fmul_rn(static_cast<float>(b_at(qa[g], j)), s0));
+        *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+      } else if constexpr (KIND == K_VADD_I8) {
+        int8_t q[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int v = int(b_at(qa[g], j)) + int(b_at(qb[g], j));
+          q[j] = static_cast<int8_t>(v < -128 ? -128 : (v > 127 ? 127 : v));
+        }
+        *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+      } else if constexpr (KIND == K_DEQUANT_ADD) {
+        int8_t q[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float accv = __fmul_rn(__int2float_rn(i_at(ia[g], j)), s0);
+          const float skip = __fmul_rn(static_cast<float>(b_at(qb[g], j)), s1);
+          q[j] = sat8(__fadd_rn(accv, skip));
+        }
+        *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
+      } else if constexpr (KIND == K_GELU_I8) {
+        int8_t q[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float x = (op.flags & F_SRC_I32) ? __fmul_rn(__int2float_rn(i_at(ia[g], j)), s0)
+                                                 : __fmul_rn(static_cast<float>(b_at(qa[g], j)), s0);
+          const float y = gelu_f32(x);
+          q[j] = s1 == 0.f ? int8_t(0) : sat8(__fdiv_rn(y, s1));
+        }
+        *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
       }
-      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
-    } else if constexpr (KIND == K_GELU_F16) {
-      uint16_t h[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) h[j] = f2h(gelu_f32(h2f(h_at(ra[g], j))));
-      *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
-    } else if constexpr (KIND == K_VADD_F16) {
-      uint16_t h[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) h[j] = f2h(__fadd_rn(h2f(h_at(ra[g], j)), h2f(h_at(rb[g], j))));
-      *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
-    } else if constexpr (KIND == K_DEQUANT_SCALED) {
-      uint16_t h[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float v = __fmul_rn(__int2float_rn(i_at(ia[g], j)), h2f(h_at(rb[g], j)));
-        v = __fmul_rn(v, s0);
-        h[j] = f2h(__fadd_rn(v, h2f(h_at(rc[g], j))));
-      }
-      *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
-    } else if constexpr (KIND == K_DEQUANT_ACCUM) {
-      uint16_t h[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) h[j] = f2h(__fmul_rn(__int2float_rn(i_at(ia[g], j)), h2f(h_at(rb[g], j))));
-      *reinterpret_cast<uint4*>(d + e0[g] * 2) = pack_h(h);
-    } else if constexpr (KIND == K_REQUANT_PC) {
-      int8_t q[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = sat8(__fmul_rn(__int2float_rn(i_at(ia[g], j)), h2f(h_at(rb[g], j))));
-      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
-    } else if constexpr (KIND == K_REQUANT) {
-      int8_t q[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = sat8(__fmul_rn(__int2float_rn(i_at(ia[g], j)), s0));
-      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
-    } else if constexpr (KIND == K_SCALE_MUL_I32) {
-      int32_t o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = sat32(__fmul_rn(__int2float_rn(i_at(ia[g], j)), s0));
-      uint4* q = reinterpret_cast<uint4*>(d + e0[g] * 4);
-      q[0] = make_uint4(o[0], o[1], o[2], o[3]);
-      q[1] = make_uint4(o[4], o[5], o[6], o[7]);
-    } else if constexpr (KIND == K_VADD_I32) {
-      const V8 rv{rb[g], rc[g]};
-      uint32_t o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = static_cast<uint32_t>(i_at(ia[g], j)) + static_cast<uint32_t>(i_at(rv, j));
-      uint4* q = reinterpret_cast<uint4*>(d + e0[g] * 4);
-      q[0] = make_uint4(o[0], o[1], o[2], o[3]);
-      q[1] = make_uint4(o[4], o[5], o[6], o[7]);
-    } else if constexpr (KIND == K_SCALE_MUL_I8) {
-      int8_t q[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = sat8(__fmul_rn(static_cast<float>(b_at(qa[g], j)), s0));
-      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
-    } else if constexpr (KIND == K_VADD_I8) {
-      int8_t q[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int v = int(b_at(qa[g], j)) + int(b_at(qb[g], j));
-        q[j] = static_cast<int8_t>(v < -128 ? -128 : (v > 127 ? 127 : v));
-      }
-      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
-    } else if constexpr (KIND == K_DEQUANT_ADD) {
-      int8_t q[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float accv = __fmul_rn(__int2float_rn(i_at(ia[g], j)), s0);
-        const float skip = __fmul_rn(static_cast<float>(b_at(qb[g], j)), s1);
-        q[j] = sat8(__fadd_rn(accv, skip));
-      }
-      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
-    } else if constexpr (KIND == K_GELU_I8) {
-      int8_t q[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float x = (op.flags & F_SRC_I32) ? __fmul_rn(__int2float_rn(i_at(ia[g], j)), s0)
-                                               : __fmul_rn(static_cast<float>(b_at(qa[g], j)), s0);
-        const float y = gelu_f32(x);
-        q[j] = s1 == 0.f ? int8_t(0) : sat8(__fdiv_rn(y, s1));
-      }
-      *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
     }
   }
 }
@@ -1148,51 +1218,16 @@ __device__ __forceinline__ float in_val(const ExecArgs& A, const DevOp& op, uint
   }
 }
 
-__device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem, uint32_t opi) {
-  const int warp = htid() >> 5, lane = htid() & 31;
-  const uint32_t seq = t.seq0, N = op.N;
-  const uint32_t r = t.tile * 8 + warp;
-  float* rowbuf = reinterpret_cast<float*>(smem) + warp * kRowCap;
-  uint32_t* pw = reinterpret_cast<uint32_t*>(smem + kWarps * kRowCap * 4) + warp * (3 * kPwMaxLeaves);
-  if (r >= op.M) return;
-  const bool legacy = op.kind == K_LN_I8 || op.kind == K_SOFTMAX_I8 || op.kind == K_MASKED_SOFTMAX_I8;
-  const float in_scale = legacy ? sreg_f32(A, op.s[0], seq) : 0.f;
-  const float out_scale = legacy ? sreg_f32(A, op.s[1], seq) : 0.f;
+// One row of a row op (op_rows); a buffered FP16 row is already in rowbuf.
+__device__ __forceinline__ void row_one(const ExecArgs& A, const DevOp& op, uint32_t seq, uint32_t r, float* rowbuf,
+                                       uint32_t* pw, bool buffered, bool fp16_in, float in_scale, float out_scale,
+                                       int lane, uint32_t qrb, uint32_t vkl, uint32_t mode) {
+  const uint32_t N = op.N;
   const uint64_t base = uint64_t(r) * N;
-  const bool buffered = N <= kRowCap;
-  // attention context
-  uint32_t qrb = op.attn_qrb, vkl = op.attn_vkl, mode = op.attn_mode;
-  if (op.flags & F_ATTN_DYN) {
-    const uint64_t v = A.params[uint64_t(seq) * A.n_params + op.param];
-    qrb = v & 0xFFFF;
-    vkl = (v >> 16) & 0xFFFF;
-    mode = (v >> 32) & 0x3;
-  }
   auto x_at = [&](uint32_t j) -> float {
     return buffered ? rowbuf[j] : in_val(A, op, seq, base + j, in_scale);
   };
-  const bool fp16_in = op.kind == K_LAYERNORM_F16 || op.kind == K_SOFTMAX_F16 || op.kind == K_MASKED_SOFTMAX_F16;
-  if (buffered && fp16_in) {
-    // 8 FP16 per lane per load, all loads issued before any conversion
-    const uint4* src = reinterpret_cast<const uint4*>(pptr(A, op.a, seq) + base * 2);
-    const uint32_t ng = N / 8;
-    for (uint32_t half = 0; half < kRowCap / 256; half += 4) {
-      uint4 v[4];
-#pragma unroll
-      for (uint32_t k = 0; k < 4; ++k) {
-        const uint32_t g = lane + 32 * (half + k);
-        if (g < ng) v[k] = __ldcg(src + g);
-      }
-#pragma unroll
-      for (uint32_t k = 0; k < 4; ++k) {
-        const uint32_t g = lane + 32 * (half + k);
-        if (g < ng)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) rowbuf[g * 8 + j] = h2f(h_at(v[k], j));
-      }
-    }
-    __syncwarp();
-  } else if (buffered) {
+  if (!fp16_in && buffered) {
     for (uint32_t j = lane; j < N; j += 32) rowbuf[j] = in_val(A, op, seq, base + j, in_scale);
     __syncwarp();
   }
@@ -1312,8 +1347,60 @@ __device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const T
       reinterpret_cast<int8_t*>(d)[base + j] = out_scale == 0.f ? int8_t(0) : sat8(__fdiv_rn(p, out_scale));
     }
   }
+}
+
+__device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem, uint32_t opi) {
+  const int warp = htid() >> 5, lane = htid() & 31;
+  const uint32_t seq = t.seq0, N = op.N;
+  const uint32_t rpt = row_task_rows(op.kind, N), rpw = rpt / 8;   // rows per task, per warp
+  float* rowbuf0 = reinterpret_cast<float*>(smem) + warp * kRowCap;
+  uint32_t* pw = reinterpret_cast<uint32_t*>(smem + kWarps * kRowCap * 4) + warp * (3 * kPwMaxLeaves);
+  if (t.tile * rpt + warp >= op.M) return;
+  const bool legacy = op.kind == K_LN_I8 || op.kind == K_SOFTMAX_I8 || op.kind == K_MASKED_SOFTMAX_I8;
+  const float in_scale = legacy ? sreg_f32(A, op.s[0], seq) : 0.f;
+  const float out_scale = legacy ? sreg_f32(A, op.s[1], seq) : 0.f;
+  const bool buffered = rpw * N <= kRowCap;
+  // attention context
+  uint32_t qrb = op.attn_qrb, vkl = op.attn_vkl, mode = op.attn_mode;
+  if (op.flags & F_ATTN_DYN) {
+    const uint64_t v = A.params[uint64_t(seq) * A.n_params + op.param];
+    qrb = v & 0xFFFF;
+    vkl = (v >> 16) & 0xFFFF;
+    mode = (v >> 32) & 0x3;
+  }
+  const bool fp16_in = op.kind == K_LAYERNORM_F16 || op.kind == K_SOFTMAX_F16 || op.kind == K_MASKED_SOFTMAX_F16;
+  if (buffered && fp16_in) {
+    // every row of this warp: 8 FP16 per lane per load, four loads issued
+    // before any conversion; row rr of the warp lands at rowbuf0 + rr * N
+    const uint8_t* a = pptr(A, op.a, seq);
+    const uint32_t ng = N / 8, total = rpw * ng;
+    for (uint32_t k0 = 0; k0 < total; k0 += 128) {
+      uint4 v[4];
+#pragma unroll
+      for (uint32_t k = 0; k < 4; ++k) {
+        const uint32_t idx = k0 + lane + 32 * k, rr = idx / ng, g = idx - rr * ng;
+        const uint32_t r = t.tile * rpt + warp + 8 * rr;
+        if (idx < total && r < op.M) v[k] = __ldcg(reinterpret_cast<const uint4*>(a + uint64_t(r) * N * 2) + g);
+      }
+#pragma unroll
+      for (uint32_t k = 0; k < 4; ++k) {
+        const uint32_t idx = k0 + lane + 32 * k, rr = idx / ng, g = idx - rr * ng;
+        const uint32_t r = t.tile * rpt + warp + 8 * rr;
+        if (idx < total && r < op.M)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) rowbuf0[rr * N + g * 8 + j] = h2f(h_at(v[k], j));
+      }
+    }
+    __syncwarp();
+  }
+  for (uint32_t rr = 0; rr < rpw; ++rr) {
+    const uint32_t r = t.tile * rpt + warp + 8 * rr;
+    if (r >= op.M) break;
+    row_one(A, op, seq, r, rowbuf0 + rr * N, pw, buffered, fp16_in, in_scale, out_scale, lane, qrb, vkl, mode);
+  }
   (void)opi;
 }
+
 
 // Legacy fused softmax(QK^T)·V (sfu.py:323-443): one warp per query row.
 __device__ __noinline__ void op_attnv(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
@@ -1483,13 +1570,13 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
 // tcgen05 stages); the two halves' regions are followed by their TcShared slots.
 constexpr size_t kRowSmem = kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4;
 constexpr size_t kTcSmem = kTcStages * kTcStage + 1024;   // + alignment of the swizzled stages
+static_assert(2 * kTcStage128 + 1024 <= kTcSmem, "128-column tcgen05 stages outgrow the tcgen05 region");
 constexpr size_t kExecOpSmem0 = kRowSmem > kMmSmem ? kRowSmem : kMmSmem;
 constexpr size_t kExecOpSmem = kExecOpSmem0 > kTcSmem ? kExecOpSmem0 : kTcSmem;
 constexpr size_t kExecSmem = kHalves * kExecOpSmem + kHalves * 128;
 static_assert(sizeof(TcShared) <= 128, "TcShared outgrew its slot");
 static_assert(kStageBytes <= kExecOpSmem, "element-wise staging exceeds the op shared memory");
-// op_matmul_wide at its limits (M 32, K 128, N 256): A + B^T rows + raw B
-static_assert(32 * 144 + 256 * 144 + 128 * 256 <= kExecOpSmem, "wide MATMUL exceeds the op shared memory");
+static_assert(kWideMmSmem <= kExecOpSmem, "wide MATMUL exceeds the op shared memory");
 static_assert(kSegTableOff + kMaxSegRuns * 12 <= kExecOpSmem, "segment table exceeds the op shared memory");
 static_assert(kExecOpSmem % 1024 == 0 || kTcSmem <= kExecOpSmem, "half regions must keep the stage alignment slack");
 static_assert(kExecSmem <= 227 * 1024, "executor shared memory exceeds one CTA's limit");

@@ -73,6 +73,9 @@ constexpr uint16_t F_SEGA = 32;        // MAX_ABS / QUANT / VADD_F16: operand a 
 constexpr uint16_t F_WIDE = 64;        // MATMUL (per-sequence operands, M <= 32, K <= 128, N <= 256):
                                        // one task per sequence covers every column
 constexpr uint16_t F_BT = 128;         // MATMUL: operand b holds B transposed, [N][K] row-major
+constexpr uint16_t F_TC128 = 256;      // F_TC MATMUL with N >= 128: 128-column tasks (else 64)
+constexpr uint16_t F_QB = 512;         // wide MATMUL: operand b is FP16 and is quantised on load
+                                       // (rint(x * s[1]), NaN -> 0, clipped to int8), as QUANT does
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 
 // Most runs an operand read through a segment list may have (longer lists are gathered).
@@ -127,9 +130,32 @@ constexpr uint64_t kEwTaskElems = 8192;
 
 // Element-wise task size by op kind: GELU (float64 tanh per element) takes
 // 2048-element tasks (one group of 8 per thread) so its work spreads over
-// more SMs; the rest take kEwTaskElems.
+// more SMs; QUANT (FP16 in, staged in shared memory, 32 KB per task) takes
+// twice kEwTaskElems to halve its per-task overhead; the rest take
+// kEwTaskElems.
 TAC_HD constexpr uint32_t ew_task_elems(uint32_t kind) {
-  return (kind == K_GELU_F16 || kind == K_GELU_I8) ? 2048u : uint32_t(kEwTaskElems);
+  return (kind == K_GELU_F16 || kind == K_GELU_I8) ? 2048u
+         : kind == K_QUANT                         ? 2u * uint32_t(kEwTaskElems)
+                                                   : uint32_t(kEwTaskElems);
+}
+
+// Shared memory of a wide MATMUL task (op_matmul_wide): A and B^T rows of K
+// bytes padded to 32 plus 16, raw B [K][N] unless B arrives transposed, and
+// the FP16 B when it is quantised on load.
+constexpr uint32_t kWideMmSmem = 73 * 1024;
+TAC_HD constexpr uint32_t wide_mm_smem(uint32_t M, uint32_t N, uint32_t K, bool bt, bool qb) {
+  return (((M + 15) / 16) * 16) * (((K + 31) & ~31u) + 16) + (((N + 7) / 8) * 8) * (((K + 31) & ~31u) + 16) +
+         (bt ? 0u : ((K + 31) & ~31u) * N) + (qb ? K * N * 2 : 0u);
+}
+TAC_HD constexpr bool wide_mm_ok(uint32_t M, uint32_t N, uint32_t K, bool bt, bool qb) {
+  return M > 0 && M <= 32 && K > 0 && K <= 256 && N > 0 && N <= 256 && M % 16 == 0 && K % 16 == 0 &&
+         N % 16 == 0 && wide_mm_smem(M, N, K, bt, qb) <= kWideMmSmem;
+}
+
+// Rows of a row-op task: FP16 softmaxes of at most 1024 columns take 16 rows
+// (two per warp, both rows' loads in flight together); the rest take 8.
+TAC_HD constexpr uint32_t row_task_rows(uint32_t kind, uint32_t n) {
+  return ((kind == K_SOFTMAX_F16 || kind == K_MASKED_SOFTMAX_F16) && n <= 1024) ? 16u : 8u;
 }
 
 // Parameters decoded from runtime-patched instruction words, one set per

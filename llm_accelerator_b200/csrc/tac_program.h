@@ -23,7 +23,7 @@ struct VarInfo {
 
 // A condition on runtime parameters that the compiler could not decide.
 enum CheckKind : uint32_t {
-  CHK_ADDR = 1,        // param + dconst is 16-byte aligned and lies in [lo, hi)
+  CHK_ADDR = 1,        // param + dconst is 16-byte aligned; the nbytes there lie in [lo, hi)
   CHK_ATTN_SET = 2,    // CONFIG_ATTN: mode != 0 and valid_kv_len != 0
   CHK_ATTN_KEYS = 3,   // masked softmax: context fits `key_cols` columns
   CHK_SAME = 4,        // param equals param `lo` (sites over one symbol extent)
@@ -34,7 +34,7 @@ struct RtCheck {
   uint32_t param;
   uint64_t pc;
   int64_t dconst;
-  uint64_t lo, hi;     // CHK_ADDR: allowed start range; CHK_ATTN_KEYS: lo = key columns;
+  uint64_t lo, hi;     // CHK_ADDR: allowed byte range; CHK_ATTN_KEYS: lo = key columns;
                        // CHK_SAME: lo = the other parameter
   uint64_t nbytes;
 };

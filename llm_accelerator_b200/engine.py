@@ -47,6 +47,10 @@ class Program:
         if h:
             _lib.tac_program_destroy(h)
 
+    def attn_key_cols(self) -> int:
+        """Fewest key columns of a runtime-configured masked softmax (0 if none)."""
+        return int(_lib.tac_program_attn_key_cols(self.handle))
+
     def dump(self):
         """(ops, segments, tasks, level_offsets) as numpy structured arrays."""
         i = self.info

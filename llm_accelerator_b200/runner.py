@@ -159,7 +159,7 @@ class BatchedRunner:
         # later step reads before writing (found from the full-state plans).
         live = [(b.logits_base, b.kv_cache_base), (b.kv_cache_base, b.required_dram_bytes)]
         sram_live = sregs_live = False
-        for name, (masked, entry, sites) in self._masked.items():
+        for name, (masked, entry, sites) in list(self._masked.items()):
             full = compile_program(self.batch, self.dram_bytes, self.shared_bytes, masked, entry, 10_000_000,
                                    L.Regs(), True, sites)
             if full.info.faulted:
@@ -168,6 +168,21 @@ class BatchedRunner:
             live += ranges
             sram_live |= sr
             sregs_live |= gr
+            # A KV site's value is its bank's base + position * kv_step_bytes,
+            # and a position must fit the stream's softmax key columns: declare
+            # that narrower range (the run-time check still enforces it), so the
+            # compiler sees each head's appends touch only its own window.
+            keys = full.attn_key_cols()
+            if keys:
+                meta = self._sites[name][1]
+                tight = []
+                for site, (kind, s) in zip(sites, meta):
+                    if kind == "addr" and s.kind == "kv_base":
+                        hi = min(site.range_hi, site.range_lo + keys * int(b.kv_step_bytes))
+                        site = Site(site.kind, site.addr_reg, site.lo_pc, site.hi_pc, site.range_lo, hi)
+                    tight.append(site)
+                self._masked[name] = (masked, entry, tight)
+                self._sites[name] = (tight, meta)
         self.live = live
         for name, (masked, entry, sites) in self._masked.items():
             self.plans[name] = compile_program(self.batch, self.dram_bytes, self.shared_bytes, masked, entry,

@@ -109,10 +109,15 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
                 m.sregs[r] = np.array([v], np.float16).view(np.uint16)[0]
         elif k == K["MATMUL"]:
             A = m.mem(a, M * Kd).view(np.int8).reshape(M, Kd).astype(np.int32)
-            if op["flags"] & 128:   # F_BT: b holds B^T [N][K]
-                B = m.mem(b, Kd * N).view(np.int8).reshape(N, Kd).T.astype(np.int32)
+            if op["flags"] & 512:   # F_QB: b is FP16, quantised like QUANT with register s[1]
+                v = np.round(_f16(m, b, Kd * N) * np.float32(m.sreg(s[1])))
+                raw = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8)
             else:
-                B = m.mem(b, Kd * N).view(np.int8).reshape(Kd, N).astype(np.int32)
+                raw = m.mem(b, Kd * N).view(np.int8)
+            if op["flags"] & 128:   # F_BT: b holds B^T [N][K]
+                B = raw.reshape(N, Kd).T.astype(np.int32)
+            else:
+                B = raw.reshape(Kd, N).astype(np.int32)
             acc = m.mem(c, M * N * 4).view(np.int32).reshape(M, N).copy() if op["flags"] & 1 else np.zeros((M, N), np.int32)
             acc += A @ B
             m.mem(d, M * N * 4)[:] = acc.view(np.uint8).ravel()

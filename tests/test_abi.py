@@ -15,7 +15,7 @@ def declared_symbols():
     names = set()
     for h in (ROOT / "include").glob("*.h"):
         text = h.read_text()
-        names.update(re.findall(r"^\s*(?:int|uint64_t|void)\s+(tac_\w+)\s*\(", text, flags=re.M))
+        names.update(re.findall(r"^\s*(?:int|uint32_t|uint64_t|void)\s+(tac_\w+)\s*\(", text, flags=re.M))
     return names
 
 

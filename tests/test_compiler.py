@@ -110,9 +110,23 @@ def _params(region, sites):
     return out
 
 
+def _narrow_kv(b, nm, sites, plan):
+    """KV sites narrowed to base + key_cols * kv_step_bytes, as BatchedRunner does."""
+    keys = plan.attn_key_cols()
+    meta = [s for s in b.runtime_patch_sites if s.stream == nm]
+    out = []
+    for i, site in enumerate(sites):
+        if site.kind == 0 and i < len(meta) and meta[i].kind == "kv_base" and keys:
+            site = Site(0, site.addr_reg, site.lo_pc, site.hi_pc, site.range_lo,
+                        min(site.range_hi, site.range_lo + keys * b.kv_step_bytes))
+        out.append(site)
+    return out
+
+
+@pytest.mark.parametrize("narrow", [False, True], ids=["symbol-ranges", "kv-window-ranges"])
 @pytest.mark.parametrize("reverse", [False, True], ids=["level-order", "level-reversed"])
 @pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
-def test_plan_reproduces_oracle_bundle_run(name, reverse):
+def test_plan_reproduces_oracle_bundle_run(name, reverse, narrow):
     """Prefill + decode steps: one plan per stream compiled with runtime sites,
     executed with each step's parameters, equals the oracle bit-for-bit, also
     with every level's ops run in reverse order (no hidden intra-level
@@ -131,8 +145,11 @@ def test_plan_reproduces_oracle_bundle_run(name, reverse):
                 w = int.from_bytes(region[pc * 8:pc * 8 + 8], "big") & (0x7F << 57)
                 region[pc * 8:pc * 8 + 8] = w.to_bytes(8, "big")
         entry = b.prefill_pc if nm == "prefill" else b.decode_pc
-        plans[nm] = (compile_program(1, dram_bytes, shared, bytes(region), entry, 10_000_000, L.Regs(), True, sites),
-                     sites)
+        plan = compile_program(1, dram_bytes, shared, bytes(region), entry, 10_000_000, L.Regs(), True, sites)
+        if narrow:
+            sites = _narrow_kv(b, nm, sites, plan)
+            plan = compile_program(1, dram_bytes, shared, bytes(region), entry, 10_000_000, L.Regs(), True, sites)
+        plans[nm] = (plan, sites)
     arena = max(int(p.info.arena_bytes) for p, _ in plans.values())
     slots = max(int(p.info.n_slots) for p, _ in plans.values())
     m = PE.PlanMachine(bytes(orc.state.dram), shared, arena, slots)
@@ -308,7 +325,7 @@ def test_tasks_cover_every_sequence_and_element_once(batch):
     ops, segs, tasks, lv = p.dump()
     EW_TASK = 8192
     ew_kinds = set(range(7, 18)) | {19, 27}
-    task_elems = lambda kind: 2048 if kind in (19, 27) else EW_TASK  # noqa: E731
+    task_elems = lambda kind: 2048 if kind in (19, 27) else (2 * EW_TASK if kind == 16 else EW_TASK)  # noqa: E731
     seen = {}
     for t in tasks:
         op = ops[t["op"]]
