@@ -471,6 +471,27 @@ class Compiler {
     return true;
   }
 
+  // Operand A of a wide MATMUL that is the output of a QUANT whose FP16
+  // source still holds the same bytes: the MATMUL quantises the source itself
+  // (F_QA, register in s[0]) and the QUANT goes unread.
+  bool mm_a_source(uint32_t u0, uint32_t M, uint32_t N, uint32_t K, Access& acc, DevOp& op) {
+    if (op.b & kSharedBit) return false;   // shared weights: the tensor-core path
+    const bool bt = (op.flags & F_BT) != 0, qb = (op.flags & F_QB) != 0;
+    if (!wide_mm_ok(M, N, K, bt, qb, true)) return false;
+    const uint64_t n = uint64_t(M) * K / kUnit;
+    const uint64_t* m = &sram_[u0];
+    if (!contiguous(m, n)) return false;
+    auto q = quantized_.find(m[0]);
+    if (q == quantized_.end() || q->second.rows * q->second.cols != uint64_t(M) * K) return false;
+    if (cls(q->second.src) == PC_HOME_RW && q->second.epoch != home_writes_) return false;
+    op.a = q->second.src;
+    op.s[0] = q->second.scale;
+    read_sreg(acc, op.s[0]);
+    op.flags |= F_QA | F_WIDE;
+    acc.reads.push_back({op.a, 2 * n});
+    return true;
+  }
+
   // Physical start of a contiguous copy of logical SRAM units [u0, u0+n).
   uint64_t src(uint32_t u0, uint64_t nbytes, Access& acc) {
     uint64_t n = (nbytes + kUnit - 1) / kUnit;
@@ -1024,8 +1045,8 @@ int Compiler::h_rtype(const Insn& x) {
       if (x.flags & 1) TRY(span(x.dst_buf, x.dst_off, M * N * 4));
       TRY(span(x.dst_buf, x.dst_off, M * N * 4));
       op.kind = K_MATMUL;
-      op.a = src(s1, M * K, acc);
       if (!mm_b_source(s2, M, N, K, acc, op)) op.b = src(s2, K * N, acc);
+      if (!mm_a_source(s1, M, N, K, acc, op)) op.a = src(s1, M * K, acc);
       if (x.flags & 1) {
         op.flags |= F_ACCUMULATE;
         op.c = src(d, M * N * 4, acc);

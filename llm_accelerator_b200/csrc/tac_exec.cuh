@@ -451,18 +451,23 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   const uint32_t kc32 = (K + 31) & ~31u;
   const uint32_t bts = kc32 + 16;
   const uint32_t nblocks = (M + 15) / 16, n8 = (N + 7) / 8;
-  const bool bt = (op.flags & F_BT) != 0, qb = (op.flags & F_QB) != 0;
+  const bool bt = (op.flags & F_BT) != 0, qb = (op.flags & F_QB) != 0, qa = (op.flags & F_QA) != 0;
   uint8_t* As = smem;                               // [nblocks * 16][bts]
   uint8_t* Bt = As + nblocks * 16 * bts;            // [n8 * 8][bts]
   uint8_t* Braw = Bt + n8 * 8 * bts;                // [kc32][N] (not F_BT)
   uint8_t* Bh = Braw + (bt ? 0u : kc32 * N);        // FP16 B (F_QB)
+  uint8_t* Ah = wide_mm_a_in_bt(M, N, K, bt) ? Bt : Bh + (qb ? K * N * 2 : 0u);   // FP16 A (F_QA)
   const uint8_t* Ag = pptr(A, op.a, seq);
   const uint8_t* Bg = pptr(A, op.b, seq);
   const uint32_t kv = kc32 / 16;                    // 16-byte vectors per padded row
-  for (uint32_t i = htid(); i < nblocks * 16 * kv; i += kThreads) {
-    const uint32_t r = i / kv, v = i % kv;
-    const bool in = r < M && v * 16 < K;
-    cp_async16(As + r * bts + v * 16, Ag + (in ? uint64_t(r) * K + v * 16 : 0), in ? 16u : 0u);
+  if (qa) {
+    for (uint32_t i = htid(); i < M * K / 8; i += kThreads) cp_async16(Ah + i * 16, Ag + uint64_t(i) * 16, 16u);
+  } else {
+    for (uint32_t i = htid(); i < nblocks * 16 * kv; i += kThreads) {
+      const uint32_t r = i / kv, v = i % kv;
+      const bool in = r < M && v * 16 < K;
+      cp_async16(As + r * bts + v * 16, Ag + (in ? uint64_t(r) * K + v * 16 : 0), in ? 16u : 0u);
+    }
   }
   if (qb) {
     for (uint32_t i = htid(); i < K * N / 8; i += kThreads) cp_async16(Bh + i * 16, Bg + uint64_t(i) * 16, 16u);
@@ -482,8 +487,27 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   }
   cp_async_commit();
   const uint16_t sb = qb ? sreg_bits(A, op.s[1], seq) : uint16_t(0);
+  const uint16_t sa = qa ? sreg_bits(A, op.s[0], seq) : uint16_t(0);
   cp_async_wait<0>();
   hsync();
+  if (qa) {
+    // QUANT's rule into the padded A rows; padding rows and columns are zero
+    const float s0 = h2f(sa);
+    for (uint32_t i = htid(); i < nblocks * 16 * (kc32 / 8); i += kThreads) {
+      const uint32_t r = i / (kc32 / 8), k = (i % (kc32 / 8)) * 8;
+      int8_t q8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (r < M && k < K) {
+        const uint4 x = *reinterpret_cast<const uint4*>(Ah + (uint64_t(r) * K + k) * 2);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float v = rintf(__fmul_rn(h2f(h_at(x, j)), s0));
+          q8[j] = (v == v) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(v, -128.f), 127.f))) : int8_t(0);
+        }
+      }
+      *reinterpret_cast<uint2*>(As + r * bts + k) = pack_b(q8);
+    }
+    if (!qb) hsync();
+  }
   if (qb) {
     // QUANT's rule: rint(x * s), NaN -> 0, clipped to int8; 8 elements per step
     const float s1 = h2f(sb);

@@ -76,6 +76,7 @@ constexpr uint16_t F_BT = 128;         // MATMUL: operand b holds B transposed, 
 constexpr uint16_t F_TC128 = 256;      // F_TC MATMUL with N >= 128: 128-column tasks (else 64)
 constexpr uint16_t F_QB = 512;         // wide MATMUL: operand b is FP16 and is quantised on load
                                        // (rint(x * s[1]), NaN -> 0, clipped to int8), as QUANT does
+constexpr uint16_t F_QA = 1024;        // wide MATMUL: operand a is FP16, quantised on load with s[0]
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 
 // Most runs an operand read through a segment list may have (longer lists are gathered).
@@ -143,13 +144,19 @@ TAC_HD constexpr uint32_t ew_task_elems(uint32_t kind) {
 // bytes padded to 32 plus 16, raw B [K][N] unless B arrives transposed, and
 // the FP16 B when it is quantised on load.
 constexpr uint32_t kWideMmSmem = 73 * 1024;
-TAC_HD constexpr uint32_t wide_mm_smem(uint32_t M, uint32_t N, uint32_t K, bool bt, bool qb) {
-  return (((M + 15) / 16) * 16) * (((K + 31) & ~31u) + 16) + (((N + 7) / 8) * 8) * (((K + 31) & ~31u) + 16) +
-         (bt ? 0u : ((K + 31) & ~31u) * N) + (qb ? K * N * 2 : 0u);
+// The FP16 A (F_QA) shares the B^T area when B is not transposed on arrival
+// and it fits there: B^T is written only after A has been quantised.
+TAC_HD constexpr bool wide_mm_a_in_bt(uint32_t M, uint32_t N, uint32_t K, bool bt) {
+  return !bt && M * K * 2 <= (((N + 7) / 8) * 8) * (((K + 31) & ~31u) + 16);
 }
-TAC_HD constexpr bool wide_mm_ok(uint32_t M, uint32_t N, uint32_t K, bool bt, bool qb) {
+TAC_HD constexpr uint32_t wide_mm_smem(uint32_t M, uint32_t N, uint32_t K, bool bt, bool qb, bool qa = false) {
+  return (((M + 15) / 16) * 16) * (((K + 31) & ~31u) + 16) + (((N + 7) / 8) * 8) * (((K + 31) & ~31u) + 16) +
+         (bt ? 0u : ((K + 31) & ~31u) * N) + (qb ? K * N * 2 : 0u) +
+         ((qa && !wide_mm_a_in_bt(M, N, K, bt)) ? M * K * 2 : 0u);
+}
+TAC_HD constexpr bool wide_mm_ok(uint32_t M, uint32_t N, uint32_t K, bool bt, bool qb, bool qa = false) {
   return M > 0 && M <= 32 && K > 0 && K <= 256 && N > 0 && N <= 256 && M % 16 == 0 && K % 16 == 0 &&
-         N % 16 == 0 && wide_mm_smem(M, N, K, bt, qb) <= kWideMmSmem;
+         N % 16 == 0 && wide_mm_smem(M, N, K, bt, qb, qa) <= kWideMmSmem;
 }
 
 // Rows of a row-op task: FP16 softmaxes of at most 1024 columns take 16 rows

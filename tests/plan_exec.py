@@ -108,7 +108,12 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
             for r, v in vals:
                 m.sregs[r] = np.array([v], np.float16).view(np.uint16)[0]
         elif k == K["MATMUL"]:
-            A = m.mem(a, M * Kd).view(np.int8).reshape(M, Kd).astype(np.int32)
+            if op["flags"] & 1024:   # F_QA: a is FP16, quantised like QUANT with register s[0]
+                v = np.round(_f16(m, a, M * Kd) * np.float32(m.sreg(s[0])))
+                A = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8).reshape(M, Kd)
+                A = A.astype(np.int32)
+            else:
+                A = m.mem(a, M * Kd).view(np.int8).reshape(M, Kd).astype(np.int32)
             if op["flags"] & 512:   # F_QB: b is FP16, quantised like QUANT with register s[1]
                 v = np.round(_f16(m, b, Kd * N) * np.float32(m.sreg(s[1])))
                 raw = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8)
