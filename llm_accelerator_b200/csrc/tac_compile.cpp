@@ -492,6 +492,37 @@ class Compiler {
     return true;
   }
 
+  // DEQUANT_ACCUM of a wide MATMUL's whole int32 result: the MATMUL writes the
+  // FP16 result itself (F_DQ), provided the scale row is ready by the
+  // MATMUL's level.  The DEQUANT's output extent is committed at that level.
+  bool fuse_dequant(uint32_t s1, uint32_t s2, uint32_t d, uint64_t M, uint64_t N) {
+    if ((N * 2) % kUnit) return false;
+    const uint64_t na = M * N * 4 / kUnit, nb = N * 2 / kUnit;
+    const uint64_t* ma = &sram_[s1];
+    const uint64_t* mb = &sram_[s2];
+    if (!contiguous(ma, na) || !contiguous(mb, nb)) return false;
+    auto it = mm_out_.find(ma[0]);
+    if (it == mm_out_.end()) return false;
+    const uint32_t idx = it->second;
+    DevOp& mm = P->ops[idx];
+    if ((mm.flags & F_DQ) || uint64_t(mm.M) != M || uint64_t(mm.N) != N) return false;
+    Access probe;
+    probe.reads.push_back({mb[0], nb});
+    if (level_for(probe) > int32_t(mm.level)) return false;
+    Access acc;
+    acc.reads.push_back({mb[0], nb});
+    const uint64_t out = dst(d, M * N * 2, acc);
+    commit(acc, int32_t(mm.level));
+    mm.flags |= F_DQ;
+    mm.c = mb[0];
+    mm.dconst = static_cast<int64_t>(out);
+    for (auto& w : acc.writes)
+      if (cls(w.first) == PC_ARENA) op_arena_writes_[idx].push_back(w);
+    if (cls(mb[0]) == PC_ARENA) op_arena_reads_[idx].push_back({mb[0], nb});
+    if (cls(mb[0]) != PC_ARENA && cls(mb[0]) != PC_SHARED) op_pure_[idx] = 0;   // conservative
+    return true;
+  }
+
   // Physical start of a contiguous copy of logical SRAM units [u0, u0+n).
   uint64_t src(uint32_t u0, uint64_t nbytes, Access& acc) {
     uint64_t n = (nbytes + kUnit - 1) / kUnit;
@@ -715,6 +746,8 @@ class Compiler {
     uint64_t epoch;
   };
   std::unordered_map<uint64_t, QuantOf> quantized_;
+  // int32 result extent of each emitted wide MATMUL (no accumulate) -> op index
+  std::unordered_map<uint64_t, uint32_t> mm_out_;
   uint64_t home_writes_ = 0;
   // per emitted op: its arena reads and writes, and whether arena writes are its only effect
   std::vector<std::vector<std::pair<uint64_t, uint64_t>>> op_arena_reads_, op_arena_writes_;
@@ -1145,6 +1178,10 @@ int Compiler::h_rtype(const Insn& x) {
       TRY(span(x.src1_buf, x.src1_off, M * N * 4));
       TRY(span(x.src2_buf, x.src2_off, vec));
       TRY(span(x.dst_buf, x.dst_off, M * N * 2));
+      if (o == OP_DEQUANT_ACCUM_FP32 && fuse_dequant(s1, s2, d, M, N)) {
+        cycles_ += M * N;
+        return 0;
+      }
       op.kind = o == OP_DEQUANT_ACCUM_FP32 ? K_DEQUANT_ACCUM : K_DEQUANT_SCALED;
       if (o == OP_DEQUANT_ACCUM_FP32_SCALED) {
         op.s[0] = sreg_[x.sreg];
@@ -1284,9 +1321,15 @@ int Compiler::h_rtype(const Insn& x) {
       return unsupported("unhandled opcode");
   }
 #undef TRY
+  if (op.kind == K_MATMUL && !(op.b & kSharedBit) &&
+      wide_mm_ok(uint32_t(M), uint32_t(N), uint32_t(K), op.flags & F_BT, op.flags & F_QB, op.flags & F_QA))
+    op.flags |= F_WIDE;
   emit_compute(op, acc, d, x.sreg);
   if (op.kind == K_QUANT && !(op.flags & F_SEGA) && cls(sram_[d]) == PC_ARENA)
     quantized_[sram_[d]] = QuantOf{op.a, op.s[0], M, N, home_writes_};
+  if (op.kind == K_MATMUL && (op.flags & F_WIDE) && !(op.flags & F_ACCUMULATE) && !P->ops.empty() &&
+      P->ops.back().kind == K_MATMUL && P->ops.back().d == op.d)
+    mm_out_[op.d] = static_cast<uint32_t>(P->ops.size() - 1);
   return 0;
 }
 
@@ -1449,6 +1492,9 @@ void Compiler::drop_dead_ops() {
     for (auto& w : op_arena_writes_[i]) live = live || any_read(w.first, w.second);
     if (!live) continue;
     keep[i] = 1;
+    DevOp& op = P->ops[i];
+    if ((op.flags & F_DQ) && cls(op.d) == PC_ARENA && !any_read(op.d, uint64_t(op.M) * op.N * 4 / kUnit))
+      op.flags |= F_NOI32;   // only the FP16 result is read
     for (auto& r : op_arena_reads_[i]) mark(r.first, r.second);
   }
   size_t j = 0;

@@ -457,6 +457,8 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   uint8_t* Braw = Bt + n8 * 8 * bts;                // [kc32][N] (not F_BT)
   uint8_t* Bh = Braw + (bt ? 0u : kc32 * N);        // FP16 B (F_QB)
   uint8_t* Ah = wide_mm_a_in_bt(M, N, K, bt) ? Bt : Bh + (qb ? K * N * 2 : 0u);   // FP16 A (F_QA)
+  uint8_t* Pc = Bh + (qb ? K * N * 2 : 0u) + ((qa && !wide_mm_a_in_bt(M, N, K, bt)) ? M * K * 2 : 0u);   // F_DQ row
+  const bool dq = (op.flags & F_DQ) != 0;
   const uint8_t* Ag = pptr(A, op.a, seq);
   const uint8_t* Bg = pptr(A, op.b, seq);
   const uint32_t kv = kc32 / 16;                    // 16-byte vectors per padded row
@@ -484,6 +486,10 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
       const bool in = k < K;
       cp_async16(Braw + k * N + v * 16, Bg + (in ? uint64_t(k) * N + v * 16 : 0), in ? 16u : 0u);
     }
+  }
+  if (dq) {
+    const uint8_t* pg = pptr(A, op.c, seq);
+    for (uint32_t i = htid(); i < N / 8; i += kThreads) cp_async16(Pc + i * 16, pg + uint64_t(i) * 16, 16u);
   }
   cp_async_commit();
   const uint16_t sb = qb ? sreg_bits(A, op.s[1], seq) : uint16_t(0);
@@ -581,6 +587,8 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   }
   int32_t* D = reinterpret_cast<int32_t*>(pptr(A, op.d, seq));
   const int32_t* C = (op.flags & F_ACCUMULATE) ? reinterpret_cast<const int32_t*>(pptr(A, op.c, seq)) : nullptr;
+  const bool store_i32 = !(op.flags & F_NOI32);
+  uint16_t* D16 = dq ? reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(op.dconst), seq)) : nullptr;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t p = warp + 8 * i;
@@ -598,7 +606,13 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
         v.x = static_cast<int32_t>(static_cast<uint32_t>(v.x) + static_cast<uint32_t>(c.x));
         v.y = static_cast<int32_t>(static_cast<uint32_t>(v.y) + static_cast<uint32_t>(c.y));
       }
-      *reinterpret_cast<int2*>(D + row * N + col) = v;
+      if (store_i32) *reinterpret_cast<int2*>(D + row * N + col) = v;
+      if (dq) {   // DEQUANT_ACCUM: f16(f32(acc) * f32(scale[col]))
+        const uint32_t sc = *reinterpret_cast<const uint32_t*>(Pc + col * 2);
+        const uint16_t lo = f2h(__fmul_rn(__int2float_rn(v.x), h2f(static_cast<uint16_t>(sc & 0xFFFF))));
+        const uint16_t hi = f2h(__fmul_rn(__int2float_rn(v.y), h2f(static_cast<uint16_t>(sc >> 16))));
+        *reinterpret_cast<uint32_t*>(D16 + row * N + col) = uint32_t(lo) | (uint32_t(hi) << 16);
+      }
     }
   }
 }

@@ -77,6 +77,9 @@ constexpr uint16_t F_TC128 = 256;      // F_TC MATMUL with N >= 128: 128-column 
 constexpr uint16_t F_QB = 512;         // wide MATMUL: operand b is FP16 and is quantised on load
                                        // (rint(x * s[1]), NaN -> 0, clipped to int8), as QUANT does
 constexpr uint16_t F_QA = 1024;        // wide MATMUL: operand a is FP16, quantised on load with s[0]
+constexpr uint16_t F_DQ = 2048;        // wide MATMUL: also writes DEQUANT_ACCUM's FP16 result,
+                                       // f16(f32(acc) * f32(c[col])), to the unit address in dconst
+constexpr uint16_t F_NOI32 = 4096;     // F_DQ MATMUL whose int32 result nothing reads: not stored
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 
 // Most runs an operand read through a segment list may have (longer lists are gathered).
@@ -130,12 +133,12 @@ constexpr uint64_t kEwTaskElems = 8192;
 #endif
 
 // Element-wise task size by op kind: GELU (float64 tanh per element) takes
-// 2048-element tasks (one group of 8 per thread) so its work spreads over
+// 4096-element tasks (two groups of 8 per thread) so its work spreads over
 // more SMs; QUANT (FP16 in, staged in shared memory, 32 KB per task) takes
 // twice kEwTaskElems to halve its per-task overhead; the rest take
 // kEwTaskElems.
 TAC_HD constexpr uint32_t ew_task_elems(uint32_t kind) {
-  return (kind == K_GELU_F16 || kind == K_GELU_I8) ? 2048u
+  return (kind == K_GELU_F16 || kind == K_GELU_I8) ? 4096u
          : kind == K_QUANT                         ? 2u * uint32_t(kEwTaskElems)
                                                    : uint32_t(kEwTaskElems);
 }
@@ -152,7 +155,7 @@ TAC_HD constexpr bool wide_mm_a_in_bt(uint32_t M, uint32_t N, uint32_t K, bool b
 TAC_HD constexpr uint32_t wide_mm_smem(uint32_t M, uint32_t N, uint32_t K, bool bt, bool qb, bool qa = false) {
   return (((M + 15) / 16) * 16) * (((K + 31) & ~31u) + 16) + (((N + 7) / 8) * 8) * (((K + 31) & ~31u) + 16) +
          (bt ? 0u : ((K + 31) & ~31u) * N) + (qb ? K * N * 2 : 0u) +
-         ((qa && !wide_mm_a_in_bt(M, N, K, bt)) ? M * K * 2 : 0u);
+         ((qa && !wide_mm_a_in_bt(M, N, K, bt)) ? M * K * 2 : 0u) + 512u;   // + the F_DQ scale row
 }
 TAC_HD constexpr bool wide_mm_ok(uint32_t M, uint32_t N, uint32_t K, bool bt, bool qb, bool qa = false) {
   return M > 0 && M <= 32 && K > 0 && K <= 256 && N > 0 && N <= 256 && M % 16 == 0 && K % 16 == 0 &&

@@ -125,7 +125,11 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
                 B = raw.reshape(Kd, N).astype(np.int32)
             acc = m.mem(c, M * N * 4).view(np.int32).reshape(M, N).copy() if op["flags"] & 1 else np.zeros((M, N), np.int32)
             acc += A @ B
-            m.mem(d, M * N * 4)[:] = acc.view(np.uint8).ravel()
+            if not op["flags"] & 4096:   # F_NOI32: the int32 result is not stored
+                m.mem(d, M * N * 4)[:] = acc.view(np.uint8).ravel()
+            if op["flags"] & 2048:   # F_DQ: DEQUANT_ACCUM's FP16 result as well
+                out = (acc.astype(np.float32) * _f16(m, c, N).reshape(1, N)).astype(np.float16)
+                m.mem(int(op["dconst"]), M * N * 2)[:] = out.view(np.uint8).ravel()
         elif k in (K["REQUANT"], K["REQUANT_PC"]):
             acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
             sc = np.float32(m.sreg(s[0])) if k == K["REQUANT"] else _f16(m, b, N).reshape(1, N)

@@ -325,7 +325,7 @@ def test_tasks_cover_every_sequence_and_element_once(batch):
     ops, segs, tasks, lv = p.dump()
     EW_TASK = 8192
     ew_kinds = set(range(7, 18)) | {19, 27}
-    task_elems = lambda kind: 2048 if kind in (19, 27) else (2 * EW_TASK if kind == 16 else EW_TASK)  # noqa: E731
+    task_elems = lambda kind: 4096 if kind in (19, 27) else (2 * EW_TASK if kind == 16 else EW_TASK)  # noqa: E731
     seen = {}
     for t in tasks:
         op = ops[t["op"]]
