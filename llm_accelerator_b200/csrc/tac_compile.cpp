@@ -516,10 +516,38 @@ class Compiler {
     mm.flags |= F_DQ;
     mm.c = mb[0];
     mm.dconst = static_cast<int64_t>(out);
+    dq_out_[out] = idx;
     for (auto& w : acc.writes)
       if (cls(w.first) == PC_ARENA) op_arena_writes_[idx].push_back(w);
     if (cls(mb[0]) == PC_ARENA) op_arena_reads_[idx].push_back({mb[0], nb});
     if (cls(mb[0]) != PC_ARENA && cls(mb[0]) != PC_SHARED) op_pure_[idx] = 0;   // conservative
+    return true;
+  }
+
+  // SOFTMAX / MASKED_SOFTMAX of a fused DEQUANT's whole FP16 result: the
+  // MATMUL computes the rows as well (F_SM), from shared memory.  `sm` holds
+  // the softmax's attention context (set by the masked variant's check).
+  bool fuse_softmax(uint32_t s1, uint32_t d, uint64_t M, uint64_t N, const DevOp& sm) {
+    if (N % 8 || M > 32) return false;
+    const uint64_t na = M * N * 2 / kUnit;
+    const uint64_t* ma = &sram_[s1];
+    if (!contiguous(ma, na)) return false;
+    auto it = dq_out_.find(ma[0]);
+    if (it == dq_out_.end()) return false;
+    const uint32_t idx = it->second;
+    DevOp& mm = P->ops[idx];
+    if (!(mm.flags & F_DQ) || (mm.flags & F_SM) || uint64_t(mm.M) != M || uint64_t(mm.N) != N) return false;
+    Access acc;
+    const uint64_t out = dst(d, M * N * 2, acc);
+    commit(acc, int32_t(mm.level));
+    mm.flags |= F_SM | (sm.kind == K_MASKED_SOFTMAX_F16 ? F_SMMASK : 0) | (sm.flags & F_ATTN_DYN);
+    mm.attn_qrb = sm.attn_qrb;
+    mm.attn_vkl = sm.attn_vkl;
+    mm.attn_mode = sm.attn_mode;
+    mm.param = sm.param;
+    mm.nbytes = out;
+    for (auto& w : acc.writes)
+      if (cls(w.first) == PC_ARENA) op_arena_writes_[idx].push_back(w);
     return true;
   }
 
@@ -746,8 +774,9 @@ class Compiler {
     uint64_t epoch;
   };
   std::unordered_map<uint64_t, QuantOf> quantized_;
-  // int32 result extent of each emitted wide MATMUL (no accumulate) -> op index
-  std::unordered_map<uint64_t, uint32_t> mm_out_;
+  // int32 result extent of each emitted wide MATMUL (no accumulate) -> op index,
+  // and the FP16 result extent of each fused DEQUANT -> op index
+  std::unordered_map<uint64_t, uint32_t> mm_out_, dq_out_;
   uint64_t home_writes_ = 0;
   // per emitted op: its arena reads and writes, and whether arena writes are its only effect
   std::vector<std::vector<std::pair<uint64_t, uint64_t>>> op_arena_reads_, op_arena_writes_;
@@ -1240,6 +1269,10 @@ int Compiler::h_rtype(const Insn& x) {
       TRY(span(x.dst_buf, x.dst_off, M * N * 2));
       op.kind = o == OP_GELU_FP32 ? K_GELU_F16
                                   : (o == OP_SOFTMAX_FP32 ? K_SOFTMAX_F16 : K_MASKED_SOFTMAX_F16);
+      if (op.kind != K_GELU_F16 && fuse_softmax(s1, d, M, N, op)) {
+        cycles_ += M * N;
+        return 0;
+      }
       op.a = src(s1, M * N * 2, acc);
       op.d = dst(d, M * N * 2, acc);
       cycles_ += M * N;
@@ -1495,6 +1528,8 @@ void Compiler::drop_dead_ops() {
     DevOp& op = P->ops[i];
     if ((op.flags & F_DQ) && cls(op.d) == PC_ARENA && !any_read(op.d, uint64_t(op.M) * op.N * 4 / kUnit))
       op.flags |= F_NOI32;   // only the FP16 result is read
+    if ((op.flags & F_SM) && !any_read(static_cast<uint64_t>(op.dconst), uint64_t(op.M) * op.N * 2 / kUnit))
+      op.flags |= F_NODQ;    // only the softmax rows are read
     for (auto& r : op_arena_reads_[i]) mark(r.first, r.second);
   }
   size_t j = 0;

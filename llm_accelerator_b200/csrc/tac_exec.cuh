@@ -436,6 +436,36 @@ __device__ __forceinline__ uint2 pack_b(const int8_t (&q)[8]) {
   return make_uint2(x, y);
 }
 
+// One FP16 softmax row (SOFTMAX_FP32 / MASKED_SOFTMAX_FP32, simulator.py:964-1037)
+// held as floats in rowbuf (n a multiple of 8): columns after `last` are
+// masked (last = n - 1 for the plain softmax).  exp in float64 rounded once,
+// NumPy's pairwise row sum, f16(e / sum); a masked row whose sum is zero, or
+// with no visible column (masked and last < 0), writes zeros.
+__device__ __forceinline__ void softmax_row_f16(float* rowbuf, uint32_t n, bool masked, int64_t last,
+                                                uint16_t* out, uint32_t* pw, int lane) {
+  if (masked && last < 0) {
+    for (uint32_t g = lane; g < n / 8; g += 32) reinterpret_cast<uint4*>(out)[g] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint32_t lst = masked ? static_cast<uint32_t>(last) : n - 1;
+  float mx = -INFINITY;
+  for (uint32_t j = lane; j <= lst && j < n; j += 32) mx = fmaxf(mx, rowbuf[j]);
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  __syncwarp();
+  for (uint32_t j = lane; j < n; j += 32) rowbuf[j] = j <= lst ? exp_f32(__fsub_rn(rowbuf[j], mx)) : 0.f;
+  __syncwarp();
+  const float denom = warp_pairwise_sum_smem(rowbuf, n, pw);
+  for (uint32_t g = lane; g < n / 8; g += 32) {
+    uint16_t h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float e = rowbuf[g * 8 + j];
+      h[j] = f2h(!masked ? __fdiv_rn(e, denom) : (denom > 0.f ? __fdiv_rn(e, denom) : 0.f));
+    }
+    reinterpret_cast<uint4*>(out)[g] = pack_h(h);
+  }
+}
+
 // ---------------------------------------------------------------------------------
 // MATMUL with per-sequence operands in the wide shape (F_WIDE: M <= 32,
 // K <= 256, N <= 256, shared memory by wide_mm_smem): one task computes every
@@ -457,7 +487,7 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   uint8_t* Braw = Bt + n8 * 8 * bts;                // [kc32][N] (not F_BT)
   uint8_t* Bh = Braw + (bt ? 0u : kc32 * N);        // FP16 B (F_QB)
   uint8_t* Ah = wide_mm_a_in_bt(M, N, K, bt) ? Bt : Bh + (qb ? K * N * 2 : 0u);   // FP16 A (F_QA)
-  uint8_t* Pc = Bh + (qb ? K * N * 2 : 0u) + ((qa && !wide_mm_a_in_bt(M, N, K, bt)) ? M * K * 2 : 0u);   // F_DQ row
+  uint8_t* Pc = smem + kWideMmSmem - 512;   // F_DQ scale row: the last 512 bytes (the budget's reserve)
   const bool dq = (op.flags & F_DQ) != 0;
   const uint8_t* Ag = pptr(A, op.a, seq);
   const uint8_t* Bg = pptr(A, op.b, seq);
@@ -562,6 +592,13 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   const int warp = htid() >> 5, lane = htid() & 31;
   const int g = lane >> 2, q = lane & 3;
   const uint32_t pairs = nblocks * n8;
+  const bool sm = (op.flags & F_SM) != 0;
+  uint32_t qrb = op.attn_qrb, vkl = op.attn_vkl;
+  if (sm && (op.flags & F_ATTN_DYN)) {
+    const uint64_t pv = A.params[uint64_t(seq) * A.n_params + op.param];
+    qrb = pv & 0xFFFF;
+    vkl = (pv >> 16) & 0xFFFF;
+  }
   int acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -585,10 +622,19 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
       mma_s8(acc[i], a0, a1, a2, a3, b0, b1);
     }
   }
+  if (sm) hsync();   // every warp is done with the operand tiles: the rows reuse the space
+  // F_SM: the dequantised rows [M][N] FP16 in shared memory, then per-warp
+  // float row buffers and pairwise-sum scratch behind them
+  uint16_t* Sc = reinterpret_cast<uint16_t*>(smem);
+  float* rows = reinterpret_cast<float*>(smem + 32 * 256 * 2);
+  uint32_t* pws = reinterpret_cast<uint32_t*>(smem + 32 * 256 * 2 + kWarps * 256 * 4);
   int32_t* D = reinterpret_cast<int32_t*>(pptr(A, op.d, seq));
   const int32_t* C = (op.flags & F_ACCUMULATE) ? reinterpret_cast<const int32_t*>(pptr(A, op.c, seq)) : nullptr;
   const bool store_i32 = !(op.flags & F_NOI32);
+  const bool store_dq = dq && !(op.flags & F_NODQ);
   uint16_t* D16 = dq ? reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(op.dconst), seq)) : nullptr;
+  // the F_DQ scale row: read from shared memory before the rows overwrite it
+  const uint8_t* Pcs = Pc;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t p = warp + 8 * i;
@@ -608,11 +654,27 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
       }
       if (store_i32) *reinterpret_cast<int2*>(D + row * N + col) = v;
       if (dq) {   // DEQUANT_ACCUM: f16(f32(acc) * f32(scale[col]))
-        const uint32_t sc = *reinterpret_cast<const uint32_t*>(Pc + col * 2);
+        const uint32_t sc = *reinterpret_cast<const uint32_t*>(Pcs + col * 2);
         const uint16_t lo = f2h(__fmul_rn(__int2float_rn(v.x), h2f(static_cast<uint16_t>(sc & 0xFFFF))));
         const uint16_t hi = f2h(__fmul_rn(__int2float_rn(v.y), h2f(static_cast<uint16_t>(sc >> 16))));
-        *reinterpret_cast<uint32_t*>(D16 + row * N + col) = uint32_t(lo) | (uint32_t(hi) << 16);
+        const uint32_t pr = uint32_t(lo) | (uint32_t(hi) << 16);
+        if (store_dq) *reinterpret_cast<uint32_t*>(D16 + row * N + col) = pr;
+        if (sm) *reinterpret_cast<uint32_t*>(Sc + row * N + col) = pr;
       }
+    }
+  }
+  if (sm) {
+    hsync();
+    uint16_t* out = reinterpret_cast<uint16_t*>(pptr(A, op.nbytes, seq));
+    const bool masked = (op.flags & F_SMMASK) != 0;
+    float* rb = rows + warp * N;
+    uint32_t* pw = pws + warp * (3 * kPwMaxLeaves);
+    for (uint32_t r = warp; r < M; r += kWarps) {
+      for (uint32_t j = lane; j < N; j += 32) rb[j] = h2f(Sc[r * N + j]);
+      __syncwarp();
+      const int64_t lt = int64_t(r) + qrb < int64_t(vkl) - 1 ? int64_t(r) + qrb : int64_t(vkl) - 1;
+      softmax_row_f16(rb, N, masked, masked ? lt : int64_t(N) - 1, out + uint64_t(r) * N, pw, lane);
+      __syncwarp();
     }
   }
 }
@@ -1256,6 +1318,7 @@ __device__ __forceinline__ float in_val(const ExecArgs& A, const DevOp& op, uint
   }
 }
 
+
 // One row of a row op (op_rows); a buffered FP16 row is already in rowbuf.
 __device__ __forceinline__ void row_one(const ExecArgs& A, const DevOp& op, uint32_t seq, uint32_t r, float* rowbuf,
                                        uint32_t* pw, bool buffered, bool fp16_in, float in_scale, float out_scale,
@@ -1323,6 +1386,12 @@ __device__ __forceinline__ void row_one(const ExecArgs& A, const DevOp& op, uint
   }
 
   // softmax family
+  if ((op.kind == K_SOFTMAX_F16 || op.kind == K_MASKED_SOFTMAX_F16) && buffered && N % 8 == 0) {
+    const bool mk = op.kind == K_MASKED_SOFTMAX_F16;
+    const int64_t lt = int64_t(r) + qrb < int64_t(vkl) - 1 ? int64_t(r) + qrb : int64_t(vkl) - 1;
+    softmax_row_f16(rowbuf, N, mk, mk ? lt : int64_t(N) - 1, reinterpret_cast<uint16_t*>(d) + base, pw, lane);
+    return;
+  }
   uint32_t last = N - 1;        // last visible column (FP16 masked variant)
   bool masked_f16 = op.kind == K_MASKED_SOFTMAX_F16;
   bool masked_i8 = op.kind == K_MASKED_SOFTMAX_I8;

@@ -80,6 +80,10 @@ constexpr uint16_t F_QA = 1024;        // wide MATMUL: operand a is FP16, quanti
 constexpr uint16_t F_DQ = 2048;        // wide MATMUL: also writes DEQUANT_ACCUM's FP16 result,
                                        // f16(f32(acc) * f32(c[col])), to the unit address in dconst
 constexpr uint16_t F_NOI32 = 4096;     // F_DQ MATMUL whose int32 result nothing reads: not stored
+constexpr uint16_t F_SM = 8192;        // F_DQ MATMUL: also the FP16 softmax of the dequantised rows
+                                       // (attention context in attn_* / param, output unit in nbytes)
+constexpr uint16_t F_SMMASK = 16384;   // F_SM: the masked softmax
+constexpr uint16_t F_NODQ = 32768;     // F_SM MATMUL whose dequantised rows nothing reads: not stored
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 
 // Most runs an operand read through a segment list may have (longer lists are gathered).

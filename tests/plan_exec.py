@@ -73,6 +73,35 @@ def _seg_read(m: PlanMachine, op, segs, nbytes: int) -> np.ndarray:
     return out
 
 
+def _attn_context(op, params):
+    """(query_row_base, valid_kv_len) of a masked softmax: from its runtime
+    parameter when the context is runtime-configured (flag 4), else the op."""
+    if op["flags"] & 4:
+        v = int(params[int(op["param"])])
+        return v & 0xFFFF, (v >> 16) & 0xFFFF
+    return int(op["attn_qrb"]), int(op["attn_vkl"])
+
+
+def _softmax_rows(src, masked: bool, qrb: int, vkl: int):
+    """FP32 rows of SOFTMAX_FP32 / MASKED_SOFTMAX_FP32 (simulator.py:964-1037)."""
+    M, N = src.shape
+    if not masked:
+        e = np.exp((src - src.max(axis=-1, keepdims=True)).astype(np.float32))
+        return (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
+    out = np.zeros((M, N), np.float32)
+    for i2 in range(M):
+        last = min(i2 + qrb, vkl - 1)
+        row = src[i2].copy()
+        if last + 1 < N:
+            row[last + 1:] = -np.inf
+        e = np.exp((row - float(row.max())).astype(np.float32))
+        if last + 1 < N:
+            e[last + 1:] = 0.0
+        den = float(e.sum())
+        out[i2] = e / den if den > 0 else 0.0
+    return out
+
+
 def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
     """Executes ops in level order, within a level in op order (reverse=True:
     the opposite order; ops of one level must not depend on one another, so
@@ -129,7 +158,13 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
                 m.mem(d, M * N * 4)[:] = acc.view(np.uint8).ravel()
             if op["flags"] & 2048:   # F_DQ: DEQUANT_ACCUM's FP16 result as well
                 out = (acc.astype(np.float32) * _f16(m, c, N).reshape(1, N)).astype(np.float16)
-                m.mem(int(op["dconst"]), M * N * 2)[:] = out.view(np.uint8).ravel()
+                if not op["flags"] & 32768:   # F_NODQ
+                    m.mem(int(op["dconst"]), M * N * 2)[:] = out.view(np.uint8).ravel()
+                if op["flags"] & 8192:   # F_SM: the softmax rows of the dequantised result
+                    masked = bool(op["flags"] & 16384)
+                    qrb, vkl = _attn_context(op, params)
+                    sm = _softmax_rows(out.astype(np.float32), masked, qrb, vkl)
+                    m.mem(int(op["nbytes"]), M * N * 2)[:] = sm.astype(np.float16).view(np.uint8).ravel()
         elif k in (K["REQUANT"], K["REQUANT_PC"]):
             acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
             sc = np.float32(m.sreg(s[0])) if k == K["REQUANT"] else _f16(m, b, N).reshape(1, N)
@@ -154,9 +189,7 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
             v = acc * np.float32(m.sreg(s[0])) + skip * np.float32(m.sreg(s[1]))
             m.mem(d, M * N)[:] = G._sat8(v).view(np.uint8)
         elif k == K["SOFTMAX_F16"]:
-            x = _f16(m, a, M * N).reshape(M, N)
-            e = np.exp((x - x.max(axis=-1, keepdims=True)).astype(np.float32))
-            r = (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
+            r = _softmax_rows(_f16(m, a, M * N).reshape(M, N), False, 0, 0)
             m.mem(d, M * N * 2)[:] = r.astype(np.float16).view(np.uint8).ravel()
         elif k == K["QUANT"]:
             xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
@@ -196,23 +229,8 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
         elif k == K["GELU_F16"]:
             m.mem(d, M * N * 2)[:] = G._gelu_tanh(_f16(m, a, M * N)).astype(np.float32).astype(np.float16).view(np.uint8)
         elif k == K["MASKED_SOFTMAX_F16"]:
-            if op["flags"] & 4:
-                v = int(params[int(op["param"])])
-                qrb, vkl = v & 0xFFFF, (v >> 16) & 0xFFFF
-            else:
-                qrb, vkl = int(op["attn_qrb"]), int(op["attn_vkl"])
-            src = _f16(m, a, M * N).reshape(M, N)
-            out = np.zeros((M, N), np.float32)
-            for i2 in range(M):
-                last = min(i2 + qrb, vkl - 1)
-                row = src[i2].copy()
-                if last + 1 < N:
-                    row[last + 1:] = -np.inf
-                e = np.exp((row - float(row.max())).astype(np.float32))
-                if last + 1 < N:
-                    e[last + 1:] = 0.0
-                den = float(e.sum())
-                out[i2] = e / den if den > 0 else 0.0
+            qrb, vkl = _attn_context(op, params)
+            out = _softmax_rows(_f16(m, a, M * N).reshape(M, N), True, qrb, vkl)
             m.mem(d, M * N * 2)[:] = out.astype(np.float16).view(np.uint8).ravel()
         elif k == K["TRANSPOSE"]:
             src = m.mem(a, M * N).view(np.int8).reshape(M, N)
