@@ -98,6 +98,7 @@ class Compiler {
   int compile();
   void prefetch_hint(const DevOp& op, Task& t) const;
   void drop_dead_ops();
+  void merge_dyn_stores();
   uint64_t dead_ops_ = 0;
 
  private:
@@ -1539,6 +1540,41 @@ void Compiler::drop_dead_ops() {
   P->ops.resize(j);
 }
 
+// The runtime-addressed stores of one level (the K and V appends of every
+// head) become one K_DYN_STORE_MULTI op, so each sequence takes one task for
+// all of them.  Ops of one level are independent, so their order within the
+// merged op does not matter.
+void Compiler::merge_dyn_stores() {
+  std::map<uint32_t, std::vector<uint32_t>> by_level;
+  for (uint32_t i = 0; i < P->ops.size(); ++i) {
+    const DevOp& op = P->ops[i];
+    if (op.kind == K_DYN_STORE && op.param >= 0 && op.dconst >= 0 && op.dconst < (int64_t(1) << 32))
+      by_level[op.level].push_back(i);
+  }
+  std::vector<uint8_t> drop(P->ops.size(), 0);
+  std::vector<DevOp> merged;
+  for (auto& kv : by_level) {
+    if (kv.second.size() < 2) continue;
+    DevOp m = blank(K_DYN_STORE_MULTI);
+    m.level = kv.first;
+    m.pc = P->ops[kv.second.front()].pc;
+    m.seg0 = static_cast<uint32_t>(P->segs.size());
+    for (uint32_t i : kv.second) {
+      const DevOp& op = P->ops[i];
+      P->segs.push_back(Segment{op.a, (uint64_t(uint32_t(op.param)) << 32) | uint64_t(op.dconst), op.nbytes});
+      drop[i] = 1;
+    }
+    m.nseg = static_cast<uint32_t>(kv.second.size());
+    merged.push_back(m);
+  }
+  if (merged.empty()) return;
+  size_t j = 0;
+  for (size_t i = 0; i < P->ops.size(); ++i)
+    if (!drop[i]) P->ops[j++] = P->ops[i];
+  P->ops.resize(j);
+  P->ops.insert(P->ops.end(), merged.begin(), merged.end());
+}
+
 // Splits each op into tasks (tile x sequence group) and orders them by level.
 void Compiler::build_tasks() {
   const uint32_t B = static_cast<uint32_t>(P->batch);
@@ -1616,6 +1652,7 @@ void Compiler::build_tasks() {
       case K_MAX_ABS:
       case K_DYN_LOAD:
       case K_DYN_STORE:
+      case K_DYN_STORE_MULTI:
         per_seq(i, 1);
         break;
       case K_LAYERNORM_F16: case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16:
@@ -1820,6 +1857,7 @@ int Compiler::compile() {
   if (status == TAC_E_UNSUPPORTED || status == TAC_E_SHARED_WRITE) return status;
   finalize();
   drop_dead_ops();
+  merge_dyn_stores();
   build_tasks();
 
   tac_exec_info& I = P->info;

@@ -155,6 +155,24 @@ __device__ __noinline__ void op_dyn_copy(const ExecArgs& A, const DevOp& op, con
   for (uint64_t u = htid(); u < n; u += kThreads) dst[u] = __ldcg(src + u);
 }
 
+// The runtime-addressed stores of one level for one sequence: eight threads
+// per store, each taking 16-byte units of it; the address checks of
+// op_dyn_copy apply to every store.
+__device__ __noinline__ void op_dyn_store_multi(const ExecArgs& A, const DevOp& op, const Task& t, uint32_t opi) {
+  const uint32_t seq = t.seq0;
+  for (uint32_t k = htid() / 8; k < op.nseg; k += kThreads / 8) {
+    const Segment sg = A.segs[op.seg0 + k];
+    const uint64_t addr = A.params[uint64_t(seq) * A.n_params + (sg.dst >> 32)] + (sg.dst & 0xFFFFFFFFull);
+    if ((addr & 15) || addr + sg.n > A.dram_bytes || addr < A.shared_bytes) {
+      if ((htid() & 7) == 0) raise_fault(A, DF_DYN_ADDRESS, opi, seq);
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(pptr(A, sg.src, seq));
+    uint4* dst = reinterpret_cast<uint4*>(dram_ptr(A, addr, seq));
+    for (uint64_t u = htid() & 7; u < sg.n / 16; u += 8) dst[u] = __ldcg(src + u);
+  }
+}
+
 // int8 [rows, cols] -> [cols, rows].  A matrix of at most kTransposeSmem bytes
 // (one task) is staged in shared memory: 16-byte coalesced loads, then each
 // thread gathers 16 consecutive output bytes of one column.  Larger matrices
@@ -1635,6 +1653,7 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_GATHER: op_gather(A, op, t); break;
     case K_DYN_LOAD:
     case K_DYN_STORE: op_dyn_copy(A, op, t, t.op); break;
+    case K_DYN_STORE_MULTI: op_dyn_store_multi(A, op, t, t.op); break;
     case K_SREG_LOAD: op_sreg_load(A, op, t); break;
     case K_SREG_FINAL: op_sreg_final(A, op, t); break;
     case K_MATMUL:

@@ -59,6 +59,8 @@ enum DevKind : uint16_t {
   K_GELU_I8,               // legacy INT8-I/O GELU
   K_SOFTMAX_ATTNV,         // legacy fused softmax(QK^T) @ V -> int8
   K_MASKED_SOFTMAX_ATTNV,  // legacy fused masked softmax(QK^T) @ V -> int8
+  K_DYN_STORE_MULTI,       // the runtime-addressed stores of one level: segment k copies n bytes
+                           // from src to DRAM at params[dst >> 32] + (dst & 0xFFFFFFFF)
   K_NUM_KINDS
 };
 

@@ -1,0 +1,105 @@
+"""Device-side profile of compiled decode steps (per level and per task).
+
+    python -m llm_accelerator_b200.profile [--recipe tests/golden/recipe_gpt2_medium.npz]
+                                           [--batch 64] [--steps 3] [--mhz 1965]
+
+Runs a prefill and two warm-up decode steps of a GPT-2 recipe through
+BatchedRunner, then profiles --steps decode steps with the engine's profiling
+mode 2: the device time at the end of every plan level (globaltimer) and the
+SM cycles of every task.  Prints, per op kind and shape, the task count, the
+median and 90th-percentile task time, and the task time summed over all
+halves divided by the number of halves; then the step's level time, the sum
+over levels of the busiest half's task time, and the rest (the grid-barrier
+floor).  While profiling, the executor adds one clock read and one store per
+task and nothing else.
+"""
+from __future__ import annotations
+
+import argparse
+import collections
+from pathlib import Path
+
+import numpy as np
+
+KIND_NAMES = {1: "GATHER", 2: "DYN_LOAD", 3: "DYN_STORE", 4: "SREG_LOAD", 5: "SREG_FINAL", 6: "MATMUL",
+              7: "REQUANT", 8: "REQUANT_PC", 9: "SCALE_MUL_I32", 10: "SCALE_MUL_I8", 11: "VADD_I8",
+              12: "VADD_I32", 13: "DEQUANT_ADD", 14: "DEQUANT", 15: "DEQ_SCALED", 16: "QUANT", 17: "VADD_F16",
+              18: "LN", 19: "GELU", 20: "SOFTMAX", 21: "MSOFTMAX", 22: "MAX_ABS", 23: "TRANSPOSE",
+              24: "LN_I8", 25: "SOFTMAX_I8", 26: "MSOFTMAX_I8", 27: "GELU_I8", 28: "SOFTMAX_ATTNV",
+              29: "MSOFTMAX_ATTNV", 30: "DYN_STORE_MULTI"}
+SHARED = 1 << 63
+
+
+def op_label(op) -> str:
+    """Kind and shape of a plan op, with the fusions a MATMUL carries."""
+    k = KIND_NAMES.get(int(op["kind"]), str(int(op["kind"])))
+    f = int(op["flags"])
+    if k == "MATMUL":
+        tags = [t for bit, t in ((8, "tc"), (512, "qB"), (1024, "qA"), (128, "Bt"), (2048, "dq"), (8192, "softmax"))
+                if f & bit]
+        k += (f"[{op['M']}x{op['K']}x{op['N']}{'s' if int(op['b']) & SHARED else 'p'}]" +
+              ("+" + "+".join(tags) if tags else ""))
+    elif k not in ("GATHER", "DYN_STORE", "DYN_LOAD", "DYN_STORE_MULTI", "TRANSPOSE", "SREG_LOAD", "SREG_FINAL"):
+        k += f"[{op['M']}x{op['N']}]" + ("seg" if f & 32 else "")
+    return k
+
+
+def profile_decode(recipe: str, batch: int, steps: int = 3, device: int = 0):
+    """(level_ns, task_cycles, ops, tasks, level_offsets, halves) of the decode
+    plan, medians over `steps` profiled decode steps."""
+    from .recipe import load_recipe
+    from .runner import BatchedRunner
+    b = load_recipe(recipe)
+    br = BatchedRunner(b, batch, device=device)
+    toks = np.arange(batch) % 50257
+    br.step("prefill", toks, np.zeros(batch, int))
+    for pos in (1, 2):
+        br.step("decode", toks, np.full(batch, pos))
+    br.engine.set_profiling(True, tasks=True)
+    durs, cycs = [], []
+    for i in range(steps):
+        br.step("decode", toks, np.full(batch, 3 + i))
+        durs.append(np.diff(br.engine.read_profile().astype(np.int64)))
+        cycs.append(br.engine.read_task_profile().astype(np.int64))
+    br.engine.set_profiling(False)
+    ops, _, tasks, lv = br.plans["decode"].dump()
+    halves = 2 * br.engine.grid()
+    return (np.median(np.stack(durs), axis=0), np.median(np.stack(cycs), axis=0), ops, tasks, lv, halves)
+
+
+def summarize(level_ns, task_cycles, ops, tasks, lv, halves: int, mhz: float, top: int = 25) -> str:
+    per = collections.defaultdict(list)
+    for i, t in enumerate(tasks):
+        per[op_label(ops[int(t["op"])])].append(task_cycles[i])
+    lines = [f"{'op: kind[M x K x N] or [M x N], fusions':56s} {'tasks':>7s} {'median':>9s} {'p90':>9s} "
+             f"{'sum/halves':>11s}"]
+    for k, v in sorted(per.items(), key=lambda kv: -sum(kv[1]))[:top]:
+        v = np.asarray(v, float) / mhz
+        lines.append(f"{k:56s} {len(v):7d} {np.median(v):7.2f}us {np.percentile(v, 90):7.2f}us "
+                     f"{v.sum() / halves:9.1f}us")
+    busy = 0.0
+    for L in range(len(level_ns)):
+        c = task_cycles[lv[L]:lv[L + 1]]
+        h = np.zeros(halves)
+        np.add.at(h, np.arange(len(c)) % halves, c)
+        busy += h.max() / mhz
+    total = float(np.sum(level_ns)) / 1e3
+    lines.append(f"levels {len(level_ns)}, tasks {len(tasks)}, level time {total:.0f} us, busiest-half task time "
+                 f"{busy:.0f} us, barrier floor {total - busy:.0f} us (task times at {mhz:.0f} MHz)")
+    return "\n".join(lines)
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    root = Path(__file__).resolve().parent.parent
+    ap.add_argument("--recipe", default=str(root / "tests" / "golden" / "recipe_gpt2_medium.npz"))
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--mhz", type=float, default=1965.0, help="SM clock that converts task cycles to time")
+    ap.add_argument("--top", type=int, default=25)
+    a = ap.parse_args(argv)
+    print(summarize(*profile_decode(a.recipe, a.batch, a.steps), mhz=a.mhz, top=a.top))
+
+
+if __name__ == "__main__":
+    main()

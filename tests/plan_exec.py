@@ -18,7 +18,7 @@ CONST = 1 << 31
 K = dict(GATHER=1, DYN_LOAD=2, DYN_STORE=3, SREG_LOAD=4, SREG_FINAL=5, MATMUL=6, REQUANT=7, REQUANT_PC=8,
          SCALE_MUL_I32=9, SCALE_MUL_I8=10, VADD_I8=11, VADD_I32=12, DEQUANT_ADD=13, DEQUANT_ACCUM=14,
          DEQUANT_SCALED=15, QUANT=16, VADD_F16=17, LAYERNORM_F16=18, GELU_F16=19, SOFTMAX_F16=20,
-         MASKED_SOFTMAX_F16=21, MAX_ABS=22, TRANSPOSE=23)
+         MASKED_SOFTMAX_F16=21, MAX_ABS=22, TRANSPOSE=23, DYN_STORE_MULTI=30)
 
 
 class PlanMachine:
@@ -123,6 +123,11 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
                 data.append((int(sg["dst"]), m.mem(int(sg["src"]), int(sg["n"]) * 16).copy()))
             for dst, v in data:
                 m.mem(dst, len(v))[:] = v
+        elif k == K["DYN_STORE_MULTI"]:
+            for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]:
+                dstw, n = int(sg["dst"]), int(sg["n"])
+                addr = int(params[dstw >> 32]) + (dstw & 0xFFFFFFFF)
+                m.dram_mem(addr, n)[:] = m.mem(int(sg["src"]), n)
         elif k in (K["DYN_LOAD"], K["DYN_STORE"]):
             addr = int(params[int(op["param"])]) + int(op["dconst"])
             n = int(op["nbytes"])
