@@ -525,6 +525,46 @@ class Compiler {
     return true;
   }
 
+  // DEQUANT_ACCUM_FP32_SCALED of a tcgen05 MATMUL's whole int32 result: the
+  // MATMUL's epilogue writes the FP16 result (FX_DQS), provided the
+  // [scale | bias] rows and the activation-scale register are ready by its
+  // level.  The DEQUANT's output extent is committed at that level.
+  bool fuse_dequant_scaled(uint32_t s1, uint32_t s2, uint32_t d, uint64_t M, uint64_t N, uint32_t sreg) {
+    if ((N * 2) % kUnit) return false;
+    const uint64_t na = M * N * 4 / kUnit, nh = N * 2 / kUnit;
+    const uint64_t* ma = &sram_[s1];
+    const uint64_t* mb = &sram_[s2];
+    if (!contiguous(ma, na) || !contiguous(mb, nh) || !contiguous(mb + nh, nh)) return false;
+    auto it = tc_out_.find(ma[0]);
+    if (it == tc_out_.end()) return false;
+    const uint32_t idx = it->second;
+    DevOp& mm = P->ops[idx];
+    if ((mm.flags2 & FX_DQS) || uint64_t(mm.M) != M || uint64_t(mm.N) != N) return false;
+    Access probe;
+    probe.reads.push_back({mb[0], nh});
+    probe.reads.push_back({mb[nh], nh});
+    read_sreg(probe, sreg);
+    if (level_for(probe) > int32_t(mm.level)) return false;
+    Access acc;
+    acc.reads = probe.reads;
+    acc.slot_reads = probe.slot_reads;
+    acc.sreg_home_read = probe.sreg_home_read;
+    const uint64_t out = dst(d, M * N * 2, acc);
+    commit(acc, int32_t(mm.level));
+    mm.flags2 |= FX_DQS;
+    mm.c = mb[0];
+    mm.nbytes = mb[nh];
+    mm.s[0] = sreg;
+    mm.dconst = static_cast<int64_t>(out);
+    for (auto& w : acc.writes)
+      if (cls(w.first) == PC_ARENA) op_arena_writes_[idx].push_back(w);
+    for (auto& r : acc.reads)
+      if (cls(r.first) == PC_ARENA) op_arena_reads_[idx].push_back(r);
+    for (auto& r : acc.reads)
+      if (cls(r.first) != PC_ARENA && cls(r.first) != PC_SHARED) op_pure_[idx] = 0;   // conservative
+    return true;
+  }
+
   // SOFTMAX / MASKED_SOFTMAX of a fused DEQUANT's whole FP16 result: the
   // MATMUL computes the rows as well (F_SM), from shared memory.  `sm` holds
   // the softmax's attention context (set by the masked variant's check).
@@ -778,6 +818,8 @@ class Compiler {
   // int32 result extent of each emitted wide MATMUL (no accumulate) -> op index,
   // and the FP16 result extent of each fused DEQUANT -> op index
   std::unordered_map<uint64_t, uint32_t> mm_out_, dq_out_;
+  // int32 result extent of each emitted tcgen05 MATMUL (no accumulate) -> op index
+  std::unordered_map<uint64_t, uint32_t> tc_out_;
   uint64_t home_writes_ = 0;
   // per emitted op: its arena reads and writes, and whether arena writes are its only effect
   std::vector<std::vector<std::pair<uint64_t, uint64_t>>> op_arena_reads_, op_arena_writes_;
@@ -1212,6 +1254,10 @@ int Compiler::h_rtype(const Insn& x) {
         cycles_ += M * N;
         return 0;
       }
+      if (o == OP_DEQUANT_ACCUM_FP32_SCALED && fuse_dequant_scaled(s1, s2, d, M, N, sreg_[x.sreg])) {
+        cycles_ += M * N;
+        return 0;
+      }
       op.kind = o == OP_DEQUANT_ACCUM_FP32 ? K_DEQUANT_ACCUM : K_DEQUANT_SCALED;
       if (o == OP_DEQUANT_ACCUM_FP32_SCALED) {
         op.s[0] = sreg_[x.sreg];
@@ -1364,6 +1410,9 @@ int Compiler::h_rtype(const Insn& x) {
   if (op.kind == K_MATMUL && (op.flags & F_WIDE) && !(op.flags & F_ACCUMULATE) && !P->ops.empty() &&
       P->ops.back().kind == K_MATMUL && P->ops.back().d == op.d)
     mm_out_[op.d] = static_cast<uint32_t>(P->ops.size() - 1);
+  if (op.kind == K_MATMUL && tc_eligible(op.a, op.b, op.M, op.N, op.K) && !(op.flags & F_ACCUMULATE) &&
+      !P->ops.empty() && P->ops.back().kind == K_MATMUL && P->ops.back().d == op.d)
+    tc_out_[op.d] = static_cast<uint32_t>(P->ops.size() - 1);
   return 0;
 }
 
@@ -1527,7 +1576,8 @@ void Compiler::drop_dead_ops() {
     if (!live) continue;
     keep[i] = 1;
     DevOp& op = P->ops[i];
-    if ((op.flags & F_DQ) && cls(op.d) == PC_ARENA && !any_read(op.d, uint64_t(op.M) * op.N * 4 / kUnit))
+    if (((op.flags & F_DQ) || (op.flags2 & FX_DQS)) && cls(op.d) == PC_ARENA &&
+        !any_read(op.d, uint64_t(op.M) * op.N * 4 / kUnit))
       op.flags |= F_NOI32;   // only the FP16 result is read
     if ((op.flags & F_SM) && !any_read(static_cast<uint64_t>(op.dconst), uint64_t(op.M) * op.N * 2 / kUnit))
       op.flags |= F_NODQ;    // only the softmax rows are read
@@ -1590,8 +1640,7 @@ void Compiler::build_tasks() {
   // seg0 numbers their pair of tensor maps.
   P->n_tc = 0;
   for (auto& op : P->ops) {
-    if (op.kind == K_MATMUL && (op.b & kSharedBit) && !(op.a & kSharedBit) && op.M < 128 && op.M % 16 == 0 &&
-        op.N % 16 == 0 && op.K % 16 == 0 && op.M > 0 && op.N > 0 && op.K > 0) {
+    if (op.kind == K_MATMUL && tc_eligible(op.a, op.b, op.M, op.N, op.K)) {
       op.flags |= F_TC;
       if (op.N >= 128) op.flags |= F_TC128;
       op.seg0 = P->n_tc++;

@@ -750,6 +750,31 @@ __device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp
     const uint32_t col0 = n0 + h * 32;
     const uint32_t nc = ncols - h * 32 < 32 ? ncols - h * 32 : 32;
     int32_t* D = reinterpret_cast<int32_t*>(pptr(A, op.d, seq)) + uint64_t(row) * N + col0;
+    if (op.flags2 & FX_DQS) {
+      // DEQUANT_ACCUM_FP32_SCALED: f16((f32(acc) * scale[col]) * s0 + bias[col]); the rows are the same
+      // for every lane of the warp
+      const uint16_t* sc = reinterpret_cast<const uint16_t*>(pptr(A, op.c, seq)) + col0;
+      const uint16_t* bi = reinterpret_cast<const uint16_t*>(pptr(A, op.nbytes, seq)) + col0;
+      const float s0 = h2f(sreg_bits(A, op.s[0], seq));
+      uint16_t* O = reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(op.dconst), seq)) +
+                    uint64_t(row) * N + col0;
+#pragma unroll
+      for (uint32_t j = 0; j < 32; j += 8) {
+        if (j < nc) {
+          const uint4 s8 = __ldcg(reinterpret_cast<const uint4*>(sc + j));
+          const uint4 b8 = __ldcg(reinterpret_cast<const uint4*>(bi + j));
+          uint16_t hh[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            float x = __fmul_rn(__int2float_rn(int(v[j + k])), h2f(h_at(s8, k)));
+            x = __fmul_rn(x, s0);
+            hh[k] = f2h(__fadd_rn(x, h2f(h_at(b8, k))));
+          }
+          *reinterpret_cast<uint4*>(O + j) = pack_h(hh);
+        }
+      }
+      if (op.flags & F_NOI32) return;
+    }
     const int32_t* C = (op.flags & F_ACCUMULATE)
                            ? reinterpret_cast<const int32_t*>(pptr(A, op.c, seq)) + uint64_t(row) * N + col0
                            : nullptr;

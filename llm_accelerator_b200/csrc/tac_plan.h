@@ -86,6 +86,12 @@ constexpr uint16_t F_SM = 8192;        // F_DQ MATMUL: also the FP16 softmax of 
                                        // (attention context in attn_* / param, output unit in nbytes)
 constexpr uint16_t F_SMMASK = 16384;   // F_SM: the masked softmax
 constexpr uint16_t F_NODQ = 32768;     // F_SM MATMUL whose dequantised rows nothing reads: not stored
+
+// Flags on DevOp::flags2.
+constexpr uint32_t FX_DQS = 1;         // tcgen05 MATMUL (no accumulate) also writes DEQUANT_SCALED's FP16
+                                       // result f16((f32(acc) * scale[col]) * s[0] + bias[col]) to the unit
+                                       // address in dconst; scale row at c, bias row at nbytes
+
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 
 // Most runs an operand read through a segment list may have (longer lists are gathered).
@@ -101,6 +107,7 @@ struct DevOp {
   uint32_t seg0, nseg;     // K_GATHER: segment range; K_SREG_FINAL: unused
   int32_t param;           // runtime parameter index (dynamic address / attention context)
   uint32_t attn_mode;
+  uint32_t flags2;         // more flags (FX_*)
   int64_t dconst;          // byte constant added to the runtime address
   uint64_t nbytes;         // bytes moved by dynamic copies
   uint32_t attn_qrb, attn_vkl;
@@ -137,6 +144,13 @@ constexpr uint64_t kEwTaskElems = 8192;
 #else
 #define TAC_HD
 #endif
+
+// MATMULs that run on tcgen05: shared weights (B), per-sequence A of fewer
+// than 128 rows (128 / M sequences fill one 128-row tile), 16-multiples.
+TAC_HD constexpr bool tc_eligible(uint64_t a, uint64_t b, uint32_t M, uint32_t N, uint32_t K) {
+  return (b & kSharedBit) && !(a & kSharedBit) && M > 0 && M < 128 && M % 16 == 0 && N > 0 && N % 16 == 0 &&
+         K > 0 && K % 16 == 0;
+}
 
 // Element-wise task size by op kind: GELU (float64 tanh per element) takes
 // 4096-element tasks (two groups of 8 per thread) so its work spreads over

@@ -17,7 +17,7 @@ DEVOP_DTYPE = np.dtype([
     ("kind", "<u2"), ("flags", "<u2"), ("M", "<u4"), ("N", "<u4"), ("K", "<u4"),
     ("a", "<u8"), ("b", "<u8"), ("c", "<u8"), ("d", "<u8"), ("s", "<u4", (4,)),
     ("out_slot", "<u4"), ("seg0", "<u4"), ("nseg", "<u4"), ("param", "<i4"), ("attn_mode", "<u4"),
-    ("_pad", "<u4"), ("dconst", "<i8"), ("nbytes", "<u8"), ("attn_qrb", "<u4"), ("attn_vkl", "<u4"),
+    ("flags2", "<u4"), ("dconst", "<i8"), ("nbytes", "<u8"), ("attn_qrb", "<u4"), ("attn_vkl", "<u4"),
     ("pc", "<u4"), ("level", "<u4")])
 SEGMENT_DTYPE = np.dtype([("src", "<u8"), ("dst", "<u8"), ("n", "<u8")])
 TASK_DTYPE = np.dtype([("op", "<u4"), ("seq0", "<u4"), ("nseq", "<u4"), ("tile", "<u4"), ("aux", "<u4"),

@@ -37,6 +37,8 @@ def op_label(op) -> str:
     if k == "MATMUL":
         tags = [t for bit, t in ((8, "tc"), (512, "qB"), (1024, "qA"), (128, "Bt"), (2048, "dq"), (8192, "softmax"))
                 if f & bit]
+        if int(op["flags2"]) & 1:
+            tags.append("dqs")
         k += (f"[{op['M']}x{op['K']}x{op['N']}{'s' if int(op['b']) & SHARED else 'p'}]" +
               ("+" + "+".join(tags) if tags else ""))
     elif k not in ("GATHER", "DYN_STORE", "DYN_LOAD", "DYN_STORE_MULTI", "TRANSPOSE", "SREG_LOAD", "SREG_FINAL"):

@@ -161,6 +161,10 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
             acc += A @ B
             if not op["flags"] & 4096:   # F_NOI32: the int32 result is not stored
                 m.mem(d, M * N * 4)[:] = acc.view(np.uint8).ravel()
+            if op["flags2"] & 1:   # FX_DQS: DEQUANT_ACCUM_FP32_SCALED's FP16 result as well
+                r = (acc.astype(np.float32) * _f16(m, c, N).reshape(1, N) * np.float32(m.sreg(s[0]))
+                     + _f16(m, int(op["nbytes"]), N).reshape(1, N))
+                m.mem(int(op["dconst"]), M * N * 2)[:] = r.astype(np.float32).astype(np.float16).view(np.uint8).ravel()
             if op["flags"] & 2048:   # F_DQ: DEQUANT_ACCUM's FP16 result as well
                 out = (acc.astype(np.float32) * _f16(m, c, N).reshape(1, N)).astype(np.float16)
                 if not op["flags"] & 32768:   # F_NODQ
