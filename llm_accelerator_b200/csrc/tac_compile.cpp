@@ -525,6 +525,42 @@ class Compiler {
     return true;
   }
 
+  // QUANT of exactly the units a MAX_ABS just reduced, with that MAX_ABS's
+  // inverse scale: the MAX_ABS op writes the int8 result as well (FX_MAXQ).
+  // The input units must be immutable (arena or shared), so the values the
+  // MAX_ABS reads are the ones the QUANT would read; the QUANT's output is
+  // committed at the MAX_ABS's level.  The operand checks (span, buffer
+  // faults) have already run.
+  bool fuse_quant_into_maxabs(const DevOp& q, uint32_t s1, uint32_t d, uint64_t M, uint64_t N) {
+    const uint32_t slot = q.s[0];
+    if (slot & kSregConst || slot < kSregSlotBase) return false;
+    auto it = maxabs_by_slot_.find(slot);
+    if (it == maxabs_by_slot_.end() || it->second.elems != M * N || M * N > 16384) return false;
+    DevOp& mx = P->ops[it->second.op];
+    if (mx.out_slot != slot) return false;
+    const uint64_t n = (M * N * 2 + kUnit - 1) / kUnit;
+    if (it->second.units.size() != n) return false;
+    for (uint64_t i = 0; i < n; ++i) {
+      const uint64_t u = sram_[s1 + i];
+      if (u != it->second.units[i] || (cls(u) != PC_ARENA && cls(u) != PC_SHARED)) return false;
+    }
+    if (mx.flags2 & FX_MAXQ) {   // the same QUANT again: its result is the fused one (as CSE would do)
+      const uint64_t nq = (M * N + kUnit - 1) / kUnit;
+      for (uint64_t i = 0; i < nq; ++i) sram_[d + i] = mx.d + i;
+      cycles_ += M * N;
+      return true;
+    }
+    Access acc;
+    const uint64_t out = dst(d, M * N, acc);
+    commit(acc, int32_t(mx.level));
+    mx.flags2 |= FX_MAXQ;
+    mx.d = out;
+    for (auto& w : acc.writes)
+      if (cls(w.first) == PC_ARENA) op_arena_writes_[it->second.op].push_back(w);
+    cycles_ += M * N;
+    return true;
+  }
+
   // DEQUANT_ACCUM_FP32_SCALED of a tcgen05 MATMUL's whole int32 result: the
   // MATMUL's epilogue writes the FP16 result (FX_DQS), provided the
   // [scale | bias] rows and the activation-scale register are ready by its
@@ -820,6 +856,14 @@ class Compiler {
   std::unordered_map<uint64_t, uint32_t> mm_out_, dq_out_;
   // int32 result extent of each emitted tcgen05 MATMUL (no accumulate) -> op index
   std::unordered_map<uint64_t, uint32_t> tc_out_;
+  // inverse-scale slot of each emitted MAX_ABS -> the op and the physical units it reduced
+  struct MaxAbsOf {
+    uint32_t op = 0;
+    std::vector<uint64_t> units;
+    uint64_t elems = 0;
+  };
+  std::unordered_map<uint32_t, MaxAbsOf> maxabs_by_slot_;
+  std::vector<uint64_t> maxabs_pending_;
   uint64_t home_writes_ = 0;
   // per emitted op: its arena reads and writes, and whether arena writes are its only effect
   std::vector<std::vector<std::pair<uint64_t, uint64_t>>> op_arena_reads_, op_arena_writes_;
@@ -1277,6 +1321,7 @@ int Compiler::h_rtype(const Insn& x) {
       TRY(span(x.dst_buf, x.dst_off, M * N));
       op.kind = K_QUANT;
       op.s[0] = sreg_[x.sreg];
+      if (fuse_quant_into_maxabs(op, s1, d, M, N)) return 0;
       read_sreg(acc, op.s[0]);
       if (!src_segments(s1, M * N * 2, acc, op)) op.a = src(s1, M * N * 2, acc);
       op.d = dst(d, M * N, acc);
@@ -1337,6 +1382,7 @@ int Compiler::h_rtype(const Insn& x) {
       acc.slot_writes.push_back(op.out_slot + 1);
       sreg_[x.sreg] = op.out_slot;
       sreg_[x.sreg + 1] = op.out_slot + 1;
+      maxabs_pending_ = std::vector<uint64_t>(&sram_[s1], &sram_[s1] + (M * N * 2 + kUnit - 1) / kUnit);
       cycles_ += M * N;
       break;
     }
@@ -1405,6 +1451,15 @@ int Compiler::h_rtype(const Insn& x) {
       wide_mm_ok(uint32_t(M), uint32_t(N), uint32_t(K), op.flags & F_BT, op.flags & F_QB, op.flags & F_QA))
     op.flags |= F_WIDE;
   emit_compute(op, acc, d, x.sreg);
+  if (op.kind == K_MAX_ABS) {   // remember the input of the MAX_ABS just emitted
+    if (!P->ops.empty() && P->ops.back().kind == K_MAX_ABS && P->ops.back().out_slot == op.out_slot) {
+      MaxAbsOf& m = maxabs_by_slot_[op.out_slot];
+      m.op = static_cast<uint32_t>(P->ops.size() - 1);
+      m.units = std::move(maxabs_pending_);
+      m.elems = M * N;
+    }
+    maxabs_pending_.clear();
+  }
   if (op.kind == K_QUANT && !(op.flags & F_SEGA) && cls(sram_[d]) == PC_ARENA)
     quantized_[sram_[d]] = QuantOf{op.a, op.s[0], M, N, home_writes_};
   if (op.kind == K_MATMUL && (op.flags & F_WIDE) && !(op.flags & F_ACCUMULATE) && !P->ops.empty() &&

@@ -1215,6 +1215,7 @@ __device__ __noinline__ void op_elementwise(const ExecArgs& A, const DevOp& op, 
 // kSegTableOff bytes and each unit found by binary search, so every thread
 // keeps four 16-byte loads in flight however the runs are sized.
 constexpr uint32_t kSegTableOff = 4096;
+constexpr uint32_t kMaxQStage = 8192;   // MAX_ABS + QUANT: the reduced input, 16384 FP16 at most
 
 __device__ __forceinline__ void seg_stage(const ExecArgs& A, const DevOp& op, uint8_t* smem) {
   uint32_t* ofs = reinterpret_cast<uint32_t*>(smem + kSegTableOff);
@@ -1294,6 +1295,8 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
   const uint4* xv = reinterpret_cast<const uint4*>(x);
   const uint64_t ng = MN / 8;   // MN is a multiple of 256
   const bool seg = op.flags & F_SEGA;
+  const bool maxq = (op.flags2 & FX_MAXQ) != 0;   // also QUANT's result (MN <= 16384)
+  uint4* keep = reinterpret_cast<uint4*>(smem + kMaxQStage);   // the input, kept for the QUANT
   if (seg) seg_stage(A, op, smem);
   for (uint64_t g0 = htid(); g0 < ng; g0 += uint64_t(kThreads) * 8) {
     uint4 v[8];
@@ -1301,6 +1304,13 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
     for (int k = 0; k < 8; ++k) {
       const uint64_t g = g0 + uint64_t(k) * kThreads;
       v[k] = g < ng ? __ldcg(seg ? seg_unit(A, op, smem, seq, uint32_t(g)) : xv + g) : make_uint4(0, 0, 0, 0);
+    }
+    if (maxq) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint64_t g = g0 + uint64_t(k) * kThreads;
+        if (g < ng) keep[g] = v[k];
+      }
     }
 #pragma unroll
     for (int k = 0; k < 8; ++k)
@@ -1332,8 +1342,24 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
     }
     A.sregs[uint64_t(seq) * A.sreg_stride + op.out_slot] = inv;
     A.sregs[uint64_t(seq) * A.sreg_stride + op.out_slot + 1] = fwd;
+    red[kWarps] = inv;
   }
   hsync();
+  if (maxq) {
+    // QUANT's rule with the inverse scale just derived: rint(x * inv), NaN -> 0, clipped to int8
+    const float s0 = h2f(static_cast<uint16_t>(red[kWarps]));
+    int8_t* out = reinterpret_cast<int8_t*>(pptr(A, op.d, seq));
+    for (uint64_t g = htid(); g < ng; g += kThreads) {
+      const uint4 x8 = keep[g];
+      int8_t q8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float r = rintf(__fmul_rn(h2f(h_at(x8, j)), s0));
+        q8[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+      }
+      *reinterpret_cast<uint2*>(out + g * 8) = pack_b(q8);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------
@@ -1729,6 +1755,8 @@ static_assert(sizeof(TcShared) <= 128, "TcShared outgrew its slot");
 static_assert(kStageBytes <= kExecOpSmem, "element-wise staging exceeds the op shared memory");
 static_assert(kWideMmSmem <= kExecOpSmem, "wide MATMUL exceeds the op shared memory");
 static_assert(kSegTableOff + kMaxSegRuns * 12 <= kExecOpSmem, "segment table exceeds the op shared memory");
+static_assert(kSegTableOff + kMaxSegRuns * 12 <= kMaxQStage && kMaxQStage + 16384 * 2 <= kExecOpSmem,
+              "MAX_ABS staging overlaps the segment table or exceeds the op shared memory");
 static_assert(kExecOpSmem % 1024 == 0 || kTcSmem <= kExecOpSmem, "half regions must keep the stage alignment slack");
 static_assert(kExecSmem <= 227 * 1024, "executor shared memory exceeds one CTA's limit");
 

@@ -91,6 +91,8 @@ constexpr uint16_t F_NODQ = 32768;     // F_SM MATMUL whose dequantised rows not
 constexpr uint32_t FX_DQS = 1;         // tcgen05 MATMUL (no accumulate) also writes DEQUANT_SCALED's FP16
                                        // result f16((f32(acc) * scale[col]) * s[0] + bias[col]) to the unit
                                        // address in dconst; scale row at c, bias row at nbytes
+constexpr uint32_t FX_MAXQ = 2;        // MAX_ABS also writes QUANT's int8 result of its input with the
+                                       // inverse scale it derives, to the unit address in d
 
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 

@@ -42,7 +42,7 @@ def op_label(op) -> str:
         k += (f"[{op['M']}x{op['K']}x{op['N']}{'s' if int(op['b']) & SHARED else 'p'}]" +
               ("+" + "+".join(tags) if tags else ""))
     elif k not in ("GATHER", "DYN_STORE", "DYN_LOAD", "DYN_STORE_MULTI", "TRANSPOSE", "SREG_LOAD", "SREG_FINAL"):
-        k += f"[{op['M']}x{op['N']}]" + ("seg" if f & 32 else "")
+        k += f"[{op['M']}x{op['N']}]" + ("seg" if f & 32 else "") + ("+quant" if int(op["flags2"]) & 2 else "")
     return k
 
 

@@ -212,6 +212,10 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
             inv, fwd = G.max_abs_scales(float(np.max(np.abs(xa))))
             m.sregs[int(op["out_slot"])] = np.array([inv], np.float16).view(np.uint16)[0]
             m.sregs[int(op["out_slot"]) + 1] = np.array([fwd], np.float16).view(np.uint16)[0]
+            if op["flags2"] & 2:   # FX_MAXQ: QUANT's result with the inverse scale
+                v = np.round(xa * np.float32(np.float16(inv)))
+                q = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8)
+                m.mem(d, M * N)[:] = q.view(np.uint8)
         elif k in (K["DEQUANT_SCALED"], K["DEQUANT_ACCUM"]):
             acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
             if op["flags"] & 16:   # F_SPLIT: second half of the vector at c
