@@ -99,6 +99,7 @@ class Compiler {
   void prefetch_hint(const DevOp& op, Task& t) const;
   void drop_dead_ops();
   void merge_dyn_stores();
+  void write_vadd_chains();
   uint64_t dead_ops_ = 0;
 
  private:
@@ -525,6 +526,53 @@ class Compiler {
     return true;
   }
 
+  // VADD of the running sum of an earlier VADD (or chain) and a new operand
+  // ready before that op's level: the op becomes (or grows as) a
+  // K_VADD_CHAIN, which adds the operands in the program's order with an FP16
+  // rounding after each add, exactly as the separate VADDs do.  The new sum
+  // is committed at the chain's level.  The chain's segments are written out
+  // after compilation (write_vadd_chains); op.param numbers the chain.  op.d
+  // stays the first sum, the value a CSE hit on the original VADD stands for.
+  bool extend_vadd_chain(uint32_t s1, uint32_t s2, uint32_t d, uint64_t M, uint64_t N) {
+    const uint64_t n = M * N * 2 / kUnit;
+    if ((M * N * 2) % kUnit || n == 0) return false;
+    const uint64_t* ma = &sram_[s1];
+    const uint64_t* mb = &sram_[s2];
+    if (!contiguous(ma, n) || !contiguous(mb, n)) return false;
+    uint64_t tail = ma[0], other = mb[0];
+    auto it = vadd_tail_.find(tail);
+    if (it == vadd_tail_.end()) {
+      std::swap(tail, other);   // a + b == b + a exactly
+      it = vadd_tail_.find(tail);
+    }
+    if (it == vadd_tail_.end() || other == tail) return false;
+    const uint32_t idx = it->second;
+    DevOp& op = P->ops[idx];
+    if (uint64_t(op.M) * op.N != M * N) return false;
+    if (op.kind == K_VADD_CHAIN && chains_[op.param].size() >= kVaddChainMax) return false;
+    Access probe;
+    probe.reads.push_back({other, n});
+    if (level_for(probe) > int32_t(op.level)) return false;
+    if (op.kind == K_VADD_F16) {   // becomes a chain: its own two operands first
+      op.kind = K_VADD_CHAIN;
+      op.param = static_cast<int32_t>(chains_.size());
+      chains_.push_back({Segment{op.a, 0, n}, Segment{op.b, op.d, n}});
+      op.a = op.b = 0;
+    }
+    Access acc;
+    acc.reads.push_back({other, n});
+    const uint64_t out = dst(d, M * N * 2, acc);
+    commit(acc, int32_t(op.level));
+    chains_[op.param].push_back(Segment{other, out, n});
+    vadd_tail_.erase(it);
+    vadd_tail_[out] = idx;
+    for (auto& w : acc.writes)
+      if (cls(w.first) == PC_ARENA) op_arena_writes_[idx].push_back(w);
+    if (cls(other) == PC_ARENA) op_arena_reads_[idx].push_back({other, n});
+    if (cls(other) != PC_ARENA && cls(other) != PC_SHARED) op_pure_[idx] = 0;   // conservative
+    return true;
+  }
+
   // QUANT of exactly the units a MAX_ABS just reduced, with that MAX_ABS's
   // inverse scale: the MAX_ABS op writes the int8 result as well (FX_MAXQ).
   // The input units must be immutable (arena or shared), so the values the
@@ -863,6 +911,9 @@ class Compiler {
     uint64_t elems = 0;
   };
   std::unordered_map<uint32_t, MaxAbsOf> maxabs_by_slot_;
+  // output extent of the latest VADD of each open chain -> op index; operand lists of the chains
+  std::unordered_map<uint64_t, uint32_t> vadd_tail_;
+  std::vector<std::vector<Segment>> chains_;
   std::vector<uint64_t> maxabs_pending_;
   uint64_t home_writes_ = 0;
   // per emitted op: its arena reads and writes, and whether arena writes are its only effect
@@ -1337,6 +1388,10 @@ int Compiler::h_rtype(const Insn& x) {
       TRY(span(x.src2_buf, x.src2_off, b_bytes));
       TRY(span(x.dst_buf, x.dst_off, M * N * 2));
       op.kind = o == OP_VADD_FP32 ? K_VADD_F16 : K_LAYERNORM_F16;
+      if (o == OP_VADD_FP32 && extend_vadd_chain(s1, s2, d, M, N)) {
+        cycles_ += M * N;
+        return 0;
+      }
       if (o == OP_LAYERNORM_FP32) {
         op.a = src(s1, M * N * 2, acc);
         src_pair(s2, N * 2, acc, op);
@@ -1451,6 +1506,9 @@ int Compiler::h_rtype(const Insn& x) {
       wide_mm_ok(uint32_t(M), uint32_t(N), uint32_t(K), op.flags & F_BT, op.flags & F_QB, op.flags & F_QA))
     op.flags |= F_WIDE;
   emit_compute(op, acc, d, x.sreg);
+  if (op.kind == K_VADD_F16 && !(op.flags & F_SEGA) && !P->ops.empty() && P->ops.back().kind == K_VADD_F16 &&
+      P->ops.back().d == op.d && cls(op.d) == PC_ARENA)
+    vadd_tail_[op.d] = static_cast<uint32_t>(P->ops.size() - 1);
   if (op.kind == K_MAX_ABS) {   // remember the input of the MAX_ABS just emitted
     if (!P->ops.empty() && P->ops.back().kind == K_MAX_ABS && P->ops.back().out_slot == op.out_slot) {
       MaxAbsOf& m = maxabs_by_slot_[op.out_slot];
@@ -1625,6 +1683,12 @@ void Compiler::drop_dead_ops() {
     }
     return false;
   };
+  // A K_VADD_CHAIN op sits at the index of its first VADD but reads operands
+  // that ops emitted after it produce: those reads are marked up front (a
+  // chain whose sum nobody reads would keep its operands' producers, which
+  // the decode streams never have).
+  for (const auto& ch : chains_)
+    for (size_t k = 2; k < ch.size(); ++k) mark(ch[k].src, ch[k].n);
   for (size_t i = n; i-- > 0;) {
     bool live = !op_pure_[i];
     for (auto& w : op_arena_writes_[i]) live = live || any_read(w.first, w.second);
@@ -1636,6 +1700,11 @@ void Compiler::drop_dead_ops() {
       op.flags |= F_NOI32;   // only the FP16 result is read
     if ((op.flags & F_SM) && !any_read(static_cast<uint64_t>(op.dconst), uint64_t(op.M) * op.N * 2 / kUnit))
       op.flags |= F_NODQ;    // only the softmax rows are read
+    if (op.kind == K_VADD_CHAIN) {   // intermediate sums nobody reads are not stored (the last always is)
+      auto& ch = chains_[op.param];
+      for (size_t k = 1; k + 1 < ch.size(); ++k)
+        if (ch[k].dst && !any_read(ch[k].dst, ch[k].n)) ch[k].dst = 0;
+    }
     for (auto& r : op_arena_reads_[i]) mark(r.first, r.second);
   }
   size_t j = 0;
@@ -1643,6 +1712,18 @@ void Compiler::drop_dead_ops() {
     if (keep[i]) P->ops[j++] = P->ops[i];
   dead_ops_ = n - j;
   P->ops.resize(j);
+}
+
+// Each K_VADD_CHAIN's operand list goes to the segment table, contiguously.
+void Compiler::write_vadd_chains() {
+  for (DevOp& op : P->ops) {
+    if (op.kind != K_VADD_CHAIN) continue;
+    const auto& ch = chains_[op.param];
+    op.seg0 = static_cast<uint32_t>(P->segs.size());
+    op.nseg = static_cast<uint32_t>(ch.size());
+    P->segs.insert(P->segs.end(), ch.begin(), ch.end());
+    op.param = -1;
+  }
 }
 
 // The runtime-addressed stores of one level (the K and V appends of every
@@ -1759,6 +1840,9 @@ void Compiler::build_tasks() {
       case K_DYN_STORE_MULTI:
         per_seq(i, 1);
         break;
+      case K_VADD_CHAIN:
+        per_seq(i, static_cast<uint32_t>((MN + kVaddChainTask - 1) / kVaddChainTask));
+        break;
       case K_LAYERNORM_F16: case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16:
       case K_LN_I8: case K_SOFTMAX_I8: case K_MASKED_SOFTMAX_I8:
       case K_SOFTMAX_ATTNV: case K_MASKED_SOFTMAX_ATTNV: {
@@ -1854,6 +1938,14 @@ void Compiler::prefetch_hint(const DevOp& op, Task& t) const {
         if (r0 < op.M && op.N % 8 == 0) {
           phys = op.a + r0 * row_units;
           units = std::min<uint64_t>(rpt, op.M - r0) * row_units;
+        }
+        break;
+      }
+      case K_VADD_CHAIN: {   // the first operand's slice of this task
+        const uint64_t e0 = uint64_t(t.tile) * kVaddChainTask;
+        if (op.nseg && e0 < MN) {
+          phys = P->segs[op.seg0].src + e0 * 2 / kUnit;
+          units = std::min<uint64_t>(kVaddChainTask, MN - e0) * 2 / kUnit;
         }
         break;
       }
@@ -1962,6 +2054,7 @@ int Compiler::compile() {
   finalize();
   drop_dead_ops();
   merge_dyn_stores();
+  write_vadd_chains();
   build_tasks();
 
   tac_exec_info& I = P->info;

@@ -1180,6 +1180,54 @@ __device__ __noinline__ void ew_staged(const ExecArgs& A, const DevOp& op, const
   }
 }
 
+// K_VADD_CHAIN: the running FP16 sum of the op's segment operands over
+// kVaddChainTask elements of one sequence.  One thread stages every operand's
+// slice in shared memory with bulk copies on the stage barrier, then each
+// thread adds 8 elements at a time, rounding to FP16 after each add in the
+// program's order, and stores each partial sum whose segment names a dst.
+static_assert(kVaddChainMax * kVaddChainTask * 2 <= kStageBytes, "chain operands exceed the staging area");
+__device__ __noinline__ void op_vadd_chain(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
+                                           TcShared* tc, uint32_t opi) {
+  const uint32_t MN = op.M * op.N;
+  const uint32_t e_begin = t.tile * kVaddChainTask;
+  if (e_begin >= MN) return;   // the same for every thread of the half
+  const uint32_t e_count = min(kVaddChainTask, MN - e_begin);
+  const uint32_t n = op.nseg < kVaddChainMax ? op.nseg : kVaddChainMax;
+  const Segment* sg = A.segs + op.seg0;
+  const uint32_t par = tc->phase_stage;
+  hsync();   // every thread has the parity before it flips
+  if (htid() == 0) {
+    tc->phase_stage = par ^ 1u;
+    sm100::fence_proxy_async();
+    sm100::mbar_arrive_expect_tx(&tc->stage, n * e_count * 2);
+    for (uint32_t k = 0; k < n; ++k)
+      sm100::bulk_g2s(smem + k * e_count * 2, pptr(A, sg[k].src, t.seq0) + uint64_t(e_begin) * 2, e_count * 2,
+                      &tc->stage);
+  }
+  if (!sm100::mbar_wait(&tc->stage, par, nullptr, 0)) {
+    sm100::mbar_wait(&tc->stage, par, nullptr, 0);   // bounded: let copies in flight land, then fault
+    if (htid() == 0) raise_fault(A, DF_STAGE_TIMEOUT, opi, t.seq0);
+    return;
+  }
+  for (uint32_t i = htid() * 8; i < e_count; i += kThreads * 8) {
+    const uint4 x0 = *reinterpret_cast<const uint4*>(smem + uint64_t(i) * 2);
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = h2f(h_at(x0, j));
+    for (uint32_t k = 1; k < n; ++k) {
+      const uint4 x = *reinterpret_cast<const uint4*>(smem + (uint64_t(k) * e_count + i) * 2);
+      uint16_t h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        h[j] = f2h(__fadd_rn(acc[j], h2f(h_at(x, j))));
+        acc[j] = h2f(h[j]);
+      }
+      const uint64_t d = sg[k].dst;
+      if (d) *reinterpret_cast<uint4*>(pptr(A, d, t.seq0) + (uint64_t(e_begin) + i) * 2) = pack_h(h);
+    }
+  }
+}
+
 // Whether a task can take the staged path.
 template <int KIND>
 __device__ __forceinline__ bool can_stage(const DevOp& op, const Task& t) {
@@ -1705,6 +1753,7 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_DYN_LOAD:
     case K_DYN_STORE: op_dyn_copy(A, op, t, t.op); break;
     case K_DYN_STORE_MULTI: op_dyn_store_multi(A, op, t, t.op); break;
+    case K_VADD_CHAIN: op_vadd_chain(A, op, t, smem, tc, t.op); break;
     case K_SREG_LOAD: op_sreg_load(A, op, t); break;
     case K_SREG_FINAL: op_sreg_final(A, op, t); break;
     case K_MATMUL:

@@ -61,6 +61,8 @@ enum DevKind : uint16_t {
   K_MASKED_SOFTMAX_ATTNV,  // legacy fused masked softmax(QK^T) @ V -> int8
   K_DYN_STORE_MULTI,       // the runtime-addressed stores of one level: segment k copies n bytes
                            // from src to DRAM at params[dst >> 32] + (dst & 0xFFFFFFFF)
+  K_VADD_CHAIN,            // FP16 running sum of the segments' operands in order: s0 = seg 0, sk =
+                           // f16(sk-1 + seg k); sk stored at seg k's dst unless that is 0
   K_NUM_KINDS
 };
 
@@ -159,6 +161,9 @@ TAC_HD constexpr bool tc_eligible(uint64_t a, uint64_t b, uint32_t M, uint32_t N
 // more SMs; QUANT (FP16 in, staged in shared memory, 32 KB per task) takes
 // twice kEwTaskElems to halve its per-task overhead; the rest take
 // kEwTaskElems.
+constexpr uint32_t kVaddChainMax = 8;     // operands of one K_VADD_CHAIN op at most
+constexpr uint32_t kVaddChainTask = 4096;  // elements of one K_VADD_CHAIN task (all operands staged: 64 KB)
+
 TAC_HD constexpr uint32_t ew_task_elems(uint32_t kind) {
   return (kind == K_GELU_F16 || kind == K_GELU_I8) ? 4096u
          : kind == K_QUANT                         ? 2u * uint32_t(kEwTaskElems)

@@ -26,7 +26,7 @@ KIND_NAMES = {1: "GATHER", 2: "DYN_LOAD", 3: "DYN_STORE", 4: "SREG_LOAD", 5: "SR
               12: "VADD_I32", 13: "DEQUANT_ADD", 14: "DEQUANT", 15: "DEQ_SCALED", 16: "QUANT", 17: "VADD_F16",
               18: "LN", 19: "GELU", 20: "SOFTMAX", 21: "MSOFTMAX", 22: "MAX_ABS", 23: "TRANSPOSE",
               24: "LN_I8", 25: "SOFTMAX_I8", 26: "MSOFTMAX_I8", 27: "GELU_I8", 28: "SOFTMAX_ATTNV",
-              29: "MSOFTMAX_ATTNV", 30: "DYN_STORE_MULTI"}
+              29: "MSOFTMAX_ATTNV", 30: "DYN_STORE_MULTI", 31: "VADD_CHAIN"}
 SHARED = 1 << 63
 
 
@@ -43,6 +43,8 @@ def op_label(op) -> str:
               ("+" + "+".join(tags) if tags else ""))
     elif k not in ("GATHER", "DYN_STORE", "DYN_LOAD", "DYN_STORE_MULTI", "TRANSPOSE", "SREG_LOAD", "SREG_FINAL"):
         k += f"[{op['M']}x{op['N']}]" + ("seg" if f & 32 else "") + ("+quant" if int(op["flags2"]) & 2 else "")
+        if k.startswith("VADD_CHAIN"):
+            k += f"x{int(op['nseg'])}"
     return k
 
 

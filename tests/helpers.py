@@ -52,6 +52,61 @@ class ProgramStub:
         self.trace_manifest = {}
 
 
+def vadd_chain_program(M: int, N: int, parts: int = 8, commute: bool = False, produced: bool = False,
+                       seed: int = 11):
+    """(instruction words, DRAM image, parts): `parts` FP16 [M, N] vectors
+    summed into WBUF[0] by VADD_FP32s, the accumulator as src1 (commute=False)
+    or src2; the sum after the fourth vector is STOREd to DRAM.  The vectors
+    are LOADed from DRAM into ABUF, or (produced=True) each is computed just
+    before it is added: an INT32 tile LOADed into ACCUM and dequantised by
+    DEQUANT_ACCUM_FP32 into the same ABUF scratch every time, as the K-split
+    projections of the compiler's decode streams do."""
+    from llm_accelerator_b200 import isa
+    from types import SimpleNamespace
+    units = M * N * 2 // 16
+    X = 8192 // 16                       # DRAM unit of the inputs
+    rng = np.random.default_rng(seed)
+    prog = [dict(opcode=0x05, addr_reg=0, imm28=0), dict(opcode=0x06, addr_reg=0, imm28=0),
+            dict(opcode=0x03, M=M // 16 - 1, N=N // 16 - 1, K=0)]
+
+    def add(k, part_buf, part_off):      # WBUF[0] <- WBUF[0] + part (or part + WBUF[0])
+        srcs = (dict(src1_buf=part_buf, src1_off=part_off, src2_buf=1, src2_off=0) if commute else
+                dict(src1_buf=1, src1_off=0, src2_buf=part_buf, src2_off=part_off))
+        prog.append(dict(opcode=0x19, dst_buf=1, dst_off=0, **srcs))
+        if k == 3:
+            prog.append(dict(opcode=0x08, buf_id=1, sram_off=0, xfer_len=units, addr_reg=0, dram_off=Y))
+
+    if produced:
+        iunits = M * N * 4 // 16
+        S = X + parts * iunits           # DRAM unit of the FP16 scale row
+        Y = S + N * 2 // 16 + 64         # DRAM unit of the stored partial sum
+        data = [(S, (rng.random(N) * 2e-3 + 1e-4).astype(np.float16)),
+                (X, rng.integers(-(1 << 20), 1 << 20, parts * M * N).astype(np.int32))]
+        prog.append(dict(opcode=0x07, buf_id=1, sram_off=units, xfer_len=N * 2 // 16, addr_reg=0, dram_off=S))
+        for k in range(parts):
+            prog.append(dict(opcode=0x07, buf_id=2, sram_off=0, xfer_len=iunits, addr_reg=0, dram_off=X + k * iunits))
+            dst = dict(dst_buf=1, dst_off=0) if k == 0 else dict(dst_buf=0, dst_off=0)
+            prog.append(dict(opcode=0x17, src1_buf=2, src1_off=0, src2_buf=1, src2_off=units, **dst))
+            if k:
+                add(k, 0, 0)
+    else:
+        Y = X + parts * units + 64
+        data = [(X, (rng.standard_normal(parts * M * N) * 4).astype(np.float16))]
+        for k in range(parts):   # ABUF[k * units] <- p_k
+            prog.append(dict(opcode=0x07, buf_id=0, sram_off=k * units, xfer_len=units, addr_reg=0,
+                             dram_off=X + k * units))
+        prog.append(dict(opcode=0x19, src1_buf=0, src1_off=0, src2_buf=0, src2_off=units, dst_buf=1, dst_off=0))
+        for k in range(2, parts):
+            add(k, 0, k * units)
+    prog.append(dict(opcode=0x01))
+    words = [isa.word_of(isa.encode(SimpleNamespace(**d))) for d in prog]
+    img = np.zeros((Y + units) * 16 + 4096, np.uint8)
+    img[:len(words) * 8] = np.frombuffer(b"".join(int(w).to_bytes(8, "big") for w in words), np.uint8)
+    for at, v in data:
+        img[at * 16:at * 16 + v.nbytes] = v.view(np.uint8)
+    return words, img, parts
+
+
 def run_oracle_case(case):
     """Runs an op case on the oracle; returns (err name, post dict, cycles, pc)."""
     abuf, wbuf, accum, sregs, dram = oc.pre_state(case)

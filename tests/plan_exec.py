@@ -18,7 +18,7 @@ CONST = 1 << 31
 K = dict(GATHER=1, DYN_LOAD=2, DYN_STORE=3, SREG_LOAD=4, SREG_FINAL=5, MATMUL=6, REQUANT=7, REQUANT_PC=8,
          SCALE_MUL_I32=9, SCALE_MUL_I8=10, VADD_I8=11, VADD_I32=12, DEQUANT_ADD=13, DEQUANT_ACCUM=14,
          DEQUANT_SCALED=15, QUANT=16, VADD_F16=17, LAYERNORM_F16=18, GELU_F16=19, SOFTMAX_F16=20,
-         MASKED_SOFTMAX_F16=21, MAX_ABS=22, TRANSPOSE=23, DYN_STORE_MULTI=30)
+         MASKED_SOFTMAX_F16=21, MAX_ABS=22, TRANSPOSE=23, DYN_STORE_MULTI=30, VADD_CHAIN=31)
 
 
 class PlanMachine:
@@ -128,6 +128,14 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
                 dstw, n = int(sg["dst"]), int(sg["n"])
                 addr = int(params[dstw >> 32]) + (dstw & 0xFFFFFFFF)
                 m.dram_mem(addr, n)[:] = m.mem(int(sg["src"]), n)
+        elif k == K["VADD_CHAIN"]:
+            # running FP16 sum of the segment operands, each add rounded (simulator.py:869-891)
+            chain = segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]
+            acc = m.mem(int(chain[0]["src"]), M * N * 2).view(np.float16).copy()
+            for sg in chain[1:]:
+                acc = (acc.astype(np.float32) + _f16(m, int(sg["src"]), M * N)).astype(np.float16)
+                if int(sg["dst"]):
+                    m.mem(int(sg["dst"]), M * N * 2)[:] = acc.view(np.uint8)
         elif k in (K["DYN_LOAD"], K["DYN_STORE"]):
             addr = int(params[int(op["param"])]) + int(op["dconst"])
             n = int(op["nbytes"])

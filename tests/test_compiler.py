@@ -14,7 +14,7 @@ import pytest
 
 import op_cases as oc
 import plan_exec as PE
-from helpers import GOLDEN, load_bundle, load_op_golden, load_run
+from helpers import GOLDEN, load_bundle, load_op_golden, load_run, vadd_chain_program
 from llm_accelerator_b200 import _lib as L
 from llm_accelerator_b200.engine import Site, compile_program
 from oracle import golden as G
@@ -123,16 +123,11 @@ def _narrow_kv(b, nm, sites, plan):
     return out
 
 
-@pytest.mark.parametrize("narrow", [False, True], ids=["symbol-ranges", "kv-window-ranges"])
-@pytest.mark.parametrize("reverse", [False, True], ids=["level-order", "level-reversed"])
-@pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
-def test_plan_reproduces_oracle_bundle_run(name, reverse, narrow):
-    """Prefill + decode steps: one plan per stream compiled with runtime sites,
-    executed with each step's parameters, equals the oracle bit-for-bit, also
-    with every level's ops run in reverse order (no hidden intra-level
-    dependency, e.g. between the KV-cache appends of one step)."""
-    b = load_bundle(name)
-    gold = load_run(name)
+def _check_plans_against_oracle(b, tokens, reverse: bool, narrow: bool):
+    """Compiles b's prefill and decode streams once (runtime sites as plan
+    parameters), runs prefill + decode steps of `tokens` through the plans
+    with each step's parameters, and compares the whole machine state with the
+    oracle's after every step."""
     orc = G.OracleSimulator()
     orc.load_bundle(b)
     dram_bytes, shared = len(orc.state.dram), b.temp_base // 16 * 16
@@ -153,10 +148,8 @@ def test_plan_reproduces_oracle_bundle_run(name, reverse, narrow):
     arena = max(int(p.info.arena_bytes) for p, _ in plans.values())
     slots = max(int(p.info.n_slots) for p, _ in plans.values())
     m = PE.PlanMachine(bytes(orc.state.dram), shared, arena, slots)
-    prompt = gold["prompt"]
-    for pos in range(0, 6):
+    for pos, tok in enumerate(tokens):
         nm = "prefill" if pos == 0 else "decode"
-        tok = int(prompt[pos]) if pos < len(prompt) else int(gold["tokens"][pos])
         row = b.embedding_row_bytes
         for s in b.runtime_patch_sites:
             if s.stream == nm:
@@ -177,6 +170,32 @@ def test_plan_reproduces_oracle_bundle_run(name, reverse, narrow):
         assert f["abuf"] == bytes(st.abuf) and f["wbuf"] == bytes(st.wbuf)
         assert f["accum"] == st.accum.tobytes() and f["sregs"] == st.scale_regs.tobytes()
         assert f["dram"] == bytes(st.dram[:len(f["dram"])])
+
+
+@pytest.mark.parametrize("narrow", [False, True], ids=["symbol-ranges", "kv-window-ranges"])
+@pytest.mark.parametrize("reverse", [False, True], ids=["level-order", "level-reversed"])
+@pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
+def test_plan_reproduces_oracle_bundle_run(name, reverse, narrow):
+    """Prefill + decode steps: one plan per stream compiled with runtime sites,
+    executed with each step's parameters, equals the oracle bit-for-bit, also
+    with every level's ops run in reverse order (no hidden intra-level
+    dependency, e.g. between the KV-cache appends of one step)."""
+    b = load_bundle(name)
+    gold = load_run(name)
+    prompt = gold["prompt"]
+    tokens = [int(prompt[pos]) if pos < len(prompt) else int(gold["tokens"][pos]) for pos in range(6)]
+    _check_plans_against_oracle(b, tokens, reverse, narrow)
+
+
+def test_plan_reproduces_oracle_gpt2_small():
+    """GPT-2 small (12 layers, d_model 768): the decode plan carries every
+    fusion of the full-size streams (tcgen05 projections with their dequant
+    epilogues, the K-split partial sums as VADD chains, MAX_ABS + QUANT,
+    attention with the softmax in the QK^T task); prefill and two decode
+    steps equal the oracle bit-for-bit."""
+    from llm_accelerator_b200.recipe import load_recipe
+    b = load_recipe(GOLDEN / "recipe_gpt2_small.npz")
+    _check_plans_against_oracle(b, [464, 2068, 7586], reverse=True, narrow=True)
 
 
 def test_runtime_site_out_of_range_requests_recompile():
@@ -345,3 +364,38 @@ def test_tasks_cover_every_sequence_and_element_once(batch):
     assert seen, "no element-wise ops in the plan"
     for opi, cov in seen.items():
         assert (cov == 1).all(), f"op {opi}: coverage {np.unique(cov)}"
+
+
+
+@pytest.mark.parametrize("reverse", [False, True], ids=["level-order", "level-reversed"])
+@pytest.mark.parametrize("commute", [False, True], ids=["sum-first", "sum-second"])
+@pytest.mark.parametrize("produced", [False, True], ids=["loaded", "produced"])
+@pytest.mark.parametrize("shape,parts", [((16, 32), 8), ((16, 256), 8), ((16, 256), 11)],
+                         ids=["16x32", "16x256", "16x256-11-parts"])
+def test_running_fp16_sum_becomes_one_chain_op(shape, parts, produced, commute, reverse):
+    """FP16 vectors summed by VADD_FP32s into one accumulator (the partial
+    sums of a K-split projection) compile to K_VADD_CHAIN ops of at most 8
+    operands, one level each; the plan, including an intermediate sum a
+    STORE reads and an in-place accumulator, equals the oracle bit-for-bit.
+    With produced vectors the ops that compute them follow the chain op in
+    the plan, and dead-op elimination must keep them."""
+    from types import SimpleNamespace
+    words, img, _ = vadd_chain_program(*shape, parts=parts, commute=commute, produced=produced)
+    region = b"".join(int(w).to_bytes(8, "big") for w in words)
+    p = compile_program(1, len(img), 0, region, 0, 1000, L.Regs(), True, ())
+    assert not p.info.faulted
+    ops, segs, tasks, lv = p.dump()
+    chains = ops[ops["kind"] == PE.K["VADD_CHAIN"]]
+    # at most 8 operands a chain: the sum so far starts the next one
+    assert [int(c["nseg"]) for c in chains] == ([8, parts - 8 + 1] if parts > 8 else [parts])
+    assert not (ops["kind"] == PE.K["VADD_F16"]).any()
+    m = PE.PlanMachine(img.tobytes(), 0, int(p.info.arena_bytes), int(p.info.n_slots))
+    PE.run_plan(m, ops, segs, lv, reverse=reverse)
+    f = PE.final_state(m)
+    orc = G.OracleSimulator()
+    orc.load_program(SimpleNamespace(instructions=region, data_base=0, data=img.tobytes(), entry_point=0,
+                                     insn_count=len(words)))
+    assert orc.run(1000) == int(p.info.executed)
+    st = orc.state
+    assert f["abuf"] == bytes(st.abuf) and f["wbuf"] == bytes(st.wbuf)
+    assert f["dram"] == bytes(st.dram[:len(f["dram"])])

@@ -16,7 +16,7 @@ import pytest
 
 import op_cases as oc
 from helpers import (ProgramStub, expected_post, fp16_ulp_diff, load_bundle, load_op_golden, load_run,
-                     run_bundle_sequence)
+                     run_bundle_sequence, vadd_chain_program)
 from oracle import isa as OI
 
 pytestmark = pytest.mark.gpu
@@ -96,6 +96,33 @@ def test_engine_op_case(i):
             assert d.max() <= 1, f"{nm}: max int8 step {d.max()}"
         else:
             np.testing.assert_array_equal(got, want, err_msg=nm)
+
+
+@pytest.mark.parametrize("commute", [False, True], ids=["sum-first", "sum-second"])
+@pytest.mark.parametrize("produced", [False, True], ids=["loaded", "produced"])
+@pytest.mark.parametrize("shape,parts", [((16, 32), 8), ((16, 256), 8), ((16, 512), 8), ((16, 256), 11)],
+                         ids=["16x32", "16x256", "16x512", "16x256-11-parts"])
+def test_engine_running_fp16_sum(shape, parts, produced, commute):
+    """A running FP16 sum over VADD_FP32s (K_VADD_CHAIN ops on the device,
+    operands staged by bulk copies, tasks of 4096 elements) is bit-exact
+    against the oracle, including the intermediate sum a STORE writes to
+    DRAM."""
+    from types import SimpleNamespace
+    from oracle import golden as G
+    words, img, _ = vadd_chain_program(*shape, parts=parts, commute=commute, produced=produced)
+    sim = _sim()
+    sim.load_program(ProgramStub(words))
+    sim.state.dram[:len(img)] = img.tobytes()
+    sim.run()
+    orc = G.OracleSimulator()
+    stub = ProgramStub(words)
+    orc.load_program(SimpleNamespace(instructions=stub.instructions, data_base=0, data=img.tobytes(), entry_point=0,
+                                     insn_count=stub.insn_count))
+    orc.run()
+    for nm in ("abuf", "wbuf"):
+        assert bytes(getattr(sim.state, nm)) == bytes(getattr(orc.state, nm)), nm
+    assert bytes(sim.state.dram[:len(img)]) == bytes(orc.state.dram[:len(img)])
+    assert sim.state.cycle_count == orc.state.cycle_count
 
 
 @pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
