@@ -100,6 +100,7 @@ class Compiler {
   void drop_dead_ops();
   void merge_dyn_stores();
   void write_vadd_chains();
+  int link_pv_pairs();
   uint64_t dead_ops_ = 0;
 
  private:
@@ -281,6 +282,7 @@ class Compiler {
       }
     pending_same_.clear();
     int32_t L = level_for(a);
+    if (force_level_ >= 0) L = force_level_;   // a P.V MATMUL placed in its QK^T task's level
     commit(a, L);
     for (int prm : pending_same_) {   // equalities the level relied on
       const int g = site_group_[prm];
@@ -671,9 +673,28 @@ class Compiler {
     mm.attn_mode = sm.attn_mode;
     mm.param = sm.param;
     mm.nbytes = out;
+    sm_out_[out] = idx;
     for (auto& w : acc.writes)
       if (cls(w.first) == PC_ARENA) op_arena_writes_[idx].push_back(w);
     return true;
+  }
+
+  // A wide MATMUL whose A is the softmax output of a wide QK^T + softmax op
+  // (quantised on load, F_QA) and whose other operands are ready by that op's
+  // level: it runs in the QK^T op's task (FX_PV / FX_PVY), the softmax rows
+  // going straight into its A tile.  Returns the QK^T op's index, or -1.
+  int32_t pv_partner(const DevOp& op, const Access& acc) {
+    if (!(op.flags & F_QA) || !(op.flags & F_WIDE) || (op.flags & F_ACCUMULATE)) return -1;
+    auto it = sm_out_.find(op.a);
+    if (it == sm_out_.end() || pv_of_.count(it->second)) return -1;
+    const DevOp& x = P->ops[it->second];
+    if (!(x.flags & F_WIDE) || x.M != op.M || x.N != op.K || op.M % 16 || op.K % 16) return -1;
+    Access rest = acc;   // every read but the softmax rows
+    rest.reads.erase(std::remove_if(rest.reads.begin(), rest.reads.end(),
+                                    [&](const std::pair<uint64_t, uint64_t>& r) { return r.first == op.a; }),
+                     rest.reads.end());
+    if (level_for(rest) > int32_t(x.level)) return -1;
+    return static_cast<int32_t>(it->second);
   }
 
   // Physical start of a contiguous copy of logical SRAM units [u0, u0+n).
@@ -913,6 +934,10 @@ class Compiler {
   std::unordered_map<uint32_t, MaxAbsOf> maxabs_by_slot_;
   // output extent of the latest VADD of each open chain -> op index; operand lists of the chains
   std::unordered_map<uint64_t, uint32_t> vadd_tail_;
+  // softmax output extent of a wide QK^T + softmax op -> op index; QK^T op -> its P.V op
+  std::unordered_map<uint64_t, uint32_t> sm_out_;
+  std::unordered_map<uint32_t, uint32_t> pv_of_;
+  int32_t force_level_ = -1;
   std::vector<std::vector<Segment>> chains_;
   std::vector<uint64_t> maxabs_pending_;
   uint64_t home_writes_ = 0;
@@ -1505,7 +1530,21 @@ int Compiler::h_rtype(const Insn& x) {
   if (op.kind == K_MATMUL && !(op.b & kSharedBit) &&
       wide_mm_ok(uint32_t(M), uint32_t(N), uint32_t(K), op.flags & F_BT, op.flags & F_QB, op.flags & F_QA))
     op.flags |= F_WIDE;
+  const int32_t pv_x = op.kind == K_MATMUL ? pv_partner(op, acc) : -1;
+  const size_t n_before = P->ops.size();
+  if (pv_x >= 0) force_level_ = static_cast<int32_t>(P->ops[pv_x].level);
   emit_compute(op, acc, d, x.sreg);
+  force_level_ = -1;
+  if (pv_x >= 0 && P->ops.size() == n_before + 1) {
+    const uint32_t y = static_cast<uint32_t>(n_before);
+    pv_of_[static_cast<uint32_t>(pv_x)] = y;
+    P->ops[pv_x].flags2 |= FX_PV;
+    P->ops[y].flags2 |= FX_PVY;
+    auto& rd = op_arena_reads_[y];   // read inside the QK^T task: keeps nothing else live
+    rd.erase(std::remove_if(rd.begin(), rd.end(),
+                            [&](const std::pair<uint64_t, uint64_t>& r) { return r.first == op.a; }),
+             rd.end());
+  }
   if (op.kind == K_VADD_F16 && !(op.flags & F_SEGA) && !P->ops.empty() && P->ops.back().kind == K_VADD_F16 &&
       P->ops.back().d == op.d && cls(op.d) == PC_ARENA)
     vadd_tail_[op.d] = static_cast<uint32_t>(P->ops.size() - 1);
@@ -1692,9 +1731,16 @@ void Compiler::drop_dead_ops() {
   for (size_t i = n; i-- > 0;) {
     bool live = !op_pure_[i];
     for (auto& w : op_arena_writes_[i]) live = live || any_read(w.first, w.second);
+    auto pv = pv_of_.find(static_cast<uint32_t>(i));
+    const bool pv_kept = pv != pv_of_.end() && keep[pv->second];
+    live = live || pv_kept;   // the task that runs a kept P.V op
     if (!live) continue;
     keep[i] = 1;
     DevOp& op = P->ops[i];
+    if (op.flags2 & FX_PV) {
+      if (!pv_kept) op.flags2 &= ~FX_PV;
+      else if (!any_read(op.nbytes, uint64_t(op.M) * op.N * 2 / kUnit)) op.flags2 |= FX_SMSKIP;
+    }
     if (((op.flags & F_DQ) || (op.flags2 & FX_DQS)) && cls(op.d) == PC_ARENA &&
         !any_read(op.d, uint64_t(op.M) * op.N * 4 / kUnit))
       op.flags |= F_NOI32;   // only the FP16 result is read
@@ -1712,6 +1758,24 @@ void Compiler::drop_dead_ops() {
     if (keep[i]) P->ops[j++] = P->ops[i];
   dead_ops_ = n - j;
   P->ops.resize(j);
+}
+
+// Each FX_PV op names its P.V op (seg0) by index in the final op list: the
+// P.V op is the FX_PVY op whose A is this op's softmax output.
+int Compiler::link_pv_pairs() {
+  std::unordered_map<uint64_t, uint32_t> ys;
+  for (uint32_t i = 0; i < P->ops.size(); ++i)
+    if (P->ops[i].flags2 & FX_PVY) ys[P->ops[i].a] = i;
+  for (DevOp& op : P->ops) {
+    if (!(op.flags2 & FX_PV)) continue;
+    auto it = ys.find(op.nbytes);
+    if (it == ys.end()) return unsupported("internal: a QK^T task lost its P.V op");
+    op.seg0 = it->second;
+    op.nseg = 0;
+    ys.erase(it);
+  }
+  if (!ys.empty()) return unsupported("internal: a P.V op lost its QK^T task");
+  return 0;
 }
 
 // Each K_VADD_CHAIN's operand list goes to the segment table, contiguously.
@@ -1809,6 +1873,7 @@ void Compiler::build_tasks() {
         break;
       }
       case K_MATMUL: {
+        if (op.flags2 & FX_PVY) break;   // runs in its QK^T op's task
         const uint32_t ntile = (op.N + 63) / 64;
         const bool shared_b = (op.b & kSharedBit) != 0;
         if ((op.flags & F_WIDE) || (!(op.flags & F_TC) && !shared_b && wide_mm_ok(op.M, op.N, op.K, false, false))) {
@@ -2055,6 +2120,7 @@ int Compiler::compile() {
   drop_dead_ops();
   merge_dyn_stores();
   write_vadd_chains();
+  if (int s = link_pv_pairs()) return s;
   build_tasks();
 
   tac_exec_info& I = P->info;

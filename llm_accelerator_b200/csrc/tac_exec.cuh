@@ -460,9 +460,13 @@ __device__ __forceinline__ uint2 pack_b(const int8_t (&q)[8]) {
 // NumPy's pairwise row sum, f16(e / sum); a masked row whose sum is zero, or
 // with no visible column (masked and last < 0), writes zeros.
 __device__ __forceinline__ void softmax_row_f16(float* rowbuf, uint32_t n, bool masked, int64_t last,
-                                                uint16_t* out, uint32_t* pw, int lane) {
+                                                uint16_t* out, uint32_t* pw, int lane, int8_t* qout = nullptr,
+                                                float qs = 0.f) {
   if (masked && last < 0) {
-    for (uint32_t g = lane; g < n / 8; g += 32) reinterpret_cast<uint4*>(out)[g] = make_uint4(0, 0, 0, 0);
+    for (uint32_t g = lane; g < n / 8; g += 32) {
+      if (out) reinterpret_cast<uint4*>(out)[g] = make_uint4(0, 0, 0, 0);
+      if (qout) reinterpret_cast<uint2*>(qout)[g] = make_uint2(0, 0);
+    }
     return;
   }
   const uint32_t lst = masked ? static_cast<uint32_t>(last) : n - 1;
@@ -480,7 +484,16 @@ __device__ __forceinline__ void softmax_row_f16(float* rowbuf, uint32_t n, bool 
       const float e = rowbuf[g * 8 + j];
       h[j] = f2h(!masked ? __fdiv_rn(e, denom) : (denom > 0.f ? __fdiv_rn(e, denom) : 0.f));
     }
-    reinterpret_cast<uint4*>(out)[g] = pack_h(h);
+    if (out) reinterpret_cast<uint4*>(out)[g] = pack_h(h);
+    if (qout) {   // QUANT's rule on the FP16 value: rint(x * s), NaN -> 0, clipped to int8
+      int8_t q8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float r = rintf(__fmul_rn(h2f(h[j]), qs));
+        q8[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+      }
+      reinterpret_cast<uint2*>(qout)[g] = pack_b(q8);
+    }
   }
 }
 
@@ -492,14 +505,18 @@ __device__ __forceinline__ void softmax_row_f16(float* rowbuf, uint32_t n, bool 
 // of a fragment load sit on distinct banks).  B^T is copied row by row when
 // the op holds it (F_BT), else B [K][N] is loaded and transposed in 4 x 4 byte
 // blocks.  With F_QB, B arrives as FP16 and is quantised on the way in, with
-// QUANT's rule.  Padding bytes are zero.
+// QUANT's rule.  Padding bytes are zero.  a_staged: the int8 A tile is
+// already in shared memory (the P.V op of an FX_PV pair, whose QK^T softmax
+// wrote it there).
 // ---------------------------------------------------------------------------------
-__device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+__device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
+                                            bool a_staged) {
   const uint32_t M = op.M, N = op.N, K = op.K, seq = t.seq0;
   const uint32_t kc32 = (K + 31) & ~31u;
   const uint32_t bts = kc32 + 16;
   const uint32_t nblocks = (M + 15) / 16, n8 = (N + 7) / 8;
-  const bool bt = (op.flags & F_BT) != 0, qb = (op.flags & F_QB) != 0, qa = (op.flags & F_QA) != 0;
+  const bool bt = (op.flags & F_BT) != 0, qb = (op.flags & F_QB) != 0;
+  const bool qa = !a_staged && (op.flags & F_QA) != 0;
   uint8_t* As = smem;                               // [nblocks * 16][bts]
   uint8_t* Bt = As + nblocks * 16 * bts;            // [n8 * 8][bts]
   uint8_t* Braw = Bt + n8 * 8 * bts;                // [kc32][N] (not F_BT)
@@ -512,7 +529,7 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   const uint32_t kv = kc32 / 16;                    // 16-byte vectors per padded row
   if (qa) {
     for (uint32_t i = htid(); i < M * K / 8; i += kThreads) cp_async16(Ah + i * 16, Ag + uint64_t(i) * 16, 16u);
-  } else {
+  } else if (!a_staged) {
     for (uint32_t i = htid(); i < nblocks * 16 * kv; i += kThreads) {
       const uint32_t r = i / kv, v = i % kv;
       const bool in = r < M && v * 16 < K;
@@ -642,10 +659,13 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   }
   if (sm) hsync();   // every warp is done with the operand tiles: the rows reuse the space
   // F_SM: the dequantised rows [M][N] FP16 in shared memory, then per-warp
-  // float row buffers and pairwise-sum scratch behind them
-  uint16_t* Sc = reinterpret_cast<uint16_t*>(smem);
-  float* rows = reinterpret_cast<float*>(smem + 32 * 256 * 2);
-  uint32_t* pws = reinterpret_cast<uint32_t*>(smem + 32 * 256 * 2 + kWarps * 256 * 4);
+  // float row buffers and pairwise-sum scratch behind them (FX_PV: all of it
+  // behind the P.V op's A tile, which the softmax rows are quantised into)
+  const bool pv = (op.flags2 & FX_PV) != 0;
+  uint8_t* sbase = smem + (pv ? kPvSoftmaxOff : 0u);
+  uint16_t* Sc = reinterpret_cast<uint16_t*>(sbase);
+  float* rows = reinterpret_cast<float*>(sbase + 32 * 256 * 2);
+  uint32_t* pws = reinterpret_cast<uint32_t*>(sbase + 32 * 256 * 2 + kWarps * 256 * 4);
   int32_t* D = reinterpret_cast<int32_t*>(pptr(A, op.d, seq));
   const int32_t* C = (op.flags & F_ACCUMULATE) ? reinterpret_cast<const int32_t*>(pptr(A, op.c, seq)) : nullptr;
   const bool store_i32 = !(op.flags & F_NOI32);
@@ -683,7 +703,14 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   }
   if (sm) {
     hsync();
-    uint16_t* out = reinterpret_cast<uint16_t*>(pptr(A, op.nbytes, seq));
+    uint16_t* out = (op.flags2 & FX_SMSKIP) ? nullptr : reinterpret_cast<uint16_t*>(pptr(A, op.nbytes, seq));
+    int8_t* qout = nullptr;
+    float qs = 0.f;
+    const uint32_t qstride = ((N + 31) & ~31u) + 16;   // the P.V op's A rows: K = N bytes, padded
+    if (pv) {
+      qout = reinterpret_cast<int8_t*>(smem);
+      qs = h2f(sreg_bits(A, A.ops[op.seg0].s[0], seq));
+    }
     const bool masked = (op.flags & F_SMMASK) != 0;
     float* rb = rows + warp * N;
     uint32_t* pw = pws + warp * (3 * kPwMaxLeaves);
@@ -691,7 +718,11 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
       for (uint32_t j = lane; j < N; j += 32) rb[j] = h2f(Sc[r * N + j]);
       __syncwarp();
       const int64_t lt = int64_t(r) + qrb < int64_t(vkl) - 1 ? int64_t(r) + qrb : int64_t(vkl) - 1;
-      softmax_row_f16(rb, N, masked, masked ? lt : int64_t(N) - 1, out + uint64_t(r) * N, pw, lane);
+      softmax_row_f16(rb, N, masked, masked ? lt : int64_t(N) - 1, out ? out + uint64_t(r) * N : nullptr, pw, lane,
+                      qout ? qout + uint64_t(r) * qstride : nullptr, qs);
+      if (qout)   // the A row's padding columns N .. (N rounded up to 32) are zero
+        for (uint32_t g = N / 16 + lane; g < (qstride - 16) / 16; g += 32)
+          reinterpret_cast<uint4*>(qout + uint64_t(r) * qstride)[g] = make_uint4(0, 0, 0, 0);
       __syncwarp();
     }
   }
@@ -1758,7 +1789,13 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_SREG_FINAL: op_sreg_final(A, op, t); break;
     case K_MATMUL:
       if (op.flags & F_TC) op_matmul_tc(A, op, t, smem, tc, t.op);
-      else if (op.flags & F_WIDE) op_matmul_wide(A, op, t, smem);
+      else if (op.flags & F_WIDE) {
+        op_matmul_wide(A, op, t, smem, false);
+        if (op.flags2 & FX_PV) {   // the P.V op, its A tile written by the softmax above
+          hsync();
+          op_matmul_wide(A, A.ops[op.seg0], t, smem, true);
+        }
+      }
       else op_matmul(A, op, t, smem);
       break;
     case K_TRANSPOSE: op_transpose(A, op, t, smem); break;

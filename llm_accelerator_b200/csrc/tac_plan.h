@@ -95,6 +95,13 @@ constexpr uint32_t FX_DQS = 1;         // tcgen05 MATMUL (no accumulate) also wr
                                        // address in dconst; scale row at c, bias row at nbytes
 constexpr uint32_t FX_MAXQ = 2;        // MAX_ABS also writes QUANT's int8 result of its input with the
                                        // inverse scale it derives, to the unit address in d
+constexpr uint32_t FX_PV = 4;          // wide F_SM MATMUL (QK^T) whose task also runs the wide MATMUL at op
+                                       // index seg0 (P.V), that op's A being these softmax rows quantised
+                                       // straight into its shared-memory A tile
+constexpr uint32_t FX_PVY = 8;         // the P.V op of an FX_PV pair: same level, no tasks of its own
+constexpr uint32_t FX_SMSKIP = 16;     // FX_PV op whose softmax rows only its P.V op reads: not stored
+constexpr uint32_t kPvSoftmaxOff = 9216;   // FX_PV: the softmax scratch starts after the P.V A tile
+                                           // (at most 32 rows of 256 + 16 bytes)
 
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 

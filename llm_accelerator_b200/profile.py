@@ -39,6 +39,8 @@ def op_label(op) -> str:
                 if f & bit]
         if int(op["flags2"]) & 1:
             tags.append("dqs")
+        if int(op["flags2"]) & 4:
+            tags.append("pv")
         k += (f"[{op['M']}x{op['K']}x{op['N']}{'s' if int(op['b']) & SHARED else 'p'}]" +
               ("+" + "+".join(tags) if tags else ""))
     elif k not in ("GATHER", "DYN_STORE", "DYN_LOAD", "DYN_STORE_MULTI", "TRANSPOSE", "SREG_LOAD", "SREG_FINAL"):

@@ -113,151 +113,162 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
         order = np.argsort(ops["level"], kind="stable")
     for i in order:
         op = ops[i]
-        k = int(op["kind"])
-        M, N, Kd = int(op["M"]), int(op["N"]), int(op["K"])
-        a, b, c, d = (int(op[x]) for x in "abcd")
-        s = [int(v) for v in op["s"]]
-        if k == K["GATHER"]:
-            data = []
-            for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]:
-                data.append((int(sg["dst"]), m.mem(int(sg["src"]), int(sg["n"]) * 16).copy()))
-            for dst, v in data:
-                m.mem(dst, len(v))[:] = v
-        elif k == K["DYN_STORE_MULTI"]:
-            for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]:
-                dstw, n = int(sg["dst"]), int(sg["n"])
-                addr = int(params[dstw >> 32]) + (dstw & 0xFFFFFFFF)
-                m.dram_mem(addr, n)[:] = m.mem(int(sg["src"]), n)
-        elif k == K["VADD_CHAIN"]:
-            # running FP16 sum of the segment operands, each add rounded (simulator.py:869-891)
-            chain = segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]
-            acc = m.mem(int(chain[0]["src"]), M * N * 2).view(np.float16).copy()
-            for sg in chain[1:]:
-                acc = (acc.astype(np.float32) + _f16(m, int(sg["src"]), M * N)).astype(np.float16)
-                if int(sg["dst"]):
-                    m.mem(int(sg["dst"]), M * N * 2)[:] = acc.view(np.uint8)
-        elif k in (K["DYN_LOAD"], K["DYN_STORE"]):
-            addr = int(params[int(op["param"])]) + int(op["dconst"])
-            n = int(op["nbytes"])
-            if k == K["DYN_LOAD"]:
-                m.mem(d, n)[:] = m.dram_mem(addr, n)
-            else:
-                m.dram_mem(addr, n)[:] = m.mem(a, n)
-        elif k == K["SREG_LOAD"]:
-            m.sregs[int(op["out_slot"])] = m.mem(a, 2).view(np.uint16)[0]
-        elif k == K["SREG_FINAL"]:
-            vals = [(int(sg["dst"]), m.sreg(int(sg["src"]))) for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]]
-            for r, v in vals:
-                m.sregs[r] = np.array([v], np.float16).view(np.uint16)[0]
-        elif k == K["MATMUL"]:
-            if op["flags"] & 1024:   # F_QA: a is FP16, quantised like QUANT with register s[0]
-                v = np.round(_f16(m, a, M * Kd) * np.float32(m.sreg(s[0])))
-                A = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8).reshape(M, Kd)
-                A = A.astype(np.int32)
-            else:
-                A = m.mem(a, M * Kd).view(np.int8).reshape(M, Kd).astype(np.int32)
-            if op["flags"] & 512:   # F_QB: b is FP16, quantised like QUANT with register s[1]
-                v = np.round(_f16(m, b, Kd * N) * np.float32(m.sreg(s[1])))
-                raw = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8)
-            else:
-                raw = m.mem(b, Kd * N).view(np.int8)
-            if op["flags"] & 128:   # F_BT: b holds B^T [N][K]
-                B = raw.reshape(N, Kd).T.astype(np.int32)
-            else:
-                B = raw.reshape(Kd, N).astype(np.int32)
-            acc = m.mem(c, M * N * 4).view(np.int32).reshape(M, N).copy() if op["flags"] & 1 else np.zeros((M, N), np.int32)
-            acc += A @ B
-            if not op["flags"] & 4096:   # F_NOI32: the int32 result is not stored
-                m.mem(d, M * N * 4)[:] = acc.view(np.uint8).ravel()
-            if op["flags2"] & 1:   # FX_DQS: DEQUANT_ACCUM_FP32_SCALED's FP16 result as well
-                r = (acc.astype(np.float32) * _f16(m, c, N).reshape(1, N) * np.float32(m.sreg(s[0]))
-                     + _f16(m, int(op["nbytes"]), N).reshape(1, N))
-                m.mem(int(op["dconst"]), M * N * 2)[:] = r.astype(np.float32).astype(np.float16).view(np.uint8).ravel()
-            if op["flags"] & 2048:   # F_DQ: DEQUANT_ACCUM's FP16 result as well
-                out = (acc.astype(np.float32) * _f16(m, c, N).reshape(1, N)).astype(np.float16)
-                if not op["flags"] & 32768:   # F_NODQ
-                    m.mem(int(op["dconst"]), M * N * 2)[:] = out.view(np.uint8).ravel()
-                if op["flags"] & 8192:   # F_SM: the softmax rows of the dequantised result
-                    masked = bool(op["flags"] & 16384)
-                    qrb, vkl = _attn_context(op, params)
-                    sm = _softmax_rows(out.astype(np.float32), masked, qrb, vkl)
-                    m.mem(int(op["nbytes"]), M * N * 2)[:] = sm.astype(np.float16).view(np.uint8).ravel()
-        elif k in (K["REQUANT"], K["REQUANT_PC"]):
-            acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
-            sc = np.float32(m.sreg(s[0])) if k == K["REQUANT"] else _f16(m, b, N).reshape(1, N)
-            m.mem(d, M * N)[:] = G._sat8(acc * sc).view(np.uint8).ravel()
-        elif k == K["SCALE_MUL_I32"]:
-            v = np.round(m.mem(a, M * N * 4).view(np.int32).astype(np.float32) * np.float32(m.sreg(s[0])))
-            with np.errstate(invalid="ignore"):
-                r = np.clip(v, np.iinfo(np.int32).min, np.iinfo(np.int32).max).astype(np.int32)
-            m.mem(d, M * N * 4)[:] = r.view(np.uint8)
-        elif k == K["SCALE_MUL_I8"]:
-            v = m.mem(a, M * N).view(np.int8).astype(np.float32) * np.float32(m.sreg(s[0]))
-            m.mem(d, M * N)[:] = G._sat8(v).view(np.uint8)
-        elif k == K["VADD_I8"]:
-            v = m.mem(a, M * N).view(np.int8).astype(np.int16) + m.mem(b, M * N).view(np.int8).astype(np.int16)
-            m.mem(d, M * N)[:] = np.clip(v, -128, 127).astype(np.int8).view(np.uint8)
-        elif k == K["VADD_I32"]:
-            v = m.mem(a, M * N * 4).view(np.int32).reshape(M, N) + m.mem(b, N * 4).view(np.int32).reshape(1, N)
-            m.mem(d, M * N * 4)[:] = v.astype(np.int32).view(np.uint8).ravel()
-        elif k == K["DEQUANT_ADD"]:
-            acc = m.mem(a, M * N * 4).view(np.int32).astype(np.float32)
-            skip = m.mem(b, M * N).view(np.int8).astype(np.float32)
-            v = acc * np.float32(m.sreg(s[0])) + skip * np.float32(m.sreg(s[1]))
-            m.mem(d, M * N)[:] = G._sat8(v).view(np.uint8)
-        elif k == K["SOFTMAX_F16"]:
-            r = _softmax_rows(_f16(m, a, M * N).reshape(M, N), False, 0, 0)
-            m.mem(d, M * N * 2)[:] = r.astype(np.float16).view(np.uint8).ravel()
-        elif k == K["QUANT"]:
-            xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
-                else _f16(m, a, M * N)
-            x = xa * np.float32(m.sreg(s[0]))
-            v = np.round(x)
-            m.mem(d, M * N)[:] = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8).view(np.uint8)
-        elif k == K["MAX_ABS"]:
-            xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
-                else _f16(m, a, M * N)
-            inv, fwd = G.max_abs_scales(float(np.max(np.abs(xa))))
-            m.sregs[int(op["out_slot"])] = np.array([inv], np.float16).view(np.uint16)[0]
-            m.sregs[int(op["out_slot"]) + 1] = np.array([fwd], np.float16).view(np.uint16)[0]
-            if op["flags2"] & 2:   # FX_MAXQ: QUANT's result with the inverse scale
-                v = np.round(xa * np.float32(np.float16(inv)))
-                q = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8)
-                m.mem(d, M * N)[:] = q.view(np.uint8)
-        elif k in (K["DEQUANT_SCALED"], K["DEQUANT_ACCUM"]):
-            acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
-            if op["flags"] & 16:   # F_SPLIT: second half of the vector at c
-                vec = np.concatenate([_f16(m, b, N), _f16(m, c, N)])
-            else:
-                vec = _f16(m, b, 2 * N if k == K["DEQUANT_SCALED"] else N)
-            if k == K["DEQUANT_SCALED"]:
-                r = acc * vec[:N].reshape(1, N) * np.float32(m.sreg(s[0])) + vec[N:].reshape(1, N)
-            else:
-                r = acc * vec[:N].reshape(1, N)
-            m.mem(d, M * N * 2)[:] = r.astype(np.float32).astype(np.float16).view(np.uint8).ravel()
-        elif k == K["VADD_F16"]:
-            xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
-                else _f16(m, a, M * N)
-            r = xa + _f16(m, b, M * N)
-            m.mem(d, M * N * 2)[:] = r.astype(np.float16).view(np.uint8)
-        elif k == K["LAYERNORM_F16"]:
-            x = _f16(m, a, M * N).reshape(M, N)
-            gb = np.concatenate([_f16(m, b, N), _f16(m, c, N)]) if op["flags"] & 16 else _f16(m, b, 2 * N)
-            mean = x.mean(axis=-1, keepdims=True).astype(np.float32)
-            var = x.var(axis=-1, keepdims=True).astype(np.float32)
-            y = (x - mean) / np.sqrt(var + np.float32(1e-5))
-            m.mem(d, M * N * 2)[:] = (y * gb[:N] + gb[N:]).astype(np.float32).astype(np.float16).view(np.uint8).ravel()
-        elif k == K["GELU_F16"]:
-            m.mem(d, M * N * 2)[:] = G._gelu_tanh(_f16(m, a, M * N)).astype(np.float32).astype(np.float16).view(np.uint8)
-        elif k == K["MASKED_SOFTMAX_F16"]:
-            qrb, vkl = _attn_context(op, params)
-            out = _softmax_rows(_f16(m, a, M * N).reshape(M, N), True, qrb, vkl)
-            m.mem(d, M * N * 2)[:] = out.astype(np.float16).view(np.uint8).ravel()
-        elif k == K["TRANSPOSE"]:
-            src = m.mem(a, M * N).view(np.int8).reshape(M, N)
-            m.mem(d, M * N)[:] = np.ascontiguousarray(src.T).view(np.uint8).ravel()
+        if op["flags2"] & 8:   # FX_PVY: runs inside its QK^T op's task
+            continue
+        _run_op(m, op, segs, params)
+        if op["flags2"] & 4:   # FX_PV: the P.V op right after the softmax rows
+            _run_op(m, ops[int(op["seg0"])], segs, params)
+            if op["flags2"] & 16:   # FX_SMSKIP: the rows are not stored; nothing else may read them
+                m.mem(int(op["nbytes"]), int(op["M"]) * int(op["N"]) * 2)[:] = 0xFF
+
+
+def _run_op(m: PlanMachine, op, segs, params):
+    """Executes one plan op on the machine."""
+    k = int(op["kind"])
+    M, N, Kd = int(op["M"]), int(op["N"]), int(op["K"])
+    a, b, c, d = (int(op[x]) for x in "abcd")
+    s = [int(v) for v in op["s"]]
+    if k == K["GATHER"]:
+        data = []
+        for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]:
+            data.append((int(sg["dst"]), m.mem(int(sg["src"]), int(sg["n"]) * 16).copy()))
+        for dst, v in data:
+            m.mem(dst, len(v))[:] = v
+    elif k == K["DYN_STORE_MULTI"]:
+        for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]:
+            dstw, n = int(sg["dst"]), int(sg["n"])
+            addr = int(params[dstw >> 32]) + (dstw & 0xFFFFFFFF)
+            m.dram_mem(addr, n)[:] = m.mem(int(sg["src"]), n)
+    elif k == K["VADD_CHAIN"]:
+        # running FP16 sum of the segment operands, each add rounded (simulator.py:869-891)
+        chain = segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]
+        acc = m.mem(int(chain[0]["src"]), M * N * 2).view(np.float16).copy()
+        for sg in chain[1:]:
+            acc = (acc.astype(np.float32) + _f16(m, int(sg["src"]), M * N)).astype(np.float16)
+            if int(sg["dst"]):
+                m.mem(int(sg["dst"]), M * N * 2)[:] = acc.view(np.uint8)
+    elif k in (K["DYN_LOAD"], K["DYN_STORE"]):
+        addr = int(params[int(op["param"])]) + int(op["dconst"])
+        n = int(op["nbytes"])
+        if k == K["DYN_LOAD"]:
+            m.mem(d, n)[:] = m.dram_mem(addr, n)
         else:
-            raise NotImplementedError(f"plan executor: op kind {k}")
+            m.dram_mem(addr, n)[:] = m.mem(a, n)
+    elif k == K["SREG_LOAD"]:
+        m.sregs[int(op["out_slot"])] = m.mem(a, 2).view(np.uint16)[0]
+    elif k == K["SREG_FINAL"]:
+        vals = [(int(sg["dst"]), m.sreg(int(sg["src"]))) for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]]
+        for r, v in vals:
+            m.sregs[r] = np.array([v], np.float16).view(np.uint16)[0]
+    elif k == K["MATMUL"]:
+        if op["flags"] & 1024:   # F_QA: a is FP16, quantised like QUANT with register s[0]
+            v = np.round(_f16(m, a, M * Kd) * np.float32(m.sreg(s[0])))
+            A = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8).reshape(M, Kd)
+            A = A.astype(np.int32)
+        else:
+            A = m.mem(a, M * Kd).view(np.int8).reshape(M, Kd).astype(np.int32)
+        if op["flags"] & 512:   # F_QB: b is FP16, quantised like QUANT with register s[1]
+            v = np.round(_f16(m, b, Kd * N) * np.float32(m.sreg(s[1])))
+            raw = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8)
+        else:
+            raw = m.mem(b, Kd * N).view(np.int8)
+        if op["flags"] & 128:   # F_BT: b holds B^T [N][K]
+            B = raw.reshape(N, Kd).T.astype(np.int32)
+        else:
+            B = raw.reshape(Kd, N).astype(np.int32)
+        acc = m.mem(c, M * N * 4).view(np.int32).reshape(M, N).copy() if op["flags"] & 1 else np.zeros((M, N), np.int32)
+        acc += A @ B
+        if not op["flags"] & 4096:   # F_NOI32: the int32 result is not stored
+            m.mem(d, M * N * 4)[:] = acc.view(np.uint8).ravel()
+        if op["flags2"] & 1:   # FX_DQS: DEQUANT_ACCUM_FP32_SCALED's FP16 result as well
+            r = (acc.astype(np.float32) * _f16(m, c, N).reshape(1, N) * np.float32(m.sreg(s[0]))
+                 + _f16(m, int(op["nbytes"]), N).reshape(1, N))
+            m.mem(int(op["dconst"]), M * N * 2)[:] = r.astype(np.float32).astype(np.float16).view(np.uint8).ravel()
+        if op["flags"] & 2048:   # F_DQ: DEQUANT_ACCUM's FP16 result as well
+            out = (acc.astype(np.float32) * _f16(m, c, N).reshape(1, N)).astype(np.float16)
+            if not op["flags"] & 32768:   # F_NODQ
+                m.mem(int(op["dconst"]), M * N * 2)[:] = out.view(np.uint8).ravel()
+            if op["flags"] & 8192:   # F_SM: the softmax rows of the dequantised result
+                masked = bool(op["flags"] & 16384)
+                qrb, vkl = _attn_context(op, params)
+                sm = _softmax_rows(out.astype(np.float32), masked, qrb, vkl)
+                m.mem(int(op["nbytes"]), M * N * 2)[:] = sm.astype(np.float16).view(np.uint8).ravel()
+    elif k in (K["REQUANT"], K["REQUANT_PC"]):
+        acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
+        sc = np.float32(m.sreg(s[0])) if k == K["REQUANT"] else _f16(m, b, N).reshape(1, N)
+        m.mem(d, M * N)[:] = G._sat8(acc * sc).view(np.uint8).ravel()
+    elif k == K["SCALE_MUL_I32"]:
+        v = np.round(m.mem(a, M * N * 4).view(np.int32).astype(np.float32) * np.float32(m.sreg(s[0])))
+        with np.errstate(invalid="ignore"):
+            r = np.clip(v, np.iinfo(np.int32).min, np.iinfo(np.int32).max).astype(np.int32)
+        m.mem(d, M * N * 4)[:] = r.view(np.uint8)
+    elif k == K["SCALE_MUL_I8"]:
+        v = m.mem(a, M * N).view(np.int8).astype(np.float32) * np.float32(m.sreg(s[0]))
+        m.mem(d, M * N)[:] = G._sat8(v).view(np.uint8)
+    elif k == K["VADD_I8"]:
+        v = m.mem(a, M * N).view(np.int8).astype(np.int16) + m.mem(b, M * N).view(np.int8).astype(np.int16)
+        m.mem(d, M * N)[:] = np.clip(v, -128, 127).astype(np.int8).view(np.uint8)
+    elif k == K["VADD_I32"]:
+        v = m.mem(a, M * N * 4).view(np.int32).reshape(M, N) + m.mem(b, N * 4).view(np.int32).reshape(1, N)
+        m.mem(d, M * N * 4)[:] = v.astype(np.int32).view(np.uint8).ravel()
+    elif k == K["DEQUANT_ADD"]:
+        acc = m.mem(a, M * N * 4).view(np.int32).astype(np.float32)
+        skip = m.mem(b, M * N).view(np.int8).astype(np.float32)
+        v = acc * np.float32(m.sreg(s[0])) + skip * np.float32(m.sreg(s[1]))
+        m.mem(d, M * N)[:] = G._sat8(v).view(np.uint8)
+    elif k == K["SOFTMAX_F16"]:
+        r = _softmax_rows(_f16(m, a, M * N).reshape(M, N), False, 0, 0)
+        m.mem(d, M * N * 2)[:] = r.astype(np.float16).view(np.uint8).ravel()
+    elif k == K["QUANT"]:
+        xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
+            else _f16(m, a, M * N)
+        x = xa * np.float32(m.sreg(s[0]))
+        v = np.round(x)
+        m.mem(d, M * N)[:] = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8).view(np.uint8)
+    elif k == K["MAX_ABS"]:
+        xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
+            else _f16(m, a, M * N)
+        inv, fwd = G.max_abs_scales(float(np.max(np.abs(xa))))
+        m.sregs[int(op["out_slot"])] = np.array([inv], np.float16).view(np.uint16)[0]
+        m.sregs[int(op["out_slot"]) + 1] = np.array([fwd], np.float16).view(np.uint16)[0]
+        if op["flags2"] & 2:   # FX_MAXQ: QUANT's result with the inverse scale
+            v = np.round(xa * np.float32(np.float16(inv)))
+            q = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8)
+            m.mem(d, M * N)[:] = q.view(np.uint8)
+    elif k in (K["DEQUANT_SCALED"], K["DEQUANT_ACCUM"]):
+        acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
+        if op["flags"] & 16:   # F_SPLIT: second half of the vector at c
+            vec = np.concatenate([_f16(m, b, N), _f16(m, c, N)])
+        else:
+            vec = _f16(m, b, 2 * N if k == K["DEQUANT_SCALED"] else N)
+        if k == K["DEQUANT_SCALED"]:
+            r = acc * vec[:N].reshape(1, N) * np.float32(m.sreg(s[0])) + vec[N:].reshape(1, N)
+        else:
+            r = acc * vec[:N].reshape(1, N)
+        m.mem(d, M * N * 2)[:] = r.astype(np.float32).astype(np.float16).view(np.uint8).ravel()
+    elif k == K["VADD_F16"]:
+        xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
+            else _f16(m, a, M * N)
+        r = xa + _f16(m, b, M * N)
+        m.mem(d, M * N * 2)[:] = r.astype(np.float16).view(np.uint8)
+    elif k == K["LAYERNORM_F16"]:
+        x = _f16(m, a, M * N).reshape(M, N)
+        gb = np.concatenate([_f16(m, b, N), _f16(m, c, N)]) if op["flags"] & 16 else _f16(m, b, 2 * N)
+        mean = x.mean(axis=-1, keepdims=True).astype(np.float32)
+        var = x.var(axis=-1, keepdims=True).astype(np.float32)
+        y = (x - mean) / np.sqrt(var + np.float32(1e-5))
+        m.mem(d, M * N * 2)[:] = (y * gb[:N] + gb[N:]).astype(np.float32).astype(np.float16).view(np.uint8).ravel()
+    elif k == K["GELU_F16"]:
+        m.mem(d, M * N * 2)[:] = G._gelu_tanh(_f16(m, a, M * N)).astype(np.float32).astype(np.float16).view(np.uint8)
+    elif k == K["MASKED_SOFTMAX_F16"]:
+        qrb, vkl = _attn_context(op, params)
+        out = _softmax_rows(_f16(m, a, M * N).reshape(M, N), True, qrb, vkl)
+        m.mem(d, M * N * 2)[:] = out.astype(np.float16).view(np.uint8).ravel()
+    elif k == K["TRANSPOSE"]:
+        src = m.mem(a, M * N).view(np.int8).reshape(M, N)
+        m.mem(d, M * N)[:] = np.ascontiguousarray(src.T).view(np.uint8).ravel()
+    else:
+        raise NotImplementedError(f"plan executor: op kind {k}")
 
 
 def final_state(m: PlanMachine):
