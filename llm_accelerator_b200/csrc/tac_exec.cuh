@@ -489,8 +489,7 @@ __device__ __forceinline__ void softmax_row_f16(float* rowbuf, uint32_t n, bool 
       int8_t q8[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float r = rintf(__fmul_rn(h2f(h[j]), qs));
-        q8[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+        q8[j] = sat8(__fmul_rn(h2f(h[j]), qs));
       }
       reinterpret_cast<uint2*>(qout)[g] = pack_b(q8);
     }
@@ -571,8 +570,7 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
         const uint4 x = *reinterpret_cast<const uint4*>(Ah + (uint64_t(r) * K + k) * 2);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float v = rintf(__fmul_rn(h2f(h_at(x, j)), s0));
-          q8[j] = (v == v) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(v, -128.f), 127.f))) : int8_t(0);
+          q8[j] = sat8(__fmul_rn(h2f(h_at(x, j)), s0));
         }
       }
       *reinterpret_cast<uint2*>(As + r * bts + k) = pack_b(q8);
@@ -587,8 +585,7 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
       int8_t q8[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float r = rintf(__fmul_rn(h2f(h_at(x, j)), s1));
-        q8[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+        q8[j] = sat8(__fmul_rn(h2f(h_at(x, j)), s1));
       }
       const uint32_t e = i * 8;
       uint8_t* dst = bt ? Bt + (e / K) * bts + (e % K) : Braw + e;   // [N][K] rows or [K][N]
@@ -999,8 +996,7 @@ __device__ __noinline__ void ew_kernel(const ExecArgs& A, const DevOp& op, const
         int8_t q[8];
   #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float r = rintf(__fmul_rn(h2f(h_at(ra[g], j)), s0));
-          q[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+          q[j] = sat8(__fmul_rn(h2f(h_at(ra[g], j)), s0));
         }
         *reinterpret_cast<uint2*>(d + e0[g]) = pack_b(q);
       } else if constexpr (KIND == K_GELU_F16) {
@@ -1173,8 +1169,7 @@ __device__ __noinline__ void ew_staged(const ExecArgs& A, const DevOp& op, const
       int8_t q[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float r = rintf(__fmul_rn(h2f(h_at(x, j)), s0));
-        q[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+        q[j] = sat8(__fmul_rn(h2f(h_at(x, j)), s0));
       }
       *reinterpret_cast<uint2*>(d + e) = pack_b(q);
     } else if constexpr (KIND == K_GELU_F16) {
@@ -1350,8 +1345,7 @@ __device__ __noinline__ void op_seg_ew(const ExecArgs& A, const DevOp& op, const
         int8_t o[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float r = rintf(__fmul_rn(h2f(h_at(va[q], j)), s0));
-          o[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+          o[j] = sat8(__fmul_rn(h2f(h_at(va[q], j)), s0));
         }
         *reinterpret_cast<uint2*>(d + uint64_t(u) * 8) = pack_b(o);
       } else {
@@ -1433,8 +1427,7 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
       int8_t q8[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float r = rintf(__fmul_rn(h2f(h_at(x8, j)), s0));
-        q8[j] = (r == r) ? static_cast<int8_t>(static_cast<int>(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+        q8[j] = sat8(__fmul_rn(h2f(h_at(x8, j)), s0));
       }
       *reinterpret_cast<uint2*>(out + g * 8) = pack_b(q8);
     }

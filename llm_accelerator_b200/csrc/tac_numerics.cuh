@@ -32,12 +32,13 @@ __device__ __forceinline__ uint16_t d2h(double d) {
   return h;
 }
 
-// np.clip(np.round(v), -128, 127).astype(np.int8)
+// np.clip(np.round(v), -128, 127).astype(np.int8) with NaN -> 0 (QUANT's rule and the
+// REQUANT family's): one convert that rounds to nearest even, saturates to the int8
+// range and turns NaN into 0 (PTX cvt.rni.sat.s8.f32, written to a 32-bit register).
 __device__ __forceinline__ int8_t sat8(float v) {
-  float r = rintf(v);
-  if (r != r) return 0;
-  r = fminf(fmaxf(r, -128.f), 127.f);
-  return static_cast<int8_t>(static_cast<int>(r));
+  int32_t r;
+  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return static_cast<int8_t>(r);
 }
 
 // np.clip(np.round(v), int32.min, int32.max).astype(np.int32) for float32 v

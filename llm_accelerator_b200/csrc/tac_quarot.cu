@@ -33,6 +33,7 @@ namespace {
 using tac::d2h;
 using tac::f2h;
 using tac::h2f;
+using tac::sat8;
 
 constexpr int kFwhtWarps = 8;
 
@@ -125,16 +126,14 @@ __global__ void quant_act_kernel(const uint16_t* __restrict__ XR, int8_t* __rest
       uint32_t lo = 0, hi = 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float r = rintf(__fmul_rn(h2f(uint16_t(wd[j / 2] >> (16 * (j & 1)))), inv));
-        const int8_t q = (r == r) ? int8_t(int(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+        const int8_t q = sat8(__fmul_rn(h2f(uint16_t(wd[j / 2] >> (16 * (j & 1)))), inv));
         if (j < 4) lo |= uint32_t(uint8_t(q)) << (8 * j);
         else hi |= uint32_t(uint8_t(q)) << (8 * (j - 4));
       }
       *reinterpret_cast<uint2*>(XQ + i) = make_uint2(lo, hi);
     } else {
       for (long j = i; j < n; ++j) {
-        const float r = rintf(__fmul_rn(h2f(XR[j]), inv));
-        XQ[j] = (r == r) ? int8_t(int(fminf(fmaxf(r, -128.f), 127.f))) : int8_t(0);
+        XQ[j] = sat8(__fmul_rn(h2f(XR[j]), inv));
       }
     }
   }

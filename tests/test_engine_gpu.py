@@ -125,6 +125,40 @@ def test_engine_running_fp16_sum(shape, parts, produced, commute):
     assert sim.state.cycle_count == orc.state.cycle_count
 
 
+@pytest.mark.parametrize("scale", [0x3C00, 0x2000, 0x50B0, 0x7BFF, 0x0001, 0xC200, 0x7C00, 0x7E00],
+                         ids=["1", "2^-7", "37.5", "65504", "2^-24", "-3", "inf", "nan"])
+def test_engine_quant_every_fp16_value(scale):
+    """QUANT_FP32_INT8 of all 65536 FP16 bit patterns (NaNs, infinities,
+    subnormals, halfway cases) with one scale register is bit-exact against
+    the oracle: rint(x * s) ties to even, NaN -> 0, clipped to int8."""
+    from types import SimpleNamespace
+    from llm_accelerator_b200 import isa
+    from oracle import golden as G
+    X = 8192 // 16
+    prog = [dict(opcode=0x05, addr_reg=0, imm28=0), dict(opcode=0x06, addr_reg=0, imm28=0),
+            dict(opcode=0x03, M=64 // 16 - 1, N=1024 // 16 - 1, K=0),
+            dict(opcode=0x07, buf_id=0, sram_off=0, xfer_len=8192, addr_reg=0, dram_off=X),
+            dict(opcode=0x04, sreg=1, src_mode=0, imm16=scale),
+            dict(opcode=0x18, src1_buf=0, src1_off=0, src2_buf=0, src2_off=0, dst_buf=1, dst_off=0, sreg=1),
+            dict(opcode=0x01)]
+    words = [isa.word_of(isa.encode(SimpleNamespace(**d))) for d in prog]
+    img = np.zeros(X * 16 + 131072 + 4096, np.uint8)
+    img[X * 16:X * 16 + 131072] = np.arange(65536, dtype=np.uint16).view(np.uint8)
+    sim = _sim()
+    sim.load_program(ProgramStub(words))
+    sim.state.dram[:len(img)] = img.tobytes()
+    sim.run()
+    orc = G.OracleSimulator()
+    stub = ProgramStub(words)
+    orc.load_program(SimpleNamespace(instructions=stub.instructions, data_base=0, data=img.tobytes(), entry_point=0,
+                                     insn_count=stub.insn_count))
+    orc.run()
+    got = np.frombuffer(bytes(sim.state.wbuf), np.int8)[:65536]
+    want = np.frombuffer(bytes(orc.state.wbuf), np.int8)[:65536]
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, f"{bad.size} values differ, first FP16 bits {bad[:4]}: got {got[bad[:4]]} want {want[bad[:4]]}"
+
+
 @pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
 def test_engine_bundle_run_matches_reference(name):
     from llm_accelerator_b200.runner import HostRunner
