@@ -688,7 +688,7 @@ class Compiler {
     auto it = sm_out_.find(op.a);
     if (it == sm_out_.end() || pv_of_.count(it->second)) return -1;
     const DevOp& x = P->ops[it->second];
-    if (!(x.flags & F_WIDE) || x.M != op.M || x.N != op.K || op.M % 16 || op.K % 16) return -1;
+    if (!(x.flags & F_WIDE) || x.M != op.M || x.N != op.K || op.M % 16 || op.K % 16 || !pv_ok(x.M, x.N)) return -1;
     Access rest = acc;   // every read but the softmax rows
     rest.reads.erase(std::remove_if(rest.reads.begin(), rest.reads.end(),
                                     [&](const std::pair<uint64_t, uint64_t>& r) { return r.first == op.a; }),
@@ -727,7 +727,7 @@ class Compiler {
     op.b = src(u0, 2 * half_bytes, acc);
   }
 
-  // Operand a of a MAX_ABS / QUANT / VADD_F16 read straight from scattered
+  // Operand a of a MAX_ABS / QUANT / VADD_F16 / GELU read straight from scattered
   // units through a segment list (F_SEGA) rather than gathered first: the
   // gather would be a dependency level of its own.  Returns false (nothing
   // emitted) when the units are contiguous or form too many runs.
@@ -1445,7 +1445,7 @@ int Compiler::h_rtype(const Insn& x) {
         cycles_ += M * N;
         return 0;
       }
-      op.a = src(s1, M * N * 2, acc);
+      if (op.kind != K_GELU_F16 || !src_segments(s1, M * N * 2, acc, op)) op.a = src(s1, M * N * 2, acc);
       op.d = dst(d, M * N * 2, acc);
       cycles_ += M * N;
       break;
@@ -1538,7 +1538,9 @@ int Compiler::h_rtype(const Insn& x) {
   if (pv_x >= 0 && P->ops.size() == n_before + 1) {
     const uint32_t y = static_cast<uint32_t>(n_before);
     pv_of_[static_cast<uint32_t>(pv_x)] = y;
-    P->ops[pv_x].flags2 |= FX_PV;
+    DevOp& xo = P->ops[pv_x];
+    xo.flags2 |= FX_PV;
+    if ((op.flags & F_QB) && pvpf_ok(xo.M, xo.N, xo.K, op.N, op.flags & F_BT)) xo.flags2 |= FX_PVPF;
     P->ops[y].flags2 |= FX_PVY;
     auto& rd = op_arena_reads_[y];   // read inside the QK^T task: keeps nothing else live
     rd.erase(std::remove_if(rd.begin(), rd.end(),
@@ -1919,8 +1921,8 @@ void Compiler::build_tasks() {
         per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN + 16383) / 16384)));
         break;
       default: {  // element-wise ops: ew_task_elems(kind) elements per task
-        if (op.flags & F_SEGA) {   // segment-list operand: one task per sequence
-          per_seq(i, 1);
+        if (op.flags & F_SEGA) {   // segment-list operand: kSegTaskUnits operand units per task
+          per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN / 8 + kSegTaskUnits - 1) / kSegTaskUnits)));
           break;
         }
         const uint64_t te = ew_task_elems(op.kind);
@@ -1964,10 +1966,15 @@ void Compiler::prefetch_hint(const DevOp& op, Task& t) const {
         return 1;
     }
   };
-  if (op.flags & F_SEGA) {
-    if (op.nseg) {
-      phys = P->segs[op.seg0].src;
-      units = P->segs[op.seg0].n;
+  if (op.flags & F_SEGA) {   // the segment holding the task's first operand unit, from that unit on
+    const uint64_t u0 = op.kind == K_MAX_ABS ? 0 : uint64_t(t.tile) * kSegTaskUnits;
+    for (uint32_t k = 0; k < op.nseg; ++k) {
+      const Segment& sg = P->segs[op.seg0 + k];
+      if (sg.dst <= u0 && u0 < sg.dst + sg.n) {
+        phys = sg.src + (u0 - sg.dst);
+        units = std::min<uint64_t>(sg.dst + sg.n - u0, op.kind == K_MAX_ABS ? sg.n : kSegTaskUnits);
+        break;
+      }
     }
   } else {
     switch (op.kind) {
@@ -1983,9 +1990,9 @@ void Compiler::prefetch_hint(const DevOp& op, Task& t) const {
         break;
       case K_MATMUL:
         if (op.flags & F_TC) break;
-        if (!(op.b & kSharedBit)) {   // per-sequence B: the whole matrix
+        if (!(op.b & kSharedBit)) {   // per-sequence B: the whole matrix (FP16 when quantised on load)
           phys = op.b;
-          units = uint64_t(op.K) * op.N / kUnit;
+          units = uint64_t(op.K) * op.N * ((op.flags & F_QB) ? 2 : 1) / kUnit;
         } else {
           phys = op.a;
           units = uint64_t(std::min<uint32_t>(op.M, 128)) * op.K / kUnit;

@@ -506,10 +506,10 @@ __device__ __forceinline__ void softmax_row_f16(float* rowbuf, uint32_t n, bool 
 // blocks.  With F_QB, B arrives as FP16 and is quantised on the way in, with
 // QUANT's rule.  Padding bytes are zero.  a_staged: the int8 A tile is
 // already in shared memory (the P.V op of an FX_PV pair, whose QK^T softmax
-// wrote it there).
+// wrote it there); b_staged: so are the FP16 B copies (FX_PVPF).
 // ---------------------------------------------------------------------------------
 __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
-                                            bool a_staged) {
+                                            bool a_staged, bool b_staged) {
   const uint32_t M = op.M, N = op.N, K = op.K, seq = t.seq0;
   const uint32_t kc32 = (K + 31) & ~31u;
   const uint32_t bts = kc32 + 16;
@@ -536,7 +536,8 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
     }
   }
   if (qb) {
-    for (uint32_t i = htid(); i < K * N / 8; i += kThreads) cp_async16(Bh + i * 16, Bg + uint64_t(i) * 16, 16u);
+    if (!b_staged)
+      for (uint32_t i = htid(); i < K * N / 8; i += kThreads) cp_async16(Bh + i * 16, Bg + uint64_t(i) * 16, 16u);
   } else if (bt) {
     for (uint32_t i = htid(); i < n8 * 8 * kv; i += kThreads) {
       const uint32_t n = i / kv, v = i % kv;
@@ -621,6 +622,13 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
     }
     hsync();
   }
+  if (op.flags2 & FX_PVPF) {   // V for the P.V op: in flight while this op multiplies and takes the softmax
+    const DevOp& y = A.ops[op.seg0];
+    uint8_t* vs = smem + wide_mm_bh_off(y.M, y.N, y.K, (y.flags & F_BT) != 0);
+    const uint8_t* vg = pptr(A, y.b, seq);
+    for (uint32_t i = htid(); i < y.K * y.N / 8; i += kThreads) cp_async16(vs + i * 16, vg + uint64_t(i) * 16, 16u);
+    cp_async_commit();
+  }
   const int warp = htid() >> 5, lane = htid() & 31;
   const int g = lane >> 2, q = lane & 3;
   const uint32_t pairs = nblocks * n8;
@@ -656,13 +664,13 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   }
   if (sm) hsync();   // every warp is done with the operand tiles: the rows reuse the space
   // F_SM: the dequantised rows [M][N] FP16 in shared memory, then per-warp
-  // float row buffers and pairwise-sum scratch behind them (FX_PV: all of it
+  // float row buffers and pairwise-sum scratch behind them (FX_PV: packed
   // behind the P.V op's A tile, which the softmax rows are quantised into)
   const bool pv = (op.flags2 & FX_PV) != 0;
-  uint8_t* sbase = smem + (pv ? kPvSoftmaxOff : 0u);
+  uint8_t* sbase = smem + (pv ? pv_a_bytes(M, N) : 0u);
   uint16_t* Sc = reinterpret_cast<uint16_t*>(sbase);
-  float* rows = reinterpret_cast<float*>(sbase + 32 * 256 * 2);
-  uint32_t* pws = reinterpret_cast<uint32_t*>(sbase + 32 * 256 * 2 + kWarps * 256 * 4);
+  float* rows = reinterpret_cast<float*>(sbase + (pv ? M * N * 2 : 32u * 256 * 2));
+  uint32_t* pws = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(rows) + kWarps * (pv ? N : 256u) * 4);
   int32_t* D = reinterpret_cast<int32_t*>(pptr(A, op.d, seq));
   const int32_t* C = (op.flags & F_ACCUMULATE) ? reinterpret_cast<const int32_t*>(pptr(A, op.c, seq)) : nullptr;
   const bool store_i32 = !(op.flags & F_NOI32);
@@ -1316,17 +1324,19 @@ __device__ __forceinline__ const uint4* seg_unit(const ExecArgs& A, const DevOp&
   return reinterpret_cast<const uint4*>(pptr(A, src[lo], seq)) + (u - ofs[lo]);
 }
 
-// QUANT / VADD_F16 with a segment-list first operand; one sequence per task.
+// QUANT / VADD_F16 / GELU with a segment-list first operand; a task takes
+// operand units [tile * kSegTaskUnits, +kSegTaskUnits) of one sequence.
 __device__ __noinline__ void op_seg_ew(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
   const uint32_t seq = t.seq0;
-  const uint32_t units = op.M * op.N / 8;   // FP16 operand: 8 elements per 16-byte unit
+  const uint32_t u_begin = t.tile * kSegTaskUnits;
+  const uint32_t units = min(op.M * op.N / 8, u_begin + kSegTaskUnits);   // FP16 operand: 8 elements per unit
   // the register's raw bits load while the segment table is staged; they are
   // converted at their first use, after the operand loads are in flight
   const uint16_t s0b = op.kind == K_QUANT ? sreg_bits(A, op.s[0], seq) : uint16_t(0);
   seg_stage(A, op, smem);
   const uint4* b = reinterpret_cast<const uint4*>(pptr(A, op.b, seq));
   uint8_t* d = pptr(A, op.d, seq);
-  for (uint32_t u0 = htid(); u0 < units; u0 += 4 * kThreads) {
+  for (uint32_t u0 = u_begin + htid(); u0 < units; u0 += 4 * kThreads) {
     uint4 va[4], vb[4];
 #pragma unroll
     for (uint32_t q = 0; q < 4; ++q) {
@@ -1348,6 +1358,11 @@ __device__ __noinline__ void op_seg_ew(const ExecArgs& A, const DevOp& op, const
           o[j] = sat8(__fmul_rn(h2f(h_at(va[q], j)), s0));
         }
         *reinterpret_cast<uint2*>(d + uint64_t(u) * 8) = pack_b(o);
+      } else if (op.kind == K_GELU_F16) {
+        uint16_t h[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = f2h(gelu_f32(h2f(h_at(va[q], j))));
+        *reinterpret_cast<uint4*>(d + uint64_t(u) * 16) = pack_h(h);
       } else {
         uint16_t h[8];
 #pragma unroll
@@ -1783,10 +1798,10 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_MATMUL:
       if (op.flags & F_TC) op_matmul_tc(A, op, t, smem, tc, t.op);
       else if (op.flags & F_WIDE) {
-        op_matmul_wide(A, op, t, smem, false);
+        op_matmul_wide(A, op, t, smem, false, false);
         if (op.flags2 & FX_PV) {   // the P.V op, its A tile written by the softmax above
           hsync();
-          op_matmul_wide(A, A.ops[op.seg0], t, smem, true);
+          op_matmul_wide(A, A.ops[op.seg0], t, smem, true, (op.flags2 & FX_PVPF) != 0);
         }
       }
       else op_matmul(A, op, t, smem);
@@ -1833,6 +1848,8 @@ constexpr size_t kExecSmem = kHalves * kExecOpSmem + kHalves * 128;
 static_assert(sizeof(TcShared) <= 128, "TcShared outgrew its slot");
 static_assert(kStageBytes <= kExecOpSmem, "element-wise staging exceeds the op shared memory");
 static_assert(kWideMmSmem <= kExecOpSmem, "wide MATMUL exceeds the op shared memory");
+static_assert(kWarps == int(kExecWarps) && kPwScratchBytes == kWarps * 3 * kPwMaxLeaves * 4,
+              "FX_PV layout constants disagree with the executor");
 static_assert(kSegTableOff + kMaxSegRuns * 12 <= kExecOpSmem, "segment table exceeds the op shared memory");
 static_assert(kSegTableOff + kMaxSegRuns * 12 <= kMaxQStage && kMaxQStage + 16384 * 2 <= kExecOpSmem,
               "MAX_ABS staging overlaps the segment table or exceeds the op shared memory");

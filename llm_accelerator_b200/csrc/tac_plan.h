@@ -100,13 +100,15 @@ constexpr uint32_t FX_PV = 4;          // wide F_SM MATMUL (QK^T) whose task als
                                        // straight into its shared-memory A tile
 constexpr uint32_t FX_PVY = 8;         // the P.V op of an FX_PV pair: same level, no tasks of its own
 constexpr uint32_t FX_SMSKIP = 16;     // FX_PV op whose softmax rows only its P.V op reads: not stored
-constexpr uint32_t kPvSoftmaxOff = 9216;   // FX_PV: the softmax scratch starts after the P.V A tile
-                                           // (at most 32 rows of 256 + 16 bytes)
+constexpr uint32_t FX_PVPF = 32;       // FX_PV op that stages its P.V op's FP16 B (V) in shared memory once
+                                       // its own operand tiles are quantised; the P.V op skips that load
 
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 
 // Most runs an operand read through a segment list may have (longer lists are gathered).
 constexpr uint32_t kMaxSegRuns = 256;
+constexpr uint32_t kSegTaskUnits = 512;   // operand units (4096 FP16 elements) of one QUANT / VADD_F16 task
+                                          // whose first operand is a segment list
 
 struct DevOp {
   uint16_t kind;
@@ -194,6 +196,33 @@ TAC_HD constexpr uint32_t wide_mm_smem(uint32_t M, uint32_t N, uint32_t K, bool 
 TAC_HD constexpr bool wide_mm_ok(uint32_t M, uint32_t N, uint32_t K, bool bt, bool qb, bool qa = false) {
   return M > 0 && M <= 32 && K > 0 && K <= 256 && N > 0 && N <= 256 && M % 16 == 0 && K % 16 == 0 &&
          N % 16 == 0 && wide_mm_smem(M, N, K, bt, qb, qa) <= kWideMmSmem;
+}
+// Offset of the FP16 B (F_QB) in the wide MATMUL layout: after the A and B^T
+// tiles and, when B is not read transposed, the raw int8 B.
+TAC_HD constexpr uint32_t wide_mm_bh_off(uint32_t M, uint32_t N, uint32_t K, bool bt) {
+  return ((M + 15) / 16) * 16 * (((K + 31) & ~31u) + 16) + ((N + 7) / 8) * 8 * (((K + 31) & ~31u) + 16) +
+         (bt ? 0u : ((K + 31) & ~31u) * N);
+}
+
+// Shared memory of an FX_PV task (QK^T [M x K] x [K x N], then P.V with
+// K' = N): the P.V op's int8 A tile at 0, then the softmax scratch (the
+// dequantised rows [M][N] FP16, kExecWarps row buffers of N floats, the
+// pairwise-sum scratch); the QK^T op's F_DQ scale row keeps the last 512
+// bytes.  With FX_PVPF, V lands at the P.V op's FP16-B offset, which must
+// clear the softmax scratch and the QK^T op's A and B^T tiles (read by its
+// MMAs while V is in flight).
+constexpr uint32_t kExecWarps = 8;                           // warps of one half
+constexpr uint32_t kPwScratchBytes = kExecWarps * 3 * 64 * 4;   // pairwise-sum scratch of every warp
+TAC_HD constexpr uint32_t pv_a_bytes(uint32_t M, uint32_t N) { return ((M + 15) / 16) * 16 * (((N + 31) & ~31u) + 16); }
+TAC_HD constexpr uint32_t pv_scratch_end(uint32_t M, uint32_t N) {
+  return pv_a_bytes(M, N) + M * N * 2 + kExecWarps * N * 4 + kPwScratchBytes;
+}
+TAC_HD constexpr bool pv_ok(uint32_t M, uint32_t N) { return pv_scratch_end(M, N) <= kWideMmSmem - 512; }
+TAC_HD constexpr bool pvpf_ok(uint32_t M, uint32_t N, uint32_t K, uint32_t n_pv, bool bt_pv) {
+  return pv_scratch_end(M, N) <= wide_mm_bh_off(M, n_pv, N, bt_pv) &&
+         ((M + 15) / 16) * 16 * (((K + 31) & ~31u) + 16) + ((N + 7) / 8) * 8 * (((K + 31) & ~31u) + 16) <=
+             wide_mm_bh_off(M, n_pv, N, bt_pv) &&
+         wide_mm_bh_off(M, n_pv, N, bt_pv) + N * n_pv * 2 <= kWideMmSmem - 512;
 }
 
 // Rows of a row-op task: FP16 softmaxes of at most 1024 columns take 16 rows

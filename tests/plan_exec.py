@@ -259,7 +259,9 @@ def _run_op(m: PlanMachine, op, segs, params):
         y = (x - mean) / np.sqrt(var + np.float32(1e-5))
         m.mem(d, M * N * 2)[:] = (y * gb[:N] + gb[N:]).astype(np.float32).astype(np.float16).view(np.uint8).ravel()
     elif k == K["GELU_F16"]:
-        m.mem(d, M * N * 2)[:] = G._gelu_tanh(_f16(m, a, M * N)).astype(np.float32).astype(np.float16).view(np.uint8)
+        xa = _seg_read(m, op, segs, M * N * 2).view(np.float16).astype(np.float32) if op["flags"] & 32 \
+            else _f16(m, a, M * N)
+        m.mem(d, M * N * 2)[:] = G._gelu_tanh(xa).astype(np.float32).astype(np.float16).view(np.uint8)
     elif k == K["MASKED_SOFTMAX_F16"]:
         qrb, vkl = _attn_context(op, params)
         out = _softmax_rows(_f16(m, a, M * N).reshape(M, N), True, qrb, vkl)

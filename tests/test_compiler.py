@@ -224,6 +224,12 @@ def _check_prefetch_hints(p, dram_bytes, shared_bytes):
     assert np.all(end[shared] <= np.uint64(shared_bytes // 16))
     assert np.all(end[~shared] <= np.uint64(block_units))
     assert np.all(units <= 4096)
+    # a per-sequence MATMUL operand B: the hint covers at most B's bytes (FP16 under F_QB)
+    for t in hinted:
+        op = ops[int(t["op"])]
+        if int(op["kind"]) == PE.K["MATMUL"] and not int(op["b"]) >> 63 and not int(op["flags"]) & 8:
+            b_units = int(op["K"]) * int(op["N"]) * (2 if int(op["flags"]) & 512 else 1) // 16
+            assert int(t["pf_phys"]) == int(op["b"]) and int(t["pf_units"]) == min(b_units, 4096)
 
 
 @pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
@@ -354,7 +360,7 @@ def test_tasks_cover_every_sequence_and_element_once(batch):
         cov = seen.setdefault(int(t["op"]), np.zeros((batch, MN), np.int32))
         s0, n = int(t["seq0"]), int(t["nseq"])
         assert s0 + n <= batch
-        te = task_elems(int(op["kind"]))
+        te = 4096 if int(op["flags"]) & 32 else task_elems(int(op["kind"]))   # F_SEGA: 512 operand units
         if n > 1:
             assert n * MN <= te and int(t["tile"]) == 0
             cov[s0:s0 + n] += 1
