@@ -7,9 +7,12 @@ ProgramBundle with a 256-position KV cache; 64 independent sequences per GPU
 (weak scaling: N GPUs run 64 x N sequences, each rank its own shard of the
 sequence ids, no collective on the data path; ``--strong`` splits a fixed
 global batch instead).  A step runs the decode stream once for every sequence
-(one token each).  ``value`` times K teacher-forced prompt steps with
-their runtime parameters already in device memory; ``e2e`` times K greedy
-steps through the public runner API with host buffers (runtime words in,
+(one token each).  Every sequence first consumes a 128-token random prompt
+(prefill + teacher-forced decode steps, untimed; shorter when the KV window
+must also hold the warm-up, timed and e2e steps), then runs W warm-up steps.
+``value`` times the next K teacher-forced decode steps with their runtime
+parameters already in device memory; ``e2e`` times the K greedy steps after
+them through the public runner API with host buffers (runtime words in,
 argmax token ids out, every step).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -350,22 +353,24 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     K, W = args.steps, args.warmup
     if 1 + W + 2 * K >= w["kv_len"]:
         raise SystemExit("steps + warmup exceed the KV length of the workload")
-    # per-sequence prompt tokens (seeded by sequence id); teacher-forced steps
-    # past the prompt keep drawing from the same generator
-    prompts = np.stack([np.random.default_rng(int(s)).integers(0, VOCAB, max(w["prompt"], 1 + W + K))
-                        for s in seqs])
+    # the workload's prompt is consumed first (untimed), as far as the KV
+    # window leaves room for the warm-up, timed and e2e steps after it
+    P = max(1, min(w["prompt"], w["kv_len"] - 1 - W - 2 * K))
+    # per-sequence tokens (seeded by sequence id): the prompt, then the
+    # teacher-forced continuation of the warm-up and timed steps
+    prompts = np.stack([np.random.default_rng(int(s)).integers(0, VOCAB, P + W + K) for s in seqs])
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    # warm-up: prefill + W teacher-forced prompt steps
+    # the prompt (prefill + P - 1 decode steps), then W warm-up steps, all teacher-forced
     runner.step("prefill", prompts[:, 0], np.zeros(B, int))
-    for pos in range(1, 1 + W):
+    for pos in range(1, P + W):
         runner.step("decode", prompts[:, pos], np.full(B, pos))
-    # value: K teacher-forced prompt steps, parameters staged on the device
-    p0 = 1 + W
+    # value: K teacher-forced steps, parameters staged on the device
+    p0 = P + W
     params = np.stack([runner.params("decode", prompts[:, p], np.full(B, p)) for p in range(p0, p0 + K)])
     d_params = torch.from_numpy(params.view(np.int64)).to(dev)
     stride = params.shape[1] * params.shape[2] * 8
@@ -431,8 +436,9 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
             "data": "synthetic: seeded random-init weights in the reference-compiled program",
             "config": {"workload": w["desc"], "global_batch": B_total, "per_gpu_batch": B,
                        "parallelism": f"sequences sharded over {world} GPU(s)",
-                       "timed": f"{K} teacher-forced decode steps (positions {p0}..{p0 + K - 1}); "
-                                f"e2e: {K} greedy steps",
+                       "timed": f"{K} teacher-forced decode steps (positions {p0}..{p0 + K - 1}, after a "
+                                f"{P}-token prompt and {W} warm-up steps); e2e: {K} greedy steps "
+                                f"(positions {p0 + K}..{p0 + 2 * K - 1})",
                        "l2": f"inputs larger than L2: {shared_b / 1e6:.0f} MB of weights read per step"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic_per_launch(args.workload, B),

@@ -476,7 +476,20 @@ __device__ __forceinline__ void softmax_row_f16(float* rowbuf, uint32_t n, bool 
   __syncwarp();
   for (uint32_t j = lane; j < n; j += 32) rowbuf[j] = j <= lst ? exp_f32(__fsub_rn(rowbuf[j], mx)) : 0.f;
   __syncwarp();
-  const float denom = warp_pairwise_sum_smem(rowbuf, n, pw);
+  const float denom = warp_pairwise_sum_smem(rowbuf, n, pw, false, 0.f, lst + 1);
+  if (!out && qout) {   // only the quantised rows: column j on lane j % 32; masked columns are zero
+    for (uint32_t j0 = 0; j0 < n; j0 += 32) {
+      const uint32_t j = j0 + lane;
+      int8_t q8 = 0;
+      if (j0 <= lst && j <= lst) {
+        const float e = rowbuf[j];
+        const uint16_t h = f2h(!masked ? __fdiv_rn(e, denom) : (denom > 0.f ? __fdiv_rn(e, denom) : 0.f));
+        q8 = sat8(__fmul_rn(h2f(h), qs));
+      }
+      if (j < n) qout[j] = q8;
+    }
+    return;
+  }
   for (uint32_t g = lane; g < n / 8; g += 32) {
     uint16_t h[8];
 #pragma unroll
@@ -508,10 +521,14 @@ __device__ __forceinline__ void softmax_row_f16(float* rowbuf, uint32_t n, bool 
 // already in shared memory (the P.V op of an FX_PV pair, whose QK^T softmax
 // wrote it there); b_staged: so are the FP16 B copies (FX_PVPF).
 // ---------------------------------------------------------------------------------
-__device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
-                                            bool a_staged, bool b_staged) {
+__device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
+                                                bool a_staged, bool b_staged, uint32_t k_used = 0xFFFFFFFFu) {
   const uint32_t M = op.M, N = op.N, K = op.K, seq = t.seq0;
   const uint32_t kc32 = (K + 31) & ~31u;
+  // K rows that can be nonzero in A (the P.V op: P is zero past the QK^T
+  // op's key columns kept), rounded up to the MMA's 32; zeros times any int8
+  // add nothing, so the rows past them are neither quantised nor multiplied
+  const uint32_t kr = k_used < K ? ((k_used + 31) & ~31u) : kc32;
   const uint32_t bts = kc32 + 16;
   const uint32_t nblocks = (M + 15) / 16, n8 = (N + 7) / 8;
   const bool bt = (op.flags & F_BT) != 0, qb = (op.flags & F_QB) != 0;
@@ -559,6 +576,23 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   cp_async_commit();
   const uint16_t sb = qb ? sreg_bits(A, op.s[1], seq) : uint16_t(0);
   const uint16_t sa = qa ? sreg_bits(A, op.s[0], seq) : uint16_t(0);
+  const bool sm = (op.flags & F_SM) != 0;
+  uint32_t qrb = op.attn_qrb, vkl = op.attn_vkl;
+  if (sm && (op.flags & F_ATTN_DYN)) {
+    const uint64_t pv = A.params[uint64_t(seq) * A.n_params + op.param];
+    qrb = pv & 0xFFFF;
+    vkl = (pv >> 16) & 0xFFFF;
+  }
+  // masked softmax whose int32 and dequantised scores nothing reads: key
+  // columns past every row's last visible one (min(M - 1 + qrb, vkl - 1))
+  // are zero after the softmax whatever their scores, so only the first nk
+  // keys (B^T rows) are quantised, multiplied and dequantised
+  uint32_t nk = N;
+  if (sm && bt && (op.flags & F_SMMASK) && (op.flags & F_NOI32) && (op.flags & F_NODQ) &&
+      !(op.flags & F_ACCUMULATE)) {
+    const int64_t lmax = int64_t(M) - 1 + qrb < int64_t(vkl) - 1 ? int64_t(M) - 1 + qrb : int64_t(vkl) - 1;
+    nk = lmax < 0 ? 0u : min(N, (uint32_t(lmax) + 8) & ~7u);
+  }
   cp_async_wait<0>();
   hsync();
   if (qa) {
@@ -581,7 +615,8 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   if (qb) {
     // QUANT's rule: rint(x * s), NaN -> 0, clipped to int8; 8 elements per step
     const float s1 = h2f(sb);
-    for (uint32_t i = htid(); i < K * N / 8; i += kThreads) {
+    const uint32_t qn = bt ? nk * K / 8 : min(K, kr) * N / 8;   // B^T rows of the kept keys, or B's K rows < kr
+    for (uint32_t i = htid(); i < qn; i += kThreads) {
       const uint4 x = *reinterpret_cast<const uint4*>(Bh + i * 16);
       int8_t q8[8];
 #pragma unroll
@@ -608,7 +643,7 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   }
   if (!bt) {
     const uint32_t nb4 = N / 4;
-    for (uint32_t i = htid(); i < (kc32 / 4) * nb4; i += kThreads) {
+    for (uint32_t i = htid(); i < (kr / 4) * nb4; i += kThreads) {
       const uint32_t kb = (i / nb4) * 4, nb = (i % nb4) * 4;
       uint32_t r[4];
 #pragma unroll
@@ -632,13 +667,6 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
   const int warp = htid() >> 5, lane = htid() & 31;
   const int g = lane >> 2, q = lane & 3;
   const uint32_t pairs = nblocks * n8;
-  const bool sm = (op.flags & F_SM) != 0;
-  uint32_t qrb = op.attn_qrb, vkl = op.attn_vkl;
-  if (sm && (op.flags & F_ATTN_DYN)) {
-    const uint64_t pv = A.params[uint64_t(seq) * A.n_params + op.param];
-    qrb = pv & 0xFFFF;
-    vkl = (pv >> 16) & 0xFFFF;
-  }
   int acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -647,12 +675,12 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t p = warp + 8 * i;
-    if (p >= pairs) continue;
+    if (p >= pairs || (p % n8) * 8 >= nk) continue;
     const uint32_t blk = p / n8, ns = p % n8;
     const uint8_t* a_row0 = As + (blk * 16 + g) * bts;
     const uint8_t* a_row8 = a_row0 + 8 * bts;
     const uint8_t* b_col = Bt + (ns * 8 + g) * bts;
-    for (uint32_t ks = 0; ks < kc32; ks += 32) {
+    for (uint32_t ks = 0; ks < kr; ks += 32) {
       const uint32_t a0 = *reinterpret_cast<const uint32_t*>(a_row0 + ks + q * 4);
       const uint32_t a1 = *reinterpret_cast<const uint32_t*>(a_row8 + ks + q * 4);
       const uint32_t a2 = *reinterpret_cast<const uint32_t*>(a_row0 + ks + 16 + q * 4);
@@ -684,7 +712,7 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
     if (p >= pairs) continue;
     const uint32_t blk = p / n8, ns = p % n8;
     const uint32_t col = ns * 8 + q * 2;
-    if (col >= N) continue;
+    if (col >= nk) continue;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint64_t row = blk * 16 + g + 8 * h;
@@ -720,9 +748,10 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
     float* rb = rows + warp * N;
     uint32_t* pw = pws + warp * (3 * kPwMaxLeaves);
     for (uint32_t r = warp; r < M; r += kWarps) {
-      for (uint32_t j = lane; j < N; j += 32) rb[j] = h2f(Sc[r * N + j]);
-      __syncwarp();
       const int64_t lt = int64_t(r) + qrb < int64_t(vkl) - 1 ? int64_t(r) + qrb : int64_t(vkl) - 1;
+      const uint32_t nr = masked ? (lt < 0 ? 0u : min(N, uint32_t(lt) + 1)) : N;   // columns the row reads
+      for (uint32_t j = lane; j < nr; j += 32) rb[j] = h2f(Sc[r * N + j]);
+      __syncwarp();
       softmax_row_f16(rb, N, masked, masked ? lt : int64_t(N) - 1, out ? out + uint64_t(r) * N : nullptr, pw, lane,
                       qout ? qout + uint64_t(r) * qstride : nullptr, qs);
       if (qout)   // the A row's padding columns N .. (N rounded up to 32) are zero
@@ -731,6 +760,7 @@ __device__ __noinline__ void op_matmul_wide(const ExecArgs& A, const DevOp& op, 
       __syncwarp();
     }
   }
+  return nk;
 }
 
 // ---------------------------------------------------------------------------------
@@ -1798,10 +1828,10 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_MATMUL:
       if (op.flags & F_TC) op_matmul_tc(A, op, t, smem, tc, t.op);
       else if (op.flags & F_WIDE) {
-        op_matmul_wide(A, op, t, smem, false, false);
-        if (op.flags2 & FX_PV) {   // the P.V op, its A tile written by the softmax above
+        const uint32_t nk = op_matmul_wide(A, op, t, smem, false, false);
+        if (op.flags2 & FX_PV) {   // the P.V op, its A tile written by the softmax above (zero past nk)
           hsync();
-          op_matmul_wide(A, A.ops[op.seg0], t, smem, true, (op.flags2 & FX_PVPF) != 0);
+          op_matmul_wide(A, A.ops[op.seg0], t, smem, true, (op.flags2 & FX_PVPF) != 0, nk);
         }
       }
       else op_matmul(A, op, t, smem);

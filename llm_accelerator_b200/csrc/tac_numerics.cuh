@@ -166,7 +166,10 @@ template <class Get>
 __device__ inline float warp_pairwise_sum(const Get& get, uint32_t n, uint32_t* scratch);
 
 __device__ __forceinline__ float warp_pairwise_sum_smem(const float* x, uint32_t n, uint32_t* scratch,
-                                                        bool sq = false, float mean = 0.f) {
+                                                        bool sq = false, float mean = 0.f,
+                                                        uint32_t nz = 0xFFFFFFFFu) {
+  // nz (plain sums of non-negative values only): x[nz..n) are +0; adding +0
+  // leaves every partial sum as it is, so a leaf stops at nz
   uint32_t bnl, bL;
   if (pw_balanced(n, bnl, bL)) {
     const uint32_t lane = threadIdx.x & 31, leaf = lane >> 2, p = lane & 3;
@@ -186,7 +189,8 @@ __device__ __forceinline__ float warp_pairwise_sum_smem(const float* x, uint32_t
       } else {
         r0 = q[0];
         r1 = q[1];
-        for (uint32_t i = 8; i < bL; i += 8) {
+        const uint32_t base = leaf * bL + 2 * p;
+        for (uint32_t i = 8; i < bL && base + i < nz; i += 8) {
           r0 = __fadd_rn(r0, q[i]);
           r1 = __fadd_rn(r1, q[i + 1]);
         }

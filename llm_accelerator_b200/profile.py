@@ -1,10 +1,11 @@
 """Device-side profile of compiled decode steps (per level and per task).
 
     python -m llm_accelerator_b200.profile [--recipe tests/golden/recipe_gpt2_medium.npz]
-                                           [--batch 64] [--steps 3] [--mhz 1965]
+                                           [--batch 64] [--steps 3] [--position 130] [--mhz 1965]
 
-Runs a prefill and two warm-up decode steps of a GPT-2 recipe through
-BatchedRunner, then profiles --steps decode steps with the engine's profiling
+Runs a prefill and teacher-forced decode steps of a GPT-2 recipe through
+BatchedRunner up to --position (the bench's timed steps follow a 128-token
+prompt), then profiles --steps decode steps with the engine's profiling
 mode 2: the device time at the end of every plan level (globaltimer) and the
 SM cycles of every task.  Prints, per op kind and shape, the task count, the
 median and 90th-percentile task time, and the task time summed over all
@@ -50,21 +51,23 @@ def op_label(op) -> str:
     return k
 
 
-def profile_decode(recipe: str, batch: int, steps: int = 3, device: int = 0):
+def profile_decode(recipe: str, batch: int, steps: int = 3, device: int = 0, position: int = 130):
     """(level_ns, task_cycles, ops, tasks, level_offsets, halves) of the decode
-    plan, medians over `steps` profiled decode steps."""
+    plan, medians over `steps` profiled decode steps at positions
+    position .. position + steps - 1 (earlier positions run unprofiled)."""
     from .recipe import load_recipe
     from .runner import BatchedRunner
     b = load_recipe(recipe)
     br = BatchedRunner(b, batch, device=device)
     toks = np.arange(batch) % 50257
     br.step("prefill", toks, np.zeros(batch, int))
-    for pos in (1, 2):
+    position = max(1, position)
+    for pos in range(1, position):
         br.step("decode", toks, np.full(batch, pos))
     br.engine.set_profiling(True, tasks=True)
     durs, cycs = [], []
     for i in range(steps):
-        br.step("decode", toks, np.full(batch, 3 + i))
+        br.step("decode", toks, np.full(batch, position + i))
         durs.append(np.diff(br.engine.read_profile().astype(np.int64)))
         cycs.append(br.engine.read_task_profile().astype(np.int64))
     br.engine.set_profiling(False)
@@ -101,10 +104,11 @@ def main(argv=None) -> None:
     ap.add_argument("--recipe", default=str(root / "tests" / "golden" / "recipe_gpt2_medium.npz"))
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--position", type=int, default=130, help="KV position of the first profiled step")
     ap.add_argument("--mhz", type=float, default=1965.0, help="SM clock that converts task cycles to time")
     ap.add_argument("--top", type=int, default=25)
     a = ap.parse_args(argv)
-    print(summarize(*profile_decode(a.recipe, a.batch, a.steps), mhz=a.mhz, top=a.top))
+    print(summarize(*profile_decode(a.recipe, a.batch, a.steps, position=a.position), mhz=a.mhz, top=a.top))
 
 
 if __name__ == "__main__":
