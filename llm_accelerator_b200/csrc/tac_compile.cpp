@@ -1922,7 +1922,20 @@ void Compiler::build_tasks() {
         break;
       default: {  // element-wise ops: ew_task_elems(kind) elements per task
         if (op.flags & F_SEGA) {   // segment-list operand: kSegTaskUnits operand units per task
-          per_seq(i, static_cast<uint32_t>(std::max<uint64_t>(1, (MN / 8 + kSegTaskUnits - 1) / kSegTaskUnits)));
+          const uint64_t units = MN / 8;
+          const uint32_t tiles = static_cast<uint32_t>(std::max<uint64_t>(1, (units + kSegTaskUnits - 1) / kSegTaskUnits));
+          for (uint32_t t = 0; t < tiles; ++t) {
+            // the segments holding the tile's units: first | count << 16 (segments are in operand order)
+            const uint64_t u0 = uint64_t(t) * kSegTaskUnits, u1 = std::min<uint64_t>(units, u0 + kSegTaskUnits);
+            uint32_t first = 0, last = 0;
+            for (uint32_t k = 0; k < op.nseg; ++k) {
+              const Segment& sg = P->segs[op.seg0 + k];
+              if (sg.dst + sg.n <= u0) first = k + 1;
+              if (sg.dst < u1) last = k;
+            }
+            const uint32_t aux = first | ((last - first + 1) << 16);
+            for (uint32_t s = 0; s < B; ++s) per_level[op.level].push_back(Task{i, s, 1, t, aux});
+          }
           break;
         }
         const uint64_t te = ew_task_elems(op.kind);

@@ -1329,23 +1329,28 @@ __device__ __noinline__ void op_elementwise(const ExecArgs& A, const DevOp& op, 
 constexpr uint32_t kSegTableOff = 4096;
 constexpr uint32_t kMaxQStage = 8192;   // MAX_ABS + QUANT: the reduced input, 16384 FP16 at most
 
-__device__ __forceinline__ void seg_stage(const ExecArgs& A, const DevOp& op, uint8_t* smem) {
+// A task whose units touch only part of the list names that part in
+// Task::aux (first segment | count << 16); aux 0 stands for the whole list.
+// Returns the number of segments staged.
+__device__ __forceinline__ uint32_t seg_stage(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
   uint32_t* ofs = reinterpret_cast<uint32_t*>(smem + kSegTableOff);
   uint64_t* src = reinterpret_cast<uint64_t*>(smem + kSegTableOff + kMaxSegRuns * 4);
-  for (uint32_t k = htid(); k < op.nseg; k += kThreads) {
-    const Segment sg = A.segs[op.seg0 + k];
+  const uint32_t first = t.aux ? (t.aux & 0xFFFFu) : 0u, count = t.aux ? (t.aux >> 16) : op.nseg;
+  for (uint32_t k = htid(); k < count; k += kThreads) {
+    const Segment sg = A.segs[op.seg0 + first + k];
     ofs[k] = static_cast<uint32_t>(sg.dst);
     src[k] = sg.src;
   }
   hsync();
+  return count;
 }
 
-// Address of operand unit u (segments staged by seg_stage).
-__device__ __forceinline__ const uint4* seg_unit(const ExecArgs& A, const DevOp& op, const uint8_t* smem,
+// Address of operand unit u (segments staged by seg_stage; nseg of them).
+__device__ __forceinline__ const uint4* seg_unit(const ExecArgs& A, uint32_t nseg, const uint8_t* smem,
                                                  uint32_t seq, uint32_t u) {
   const uint32_t* ofs = reinterpret_cast<const uint32_t*>(smem + kSegTableOff);
   const uint64_t* src = reinterpret_cast<const uint64_t*>(smem + kSegTableOff + kMaxSegRuns * 4);
-  uint32_t lo = 0, hi = op.nseg;   // last k with ofs[k] <= u
+  uint32_t lo = 0, hi = nseg;   // last k with ofs[k] <= u
   while (hi - lo > 1) {
     const uint32_t mid = (lo + hi) >> 1;
     if (ofs[mid] <= u) lo = mid;
@@ -1363,7 +1368,7 @@ __device__ __noinline__ void op_seg_ew(const ExecArgs& A, const DevOp& op, const
   // the register's raw bits load while the segment table is staged; they are
   // converted at their first use, after the operand loads are in flight
   const uint16_t s0b = op.kind == K_QUANT ? sreg_bits(A, op.s[0], seq) : uint16_t(0);
-  seg_stage(A, op, smem);
+  const uint32_t nseg = seg_stage(A, op, t, smem);
   const uint4* b = reinterpret_cast<const uint4*>(pptr(A, op.b, seq));
   uint8_t* d = pptr(A, op.d, seq);
   for (uint32_t u0 = u_begin + htid(); u0 < units; u0 += 4 * kThreads) {
@@ -1372,7 +1377,7 @@ __device__ __noinline__ void op_seg_ew(const ExecArgs& A, const DevOp& op, const
     for (uint32_t q = 0; q < 4; ++q) {
       const uint32_t u = u0 + q * kThreads;
       if (u < units) {
-        va[q] = __ldcg(seg_unit(A, op, smem, seq, u));
+        va[q] = __ldcg(seg_unit(A, nseg, smem, seq, u));
         if (op.kind == K_VADD_F16) vb[q] = __ldcg(b + u);
       }
     }
@@ -1415,13 +1420,13 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
   const bool seg = op.flags & F_SEGA;
   const bool maxq = (op.flags2 & FX_MAXQ) != 0;   // also QUANT's result (MN <= 16384)
   uint4* keep = reinterpret_cast<uint4*>(smem + kMaxQStage);   // the input, kept for the QUANT
-  if (seg) seg_stage(A, op, smem);
+  const uint32_t nseg = seg ? seg_stage(A, op, t, smem) : 0u;
   for (uint64_t g0 = htid(); g0 < ng; g0 += uint64_t(kThreads) * 8) {
     uint4 v[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const uint64_t g = g0 + uint64_t(k) * kThreads;
-      v[k] = g < ng ? __ldcg(seg ? seg_unit(A, op, smem, seq, uint32_t(g)) : xv + g) : make_uint4(0, 0, 0, 0);
+      v[k] = g < ng ? __ldcg(seg ? seg_unit(A, nseg, smem, seq, uint32_t(g)) : xv + g) : make_uint4(0, 0, 0, 0);
     }
     if (maxq) {
 #pragma unroll
@@ -1788,7 +1793,7 @@ __device__ __forceinline__ bool grid_barrier(const ExecArgs& A, uint32_t target,
     }
     ok = st == 0;
   } else if (htid() == 32 && next_level < A.n_levels) {
-    const uint32_t ti = A.level_off[next_level] + blockIdx.x * kHalves + hidx();
+    const uint32_t ti = A.level_off[next_level] + hidx() * gridDim.x + blockIdx.x;
     if (ti < A.level_off[next_level + 1]) {
       const Task tn = A.tasks[ti];
       prefetch_l1(A.ops + tn.op);
@@ -1914,7 +1919,8 @@ __global__ void __launch_bounds__(kCtaThreads, 1) exec_kernel(const __grid_const
     for (int h = 1; h < kHalves; ++h) tcs[h].tmem = tcs[0].tmem + h * kTcCols;   // column offset
   __syncthreads();
   if (A.prof && blockIdx.x == 0 && threadIdx.x == 0) A.prof[0] = global_ns();
-  const uint32_t vid = blockIdx.x * kHalves + hidx(), vgrid = gridDim.x * kHalves;
+  // half-major: a level's first gridDim.x tasks take one half of every SM
+  const uint32_t vid = hidx() * gridDim.x + blockIdx.x, vgrid = gridDim.x * kHalves;
   for (uint32_t L = 0; L < A.n_levels; ++L) {
     const uint32_t t0 = A.level_off[L], t1 = A.level_off[L + 1];
     for (uint32_t ti = t0 + vid; ti < t1; ti += vgrid) {

@@ -405,3 +405,31 @@ def test_running_fp16_sum_becomes_one_chain_op(shape, parts, produced, commute, 
     st = orc.state
     assert f["abuf"] == bytes(st.abuf) and f["wbuf"] == bytes(st.wbuf)
     assert f["dram"] == bytes(st.dram[:len(f["dram"])])
+
+
+def test_segment_list_tasks_name_the_segments_they_read():
+    """A segment-list element-wise task covers 512 operand units and stages
+    only the segments holding them (Task.aux = first | count << 16); together
+    those segments cover the task's units and nothing outside one segment on
+    either side."""
+    from llm_accelerator_b200.recipe import load_recipe
+    b = load_recipe(GOLDEN / "recipe_gpt2_small.npz")
+    p = compile_program(2, 1 << 30, b.temp_base // 16 * 16, bytes(b.instruction_region()), b.decode_pc,
+                        10_000_000, L.Regs(), True, _sites(b, "decode"))
+    ops, segs, tasks, lv = p.dump()
+    seen = 0
+    for t in tasks:
+        op = ops[int(t["op"])]
+        if not int(op["flags"]) & 32 or int(op["kind"]) == PE.K["MAX_ABS"]:
+            continue
+        units = int(op["M"]) * int(op["N"]) // 8
+        u0 = int(t["tile"]) * 512
+        u1 = min(units, u0 + 512)
+        first, count = int(t["aux"]) & 0xFFFF, int(t["aux"]) >> 16
+        assert count >= 1 and first + count <= int(op["nseg"])
+        sl = segs[int(op["seg0"]) + first:int(op["seg0"]) + first + count]
+        assert int(sl[0]["dst"]) <= u0 < int(sl[0]["dst"]) + int(sl[0]["n"])
+        assert int(sl[-1]["dst"]) < u1 <= int(sl[-1]["dst"]) + int(sl[-1]["n"])
+        assert all(int(a["dst"]) + int(a["n"]) == int(c["dst"]) for a, c in zip(sl[:-1], sl[1:]))
+        seen += 1
+    assert seen > 0
