@@ -509,6 +509,21 @@ __device__ __forceinline__ void softmax_row_f16(float* rowbuf, uint32_t n, bool 
   }
 }
 
+constexpr int kTcStages = 3;                            // stage slots (64-column tasks use 3, 128-column 2)
+
+// Per-half state of the TMA / tcgen05 stages and of the bulk-copy stage
+// barrier: mbarriers, the half's TMEM columns and the next phase parities.
+struct TcShared {
+  uint64_t full[kTcStages];    // TMA bytes of a stage landed
+  uint64_t empty[kTcStages];   // the MMAs reading a stage completed
+  uint64_t stage;              // bulk-copied element-wise operands landed
+  uint32_t tmem;
+  uint32_t phase_full;         // bit s: parity of the next phase of full[s]
+  uint32_t phase_empty;
+  uint32_t phase_stage;        // parity of the next phase of `stage`
+  uint32_t pv_phase;           // FX_PVPF: parity of the `stage` phase that brings V
+};
+
 // ---------------------------------------------------------------------------------
 // MATMUL with per-sequence operands in the wide shape (F_WIDE: M <= 32,
 // K <= 256, N <= 256, shared memory by wide_mm_smem): one task computes every
@@ -522,7 +537,8 @@ __device__ __forceinline__ void softmax_row_f16(float* rowbuf, uint32_t n, bool 
 // wrote it there); b_staged: so are the FP16 B copies (FX_PVPF).
 // ---------------------------------------------------------------------------------
 __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
-                                                bool a_staged, bool b_staged, uint32_t k_used = 0xFFFFFFFFu) {
+                                                TcShared* tc, bool a_staged, bool b_staged,
+                                                uint32_t k_used = 0xFFFFFFFFu) {
   const uint32_t M = op.M, N = op.N, K = op.K, seq = t.seq0;
   const uint32_t kc32 = (K + 31) & ~31u;
   // K rows that can be nonzero in A (the P.V op: P is zero past the QK^T
@@ -543,9 +559,25 @@ __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& 
   const uint8_t* Ag = pptr(A, op.a, seq);
   const uint8_t* Bg = pptr(A, op.b, seq);
   const uint32_t kv = kc32 / 16;                    // 16-byte vectors per padded row
-  if (qa) {
-    for (uint32_t i = htid(); i < M * K / 8; i += kThreads) cp_async16(Ah + i * 16, Ag + uint64_t(i) * 16, 16u);
-  } else if (!a_staged) {
+  // the contiguous operands (FP16 A and B, quantised on load, and the F_DQ
+  // scale row) arrive by bulk copies that one thread issues on the half's
+  // stage barrier; padded int8 tiles take 16-byte copies per thread
+  const bool bulk_b = qb && !b_staged, bulk_pc = dq && !b_staged;
+  const uint32_t bulk_bytes = (qa ? M * K * 2 : 0u) + (bulk_b ? K * N * 2 : 0u) + (bulk_pc ? N * 2 : 0u);
+  uint32_t par = 0;
+  if (bulk_bytes) {
+    par = tc->phase_stage;
+    hsync();   // every thread has the parity before it flips
+    if (htid() == 0) {
+      tc->phase_stage = par ^ 1u;
+      sm100::fence_proxy_async();
+      sm100::mbar_arrive_expect_tx(&tc->stage, bulk_bytes);
+      if (qa) sm100::bulk_g2s(Ah, Ag, M * K * 2, &tc->stage);
+      if (bulk_b) sm100::bulk_g2s(Bh, Bg, K * N * 2, &tc->stage);
+      if (bulk_pc) sm100::bulk_g2s(Pc, pptr(A, op.c, seq), N * 2, &tc->stage);
+    }
+  }
+  if (!qa && !a_staged) {
     for (uint32_t i = htid(); i < nblocks * 16 * kv; i += kThreads) {
       const uint32_t r = i / kv, v = i % kv;
       const bool in = r < M && v * 16 < K;
@@ -553,8 +585,7 @@ __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& 
     }
   }
   if (qb) {
-    if (!b_staged)
-      for (uint32_t i = htid(); i < K * N / 8; i += kThreads) cp_async16(Bh + i * 16, Bg + uint64_t(i) * 16, 16u);
+    // bulk copy above, or already staged
   } else if (bt) {
     for (uint32_t i = htid(); i < n8 * 8 * kv; i += kThreads) {
       const uint32_t n = i / kv, v = i % kv;
@@ -569,7 +600,7 @@ __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& 
       cp_async16(Braw + k * N + v * 16, Bg + (in ? uint64_t(k) * N + v * 16 : 0), in ? 16u : 0u);
     }
   }
-  if (dq) {
+  if (dq && !bulk_pc) {
     const uint8_t* pg = pptr(A, op.c, seq);
     for (uint32_t i = htid(); i < N / 8; i += kThreads) cp_async16(Pc + i * 16, pg + uint64_t(i) * 16, 16u);
   }
@@ -594,6 +625,13 @@ __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& 
     nk = lmax < 0 ? 0u : min(N, (uint32_t(lmax) + 8) & ~7u);
   }
   cp_async_wait<0>();
+  // the bulk copies of this op, then (FX_PVPF) V, issued by its QK^T op
+  const bool bulk_ok = !bulk_bytes || sm100::mbar_wait(&tc->stage, par, nullptr, 0);
+  if (!bulk_ok || (b_staged && !sm100::mbar_wait(&tc->stage, tc->pv_phase, nullptr, 0))) {
+    sm100::mbar_wait(&tc->stage, bulk_ok ? tc->pv_phase : par, nullptr, 0);   // bounded: let copies land
+    if (htid() == 0) raise_fault(A, DF_STAGE_TIMEOUT, t.op, seq);
+    return 0xFFFFFFFFu;
+  }
   hsync();
   if (qa) {
     // QUANT's rule into the padded A rows; padding rows and columns are zero
@@ -657,12 +695,17 @@ __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& 
     }
     hsync();
   }
-  if (op.flags2 & FX_PVPF) {   // V for the P.V op: in flight while this op multiplies and takes the softmax
+  if ((op.flags2 & FX_PVPF) && htid() == 0) {
+    // V for the P.V op, one bulk copy in flight while this op multiplies and
+    // takes the softmax; its region was last read before the barrier above
     const DevOp& y = A.ops[op.seg0];
-    uint8_t* vs = smem + wide_mm_bh_off(y.M, y.N, y.K, (y.flags & F_BT) != 0);
-    const uint8_t* vg = pptr(A, y.b, seq);
-    for (uint32_t i = htid(); i < y.K * y.N / 8; i += kThreads) cp_async16(vs + i * 16, vg + uint64_t(i) * 16, 16u);
-    cp_async_commit();
+    const uint32_t vpar = tc->phase_stage;
+    tc->pv_phase = vpar;
+    tc->phase_stage = vpar ^ 1u;
+    sm100::fence_proxy_async();
+    sm100::mbar_arrive_expect_tx(&tc->stage, y.K * y.N * 2);
+    sm100::bulk_g2s(smem + wide_mm_bh_off(y.M, y.N, y.K, (y.flags & F_BT) != 0), pptr(A, y.b, seq),
+                    y.K * y.N * 2, &tc->stage);
   }
   const int warp = htid() >> 5, lane = htid() & 31;
   const int g = lane >> 2, q = lane & 3;
@@ -774,7 +817,6 @@ __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& 
 // that read it have committed.  The eight warps read the int32 accumulator
 // back with tcgen05.ld.  Waits are bounded (DF_MMA_TIMEOUT).
 // ---------------------------------------------------------------------------------
-constexpr int kTcStages = 3;                            // stage slots (64-column tasks use 3, 128-column 2)
 constexpr uint32_t kTcAStage = 128 * 128;
 constexpr uint32_t kTcBStage = 128 * 64;                // 64 columns x 128 K rows
 constexpr uint32_t kTcStage = kTcAStage + kTcBStage;    // a multiple of 1024
@@ -784,15 +826,6 @@ constexpr uint32_t kTcIdesc = sm100::idesc_i8(128, 64, 1);
 constexpr uint32_t kTcIdesc128 = sm100::idesc_i8(128, 128, 1);
 
 
-struct TcShared {
-  uint64_t full[kTcStages];    // TMA bytes of a stage landed
-  uint64_t empty[kTcStages];   // the MMAs reading a stage completed
-  uint64_t stage;              // bulk-copied element-wise operands landed
-  uint32_t tmem;
-  uint32_t phase_full;         // bit s: parity of the next phase of full[s]
-  uint32_t phase_empty;
-  uint32_t phase_stage;        // parity of the next phase of `stage`
-};
 
 // shared-memory descriptor, 64-byte swizzle (layout type 4)
 __device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -1833,10 +1866,10 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_MATMUL:
       if (op.flags & F_TC) op_matmul_tc(A, op, t, smem, tc, t.op);
       else if (op.flags & F_WIDE) {
-        const uint32_t nk = op_matmul_wide(A, op, t, smem, false, false);
-        if (op.flags2 & FX_PV) {   // the P.V op, its A tile written by the softmax above (zero past nk)
+        const uint32_t nk = op_matmul_wide(A, op, t, smem, tc, false, false);
+        if ((op.flags2 & FX_PV) && nk != 0xFFFFFFFFu) {   // the P.V op, its A tile from the softmax above
           hsync();
-          op_matmul_wide(A, A.ops[op.seg0], t, smem, true, (op.flags2 & FX_PVPF) != 0, nk);
+          op_matmul_wide(A, A.ops[op.seg0], t, smem, tc, true, (op.flags2 & FX_PVPF) != 0, nk);
         }
       }
       else op_matmul(A, op, t, smem);
