@@ -196,6 +196,23 @@ int tac_encode_params(const tac_program* p, int batch, const uint64_t* var_words
 int tac_run_async_params(tac_engine* e, tac_program* p, const uint64_t* params_dev, void* stream,
                          tac_fault* fault);
 
+/* Runtime words as affine functions of a sequence's token and position, so a
+ * runner need not build the words every step (the values HostRunner patches,
+ * host_runner.py:51-62; no reference counterpart as an entry point).  One
+ * entry per runtime site, in site order: a SET_ADDR pair holds
+ * base + token * tok_mul + position * pos_mul; a CONFIG_ATTN word holds
+ * query_row_base = position, valid_kv_len = position + 1 and mode (the other
+ * arrays' entries are ignored).  tac_encode_params_tp gives exactly what
+ * tac_encode_params gives for the words those formulas produce, faults
+ * included (TAC_E_RECOMPILE outside the compiled ranges); tac_run_async_tp is
+ * tac_run_async fed that way.  tokens, positions: int64[batch]. */
+int tac_program_set_var_formula(tac_program* p, uint32_t n_sites, const uint64_t* base, const uint64_t* tok_mul,
+                                const uint64_t* pos_mul, const uint32_t* mode);
+int tac_encode_params_tp(const tac_program* p, int batch, const int64_t* tokens, const int64_t* positions,
+                         uint64_t* params_out, tac_fault* fault);
+int tac_run_async_tp(tac_engine* e, tac_program* p, const int64_t* tokens, const int64_t* positions, void* stream,
+                     tac_fault* fault);
+
 /* Greedy decode helpers for batched generation (HostRunner._greedy_token,
  * host_runner.py:97-101): argmax over `count` FP16 values at DRAM address
  * `addr` of every sequence, written to out_tokens (device int32[batch]).

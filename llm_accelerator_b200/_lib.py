@@ -79,6 +79,9 @@ SIGNATURES = {
     "tac_program_attn_key_cols": (C.c_uint32, [_P]),
     "tac_encode_params": (_I, [_P, _I, _P, _P, C.POINTER(Fault)]),
     "tac_run_async_params": (_I, [_P, _P, _P, _P, C.POINTER(Fault)]),
+    "tac_program_set_var_formula": (_I, [_P, C.c_uint32, _P, _P, _P, _P]),
+    "tac_encode_params_tp": (_I, [_P, _I, _P, _P, _P, C.POINTER(Fault)]),
+    "tac_run_async_tp": (_I, [_P, _P, _P, _P, _P, C.POINTER(Fault)]),
     "tac_argmax_f16": (_I, [_P, _U64, _U64, _P, _P]),
     "tac_set_profiling": (_I, [_P, _I]),
     "tac_read_profile": (_I, [_P, _P, C.c_uint32, _P]),

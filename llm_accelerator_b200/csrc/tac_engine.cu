@@ -173,6 +173,8 @@ uint32_t insn_bits(uint64_t w, int shift, int width) { return static_cast<uint32
 
 // Decodes one sequence's runtime words into parameters and checks them
 // against the ranges the plan was compiled for.
+int check_params(const tac_program* p, const uint64_t* params, tac_fault* f);
+
 int decode_params(const tac_program* p, const uint64_t* words, uint64_t* params, tac_fault* f) {
   for (size_t i = 0; i < p->vars.size(); ++i) {
     const VarInfo& v = p->vars[i];
@@ -190,6 +192,31 @@ int decode_params(const tac_program* p, const uint64_t* words, uint64_t* params,
                   (uint64_t(insn_bits(w, 33, 2)) << 32);
     }
   }
+  return check_params(p, params, f);
+}
+
+// The parameters the runtime words of one sequence would decode to, from its
+// token and position through the program's site formulas: the same values,
+// and the same faults, as encoding the words (SET_ADDR_LO/HI carry 28 bits
+// each; CONFIG_ATTN's fields are 12 bits, and a wider value reaches the
+// opcode bits of the word).
+int formula_params(const tac_program* p, int64_t token, int64_t position, uint64_t* params, tac_fault* f) {
+  const uint64_t tok = static_cast<uint64_t>(token), pos = static_cast<uint64_t>(position);
+  for (size_t i = 0; i < p->vars.size(); ++i) {
+    const VarInfo& v = p->vars[i];
+    const VarFormula& fm = p->formula[i];
+    if (v.kind == 0) {
+      params[i] = (fm.base + tok * fm.tok_mul + pos * fm.pos_mul) & ((1ull << 56) - 1);
+    } else {
+      if ((pos << 47) >> 59 || ((pos + 1) << 35) >> 59)
+        return set_fault(f, TAC_E_RECOMPILE, "runtime CONFIG_ATTN word changed its form", v.lo_pc);
+      params[i] = (pos & 0xFFF) | (((pos + 1) & 0xFFF) << 16) | (uint64_t(fm.mode & 3) << 32);
+    }
+  }
+  return check_params(p, params, f);
+}
+
+int check_params(const tac_program* p, const uint64_t* params, tac_fault* f) {
   for (const RtCheck& c : p->checks) {
     const uint64_t v = params[c.param];
     bool ok = true;
@@ -452,15 +479,41 @@ int tac_encode_params(const tac_program* p, int batch, const uint64_t* var_words
   return TAC_OK;
 }
 
+int tac_program_set_var_formula(tac_program* p, uint32_t n_vars, const uint64_t* base, const uint64_t* tok_mul,
+                                const uint64_t* pos_mul, const uint32_t* mode) {
+  if (!p || n_vars != p->vars.size() || (n_vars && (!base || !tok_mul || !pos_mul || !mode))) return TAC_E_ARGUMENT;
+  p->formula.resize(n_vars);
+  for (uint32_t i = 0; i < n_vars; ++i) p->formula[i] = VarFormula{base[i], tok_mul[i], pos_mul[i], mode[i]};
+  return TAC_OK;
+}
+
+int tac_encode_params_tp(const tac_program* p, int batch, const int64_t* tokens, const int64_t* positions,
+                         uint64_t* out, tac_fault* f) {
+  if (!p || !out || batch <= 0 || !tokens || !positions) return set_fault(f, TAC_E_ARGUMENT, "bad arguments");
+  if (p->formula.size() != p->vars.size()) return set_fault(f, TAC_E_ARGUMENT, "no site formulas set");
+  const uint32_t np = std::max<uint32_t>(p->n_params, 1);
+  std::memset(out, 0, sizeof(uint64_t) * np * batch);
+  for (int s = 0; s < batch && p->n_params; ++s) {
+    if (int r = formula_params(p, tokens[s], positions[s], out + size_t(s) * np, f)) {
+      if (f) f->buf_id = s;
+      return r;
+    }
+  }
+  return TAC_OK;
+}
+
 int tac_run_async_params(tac_engine* e, tac_program* p, const uint64_t* params_dev, void* stream, tac_fault* f) {
   if (int s = prepare(e, p, f)) return s;
   if (p->n_params && !params_dev) return set_fault(f, TAC_E_ARGUMENT, "missing parameters");
   return launch(e, p, p->n_params ? params_dev : reinterpret_cast<const uint64_t*>(e->d_status + 8), static_cast<cudaStream_t>(stream), f);
 }
 
-int tac_run_async(tac_engine* e, tac_program* p, const uint64_t* var_words, void* stream, tac_fault* f) {
-  if (int s = prepare(e, p, f)) return s;
-  if (p->n_var_words && !var_words) return set_fault(f, TAC_E_ARGUMENT, "missing runtime words");
+// Shared body of tac_run_async and tac_run_async_tp: the parameters are
+// encoded into the next slot of the pinned staging ring (from runtime words,
+// or from tokens and positions when `tokens` is set), uploaded on the stream
+// and the step launched.
+static int run_staged(tac_engine* e, tac_program* p, const uint64_t* var_words, const int64_t* tokens,
+                      const int64_t* positions, void* stream, tac_fault* f) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint32_t np = std::max<uint32_t>(p->n_params, 1);
   const size_t n = size_t(np) * e->batch;
@@ -483,11 +536,26 @@ int tac_run_async(tac_engine* e, tac_program* p, const uint64_t* var_words, void
   if (e->ring_used[slot]) CK(cudaEventSynchronize(e->ring_ev[slot]), f, "staging slot");
   uint64_t* h = e->h_pinned + size_t(slot) * e->pinned_cap;
   uint64_t* d = e->d_params + size_t(slot) * e->params_cap;
-  if (int r = tac_encode_params(p, e->batch, var_words, h, f)) return r;
+  if (int r = tokens ? tac_encode_params_tp(p, e->batch, tokens, positions, h, f)
+                     : tac_encode_params(p, e->batch, var_words, h, f))
+    return r;
   CK(cudaMemcpyAsync(d, h, n * 8, cudaMemcpyHostToDevice, st), f, "upload params");
   CK(cudaEventRecord(e->ring_ev[slot], st), f, "record staging event");
   e->ring_used[slot] = true;
   return launch(e, p, d, st, f);
+}
+
+int tac_run_async(tac_engine* e, tac_program* p, const uint64_t* var_words, void* stream, tac_fault* f) {
+  if (int s = prepare(e, p, f)) return s;
+  if (p->n_var_words && !var_words) return set_fault(f, TAC_E_ARGUMENT, "missing runtime words");
+  return run_staged(e, p, var_words, nullptr, nullptr, stream, f);
+}
+
+int tac_run_async_tp(tac_engine* e, tac_program* p, const int64_t* tokens, const int64_t* positions, void* stream,
+                     tac_fault* f) {
+  if (int s = prepare(e, p, f)) return s;
+  if (!tokens || !positions) return set_fault(f, TAC_E_ARGUMENT, "missing tokens or positions");
+  return run_staged(e, p, nullptr, tokens, positions, stream, f);
 }
 
 int tac_check_device_status(tac_engine* e, tac_fault* f) {

@@ -21,6 +21,16 @@ struct VarInfo {
   uint64_t base_lo, base_hi;  // compile-time words (opcode / register must not change)
 };
 
+// A runtime site's value as an affine function of a sequence's token and
+// position (set by the runner; HostRunner's patches, host_runner.py:51-62):
+// a SET_ADDR pair holds base + token * tok_mul + position * pos_mul; a
+// CONFIG_ATTN word holds query_row_base = position, valid_kv_len =
+// position + 1 and the site's mode.
+struct VarFormula {
+  uint64_t base = 0, tok_mul = 0, pos_mul = 0;
+  uint32_t mode = 0;
+};
+
 // A condition on runtime parameters that the compiler could not decide.
 enum CheckKind : uint32_t {
   CHK_ADDR = 1,        // param + dconst is 16-byte aligned; the nbytes there lie in [lo, hi)
@@ -49,6 +59,7 @@ struct tac_program {
   std::vector<tac::Task> tasks;
   std::vector<uint32_t> level_off;
   std::vector<tac::VarInfo> vars;
+  std::vector<tac::VarFormula> formula;  // per var, when the runner set one
   std::vector<tac::RtCheck> checks;
   uint32_t n_var_words = 0;
   uint32_t n_params = 0;

@@ -51,6 +51,16 @@ class Program:
         """Fewest key columns of a runtime-configured masked softmax (0 if none)."""
         return int(_lib.tac_program_attn_key_cols(self.handle))
 
+    def set_var_formula(self, base, tok_mul, pos_mul, mode) -> None:
+        """Per runtime site (site order): an address site holds base + token *
+        tok_mul + position * pos_mul; an attention site the position's context
+        with `mode` (see tac_program_set_var_formula)."""
+        arrs = [np.ascontiguousarray(np.asarray(a, dtype=np.uint64)) for a in (base, tok_mul, pos_mul)]
+        md = np.ascontiguousarray(np.asarray(mode, dtype=np.uint32))
+        n = len(md)
+        L.check(_lib.tac_program_set_var_formula(self.handle, n, *(a.ctypes.data for a in arrs), md.ctypes.data),
+                "tac_program_set_var_formula")
+
     def dump(self):
         """(ops, segments, tasks, level_offsets) as numpy structured arrays."""
         i = self.info
@@ -188,6 +198,29 @@ class Engine:
         if st != L.OK:
             raise L.fault_to_exception(f, st)
         return out
+
+    def encode_params_tp(self, prog: Program, tokens, positions) -> np.ndarray:
+        """encode_params for the words the program's site formulas give
+        (Program.set_var_formula) for these tokens and positions."""
+        n = int(_lib.tac_program_param_count(prog.handle))
+        out = np.zeros((self.batch, n), np.uint64)
+        tok = np.ascontiguousarray(np.asarray(tokens, dtype=np.int64).reshape(self.batch))
+        pos = np.ascontiguousarray(np.asarray(positions, dtype=np.int64).reshape(self.batch))
+        f = L.Fault()
+        st = _lib.tac_encode_params_tp(prog.handle, self.batch, tok.ctypes.data, pos.ctypes.data, out.ctypes.data,
+                                       C.byref(f))
+        if st != L.OK:
+            raise L.fault_to_exception(f, st)
+        return out
+
+    def run_async_tp(self, prog: Program, tokens, positions, stream=None) -> None:
+        """run_async with the runtime words given by the site formulas."""
+        tok = np.ascontiguousarray(np.asarray(tokens, dtype=np.int64).reshape(self.batch))
+        pos = np.ascontiguousarray(np.asarray(positions, dtype=np.int64).reshape(self.batch))
+        f = L.Fault()
+        st = _lib.tac_run_async_tp(self.handle, prog.handle, tok.ctypes.data, pos.ctypes.data, stream, C.byref(f))
+        if st != L.OK and not (prog.info.faulted and st == prog.fault.status):
+            raise L.fault_to_exception(f, st)
 
     def run_async_params(self, prog: Program, params_dev_ptr: int, stream=None) -> None:
         """Runs with a parameter block already in device memory."""

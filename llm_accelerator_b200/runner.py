@@ -188,6 +188,7 @@ class BatchedRunner:
             self.plans[name] = compile_program(self.batch, self.dram_bytes, self.shared_bytes, masked, entry,
                                                10_000_000, L.Regs(), True, sites, live=live,
                                                sram_live=sram_live, sregs_live=sregs_live)
+            self.plans[name].set_var_formula(*self.var_formula(name))
 
     # ---- runtime words ------------------------------------------------------------------
     def _var_layout(self, name: str):
@@ -219,6 +220,23 @@ class BatchedRunner:
                    t_mode=u(t_mode) << np.uint64(33), n=col)
         cache[name] = lay
         return lay
+
+    def var_formula(self, name: str):
+        """(base, tok_mul, pos_mul, mode) of every runtime site of a stream, in
+        site order: the affine form var_words evaluates, for the engine's
+        token / position path (Engine.run_async_tp)."""
+        b = self.bundle
+        row, kv = int(b.embedding_row_bytes), int(b.kv_step_bytes)
+        out = ([], [], [], [])
+        for (kind, s) in self._sites[name][1]:
+            if kind == "addr":
+                vals = (b.symbol_address(s.base_symbol), row if s.kind == "token_embed" else 0,
+                        row if s.kind == "pos_embed" else (0 if s.kind == "token_embed" else kv), 0)
+            else:
+                vals = (0, 0, 0, s.mode)
+            for lst, v in zip(out, vals):
+                lst.append(v)
+        return out
 
     def var_words(self, name: str, tokens: Sequence[int], positions: Sequence[int]) -> np.ndarray:
         """[batch, n_var_words] runtime words for one step of every sequence:
@@ -254,7 +272,10 @@ class BatchedRunner:
         self.engine.argmax_f16(self.logits_offset(name), vocab, out_dev_ptr, stream)
 
     def step_async(self, name: str, tokens, positions, stream=None) -> None:
-        self.engine.run_async(self.plans[name], self.var_words(name, tokens, positions), stream)
+        """One step, its runtime parameters computed from tokens and positions
+        on the host without building the instruction words (the same values
+        and checks as var_words + Engine.run_async)."""
+        self.engine.run_async_tp(self.plans[name], tokens, positions, stream)
 
     def step(self, name: str, tokens, positions) -> None:
         st = self.engine.run(self.plans[name], self.var_words(name, tokens, positions))

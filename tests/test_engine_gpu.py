@@ -174,7 +174,11 @@ def test_engine_bundle_run_matches_reference(name):
     assert sim.state.cycle_count == int(gold["cycles"][0])
 
 
-def test_batched_runner_matches_single_sequence_runs():
+@pytest.mark.parametrize("path", ["words", "formulas"])
+def test_batched_runner_matches_single_sequence_runs(path):
+    """BatchedRunner.step (runtime words) and step_async (parameters from
+    tokens and positions through the site formulas) both reproduce
+    single-sequence runs bit for bit."""
     from llm_accelerator_b200.runner import BatchedRunner, HostRunner
     b = load_bundle("tiny_l2_d128")
     B, steps, vocab = 4, 6, 512
@@ -184,7 +188,11 @@ def test_batched_runner_matches_single_sequence_runs():
     batched = []
     for pos in range(steps):
         name = "prefill" if pos == 0 else "decode"
-        br.step(name, prompts[:, pos], np.full(B, pos))
+        if path == "words":
+            br.step(name, prompts[:, pos], np.full(B, pos))
+        else:
+            br.step_async(name, prompts[:, pos], np.full(B, pos))
+            br.engine.check_device()
         batched.append(np.stack([br.logits(name, s) for s in range(B)]))
     batched = np.stack(batched, axis=1)   # [B, steps, vocab_pad]
     for s in range(B):

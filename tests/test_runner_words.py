@@ -66,3 +66,47 @@ def test_var_words_match_patched_instruction_words(name, stream):
             pcs = (site.lo_pc, site.hi_pc) if site.kind == 0 else (site.lo_pc,)
             want += [isa.word_of(region[pc * 8:pc * 8 + 8]) for pc in pcs]
         assert got[i].tolist() == want
+
+
+@pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
+@pytest.mark.parametrize("stream", ["prefill", "decode"])
+def test_site_formulas_give_the_words_parameters(name, stream):
+    """tac_encode_params_tp (the parameters from tokens and positions through
+    the runner's site formulas) equals tac_encode_params of the runner's
+    runtime words, values and faults alike: positions past the compiled KV
+    window return TAC_E_RECOMPILE from both."""
+    import ctypes as C
+    from llm_accelerator_b200 import _lib as L
+    from llm_accelerator_b200.engine import compile_program
+    b = load_bundle(name)
+    batch = 6
+    r = _runner(b, stream, batch)
+    sites = r._sites[stream][0]
+    entry = b.prefill_pc if stream == "prefill" else b.decode_pc
+    p = compile_program(batch, 16 << 20, b.temp_base // 16 * 16, bytes(b.instruction_region()), entry,
+                        10_000_000, L.Regs(), True, sites)
+    p.set_var_formula(*r.var_formula(stream))
+    n = int(L.lib.tac_program_param_count(p.handle))
+    rng = np.random.default_rng(5)
+    keys = p.attn_key_cols() or 1
+    seen = set()
+    # position 0; positions inside the KV window (a prefill stream compiles for
+    # position 0 only, so these recompile there); then tokens past the
+    # embedding table and positions past the window and CONFIG_ATTN's fields
+    for lo, hi, vocab in ((0, 1, 64), (0, keys, 64), (keys, 5000, 50257)):
+        tokens = rng.integers(0, vocab, batch).astype(np.int64)   # the tiny bundles embed 128 tokens
+        positions = rng.integers(lo, hi, batch).astype(np.int64)
+        words = r.var_words(stream, tokens, positions)
+        a, c = np.zeros((batch, max(n, 1)), np.uint64), np.zeros((batch, max(n, 1)), np.uint64)
+        fa, fc = L.Fault(), L.Fault()
+        sa = L.lib.tac_encode_params(p.handle, batch, words.ctypes.data, a.ctypes.data, C.byref(fa))
+        sc = L.lib.tac_encode_params_tp(p.handle, batch, tokens.ctypes.data, positions.ctypes.data, c.ctypes.data,
+                                        C.byref(fc))
+        assert sa == sc
+        assert fa.buf_id == fc.buf_id and fa.pc == fc.pc
+        if sa == L.OK:
+            assert np.array_equal(a, c)
+        else:
+            assert sa == L.E_RECOMPILE
+        seen.add(sa)
+    assert seen == {L.OK, L.E_RECOMPILE}
