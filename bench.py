@@ -31,6 +31,7 @@ import multiprocessing as mp
 import os
 import statistics
 import subprocess
+import tempfile
 import sys
 import time
 from pathlib import Path
@@ -196,8 +197,10 @@ class ClockSampler:
         self.p = None
 
     def __enter__(self):
-        self.out = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
-        self.out.parent.mkdir(exist_ok=True)
+        # samples go to $TAC_CLOCKS_DIR (kept) or a temporary directory
+        d = os.environ.get("TAC_CLOCKS_DIR") or tempfile.mkdtemp(prefix="tac_clocks_")
+        self.out = Path(d) / f"clocks_{os.getpid()}.csv"
+        self.out.parent.mkdir(parents=True, exist_ok=True)
         try:
             self.p = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"

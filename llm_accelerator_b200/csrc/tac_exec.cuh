@@ -524,6 +524,49 @@ struct TcShared {
   uint32_t pv_phase;           // FX_PVPF: parity of the `stage` phase that brings V
 };
 
+// Two softmax rows of one warp quantised for the P.V A tile only (rows in
+// rb0 / rb1 as floats, last visible columns last0 / last1, -1 for none): the
+// bytes two softmax_row_f16 calls with out == nullptr write, the two rows'
+// chains interleaved.
+__device__ __forceinline__ void softmax_rows2_q(float* rb0, float* rb1, uint32_t n, bool masked, int64_t last0,
+                                                int64_t last1, uint32_t* pw0, uint32_t* pw1, int lane, int8_t* q0,
+                                                int8_t* q1, float qs) {
+  const int64_t l0 = masked ? last0 : int64_t(n) - 1, l1 = masked ? last1 : int64_t(n) - 1;
+  float m0 = -INFINITY, m1 = -INFINITY;
+  for (uint32_t j = lane; j < n; j += 32) {
+    if (int64_t(j) <= l0) m0 = fmaxf(m0, rb0[j]);
+    if (int64_t(j) <= l1) m1 = fmaxf(m1, rb1[j]);
+  }
+  for (int o = 16; o; o >>= 1) {
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+  }
+  __syncwarp();
+  for (uint32_t j = lane; j < n; j += 32) {
+    rb0[j] = int64_t(j) <= l0 ? exp_f32(__fsub_rn(rb0[j], m0)) : 0.f;
+    rb1[j] = int64_t(j) <= l1 ? exp_f32(__fsub_rn(rb1[j], m1)) : 0.f;
+  }
+  __syncwarp();
+  float d0, d1;
+  warp_pairwise_sum2_smem(rb0, rb1, n, pw0, pw1, uint32_t(l0 + 1), uint32_t(l1 + 1), d0, d1);
+  for (uint32_t j0 = 0; j0 < n; j0 += 32) {
+    const uint32_t j = j0 + lane;
+    int8_t a = 0, b = 0;
+    if (int64_t(j0) <= l0 && int64_t(j) <= l0) {
+      const float e = rb0[j];
+      a = sat8(__fmul_rn(h2f(f2h(!masked ? __fdiv_rn(e, d0) : (d0 > 0.f ? __fdiv_rn(e, d0) : 0.f))), qs));
+    }
+    if (int64_t(j0) <= l1 && int64_t(j) <= l1) {
+      const float e = rb1[j];
+      b = sat8(__fmul_rn(h2f(f2h(!masked ? __fdiv_rn(e, d1) : (d1 > 0.f ? __fdiv_rn(e, d1) : 0.f))), qs));
+    }
+    if (j < n) {
+      q0[j] = a;
+      q1[j] = b;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------
 // MATMUL with per-sequence operands in the wide shape (F_WIDE: M <= 32,
 // K <= 256, N <= 256, shared memory by wide_mm_smem): one task computes every
@@ -741,7 +784,8 @@ __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& 
   uint8_t* sbase = smem + (pv ? pv_a_bytes(M, N) : 0u);
   uint16_t* Sc = reinterpret_cast<uint16_t*>(sbase);
   float* rows = reinterpret_cast<float*>(sbase + (pv ? M * N * 2 : 32u * 256 * 2));
-  uint32_t* pws = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(rows) + kWarps * (pv ? N : 256u) * 4);
+  // (FX_PV: two row buffers per warp, for the two-row softmax)
+  uint32_t* pws = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(rows) + kWarps * (pv ? 2 * N : 256u) * 4);
   int32_t* D = reinterpret_cast<int32_t*>(pptr(A, op.d, seq));
   const int32_t* C = (op.flags & F_ACCUMULATE) ? reinterpret_cast<const int32_t*>(pptr(A, op.c, seq)) : nullptr;
   const bool store_i32 = !(op.flags & F_NOI32);
@@ -788,18 +832,43 @@ __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& 
       qs = h2f(sreg_bits(A, A.ops[op.seg0].s[0], seq));
     }
     const bool masked = (op.flags & F_SMMASK) != 0;
-    float* rb = rows + warp * N;
+    float* rb = rows + warp * (pv ? 2 * N : N);
     uint32_t* pw = pws + warp * (3 * kPwMaxLeaves);
-    for (uint32_t r = warp; r < M; r += kWarps) {
-      const int64_t lt = int64_t(r) + qrb < int64_t(vkl) - 1 ? int64_t(r) + qrb : int64_t(vkl) - 1;
+    auto row_last = [&](uint32_t r) -> int64_t {
+      return int64_t(r) + qrb < int64_t(vkl) - 1 ? int64_t(r) + qrb : int64_t(vkl) - 1;
+    };
+    auto zero_pad = [&](uint32_t r) {   // the A row's padding columns N .. (N rounded up to 32) are zero
+      for (uint32_t g = N / 16 + lane; g < (qstride - 16) / 16; g += 32)
+        reinterpret_cast<uint4*>(qout + uint64_t(r) * qstride)[g] = make_uint4(0, 0, 0, 0);
+    };
+    uint32_t r_single = 0;   // first row left to the one-row loop below
+    if (qout && !out) {      // rows r and r + kWarps of this warp together
+      float* rb1 = rb + N;
+      for (uint32_t r = warp; r + kWarps < M; r += 2 * kWarps) {
+        const uint32_t r1 = r + kWarps;
+        const int64_t lt0 = masked ? row_last(r) : int64_t(N) - 1, lt1 = masked ? row_last(r1) : int64_t(N) - 1;
+        const uint32_t n0 = lt0 < 0 ? 0u : min(N, uint32_t(lt0) + 1), n1 = lt1 < 0 ? 0u : min(N, uint32_t(lt1) + 1);
+        for (uint32_t j = lane; j < n0 || j < n1; j += 32) {
+          if (j < n0) rb[j] = h2f(Sc[r * N + j]);
+          if (j < n1) rb1[j] = h2f(Sc[r1 * N + j]);
+        }
+        __syncwarp();
+        softmax_rows2_q(rb, rb1, N, masked, lt0, lt1, pw, pw, lane, qout + uint64_t(r) * qstride,
+                        qout + uint64_t(r1) * qstride, qs);
+        zero_pad(r);
+        zero_pad(r1);
+        __syncwarp();
+      }
+      r_single = M - M % (2 * kWarps);   // rows past the last full pair of passes
+    }
+    for (uint32_t r = r_single + warp; r < M; r += kWarps) {
+      const int64_t lt = row_last(r);
       const uint32_t nr = masked ? (lt < 0 ? 0u : min(N, uint32_t(lt) + 1)) : N;   // columns the row reads
       for (uint32_t j = lane; j < nr; j += 32) rb[j] = h2f(Sc[r * N + j]);
       __syncwarp();
       softmax_row_f16(rb, N, masked, masked ? lt : int64_t(N) - 1, out ? out + uint64_t(r) * N : nullptr, pw, lane,
                       qout ? qout + uint64_t(r) * qstride : nullptr, qs);
-      if (qout)   // the A row's padding columns N .. (N rounded up to 32) are zero
-        for (uint32_t g = N / 16 + lane; g < (qstride - 16) / 16; g += 32)
-          reinterpret_cast<uint4*>(qout + uint64_t(r) * qstride)[g] = make_uint4(0, 0, 0, 0);
+      if (qout) zero_pad(r);
       __syncwarp();
     }
   }

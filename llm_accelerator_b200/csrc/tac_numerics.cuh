@@ -208,6 +208,51 @@ __device__ __forceinline__ float warp_pairwise_sum_smem(const float* x, uint32_t
   return warp_pairwise_sum([&](uint32_t j) { return x[j]; }, n, scratch);
 }
 
+// Two rows' np.sum at once (x0[0..n), x1[0..n) in shared memory, non-negative,
+// +0 from nz0 / nz1 on): the values of two warp_pairwise_sum_smem calls, the
+// two trees' adds interleaved.
+__device__ __forceinline__ void warp_pairwise_sum2_smem(const float* x0, const float* x1, uint32_t n,
+                                                        uint32_t* scratch0, uint32_t* scratch1, uint32_t nz0,
+                                                        uint32_t nz1, float& s0, float& s1) {
+  uint32_t bnl, bL;
+  if (!pw_balanced(n, bnl, bL)) {
+    s0 = warp_pairwise_sum_smem(x0, n, scratch0, false, 0.f, nz0);
+    s1 = warp_pairwise_sum_smem(x1, n, scratch1, false, 0.f, nz1);
+    return;
+  }
+  const uint32_t lane = threadIdx.x & 31, leaf = lane >> 2, p = lane & 3;
+  float v0 = 0.f, v1 = 0.f;
+  if (leaf < bnl) {
+    const uint32_t base = leaf * bL + 2 * p;
+    const float* q0 = x0 + base;
+    const float* q1 = x1 + base;
+    float a0 = q0[0], a1 = q0[1], b0 = q1[0], b1 = q1[1];
+    const uint32_t nz = nz0 > nz1 ? nz0 : nz1;
+    for (uint32_t i = 8; i < bL && base + i < nz; i += 8) {
+      if (base + i < nz0) {
+        a0 = __fadd_rn(a0, q0[i]);
+        a1 = __fadd_rn(a1, q0[i + 1]);
+      }
+      if (base + i < nz1) {
+        b0 = __fadd_rn(b0, q1[i]);
+        b1 = __fadd_rn(b1, q1[i + 1]);
+      }
+    }
+    v0 = __fadd_rn(a0, a1);
+    v1 = __fadd_rn(b0, b1);
+  }
+  v0 = __fadd_rn(v0, __shfl_xor_sync(0xffffffffu, v0, 1));
+  v1 = __fadd_rn(v1, __shfl_xor_sync(0xffffffffu, v1, 1));
+  v0 = __fadd_rn(v0, __shfl_xor_sync(0xffffffffu, v0, 2));
+  v1 = __fadd_rn(v1, __shfl_xor_sync(0xffffffffu, v1, 2));
+  for (uint32_t sh = 4; sh < 4 * bnl; sh <<= 1) {
+    v0 = __fadd_rn(v0, __shfl_xor_sync(0xffffffffu, v0, sh));
+    v1 = __fadd_rn(v1, __shfl_xor_sync(0xffffffffu, v1, sh));
+  }
+  s0 = __fadd_rn(0.0f, __shfl_sync(0xffffffffu, v0, 0));
+  s1 = __fadd_rn(0.0f, __shfl_sync(0xffffffffu, v1, 0));
+}
+
 template <class Get>
 __device__ inline float warp_pairwise_sum(const Get& get, uint32_t n, uint32_t* scratch) {
   const int lane = threadIdx.x & 31;

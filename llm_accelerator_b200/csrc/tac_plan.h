@@ -206,7 +206,7 @@ TAC_HD constexpr uint32_t wide_mm_bh_off(uint32_t M, uint32_t N, uint32_t K, boo
 
 // Shared memory of an FX_PV task (QK^T [M x K] x [K x N], then P.V with
 // K' = N): the P.V op's int8 A tile at 0, then the softmax scratch (the
-// dequantised rows [M][N] FP16, kExecWarps row buffers of N floats, the
+// dequantised rows [M][N] FP16, two row buffers of N floats per warp, the
 // pairwise-sum scratch); the QK^T op's F_DQ scale row keeps the last 512
 // bytes.  With FX_PVPF, V lands at the P.V op's FP16-B offset, which must
 // clear the softmax scratch and the QK^T op's A and B^T tiles (read by its
@@ -215,7 +215,7 @@ constexpr uint32_t kExecWarps = 8;                           // warps of one hal
 constexpr uint32_t kPwScratchBytes = kExecWarps * 3 * 64 * 4;   // pairwise-sum scratch of every warp
 TAC_HD constexpr uint32_t pv_a_bytes(uint32_t M, uint32_t N) { return ((M + 15) / 16) * 16 * (((N + 31) & ~31u) + 16); }
 TAC_HD constexpr uint32_t pv_scratch_end(uint32_t M, uint32_t N) {
-  return pv_a_bytes(M, N) + M * N * 2 + kExecWarps * N * 4 + kPwScratchBytes;
+  return pv_a_bytes(M, N) + M * N * 2 + 2 * kExecWarps * N * 4 + kPwScratchBytes;
 }
 TAC_HD constexpr bool pv_ok(uint32_t M, uint32_t N) { return pv_scratch_end(M, N) <= kWideMmSmem - 512; }
 TAC_HD constexpr bool pvpf_ok(uint32_t M, uint32_t N, uint32_t K, uint32_t n_pv, bool bt_pv) {
