@@ -277,6 +277,18 @@ def quarot_line():
             "timing": "median of 20 calls (4 stream-ordered launches), CUDA events, L2 flushed"}
 
 
+def ptq_line():
+    """Offline weight quantisation of GPT-2's lm_head (50257 x 768 float32 ->
+    per-channel INT8 [768, 50272] image + FP16 scales): device time of
+    tac_quantize_weight_i8 against the measured HBM copy bandwidth."""
+    from llm_accelerator_b200.ptq import time_quantizer
+    r = time_quantizer(50257, 768)
+    peak_gbs, _ = measured_peak()
+    return {"shape": r["shape"], "ms": round(r["ms"], 4), "gbs": round(r["gbs"], 1),
+            "frac_of_measured_hbm": round(r["gbs"] / peak_gbs, 4), "algorithmic_bytes": r["bytes"],
+            "timing": "median of 20 calls (2 stream-ordered launches), CUDA events, L2 flushed"}
+
+
 def traffic_per_launch(workload, batch):
     """DRAM bytes per executor launch from the committed ncu summary: the
     measured line for this batch, else a least-squares line through the
@@ -418,10 +430,11 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     e2e = B_total * K / float(t.item())
     runner.engine.check_device()
 
-    gemm_line = quarot = None
+    gemm_line = quarot = ptq = None
     if rank == 0 and not args.no_gemm:
         gemm_line = int8_gemm_line()
         quarot = quarot_line()
+        ptq = ptq_line()
     barrier()
 
     plan = runner.plans["decode"]
@@ -459,6 +472,8 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
             line["int8_gemm"] = gemm_line
         if quarot is not None:
             line["quarot_w8a16"] = quarot
+        if ptq is not None:
+            line["ptq_quantize"] = ptq
         print(json.dumps(line), flush=True)
 
 

@@ -302,6 +302,21 @@ int tac_quarot_w8a16(const uint16_t* X, const int8_t* W, const uint16_t* w_scale
                      uint16_t* Y, void* workspace, uint64_t workspace_bytes, int M, int N, int K,
                      int block, void* stream);
 
+/* ---- Offline weight quantisation ------------------------------------------
+ * Per-channel (per_channel = 1) or per-tensor symmetric INT8 quantisation of
+ * a float32 weight W[out_ch, in_features] (row-major, PyTorch layout), as
+ * quantize_tensor (quantizer/quantize.py:6-33) computes it:
+ * scale = max(max|W[n,:]|, 1e-8) / 127 in float32, q = clip(rint(W / scale),
+ * -128, 127) with IEEE float32 division; then laid out as
+ * _quantize_linear_weight (runtime/tiny_fixture.py:149-159) does: zero-padded
+ * to multiples of 16 and transposed, q_kn[K_pad, N_pad] int8 (K = in_features,
+ * N = out_ch), scale_f16[N_pad] FP16 bits (padding rows repeat the last
+ * channel's scale), scale_f32[out_ch] scratch that ends holding the float32
+ * scales of the out_ch channels.  Inputs must be finite.  All pointers are
+ * device pointers; q_kn 16-byte aligned.  Stream-ordered, 2 or 3 launches. */
+int tac_quantize_weight_i8(const float* W, int out_ch, int in_features, int per_channel, int8_t* q_kn,
+                           uint16_t* scale_f16, float* scale_f32, void* stream);
+
 /* The stand-alone GEMMs run on the tcgen05 kernel when K and N are
  * multiples of 16 and A, B and the output are 16-byte aligned, otherwise on
  * an mma.sync kernel; both are exact.  Every wait inside the tcgen05 kernel

@@ -96,6 +96,7 @@ SIGNATURES = {
     "tac_fwht_f16": (_I, [_P, _P, _I, _I, _I, _P]),
     "tac_quarot_workspace_bytes": (_U64, [_I, _I]),
     "tac_quarot_w8a16": (_I, [_P, _P, _P, _P, _P, _P, _U64, _I, _I, _I, _I, _P]),
+    "tac_quantize_weight_i8": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
 }
 
 
