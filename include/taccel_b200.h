@@ -260,6 +260,16 @@ int tac_gemm_i8_requant_shift(const int8_t* A, const int8_t* B, const int32_t* m
 int tac_gemm_i8_i32(const int8_t* A, const int8_t* B, int32_t* C, int M, int N, int K,
                     void* stream);
 
+/* The same products with B supplied transposed, Bt[N,K] row-major (K-major,
+ * as static weights can be stored once), the layout the INT8 tensor-core MMA
+ * reads fastest.  tcgen05 shapes only: K and N multiples of 16, pointers
+ * 16-byte aligned (TAC_E_ARGUMENT otherwise).  Results equal
+ * tac_gemm_i8_requant_pc / tac_gemm_i8_i32 on B = Bt^T.  The MATMUL of
+ * systolic.py:31-71 with a different operand layout. */
+int tac_gemm_i8_requant_pc_bt(const int8_t* A, const int8_t* Bt, const uint16_t* scale_f16,
+                              int8_t* out, int M, int N, int K, void* stream);
+int tac_gemm_i8_i32_bt(const int8_t* A, const int8_t* Bt, int32_t* C, int M, int N, int K, void* stream);
+
 /* Decode GEMV with the REQUANT_PC epilogue that allocates nothing: out[M,N]
  * int8 = the same result as tac_gemm_i8_requant_pc, for M <= 16 rows, computed
  * split-K over about two CTAs per SM.  Its int32 partial sums and per-column-

@@ -1,7 +1,8 @@
 // Stand-alone INT8 GEMM entry points (MATMUL + requant epilogues).
 //
 // Shapes with K and N multiples of 16 and 16-byte aligned pointers run on the
-// tcgen05 kernel (tac_gemm_tc.cuh); anything else on the mma.sync tile
+// tcgen05 kernels (tac_gemm_tc.cuh; tac_gemm_tc2.cuh on CTA pairs when
+// TAC_GEMM_2SM=1); anything else on the mma.sync tile
 // (tac_gemm_sync.cuh).  Both are exact integer GEMMs, so the choice never
 // changes a result.
 #include <cuda.h>
@@ -14,6 +15,7 @@
 #include "../../include/taccel_b200.h"
 #include "tac_gemm_sync.cuh"
 #include "tac_gemm_tc.cuh"
+#include "tac_gemm_tc2.cuh"
 
 namespace {
 
@@ -47,7 +49,8 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer) 
 
 struct DeviceInfo {
   int sms = 0;
-  bool smem_set[2] = {false, false};
+  bool smem_set[3] = {false, false, false};
+  int pair_clusters = -1;   // co-resident CTA pairs of gemm_tc2_kernel (0: none)
 };
 
 DeviceInfo& device_info(int dev) {
@@ -60,6 +63,13 @@ DeviceInfo& device_info(int dev) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// 256-wide tiles of a last, partial wave run as two 128-wide units when that
+// wave then still fits on the SMs (the units of one round run concurrently).
+bool split_tail(long tiles, int sms) {
+  const long rem = tiles % sms;
+  return tiles > sms && rem > 0 && 2 * rem <= sms;
+}
 
 // Output-tile width: 256 halves the shared-memory traffic per MMA, 128 gives
 // finer waves; pick the one with fewer SM-tile-columns of work on the critical
@@ -74,7 +84,8 @@ int pick_bn(int M, int N, int sms) {
   const long mt = (M + 127) / 128;
   const long t128 = mt * ((N + 127) / 128), t256 = mt * ((N + 255) / 256);
   const double c128 = double((t128 + sms - 1) / sms) * 128 * 1.15;
-  const double c256 = double((t256 + sms - 1) / sms) * 256;
+  const double c256 = split_tail(t256, sms) ? double(t256 / sms) * 256 + 128 * 1.15
+                                            : double((t256 + sms - 1) / sms) * 256;
   return c256 <= c128 ? 256 : 128;
 }
 
@@ -94,7 +105,52 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, tac::TcGemmParams p,
   p.k_blocks = (p.K + Cfg::kBK - 1) / Cfg::kBK;
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < di.sms ? tiles : di.sms;
+  p.full_units = p.total_units = tiles;
+  if (BN == 256 && split_tail(tiles, di.sms)) {
+    p.full_units = tiles - tiles % di.sms;
+    p.total_units = p.full_units + 2 * (tiles % di.sms);
+  }
   kern<<<grid, Cfg::kThreads, Cfg::kSmem, stream>>>(ma, mb, p);
+  return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
+}
+
+// 256 x 256 tiles on CTA pairs, opt-in (TAC_GEMM_2SM=1, read at every call),
+// for shapes that fill at least one wave of 128 x 256 single-SM tiles.  At
+// 4096^3 the pair kernel measured 72-76 us against 63-66 us for the
+// single-SM kernel with half-width tail units: per SM both take the same
+// time per 128 x 256 x K tile, and the pair kernel has no tail split.
+bool use_pair(int M, int N, int sms) {
+  const char* env = std::getenv("TAC_GEMM_2SM");
+  if (!env || env[0] != '1' || pick_bn(M, N, sms) != 256) return false;
+  return long((M + 127) / 128) * long((N + 255) / 256) >= sms;
+}
+
+int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, tac::TcGemmParams p, DeviceInfo& di,
+               cudaStream_t stream) {
+  using Cfg = tac::Tc2Cfg;
+  if (!di.smem_set[2]) {
+    if (cudaFuncSetAttribute(tac::gemm_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
+        cudaSuccess)
+      return TAC_E_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (di.sms / 2));
+    cfg.blockDim = dim3(Cfg::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, tac::gemm_tc2_kernel, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    di.pair_clusters = n < di.sms / 2 ? n : di.sms / 2;
+    di.smem_set[2] = true;
+  }
+  if (di.pair_clusters <= 0) return -1;   // caller falls back to the single-SM kernel
+  p.m_tiles = (p.M + 2 * Cfg::kBM - 1) / (2 * Cfg::kBM);
+  p.n_tiles = (p.N + Cfg::kBN - 1) / Cfg::kBN;
+  p.k_blocks = (p.K + Cfg::kBK - 1) / Cfg::kBK;
+  p.full_units = p.total_units = p.m_tiles * p.n_tiles;
+  const int clusters = p.total_units < di.pair_clusters ? p.total_units : di.pair_clusters;
+  tac::gemm_tc2_kernel<<<2 * clusters, Cfg::kThreads, Cfg::kSmem, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
 }
 
@@ -103,9 +159,10 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, tac::TcGemmParams p,
 namespace tac {
 
 // The stand-alone GEMM dispatcher (also used by the QuaRot layer).
-int gemm_launch(const int8_t* A, const int8_t* B, void* out, const uint16_t* scale, const int32_t* mult,
-                const int32_t* shift, int M, int N, int K, int epi, void* stream, const uint16_t* act_scale,
-                const uint16_t* bias) {
+// b_kmajor: B given transposed ([N, K] row-major); tcgen05 shapes only.
+int gemm_launch_ex(const int8_t* A, const int8_t* B, void* out, const uint16_t* scale, const int32_t* mult,
+                   const int32_t* shift, int M, int N, int K, int epi, void* stream, const uint16_t* act_scale,
+                   const uint16_t* bias, int b_kmajor) {
   if (!A || !B || !out || M <= 0 || N <= 0 || K <= 0) return TAC_E_ARGUMENT;
   if ((epi == tac::EPI_REQUANT_PC || epi == tac::EPI_DEQUANT_SCALED) && !scale) return TAC_E_ARGUMENT;
   if (epi == tac::EPI_DEQUANT_SCALED && !act_scale) return TAC_E_ARGUMENT;
@@ -113,20 +170,32 @@ int gemm_launch(const int8_t* A, const int8_t* B, void* out, const uint16_t* sca
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (K % 16 == 0 && N % 16 == 0 && aligned16(A) && aligned16(B) && aligned16(out)) {
     CUtensorMap ma, mb;
-    if (make_map(&ma, A, uint64_t(K), uint64_t(M)) && make_map(&mb, B, uint64_t(N), uint64_t(K))) {
+    const bool mb_ok = b_kmajor ? make_map(&mb, B, uint64_t(K), uint64_t(N)) : make_map(&mb, B, uint64_t(N), uint64_t(K));
+    if (make_map(&ma, A, uint64_t(K), uint64_t(M)) && mb_ok) {
       int dev = 0;
       if (cudaGetDevice(&dev) != cudaSuccess) return TAC_E_CUDA;
       DeviceInfo& di = device_info(dev);
       int* fault = nullptr;
       if (cudaGetSymbolAddress(reinterpret_cast<void**>(&fault), g_tc_gemm_fault) != cudaSuccess) return TAC_E_CUDA;
-      tac::TcGemmParams p{out, scale, mult, shift, M, N, K, epi, 0, 0, 0, fault, act_scale, bias};
+      tac::TcGemmParams p{out, scale, mult, shift, M, N, K, epi, 0, 0, 0, fault, act_scale, bias, 0, 0, b_kmajor};
+      if (use_pair(M, N, di.sms)) {
+        const int r = launch_tc2(ma, mb, p, di, st);
+        if (r >= 0) return r;
+      }
       return pick_bn(M, N, di.sms) == 256 ? launch_tc<256>(ma, mb, p, di, st) : launch_tc<128>(ma, mb, p, di, st);
     }
   }
+  if (b_kmajor) return TAC_E_ARGUMENT;
   tac::GemmArgs g{A, B, out, scale, mult, shift, M, N, K, epi, act_scale, bias};
   dim3 grid((N + tac::kSgBN - 1) / tac::kSgBN, (M + tac::kSgBM - 1) / tac::kSgBM);
   tac::gemm_sync_kernel<<<grid, 256, 0, st>>>(g);
   return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
+}
+
+int gemm_launch(const int8_t* A, const int8_t* B, void* out, const uint16_t* scale, const int32_t* mult,
+                const int32_t* shift, int M, int N, int K, int epi, void* stream, const uint16_t* act_scale,
+                const uint16_t* bias) {
+  return gemm_launch_ex(A, B, out, scale, mult, shift, M, N, K, epi, stream, act_scale, bias, 0);
 }
 
 }  // namespace tac
@@ -152,6 +221,16 @@ extern "C" int tac_gemm_i8_requant_pc(const int8_t* A, const int8_t* B, const ui
 extern "C" int tac_gemm_i8_requant_shift(const int8_t* A, const int8_t* B, const int32_t* mult,
                                          const int32_t* shift, int8_t* out, int M, int N, int K, void* stream) {
   return launch_gemm(A, B, out, nullptr, mult, shift, M, N, K, tac::EPI_REQUANT_SHIFT, stream);
+}
+
+extern "C" int tac_gemm_i8_requant_pc_bt(const int8_t* A, const int8_t* Bt, const uint16_t* scale_f16, int8_t* out,
+                                         int M, int N, int K, void* stream) {
+  return tac::gemm_launch_ex(A, Bt, out, scale_f16, nullptr, nullptr, M, N, K, tac::EPI_REQUANT_PC, stream, nullptr,
+                             nullptr, 1);
+}
+
+extern "C" int tac_gemm_i8_i32_bt(const int8_t* A, const int8_t* Bt, int32_t* C, int M, int N, int K, void* stream) {
+  return tac::gemm_launch_ex(A, Bt, C, nullptr, nullptr, nullptr, M, N, K, tac::EPI_I32, stream, nullptr, nullptr, 1);
 }
 
 extern "C" int tac_gemm_status(int* fault_code) {

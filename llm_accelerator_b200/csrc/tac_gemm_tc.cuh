@@ -5,7 +5,8 @@
 //
 // Layout: A row-major (K-major), B row-major [K,N] (MN-major), both moved by
 // TMA with 128-byte swizzle into a ring of shared-memory stages.  One CTA per
-// SM walks output tiles [128 x BN] in a static round-robin; warp roles:
+// SM walks output tiles [128 x BN] in a static round-robin (with BN 256, the
+// tiles of a last, partial wave run as half-width units); warp roles:
 //   warp 0      one thread issues the TMA loads of each K block,
 //   warp 1      allocates TMEM; one thread issues tcgen05.mma (M=128, N=BN,
 //               K=32 per instruction, four per 128-byte K block),
@@ -39,7 +40,27 @@ struct TcGemmParams {
   int* fault;
   const uint16_t* act_scale;   // EPI_DEQUANT_SCALED
   const uint16_t* bias;
+  // Work units: tiles [0, full_units) are whole BN-wide tiles; when
+  // total_units > full_units, each later tile t (the last, partial wave) is
+  // two half-width units 2(t - full_units) and 2(t - full_units) + 1 (BN 256
+  // only), so the last wave takes half as long.
+  int full_units, total_units;
+  // 0: B row-major [K, N] (MN-major, the ISA's layout); 1: B given transposed,
+  // row-major [N, K] (K-major, like A)
+  int b_kmajor;
 };
+
+// One unit of work: output rows [mb * 128, +128), columns [n0, n0 + width).
+struct TcUnit {
+  int mb, n0, width;
+};
+
+template <int BN>
+__device__ __forceinline__ TcUnit tc_unit(const TcGemmParams& p, int u) {
+  if (u < p.full_units) return {u % p.m_tiles, (u / p.m_tiles) * BN, BN};
+  const int v = u - p.full_units, t = p.full_units + (v >> 1);
+  return {t % p.m_tiles, (t / p.m_tiles) * BN + (v & 1) * (BN / 2), BN / 2};
+}
 
 template <int BN>
 struct TcGemmCfg {
@@ -54,6 +75,9 @@ struct TcGemmCfg {
   static constexpr int kThreads = 192;
   // kind::i8, int32 accumulate, A K-major, B MN-major
   static constexpr uint32_t kIdesc = sm100::idesc_i8(kBM, BN, 1);
+  static constexpr uint32_t kIdescHalf = sm100::idesc_i8(kBM, BN / 2, 1);
+  static constexpr uint32_t kIdescK = sm100::idesc_i8(kBM, BN, 0);
+  static constexpr uint32_t kIdescHalfK = sm100::idesc_i8(kBM, BN / 2, 0);
 };
 
 __device__ __forceinline__ void tc_store_chunk(const TcGemmParams& p, int row, int col0, const uint32_t (&v)[32]) {
@@ -179,7 +203,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = tmem_base;
-  const int total = p.m_tiles * p.n_tiles;
+  const int total = p.total_units;
   volatile int* abort_v = &abort_flag;
 
   if (warp == 0) {
@@ -187,7 +211,8 @@ __global__ void __launch_bounds__(192, 1)
       // ---- TMA producer ----
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < total && !*abort_v; tile += gridDim.x) {
-        const int mb = tile % p.m_tiles, nb = tile / p.m_tiles;
+        const TcUnit un = tc_unit<BN>(p, tile);
+        const int nbox = un.width / 128;
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1;
           if (!sm100::mbar_wait(&empty_bar[s], ph ^ 1, p.fault, TC_TIMEOUT_EMPTY) || *abort_v) {
@@ -195,12 +220,14 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           uint8_t* st = smem + s * Cfg::kStageBytes;
-          sm100::mbar_arrive_expect_tx(&full_bar[s], Cfg::kStageBytes);
-          sm100::tma_load_2d(st, &tm_a, kb * Cfg::kBK, mb * Cfg::kBM, &full_bar[s]);
-#pragma unroll
-          for (int h = 0; h < BN / 128; ++h)
-            sm100::tma_load_2d(st + Cfg::kABytes + h * 128 * Cfg::kBK, &tm_b, nb * BN + h * 128, kb * Cfg::kBK,
-                               &full_bar[s]);
+          sm100::mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + nbox * 128 * Cfg::kBK);
+          sm100::tma_load_2d(st, &tm_a, kb * Cfg::kBK, un.mb * Cfg::kBM, &full_bar[s]);
+          for (int h = 0; h < nbox; ++h) {
+            // MN-major: 128 columns x 128 K rows; K-major: 128 rows of B^T x 128 K bytes
+            const int c0 = p.b_kmajor ? kb * Cfg::kBK : un.n0 + h * 128;
+            const int c1 = p.b_kmajor ? un.n0 + h * 128 : kb * Cfg::kBK;
+            sm100::tma_load_2d(st + Cfg::kABytes + h * 128 * Cfg::kBK, &tm_b, c0, c1, &full_bar[s]);
+          }
         }
         if (*abort_v) break;
       }
@@ -221,6 +248,8 @@ __global__ void __launch_bounds__(192, 1)
         }
         sm100::tc_fence_after();
         const uint32_t d = tmem + b * BN;
+        const uint32_t idesc = p.b_kmajor ? (tile < p.full_units ? Cfg::kIdescK : Cfg::kIdescHalfK)
+                                          : (tile < p.full_units ? Cfg::kIdesc : Cfg::kIdescHalf);
         bool ok = true;
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const uint32_t s = it % S, ph = (it / S) & 1;
@@ -238,8 +267,10 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t da = sm100::smem_desc_sw128(a_addr + k * 32, 16, 1024);
             // B: MN-major 128-byte rows (one per K), 8-K groups 1024 B apart,
             // 128-column blocks (BN 256) 16 KB apart; step 32 K rows = 4 KB
-            const uint64_t db = sm100::smem_desc_sw128(b_addr + k * 32 * 128, 128 * Cfg::kBK, 1024);
-            sm100::mma_i8(d, da, db, Cfg::kIdesc, (kb | k) != 0);
+            // K-major B: like A, 128-byte rows of B^T in 8-row groups 1024 B apart
+            const uint64_t db = p.b_kmajor ? sm100::smem_desc_sw128(b_addr + k * 32, 16, 1024)
+                                           : sm100::smem_desc_sw128(b_addr + k * 32 * 128, 128 * Cfg::kBK, 1024);
+            sm100::mma_i8(d, da, db, idesc, (kb | k) != 0);
           }
           sm100::mma_commit(&empty_bar[s]);
         }
@@ -263,14 +294,14 @@ __global__ void __launch_bounds__(192, 1)
       }
       __syncwarp();
       sm100::tc_fence_after();
-      const int mb = tile % p.m_tiles, nb = tile / p.m_tiles;
-      const int row = mb * Cfg::kBM + q * 32 + lane;
+      const TcUnit un = tc_unit<BN>(p, tile);
+      const int row = un.mb * Cfg::kBM + q * 32 + lane;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < un.width / 32; ++c) {
         uint32_t v[32];
         __syncwarp();   // tcgen05.ld is warp-aligned
         sm100::tmem_ld32(tmem + (uint32_t(q * 32) << 16) + b * BN + c * 32, v);
-        tc_store_chunk(p, row, nb * BN + c * 32, v);
+        tc_store_chunk(p, row, un.n0 + c * 32, v);
       }
       sm100::tc_fence_before();
       sm100::mbar_arrive(&acc_empty[b]);

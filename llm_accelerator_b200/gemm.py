@@ -50,6 +50,38 @@ def gemm_i8_requant_pc(A, B, scale_f16, out=None):
     return out
 
 
+def _check_bt(A, Bt):
+    import torch
+    if A.dtype != torch.int8 or Bt.dtype != torch.int8 or not A.is_cuda or not Bt.is_cuda:
+        raise TypeError("A and Bt must be int8 CUDA tensors")
+    if A.dim() != 2 or Bt.dim() != 2 or A.shape[1] != Bt.shape[1]:
+        raise ValueError(f"shape mismatch {tuple(A.shape)} @ {tuple(Bt.shape)}^T")
+    if not (A.is_contiguous() and Bt.is_contiguous()):
+        raise ValueError("A and Bt must be contiguous (row-major)")
+    return A.shape[0], Bt.shape[0], A.shape[1]
+
+
+def gemm_i8_i32_bt(A, Bt, out=None):
+    """A @ Bt^T, int32; Bt is B transposed ([N, K] row-major)."""
+    import torch
+    M, N, K = _check_bt(A, Bt)
+    out = torch.empty((M, N), dtype=torch.int32, device=A.device) if out is None else out
+    L.check(L.lib.tac_gemm_i8_i32_bt(_ptr(A), _ptr(Bt), _ptr(out), M, N, K, _stream()), "tac_gemm_i8_i32_bt")
+    return out
+
+
+def gemm_i8_requant_pc_bt(A, Bt, scale_f16, out=None):
+    """REQUANT_PC(A @ Bt^T); Bt is B transposed ([N, K] row-major)."""
+    import torch
+    M, N, K = _check_bt(A, Bt)
+    if scale_f16.dtype != torch.float16 or scale_f16.numel() != N:
+        raise ValueError("scale_f16 must be float16 with N elements")
+    out = torch.empty((M, N), dtype=torch.int8, device=A.device) if out is None else out
+    L.check(L.lib.tac_gemm_i8_requant_pc_bt(_ptr(A), _ptr(Bt), _ptr(scale_f16.contiguous()), _ptr(out), M, N, K,
+                                            _stream()), "tac_gemm_i8_requant_pc_bt")
+    return out
+
+
 def gemm_i8_requant_shift(A, B, mult, shift, out=None):
     import torch
     M, N, K = _check(A, B)
@@ -62,17 +94,23 @@ def gemm_i8_requant_shift(A, B, mult, shift, out=None):
 
 
 def time_gemm(M: int, N: int, K: int, *, epilogue: str = "requant_pc", iters: int = 20, warmup: int = 5,
-              seed: int = 0, compare_cublas: bool = True) -> dict:
+              seed: int = 0, compare_cublas: bool = True, b_transposed: bool = False) -> dict:
     """Device time of one stand-alone GEMM (median over `iters` launches, CUDA
     events on the launching stream, L2 flushed between launches by writing a
     256 MB buffer) and, for comparison, torch._int_mm (cuBLASLt INT8) on the
-    same operands."""
+    same operands.  b_transposed: time the K-major-B entry points (B stored
+    as [N, K])."""
     import torch
     g = torch.Generator(device="cuda").manual_seed(seed)
     A = torch.randint(-128, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
     B = torch.randint(-128, 128, (K, N), dtype=torch.int8, device="cuda", generator=g)
     scale = torch.full((N,), 1e-3, dtype=torch.float16, device="cuda")
-    if epilogue == "i32":
+    Bt = B.t().contiguous() if b_transposed else None
+    if b_transposed:
+        out = torch.empty((M, N), dtype=torch.int32 if epilogue == "i32" else torch.int8, device="cuda")
+        fn = ((lambda: gemm_i8_i32_bt(A, Bt, out)) if epilogue == "i32"  # noqa: E731
+              else (lambda: gemm_i8_requant_pc_bt(A, Bt, scale, out)))
+    elif epilogue == "i32":
         out = torch.empty((M, N), dtype=torch.int32, device="cuda")
         fn = lambda: gemm_i8_i32(A, B, out)  # noqa: E731
     else:
@@ -101,7 +139,8 @@ def time_gemm(M: int, N: int, K: int, *, epilogue: str = "requant_pc", iters: in
     if st != L.OK:
         raise RuntimeError(f"GEMM kernel reported device fault status {st}")
     ops = 2.0 * M * N * K
-    res = {"shape": [M, N, K], "epilogue": epilogue, "ms": ms, "tops": ops / ms / 1e9}
+    res = {"shape": [M, N, K], "epilogue": epilogue, "b_layout": "[N,K]" if b_transposed else "[K,N]", "ms": ms,
+           "tops": ops / ms / 1e9}
     if compare_cublas and M > 16:
         Bc = B.t().contiguous().t()   # column-major operand for cuBLASLt
         cms = med(lambda: torch._int_mm(A, Bc))
@@ -120,6 +159,7 @@ if __name__ == "__main__":
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--bt", action="store_true", help="B stored transposed ([N, K], K-major)")
     a = ap.parse_args()
     print(json.dumps(time_gemm(a.M, a.N, a.K, epilogue=a.epilogue, iters=a.iters, warmup=a.warmup,
-                               compare_cublas=not a.no_cublas)))
+                               compare_cublas=not a.no_cublas, b_transposed=a.bt)))

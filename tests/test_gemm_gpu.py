@@ -29,10 +29,12 @@ def _requant_shift_ref(acc, mult, shift):
 # K and N multiples of 16 run on the tcgen05 kernel, the rest on the mma.sync
 # tile.  Covered: partial 128-row / 128- and 256-column tiles, K not a multiple
 # of the 128-byte K block, a single K block, the decode GEMV (M=1), and a
-# 256-column-tile case with ragged M, N and K (1936 x 2064 x 784).
+# 256-column-tile case with ragged M, N and K (1936 x 2064 x 784), and
+# last partial waves run as half-width units (160 tiles on 148 SMs): whole,
+# ragged in M, N and K, and with a half unit entirely past column N.
 SHAPES = [(64, 64, 64), (64, 768, 768), (768, 64, 3072), (1, 3072, 768), (16, 48, 64), (100, 200, 48),
           (768, 768, 768), (256, 4096, 512), (4096, 64, 768), (130, 272, 144), (1, 16, 16), (300, 208, 4096),
-          (1936, 2064, 784), (3072, 3072, 64)]
+          (1936, 2064, 784), (3072, 3072, 64), (2560, 2048, 256), (2500, 2000, 400), (2560, 1920, 128)]
 
 
 def _exact_matmul(A, B):
@@ -86,3 +88,59 @@ def test_gemm_4096_cubed_sampled():
     np.testing.assert_array_equal(q, _requant_pc_ref(Cn, scale.cpu().numpy()))
     assert L.lib.tac_gemm_status(None) == L.OK
 
+
+
+# B supplied transposed ([N, K], K-major): single-SM and CTA-pair kernels,
+# whole and half-width tail units, ragged M, N and K.
+BT_SHAPES = [(64, 768, 768), (130, 272, 144), (1936, 2064, 784), (2560, 2048, 256), (2500, 2000, 400),
+             (2560, 1920, 128), (3072, 3072, 64)]
+
+
+@pytest.mark.parametrize("M,N,K", BT_SHAPES)
+def test_gemm_bt_exact(M, N, K):
+    import torch
+    from llm_accelerator_b200 import gemm
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    scale = (rng.random(N) * 2e-4 + 1e-5).astype(np.float16)
+    acc = _exact_matmul(A, B)
+    Ad, Btd = torch.from_numpy(A).cuda(), torch.from_numpy(np.ascontiguousarray(B.T)).cuda()
+    got32 = gemm.gemm_i8_i32_bt(Ad, Btd).cpu().numpy()
+    np.testing.assert_array_equal(got32, acc.astype(np.int32))
+    got8 = gemm.gemm_i8_requant_pc_bt(Ad, Btd, torch.from_numpy(scale).cuda()).cpu().numpy()
+    np.testing.assert_array_equal(got8, _requant_pc_ref(acc, scale))
+    assert L.lib.tac_gemm_status(None) == L.OK
+
+
+def test_gemm_bt_rejects_non_tcgen05_shapes():
+    import torch
+    from llm_accelerator_b200 import gemm
+    A = torch.zeros((8, 24), dtype=torch.int8, device="cuda")
+    Bt = torch.zeros((40, 24), dtype=torch.int8, device="cuda")   # K = 24: not a multiple of 16
+    with pytest.raises(Exception):
+        gemm.gemm_i8_i32_bt(A, Bt)
+
+
+@pytest.mark.parametrize("bt", [False, True])
+def test_gemm_cta_pair_kernel_exact(bt, monkeypatch):
+    """The opt-in CTA-pair (cta_group::2) kernel: 256 x 256 tiles, ragged M, N, K."""
+    import torch
+    from llm_accelerator_b200 import gemm
+    monkeypatch.setenv("TAC_GEMM_2SM", "1")
+    for M, N, K in [(2560, 2048, 256), (2500, 2000, 400), (2560, 1920, 128), (3072, 3072, 64)]:
+        rng = np.random.default_rng(M + N + K + int(bt))
+        A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+        B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+        scale = (rng.random(N) * 2e-4 + 1e-5).astype(np.float16)
+        acc = _exact_matmul(A, B)
+        Ad, sd = torch.from_numpy(A).cuda(), torch.from_numpy(scale).cuda()
+        if bt:
+            Btd = torch.from_numpy(np.ascontiguousarray(B.T)).cuda()
+            got32, got8 = gemm.gemm_i8_i32_bt(Ad, Btd), gemm.gemm_i8_requant_pc_bt(Ad, Btd, sd)
+        else:
+            Bd = torch.from_numpy(B).cuda()
+            got32, got8 = gemm.gemm_i8_i32(Ad, Bd), gemm.gemm_i8_requant_pc(Ad, Bd, sd)
+        np.testing.assert_array_equal(got32.cpu().numpy(), acc.astype(np.int32))
+        np.testing.assert_array_equal(got8.cpu().numpy(), _requant_pc_ref(acc, scale))
+    assert L.lib.tac_gemm_status(None) == L.OK
