@@ -16,9 +16,15 @@
 //                      rows of the transposed, zero-padded [K_pad, N_pad]
 //                      image; FP16 scales (round to nearest even, padded with
 //                      the last channel's scale).
+//   quant_rows_kernel  per-channel weights with in_features <= 1600 (every
+//                      GPT-2 weight but the c_proj of the MLP): 16 whole
+//                      channels staged in shared memory, their scales taken
+//                      from there and each thread writing the 16 channel
+//                      bytes of one input row -- W is read from DRAM once.
 //
-// HBM-bound: W is read twice (the second read mostly from L2 for weights
-// below its size), the INT8 image written once.
+// HBM-bound: the staged kernel reads W once; the two-pass path reads it
+// twice (the second read from L2 for weights below its size).  The INT8
+// image is written once.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -122,6 +128,69 @@ __global__ void __launch_bounds__(256) quant_t_kernel(const float* __restrict__ 
   }
 }
 
+constexpr int kRowsCh = 16;            // channels per staged CTA
+constexpr int kRowsMaxIn = 1600;       // in_features bound of the staged kernel (100 KB of shared memory)
+
+// 256 threads, kRowsCh * I floats of dynamic shared memory.  Warp w loads
+// channels 2w and 2w + 1 (coalesced), keeping their max |w|; then thread t
+// quantises input rows k = t, t + 256, ... of all 16 channels.
+__global__ void __launch_bounds__(256) quant_rows_kernel(const float* __restrict__ W, int O, int I, int Np, int Kp,
+                                                         float* __restrict__ scale_f32, int8_t* __restrict__ Q,
+                                                         uint16_t* __restrict__ scale_f16) {
+  extern __shared__ float rows[];
+  __shared__ float sc[kRowsCh];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kRowsCh;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int c = 2 * warp + j, n = n0 + c;
+    float m = 0.f;
+    float* dst = rows + c * I;
+    if (n < O) {
+      const float* src = W + uint64_t(n) * I;
+#pragma unroll 4
+      for (int k = lane; k < I; k += 32) {
+        const float v = __ldg(src + k);
+        dst[k] = v;
+        m = fmaxf(m, fabsf(v));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) {
+      const float s = channel_scale(m);
+      sc[c] = s;
+      if (n < O) scale_f32[n] = s;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < kRowsCh) {
+    // padding channels repeat the last real channel's scale, whichever CTA computed it
+    const int n = n0 + threadIdx.x;
+    if (n < O) scale_f16[n] = f2h(sc[threadIdx.x]);
+  }
+  for (int k = threadIdx.x; k < Kp; k += blockDim.x) {
+    uint32_t w[4] = {0, 0, 0, 0};
+    if (k < I) {
+#pragma unroll
+      for (int c = 0; c < kRowsCh; ++c) {
+        if (n0 + c < O) {
+          int q = __float2int_rn(__fdiv_rn(rows[c * I + k], sc[c]));
+          q = q < -128 ? -128 : (q > 127 ? 127 : q);
+          w[c >> 2] |= uint32_t(uint8_t(int8_t(q))) << (8 * (c & 3));
+        }
+      }
+    }
+    *reinterpret_cast<uint4*>(Q + uint64_t(k) * Np + n0) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// FP16 scales of the padding channels [O, Np): the last real channel's.
+__global__ void pad_scales_kernel(const float* __restrict__ scale_f32, int O, int Np, uint16_t* __restrict__ scale_f16) {
+  const int n = O + threadIdx.x;
+  if (n < Np) scale_f16[n] = f2h(scale_f32[O - 1]);
+}
+
 }  // namespace
 
 extern "C" int tac_quantize_weight_i8(const float* W, int out_ch, int in_features, int per_channel, int8_t* q_kn,
@@ -131,6 +200,25 @@ extern "C" int tac_quantize_weight_i8(const float* W, int out_ch, int in_feature
   const int Np = (out_ch + 15) & ~15, Kp = (in_features + 15) & ~15;
   if (Np < out_ch || Kp < in_features) return TAC_E_ARGUMENT;   // int overflow
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (per_channel && in_features <= kRowsMaxIn) {
+    const int smem = kRowsCh * in_features * int(sizeof(float));
+    static bool attr_set[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return TAC_E_CUDA;
+    if (!attr_set[dev & 63]) {
+      if (cudaFuncSetAttribute(quant_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kRowsCh * kRowsMaxIn * int(sizeof(float))) != cudaSuccess)
+        return TAC_E_CUDA;
+      attr_set[dev & 63] = true;
+    }
+    quant_rows_kernel<<<Np / kRowsCh, 256, smem, st>>>(W, out_ch, in_features, Np, Kp, scale_f32, q_kn, scale_f16);
+    if (cudaGetLastError() != cudaSuccess) return TAC_E_CUDA;
+    if (Np > out_ch) {
+      pad_scales_kernel<<<1, 16, 0, st>>>(scale_f32, out_ch, Np, scale_f16);
+      if (cudaGetLastError() != cudaSuccess) return TAC_E_CUDA;
+    }
+    return TAC_OK;
+  }
   const int warps_per_block = 8;
   row_scale_kernel<<<(out_ch + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, st>>>(
       W, out_ch, in_features, per_channel, scale_f32);
