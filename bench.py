@@ -277,6 +277,22 @@ def quarot_line():
             "timing": "median of 20 calls (4 stream-ordered launches), CUDA events, L2 flushed"}
 
 
+def gemv_line():
+    """The decode GEMV of the MATMUL sweep (M 1, K 768, N 3072, MATMUL +
+    REQUANT_PC): per-call device time with the weights cycling through 256 MB
+    of distinct buffers, against the measured HBM copy bandwidth."""
+    from llm_accelerator_b200.gemm import time_gemv
+    r = time_gemv(1, 3072, 768)
+    peak_gbs, _ = measured_peak()
+    out = {"shape": r["shape"], "algorithmic_bytes": r["bytes"], "weight_buffers": r["weight_buffers"],
+           "timing": "400 calls captured in one CUDA graph, replay timed with CUDA events (median of 3), "
+                     "weights rotated over 256 MB"}
+    for k in ("general", "splitk_static"):
+        out[k] = {"us": round(r[k]["us"], 2), "gbs": round(r[k]["gbs"], 1),
+                  "frac_of_measured_hbm": round(r[k]["gbs"] / peak_gbs, 4)}
+    return out
+
+
 def ptq_line():
     """Offline weight quantisation of GPT-2's lm_head (50257 x 768 float32 ->
     per-channel INT8 [768, 50272] image + FP16 scales): device time of
@@ -430,9 +446,10 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
     e2e = B_total * K / float(t.item())
     runner.engine.check_device()
 
-    gemm_line = quarot = ptq = None
+    gemm_line = quarot = ptq = gemv = None
     if rank == 0 and not args.no_gemm:
         gemm_line = int8_gemm_line()
+        gemv = gemv_line()
         quarot = quarot_line()
         ptq = ptq_line()
     barrier()
@@ -472,6 +489,8 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
             line["int8_gemm"] = gemm_line
         if quarot is not None:
             line["quarot_w8a16"] = quarot
+        if gemv is not None:
+            line["decode_gemv"] = gemv
         if ptq is not None:
             line["ptq_quantize"] = ptq
         print(json.dumps(line), flush=True)

@@ -1,6 +1,8 @@
 // Stand-alone INT8 GEMM entry points (MATMUL + requant epilogues).
 //
-// Shapes with K and N multiples of 16 and 16-byte aligned pointers run on the
+// Decode shapes (M <= 16, K and N multiples of 4, B row-major) run on the
+// cluster split-K GEMV (tac_gemv_cluster.cuh).  Other shapes with K and N
+// multiples of 16 and 16-byte aligned pointers run on the
 // tcgen05 kernels (tac_gemm_tc.cuh; tac_gemm_tc2.cuh on CTA pairs when
 // TAC_GEMM_2SM=1); anything else on the mma.sync tile
 // (tac_gemm_sync.cuh).  Both are exact integer GEMMs, so the choice never
@@ -16,6 +18,7 @@
 #include "tac_gemm_sync.cuh"
 #include "tac_gemm_tc.cuh"
 #include "tac_gemm_tc2.cuh"
+#include "tac_gemv_cluster.cuh"
 
 namespace {
 
@@ -49,6 +52,7 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer) 
 
 struct DeviceInfo {
   int sms = 0;
+  int gemv_max_splits = 0;   // largest cluster the GEMV kernel may use (0: not yet queried)
   bool smem_set[3] = {false, false, false};
   int pair_clusters = -1;   // co-resident CTA pairs of gemm_tc2_kernel (0: none)
 };
@@ -154,6 +158,70 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, tac::TcGemmParams p
   return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
 }
 
+// Largest cluster of gemv_cluster_kernel the device can co-schedule: 16
+// when the non-portable size is allowed and at least one such cluster fits,
+// else the portable 8.  Queried once per device.
+int gemv_max_splits(DeviceInfo& di) {
+  if (di.gemv_max_splits) return di.gemv_max_splits;
+  int best = 8;
+  if (cudaFuncSetAttribute(tac::gemv_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+      cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, tac::kGcMaxSplits);
+    cfg.blockDim = dim3(tac::kGcThreads);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = tac::kGcMaxSplits;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, tac::gemv_cluster_kernel, &cfg) == cudaSuccess && n > 0)
+      best = tac::kGcMaxSplits;
+  }
+  cudaGetLastError();
+  di.gemv_max_splits = best;
+  return best;
+}
+
+// M <= 16 rows (decode): split-K over a cluster of 8 CTAs (16 for narrow
+// outputs), K rows per CTA a multiple of 32 (8 warps x 4 rows).
+int launch_gemv_cluster(const tac::GcParams& base, DeviceInfo& di, cudaStream_t stream) {
+  tac::GcParams p = base;
+  const int col_blocks = (p.N + tac::kGcCols - 1) / tac::kGcCols;
+  if (col_blocks > 65535) return -1;
+  const int groups = (p.K + 31) / 32;
+  const int max_splits = gemv_max_splits(di);
+  // Measured on B200 (CUDA-graph replay, weights from HBM): portable 8-CTA
+  // clusters are fastest once 8 splits give every SM a CTA (1 x 3072 x 768:
+  // 5.8 us at 8, 7.1 at 6, 8.9 at 12 or 16); narrower outputs need 16
+  // (1 x 768 x 3072: 8.5 us at 16, 14.0 at 8).
+  int splits = col_blocks * 8 >= di.sms ? 8 : max_splits;
+  if (splits > groups) splits = groups;
+  // TAC_GEMV_SPLITS=n (1..16, read at every call) overrides the choice
+  if (const char* env = std::getenv("TAC_GEMV_SPLITS")) {
+    const int f = std::atoi(env);
+    if (f >= 1 && f <= max_splits) splits = f < groups ? f : groups;
+  }
+  p.kper = ((groups + splits - 1) / splits) * 32;
+  splits = (p.K + p.kper - 1) / p.kper;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(col_blocks, splits);
+  cfg.blockDim = dim3(tac::kGcThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = splits;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, tac::gemv_cluster_kernel, p) == cudaSuccess ? TAC_OK : TAC_E_CUDA;
+}
+
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3) == 0; }
+
 }  // namespace
 
 namespace tac {
@@ -168,6 +236,13 @@ int gemm_launch_ex(const int8_t* A, const int8_t* B, void* out, const uint16_t* 
   if (epi == tac::EPI_DEQUANT_SCALED && !act_scale) return TAC_E_ARGUMENT;
   if (epi == tac::EPI_REQUANT_SHIFT && (!mult || !shift)) return TAC_E_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!b_kmajor && M <= tac::kGcMaxM && K % 4 == 0 && N % 4 == 0 && aligned4(A) && aligned4(B)) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return TAC_E_CUDA;
+    tac::GcParams g{A, B, out, scale, mult, shift, act_scale, bias, M, N, K, epi, 0};
+    const int r = launch_gemv_cluster(g, device_info(dev), st);
+    if (r >= 0) return r;
+  }
   if (K % 16 == 0 && N % 16 == 0 && aligned16(A) && aligned16(B) && aligned16(out)) {
     CUtensorMap ma, mb;
     const bool mb_ok = b_kmajor ? make_map(&mb, B, uint64_t(K), uint64_t(N)) : make_map(&mb, B, uint64_t(N), uint64_t(K));

@@ -163,3 +163,62 @@ if __name__ == "__main__":
     a = ap.parse_args()
     print(json.dumps(time_gemm(a.M, a.N, a.K, epilogue=a.epilogue, iters=a.iters, warmup=a.warmup,
                                compare_cublas=not a.no_cublas, b_transposed=a.bt)))
+
+
+def time_gemv(M: int = 1, N: int = 3072, K: int = 768, *, calls: int = 400, warmup: int = 20,
+              rotate_bytes: int = 256 << 20, seed: int = 0) -> dict:
+    """Decode GEMV (MATMUL + REQUANT_PC with M <= 16 rows): average device time
+    per call over `calls` back-to-back calls whose weight operands cycle
+    through distinct buffers totalling `rotate_bytes` (so every call reads its
+    weights from HBM, not L2).  The calls are captured once in a CUDA graph
+    and the graph replay is timed with CUDA events, so host issue time (a
+    ctypes call costs more than the kernel) stays out of the figure.  Times
+    the general entry point (the cluster split-K GEMV for these shapes) and
+    the split-K kernel of tac_gemv_i8_requant_pc_static.  Algorithmic bytes
+    per call: K*N weights + M*K activations + 2*N scale bytes + M*N output."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    nbuf = max(2, -(-rotate_bytes // (K * N)))
+    Bs = [torch.randint(-128, 128, (K, N), dtype=torch.int8, device="cuda", generator=g) for _ in range(nbuf)]
+    A = torch.randint(-128, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+    scale = torch.full((N,), 1e-3, dtype=torch.float16, device="cuda")
+    out = torch.empty((M, N), dtype=torch.int8, device="cuda")
+    stream = torch.cuda.current_stream()
+    hbm = K * N + M * K + 2 * N + M * N
+    res = {"shape": [M, N, K], "weight_buffers": nbuf, "bytes": hbm}
+
+    def loop(fn):
+        for i in range(warmup):   # first calls do the per-device set-up, outside the capture
+            fn(Bs[i % nbuf])
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(calls):
+                fn(Bs[i % nbuf])
+        graph.replay()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) / calls)
+        del graph
+        return sorted(times)[1]
+
+    def general(B):
+        L.check(L.lib.tac_gemm_i8_requant_pc(_ptr(A), _ptr(B), _ptr(scale), _ptr(out), M, N, K, _stream()),
+                "tac_gemm_i8_requant_pc")
+
+    def splitk(B):
+        L.check(L.lib.tac_gemv_i8_requant_pc_static(_ptr(A), _ptr(B), _ptr(scale), _ptr(out), M, N, K, _stream()),
+                "tac_gemv_i8_requant_pc_static")
+
+    for name, fn in (("general", general), ("splitk_static", splitk)):
+        ms = loop(fn)
+        res[name] = {"us": ms * 1e3, "gbs": hbm / ms / 1e6}
+    if L.lib.tac_gemm_status(None) != L.OK:
+        raise RuntimeError("GEMM kernel reported a device fault")
+    return res

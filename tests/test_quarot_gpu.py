@@ -64,6 +64,18 @@ def test_quarot_layer_unaligned_shape_takes_the_portable_gemm():
     np.testing.assert_array_equal(y.view(np.uint16), Q.quarot_w8a16_layer(x, w, s, b, block=128).view(np.uint16))
 
 
+@pytest.mark.parametrize("M,N,with_bias", [(1, 3072, True), (9, 200, False), (16, 768, True)])
+def test_quarot_layer_decode_rows_take_the_cluster_gemv(M, N, with_bias):
+    """M <= 16 rows: the dequant GEMM runs on the cluster split-K GEMV."""
+    import torch
+    from llm_accelerator_b200.quarot import quarot_w8a16
+    x, w, s, b = Q.layer_inputs(M, 768, N, seed=M)
+    bias = b if with_bias else None
+    args = [torch.from_numpy(a).cuda() for a in (x, w, s)] + [torch.from_numpy(b).cuda() if with_bias else None]
+    y = quarot_w8a16(*args, block=256).cpu().numpy()
+    np.testing.assert_array_equal(y.view(np.uint16), Q.quarot_w8a16_layer(x, w, s, bias, block=256).view(np.uint16))
+
+
 def test_quarot_rejects_bad_arguments_without_launching():
     p = C.c_void_p(256)
     assert L.lib.tac_fwht_f16(p, p, 4, 768, 48, None) == L.E_ARGUMENT        # block not a power of two
