@@ -32,13 +32,13 @@ def _requant_shift_ref(acc, mult, shift):
 # 256-column-tile case with ragged M, N and K (1936 x 2064 x 784), and
 # last partial waves run as half-width units (160 tiles on 148 SMs): whole,
 # ragged in M, N and K, and with a half unit entirely past column N.  M <= 16
-# with K and N multiples of 4 runs on the cluster split-K GEMV (one to eight
-# K splits, ragged column blocks).
+# with K and N multiples of 4 runs on the cluster split-K GEMV (clusters of
+# 1 to 16 CTAs, odd sizes 7, 10 and 12 included; ragged column blocks).
 SHAPES = [(64, 64, 64), (64, 768, 768), (768, 64, 3072), (1, 3072, 768), (16, 48, 64), (100, 200, 48),
           (768, 768, 768), (256, 4096, 512), (4096, 64, 768), (130, 272, 144), (1, 16, 16), (300, 208, 4096),
           (1936, 2064, 784), (3072, 3072, 64), (2560, 2048, 256), (2500, 2000, 400), (2560, 1920, 128),
           (5, 3072, 768), (16, 768, 3072), (7, 1000, 100), (3, 52, 36), (16, 50272, 1024), (2, 4, 4),
-          (16, 256, 8192)]
+          (16, 256, 8192), (1, 256, 320), (4, 512, 224), (1, 768, 768)]
 
 
 def _exact_matmul(A, B):
