@@ -327,6 +327,28 @@ int tac_quarot_w8a16(const uint16_t* X, const int8_t* W, const uint16_t* w_scale
 int tac_quantize_weight_i8(const float* W, int out_ch, int in_features, int per_channel, int8_t* q_kn,
                            uint16_t* scale_f16, float* scale_f32, void* stream);
 
+/* ---- Bundle files ------------------------------------------------------------
+ * A saved ProgramBundle (ProgramBundle.save: an uncompressed .npz of the
+ * prefill and decode instruction streams, the shared data image and a JSON
+ * metadata record, each a 1-D uint8 array) mapped read-only into memory.
+ * The pointers stay valid until tac_bundle_close; nothing is copied.  Stands
+ * in for loading the reference's ProgramBundle (assembler/assembler.py:163-548).
+ * TAC_E_ARGUMENT for a missing, truncated or malformed file or entry,
+ * TAC_E_UNSUPPORTED for a compressed entry.  Host only. */
+typedef struct tac_bundle_view {
+  const uint8_t* prefill;
+  uint64_t prefill_len;
+  const uint8_t* decode;
+  uint64_t decode_len;
+  const uint8_t* shared;
+  uint64_t shared_len;
+  const char* meta_json;   /* not NUL-terminated */
+  uint64_t meta_len;
+} tac_bundle_view;
+
+int tac_bundle_open(const char* path, tac_bundle_view* view, void** handle);
+int tac_bundle_close(void* handle);
+
 /* The stand-alone GEMMs run on the tcgen05 kernel when K and N are
  * multiples of 16 and A, B and the output are 16-byte aligned, otherwise on
  * an mma.sync kernel; both are exact.  Every wait inside the tcgen05 kernel

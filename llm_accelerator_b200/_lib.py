@@ -35,6 +35,12 @@ class VarSite(C.Structure):
                 ("range_lo", C.c_uint64), ("range_hi", C.c_uint64)]
 
 
+class BundleView(C.Structure):
+    _fields_ = [("prefill", C.c_void_p), ("prefill_len", C.c_uint64), ("decode", C.c_void_p),
+                ("decode_len", C.c_uint64), ("shared", C.c_void_p), ("shared_len", C.c_uint64),
+                ("meta_json", C.c_void_p), ("meta_len", C.c_uint64)]
+
+
 class ExecInfo(C.Structure):
     _fields_ = [("executed", C.c_uint64), ("final_pc", C.c_uint64), ("halted", C.c_int32),
                 ("faulted", C.c_int32), ("cycles", C.c_uint64), ("n_ops", C.c_uint64),
@@ -99,6 +105,8 @@ SIGNATURES = {
     "tac_quarot_workspace_bytes": (_U64, [_I, _I]),
     "tac_quarot_w8a16": (_I, [_P, _P, _P, _P, _P, _P, _U64, _I, _I, _I, _I, _P]),
     "tac_quantize_weight_i8": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
+    "tac_bundle_open": (_I, [C.c_char_p, C.POINTER(BundleView), C.POINTER(_P)]),
+    "tac_bundle_close": (_I, [_P]),
 }
 
 

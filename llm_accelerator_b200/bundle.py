@@ -255,6 +255,45 @@ class ProgramBundle:
             embedding_row_bytes=meta["embedding_row_bytes"], kv_step_bytes=meta["kv_step_bytes"])
 
     @classmethod
+    def load_mapped(cls, path: Union[str, Path]) -> "ProgramBundle":
+        """load() through the native reader (tac_bundle_open): the file is
+        mapped read-only and the instruction streams and the shared image are
+        NumPy views of the mapping, not copies.  The mapping lives as long as
+        the returned bundle.  Same result as load()."""
+        import ctypes as C
+        from . import _lib as L
+        view, handle = L.BundleView(), C.c_void_p()
+        st = L.lib.tac_bundle_open(str(path).encode(), C.byref(view), C.byref(handle))
+        if st != L.OK:
+            raise ValueError(f"cannot read bundle file {path} (status {st})")
+        mapping = _BundleMapping(handle)
+
+        def arr(ptr, n):
+            if n == 0:
+                return np.zeros(0, np.uint8)
+            a = np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_uint8)), shape=(int(n),))
+            a.flags.writeable = False
+            return a
+
+        meta = json.loads(C.string_at(view.meta_json, view.meta_len).decode())
+        if meta.get("version") != FORMAT_VERSION:
+            raise ValueError(f"unsupported bundle format version {meta.get('version')}")
+        b = cls(
+            prefill_instrs=arr(view.prefill, view.prefill_len).tobytes(),
+            decode_instrs=arr(view.decode, view.decode_len).tobytes(),
+            shared_data=arr(view.shared, view.shared_len), temp_size=meta["temp_size"],
+            logits_size=meta["logits_size"], kv_cache_size=meta["kv_cache_size"], input_offset=meta["input_offset"],
+            prefill_logits_offset=meta["prefill_logits_offset"],
+            decode_logits_offset=meta["decode_logits_offset"], symbol_offsets=meta["symbol_offsets"],
+            symbol_regions=meta["symbol_regions"],
+            relocation_sites=[RelocationSite(**s) for s in meta["relocation_sites"]],
+            runtime_patch_sites=[RuntimePatchSite(**s) for s in meta["runtime_patch_sites"]],
+            runtime_config_attn_sites=[RuntimeConfigAttnSite(**s) for s in meta["runtime_config_attn_sites"]],
+            embedding_row_bytes=meta["embedding_row_bytes"], kv_step_bytes=meta["kv_step_bytes"])
+        b._mapping = mapping
+        return b
+
+    @classmethod
     def from_any(cls, b) -> "ProgramBundle":
         """Copies any object with ProgramBundle's fields (e.g. the reference's)."""
         if isinstance(b, cls):
@@ -273,3 +312,16 @@ class ProgramBundle:
             runtime_config_attn_sites=[RuntimeConfigAttnSite(s.stream, s.local_pc, s.absolute_pc, s.mode)
                                        for s in b.runtime_config_attn_sites],
             embedding_row_bytes=b.embedding_row_bytes, kv_step_bytes=b.kv_step_bytes)
+
+
+class _BundleMapping:
+    """Owns a tac_bundle_open handle; unmaps the file when collected."""
+
+    def __init__(self, handle):
+        self.handle = handle
+
+    def __del__(self):
+        if self.handle:
+            from . import _lib as L
+            L.lib.tac_bundle_close(self.handle)
+            self.handle = None
