@@ -26,6 +26,40 @@ def _align(v: int, a: int) -> int:
     return (v + a - 1) & ~(a - 1)
 
 
+def symbol_extent(bundle, symbol: str) -> tuple[int, int]:
+    """[start, end) DRAM bytes a symbol may span: up to the next symbol of its
+    region, or the end of the region.  Reads only fields and methods the
+    reference's ProgramBundle has too (``symbol_address``, ``symbol_offsets``,
+    ``symbol_regions`` and the region bases, ``assembler.py:163-300``), so it
+    works on either class."""
+    start = bundle.symbol_address(symbol)
+    region = bundle.symbol_regions.get(symbol, "data")
+    ends = {"data": bundle.temp_base, "shared_data": bundle.temp_base, "temp": bundle.logits_base,
+            "logits": bundle.kv_cache_base, "kv_cache": bundle.required_dram_bytes}
+    end = ends.get(region, bundle.required_dram_bytes)
+    for name in bundle.symbol_offsets:
+        if bundle.symbol_regions.get(name, "data") != region:
+            continue
+        a = bundle.symbol_address(name)
+        if start < a < end:
+            end = a
+    return start, end
+
+
+def instruction_region(bundle, *, reset_runtime: bool = False) -> bytearray:
+    """Both runtime streams at their DRAM offsets (the image's first
+    ``data_base`` bytes), from the public stream API of either ProgramBundle
+    class; ``reset_runtime`` first re-applies the relocations, as
+    ``materialize(reset_runtime=True)`` does."""
+    if reset_runtime:
+        bundle.reset_runtime_images()
+    reg = bytearray(bundle.data_base)
+    for name, off in (("prefill", bundle.prefill_instrs_offset), ("decode", bundle.decode_instrs_offset)):
+        s = bundle.stream_bytes(name)
+        reg[off:off + len(s)] = s
+    return reg
+
+
 @dataclass(frozen=True)
 class RelocationSite:
     stream: str
@@ -144,20 +178,8 @@ class ProgramBundle:
         raise KeyError(f"Unknown ProgramBundle symbol: {symbol}")
 
     def symbol_extent(self, symbol: str) -> tuple[int, int]:
-        """[start, end) bytes a symbol may span: up to the next symbol of its
-        region, or the end of the region."""
-        start = self.symbol_address(symbol)
-        region = self.symbol_regions.get(symbol, "data")
-        ends = {"data": self.temp_base, "shared_data": self.temp_base, "temp": self.logits_base,
-                "logits": self.kv_cache_base, "kv_cache": self.required_dram_bytes}
-        end = ends.get(region, self.required_dram_bytes)
-        for name in self.symbol_offsets:
-            if self.symbol_regions.get(name, "data") != region:
-                continue
-            a = self.symbol_address(name)
-            if start < a < end:
-                end = a
-        return start, end
+        """[start, end) bytes a symbol may span (see the module function)."""
+        return symbol_extent(self, symbol)
 
     # ---- runtime streams -------------------------------------------------------------
     def _stream(self, stream: str) -> bytearray:
@@ -257,9 +279,10 @@ class ProgramBundle:
     @classmethod
     def load_mapped(cls, path: Union[str, Path]) -> "ProgramBundle":
         """load() through the native reader (tac_bundle_open): the file is
-        mapped read-only and the instruction streams and the shared image are
-        NumPy views of the mapping, not copies.  The mapping lives as long as
-        the returned bundle.  Same result as load()."""
+        mapped read-only and the shared image is a NumPy view of the mapping,
+        not a copy.  The view owns a reference to the mapping, so the file
+        stays mapped as long as the bundle or any array taken from it lives.
+        Same result as load()."""
         import ctypes as C
         from . import _lib as L
         view, handle = L.BundleView(), C.c_void_p()
@@ -271,7 +294,9 @@ class ProgramBundle:
         def arr(ptr, n):
             if n == 0:
                 return np.zeros(0, np.uint8)
-            a = np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_uint8)), shape=(int(n),))
+            raw = (C.c_uint8 * int(n)).from_address(int(ptr))
+            raw._mapping = mapping          # the array's buffer keeps the file mapped
+            a = np.frombuffer(raw, np.uint8)
             a.flags.writeable = False
             return a
 

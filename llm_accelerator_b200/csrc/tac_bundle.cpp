@@ -72,6 +72,9 @@ bool npy_u8(const uint8_t* p, uint64_t avail, const uint8_t** data, uint64_t* le
   return true;
 }
 
+// True when [at, at + len) lies inside [0, n); written so that no sum wraps.
+inline bool fits(uint64_t at, uint64_t len, uint64_t n) { return at <= n && len <= n - at; }
+
 // Finds the stored entry `name`; its payload bounds in *off, *len.
 int zip_entry(const Mapping& m, const char* name, uint64_t* off, uint64_t* len) {
   const uint8_t* b = m.base;
@@ -89,18 +92,18 @@ int zip_entry(const Mapping& m, const char* name, uint64_t* off, uint64_t* len) 
   uint64_t cd_off = rd32(b + eocd + 16), cd_entries = rd16(b + eocd + 10);
   if (eocd >= 20 && rd32(b + eocd - 20) == 0x07064b50u) {   // zip64 locator
     const uint64_t z64 = rd64(b + eocd - 20 + 8);
-    if (z64 + 56 > n || rd32(b + z64) != 0x06064b50u) return TAC_E_ARGUMENT;
+    if (!fits(z64, 56, n) || rd32(b + z64) != 0x06064b50u) return TAC_E_ARGUMENT;
     cd_entries = rd64(b + z64 + 32);
     cd_off = rd64(b + z64 + 48);
   }
   uint64_t p = cd_off;
   const size_t want = std::strlen(name);
   for (uint64_t e = 0; e < cd_entries; ++e) {
-    if (p + 46 > n || rd32(b + p) != 0x02014b50u) return TAC_E_ARGUMENT;
+    if (!fits(p, 46, n) || rd32(b + p) != 0x02014b50u) return TAC_E_ARGUMENT;
     const uint16_t method = rd16(b + p + 10);
     uint64_t csize = rd32(b + p + 20), usize = rd32(b + p + 24), lh = rd32(b + p + 42);
     const uint16_t nlen = rd16(b + p + 28), xlen = rd16(b + p + 30), clen = rd16(b + p + 32);
-    if (p + 46 + nlen + xlen + clen > n) return TAC_E_ARGUMENT;
+    if (!fits(p, 46 + uint64_t(nlen) + xlen + clen, n)) return TAC_E_ARGUMENT;
     const bool match = nlen == want && std::memcmp(b + p + 46, name, want) == 0;
     // zip64 extra field: the 0xFFFFFFFF fields in order usize, csize, local header offset
     for (uint64_t x = p + 46 + nlen; x + 4 <= p + 46 + nlen + xlen;) {
@@ -117,7 +120,7 @@ int zip_entry(const Mapping& m, const char* name, uint64_t* off, uint64_t* len) 
     }
     if (match) {
       if (method != 0 || csize != usize) return TAC_E_UNSUPPORTED;   // compressed entry
-      if (lh + 30 > n || rd32(b + lh) != 0x04034b50u) return TAC_E_ARGUMENT;
+      if (!fits(lh, 30, n) || rd32(b + lh) != 0x04034b50u) return TAC_E_ARGUMENT;
       const uint64_t data = lh + 30 + rd16(b + lh + 26) + rd16(b + lh + 28);
       if (data > n || csize > n - data) return TAC_E_ARGUMENT;
       *off = data;

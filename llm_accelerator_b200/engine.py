@@ -137,8 +137,17 @@ class Engine:
 
     # ---- memory ----------------------------------------------------------------------
     def write_dram(self, seq: int, addr: int, data) -> None:
-        b = bytes(data)
-        L.check(_lib.tac_dram_write(self.handle, seq, addr, b, len(b)), "tac_dram_write")
+        """Copies bytes (any buffer: bytes, bytearray, a NumPy array or a view
+        of a mapped file) to DRAM without an intermediate host copy; seq -1
+        writes every sequence (the shared region is written once)."""
+        if isinstance(data, (bytes, bytearray, memoryview, np.ndarray)):
+            a = np.frombuffer(data, np.uint8) if not isinstance(data, np.ndarray) else data.reshape(-1).view(np.uint8)
+            if not a.flags.c_contiguous:
+                a = np.ascontiguousarray(a)
+        else:
+            a = np.frombuffer(bytes(data), np.uint8)
+        if a.size:
+            L.check(_lib.tac_dram_write(self.handle, seq, addr, a.ctypes.data, a.size), "tac_dram_write")
 
     def read_dram(self, seq: int, addr: int, n: int) -> bytes:
         out = C.create_string_buffer(n)

@@ -19,7 +19,7 @@ import numpy as np
 
 from . import _lib as L
 from . import isa
-from .bundle import ProgramBundle
+from .bundle import ProgramBundle, instruction_region, symbol_extent
 from .engine import Engine, Site, compile_program, home_reads
 
 
@@ -123,15 +123,16 @@ class BatchedRunner:
     def __init__(self, bundle, batch: int, *, device: int = 0):
         b = ProgramBundle.from_any(bundle)
         self.bundle, self.batch, self.device = b, int(batch), device
-        image = b.materialize(reset_runtime=True)
         self.dram_bytes = max(16 * 1024 * 1024, b.required_dram_bytes)
         self.shared_bytes = (b.temp_base // 16) * 16
         self.engine = Engine(self.batch, self.dram_bytes, self.shared_bytes, device)
-        self.engine.write_dram(-1, 0, image[:self.shared_bytes])
-        tail = image[self.shared_bytes:]
-        if any(tail):
-            self.engine.write_dram(-1, self.shared_bytes, tail)
-        self.region = bytes(b.instruction_region())
+        # the image without a materialised host copy: relocated streams, then
+        # the shared data from the bundle's own buffer (a mapped file's view
+        # stays a view); the writable tail starts zeroed in a new engine
+        region = instruction_region(b, reset_runtime=True)
+        self.engine.write_dram(-1, 0, region)
+        self.engine.write_dram(-1, b.data_base, b.shared_data)
+        self.region = bytes(region)
         self.logits_count = int(b.logits_size) // 2
         self.plans = {}
         self._sites = {}
@@ -139,7 +140,7 @@ class BatchedRunner:
             sites, meta = [], []
             for s in b.runtime_patch_sites:
                 if s.stream == name:
-                    lo, hi = b.symbol_extent(s.base_symbol)
+                    lo, hi = symbol_extent(b, s.base_symbol)
                     sites.append(Site(0, s.addr_reg, s.absolute_lo_pc, s.absolute_hi_pc, lo, hi))
                     meta.append(("addr", s))
             for s in b.runtime_config_attn_sites:

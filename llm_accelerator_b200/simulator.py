@@ -21,7 +21,7 @@ import numpy as np
 from . import _lib as L
 from . import errors as E
 from . import isa
-from .bundle import ProgramBundle
+from .bundle import ProgramBundle, instruction_region, symbol_extent
 from .engine import Engine, Site, compile_program
 
 DRAM_MIN_BYTES = 16 * 1024 * 1024
@@ -298,7 +298,12 @@ class B200Simulator:
 
     # ---- program loading (simulator.py:85-179) ------------------------------------------
     def load_bundle(self, bundle, *, strict_dram_size: bool = False, max_dram_bytes: int = 1 << 30) -> None:
-        image = bundle.materialize(reset_runtime=True)
+        """Loads the bundle's image (simulator.py:162-179): the relocated
+        streams, the shared data and a zeroed writable tail.  The shared data
+        goes to the device straight from the bundle's own buffer (bytes, or a
+        view of a mapped bundle file from ProgramBundle.load_mapped); no
+        materialised host copy of the image is made."""
+        region = instruction_region(bundle, reset_runtime=True)
         need = bundle.required_dram_bytes
         size = self._dram_bytes
         if need > size:
@@ -310,8 +315,12 @@ class B200Simulator:
         # instructions + shared data form one read-only image shared by all sequences
         self._relayout(size, (bundle.temp_base // 16) * 16)
         e = self._eng()
-        e.write_dram(-1, 0, image)
-        self._insn = bytearray(image[:bundle.data_base])
+        e.write_dram(-1, 0, region)
+        e.write_dram(-1, bundle.data_base, bundle.shared_data)
+        end = bundle.data_base + len(bundle.shared_data)
+        if need > end:
+            e.write_dram(-1, end, np.zeros(need - end, np.uint8))
+        self._insn = region
         self._insn_from_dram = True
         self.bundle = self.program = bundle
         self.trace_manifest, self.runtime_twin_specs = {}, {}
@@ -386,7 +395,7 @@ class B200Simulator:
             return cached[1]
         sites = []
         for s in bundle.runtime_patch_sites:
-            lo, hi = bundle.symbol_extent(s.base_symbol)
+            lo, hi = symbol_extent(bundle, s.base_symbol)
             sites.append(Site(0, s.addr_reg, s.absolute_lo_pc, s.absolute_hi_pc, lo, hi))
         for s in bundle.runtime_config_attn_sites:
             sites.append(Site(1, 0, s.absolute_pc))

@@ -25,6 +25,12 @@ def has_gpu() -> bool:
         return False
 
 
+def has_reference() -> bool:
+    """The reference's taccel package: installed under baseline/_ref, or the
+    checkout named by TACCEL_REFERENCE."""
+    return (ROOT / "baseline" / "_ref" / "taccel").is_dir() or (REFERENCE / "software" / "taccel").is_dir()
+
+
 def pytest_collection_modifyitems(config, items):
     gpu = has_gpu()
     skip_gpu = pytest.mark.skip(reason="no CUDA device")
@@ -32,5 +38,5 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords and not gpu:
             item.add_marker(skip_gpu)
-        if "reference" in item.keywords and not (REFERENCE / "software" / "taccel").exists():
+        if "reference" in item.keywords and not has_reference():
             item.add_marker(skip_ref)

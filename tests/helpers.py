@@ -179,3 +179,39 @@ def run_bundle_sequence(sim_factory, bundle, prompt, n_steps, vocab, runner_cls)
             toks.append(tok)
         logits.append(r.run_decode_step(tok, pos))
     return toks, np.stack(logits), sim
+
+
+def import_reference() -> bool:
+    """Puts the reference's ``taccel`` package on sys.path when it is present:
+    an install under ``baseline/_ref`` beside the repository, else the
+    checkout named by TACCEL_REFERENCE (default: the conftest's path).
+    Returns whether ``taccel`` imports."""
+    import importlib
+    import sys
+    from conftest import REFERENCE, ROOT
+    for p in (ROOT / "baseline" / "_ref", REFERENCE / "software"):
+        if (p / "taccel").is_dir() and str(p) not in sys.path:
+            sys.path.insert(0, str(p))
+            break
+    sys.dont_write_bytecode = True
+    try:
+        importlib.import_module("taccel.runtime.host_runner")
+        return True
+    except ImportError:
+        return False
+
+
+def to_reference_bundle(b):
+    """The reference's own ProgramBundle object with b's fields
+    (taccel/assembler/assembler.py:163), built through its constructor."""
+    from taccel.assembler.assembler import ProgramBundle as RefBundle
+    from taccel.assembler.assembler import RelocationSite as RS, RuntimeConfigAttnSite as RC, RuntimePatchSite as RP
+    return RefBundle(prefill_instrs=b.prefill_instrs, decode_instrs=b.decode_instrs,
+                     shared_data=bytes(b.shared_data), temp_size=b.temp_size, logits_size=b.logits_size,
+                     kv_cache_size=b.kv_cache_size, input_offset=b.input_offset,
+                     prefill_logits_offset=b.prefill_logits_offset, decode_logits_offset=b.decode_logits_offset,
+                     symbol_offsets=dict(b.symbol_offsets), symbol_regions=dict(b.symbol_regions),
+                     relocation_sites=[RS(**vars(x)) for x in b.relocation_sites],
+                     runtime_patch_sites=[RP(**vars(x)) for x in b.runtime_patch_sites],
+                     runtime_config_attn_sites=[RC(**vars(x)) for x in b.runtime_config_attn_sites],
+                     embedding_row_bytes=b.embedding_row_bytes, kv_step_bytes=b.kv_step_bytes)

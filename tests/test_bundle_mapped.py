@@ -77,3 +77,38 @@ def test_malformed_files_are_rejected(tmp_path, case):
 def test_missing_file_is_rejected(tmp_path):
     with pytest.raises(ValueError, match="status 16"):
         ProgramBundle.load_mapped(tmp_path / "absent.npz")
+
+
+def test_shared_data_outlives_the_bundle():
+    """The mapped shared image keeps the file mapped after the bundle is gone."""
+    import gc
+    want = bytes(ProgramBundle.load(GOLDEN / BUNDLES[1]).shared_data)
+    shared = ProgramBundle.load_mapped(GOLDEN / BUNDLES[1]).shared_data
+    gc.collect()
+    assert bytes(shared) == want
+    view = shared[1000:2000]
+    del shared
+    gc.collect()
+    assert bytes(view) == want[1000:2000]
+
+
+@pytest.mark.parametrize("where", ["locator", "directory"])
+def test_huge_zip64_offsets_are_rejected(tmp_path, where):
+    """zip64 offsets near 2**64 must not wrap the reader's bounds checks."""
+    import struct
+    good = tmp_path / "good.npz"
+    np.savez(good, **_arrays(BUNDLES[0]))
+    data = good.read_bytes()
+    eocd = data.rfind(b"PK\x05\x06")
+    huge = (1 << 64) - 24
+    if where == "locator":          # the locator points past the end of the file
+        z64 = huge
+        extra = b""
+    else:                           # a valid zip64 record whose directory offset is huge
+        z64 = eocd
+        extra = struct.pack("<IQHHIIQQQQ", 0x06064b50, 44, 45, 45, 0, 0, 4, 4, 0, huge)
+    locator = struct.pack("<IIQI", 0x07064b50, 0, z64, 1)
+    p = tmp_path / "bad.npz"
+    p.write_bytes(data[:eocd] + extra + locator + data[eocd:])
+    with pytest.raises(ValueError, match="status 16"):
+        ProgramBundle.load_mapped(p)
