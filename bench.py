@@ -3,25 +3,33 @@
 
 Workload (default ``gpt2-medium``): GPT-2 medium (24 layers, d_model 1024,
 16 heads, vocab 50257) compiled by the reference toolchain to a W8A16
-ProgramBundle with a 256-position KV cache; 64 independent sequences per GPU
-(weak scaling: N GPUs run 64 x N sequences, each rank its own shard of the
-sequence ids, no collective on the data path; ``--strong`` splits a fixed
-global batch instead).  A step runs the decode stream once for every sequence
-(one token each).  Every sequence first consumes a 128-token random prompt
-(prefill + teacher-forced decode steps, untimed; shorter when the KV window
-must also hold the warm-up, timed and e2e steps), then runs W warm-up steps.
-``value`` times the next K teacher-forced decode steps with their runtime
-parameters already in device memory; ``e2e`` times the K greedy steps after
-them through the public runner API with host buffers (runtime words in,
-argmax token ids out, every step).
+ProgramBundle with a 256-position KV window; a fixed global batch of 64
+independent sequences split over the N GPUs (strong scaling: each rank owns a
+contiguous block of sequence ids, no collective on the data path; ``--weak``
+gives every GPU 64 sequences of its own instead).  A step runs the decode
+stream once for every sequence (one token each).  Every sequence first
+consumes a 128-token random prompt (prefill + teacher-forced decode steps,
+untimed; shorter when the KV window must also hold the warm-up, timed and e2e
+steps), then runs W warm-up steps.  ``value`` times the next K teacher-forced
+decode steps with their runtime parameters already in device memory; ``e2e``
+times the K greedy steps after them through the public runner API with host
+buffers (runtime words in, argmax token ids out, every step; the ranks
+all-gather the token ids).  At N > 1 the same run also times 64 sequences per
+GPU (``weak``).
+
+Parity: after timing, the logits of the last timed step and the greedy tokens
+of the e2e steps of the sequences the reference golden simulator ran
+(tests/golden/run_gpt2_medium_late.npz) are compared with its results; the
+line carries the outcome and the process exits 1 on a mismatch.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gpt2-medium|gpt2-small] [--batch B] [--strong]
+                    [--workload gpt2-medium|gpt2-small] [--batch B] [--weak]
 
-``--batch`` is the per-GPU batch (the global batch with ``--strong``).
+``--batch`` is the global batch (the per-GPU batch with ``--weak``).
 
 ``--impl reference`` times the CPU oracle port of the golden simulator on the
-host cores (rank 0 only) with the same metric.
+host cores (rank 0 only) with the same metric: whole decode steps, one
+sequence per host process.
 """
 from __future__ import annotations
 
@@ -57,7 +65,7 @@ SHARED = 1 << 63
 
 
 # ----------------------------------------------------------------------------------------
-# CPU oracle sample (golden-simulator port); runs in forked workers before CUDA starts
+# CPU oracle port of the golden simulator; workers fork before CUDA starts
 # ----------------------------------------------------------------------------------------
 _W = {}
 
@@ -70,57 +78,55 @@ def _worker_init():
     _W["sim"] = sim
 
 
-def _worker_run(n_insns):
+def _worker_step(_):
+    """One whole decode step of this worker's sequence; its duration."""
     t = time.perf_counter()
-    _W["sim"].run_program(_W["bundle"], "decode", max_instructions=int(n_insns))
+    _W["sim"].run_program(_W["bundle"], "decode")
     return time.perf_counter() - t
 
 
-def _mac_profile(bundle):
-    """Cumulative padded MATMUL MACs along the decode stream."""
-    from oracle import isa as OI
-    raw = bundle.stream_bytes("decode")
-    macs = np.zeros(len(raw) // 8, np.float64)
-    tile = (0, 0, 0)
-    for i in range(len(raw) // 8):
-        x = OI.decode_bytes(raw[i * 8:i * 8 + 8])
-        if x.opcode == OI.CONFIG_TILE:
-            tile = (x.M, x.N, x.K)
-        elif x.opcode == OI.MATMUL:
-            macs[i] = (tile[0] + 1) * (tile[1] + 1) * (tile[2] + 1) * 4096.0
-    return np.cumsum(macs)
+def host_cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 class CpuSampler:
-    """Times prefixes of one decode step on `workers` host processes (one
-    sequence each) and extrapolates tokens/s by the prefix's share of the
-    step's MATMUL work (MATMUL is ~83% of the golden simulator's time)."""
+    """Whole decode steps on `workers` host processes, one sequence each (the
+    golden simulator is single-threaded NumPy; its int32 matmul uses one
+    core).  A sample is one step of every worker: `workers` tokens in the
+    slowest worker's time."""
 
     def __init__(self, bundle, workers: int):
         _patch_decode(bundle, token=1, pos=1)
         self.bundle = bundle
-        self.cum = _mac_profile(bundle)
         _W["bundle"] = bundle
         _W["image"] = bundle.materialize(reset_runtime=False)
         _patch_decode(bundle, token=1, pos=1)
         self.workers = workers
         self.pool = mp.get_context("fork").Pool(workers, initializer=_worker_init)
-        # calibrate on the first ~2% of the step's work
-        n_cal = int(np.searchsorted(self.cum, 0.02 * self.cum[-1])) + 1
-        t = max(self.pool.map(_worker_run, [n_cal] * workers))
-        self.rate = self.cum[n_cal - 1] / max(t, 1e-6)   # MAC/s per worker
 
-    def sample(self, seconds: float):
-        target = min(self.cum[-1], self.rate * seconds)
-        n = int(np.searchsorted(self.cum, target)) + 1
-        n = min(n, len(self.cum))
-        t = max(self.pool.map(_worker_run, [n] * self.workers))
-        frac = float(self.cum[n - 1] / self.cum[-1])
-        return dict(tokens=self.workers * frac, seconds=t, insns=n, frac=frac)
+    def step(self):
+        t = max(self.pool.map(_worker_step, range(self.workers)))
+        return dict(tokens=float(self.workers), seconds=t)
 
     def close(self):
         self.pool.close()
         self.pool.join()
+
+    def describe(self) -> str:
+        return (f"{self.workers} host processes ({host_cpu_model()}), one sequence each; a step is one whole "
+                f"decode step of every process (no extrapolation)")
+
+
+def cpu_workers() -> int:
+    """Host processes for the CPU arm: every core, at most 32 (each holds a
+    private ~0.9 GB DRAM image)."""
+    return max(1, min(os.cpu_count() or 1, 32))
 
 
 def _patch_decode(b, token, pos):
@@ -143,17 +149,19 @@ def load_workload(name):
     return w, load_recipe(ROOT / w["recipe"])
 
 
-def algorithmic_bytes(plan, batch, bundle):
-    """Bytes one decode step must move: the shared weights / tables it reads
-    once (union of shared operand ranges) plus, per sequence, the KV-cache
-    bytes it reads and appends and the embedding rows it loads."""
+def algorithmic_bytes(plan, batch, bundle, w, positions):
+    """Bytes one decode step must move, averaged over the timed steps:
+    the shared weights / tables it reads once (the union of the plan's shared
+    operand ranges), plus per sequence
+      - the KV cache it reads: n_layer x (K and V) x d_model x 2 B for each of
+        the pos + 1 valid key positions of the step,
+      - the KV rows it appends and the embedding rows it loads (the plan's
+        runtime-addressed stores and loads),
+      - the FP16 logits it writes.
+    Returns (total, shared bytes, per-sequence bytes)."""
     ops, segs, _, _ = plan.dump()
     ranges = []
     per_seq = 0
-    shared_bytes = bundle.temp_base // 16 * 16
-    kv_lo = bundle.kv_cache_base - shared_bytes
-    rw_base = 8192 + 16384 + 4096
-    rw_end = rw_base + (max(16 << 20, bundle.required_dram_bytes) - shared_bytes + 15) // 16
 
     def add(p, nbytes):
         if int(p) & SHARED:
@@ -167,16 +175,13 @@ def algorithmic_bytes(plan, batch, bundle):
             add(op["b"], K * N)
         elif k in (14, 15, 18):   # DEQUANT_ACCUM / DEQUANT_SCALED / LAYERNORM vectors
             add(op["b"], (2 * N if k == 14 else 4 * N))
-        elif k == 2:      # runtime-addressed load (embedding rows)
+        elif k in (2, 3):         # runtime-addressed loads (embedding rows) and stores (KV appends)
             per_seq += int(op["nbytes"])
-        elif k == 3:      # runtime-addressed store (KV append)
-            per_seq += int(op["nbytes"])
-        elif k == 1:      # gathers: KV-cache reads come from the writable home region
+        elif k == 30:             # merged runtime-addressed stores: one segment (n bytes) each
+            per_seq += int(segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]["n"].sum())
+        elif k == 1:      # gathers of shared data
             for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]:
-                src = int(sg["src"])
-                if not (src & SHARED) and rw_base <= src < rw_end and (src - rw_base) * 16 >= kv_lo:
-                    per_seq += int(sg["n"]) * 16
-                add(src, int(sg["n"]) * 16)
+                add(int(sg["src"]), int(sg["n"]) * 16)
     ranges.sort()
     total, cur_lo, cur_hi = 0, None, None
     for lo, hi in ranges:
@@ -188,6 +193,8 @@ def algorithmic_bytes(plan, batch, bundle):
             cur_hi = max(cur_hi, hi)
     if cur_hi is not None:
         total += cur_hi - cur_lo
+    kv_read = w["n_layer"] * 2 * w["d_model"] * 2 * float(np.mean([p + 1 for p in positions]))
+    per_seq += kv_read + int(bundle.logits_size)
     return total * 16 + batch * per_seq, total * 16, per_seq
 
 
@@ -306,9 +313,10 @@ def ptq_line():
 
 
 def traffic_per_launch(workload, batch):
-    """DRAM bytes per executor launch from the committed ncu summary: the
-    measured line for this batch, else a least-squares line through the
-    measured batches (None without a summary)."""
+    """DRAM bytes per executor launch from the committed ncu summary (a
+    capture of an earlier run of this bench command, not of this run): the
+    line for this batch, else a least-squares line through the captured
+    batches (None without a summary)."""
     f = ROOT / "profiles" / f"exec_kernel_{workload}.txt"
     if not f.exists():
         return None
@@ -330,121 +338,248 @@ def traffic_per_launch(workload, batch):
 
 
 # ----------------------------------------------------------------------------------------
+# parity against the reference golden simulator's own runs
+# ----------------------------------------------------------------------------------------
+LATE_GOLDEN = {"gpt2-medium": "tests/golden/run_gpt2_medium_late.npz"}
+# a logits vector that is not bit-exact may differ by at most this fraction of
+# its largest |logit| (transcendental ops are evaluated in float64 and rounded
+# once; NumPy's float32 exp / tanh are not correctly rounded, and a one-ulp
+# difference can move an INT8 quantisation step further down the network)
+LOGIT_TOL = 0.05
+
+
+def sequence_tokens(seq: int, n: int) -> np.ndarray:
+    """Token ids of sequence `seq`: the prompt and its teacher-forced
+    continuation (prefix-consistent in n)."""
+    return np.random.default_rng(int(seq)).integers(0, VOCAB, n)
+
+
+class Parity:
+    """The golden sequences this rank owns, checked against the reference's
+    results: the logits after the last timed step (teacher-forced position q)
+    and the greedy tokens of the e2e steps (when they continue the golden
+    run, i.e. q is its last teacher-forced position)."""
+
+    def __init__(self, workload, seqs):
+        self.path = LATE_GOLDEN.get(workload)
+        self.z = None
+        if self.path and (ROOT / self.path).exists():
+            z = np.load(ROOT / self.path)
+            self.z = {k: z[k] for k in z.files}
+        self.local = {}
+        if self.z is not None:
+            for s in self.z["seqs"].tolist():
+                if s in seqs:
+                    self.local[int(s)] = list(seqs).index(s)
+        self.checks, self.failures = [], []
+
+    def _fail(self, msg):
+        self.failures.append(msg)
+
+    def check_logits(self, runner, q):
+        if self.z is None or q > int(self.z["tf_last"][0]):
+            return
+        import hashlib
+        for s, i in self.local.items():
+            got = runner.logits("decode", i)
+            dig = np.frombuffer(hashlib.sha256(got.tobytes()).digest(), np.uint8)
+            exact = bool(np.array_equal(dig, self.z[f"s{s}_digest"][q]))
+            v = got[:VOCAB].astype(np.float32)
+            tok_ok = int(np.argmax(v)) == int(self.z[f"s{s}_token"][q])
+            idx = np.concatenate([self.z["sample_idx"], self.z[f"s{s}_top_idx"][q]])
+            want = np.concatenate([self.z[f"s{s}_sample"][q], self.z[f"s{s}_top_val"][q]]).astype(np.float32)
+            fs = self.z["full_steps"].tolist()
+            if q in fs:
+                idx = np.arange(VOCAB)
+                want = self.z[f"s{s}_full"][fs.index(q)][:VOCAB].astype(np.float32)
+            err = float(np.max(np.abs(v[idx] - want)))
+            tol = LOGIT_TOL * float(self.z[f"s{s}_maxabs"][q])
+            self.checks.append(dict(seq=s, pos=q, exact=exact, token=tok_ok, max_abs_err=round(err, 5)))
+            if not (exact or (tok_ok and err <= tol)):
+                self._fail(f"seq {s} pos {q}: logits differ (max abs {err:.4g} > {tol:.4g} or token)")
+
+    def check_tokens(self, seq_tokens, pos0, q):
+        """seq_tokens[i]: the gathered greedy token of every sequence at position pos0 + i."""
+        if self.z is None or q != int(self.z["tf_last"][0]):
+            return
+        last = int(self.z["tf_last"][0]) + int(self.z["greedy"][0])
+        for s in self.z["seqs"].tolist():
+            want = self.z[f"s{s}_token"]
+            n = ok = 0
+            for i, toks in enumerate(seq_tokens):
+                pos = pos0 + i
+                if pos > last:
+                    break
+                n += 1
+                ok += int(toks[s]) == int(want[pos])
+                if int(toks[s]) != int(want[pos]):
+                    self._fail(f"seq {s} pos {pos}: greedy token {int(toks[s])} != reference {int(want[pos])}")
+                    break
+            self.checks.append(dict(seq=int(s), greedy_steps=n, tokens_equal=ok))
+
+    def summary(self):
+        if self.z is None:
+            return "unchecked: no reference run of this workload"
+        if not self.checks:
+            return "unchecked: timed positions outside the reference run"
+        return "failed" if self.failures else "checked"
+
+
+# ----------------------------------------------------------------------------------------
 def run_reference(args, w, bundle, rank, world):
     if rank != 0:
         return
-    workers = min(os.cpu_count() or 1, 16)
-    sampler = CpuSampler(bundle, workers)
-    budget = max(2.0, 150.0 / max(1, args.steps + min(args.warmup, 1)))
-    for _ in range(min(args.warmup, 1)):
-        sampler.sample(budget)
+    sampler = CpuSampler(bundle, cpu_workers())
+    W = args.warmup
+    for _ in range(W):
+        sampler.step()
     toks = secs = 0.0
-    last = None
     for _ in range(args.steps):
-        s = sampler.sample(budget)
-        toks += s["tokens"]
-        secs += s["seconds"]
-        last = s
+        r = sampler.step()
+        toks += r["tokens"]
+        secs += r["seconds"]
     sampler.close()
     v = toks / secs
-    sample = (f"{workers} host processes, one sequence each; per step each runs the first {last['insns']} "
-              f"instructions of one decode step ({100 * last['frac']:.1f}% of its MATMUL work), "
-              f"tokens credited by that MATMUL-work share")
+    B_total = args.batch or w["batch"]
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": min(args.warmup, 1), "ms_per_step": round(1000 * secs / args.steps, 1),
-        "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
-        "dtype": "int8", "data": "synthetic",
-        "config": {"workload": w["desc"],
-                   "global_batch": (args.batch or w["batch"]) * (1 if args.strong else max(args.gpus, world))},
-        "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": workers, "kind": "port",
-                         "sample": sample},
+        "steps": args.steps, "warmup": W, "ms_per_step": round(1000 * secs / args.steps, 1),
+        "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic: seeded random-init weights in the reference-compiled program",
+        "config": {"workload": w["desc"], "global_batch": B_total * (max(args.gpus, world) if args.weak else 1)},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": sampler.workers, "kind": "port",
+                         "sample": sampler.describe(), "cpu": host_cpu_model()},
         "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
-def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
+def _time_decode(runner, prompts, p0, K, dev, stream, barrier):
+    """K teacher-forced steps at positions p0.. with device-resident
+    parameters; CUDA-event milliseconds on the launching stream."""
     import torch
-    import torch.distributed as dist
-    from llm_accelerator_b200.runner import BatchedRunner
-
-    from llm_accelerator_b200.shard import gather_tokens, shard
-    if args.strong:
-        B_total = args.batch or w["batch"]
-        if B_total % world:
-            raise SystemExit(f"batch {B_total} does not split over {world} GPUs")
-    else:
-        B_total = (args.batch or w["batch"]) * world
-    B = B_total // world
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    stream = torch.cuda.current_stream(dev)
-    runner = BatchedRunner(bundle, B, device=local_rank)
-    seqs = np.asarray(shard(B_total, world, rank))
-    K, W = args.steps, args.warmup
-    if 1 + W + 2 * K >= w["kv_len"]:
-        raise SystemExit("steps + warmup exceed the KV length of the workload")
-    # the workload's prompt is consumed first (untimed), as far as the KV
-    # window leaves room for the warm-up, timed and e2e steps after it
-    P = max(1, min(w["prompt"], w["kv_len"] - 1 - W - 2 * K))
-    # per-sequence tokens (seeded by sequence id): the prompt, then the
-    # teacher-forced continuation of the warm-up and timed steps
-    prompts = np.stack([np.random.default_rng(int(s)).integers(0, VOCAB, P + W + K) for s in seqs])
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    # the prompt (prefill + P - 1 decode steps), then W warm-up steps, all teacher-forced
-    runner.step("prefill", prompts[:, 0], np.zeros(B, int))
-    for pos in range(1, P + W):
-        runner.step("decode", prompts[:, pos], np.full(B, pos))
-    # value: K teacher-forced steps, parameters staged on the device
-    p0 = P + W
+    B = runner.batch
     params = np.stack([runner.params("decode", prompts[:, p], np.full(B, p)) for p in range(p0, p0 + K)])
     d_params = torch.from_numpy(params.view(np.int64)).to(dev)
     stride = params.shape[1] * params.shape[2] * 8
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
-    with ClockSampler(local_rank) as clocks:
-        ev0.record(stream)
-        for i in range(K):
-            runner.step_params_async("decode", d_params.data_ptr() + i * stride, stream.cuda_stream)
-        ev1.record(stream)
-        barrier()
+    ev0.record(stream)
+    for i in range(K):
+        runner.step_params_async("decode", d_params.data_ptr() + i * stride, stream.cuda_stream)
+    ev1.record(stream)
+    barrier()
     runner.engine.check_device()
-    ms = ev0.elapsed_time(ev1)
-    t = torch.tensor([ms], device=dev)
+    return ev0.elapsed_time(ev1)
+
+
+def _consume_prompt(runner, prompts, upto):
+    B = runner.batch
+    runner.step("prefill", prompts[:, 0], np.zeros(B, int))
+    for pos in range(1, upto):
+        runner.step("decode", prompts[:, pos], np.full(B, pos))
+
+
+def _max_over_ranks(x, dev, world):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    return float(t.item())
+
+
+def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
+    import torch
+    from llm_accelerator_b200.runner import BatchedRunner
+    from llm_accelerator_b200.shard import gather_tokens, shard
+
+    if args.weak:
+        B_total = (args.batch or w["batch"]) * world
+    else:
+        B_total = args.batch or w["batch"]
+        if B_total % world:
+            raise SystemExit(f"batch {B_total} does not split over {world} GPUs")
+    B = B_total // world
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    K, W = args.steps, args.warmup
+    if 1 + W + 2 * K >= w["kv_len"]:
+        raise SystemExit("steps + warmup exceed the KV length of the workload")
+    # the prompt is consumed first (untimed), as far as the KV window leaves
+    # room for the warm-up, timed and e2e steps after it
+    P = max(1, min(w["prompt"], w["kv_len"] - 1 - W - 2 * K))
+    p0 = P + W
+    q = p0 + K - 1
+    seqs = np.asarray(shard(B_total, world, rank))
+    prompts = np.stack([sequence_tokens(s, P + W + K) for s in seqs])
+    runner = BatchedRunner(bundle, B, device=local_rank)
+    _consume_prompt(runner, prompts, P + W)
+
+    with ClockSampler(local_rank) as clocks:
+        ms = _time_decode(runner, prompts, p0, K, dev, stream, barrier)
+    ms = _max_over_ranks(ms, dev, world)
     value = B_total * K / (ms / 1000.0)
+    parity = Parity(args.workload, list(seqs))
+    parity.check_logits(runner, q)
 
     # e2e: K greedy steps through the runner API with host buffers each step
     tok_dev = torch.zeros(B, dtype=torch.int32, device=dev)
     tok_host = torch.zeros(B, dtype=torch.int32).pin_memory()
-    tokens = prompts[:, p0 + K - 1].copy()
     runner.argmax_async("decode", tok_dev.data_ptr(), VOCAB, stream.cuda_stream)
     tok_host.copy_(tok_dev)
     tokens = tok_host.numpy().astype(np.int64)
+    first = gather_tokens(tok_dev, world).cpu().numpy()
     pos0 = p0 + K
+    gathered = []
+    all_host = torch.zeros(B_total, dtype=torch.int32).pin_memory()
     barrier()
     t0 = time.perf_counter()
     for i in range(K):
         runner.step_async("decode", tokens, np.full(B, pos0 + i), stream.cuda_stream)
         runner.argmax_async("decode", tok_dev.data_ptr(), VOCAB, stream.cuda_stream)
-        gather_tokens(tok_dev, world)   # every rank sees the whole batch's tokens (NCCL all-gather)
-        tok_host.copy_(tok_dev, non_blocking=True)
+        all_dev = gather_tokens(tok_dev, world)   # every rank sees the whole batch's tokens (NCCL all-gather)
+        all_host.copy_(all_dev, non_blocking=True)
         stream.synchronize()
-        tokens = tok_host.numpy().astype(np.int64)
+        allt = all_host.numpy()
+        gathered.append(allt.copy())
+        tokens = allt[rank * B:(rank + 1) * B].astype(np.int64)
     barrier()
-    e2e_s = time.perf_counter() - t0
-    t = torch.tensor([e2e_s], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e = B_total * K / float(t.item())
+    e2e_s = _max_over_ranks(time.perf_counter() - t0, dev, world)
+    e2e = B_total * K / e2e_s
     runner.engine.check_device()
+    # the first greedy token (argmax at q) and the K e2e tokens, all sequences
+    parity.check_tokens([first] + gathered, q, q)
+    import hashlib
+    tokens_sha = hashlib.sha256(np.stack([first] + gathered).astype(np.int32).tobytes()).hexdigest()[:16]
+
+    plan = runner.plans["decode"]
+    algo, shared_b, per_seq_b = algorithmic_bytes(plan, B, bundle, w, range(p0, p0 + K))
+    from llm_accelerator_b200 import _lib as L
+    n_params = int(L.lib.tac_program_param_count(plan.handle))   # 8-byte words staged per sequence and step
+    del runner
+    torch.cuda.empty_cache()
+
+    # weak scaling beside the strong line: 64 sequences per GPU in the same run
+    weak = None
+    if world > 1 and not args.weak:
+        Bw = args.batch or w["batch"]
+        wseqs = np.asarray(shard(Bw * world, world, rank))
+        wprompts = np.stack([sequence_tokens(s, P + W + K) for s in wseqs])
+        wr = BatchedRunner(bundle, Bw, device=local_rank)
+        _consume_prompt(wr, wprompts, P + W)
+        wms = _max_over_ranks(_time_decode(wr, wprompts, p0, K, dev, stream, barrier), dev, world)
+        weak = {"value": round(Bw * world * K / (wms / 1000.0), 2), "unit": "tokens/s",
+                "global_batch": Bw * world, "per_gpu_batch": Bw, "ms_per_step": round(wms / K, 3)}
+        del wr
+        torch.cuda.empty_cache()
 
     gemm_line = quarot = ptq = gemv = None
     if rank == 0 and not args.no_gemm:
@@ -454,35 +589,47 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
         ptq = ptq_line()
     barrier()
 
-    plan = runner.plans["decode"]
-    algo, shared_b, per_seq_b = algorithmic_bytes(plan, B, bundle)
+    n_fail = _max_over_ranks(len(parity.failures), dev, world)
+    n_checks = _max_over_ranks(len(parity.checks), dev, world)
+    if parity.failures:
+        for f in parity.failures:
+            print(f"rank {rank} parity: {f}", file=sys.stderr, flush=True)
     per_launch_s = ms / 1000.0 / K
     peak, peak_kind = measured_peak()
     achieved = algo / per_launch_s / 1e9
     clk = clocks.summary()
+    status = "failed" if n_fail else parity.summary() if n_checks else "unchecked: no golden sequence in this run"
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": round(ms / K, 3), "higher_is_better": True,
-            "scaling": "strong" if args.strong else "weak",
+            "scaling": "weak" if args.weak else "strong",
             "vs_baseline": None, "dtype": "int8",
             "data": "synthetic: seeded random-init weights in the reference-compiled program",
             "config": {"workload": w["desc"], "global_batch": B_total, "per_gpu_batch": B,
                        "parallelism": f"sequences sharded over {world} GPU(s)",
-                       "timed": f"{K} teacher-forced decode steps (positions {p0}..{p0 + K - 1}, after a "
+                       "timed": f"{K} teacher-forced decode steps (positions {p0}..{q}, after a "
                                 f"{P}-token prompt and {W} warm-up steps); e2e: {K} greedy steps "
-                                f"(positions {p0 + K}..{p0 + 2 * K - 1})",
+                                f"(positions {pos0}..{pos0 + K - 1})",
                        "l2": f"inputs larger than L2: {shared_b / 1e6:.0f} MB of weights read per step"},
+            "parity": {"status": status, "reference": LATE_GOLDEN.get(args.workload),
+                       "checks": parity.checks, "e2e_tokens_sha256_16": tokens_sha},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic_per_launch(args.workload, B),
+                         "traffic_source": f"profiles/exec_kernel_{args.workload}.txt (ncu capture of an "
+                                           f"earlier run at this batch), not measured in this run",
                          "peak_kind": peak_kind, "kernel": "tac::exec_kernel",
-                         "algorithmic_bytes_per_launch": algo},
+                         "algorithmic_bytes_per_launch": round(algo),
+                         "algorithmic_split": {"shared_weights_tables": shared_b,
+                                               "per_sequence_kv_logits_rows": round(per_seq_b)}},
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(B_total * plan.n_var_words * 8),
+                    "h2d_bytes_per_step": int(B_total * n_params * 8),
                     "d2h_bytes_per_step": int(B_total * 4)},
             "gpu_launches": K,
             "clocks": clk,
         }
+        if weak is not None:
+            line["weak"] = weak
         if cpu_baseline is not None:
             line["cpu_baseline"] = cpu_baseline
         if gemm_line is not None:
@@ -494,6 +641,7 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
         if ptq is not None:
             line["ptq_quantize"] = ptq
         print(json.dumps(line), flush=True)
+    return 1 if n_fail else 0
 
 
 def main():
@@ -503,8 +651,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="gpt2-medium", choices=sorted(WORKLOADS))
-    ap.add_argument("--batch", type=int, default=0, help="per-GPU batch (global batch with --strong)")
-    ap.add_argument("--strong", action="store_true", help="split one global batch over the GPUs")
+    ap.add_argument("--batch", type=int, default=0, help="global batch (per-GPU batch with --weak)")
+    ap.add_argument("--weak", action="store_true", help="every GPU runs a batch of its own")
+    ap.add_argument("--strong", action="store_true", help="(default) split one global batch over the GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true",
                     help="skip the stand-alone 4096^3 INT8 GEMM and QuaRot layer measurements")
@@ -513,23 +662,20 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference" and rank != 0:
-        return
+        return 0
     w, bundle = load_workload(args.workload)
     if args.impl == "reference":
         run_reference(args, w, bundle, rank, world)
-        return
+        return 0
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        workers = min(os.cpu_count() or 1, 16)
         from llm_accelerator_b200.recipe import load_recipe
-        sampler = CpuSampler(load_recipe(ROOT / w["recipe"]), workers)
-        s = sampler.sample(15.0)
+        sampler = CpuSampler(load_recipe(ROOT / w["recipe"]), cpu_workers())
+        r = sampler.step()
         sampler.close()
-        cpu_baseline = {"value": round(s["tokens"] / s["seconds"], 4), "unit": "tokens/s", "cores": workers,
-                        "kind": "port",
-                        "sample": f"{workers} host processes, one sequence each, first {s['insns']} "
-                                  f"instructions of one decode step ({100 * s['frac']:.1f}% of its MATMUL work), "
-                                  f"tokens credited by that share"}
+        cpu_baseline = {"value": round(r["tokens"] / r["seconds"], 4), "unit": "tokens/s",
+                        "cores": sampler.workers, "kind": "port", "sample": sampler.describe(),
+                        "cpu": host_cpu_model()}
     if world > 1:
         import torch
         import torch.distributed as dist
@@ -538,12 +684,13 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline)
+        rc = run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline)
     finally:
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
+    return rc
 
 
 if __name__ == "__main__":
-    main()
+    sys.exit(main())

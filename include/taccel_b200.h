@@ -275,12 +275,15 @@ int tac_gemm_i8_i32_bt(const int8_t* A, const int8_t* Bt, int32_t* C, int M, int
  * split-K over about two CTAs per SM.  Its int32 partial sums and per-column-
  * block arrival counters live in a static device workspace of 8 MiB
  * (requires M * N * 4 <= 8 MiB, N <= 65536; TAC_E_ARGUMENT otherwise).
- * The first call on each device does the set-up (looks up the workspace,
- * clears the counters, synchronizes the device), so make it once before any
- * stream capture or latency-critical loop; later calls only launch.  The
- * counters return to zero at the end of every call.  Calls that overlap in
- * time on one device share the workspace and race: issue them on one stream.
- * No counterpart in the reference. */
+ * The first call on each device does the set-up (looks up the workspace's
+ * device address and clears the counters with a memset on `stream`; no device
+ * synchronisation), so make it once before any stream capture: during a
+ * capture that first call returns TAC_E_UNSUPPORTED and launches nothing.
+ * Later calls only launch.  The counters return to zero at the end of every
+ * call; after a failed launch (TAC_E_CUDA) the next call repeats the set-up,
+ * and after cudaDeviceReset the caller must reload the library.  Calls that
+ * overlap in time on one device share the workspace and race: issue them on
+ * one stream.  No counterpart in the reference. */
 int tac_gemv_i8_requant_pc_static(const int8_t* A, const int8_t* B, const uint16_t* scale_f16,
                                   int8_t* out, int M, int N, int K, void* stream);
 

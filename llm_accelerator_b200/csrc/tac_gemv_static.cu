@@ -117,8 +117,11 @@ struct GvDevice {
 };
 
 // Once per device (the device current at the call): symbol addresses of the
-// static workspace, arrival counters cleared to zero.
-int gv_setup(GvDevice** out) {
+// static workspace, and the arrival counters cleared to zero by a memset on
+// the caller's stream (ordered before the launch that follows; no device
+// synchronisation).  Set-up is refused while the stream is capturing a graph:
+// the symbol lookup may load the module, which a capture does not allow.
+int gv_setup(cudaStream_t stream, GvDevice** out) {
   static GvDevice devs[64];
   static std::mutex mu;
   int dev = 0;
@@ -126,11 +129,13 @@ int gv_setup(GvDevice** out) {
   std::lock_guard<std::mutex> lk(mu);
   GvDevice& d = devs[dev];
   if (!d.ready) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) return TAC_E_CUDA;
+    if (cap != cudaStreamCaptureStatusNone) return TAC_E_UNSUPPORTED;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&d.partial), g_gv_partial) != cudaSuccess) return TAC_E_CUDA;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&d.arrivals), g_gv_arrivals) != cudaSuccess) return TAC_E_CUDA;
-    if (cudaMemset(d.arrivals, 0, sizeof(uint32_t) * kGvMaxColBlocks) != cudaSuccess) return TAC_E_CUDA;
+    if (cudaMemsetAsync(d.arrivals, 0, sizeof(uint32_t) * kGvMaxColBlocks, stream) != cudaSuccess) return TAC_E_CUDA;
     if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return TAC_E_CUDA;
-    if (cudaDeviceSynchronize() != cudaSuccess) return TAC_E_CUDA;
     d.ready = true;
   }
   *out = &d;
@@ -148,7 +153,7 @@ extern "C" int tac_gemv_i8_requant_pc_static(const int8_t* A, const int8_t* B, c
   const size_t per_split = size_t(M) * size_t(N) * sizeof(int32_t);
   if (per_split > kGvPartialBytes) return TAC_E_ARGUMENT;
   GvDevice* d = nullptr;
-  const int rc = gv_setup(&d);
+  const int rc = gv_setup(static_cast<cudaStream_t>(stream), &d);
   if (rc != TAC_OK) return rc;
   // about two CTAs per SM, whole K chunks per split, bounded by the workspace
   const int chunks = (K + kGvKc - 1) / kGvKc;
@@ -161,5 +166,11 @@ extern "C" int tac_gemv_i8_requant_pc_static(const int8_t* A, const int8_t* B, c
   dim3 grid(col_blocks, splits);
   gemv_splitk_requant_kernel<<<grid, kGvThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       A, B, scale_f16, out, M, N, K, splits, kper, d->partial, d->arrivals);
-  return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
+  if (cudaGetLastError() != cudaSuccess) {
+    // a launch that did not run to its end may leave counters behind: the
+    // next call repeats the set-up, which clears them
+    d->ready = false;
+    return TAC_E_CUDA;
+  }
+  return TAC_OK;
 }

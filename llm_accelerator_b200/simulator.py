@@ -403,12 +403,37 @@ class B200Simulator:
         return sites
 
     def run(self, max_instructions: int = 10_000_000) -> int:
+        if self.trace_enabled and self.trace_manifest:
+            return self._run_traced(max_instructions)
         return self._execute_region(sites=(), max_instructions=max_instructions, sregs_reset=False)
 
     def step(self) -> None:
         if self.state.halted:
             return
+        pc = self.state.pc
         self._execute_region(sites=(), max_instructions=1, sregs_reset=False)
+        self._capture_trace_events(pc)
+
+    def _run_traced(self, max_instructions: int) -> int:
+        """run() with trace capture: the stream is straight-line code, so it
+        executes in segments that end at each traced pc, and the manifest's
+        tiles are read back after that instruction has completed, as the
+        reference's step() captures them (simulator.py:299-322)."""
+        import bisect
+        pcs = sorted(int(p) for p in self.trace_manifest)
+        count = 0
+        while not self.state.halted and count < max_instructions:
+            pc = int(self.state.pc)
+            i = bisect.bisect_left(pcs, pc)
+            nxt = pcs[i] if i < len(pcs) else None
+            n = max_instructions - count if nxt is None else min(nxt - pc + 1, max_instructions - count)
+            done = self._execute_region(sites=(), max_instructions=n, sregs_reset=False)
+            count += done
+            if nxt is not None and done == nxt - pc + 1:
+                self._capture_trace_events(nxt)
+            if done == 0:
+                break
+        return count
 
     def _execute(self, insn) -> None:
         """Executes one instruction object (reference dataclass or compatible)
@@ -499,13 +524,126 @@ class B200Simulator:
             raise L.fault_to_exception(f, status)
         return int(info.executed)
 
-    # ---- tracing (simulator.py:208-236) ----------------------------------------------------
+    # ---- tracing (simulator.py:208-236, 324-474) --------------------------------------------
     def enable_trace(self, node_names=None):
-        if self.trace_manifest:
-            raise NotImplementedError("trace capture of ProgramBinary trace manifests is not supported "
-                                      "by the B200 engine")
+        """Capture the trace manifest's tensors after their instructions."""
         self.trace_enabled = True
         self.trace_node_names = set(node_names) if node_names else None
+        self.trace_tensors, self.trace_raw_tensors = {}, {}
+        self.trace_saturation, self.trace_meta, self.trace_raw_events = {}, {}, []
 
     def get_trace_payload(self):
-        return {"tensors": {}, "raw_tensors": {}, "raw_events": [], "stats": {}, "meta": {}}
+        """Traced tensors, raw tiles, events, INT8 saturation statistics and
+        per-node metadata, in the reference's payload layout."""
+        stats = {}
+        for node, c in getattr(self, "trace_saturation", {}).items():
+            total = c.get("total", 0)
+            stats[node] = {"saturation_rate": (c.get("sat", 0) / total) if total else 0.0,
+                           "zero_fraction": (c.get("zero", 0) / total) if total else 0.0}
+        return {"tensors": getattr(self, "trace_tensors", {}), "raw_tensors": getattr(self, "trace_raw_tensors", {}),
+                "raw_events": getattr(self, "trace_raw_events", []), "stats": stats,
+                "meta": getattr(self, "trace_meta", {})}
+
+    def _node_shape(self, node: str):
+        rows = cols = 0
+        for events in self.trace_manifest.values():
+            for ev in events:
+                if ev["node_name"] == node:
+                    rows = max(rows, int(ev.get("row_start", 0)) + int(ev["logical_rows"]))
+                    cols = max(cols, int(ev["logical_cols"]))
+        return rows, cols
+
+    def _zero_padding(self, node: str, view: np.ndarray) -> np.ndarray:
+        """The reference's padding clean-up of two node kinds before capture:
+        the padded LayerNorm-1 input of a block and the padded projection
+        tiles of the per-head query / key / value matmuls keep only their
+        logical rows and columns (simulator.py:243-297)."""
+        base = None
+        if node.endswith("__input_padded") and node.startswith("block") and "_ln1__" in node:
+            base = node[:-len("__input_padded")]
+        else:
+            for suffix, cut in (("__act_input_padded", 7), ("__accum_pre_bias_padded", 7), ("__accum_padded", 7),
+                                ("__output_padded", 15)):
+                if node.endswith(suffix):
+                    cand = node[:-cut]
+                    if cand.split("__", 1)[0].endswith(("_query", "_key", "_value")):
+                        base = cand
+                    break
+        if base is None:
+            return view
+        rows, cols = self._node_shape(base)
+        out = view.copy()
+        if rows < out.shape[0]:
+            out[rows:, :] = 0
+        if cols < out.shape[1]:
+            out[:, cols:] = 0
+        return out
+
+    def _read_tile(self, dtype: str, buf_id: int, off_units: int, rows: int, cols: int) -> np.ndarray:
+        st = self.state
+        at = int(off_units) * 16
+        if dtype == "int32":
+            if buf_id == 2:
+                return np.frombuffer(st.accum.view(np.uint8)[at:at + rows * cols * 4], np.int32).reshape(rows, cols)
+            return np.frombuffer(st.get_buffer(buf_id)[at:at + rows * cols * 4], np.int32).reshape(rows, cols)
+        if dtype == "fp32":      # FP16 storage widened to FP32
+            return np.frombuffer(st.get_buffer(buf_id)[at:at + rows * cols * 2],
+                                 np.float16).astype(np.float32).reshape(rows, cols)
+        return np.frombuffer(st.get_buffer(buf_id)[at:at + rows * cols], np.int8).reshape(rows, cols)
+
+    def _capture_trace_events(self, pc: int) -> None:
+        if not self.trace_enabled:
+            return
+        for idx, ev in enumerate(self.trace_manifest.get(pc, [])):
+            node = ev["node_name"]
+            if self.trace_node_names is not None and node not in self.trace_node_names:
+                continue
+            rows, cols = int(ev["logical_rows"]), int(ev["logical_cols"])
+            full_rows, full_cols = int(ev["full_rows"]), int(ev["full_cols"])
+            row_start = int(ev.get("row_start", 0))
+            scale = np.float32(ev["scale"])
+            source = str(ev.get("source", "architectural"))
+            meta = self.trace_meta.setdefault(node, {"scale": float(scale), "dtype": ev["dtype"], "source": source,
+                                                     "full_rows": full_rows, "full_cols": full_cols,
+                                                     "row_start": row_start, "fragments": [],
+                                                     "raw_available": source != "virtual"})
+            meta.update(scale=float(scale), dtype=ev["dtype"], source=source, full_rows=full_rows,
+                        full_cols=full_cols)
+            meta["raw_available"] = bool(meta.get("raw_available", False) or source != "virtual")
+            meta["fragments"].append({"pc": int(pc), "event_index": idx, "row_start": row_start,
+                                      "logical_rows": rows, "logical_cols": cols})
+            raw_ev = {"pc": int(pc), "event_index": idx, "node_name": node, "dtype": ev["dtype"],
+                      "scale": float(scale), "source": source,
+                      "capture_phase": str(ev.get("capture_phase", "retire_cycle")), "row_start": row_start,
+                      "logical_rows": rows, "logical_cols": cols, "full_rows": full_rows, "full_cols": full_cols}
+            if source == "virtual":
+                # the fused legacy SOFTMAX_ATTNV ops keep no side payload on the device
+                raw_ev["raw_available"] = False
+                self.trace_raw_events.append(raw_ev)
+                continue
+            dtype = ev["dtype"]
+            if dtype == "int32" and node.endswith(("__accum_pre_matmul", "__accum_pre_matmul_next")):
+                view = np.zeros((rows, cols), np.int32)
+            else:
+                tile = self._read_tile(dtype, int(ev["buf_id"]), int(ev["offset_units"]), int(ev["mem_rows"]),
+                                       int(ev["mem_cols"]))
+                view = tile[:rows, :cols]
+                if dtype != "fp32" and not (dtype == "int32" and
+                                            node.endswith(("__accum_pre_softmax", "__accum_pre_softmax_next"))):
+                    view = self._zero_padding(node, view)
+            deq = view.astype(np.float32) if dtype == "fp32" else view.astype(np.float32) * scale
+            raw_ev["raw_available"] = True
+            raw_ev["raw"] = view.tolist()
+            if node not in self.trace_tensors:
+                self.trace_tensors[node] = np.zeros((full_rows, full_cols), np.float32)
+            self.trace_tensors[node][row_start:row_start + rows, :cols] = deq
+            if node not in self.trace_raw_tensors:
+                rt = {"int32": np.int32, "fp32": np.float32}.get(dtype, np.int8)
+                self.trace_raw_tensors[node] = np.zeros((full_rows, full_cols), rt)
+            self.trace_raw_tensors[node][row_start:row_start + rows, :cols] = view
+            self.trace_raw_events.append(raw_ev)
+            if dtype not in ("int32", "fp32"):
+                c = self.trace_saturation.setdefault(node, {"sat": 0, "zero": 0, "total": 0})
+                c["sat"] += int(np.count_nonzero((view == 127) | (view == -128)))
+                c["zero"] += int(np.count_nonzero(view == 0))
+                c["total"] += int(view.size)

@@ -1,0 +1,158 @@
+"""GPT-2 medium (24 layers, d_model 1024, 16 heads, vocab 50257), the compiled
+W8A16 program of the reference's compiler (regenerated from the committed
+recipe), on the GPU against the reference golden simulator's own runs.
+
+* ``HostRunner`` (one sequence, ``B200Simulator``): prefill + 3 decode steps
+  against tests/golden/run_gpt2_medium.npz (written by
+  tests/golden/make_bundles.py).
+* ``BatchedRunner`` at batch 64 along the path ``bench.py`` times: the prompt
+  through ``step`` (runtime words), then teacher-forced steps with device-
+  resident parameters through ``step_params_async`` up to position 152, then
+  20 greedy steps through ``step_async`` + ``argmax_async``; sequences 0, 21,
+  42 and 63 against tests/golden/run_gpt2_medium_late.npz (the reference's
+  HostRunner over the same tokens, tests/golden/make_medium_late.py).
+
+Every step's FP16 logits are compared by SHA-256; a step that is not
+bit-exact must keep the reference's greedy token and stay within LOGIT_TOL of
+the step's largest |logit| on the stored logits (the full vector at the kept
+steps, else 1024 fixed vocabulary entries plus the reference's top 32).  The
+only source of such differences is the transcendental ops (GELU's tanh,
+softmax's exp): the engine evaluates them in float64 and rounds once, while
+NumPy's float32 SIMD routines are not correctly rounded, and a one-ulp FP16
+difference can move an INT8 quantisation step further down the network."""
+from __future__ import annotations
+
+import hashlib
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).parent / "golden"
+VOCAB = 50257
+LOGIT_TOL = 0.05
+BATCH = 64
+PARAM_FROM = 128      # first position run with device-resident parameters (the bench's timed path)
+
+
+def _digest(x):
+    return np.frombuffer(hashlib.sha256(x.tobytes()).digest(), np.uint8)
+
+
+def _tokens(seq, n):
+    return np.random.default_rng(int(seq)).integers(0, VOCAB, n)
+
+
+def test_gpt2_medium_first_steps_host_runner():
+    from llm_accelerator_b200.recipe import load_recipe
+    from llm_accelerator_b200.runner import HostRunner
+    gold = np.load(GOLDEN / "run_gpt2_medium.npz")
+    prompt = [int(t) for t in gold["prompt"]]
+    assert prompt == _tokens(0, len(prompt)).tolist()
+    r = HostRunner(load_recipe(GOLDEN / "recipe_gpt2_medium.npz"), logits_dtype=np.float16)
+    logits = [r.run_prefill([prompt[0]])] + [r.run_decode_step(prompt[p], p) for p in range(1, len(prompt))]
+    exact = [bool(np.array_equal(_digest(x), d)) for x, d in zip(logits, gold["logits_digest"])]
+    print("bit-exact steps:", exact)
+    for i, step in enumerate(gold["kept_steps"]):
+        got = logits[int(step)][:VOCAB].astype(np.float32)
+        want = gold["kept_logits"][i][:VOCAB].astype(np.float32)
+        assert int(np.argmax(got)) == int(np.argmax(want))
+        assert float(np.max(np.abs(got - want))) <= LOGIT_TOL * float(np.abs(want).max())
+    assert sum(exact) >= len(exact) - 1
+
+
+class _Late:
+    def __init__(self):
+        z = np.load(GOLDEN / "run_gpt2_medium_late.npz")
+        self.z = {k: z[k] for k in z.files}
+        self.seqs = [int(s) for s in self.z["seqs"]]
+        self.tf_last = int(self.z["tf_last"][0])
+        self.greedy = int(self.z["greedy"][0])
+        self.full = [int(s) for s in self.z["full_steps"]]
+        self.exact = self.steps = 0
+        self.worst = 0.0
+
+    def token_ok(self, s, pos, tok):
+        """The reference's greedy token, or (a near tie in the reference's
+        logits, within the tolerance) its runner-up."""
+        want = int(self.z[f"s{s}_token"][pos])
+        if tok == want:
+            return True
+        top = self.z[f"s{s}_top_val"][pos].astype(np.float32)
+        return (tok == int(self.z[f"s{s}_top_idx"][pos][1]) and
+                top[0] - top[1] <= LOGIT_TOL * float(self.z[f"s{s}_maxabs"][pos]))
+
+    def check_logits(self, s, pos, lg):
+        z = self.z
+        self.steps += 1
+        if np.array_equal(_digest(lg), z[f"s{s}_digest"][pos]):
+            self.exact += 1
+            return
+        v = lg[:VOCAB].astype(np.float32)
+        assert self.token_ok(s, pos, int(np.argmax(v))), f"seq {s} pos {pos}: greedy token differs"
+        if pos in self.full:
+            idx, want = np.arange(VOCAB), z[f"s{s}_full"][self.full.index(pos)][:VOCAB].astype(np.float32)
+        else:
+            idx = np.concatenate([z["sample_idx"], z[f"s{s}_top_idx"][pos]])
+            want = np.concatenate([z[f"s{s}_sample"][pos], z[f"s{s}_top_val"][pos]]).astype(np.float32)
+        err = float(np.max(np.abs(v[idx] - want)))
+        rel = err / float(z[f"s{s}_maxabs"][pos])
+        self.worst = max(self.worst, rel)
+        assert rel <= LOGIT_TOL, f"seq {s} pos {pos}: max abs error {err:.4g} ({rel:.3f} of max |logit|)"
+
+
+def test_gpt2_medium_batch64_bench_path_against_reference():
+    import torch
+    from llm_accelerator_b200.recipe import load_recipe
+    from llm_accelerator_b200.runner import BatchedRunner
+    gold = _Late()
+    n_tf = gold.tf_last + 1
+    prompts = np.stack([_tokens(s, n_tf) for s in range(BATCH)])
+    r = BatchedRunner(load_recipe(GOLDEN / "recipe_gpt2_medium.npz"), BATCH)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+
+    def check(pos):
+        for s in gold.seqs:
+            gold.check_logits(s, pos, r.logits("prefill" if pos == 0 else "decode", s))
+
+    r.step("prefill", prompts[:, 0], np.zeros(BATCH, int))
+    check(0)
+    for pos in range(1, PARAM_FROM):
+        r.step("decode", prompts[:, pos], np.full(BATCH, pos))
+        check(pos)
+    # the bench's timed path: parameter blocks staged on the device, launched back to back
+    params = np.stack([r.params("decode", prompts[:, p], np.full(BATCH, p)) for p in range(PARAM_FROM, n_tf)])
+    d_params = torch.from_numpy(params.view(np.int64)).to(dev)
+    stride = params.shape[1] * params.shape[2] * 8
+    for i, pos in enumerate(range(PARAM_FROM, n_tf)):
+        r.step_params_async("decode", d_params.data_ptr() + i * stride, stream.cuda_stream)
+        torch.cuda.synchronize()
+        r.engine.check_device()
+        check(pos)
+    # the bench's e2e path: greedy tokens from the on-device argmax, fed back through step_async
+    tok_dev = torch.zeros(BATCH, dtype=torch.int32, device=dev)
+    r.argmax_async("decode", tok_dev.data_ptr(), VOCAB, stream.cuda_stream)
+    tokens = tok_dev.cpu().numpy().astype(np.int64)
+    live = {s: True for s in gold.seqs}
+    for s in gold.seqs:
+        live[s] = int(tokens[s]) == int(gold.z[f"s{s}_token"][gold.tf_last])
+        assert gold.token_ok(s, gold.tf_last, int(tokens[s]))
+    for pos in range(n_tf, n_tf + gold.greedy):
+        r.step_async("decode", tokens, np.full(BATCH, pos), stream.cuda_stream)
+        r.argmax_async("decode", tok_dev.data_ptr(), VOCAB, stream.cuda_stream)
+        torch.cuda.synchronize()
+        r.engine.check_device()
+        for s in gold.seqs:
+            if live[s]:    # the greedy run continues the reference's only while the fed tokens agree
+                lg = r.logits("decode", s)
+                gold.check_logits(s, pos, lg)
+        tokens = tok_dev.cpu().numpy().astype(np.int64)
+        for s in gold.seqs:
+            if live[s]:
+                assert gold.token_ok(s, pos, int(tokens[s]))
+                live[s] = int(tokens[s]) == int(gold.z[f"s{s}_token"][pos])
+    print(f"GPT-2 medium batch {BATCH}: {gold.exact} of {gold.steps} checked logits vectors bit-exact, "
+          f"worst deviation {gold.worst:.4f} of max |logit|; greedy runs followed to the end: {live}")
+    assert gold.exact >= 0.5 * gold.steps
