@@ -72,6 +72,7 @@ class _Late:
         self.full = [int(s) for s in self.z["full_steps"]]
         self.exact = self.steps = 0
         self.worst = 0.0
+        self.exact_at = {}      # position -> bit-exact sequences
 
     def token_ok(self, s, pos, tok):
         """The reference's greedy token, or (a near tie in the reference's
@@ -88,6 +89,7 @@ class _Late:
         self.steps += 1
         if np.array_equal(_digest(lg), z[f"s{s}_digest"][pos]):
             self.exact += 1
+            self.exact_at[pos] = self.exact_at.get(pos, 0) + 1
             return
         v = lg[:VOCAB].astype(np.float32)
         assert self.token_ok(s, pos, int(np.argmax(v))), f"seq {s} pos {pos}: greedy token differs"
@@ -155,4 +157,6 @@ def test_gpt2_medium_batch64_bench_path_against_reference():
                 live[s] = int(tokens[s]) == int(gold.z[f"s{s}_token"][pos])
     print(f"GPT-2 medium batch {BATCH}: {gold.exact} of {gold.steps} checked logits vectors bit-exact, "
           f"worst deviation {gold.worst:.4f} of max |logit|; greedy runs followed to the end: {live}")
-    assert gold.exact >= 0.5 * gold.steps
+    # the first steps are bit-exact for every sequence (the one-ulp differences
+    # of the transcendental ops compound with the context length and depth)
+    assert all(gold.exact_at.get(pos, 0) == len(gold.seqs) for pos in range(4))
