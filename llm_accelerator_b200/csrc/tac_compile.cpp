@@ -101,6 +101,8 @@ class Compiler {
   void merge_dyn_stores();
   void write_vadd_chains();
   int link_pv_pairs();
+  void pack_arena();
+  uint64_t arena_unpacked_ = 0;
   uint64_t dead_ops_ = 0;
 
  private:
@@ -1827,6 +1829,212 @@ void Compiler::merge_dyn_stores() {
   P->ops.insert(P->ops.end(), merged.begin(), merged.end());
 }
 
+// Reassigns arena addresses by liveness.  While the stream is compiled every
+// compute op writes a fresh arena extent, so one decode step would touch tens
+// of MB per sequence once each and its intermediates would leave L2 as
+// write-backs.  Here the accesses of the final ops (per kind, the operand
+// ranges the executor reads and writes) are unioned into groups of
+// overlapping ranges; a group lives from the lowest to the highest level that
+// touches it and may take the memory of a group whose last level is strictly
+// lower than its first (the ops of one level run concurrently, and levels are
+// separated by the executor's grid barrier).  A group keeps its offset modulo
+// 256 bytes.  An op kind or flag combination this pass does not model leaves
+// the arena as it is.
+void Compiler::pack_arena() {
+  struct Rng {
+    uint64_t lo, hi;
+    uint32_t level;
+  };
+  std::vector<Rng> rs;
+  bool ok = true;
+  const uint64_t a0 = arena_base_, a1 = arena_base_ + arena_top_;
+  auto in_arena = [&](uint64_t x) { return !(x & kSharedBit) && x >= a0 && x < a1; };
+  auto add = [&](uint64_t x, uint64_t bytes, uint32_t L) {
+    if (bytes && in_arena(x)) rs.push_back(Rng{x, x + (bytes + kUnit - 1) / kUnit, L});
+  };
+  // per segment: bit 0 = src is an address, bit 1 = dst is an address, bit 2 = seen
+  std::vector<uint8_t> role(P->segs.size(), 0);
+  auto segs = [&](const DevOp& op, uint8_t r, uint64_t bytes_each, bool n_is_bytes) {
+    for (uint32_t k = 0; k < op.nseg; ++k) {
+      const uint32_t i = op.seg0 + k;
+      if (i >= P->segs.size() || ((role[i] & 4) && (role[i] & 3) != r)) {
+        ok = false;
+        return;
+      }
+      role[i] = r | 4;
+      const Segment& sg = P->segs[i];
+      const uint64_t b = bytes_each ? bytes_each : (n_is_bytes ? sg.n : sg.n * kUnit);
+      if (r & 1) add(sg.src, b, op.level);
+      if ((r & 2) && sg.dst) add(sg.dst, b, op.level);
+    }
+  };
+  for (const DevOp& op : P->ops) {
+    const uint32_t L = op.level;
+    const uint64_t M = op.M, N = op.N, K = op.K, MN = M * N;
+    const bool sega = (op.flags & F_SEGA) != 0;
+    auto src_a = [&](uint64_t bytes) {
+      if (sega) segs(op, 1, 0, false);
+      else add(op.a, bytes, L);
+    };
+    switch (op.kind) {
+      case K_GATHER: segs(op, 3, 0, false); break;
+      case K_DYN_LOAD: add(op.d, op.nbytes, L); break;
+      case K_DYN_STORE: add(op.a, op.nbytes, L); break;
+      case K_DYN_STORE_MULTI: segs(op, 1, 0, true); break;
+      case K_SREG_LOAD: add(op.a, 2, L); break;
+      case K_SREG_FINAL: break;
+      case K_VADD_CHAIN: segs(op, 3, MN * 2, false); break;
+      case K_MATMUL: {
+        const bool dq = (op.flags & F_DQ) || (op.flags2 & FX_DQS);
+        if ((op.flags & F_ACCUMULATE) && dq) ok = false;
+        add(op.a, M * K * ((op.flags & F_QA) ? 2 : 1), L);
+        add(op.b, K * N * ((op.flags & F_QB) ? 2 : 1), L);
+        if (op.flags & F_ACCUMULATE) add(op.c, MN * 4, L);
+        else if (dq) add(op.c, N * 2, L);
+        if (!(op.flags & F_NOI32)) add(op.d, MN * 4, L);
+        if (dq) add(static_cast<uint64_t>(op.dconst), MN * 2, L);
+        if (op.flags2 & FX_DQS) add(op.nbytes, N * 2, L);
+        if (op.flags & F_SM) add(op.nbytes, MN * 2, L);
+        break;
+      }
+      case K_TRANSPOSE: add(op.a, MN, L); add(op.d, MN, L); break;
+      case K_MAX_ABS:
+        src_a(MN * 2);
+        if (op.flags2 & FX_MAXQ) add(op.d, MN, L);
+        break;
+      case K_QUANT: src_a(MN * 2); add(op.d, MN, L); break;
+      case K_GELU_F16: src_a(MN * 2); add(op.d, MN * 2, L); break;
+      case K_VADD_F16: src_a(MN * 2); add(op.b, MN * 2, L); add(op.d, MN * 2, L); break;
+      case K_REQUANT: add(op.a, MN * 4, L); add(op.d, MN, L); break;
+      case K_REQUANT_PC: add(op.a, MN * 4, L); add(op.b, N * 2, L); add(op.d, MN, L); break;
+      case K_SCALE_MUL_I32: add(op.a, MN * 4, L); add(op.d, MN * 4, L); break;
+      case K_SCALE_MUL_I8: add(op.a, MN, L); add(op.d, MN, L); break;
+      case K_VADD_I8: add(op.a, MN, L); add(op.b, MN, L); add(op.d, MN, L); break;
+      case K_VADD_I32: add(op.a, MN * 4, L); add(op.b, N * 4, L); add(op.d, MN * 4, L); break;
+      case K_DEQUANT_ADD: add(op.a, MN * 4, L); add(op.b, MN, L); add(op.d, MN, L); break;
+      case K_DEQUANT_ACCUM: add(op.a, MN * 4, L); add(op.b, N * 2, L); add(op.d, MN * 2, L); break;
+      case K_DEQUANT_SCALED: case K_LAYERNORM_F16:
+        add(op.a, MN * (op.kind == K_DEQUANT_SCALED ? 4 : 2), L);
+        if (op.flags & F_SPLIT) {
+          add(op.b, N * 2, L);
+          add(op.c, N * 2, L);
+        } else {
+          add(op.b, N * 4, L);
+        }
+        add(op.d, MN * 2, L);
+        break;
+      case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16: add(op.a, MN * 2, L); add(op.d, MN * 2, L); break;
+      default: ok = false; break;
+    }
+    if (sega && op.kind != K_MAX_ABS && op.kind != K_QUANT && op.kind != K_GELU_F16 && op.kind != K_VADD_F16)
+      ok = false;
+    if (!ok) return;
+  }
+  if (rs.empty()) return;
+  // groups of overlapping ranges: [lo, hi), levels [first, last]
+  std::sort(rs.begin(), rs.end(), [](const Rng& x, const Rng& y) { return x.lo < y.lo; });
+  struct Grp {
+    uint64_t lo, hi;
+    uint32_t first, last;
+    uint64_t nlo;
+  };
+  std::vector<Grp> gs;
+  for (const Rng& r : rs) {
+    if (!gs.empty() && r.lo < gs.back().hi) {
+      Grp& g = gs.back();
+      g.hi = std::max(g.hi, r.hi);
+      g.first = std::min(g.first, r.level);
+      g.last = std::max(g.last, r.level);
+    } else {
+      gs.push_back(Grp{r.lo, r.hi, r.level, r.level, 0});
+    }
+  }
+  // first-fit over blocks of 16 units, in order of first level
+  std::vector<uint32_t> order(gs.size());
+  for (uint32_t i = 0; i < gs.size(); ++i) order[i] = i;
+  std::sort(order.begin(), order.end(), [&](uint32_t x, uint32_t y) {
+    return gs[x].first != gs[y].first ? gs[x].first < gs[y].first : gs[x].lo < gs[y].lo;
+  });
+  std::map<uint64_t, uint64_t> free_blocks;   // start -> units (relative to arena_base_)
+  auto release = [&](uint64_t at, uint64_t n) {
+    auto it = free_blocks.emplace(at, n).first;
+    auto nx = std::next(it);
+    if (nx != free_blocks.end() && it->first + it->second == nx->first) {
+      it->second += nx->second;
+      free_blocks.erase(nx);
+    }
+    if (it != free_blocks.begin()) {
+      auto pv = std::prev(it);
+      if (pv->first + pv->second == it->first) {
+        pv->second += it->second;
+        free_blocks.erase(it);
+      }
+    }
+  };
+  using Live = std::pair<uint32_t, uint32_t>;   // (last level, group)
+  std::vector<Live> live;                      // min-heap on the last level
+  auto cmp = [](const Live& x, const Live& y) { return x.first > y.first; };
+  std::vector<uint64_t> block_at(gs.size(), 0), block_n(gs.size(), 0);
+  uint64_t top = 0;
+  for (uint32_t gi : order) {
+    Grp& g = gs[gi];
+    while (!live.empty() && live.front().first < g.first) {
+      const uint32_t done = live.front().second;
+      std::pop_heap(live.begin(), live.end(), cmp);
+      live.pop_back();
+      release(block_at[done], block_n[done]);
+    }
+    const uint64_t mis = (g.lo - a0) & 15;
+    const uint64_t n = (mis + (g.hi - g.lo) + 15) & ~15ull;
+    uint64_t at = kNone;
+    for (auto it = free_blocks.begin(); it != free_blocks.end(); ++it) {
+      if (it->second < n) continue;
+      at = it->first;
+      const uint64_t rest = it->second - n;
+      free_blocks.erase(it);
+      if (rest) free_blocks.emplace(at + n, rest);
+      break;
+    }
+    if (at == kNone) {
+      at = top;
+      top += n;
+    }
+    block_at[gi] = at;
+    block_n[gi] = n;
+    g.nlo = a0 + at + mis;
+    live.emplace_back(g.last, gi);
+    std::push_heap(live.begin(), live.end(), cmp);
+  }
+  // relocate every address field; an arena address no modelled access covers
+  // (a result the op does not store) goes to the arena's first unit
+  auto reloc = [&](uint64_t x) -> uint64_t {
+    if (!in_arena(x)) return x;
+    size_t lo = 0, hi = gs.size();
+    while (lo < hi) {
+      const size_t mid = (lo + hi) / 2;
+      if (gs[mid].hi <= x) lo = mid + 1;
+      else hi = mid;
+    }
+    if (lo < gs.size() && gs[lo].lo <= x && x < gs[lo].hi) return gs[lo].nlo + (x - gs[lo].lo);
+    return a0;
+  };
+  for (DevOp& op : P->ops) {
+    op.a = reloc(op.a);
+    op.b = reloc(op.b);
+    op.c = reloc(op.c);
+    op.d = reloc(op.d);
+    if (op.kind == K_MATMUL && ((op.flags & F_DQ) || (op.flags2 & FX_DQS)))
+      op.dconst = static_cast<int64_t>(reloc(static_cast<uint64_t>(op.dconst)));
+    if (op.kind == K_MATMUL && ((op.flags & F_SM) || (op.flags2 & FX_DQS))) op.nbytes = reloc(op.nbytes);
+  }
+  for (size_t i = 0; i < P->segs.size(); ++i) {
+    if (role[i] & 1) P->segs[i].src = reloc(P->segs[i].src);
+    if ((role[i] & 2) && P->segs[i].dst) P->segs[i].dst = reloc(P->segs[i].dst);
+  }
+  arena_unpacked_ = arena_top_;
+  arena_top_ = std::max<uint64_t>(top, 16);
+}
+
 // Splits each op into tasks (tile x sequence group) and orders them by level.
 void Compiler::build_tasks() {
   const uint32_t B = static_cast<uint32_t>(P->batch);
@@ -2141,6 +2349,7 @@ int Compiler::compile() {
   merge_dyn_stores();
   write_vadd_chains();
   if (int s = link_pv_pairs()) return s;
+  pack_arena();
   build_tasks();
 
   tac_exec_info& I = P->info;
