@@ -281,7 +281,27 @@ def quarot_line():
             "frac_of_nominal_int8": round(r["tflops"] / INT8_DENSE_PEAK_TOPS, 4),
             "gbs": round(r["gbs"], 1), "frac_of_measured_hbm": round(r["gbs"] / peak_gbs, 4),
             "algorithmic_bytes": r["bytes"],
-            "timing": "median of 20 calls (4 stream-ordered launches), CUDA events, L2 flushed"}
+            "timing": "median of 20 calls (2 stream-ordered launches: rotation with per-CTA maxima, then the "
+                      "GEMM that quantises the rotated rows while staging them), CUDA events, L2 flushed"}
+
+
+def weight_only_line():
+    """The weight-only INT8 GEMM at the W8A16 layer shape (1024 x 768 FP16
+    activations, 768 x 3072 INT8 weights with float32 per-column scales,
+    float32 out) against the measured HBM copy bandwidth and the measured
+    bf16 tensor throughput (it runs kind::f16)."""
+    from llm_accelerator_b200.gemm import time_gemm_wo
+    r = time_gemm_wo(1024, 3072, 768)
+    peak_gbs, _ = measured_peak()
+    out = {"shape": r["shape"], "ms": round(r["ms"], 4), "tflops": round(r["tflops"], 1), "gbs": round(r["gbs"], 1),
+           "frac_of_measured_hbm": round(r["gbs"] / peak_gbs, 4), "algorithmic_bytes": r["bytes"],
+           "timing": "median of 20 launches, CUDA events, L2 flushed"}
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        bf16 = float(json.loads(p.read_text()).get("bf16_tflops", 0.0))
+        if bf16:
+            out["frac_of_measured_bf16"] = round(r["tflops"] / bf16, 4)
+    return out
 
 
 def gemv_line():
@@ -414,6 +434,8 @@ class Parity:
             return
         last = int(self.z["tf_last"][0]) + int(self.z["greedy"][0])
         for s in self.z["seqs"].tolist():
+            if s >= len(seq_tokens[0]):
+                continue        # not in this run's batch
             want = self.z[f"s{s}_token"]
             n = ok = 0
             for i, toks in enumerate(seq_tokens):
@@ -593,11 +615,12 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
         del wr
         torch.cuda.empty_cache()
 
-    gemm_line = quarot = ptq = gemv = None
+    gemm_line = quarot = ptq = gemv = wo = None
     if rank == 0 and not args.no_gemm:
         gemm_line = int8_gemm_line()
         gemv = gemv_line()
         quarot = quarot_line()
+        wo = weight_only_line()
         ptq = ptq_line()
     barrier()
 
@@ -648,6 +671,8 @@ def run_ours(args, w, bundle, rank, world, local_rank, cpu_baseline):
             line["int8_gemm"] = gemm_line
         if quarot is not None:
             line["quarot_w8a16"] = quarot
+        if wo is not None:
+            line["weight_only_gemm"] = wo
         if gemv is not None:
             line["decode_gemv"] = gemv
         if ptq is not None:

@@ -287,6 +287,20 @@ int tac_gemm_i8_i32_bt(const int8_t* A, const int8_t* Bt, int32_t* C, int M, int
 int tac_gemv_i8_requant_pc_static(const int8_t* A, const int8_t* B, const uint16_t* scale_f16,
                                   int8_t* out, int M, int N, int K, void* stream);
 
+/* Weight-only INT8 GEMM: Y[M,N] float32 = X[M,K] FP16 (bits) x (Q[K,N] * scale[n])
+ * + bias[n] (bias may be null): the reference's W8A32 weight-only path, INT8
+ * weights with per-output-channel float32 scales dequantised and multiplied in
+ * float32 (runtime/fp32_reference.py:330-345 _weight_only_qdq_per_channel, used
+ * by build_weight_only_int8_reference :389), with Q stored [K,N] as the ISA's
+ * weights are.  tcgen05 kind::f16 with float32 accumulation (an INT8 weight and
+ * an FP16 x FP16 product are exact), the scale and bias in the epilogue; the
+ * result differs from the reference's float32 products only in summation
+ * order.  K a multiple of 8, N of 16, X and Q 16-byte aligned (TAC_E_ARGUMENT
+ * otherwise).  Device pointers; asynchronous on `stream`; timeouts are
+ * reported by tac_gemm_status. */
+int tac_gemm_wo_f16_i8(const uint16_t* X, const int8_t* Q, const float* scale, const float* bias, float* Y,
+                       int M, int N, int K, void* stream);
+
 /* ---- QuaRot W8A16 layer ----------------------------------------------------
  * The reference folds QuaRot's rotation into the weights offline
  * (quantizer/rotation.py:51-135) and has no runtime Hadamard; these entry

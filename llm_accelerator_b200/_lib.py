@@ -101,6 +101,7 @@ SIGNATURES = {
     "tac_gemm_i8_requant_pc_bt": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
     "tac_gemm_i8_i32_bt": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "tac_gemv_i8_requant_pc_static": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "tac_gemm_wo_f16_i8": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "tac_fwht_f16": (_I, [_P, _P, _I, _I, _I, _P]),
     "tac_quarot_workspace_bytes": (_U64, [_I, _I]),
     "tac_quarot_w8a16": (_I, [_P, _P, _P, _P, _P, _P, _U64, _I, _I, _I, _I, _P]),

@@ -19,6 +19,8 @@
 #include "tac_gemm_tc.cuh"
 #include "tac_gemm_tc2.cuh"
 #include "tac_gemv_cluster.cuh"
+#include "tac_quarot_fused.cuh"
+#include "tac_gemm_wo.cuh"
 
 namespace {
 
@@ -267,6 +269,104 @@ int gemm_launch_ex(const int8_t* A, const int8_t* B, void* out, const uint16_t* 
   return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
 }
 
+// The QuaRot layer's GEMM (tac_quarot_fused.cuh): more than 16 rows (decode
+// rows stream the weights faster on the cluster GEMV), K whole 128-byte
+// blocks that fit in shared memory beside at least two W stages, N a
+// multiple of 16, 16-byte aligned W and Y.
+bool quarot_gemm_ok(const int8_t* W, const uint16_t* Y, int M, int N, int K) {
+  return M > 16 && K > 0 && K % kQrBK == 0 && K <= kQrMaxK && qr_stages(K) >= 2 && N > 0 && N % 16 == 0 &&
+         aligned16(W) && aligned16(Y);
+}
+
+int quarot_gemm_launch(const uint16_t* xr, const uint32_t* slots, int n_slots, const int8_t* W,
+                       const uint16_t* w_scale, const uint16_t* bias, uint16_t* Y, int M, int N, int K,
+                       cudaStream_t st) {
+  static bool smem_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TAC_E_CUDA;
+  DeviceInfo& di = device_info(dev);
+  if (!smem_set[dev]) {
+    // the largest dynamic shared memory any eligible K asks for
+    if (cudaFuncSetAttribute(quarot_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQrSmemBudget + 1024) !=
+        cudaSuccess)
+      return TAC_E_CUDA;
+    smem_set[dev] = true;
+  }
+  CUtensorMap tm_w;
+  if (!make_map(&tm_w, W, uint64_t(N), uint64_t(K))) return TAC_E_CUDA;
+  QrParams p{};
+  p.xr = xr;
+  p.slots = slots;
+  p.n_slots = n_slots;
+  p.w_scale = w_scale;
+  p.bias = bias;
+  p.y = Y;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.m_tiles = (M + kQrBM - 1) / kQrBM;
+  p.n_tiles = (N + kQrBN - 1) / kQrBN;
+  p.k_blocks = K / kQrBK;
+  p.stages = qr_stages(K);
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p.fault), g_tc_gemm_fault) != cudaSuccess) return TAC_E_CUDA;
+  const int tiles = p.m_tiles * p.n_tiles;
+  quarot_gemm_kernel<<<tiles < di.sms ? tiles : di.sms, kQrThreads, qr_smem_bytes(K), st>>>(tm_w, p);
+  return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
+}
+
+// Weight-only GEMM (tac_gemm_wo.cuh): X FP16 [M,K] (K a multiple of 8), Q INT8
+// [K,N] (N a multiple of 16), both 16-byte aligned.
+int gemm_wo_launch(const uint16_t* X, const int8_t* Q, const float* scale, const float* bias, float* Y, int M,
+                   int N, int K, cudaStream_t st) {
+  if (!X || !Q || !scale || !Y || M <= 0 || N <= 0 || K <= 0 || K % 8 || N % 16 || !aligned16(X) || !aligned16(Q) ||
+      (reinterpret_cast<uintptr_t>(Y) & 3))
+    return TAC_E_ARGUMENT;
+  static bool smem_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TAC_E_CUDA;
+  DeviceInfo& di = device_info(dev);
+  if (!smem_set[dev]) {
+    if (cudaFuncSetAttribute(gemm_wo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWoSmem) != cudaSuccess)
+      return TAC_E_CUDA;
+    smem_set[dev] = true;
+  }
+  auto fn = encode_fn();
+  if (!fn) return TAC_E_CUDA;
+  CUtensorMap tx, tq;
+  const cuuint64_t xd[2] = {cuuint64_t(K), cuuint64_t(M)}, xs[1] = {cuuint64_t(K) * 2};
+  const cuuint32_t xb[2] = {64, 128}, e1[2] = {1, 1};
+  const cuuint64_t qd[2] = {cuuint64_t(N), cuuint64_t(K)}, qs[1] = {cuuint64_t(N)};
+  const cuuint32_t qb[2] = {256, 64};
+  if (fn(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(X), xd, xs, xb, e1,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+      fn(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(Q), qd, qs, qb, e1, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return TAC_E_CUDA;
+  WoParams p{};
+  p.scale = scale;
+  p.bias = bias;
+  p.y = Y;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.m_tiles = (M + kWoBM - 1) / kWoBM;
+  p.n_tiles = (N + kWoBN - 1) / kWoBN;
+  p.k_blocks = (K + kWoBK - 1) / kWoBK;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p.fault), g_tc_gemm_fault) != cudaSuccess) return TAC_E_CUDA;
+  const int tiles = p.m_tiles * p.n_tiles;
+  gemm_wo_kernel<<<tiles < di.sms ? tiles : di.sms, kWoThreads, kWoSmem, st>>>(tx, tq, p);
+  return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
+}
+
+// Device address of the fault word the tcgen05 GEMM kernels record timeouts
+// in (read and cleared by tac_gemm_status); null on a CUDA error.
+int* gemm_fault_word() {
+  int* fault = nullptr;
+  return cudaGetSymbolAddress(reinterpret_cast<void**>(&fault), g_tc_gemm_fault) == cudaSuccess ? fault : nullptr;
+}
+
 int gemm_launch(const int8_t* A, const int8_t* B, void* out, const uint16_t* scale, const int32_t* mult,
                 const int32_t* shift, int M, int N, int K, int epi, void* stream, const uint16_t* act_scale,
                 const uint16_t* bias) {
@@ -306,6 +406,11 @@ extern "C" int tac_gemm_i8_requant_pc_bt(const int8_t* A, const int8_t* Bt, cons
 
 extern "C" int tac_gemm_i8_i32_bt(const int8_t* A, const int8_t* Bt, int32_t* C, int M, int N, int K, void* stream) {
   return tac::gemm_launch_ex(A, Bt, C, nullptr, nullptr, nullptr, M, N, K, tac::EPI_I32, stream, nullptr, nullptr, 1);
+}
+
+extern "C" int tac_gemm_wo_f16_i8(const uint16_t* X, const int8_t* Q, const float* scale, const float* bias, float* Y,
+                                  int M, int N, int K, void* stream) {
+  return tac::gemm_wo_launch(X, Q, scale, bias, Y, M, N, K, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int tac_gemm_status(int* fault_code) {

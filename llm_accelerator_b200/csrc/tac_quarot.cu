@@ -26,6 +26,12 @@ namespace tac {
 int gemm_launch(const int8_t* A, const int8_t* B, void* out, const uint16_t* scale, const int32_t* mult,
                 const int32_t* shift, int M, int N, int K, int epi, void* stream, const uint16_t* act_scale,
                 const uint16_t* bias);
+// The QuaRot layer's GEMM over rotated rows, quantised while staged
+// (tac_quarot_fused.cuh, launched from tac_gemm.cu).
+bool quarot_gemm_ok(const int8_t* W, const uint16_t* Y, int M, int N, int K);
+int quarot_gemm_launch(const uint16_t* xr, const uint32_t* slots, int n_slots, const int8_t* W,
+                       const uint16_t* w_scale, const uint16_t* bias, uint16_t* Y, int M, int N, int K,
+                       cudaStream_t st);
 }
 
 namespace {
@@ -37,10 +43,13 @@ using tac::sat8;
 
 constexpr int kFwhtWarps = 8;
 
+// max_bits: null (no maximum), one word for an atomicMax over the float
+// bits (per_cta 0), or one word per CTA that receives the CTA's maximum
+// (per_cta 1; no atomics and no zeroing before the launch).
 template <int E>
 __global__ void __launch_bounds__(kFwhtWarps * 32)
     fwht_kernel(const uint16_t* __restrict__ X, uint16_t* __restrict__ Y, int M, int K, float norm,
-                uint32_t* max_bits) {
+                uint32_t* max_bits, int per_cta) {
   constexpr int kBlock = 32 * E;
   const int lane = threadIdx.x & 31;
   const int nb = K / kBlock;
@@ -107,7 +116,18 @@ __global__ void __launch_bounds__(kFwhtWarps * 32)
   if (max_bits) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) atomicMax(max_bits, __float_as_uint(mx));
+    if (!per_cta) {
+      if (lane == 0) atomicMax(max_bits, __float_as_uint(mx));
+    } else {
+      __shared__ float wmax[kFwhtWarps];
+      if (lane == 0) wmax[threadIdx.x >> 5] = mx;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float m = wmax[0];
+        for (int w = 1; w < kFwhtWarps; ++w) m = fmaxf(m, wmax[w]);
+        max_bits[blockIdx.x] = __float_as_uint(m);
+      }
+    }
   }
 }
 
@@ -142,22 +162,27 @@ __global__ void quant_act_kernel(const uint16_t* __restrict__ XR, int8_t* __rest
 bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
 
-int launch_fwht(const uint16_t* X, uint16_t* Y, int M, int K, int block, uint32_t* max_bits, cudaStream_t st) {
-  if (!X || !Y || M <= 0 || K <= 0 || !pow2(block) || block < 32 || block > 1024 || K % block) return TAC_E_ARGUMENT;
-  if ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(Y)) & 15) return TAC_E_ARGUMENT;
-  const float norm = static_cast<float>(1.0 / std::sqrt(double(block)));
+int fwht_grid(int M, int K, int block) {
   const long work = long(M) * (K / block);
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long want = (work + kFwhtWarps - 1) / kFwhtWarps;
-  const int grid = int(want < long(sms) * 8 ? want : long(sms) * 8);
+  return int(want < long(sms) * 8 ? want : long(sms) * 8);
+}
+
+int launch_fwht(const uint16_t* X, uint16_t* Y, int M, int K, int block, uint32_t* max_bits, cudaStream_t st,
+                int per_cta = 0) {
+  if (!X || !Y || M <= 0 || K <= 0 || !pow2(block) || block < 32 || block > 1024 || K % block) return TAC_E_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(Y)) & 15) return TAC_E_ARGUMENT;
+  const float norm = static_cast<float>(1.0 / std::sqrt(double(block)));
+  const int grid = fwht_grid(M, K, block);
   switch (block / 32) {
-    case 1: fwht_kernel<1><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits); break;
-    case 2: fwht_kernel<2><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits); break;
-    case 4: fwht_kernel<4><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits); break;
-    case 8: fwht_kernel<8><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits); break;
-    case 16: fwht_kernel<16><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits); break;
-    default: fwht_kernel<32><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits); break;
+    case 1: fwht_kernel<1><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits, per_cta); break;
+    case 2: fwht_kernel<2><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits, per_cta); break;
+    case 4: fwht_kernel<4><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits, per_cta); break;
+    case 8: fwht_kernel<8><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits, per_cta); break;
+    case 16: fwht_kernel<16><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits, per_cta); break;
+    default: fwht_kernel<32><<<grid, kFwhtWarps * 32, 0, st>>>(X, Y, M, K, norm, max_bits, per_cta); break;
   }
   return cudaGetLastError() == cudaSuccess ? TAC_OK : TAC_E_CUDA;
 }
@@ -171,7 +196,9 @@ extern "C" int tac_fwht_f16(const uint16_t* X, uint16_t* Y, int M, int K, int bl
 extern "C" uint64_t tac_quarot_workspace_bytes(int M, int K) {
   if (M <= 0 || K <= 0) return 0;
   const uint64_t mk = uint64_t(M) * uint64_t(K);
-  return align256(mk * 2) + align256(mk) + 256;
+  // rotated FP16 rows; then their INT8 quantisation (four-launch path) or the
+  // rotation CTAs' maxima (two-launch path, at most 8 per SM); scale words
+  return align256(mk * 2) + align256(mk > 8192 ? mk : 8192) + 256;
 }
 
 extern "C" int tac_quarot_w8a16(const uint16_t* X, const int8_t* W, const uint16_t* w_scale, const uint16_t* bias,
@@ -185,7 +212,13 @@ extern "C" int tac_quarot_w8a16(const uint16_t* X, const int8_t* W, const uint16
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint16_t* xr = reinterpret_cast<uint16_t*>(ws);
   int8_t* xq = reinterpret_cast<int8_t*>(ws + align256(mk * 2));
-  uint32_t* stat = reinterpret_cast<uint32_t*>(ws + align256(mk * 2) + align256(mk));
+  uint32_t* stat = reinterpret_cast<uint32_t*>(ws + align256(mk * 2) + align256(mk > 8192 ? mk : 8192));
+  if (tac::quarot_gemm_ok(W, Y, M, N, K)) {
+    // two launches: rotation with per-CTA maxima, then the GEMM that quantises while staging A
+    uint32_t* slots = reinterpret_cast<uint32_t*>(xq);
+    if (int s = launch_fwht(X, xr, M, K, block, slots, st, 1)) return s;
+    return tac::quarot_gemm_launch(xr, slots, fwht_grid(M, K, block), W, w_scale, bias, Y, M, N, K, st);
+  }
   if (cudaMemsetAsync(stat, 0, 16, st) != cudaSuccess) return TAC_E_CUDA;
   if (int s = launch_fwht(X, xr, M, K, block, stat, st)) return s;
   int sms = 148, dev = 0;

@@ -93,6 +93,53 @@ def gemm_i8_requant_shift(A, B, mult, shift, out=None):
     return out
 
 
+def gemm_wo_f16_i8(X, Q, scale, bias=None, out=None):
+    """Y float32 [M, N] = X (float16 [M, K]) @ (Q int8 [K, N] * scale[N]) (+ bias[N]):
+    the weight-only INT8 GEMM (tac_gemm_wo_f16_i8)."""
+    import torch
+    if X.dtype != torch.float16 or Q.dtype != torch.int8 or scale.dtype != torch.float32:
+        raise TypeError("X float16, Q int8, scale float32 expected")
+    M, K = X.shape
+    if Q.shape[0] != K or scale.numel() != Q.shape[1]:
+        raise ValueError(f"shape mismatch {tuple(X.shape)} x {tuple(Q.shape)}")
+    N = Q.shape[1]
+    out = torch.empty((M, N), dtype=torch.float32, device=X.device) if out is None else out
+    L.check(L.lib.tac_gemm_wo_f16_i8(_ptr(X), _ptr(Q), _ptr(scale), None if bias is None else _ptr(bias), _ptr(out),
+                                     M, N, K, _stream()), "tac_gemm_wo_f16_i8")
+    return out
+
+
+def time_gemm_wo(M: int = 1024, N: int = 3072, K: int = 768, iters: int = 20, warmup: int = 5, seed: int = 0) -> dict:
+    """Device time of the weight-only GEMM (median, CUDA events, L2 flushed
+    before each launch) and its algorithmic bytes (X, Q, scales, bias, Y)."""
+    import numpy as np
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    X = torch.randn((M, K), generator=g, device="cuda").half()
+    Q = torch.randint(-127, 128, (K, N), dtype=torch.int8, device="cuda", generator=g)
+    S = torch.rand(N, generator=g, device="cuda") * 1e-3 + 1e-4
+    Bv = torch.randn(N, generator=g, device="cuda") * 0.02
+    Y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.int8, device="cuda")
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        gemm_wo_f16_i8(X, Q, S, Bv, out=Y)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        gemm_wo_f16_i8(X, Q, S, Bv, out=Y)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ms = float(np.median(ts))
+    nbytes = M * K * 2 + K * N + 8 * N + M * N * 4
+    return {"shape": [M, K, N], "ms": ms, "tflops": 2.0 * M * N * K / ms / 1e9, "gbs": nbytes / ms / 1e6,
+            "bytes": nbytes}
+
+
 def time_gemm(M: int, N: int, K: int, *, epilogue: str = "requant_pc", iters: int = 20, warmup: int = 5,
               seed: int = 0, compare_cublas: bool = True, b_transposed: bool = False) -> dict:
     """Device time of one stand-alone GEMM (median over `iters` launches, CUDA
