@@ -217,3 +217,41 @@ def test_batched_runner_ragged_positions():
         r.run_decode_step(t1, 1)
         want = r.run_decode_step(t2, p2)
         np.testing.assert_array_equal(br.logits("decode", seq).view(np.uint16), want.view(np.uint16))
+
+
+# ---- the reference's gen2 known-answer vectors on the engine (tests/golden/gen2_kats.npz) ----
+from test_oracle_pin import gen2_cases, gen2_setup  # noqa: E402
+
+
+@pytest.mark.parametrize("case", [c[0] for c in gen2_cases()])
+def test_engine_replays_reference_gen2_kats(case):
+    """Each gen2 vector through B200Simulator._execute: bit-exact, except the
+    transcendental GELU and masked softmax outputs (FP16_TOL)."""
+    name, meta, files = next(c for c in gen2_cases() if c[0] == case)
+    insn, s1buf, s2buf, attn = gen2_setup(meta, files)
+    sim = _sim()
+    st = sim.state
+    st.tile_config = (meta["M"] // 16 - 1, meta["N"] // 16 - 1, 0)
+    st.scale_regs[:] = np.frombuffer(files["scale_regs_pre.raw"], dtype=np.float16)
+
+    def put(buf, off, data):
+        view = st.accum.view(np.uint8) if buf == OI.ACCUM else (st.abuf if buf == OI.ABUF else st.wbuf)
+        view[off * 16:off * 16 + len(data)] = data
+
+    put(s1buf, meta["src1_off"], files["input_src1.raw"])
+    if "input_src2.raw" in files:
+        put(s2buf, meta["src2_off"], files["input_src2.raw"])
+    if attn:
+        st.attn_context = attn
+    sim._execute(insn)
+    exp = files["expected_out.raw"]
+    sregs = np.asarray(st.scale_regs).tobytes()
+    if insn.opcode == OI.MAX_ABS_REDUCE_FP32:
+        assert sregs == exp, name
+    elif exp:
+        got = bytes(st.abuf[meta["dst_off"] * 16:meta["dst_off"] * 16 + len(exp)])
+        if insn.opcode in (OI.GELU_FP32, OI.MASKED_SOFTMAX_FP32):
+            assert_fp16_close(np.frombuffer(got, np.uint8).copy(), np.frombuffer(exp, np.uint8).copy(), name)
+        else:
+            assert got == exp, name
+    assert sregs == files["scale_regs_post.raw"], name
