@@ -109,35 +109,45 @@ def gemm_wo_f16_i8(X, Q, scale, bias=None, out=None):
     return out
 
 
-def time_gemm_wo(M: int = 1024, N: int = 3072, K: int = 768, iters: int = 20, warmup: int = 5, seed: int = 0) -> dict:
-    """Device time of the weight-only GEMM (median, CUDA events, L2 flushed
-    before each launch) and its algorithmic bytes (X, Q, scales, bias, Y)."""
+def time_gemm_wo(M: int = 1024, N: int = 3072, K: int = 768, iters: int = 20, warmup: int = 5, seed: int = 0,
+                 rotate_bytes: int = 256 << 20) -> dict:
+    """Device time of the weight-only GEMM: ms in steady state (calls back to
+    back in a CUDA graph, each on its own input set of sets totalling
+    rotate_bytes, so inputs come from HBM), ms_cold for one call after a
+    256 MB write has flushed L2; algorithmic bytes X, Q, scales, bias, Y."""
     import numpy as np
     import torch
+    from .quarot import _graph_time
     g = torch.Generator(device="cuda").manual_seed(seed)
-    X = torch.randn((M, K), generator=g, device="cuda").half()
-    Q = torch.randint(-127, 128, (K, N), dtype=torch.int8, device="cuda", generator=g)
-    S = torch.rand(N, generator=g, device="cuda") * 1e-3 + 1e-4
-    Bv = torch.randn(N, generator=g, device="cuda") * 0.02
-    Y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    nbytes = M * K * 2 + K * N + 8 * N + M * N * 4
+    n_sets = max(2, -(-rotate_bytes // nbytes))
+    sets = [(torch.randn((M, K), generator=g, device="cuda").half(),
+             torch.randint(-127, 128, (K, N), dtype=torch.int8, device="cuda", generator=g),
+             torch.rand(N, generator=g, device="cuda") * 1e-3 + 1e-4,
+             torch.randn(N, generator=g, device="cuda") * 0.02,
+             torch.empty((M, N), dtype=torch.float32, device="cuda")) for _ in range(n_sets)]
+
+    def call(i):
+        X, Q, S, Bv, Y = sets[i]
+        gemm_wo_f16_i8(X, Q, S, Bv, out=Y)
+
+    ms = _graph_time(call, n_sets, 10 * n_sets)
     flush = torch.empty(256 << 20, dtype=torch.int8, device="cuda")
     stream = torch.cuda.current_stream()
     for _ in range(warmup):
-        gemm_wo_f16_i8(X, Q, S, Bv, out=Y)
+        call(0)
     torch.cuda.synchronize()
     ts = []
     for _ in range(iters):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        gemm_wo_f16_i8(X, Q, S, Bv, out=Y)
+        call(0)
         e1.record(stream)
         torch.cuda.synchronize()
         ts.append(e0.elapsed_time(e1))
-    ms = float(np.median(ts))
-    nbytes = M * K * 2 + K * N + 8 * N + M * N * 4
-    return {"shape": [M, K, N], "ms": ms, "tflops": 2.0 * M * N * K / ms / 1e9, "gbs": nbytes / ms / 1e6,
-            "bytes": nbytes}
+    return {"shape": [M, K, N], "ms": ms, "ms_cold": float(np.median(ts)), "tflops": 2.0 * M * N * K / ms / 1e9,
+            "gbs": nbytes / ms / 1e6, "bytes": nbytes, "input_sets": n_sets}
 
 
 def time_gemm(M: int, N: int, K: int, *, epilogue: str = "requant_pc", iters: int = 20, warmup: int = 5,
@@ -181,17 +191,39 @@ def time_gemm(M: int, N: int, K: int, *, epilogue: str = "requant_pc", iters: in
             ts.append(e0.elapsed_time(e1))
         return sorted(ts)[len(ts) // 2]
 
-    ms = med(fn)
+    ms_cold = med(fn)
     st = L.lib.tac_gemm_status(None)
     if st != L.OK:
         raise RuntimeError(f"GEMM kernel reported device fault status {st}")
     ops = 2.0 * M * N * K
+    # steady state: calls back to back in a CUDA graph, each on its own operand
+    # set (A, B, out) of sets totalling 256 MB, so operands come from HBM
+    from .quarot import _graph_time
+    per_set = M * K + K * N + M * N * (4 if epilogue == "i32" else 1)
+    n_sets = max(2, -(-(256 << 20) // per_set))
+    sets = [(torch.randint(-128, 128, (M, K), dtype=torch.int8, device="cuda", generator=g),
+             torch.randint(-128, 128, (K, N), dtype=torch.int8, device="cuda", generator=g),
+             torch.empty_like(out)) for _ in range(n_sets)]
+    if b_transposed:
+        sets = [(a, b.t().contiguous(), o) for a, b, o in sets]
+        one = ((lambda i: gemm_i8_i32_bt(sets[i][0], sets[i][1], sets[i][2])) if epilogue == "i32"  # noqa: E731
+               else (lambda i: gemm_i8_requant_pc_bt(sets[i][0], sets[i][1], scale, sets[i][2])))
+    elif epilogue == "i32":
+        one = lambda i: gemm_i8_i32(sets[i][0], sets[i][1], sets[i][2])  # noqa: E731
+    else:
+        one = lambda i: gemm_i8_requant_pc(sets[i][0], sets[i][1], scale, sets[i][2])  # noqa: E731
+    ms = _graph_time(one, n_sets, 10 * n_sets)
     res = {"shape": [M, N, K], "epilogue": epilogue, "b_layout": "[N,K]" if b_transposed else "[K,N]", "ms": ms,
-           "tops": ops / ms / 1e9}
+           "ms_cold": ms_cold, "tops": ops / ms / 1e9, "operand_sets": n_sets}
     if compare_cublas and M > 16:
         Bc = B.t().contiguous().t()   # column-major operand for cuBLASLt
-        cms = med(lambda: torch._int_mm(A, Bc))
-        res.update({"cublas_int_mm_ms": cms, "cublas_tops": ops / cms / 1e9})
+        cms_cold = med(lambda: torch._int_mm(A, Bc))
+        csets = [(a, b.t().contiguous().t()) for a, b, _ in sets] if not b_transposed else \
+            [(a, b.t()) for a, b, _ in sets]
+        cms = _graph_time(lambda i: torch._int_mm(csets[i][0], csets[i][1]), n_sets, 10 * n_sets)
+        res.update({"cublas_int_mm_ms": cms, "cublas_int_mm_ms_cold": cms_cold, "cublas_tops": ops / cms / 1e9})
+    if L.lib.tac_gemm_status(None) != L.OK:
+        raise RuntimeError("GEMM kernel reported a device fault")
     return res
 
 

@@ -54,42 +54,81 @@ def quarot_w8a16(X, W, scale, bias=None, block: int = 256, out=None, ws=None):
     return out
 
 
+def _graph_time(call, n_sets: int, calls: int, warmup: int = 4) -> float:
+    """Average ms per call of `calls` back-to-back calls captured in one CUDA
+    graph, call i on input set i % n_sets; the replay is timed with CUDA
+    events (median of 3), so host issue time stays out of the figure."""
+    import torch
+    for i in range(warmup):       # per-device set-up happens outside the capture
+        call(i % n_sets)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(calls):
+            call(i % n_sets)
+    graph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    times = []
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / calls)
+    del graph
+    return sorted(times)[1]
+
+
 def time_layer(M: int = 1024, K: int = 768, N: int = 3072, block: int = 256, iters: int = 20, warmup: int = 5,
-               seed: int = 0) -> dict:
-    """Device time of one layer call (median, CUDA events on the launching
-    stream, L2 flushed before each launch by writing 256 MB) on seeded inputs
-    of the layer workload's distribution: N(0, 1) activations with 1% of
-    channels x50, per-channel INT8 weights."""
+               seed: int = 0, rotate_bytes: int = 256 << 20) -> dict:
+    """Device time of one layer call on seeded inputs of the layer workload's
+    distribution (N(0, 1) activations with 1% of channels x50, per-channel
+    INT8 weights):
+      ms       steady state: calls back to back in a CUDA graph, each on its own
+               input set (X, W, scales, bias, Y) of sets totalling rotate_bytes,
+               so every call reads its inputs from HBM (average per call);
+      ms_cold  one call after a 256 MB write has flushed L2 (median of `iters`)."""
     import numpy as np
     import torch
     g = torch.Generator(device="cuda").manual_seed(seed)
-    X = torch.randn((M, K), generator=g, device="cuda", dtype=torch.float32)
-    ch = torch.randperm(K, generator=g, device="cuda")[:max(1, K // 100)]
-    X[:, ch] *= 50.0
-    X = X.half()
-    W = torch.randint(-127, 128, (K, N), dtype=torch.int8, device="cuda", generator=g)
-    S = (torch.rand(N, generator=g, device="cuda") * 1e-3 + 1e-4).half()
-    Bv = (torch.randn(N, generator=g, device="cuda") * 0.02).half()
-    Y = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    per_set = M * K * 2 + K * N + 4 * N + M * N * 2
+    n_sets = max(2, -(-rotate_bytes // per_set))
+    sets = []
+    for _ in range(n_sets):
+        X = torch.randn((M, K), generator=g, device="cuda", dtype=torch.float32)
+        ch = torch.randperm(K, generator=g, device="cuda")[:max(1, K // 100)]
+        X[:, ch] *= 50.0
+        W = torch.randint(-127, 128, (K, N), dtype=torch.int8, device="cuda", generator=g)
+        S = (torch.rand(N, generator=g, device="cuda") * 1e-3 + 1e-4).half()
+        Bv = (torch.randn(N, generator=g, device="cuda") * 0.02).half()
+        sets.append((X.half(), W, S, Bv, torch.empty((M, N), dtype=torch.float16, device="cuda")))
     ws = workspace(M, K)
+
+    def call(i):
+        X, W, S, Bv, Y = sets[i]
+        quarot_w8a16(X, W, S, Bv, block, out=Y, ws=ws)
+
+    ms = _graph_time(call, n_sets, 10 * n_sets)
     flush = torch.empty(256 << 20, dtype=torch.int8, device="cuda")
     stream = torch.cuda.current_stream()
     for _ in range(warmup):
-        quarot_w8a16(X, W, S, Bv, block, out=Y, ws=ws)
+        call(0)
     torch.cuda.synchronize()
     ts = []
     for _ in range(iters):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        quarot_w8a16(X, W, S, Bv, block, out=Y, ws=ws)
+        call(0)
         e1.record(stream)
         torch.cuda.synchronize()
         ts.append(e0.elapsed_time(e1))
-    ms = float(np.median(ts))
+    ms_cold = float(np.median(ts))
     flops = 2.0 * M * N * K
     # algorithmic bytes: X in, W + scales + bias in, Y out (the rotated rows
     # pass through the workspace, and L2, between the two launches)
-    hbm = M * K * 2 + K * N + 4 * N + M * N * 2
-    return {"shape": [M, K, N], "block": block, "ms": ms, "tflops": flops / ms / 1e9,
-            "gbs": hbm / ms / 1e6, "bytes": hbm}
+    hbm = per_set
+    return {"shape": [M, K, N], "block": block, "ms": ms, "ms_cold": ms_cold, "tflops": flops / ms / 1e9,
+            "gbs": hbm / ms / 1e6, "bytes": hbm, "input_sets": n_sets}

@@ -13,6 +13,7 @@ checkout at /root/reference.
 from __future__ import annotations
 
 import hashlib
+import os
 import sys
 from pathlib import Path
 
@@ -20,7 +21,7 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
-sys.path.insert(0, "/root/reference/software")
+sys.path.insert(0, str(Path(os.environ.get("TACCEL_REFERENCE", "/root/reference")) / "software"))
 
 from oracle.ptq import rotation_case, weight_case  # noqa: E402
 from taccel.quantizer.rotation import build_random_orthogonal, rotate_residual_stream_state_dict  # noqa: E402

@@ -13,6 +13,7 @@ Run from the repository root with the reference checkout at /root/reference.
 from __future__ import annotations
 
 import hashlib
+import os
 import sys
 from pathlib import Path
 
@@ -20,7 +21,7 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
-sys.path.insert(0, "/root/reference/software")
+sys.path.insert(0, str(Path(os.environ.get("TACCEL_REFERENCE", "/root/reference")) / "software"))
 
 from oracle.quarot import layer_inputs  # noqa: E402
 from taccel.quantizer.rotation import _sylvester_hadamard  # noqa: E402

@@ -54,8 +54,8 @@ def test_fwht_is_the_dense_block_hadamard(block):
 
 @pytest.mark.reference
 def test_w8a16_restatement_matches_reference_function_directly():
-    import sys
-    sys.path.insert(0, "/root/reference/software")
+    from helpers import import_reference
+    assert import_reference()
     from taccel.runtime.w8a16_simulator_reference import _w8a16_dynamic_matmul
     for seed in range(3):
         x, w, s, b = Q.layer_inputs(32, 512, 128, seed=seed)
