@@ -147,9 +147,12 @@ typedef struct tac_compile_opts {
   uint32_t n_live;
   int32_t sram_live;
   int32_t sregs_live;
-  int32_t reserved;
+  int32_t flags;          /* TAC_COMPILE_* bits */
   const uint64_t* live;   /* [n_live][2] byte ranges [lo, hi) */
 } tac_compile_opts;
+/* Keep every intermediate in an arena extent of its own (no reuse by
+ * liveness): plan checks that overwrite rows no op reads use it. */
+#define TAC_COMPILE_NO_PACK 1
 
 int tac_compile_ex(int batch, uint64_t dram_bytes, uint64_t shared_bytes,
                    const uint8_t* insn_bytes, uint64_t n_insns, uint64_t entry_pc,

@@ -49,9 +49,12 @@ class ExecInfo(C.Structure):
                 ("final_regs", Regs)]
 
 
+COMPILE_NO_PACK = 1   # TAC_COMPILE_NO_PACK
+
+
 class CompileOpts(C.Structure):
     _fields_ = [("n_live", C.c_uint32), ("sram_live", C.c_int32), ("sregs_live", C.c_int32),
-                ("reserved", C.c_int32), ("live", C.c_void_p)]
+                ("flags", C.c_int32), ("live", C.c_void_p)]
 
 
 _P = C.c_void_p

@@ -98,6 +98,7 @@ class Compiler {
   int compile();
   void prefetch_hint(const DevOp& op, Task& t) const;
   void drop_dead_ops();
+  void drop_dead_walk(std::vector<uint8_t>& keep, const std::vector<uint64_t>& chain_units);
   void merge_dyn_stores();
   void write_vadd_chains();
   int link_pv_pairs();
@@ -946,6 +947,7 @@ class Compiler {
   // per emitted op: its arena reads and writes, and whether arena writes are its only effect
   std::vector<std::vector<std::pair<uint64_t, uint64_t>>> op_arena_reads_, op_arena_writes_;
   std::vector<uint8_t> op_pure_;
+  uint64_t narrowed_ops_ = 0;   // ops drop_dead_ops narrowed to the rows read
   // site i's group: the first address site with the same value range; sites of
   // one group are assumed (and checked at run time) to carry one value
   std::vector<int> site_group_;
@@ -1704,15 +1706,134 @@ void Compiler::finalize() {
   }
 }
 
+// Row structure of a row-wise op: output row r depends only on row r of its
+// row operands (plus vectors, weights and registers every row shares), so rows
+// that no later op reads need not be computed.  Gives the element bytes of the
+// row operands; a tcgen05 MATMUL (shared weights, no accumulate, at most the
+// DEQUANT_SCALED epilogue) counts, its A rows being K int8 bytes.
+static bool row_wise(const DevOp& op, uint32_t& in_es) {
+  switch (op.kind) {
+    case K_VADD_F16: case K_GELU_F16: in_es = 2; return op.flags2 == 0 && (op.flags & ~F_SEGA) == 0;
+    case K_QUANT: in_es = 2; return op.flags2 == 0 && (op.flags & ~F_SEGA) == 0;
+    case K_LAYERNORM_F16: in_es = 2; return op.flags2 == 0 && (op.flags & ~F_SPLIT) == 0;
+    case K_SOFTMAX_F16: in_es = 2; return op.flags2 == 0 && op.flags == 0;
+    case K_MASKED_SOFTMAX_F16: in_es = 2; return op.flags2 == 0 && (op.flags & ~F_ATTN_DYN) == 0;
+    case K_DEQUANT_ACCUM: in_es = 4; return op.flags2 == 0 && op.flags == 0;
+    case K_DEQUANT_SCALED: in_es = 4; return op.flags2 == 0 && (op.flags & ~F_SPLIT) == 0;
+    case K_VADD_CHAIN: in_es = 2; return op.flags2 == 0 && op.flags == 0;
+    case K_MATMUL:
+      in_es = 1;
+      return tc_eligible(op.a, op.b, op.M, op.N, op.K) && (op.flags & ~F_NOI32) == 0 &&
+             (op.flags2 & ~FX_DQS) == 0 && (!(op.flags & F_NOI32) || (op.flags2 & FX_DQS));
+    default: return false;
+  }
+}
+
+// The outputs of a row-wise op as (first unit, units per row): its
+// destination, a chain's stored sums, a MATMUL's int32 and FP16 results.
+static std::vector<std::pair<uint64_t, uint64_t>> row_outputs(const DevOp& op, const std::vector<Segment>* chain) {
+  std::vector<std::pair<uint64_t, uint64_t>> o;
+  const uint64_t n = op.N;
+  switch (op.kind) {
+    case K_VADD_CHAIN:
+      for (size_t k = 1; k < chain->size(); ++k)
+        if ((*chain)[k].dst) o.push_back({(*chain)[k].dst, n * 2 / kUnit});
+      break;
+    case K_QUANT: o.push_back({op.d, n / kUnit}); break;
+    case K_MATMUL:
+      if (!(op.flags & F_NOI32)) o.push_back({op.d, n * 4 / kUnit});
+      if (op.flags2 & FX_DQS) o.push_back({static_cast<uint64_t>(op.dconst), n * 2 / kUnit});
+      break;
+    default: o.push_back({op.d, n * 2 / kUnit}); break;
+  }
+  return o;
+}
+
+// The ranges a row-wise op reads when it computes rows [0, m): the first m
+// rows of each row operand (for a segment list, the runs' parts below m rows)
+// and every vector operand whole.  `chain` holds a K_VADD_CHAIN's operands.
+template <class F>
+static void row_reads(const DevOp& op, uint32_t m, uint32_t in_es, const std::vector<Segment>& segs,
+                      const std::vector<Segment>* chain, F&& cb) {
+  const uint64_t ri = uint64_t(op.kind == K_MATMUL ? op.K : op.N) * in_es / kUnit, lim = m * ri;
+  auto rows = [&](uint64_t p) { cb(p, lim); };
+  auto vec = [&](uint64_t p, uint64_t bytes) { cb(p, (bytes + kUnit - 1) / kUnit); };
+  auto seglist = [&]() {
+    for (uint32_t k = op.seg0; k < op.seg0 + op.nseg; ++k)
+      if (segs[k].dst < lim) cb(segs[k].src, std::min<uint64_t>(segs[k].n, lim - segs[k].dst));
+  };
+  const uint64_t vn = uint64_t(op.N) * 2;
+  switch (op.kind) {
+    case K_VADD_F16: (op.flags & F_SEGA) ? seglist() : rows(op.a); rows(op.b); break;
+    case K_GELU_F16: case K_QUANT: (op.flags & F_SEGA) ? seglist() : rows(op.a); break;
+    case K_SOFTMAX_F16: case K_MASKED_SOFTMAX_F16: rows(op.a); break;
+    case K_LAYERNORM_F16: case K_DEQUANT_SCALED:
+      rows(op.a);
+      if (op.flags & F_SPLIT) { vec(op.b, vn); vec(op.c, vn); } else vec(op.b, 2 * vn);
+      break;
+    case K_DEQUANT_ACCUM: rows(op.a); vec(op.b, vn); break;
+    case K_VADD_CHAIN:
+      for (const Segment& c : *chain) rows(c.src);
+      break;
+    case K_MATMUL:
+      rows(op.a);
+      vec(op.b, uint64_t(op.K) * op.N);
+      if (op.flags2 & FX_DQS) { vec(op.c, vn); vec(op.nbytes, vn); }
+      break;
+    default: break;
+  }
+}
+
 // Removes ops whose only effect is arena extents no kept op reads (a
 // TRANSPOSE whose MATMUL reads its source instead, a value overwritten before
 // use).  Walks the ops backwards, keeping an op when it has another effect or
 // a kept op reads any unit it writes.
+//
+// A kept row-wise op whose later rows no kept op reads is narrowed to the
+// rows that are read (M becomes that count, m_decl keeps the tile's rows),
+// and only those rows of its row operands count as read; an FX_MAXQ MAX_ABS
+// stores only the QUANT rows that are read (q_rows).  The decode streams
+// reload their padding rows from a constant region before every MAX_ABS, so
+// most row-wise work on them is dead.  A row-wise op is narrowed only when
+// the reads it recorded while compiling are exactly the ranges row_reads
+// gives for all of its rows.
 void Compiler::drop_dead_ops() {
   const size_t n = P->ops.size();
   if (op_arena_reads_.size() != n || op_arena_writes_.size() != n || op_pure_.size() != n) return;
+  // A K_VADD_CHAIN op sits at the index of its first VADD but reads operands
+  // that ops emitted after it produce, so the walk meets those producers
+  // first: the chain's reads of them are marked up front.  A first walk marks
+  // them whole and finds the rows each chain computes; a second walk, from
+  // the ops as they were, marks only those rows (the chains' readers all come
+  // after their operands' producers, so the rows found do not change).
+  const std::vector<DevOp> ops0 = P->ops;
+  const auto chains0 = chains_;
+  std::vector<uint64_t> chain_units(chains_.size(), ~0ull);   // units of each operand a chain reads
+  std::vector<uint8_t> keep;
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass) {
+      P->ops = ops0;
+      chains_ = chains0;
+      narrowed_ops_ = 0;
+    }
+    drop_dead_walk(keep, chain_units);
+    if (chains_.empty()) break;
+    for (size_t i = 0; i < n; ++i)
+      if (keep[i] && P->ops[i].kind == K_VADD_CHAIN) chain_units[ops0[i].param] = chains_[ops0[i].param][0].n;
+  }
+  size_t j = 0;
+  for (size_t i = 0; i < n; ++i)
+    if (keep[i]) P->ops[j++] = P->ops[i];
+  dead_ops_ = n - j;
+  P->ops.resize(j);
+}
+
+// One backward walk of drop_dead_ops: sets keep[] and narrows the kept ops;
+// chain_units bounds the up-front marks of each chain's later operands.
+void Compiler::drop_dead_walk(std::vector<uint8_t>& keep, const std::vector<uint64_t>& chain_units) {
+  const size_t n = P->ops.size();
   std::vector<uint8_t> read(arena_top_, 0);
-  std::vector<uint8_t> keep(n, 0);
+  keep.assign(n, 0);
   auto mark = [&](uint64_t phys, uint64_t units) {
     for (uint64_t u = 0; u < units; ++u) {
       const uint64_t k = phys - arena_base_ + u;
@@ -1726,12 +1847,10 @@ void Compiler::drop_dead_ops() {
     }
     return false;
   };
-  // A K_VADD_CHAIN op sits at the index of its first VADD but reads operands
-  // that ops emitted after it produce: those reads are marked up front (a
-  // chain whose sum nobody reads would keep its operands' producers, which
-  // the decode streams never have).
-  for (const auto& ch : chains_)
-    for (size_t k = 2; k < ch.size(); ++k) mark(ch[k].src, ch[k].n);
+  // a chain's later operands, marked up front (a chain whose sum nobody reads
+  // would keep its operands' producers, which the decode streams never have)
+  for (size_t c = 0; c < chains_.size(); ++c)
+    for (size_t k = 2; k < chains_[c].size(); ++k) mark(chains_[c][k].src, std::min(chains_[c][k].n, chain_units[c]));
   for (size_t i = n; i-- > 0;) {
     bool live = !op_pure_[i];
     for (auto& w : op_arena_writes_[i]) live = live || any_read(w.first, w.second);
@@ -1755,13 +1874,55 @@ void Compiler::drop_dead_ops() {
       for (size_t k = 1; k + 1 < ch.size(); ++k)
         if (ch[k].dst && !any_read(ch[k].dst, ch[k].n)) ch[k].dst = 0;
     }
+    if (op.kind == K_MAX_ABS && (op.flags2 & FX_MAXQ) && op.N % kUnit == 0) {
+      const uint64_t ro = op.N / kUnit;   // int8 QUANT rows
+      uint32_t m = op.M;
+      while (m > 0 && !any_read(op.d + (m - 1) * ro, ro)) --m;
+      if (m < op.M) {
+        op.q_rows = m > 0 ? m : 1;
+        ++narrowed_ops_;
+      }
+    }
+    uint32_t in_es = 0;
+    if (op_pure_[i] && row_wise(op, in_es) && (uint64_t(op.K) * in_es) % kUnit == 0 &&
+        (uint64_t(op.N) * in_es) % kUnit == 0 && op.N % kUnit == 0) {
+      const std::vector<Segment>* chain = op.kind == K_VADD_CHAIN ? &chains_[op.param] : nullptr;
+      const auto outs = row_outputs(op, chain);
+      auto row_read = [&](uint32_t r) {
+        for (auto& o : outs)
+          if (any_read(o.first + r * o.second, o.second)) return true;
+        return false;
+      };
+      uint32_t m = op.M;
+      while (m > 1 && !row_read(m - 1)) --m;
+      if (op.kind == K_MATMUL)   // 128 / m sequences share one tensor-core tile
+        while (!tc_rows_ok(m) && m < op.M) ++m;
+      if (m < op.M) {
+        // the recorded reads must be exactly row_reads over every row
+        std::vector<uint64_t> want, got;
+        auto units = [&](std::vector<uint64_t>& v, uint64_t p, uint64_t n) {
+          if (cls(p) != PC_ARENA) return;
+          for (uint64_t u = 0; u < n; ++u) v.push_back(p + u);
+        };
+        row_reads(op, op.M, in_es, P->segs, chain, [&](uint64_t p, uint64_t n) { units(want, p, n); });
+        for (auto& r : op_arena_reads_[i]) units(got, r.first, r.second);
+        std::sort(want.begin(), want.end());
+        want.erase(std::unique(want.begin(), want.end()), want.end());
+        std::sort(got.begin(), got.end());
+        got.erase(std::unique(got.begin(), got.end()), got.end());
+        if (want == got) {
+          op.m_decl = op.M;
+          op.M = m;
+          if (chain)
+            for (Segment& c : chains_[op.param]) c.n = uint64_t(m) * op.N * 2 / kUnit;
+          row_reads(op, m, in_es, P->segs, chain, mark);
+          ++narrowed_ops_;
+          continue;
+        }
+      }
+    }
     for (auto& r : op_arena_reads_[i]) mark(r.first, r.second);
   }
-  size_t j = 0;
-  for (size_t i = 0; i < n; ++i)
-    if (keep[i]) P->ops[j++] = P->ops[i];
-  dead_ops_ = n - j;
-  P->ops.resize(j);
 }
 
 // Each FX_PV op names its P.V op (seg0) by index in the final op list: the
@@ -2349,7 +2510,7 @@ int Compiler::compile() {
   merge_dyn_stores();
   write_vadd_chains();
   if (int s = link_pv_pairs()) return s;
-  pack_arena();
+  if (!opts_ || !(opts_->flags & TAC_COMPILE_NO_PACK)) pack_arena();
   build_tasks();
 
   tac_exec_info& I = P->info;

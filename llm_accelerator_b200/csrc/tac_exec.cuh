@@ -905,9 +905,14 @@ __device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr, uint32_t lbo, uint
 // One warp's slice of the tcgen05 MATMUL epilogue: TMEM lanes 32q..32q+31,
 // columns 32h..32h+31 of the task's tile, to int32 rows (plus the previous
 // int32 tile when F_ACCUMULATE).
+// Shared memory the tcgen05 task's epilogue reads, past its operand stages:
+// the DEQUANT_SCALED scale and bias of the tile's columns (FP16, 128 each)
+// and the activation-scale register of each of the 128 rows.
+constexpr uint32_t kTcEpiBytes = 768;
+
 __device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp& op, const Task& t, TcShared* tc,
                                                   uint32_t q, uint32_t lane, uint32_t h, uint32_t n0,
-                                                  uint32_t ncols, uint32_t rows) {
+                                                  uint32_t ncols, uint32_t rows, const uint8_t* epi) {
   const uint32_t M = op.M, N = op.N;
   uint32_t v[32];
   __syncwarp();
@@ -921,16 +926,21 @@ __device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp
     if (op.flags2 & FX_DQS) {
       // DEQUANT_ACCUM_FP32_SCALED: f16((f32(acc) * scale[col]) * s0 + bias[col]); the rows are the same
       // for every lane of the warp
-      const uint16_t* sc = reinterpret_cast<const uint16_t*>(pptr(A, op.c, seq)) + col0;
-      const uint16_t* bi = reinterpret_cast<const uint16_t*>(pptr(A, op.nbytes, seq)) + col0;
-      const float s0 = h2f(sreg_bits(A, op.s[0], seq));
+      // scale, bias and this row's activation scale staged in shared memory
+      // (epi) when the vectors are shared, else read for the row's sequence
+      const bool staged = epi != nullptr;
+      const float s0 = h2f(staged ? reinterpret_cast<const uint16_t*>(epi + 512)[r] : sreg_bits(A, op.s[0], seq));
+      const uint16_t* sc = staged ? reinterpret_cast<const uint16_t*>(epi) + h * 32
+                                  : reinterpret_cast<const uint16_t*>(pptr(A, op.c, seq)) + col0;
+      const uint16_t* bi = staged ? reinterpret_cast<const uint16_t*>(epi + 256) + h * 32
+                                  : reinterpret_cast<const uint16_t*>(pptr(A, op.nbytes, seq)) + col0;
       uint16_t* O = reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(op.dconst), seq)) +
                     uint64_t(row) * N + col0;
 #pragma unroll
       for (uint32_t j = 0; j < 32; j += 8) {
         if (j < nc) {
-          const uint4 s8 = __ldcg(reinterpret_cast<const uint4*>(sc + j));
-          const uint4 b8 = __ldcg(reinterpret_cast<const uint4*>(bi + j));
+          const uint4 s8 = staged ? *reinterpret_cast<const uint4*>(sc + j) : __ldcg(reinterpret_cast<const uint4*>(sc + j));
+          const uint4 b8 = staged ? *reinterpret_cast<const uint4*>(bi + j) : __ldcg(reinterpret_cast<const uint4*>(bi + j));
           uint16_t hh[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
@@ -963,8 +973,21 @@ __device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp
   }
 }
 
+// The weight tiles a tcgen05 MATMUL task streams (its B column slice over
+// every K chunk), pulled into L2 by TMA prefetches, and its tensor maps into
+// the descriptor cache; other tasks need nothing here.
+__device__ __forceinline__ void prefetch_task_weights(const ExecArgs& A, const Task& t) {
+  const DevOp& op = A.ops[t.op];
+  if (op.kind != K_MATMUL || !(op.flags & F_TC)) return;
+  const CUtensorMap* ma = A.tmaps + 2 * op.seg0;
+  sm100::prefetch_tmap(ma);
+  sm100::prefetch_tmap(ma + 1);
+  const uint32_t tn = (op.flags & F_TC128) ? 128u : 64u;
+  for (uint32_t c = 0; c * 128 < op.K; ++c) sm100::tma_prefetch_2d(ma + 1, int32_t(t.tile * tn), int32_t(c * 128));
+}
+
 __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem,
-                                          TcShared* tc, uint32_t opi) {
+                                          TcShared* tc, uint32_t opi, uint32_t next_ti) {
   const uint32_t M = op.M, N = op.N, K = op.K;
   // tile width: 128 columns (B box 128 x 128, 128-byte swizzle, two 32 KB
   // stages) or 64 (B box 64 x 128, 64-byte swizzle, three 24 KB stages)
@@ -977,28 +1000,55 @@ __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, co
   const uint32_t rows = t.nseq * M;                       // <= 128
   const uint32_t nchunks = (K + 127) / 128;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023));
-  if (htid() == 0) {
-    const CUtensorMap* ma = A.tmaps + 2 * op.seg0;
-    const CUtensorMap* mb = ma + 1;
+  const CUtensorMap* ma = A.tmaps + 2 * op.seg0;
+  const CUtensorMap* mb = ma + 1;
+  // Chunk c uses stage c % nst for the (c / nst)-th time in this task: its
+  // full and empty barriers complete the phase of that parity relative to
+  // the task's start, whichever thread waits.  Each stage advances by one
+  // phase per chunk that uses it.
+  const uint32_t warp = htid() >> 5, lane = htid() & 31, q = warp & 3;
+  // The DEQUANT_SCALED scale and bias of the tile's columns (when shared by
+  // every sequence) and each row's activation scale go to shared memory from
+  // warps 3 and 4, idle while the K loop runs.
+  uint8_t* epi = (op.flags2 & FX_DQS) && (op.c & kSharedBit) && (op.nbytes & kSharedBit)
+                     ? base + nst * stage_bytes : nullptr;
+  if (epi && warp == 3) {
+    const uint32_t nv = (ncols + 7) / 8;   // 16-byte vectors of each row
+    for (uint32_t i = lane; i < 2 * nv; i += 32) {
+      const uint8_t* src = i < nv ? pptr(A, op.c, t.seq0) + (uint64_t(n0) + i * 8) * 2
+                                  : pptr(A, op.nbytes, t.seq0) + (uint64_t(n0) + (i - nv) * 8) * 2;
+      *reinterpret_cast<uint4*>(epi + (i < nv ? i * 16 : 256 + (i - nv) * 16)) = __ldcg(reinterpret_cast<const uint4*>(src));
+    }
+  } else if (epi && warp == 4) {
+    for (uint32_t r = lane; r < rows; r += 32)
+      reinterpret_cast<uint16_t*>(epi + 512)[r] = sreg_bits(A, op.s[0], t.seq0 + r / M);
+  }
+  const uint32_t pf0 = tc->phase_full, pe0 = tc->phase_empty;
+  auto parity = [&](uint32_t ph0, uint32_t c) { return ((ph0 >> (c % nst)) ^ (c / nst)) & 1u; };
+  uint32_t flip = 0;
+  for (uint32_t st = 0; st < nst; ++st)
+    if (((nchunks + nst - 1 - st) / nst) & 1u) flip |= 1u << st;
+  if (htid() == 32) {
+    // producer (warp 1): TMA loads; a stage is refilled once the MMAs of the
+    // chunk before it in that stage have completed
     const uint32_t bytes = (128 / M) * M * 128 + tn * 128;
-    uint32_t pf = tc->phase_full, pe = tc->phase_empty;
     bool ok = true;
-    auto load = [&](uint32_t c) {
+    sm100::fence_proxy_async();   // A was written by generic stores in earlier levels
+    for (uint32_t c = 0; c < nchunks; ++c) {
       const uint32_t st = c % nst;
+      if (c >= nst && !sm100::mbar_wait(&tc->empty[st], parity(pe0, c - nst), nullptr, 0)) ok = false;
       uint8_t* as = base + st * stage_bytes;
       sm100::mbar_arrive_expect_tx(&tc->full[st], bytes);
       sm100::tma_load_3d(as, ma, int32_t(c * 128), 0, int32_t(t.seq0), &tc->full[st]);
       sm100::tma_load_2d(as + kTcAStage, mb, int32_t(n0), int32_t(c * 128), &tc->full[st]);
-    };
-    auto wait = [&](uint64_t* bar, uint32_t& ph, uint32_t st) {
-      if (!sm100::mbar_wait(&bar[st], (ph >> st) & 1u, nullptr, 0)) ok = false;
-      ph ^= 1u << st;
-    };
-    sm100::fence_proxy_async();   // A was written by generic stores in earlier levels
-    for (uint32_t c = 0; c < nchunks && c < nst; ++c) load(c);
+    }
+    if (!ok) raise_fault(A, DF_MMA_TIMEOUT, opi, t.seq0);
+  } else if (htid() == 0) {
+    // MMA issuer (warp 0)
+    bool ok = true;
     for (uint32_t c = 0; c < nchunks; ++c) {
       const uint32_t st = c % nst;
-      wait(tc->full, pf, st);
+      if (!sm100::mbar_wait(&tc->full[st], parity(pf0, c), nullptr, 0)) ok = false;
       sm100::tc_fence_after();
       const uint32_t a_addr = sm100::smem_u32(base + st * stage_bytes), b_addr = a_addr + kTcAStage;
       const uint32_t kc = K - c * 128 < 128 ? K - c * 128 : 128;
@@ -1011,25 +1061,23 @@ __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, co
                       w128 ? kTcIdesc128 : kTcIdesc, (c | ks) != 0);
       }
       sm100::mma_commit(&tc->empty[st]);
-      if (c + nst < nchunks) {   // refill this stage once its MMAs are done
-        wait(tc->empty, pe, st);
-        load(c + nst);
-      }
     }
-    // the commits not yet waited: every MMA of the task is done after these
-    for (uint32_t j = nchunks > nst ? nchunks - nst : 0; j < nchunks; ++j) wait(tc->empty, pe, j % nst);
-    tc->phase_full = pf;
-    tc->phase_empty = pe;
+    // the commits the producer does not wait for: every MMA of the task is done after these
+    for (uint32_t c = nchunks > nst ? nchunks - nst : 0; c < nchunks; ++c)
+      if (!sm100::mbar_wait(&tc->empty[c % nst], parity(pe0, c), nullptr, 0)) ok = false;
     if (!ok) raise_fault(A, DF_MMA_TIMEOUT, opi, t.seq0);
+  } else if (htid() == 64 && next_ti != 0xFFFFFFFFu) {
+    prefetch_task_weights(A, A.tasks[next_ti]);   // warp 2 is idle during the K loop
   }
   hsync();
   sm100::tc_fence_after();
-
+  if (htid() == 0) {   // every thread has read the parities at the start (before the hsync above)
+    tc->phase_full = pf0 ^ flip;
+    tc->phase_empty = pe0 ^ flip;
+  }
   // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31; with 64 columns it
   // takes columns 32 (w / 4) .. +31, with 128 columns two such slices
-  const uint32_t warp = htid() >> 5, lane = htid() & 31, q = warp & 3;
-  for (uint32_t hh = warp >> 2; hh * 32 < tn; hh += 2)
-    tc_epilogue_slice(A, op, t, tc, q, lane, hh, n0, ncols, rows);
+  for (uint32_t hh = warp >> 2; hh * 32 < tn; hh += 2) tc_epilogue_slice(A, op, t, tc, q, lane, hh, n0, ncols, rows, epi);
   // the next tcgen05 MATMUL overwrites the accumulator only after every warp read it
   sm100::tc_fence_before();
   hsync();
@@ -1574,7 +1622,8 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
     // QUANT's rule with the inverse scale just derived: rint(x * inv), NaN -> 0, clipped to int8
     const float s0 = h2f(static_cast<uint16_t>(red[kWarps]));
     int8_t* out = reinterpret_cast<int8_t*>(pptr(A, op.d, seq));
-    for (uint64_t g = htid(); g < ng; g += kThreads) {
+    const uint64_t nq = op.q_rows ? uint64_t(op.q_rows) * op.N / 8 : ng;   // rows of the result some op reads
+    for (uint64_t g = htid(); g < nq; g += kThreads) {
       const uint4 x8 = keep[g];
       int8_t q8[8];
 #pragma unroll
@@ -1749,7 +1798,106 @@ __device__ __forceinline__ void row_one(const ExecArgs& A, const DevOp& op, uint
   }
 }
 
+// FP16 LayerNorm of one or two rows (a decode step's live row) with every warp
+// of the half, for rows whose NumPy pairwise-summation tree is balanced (nl <=
+// 8 leaves of L elements, pw_balanced): warp w sums leaf w, lanes 0..7 one of
+// its eight accumulator chains each, combined ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7))
+// by xor shuffles (IEEE addition commutes); the leaf sums then combine level
+// by level, as the tree does.  Arithmetic per element is row_one's.
+__device__ __forceinline__ bool ln_small_ok(const DevOp& op) {
+  uint32_t nl, L;
+  return op.kind == K_LAYERNORM_F16 && op.M <= 2 && op.N % 8 == 0 && op.N <= kRowCap && pw_balanced(op.N, nl, L);
+}
+
+__device__ __noinline__ void op_ln_small(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+  const uint32_t warp = htid() >> 5, lane = htid() & 31, seq = t.seq0, N = op.N;
+  uint32_t nl, L;
+  pw_balanced(N, nl, L);
+  float* x = reinterpret_cast<float*>(smem);   // the row as float32
+  float* part = x + kRowCap;                   // leaf sums: [0, 8) the row, [8, 16) the squares
+  const uint8_t* gb = pptr(A, op.b, seq);
+  const uint8_t* be = (op.flags & F_SPLIT) ? pptr(A, op.c, seq) : gb + uint64_t(N) * 2;
+  const float eps = 1e-5f;
+  const uint32_t n4 = N / 4;   // output groups of 4 elements
+  const bool has4 = htid() < n4;
+  uint2 gv = make_uint2(0, 0), bv = make_uint2(0, 0);
+  if (has4) {   // gamma and beta of this thread's outputs, in flight during the sums
+    gv = __ldcg(reinterpret_cast<const uint2*>(gb) + htid());
+    bv = __ldcg(reinterpret_cast<const uint2*>(be) + htid());
+  }
+  auto leaf_sums = [&](bool sq, float mean, float* out) {
+    float v = 0.f;
+    if (warp < nl && lane < 8) {
+      const float* q = x + warp * L + lane;
+      float r;
+      if (sq) {
+        const float d0 = __fsub_rn(q[0], mean);
+        r = __fmul_rn(d0, d0);
+        for (uint32_t i = 8; i < L; i += 8) {
+          const float d = __fsub_rn(q[i], mean);
+          r = __fadd_rn(r, __fmul_rn(d, d));
+        }
+      } else {
+        r = q[0];
+        for (uint32_t i = 8; i < L; i += 8) r = __fadd_rn(r, q[i]);
+      }
+      v = r;
+    }
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+    if (lane == 0 && warp < nl) out[warp] = v;
+  };
+  auto tree = [&](const float* leaf) {
+    float s[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s[k] = leaf[k < int(nl) ? k : 0];
+    for (uint32_t w = nl; w > 1; w >>= 1)
+#pragma unroll
+      for (uint32_t k = 0; k < 4; ++k)
+        if (k < w / 2) s[k] = __fadd_rn(s[2 * k], s[2 * k + 1]);
+    return s[0];
+  };
+  for (uint32_t r = 0; r < op.M; ++r) {
+    if (r) hsync();   // the previous row's readers are done with x and part
+    const uint4* src = reinterpret_cast<const uint4*>(pptr(A, op.a, seq) + uint64_t(r) * N * 2);
+    for (uint32_t g = htid(); g < N / 8; g += kThreads) {
+      const uint4 v = __ldcg(src + g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[g * 8 + j] = h2f(h_at(v, j));
+    }
+    hsync();
+    leaf_sums(false, 0.f, part);
+    hsync();
+    const float mean = div_count(tree(part), N);
+    leaf_sums(true, mean, part + 8);
+    hsync();
+    const float var = div_count(tree(part + 8), N);
+    const float denom = __fsqrt_rn(__fadd_rn(var, eps));
+    if (has4) {
+      const float4 xv = *reinterpret_cast<const float4*>(x + htid() * 4);
+      const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+      const uint16_t* g16 = reinterpret_cast<const uint16_t*>(&gv);
+      const uint16_t* b16 = reinterpret_cast<const uint16_t*>(&bv);
+      uint16_t h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float y = __fdiv_rn(__fsub_rn(xs[j], mean), denom);
+        h[j] = f2h(__fadd_rn(__fmul_rn(y, h2f(g16[j])), h2f(b16[j])));
+      }
+      uint2 o;
+      o.x = uint32_t(h[0]) | (uint32_t(h[1]) << 16);
+      o.y = uint32_t(h[2]) | (uint32_t(h[3]) << 16);
+      *reinterpret_cast<uint2*>(pptr(A, op.d, seq) + (uint64_t(r) * N + htid() * 4) * 2) = o;
+    }
+  }
+}
+
 __device__ __noinline__ void op_rows(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem, uint32_t opi) {
+  if (ln_small_ok(op)) {
+    op_ln_small(A, op, t, smem);
+    return;
+  }
   const int warp = htid() >> 5, lane = htid() & 31;
   const uint32_t seq = t.seq0, N = op.N;
   const uint32_t rpt = row_task_rows(op.kind, N), rpw = rpt / 8;   // rows per task, per warp
@@ -1922,6 +2070,7 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     prefetch_task_operand(A, tn);
     if (next2_ti != 0xFFFFFFFFu) prefetch_l1(A.tasks + next2_ti);
   }
+
   const Task& t = A.tasks[ti];   // read in place (L1), not copied to local memory
   const DevOp& op = A.ops[t.op];
   switch (op.kind) {
@@ -1933,7 +2082,7 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     case K_SREG_LOAD: op_sreg_load(A, op, t); break;
     case K_SREG_FINAL: op_sreg_final(A, op, t); break;
     case K_MATMUL:
-      if (op.flags & F_TC) op_matmul_tc(A, op, t, smem, tc, t.op);
+      if (op.flags & F_TC) op_matmul_tc(A, op, t, smem, tc, t.op, next_ti);
       else if (op.flags & F_WIDE) {
         const uint32_t nk = op_matmul_wide(A, op, t, smem, tc, false, false);
         if ((op.flags2 & FX_PV) && nk != 0xFFFFFFFFu) {   // the P.V op, its A tile from the softmax above
@@ -1977,8 +2126,8 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
 // Shared memory of one half: max(MATMUL tiles, row buffers + pairwise scratch,
 // tcgen05 stages); the two halves' regions are followed by their TcShared slots.
 constexpr size_t kRowSmem = kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4;
-constexpr size_t kTcSmem = kTcStages * kTcStage + 1024;   // + alignment of the swizzled stages
-static_assert(2 * kTcStage128 + 1024 <= kTcSmem, "128-column tcgen05 stages outgrow the tcgen05 region");
+constexpr size_t kTcSmem = (kTcStages * kTcStage > 2 * kTcStage128 ? kTcStages * kTcStage : 2 * kTcStage128) +
+                           1024 + kTcEpiBytes;   // + alignment of the swizzled stages, + the epilogue's vectors
 constexpr size_t kExecOpSmem0 = kRowSmem > kMmSmem ? kRowSmem : kMmSmem;
 constexpr size_t kExecOpSmem = kExecOpSmem0 > kTcSmem ? kExecOpSmem0 : kTcSmem;
 constexpr size_t kExecSmem = kHalves * kExecOpSmem + kHalves * 128;

@@ -126,7 +126,12 @@ struct DevOp {
   uint32_t attn_qrb, attn_vkl;
   uint32_t pc;             // instruction that produced the op (for error reports)
   uint32_t level;
+  uint32_t m_decl;         // row-wise op narrowed to the rows some later op reads: the instruction's
+                           // tile rows (M then holds the rows computed); 0 = not narrowed
+  uint32_t q_rows;         // FX_MAXQ MAX_ABS: rows of the QUANT result stored (0 = all M); the
+                           // reduction still reads every row
 };
+static_assert(sizeof(DevOp) == 128, "DevOp is a 128-byte record");
 
 struct Segment {
   uint64_t src;   // physical unit address
@@ -159,10 +164,12 @@ constexpr uint64_t kEwTaskElems = 8192;
 #endif
 
 // MATMULs that run on tcgen05: shared weights (B), per-sequence A of fewer
-// than 128 rows (128 / M sequences fill one 128-row tile), 16-multiples.
+// than 128 rows (128 / M sequences fill one 128-row tile): a 16-multiple, or
+// a divisor of 128 (a MATMUL narrowed to the rows some op reads), N and K
+// 16-multiples.
+TAC_HD constexpr bool tc_rows_ok(uint32_t M) { return M > 0 && M < 128 && (M % 16 == 0 || 128 % M == 0); }
 TAC_HD constexpr bool tc_eligible(uint64_t a, uint64_t b, uint32_t M, uint32_t N, uint32_t K) {
-  return (b & kSharedBit) && !(a & kSharedBit) && M > 0 && M < 128 && M % 16 == 0 && N > 0 && N % 16 == 0 &&
-         K > 0 && K % 16 == 0;
+  return (b & kSharedBit) && !(a & kSharedBit) && tc_rows_ok(M) && N > 0 && N % 16 == 0 && K > 0 && K % 16 == 0;
 }
 
 // Element-wise task size by op kind: GELU (float64 tanh per element) takes

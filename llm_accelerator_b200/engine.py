@@ -18,7 +18,7 @@ DEVOP_DTYPE = np.dtype([
     ("a", "<u8"), ("b", "<u8"), ("c", "<u8"), ("d", "<u8"), ("s", "<u4", (4,)),
     ("out_slot", "<u4"), ("seg0", "<u4"), ("nseg", "<u4"), ("param", "<i4"), ("attn_mode", "<u4"),
     ("flags2", "<u4"), ("dconst", "<i8"), ("nbytes", "<u8"), ("attn_qrb", "<u4"), ("attn_vkl", "<u4"),
-    ("pc", "<u4"), ("level", "<u4")])
+    ("pc", "<u4"), ("level", "<u4"), ("m_decl", "<u4"), ("q_rows", "<u4")])
 SEGMENT_DTYPE = np.dtype([("src", "<u8"), ("dst", "<u8"), ("n", "<u8")])
 TASK_DTYPE = np.dtype([("op", "<u4"), ("seq0", "<u4"), ("nseq", "<u4"), ("tile", "<u4"), ("aux", "<u4"),
                        ("pf_units", "<u4"), ("pf_phys", "<u8")])
@@ -76,11 +76,12 @@ class Program:
 
 def compile_program(batch: int, dram_bytes: int, shared_bytes: int, region: bytes, entry_pc: int,
                     max_insns: int, regs: L.Regs, sregs_reset: bool, sites=(), *, live=None,
-                    sram_live: bool = True, sregs_live: bool = True) -> Program:
+                    sram_live: bool = True, sregs_live: bool = True, pack: bool = True) -> Program:
     """Plans an instruction region; raises only when the stream cannot be
     planned at all (a faulting stream still yields a program).  ``live``:
     DRAM byte ranges that must hold their final values after a run (None =
-    all of DRAM); ``sram_live`` / ``sregs_live``: keep SRAM / scale registers."""
+    all of DRAM); ``sram_live`` / ``sregs_live``: keep SRAM / scale registers;
+    ``pack=False`` keeps every intermediate in its own arena extent."""
     n = len(region) // 8
     buf = C.create_string_buffer(bytes(region), len(region))
     arr = (L.VarSite * max(1, len(sites)))()
@@ -89,12 +90,13 @@ def compile_program(batch: int, dram_bytes: int, shared_bytes: int, region: byte
     h = C.c_void_p()
     info, fault = L.ExecInfo(), L.Fault()
     opts = None
-    if live is not None or not sram_live or not sregs_live:
+    if live is not None or not sram_live or not sregs_live or not pack:
         rng = np.asarray(list(live or []), dtype=np.uint64).reshape(-1, 2)
         if live is not None and len(rng) == 0:
             rng = np.zeros((1, 2), np.uint64)   # nothing in DRAM stays live
         rng = np.ascontiguousarray(rng)
-        opts = L.CompileOpts(len(rng), int(sram_live), int(sregs_live), 0, rng.ctypes.data)
+        opts = L.CompileOpts(len(rng), int(sram_live), int(sregs_live), 0 if pack else L.COMPILE_NO_PACK,
+                             rng.ctypes.data if len(rng) else None)
         opts._keep = rng
     st = _lib.tac_compile_ex(batch, dram_bytes, shared_bytes, buf, n, entry_pc, max_insns, C.byref(regs),
                              1 if sregs_reset else 0, arr, len(sites), None if opts is None else C.byref(opts),

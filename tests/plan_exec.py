@@ -69,7 +69,9 @@ def _seg_read(m: PlanMachine, op, segs, nbytes: int) -> np.ndarray:
     out = np.zeros(nbytes, np.uint8)
     for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]:
         o, n = int(sg["dst"]) * 16, int(sg["n"]) * 16
-        out[o:o + n] = m.mem(int(sg["src"]), n)
+        n = min(n, nbytes - o)   # an op narrowed to its first rows reads the runs below them
+        if n > 0:
+            out[o:o + n] = m.mem(int(sg["src"]), n)
     return out
 
 
@@ -102,10 +104,11 @@ def _softmax_rows(src, masked: bool, qrb: int, vkl: int):
     return out
 
 
-def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
+def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False, poison: bool = False):
     """Executes ops in level order, within a level in op order (reverse=True:
     the opposite order; ops of one level must not depend on one another, so
-    both orders give the same state)."""
+    both orders give the same state).  poison=True (plans compiled without
+    arena reuse only) overwrites the rows a narrowed op leaves uncomputed."""
     if reverse:
         idx = np.arange(len(ops))
         order = np.lexsort((-idx, ops["level"]))
@@ -116,10 +119,35 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False):
         if op["flags2"] & 8:   # FX_PVY: runs inside its QK^T op's task
             continue
         _run_op(m, op, segs, params)
+        if poison:
+            _poison_dead_rows(m, op, segs)
         if op["flags2"] & 4:   # FX_PV: the P.V op right after the softmax rows
             _run_op(m, ops[int(op["seg0"])], segs, params)
             if op["flags2"] & 16:   # FX_SMSKIP: the rows are not stored; nothing else may read them
                 m.mem(int(op["nbytes"]), int(op["M"]) * int(op["N"]) * 2)[:] = 0xFF
+
+
+def _poison_dead_rows(m: PlanMachine, op, segs):
+    """A row-wise op narrowed to the rows some later op reads (m_decl set)
+    leaves its other rows as they were; they are overwritten with NaN / -127
+    bytes here, so a plan that reads them anyway fails its comparison."""
+    if int(op["kind"]) == K["MAX_ABS"] and int(op["q_rows"]):
+        M, N = int(op["M"]), int(op["N"])
+        m.mem(int(op["d"]), M * N)[int(op["q_rows"]) * N:] = 0x81
+        return
+    md = int(op["m_decl"])
+    if not md:
+        return
+    k, M, N = int(op["kind"]), int(op["M"]), int(op["N"])
+    outs = [(int(op["d"]), 1 if k == K["QUANT"] else 2)]
+    if k == K["VADD_CHAIN"]:
+        chain = segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]
+        outs = [(int(sg["dst"]), 2) for sg in chain[1:] if int(sg["dst"])]
+    elif k == K["MATMUL"]:   # the int32 result unless F_NOI32, the FX_DQS FP16 result
+        outs = ([] if op["flags"] & 4096 else [(int(op["d"]), 4)]) + \
+               ([(int(op["dconst"]), 2)] if op["flags2"] & 1 else [])
+    for o, es in outs:
+        m.mem(o, md * N * es)[M * N * es:] = 0x81 if es == 1 else 0xFF
 
 
 def _run_op(m: PlanMachine, op, segs, params):
@@ -234,7 +262,8 @@ def _run_op(m: PlanMachine, op, segs, params):
         if op["flags2"] & 2:   # FX_MAXQ: QUANT's result with the inverse scale
             v = np.round(xa * np.float32(np.float16(inv)))
             q = np.where(np.isnan(v), np.float32(0), np.clip(v, -128, 127)).astype(np.int8)
-            m.mem(d, M * N)[:] = q.view(np.uint8)
+            rows = int(op["q_rows"]) or M   # the rows of the result some op reads
+            m.mem(d, rows * N)[:] = q.view(np.uint8)[:rows * N]
     elif k in (K["DEQUANT_SCALED"], K["DEQUANT_ACCUM"]):
         acc = m.mem(a, M * N * 4).view(np.int32).reshape(M, N).astype(np.float32)
         if op["flags"] & 16:   # F_SPLIT: second half of the vector at c

@@ -123,11 +123,13 @@ def _narrow_kv(b, nm, sites, plan):
     return out
 
 
-def _check_plans_against_oracle(b, tokens, reverse: bool, narrow: bool):
+def _check_plans_against_oracle(b, tokens, reverse: bool, narrow: bool, pack: bool = True):
     """Compiles b's prefill and decode streams once (runtime sites as plan
     parameters), runs prefill + decode steps of `tokens` through the plans
     with each step's parameters, and compares the whole machine state with the
-    oracle's after every step."""
+    oracle's after every step.  pack=False: plans without arena reuse, whose
+    uncomputed rows (ops narrowed to the rows read) are overwritten with NaN
+    bytes after each op, so any read of them shows."""
     orc = G.OracleSimulator()
     orc.load_bundle(b)
     dram_bytes, shared = len(orc.state.dram), b.temp_base // 16 * 16
@@ -140,10 +142,12 @@ def _check_plans_against_oracle(b, tokens, reverse: bool, narrow: bool):
                 w = int.from_bytes(region[pc * 8:pc * 8 + 8], "big") & (0x7F << 57)
                 region[pc * 8:pc * 8 + 8] = w.to_bytes(8, "big")
         entry = b.prefill_pc if nm == "prefill" else b.decode_pc
-        plan = compile_program(1, dram_bytes, shared, bytes(region), entry, 10_000_000, L.Regs(), True, sites)
+        plan = compile_program(1, dram_bytes, shared, bytes(region), entry, 10_000_000, L.Regs(), True, sites,
+                               pack=pack)
         if narrow:
             sites = _narrow_kv(b, nm, sites, plan)
-            plan = compile_program(1, dram_bytes, shared, bytes(region), entry, 10_000_000, L.Regs(), True, sites)
+            plan = compile_program(1, dram_bytes, shared, bytes(region), entry, 10_000_000, L.Regs(), True, sites,
+                                   pack=pack)
         plans[nm] = (plan, sites)
     arena = max(int(p.info.arena_bytes) for p, _ in plans.values())
     slots = max(int(p.info.n_slots) for p, _ in plans.values())
@@ -162,7 +166,7 @@ def _check_plans_against_oracle(b, tokens, reverse: bool, narrow: bool):
         m.shared[:len(region)] = np.frombuffer(region, np.uint8)
         p, sites = plans[nm]
         ops, segs, tasks, lv = p.dump()
-        PE.run_plan(m, ops, segs, lv, _params(region, sites), reverse=reverse)
+        PE.run_plan(m, ops, segs, lv, _params(region, sites), reverse=reverse, poison=not pack)
         n = orc.run_program(b, nm)
         assert n == int(p.info.executed)
         f = PE.final_state(m)
@@ -172,30 +176,33 @@ def _check_plans_against_oracle(b, tokens, reverse: bool, narrow: bool):
         assert f["dram"] == bytes(st.dram[:len(f["dram"])])
 
 
+@pytest.mark.parametrize("pack", [True, False], ids=["packed", "unpacked-poisoned"])
 @pytest.mark.parametrize("narrow", [False, True], ids=["symbol-ranges", "kv-window-ranges"])
 @pytest.mark.parametrize("reverse", [False, True], ids=["level-order", "level-reversed"])
 @pytest.mark.parametrize("name", ["tiny_l1_d64", "tiny_l2_d128"])
-def test_plan_reproduces_oracle_bundle_run(name, reverse, narrow):
+def test_plan_reproduces_oracle_bundle_run(name, reverse, narrow, pack):
     """Prefill + decode steps: one plan per stream compiled with runtime sites,
     executed with each step's parameters, equals the oracle bit-for-bit, also
     with every level's ops run in reverse order (no hidden intra-level
-    dependency, e.g. between the KV-cache appends of one step)."""
+    dependency, e.g. between the KV-cache appends of one step), and without
+    arena reuse with the rows narrowed ops skip overwritten."""
     b = load_bundle(name)
     gold = load_run(name)
     prompt = gold["prompt"]
     tokens = [int(prompt[pos]) if pos < len(prompt) else int(gold["tokens"][pos]) for pos in range(6)]
-    _check_plans_against_oracle(b, tokens, reverse, narrow)
+    _check_plans_against_oracle(b, tokens, reverse, narrow, pack)
 
 
-def test_plan_reproduces_oracle_gpt2_small():
+@pytest.mark.parametrize("pack", [True, False], ids=["packed", "unpacked-poisoned"])
+def test_plan_reproduces_oracle_gpt2_small(pack):
     """GPT-2 small (12 layers, d_model 768): the decode plan carries every
     fusion of the full-size streams (tcgen05 projections with their dequant
     epilogues, the K-split partial sums as VADD chains, MAX_ABS + QUANT,
-    attention with the softmax in the QK^T task); prefill and two decode
-    steps equal the oracle bit-for-bit."""
+    attention with the softmax in the QK^T task, row-wise ops narrowed to the
+    rows read); prefill and two decode steps equal the oracle bit-for-bit."""
     from llm_accelerator_b200.recipe import load_recipe
     b = load_recipe(GOLDEN / "recipe_gpt2_small.npz")
-    _check_plans_against_oracle(b, [464, 2068, 7586], reverse=True, narrow=True)
+    _check_plans_against_oracle(b, [464, 2068, 7586], reverse=True, narrow=True, pack=pack)
 
 
 def test_runtime_site_out_of_range_requests_recompile():
