@@ -948,6 +948,38 @@ class Compiler {
   std::vector<std::vector<std::pair<uint64_t, uint64_t>>> op_arena_reads_, op_arena_writes_;
   std::vector<uint8_t> op_pure_;
   uint64_t narrowed_ops_ = 0;   // ops drop_dead_ops narrowed to the rows read
+  std::unordered_map<uint32_t, uint32_t> pv_rows_;   // P.V op -> rows of its results read (drop_dead_walk)
+
+  // Rows [0, m) of an op's outputs (first unit, units per row) hold every unit
+  // a later op reads: the smallest such m, at least 1.
+  template <class AnyRead>
+  static uint32_t rows_read(uint32_t M, const std::vector<std::pair<uint64_t, uint64_t>>& outs, AnyRead&& any_read) {
+    uint32_t m = M;
+    auto read = [&](uint32_t r) {
+      for (auto& o : outs)
+        if (any_read(o.first + r * o.second, o.second)) return true;
+      return false;
+    };
+    while (m > 1 && !read(m - 1)) --m;
+    return m;
+  }
+
+  // Whether `reads(M, cb)` names exactly the arena units of `recorded`.
+  template <class Reads>
+  bool same_units(Reads&& reads, uint32_t M, const std::vector<std::pair<uint64_t, uint64_t>>& recorded) const {
+    std::vector<uint64_t> want, got;
+    auto units = [&](std::vector<uint64_t>& v, uint64_t p, uint64_t n) {
+      if (cls(p) != PC_ARENA) return;
+      for (uint64_t u = 0; u < n; ++u) v.push_back(p + u);
+    };
+    reads(M, [&](uint64_t p, uint64_t n) { units(want, p, n); });
+    for (auto& r : recorded) units(got, r.first, r.second);
+    std::sort(want.begin(), want.end());
+    want.erase(std::unique(want.begin(), want.end()), want.end());
+    std::sort(got.begin(), got.end());
+    got.erase(std::unique(got.begin(), got.end()), got.end());
+    return want == got;
+  }
   // site i's group: the first address site with the same value range; sites of
   // one group are assumed (and checked at run time) to carry one value
   std::vector<int> site_group_;
@@ -1834,6 +1866,7 @@ void Compiler::drop_dead_walk(std::vector<uint8_t>& keep, const std::vector<uint
   const size_t n = P->ops.size();
   std::vector<uint8_t> read(arena_top_, 0);
   keep.assign(n, 0);
+  pv_rows_.clear();
   auto mark = [&](uint64_t phys, uint64_t units) {
     for (uint64_t u = 0; u < units; ++u) {
       const uint64_t k = phys - arena_base_ + u;
@@ -1883,6 +1916,42 @@ void Compiler::drop_dead_walk(std::vector<uint8_t>& keep, const std::vector<uint
         ++narrowed_ops_;
       }
     }
+    // An attention pair (FX_PV QK^T + softmax, its P.V op run in the same
+    // task): both are row-wise in the query rows.  The P.V op, met first,
+    // records the rows of its results that are read; the QK^T op narrows the
+    // pair to the rows either op's results need.  Only the QK^T op reads a row
+    // operand (the FP16 Q rows); the P.V op reads the softmax rows in shared
+    // memory, V and a scale row.
+    if (op.kind == K_MATMUL && (op.flags2 & FX_PVY)) {
+      std::vector<std::pair<uint64_t, uint64_t>> outs;
+      if (!(op.flags & F_NOI32)) outs.push_back({op.d, uint64_t(op.N) * 4 / kUnit});
+      if ((op.flags & F_DQ) && !(op.flags & F_NODQ)) outs.push_back({static_cast<uint64_t>(op.dconst), uint64_t(op.N) * 2 / kUnit});
+      pv_rows_[i] = rows_read(op.M, outs, any_read);
+    }
+    if (op.kind == K_MATMUL && (op.flags2 & FX_PV) && op_pure_[i] && op.N % 8 == 0 && op.K % 8 == 0 &&
+        (op.flags & (F_ACCUMULATE | F_WIDE | F_QA | F_SM)) == (F_WIDE | F_QA | F_SM) && (op.flags & F_DQ)) {
+      const uint32_t y = pv_of_.at(static_cast<uint32_t>(i));
+      std::vector<std::pair<uint64_t, uint64_t>> outs;
+      if (!(op.flags & F_NOI32)) outs.push_back({op.d, uint64_t(op.N) * 4 / kUnit});
+      if (!(op.flags & F_NODQ)) outs.push_back({static_cast<uint64_t>(op.dconst), uint64_t(op.N) * 2 / kUnit});
+      if (!(op.flags2 & FX_SMSKIP)) outs.push_back({op.nbytes, uint64_t(op.N) * 2 / kUnit});
+      const uint32_t m = std::max(rows_read(op.M, outs, any_read), pv_rows_.count(y) ? pv_rows_[y] : P->ops[y].M);
+      const uint64_t ra = uint64_t(op.K) * 2 / kUnit;   // FP16 Q row
+      auto reads = [&](uint32_t rows, auto&& cb) {
+        cb(op.a, rows * ra);
+        cb(op.b, uint64_t(op.K) * op.N * 2 / kUnit);
+        cb(op.c, uint64_t(op.N) * 2 / kUnit);
+      };
+      if (m < op.M && P->ops[y].M == op.M && same_units(reads, op.M, op_arena_reads_[i])) {
+        op.m_decl = op.M;
+        op.M = m;
+        P->ops[y].m_decl = P->ops[y].M;
+        P->ops[y].M = m;
+        reads(m, mark);
+        narrowed_ops_ += 2;
+        continue;
+      }
+    }
     uint32_t in_es = 0;
     if (op_pure_[i] && row_wise(op, in_es) && (uint64_t(op.K) * in_es) % kUnit == 0 &&
         (uint64_t(op.N) * in_es) % kUnit == 0 && op.N % kUnit == 0) {
@@ -1899,18 +1968,8 @@ void Compiler::drop_dead_walk(std::vector<uint8_t>& keep, const std::vector<uint
         while (!tc_rows_ok(m) && m < op.M) ++m;
       if (m < op.M) {
         // the recorded reads must be exactly row_reads over every row
-        std::vector<uint64_t> want, got;
-        auto units = [&](std::vector<uint64_t>& v, uint64_t p, uint64_t n) {
-          if (cls(p) != PC_ARENA) return;
-          for (uint64_t u = 0; u < n; ++u) v.push_back(p + u);
-        };
-        row_reads(op, op.M, in_es, P->segs, chain, [&](uint64_t p, uint64_t n) { units(want, p, n); });
-        for (auto& r : op_arena_reads_[i]) units(got, r.first, r.second);
-        std::sort(want.begin(), want.end());
-        want.erase(std::unique(want.begin(), want.end()), want.end());
-        std::sort(got.begin(), got.end());
-        got.erase(std::unique(got.begin(), got.end()), got.end());
-        if (want == got) {
+        auto reads = [&](uint32_t rows, auto&& cb) { row_reads(op, rows, in_es, P->segs, chain, cb); };
+        if (same_units(reads, op.M, op_arena_reads_[i])) {
           op.m_decl = op.M;
           op.M = m;
           if (chain)

@@ -143,9 +143,13 @@ def _poison_dead_rows(m: PlanMachine, op, segs):
     if k == K["VADD_CHAIN"]:
         chain = segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]
         outs = [(int(sg["dst"]), 2) for sg in chain[1:] if int(sg["dst"])]
-    elif k == K["MATMUL"]:   # the int32 result unless F_NOI32, the FX_DQS FP16 result
-        outs = ([] if op["flags"] & 4096 else [(int(op["d"]), 4)]) + \
-               ([(int(op["dconst"]), 2)] if op["flags2"] & 1 else [])
+    elif k == K["MATMUL"]:
+        # the int32 result unless F_NOI32; the FP16 result of FX_DQS, or of
+        # F_DQ unless F_NODQ; the F_SM softmax rows unless FX_SMSKIP
+        f, f2 = int(op["flags"]), int(op["flags2"])
+        outs = ([] if f & 4096 else [(int(op["d"]), 4)]) + \
+               ([(int(op["dconst"]), 2)] if (f2 & 1) or ((f & 2048) and not f & 32768) else []) + \
+               ([(int(op["nbytes"]), 2)] if (f & 8192) and not f2 & 16 else [])
     for o, es in outs:
         m.mem(o, md * N * es)[M * N * es:] = 0x81 if es == 1 else 0xFF
 
