@@ -399,6 +399,41 @@ class Compiler {
     return dst;
   }
 
+  // Ops that may form a chain: per-sequence row ops whose whole tile one
+  // task covers in a few steps.
+  static bool chain_kind(const DevOp& op) {
+    return (op.kind == K_VADD_F16 || op.kind == K_LAYERNORM_F16 || op.kind == K_MAX_ABS) &&
+           uint64_t(op.M) * op.N <= 16384 && (op.flags2 & ~(FX_MAXQ | FX_CHAINED)) == 0;
+  }
+
+  // A chain-kind op that reads the result of the op emitted just before it
+  // (itself of a chain kind), and whose other operands are ready by that op's
+  // level, joins that op's level and runs right after it in the same task
+  // (FX_CHAINED): one grid barrier and one task fewer per sequence.  Returns
+  // the level to join, or -1.  A read that overlaps the previous op's
+  // results without lying inside them refuses the chain.
+  int32_t chain_level(const DevOp& op, const Access& acc) {
+    if (!chain_kind(op) || P->ops.empty() || op_arena_writes_.size() != P->ops.size()) return -1;
+    const size_t pi = P->ops.size() - 1;
+    const DevOp& prev = P->ops[pi];
+    if (!chain_kind(prev)) return -1;
+    Access probe = acc;
+    probe.reads.clear();
+    bool reads_prev = false;
+    for (auto& r : acc.reads) {
+      bool inside = false, overlap = false;
+      for (auto& w : op_arena_writes_[pi]) {
+        if (r.first < w.first + w.second && w.first < r.first + r.second) overlap = true;
+        if (r.first >= w.first && r.first + r.second <= w.first + w.second) inside = true;
+      }
+      if (overlap && !inside) return -1;
+      if (inside) reads_prev = true;
+      else probe.reads.push_back(r);
+    }
+    if (!reads_prev || level_for(probe) > int32_t(prev.level)) return -1;
+    return static_cast<int32_t>(prev.level);
+  }
+
   // Emits a compute op unless an identical op (same kind, shape and
   // immutable operands) already produced the value; then the destination
   // logical units (and scale-register slots) alias that op's output.
@@ -1568,9 +1603,12 @@ int Compiler::h_rtype(const Insn& x) {
     op.flags |= F_WIDE;
   const int32_t pv_x = op.kind == K_MATMUL ? pv_partner(op, acc) : -1;
   const size_t n_before = P->ops.size();
+  const int32_t chain_lv = pv_x < 0 ? chain_level(op, acc) : -1;
   if (pv_x >= 0) force_level_ = static_cast<int32_t>(P->ops[pv_x].level);
+  if (chain_lv >= 0) force_level_ = chain_lv;
   emit_compute(op, acc, d, x.sreg);
   force_level_ = -1;
+  if (chain_lv >= 0 && P->ops.size() == n_before + 1) P->ops.back().flags2 |= FX_CHAINED;
   if (pv_x >= 0 && P->ops.size() == n_before + 1) {
     const uint32_t y = static_cast<uint32_t>(n_before);
     pv_of_[static_cast<uint32_t>(pv_x)] = y;
@@ -1743,7 +1781,9 @@ void Compiler::finalize() {
 // that no later op reads need not be computed.  Gives the element bytes of the
 // row operands; a tcgen05 MATMUL (shared weights, no accumulate, at most the
 // DEQUANT_SCALED epilogue) counts, its A rows being K int8 bytes.
-static bool row_wise(const DevOp& op, uint32_t& in_es) {
+static bool row_wise(const DevOp& op0, uint32_t& in_es) {
+  DevOp op = op0;
+  op.flags2 &= ~FX_CHAINED;   // chained or not, the op's rows are its own
   switch (op.kind) {
     case K_VADD_F16: case K_GELU_F16: in_es = 2; return op.flags2 == 0 && (op.flags & ~F_SEGA) == 0;
     case K_QUANT: in_es = 2; return op.flags2 == 0 && (op.flags & ~F_SEGA) == 0;
@@ -2281,9 +2321,52 @@ void Compiler::build_tasks() {
     for (uint32_t s = 0; s < B; ++s)
       for (uint32_t t = 0; t < tiles; ++t) per_level[P->ops[opi].level].push_back(Task{opi, s, 1, t, 0});
   };
+  // aux of a segment-list element-wise task of tile t: the segments holding
+  // its units, first | count << 16 (segments are in operand order)
+  auto seg_aux = [&](const DevOp& op, uint32_t t) {
+    const uint64_t units = uint64_t(op.M) * op.N / 8;
+    const uint64_t u0 = uint64_t(t) * kSegTaskUnits, u1 = std::min<uint64_t>(units, u0 + kSegTaskUnits);
+    uint32_t first = 0, last = 0;
+    for (uint32_t k = 0; k < op.nseg; ++k) {
+      const Segment& sg = P->segs[op.seg0 + k];
+      if (sg.dst + sg.n <= u0) first = k + 1;
+      if (sg.dst < u1) last = k;
+    }
+    return first | ((last - first + 1) << 16);
+  };
+  // One sequence's tasks of a chain op, as templates (tile, aux; seq0 unset).
+  auto chain_tiles = [&](uint32_t opi, std::vector<Task>& out) {
+    const DevOp& op = P->ops[opi];
+    const uint64_t MN = uint64_t(op.M) * op.N;
+    uint32_t tiles = 1;
+    if (op.kind == K_LAYERNORM_F16) tiles = (op.M + row_task_rows(op.kind, op.N) - 1) / row_task_rows(op.kind, op.N);
+    else if (op.kind == K_VADD_CHAIN) tiles = static_cast<uint32_t>((MN + kVaddChainTask - 1) / kVaddChainTask);
+    else if (op.kind != K_MAX_ABS && (op.flags & F_SEGA))
+      tiles = static_cast<uint32_t>(std::max<uint64_t>(1, (MN / 8 + kSegTaskUnits - 1) / kSegTaskUnits));
+    else if (op.kind != K_MAX_ABS)
+      tiles = static_cast<uint32_t>(std::max<uint64_t>(1, (MN + ew_task_elems(op.kind) - 1) / ew_task_elems(op.kind)));
+    for (uint32_t t = 0; t < tiles; ++t)
+      out.push_back(Task{opi, 0, 1, t, (op.kind != K_MAX_ABS && (op.flags & F_SEGA)) ? seg_aux(op, t) : 0u});
+  };
+  std::vector<Task> templates;
+  std::vector<std::pair<size_t, uint32_t>> heads;   // (level, index in per_level) of chain head tasks
   for (uint32_t i = 0; i < P->ops.size(); ++i) {
     const DevOp& op = P->ops[i];
     const uint64_t MN = uint64_t(op.M) * op.N;
+    if (op.flags2 & FX_CHAINED) continue;   // runs in its chain head's task
+    if (i + 1 < P->ops.size() && (P->ops[i + 1].flags2 & FX_CHAINED)) {
+      // a chain: one task per sequence runs every tile of each op in order
+      const uint32_t first = static_cast<uint32_t>(templates.size());
+      chain_tiles(i, templates);
+      for (uint32_t j = i + 1; j < P->ops.size() && (P->ops[j].flags2 & FX_CHAINED); ++j) chain_tiles(j, templates);
+      P->ops[i].flags2 |= FX_CHAINHEAD;
+      const uint32_t count = static_cast<uint32_t>(templates.size()) - first;
+      for (uint32_t s = 0; s < B; ++s) {
+        heads.push_back({op.level, static_cast<uint32_t>(per_level[op.level].size())});
+        per_level[op.level].push_back(Task{i, s, 1, first, count});
+      }
+      continue;
+    }
     switch (op.kind) {
       case K_GATHER: {
         // runs of whole segments of about kGatherChunkUnits units per task
@@ -2353,15 +2436,7 @@ void Compiler::build_tasks() {
           const uint64_t units = MN / 8;
           const uint32_t tiles = static_cast<uint32_t>(std::max<uint64_t>(1, (units + kSegTaskUnits - 1) / kSegTaskUnits));
           for (uint32_t t = 0; t < tiles; ++t) {
-            // the segments holding the tile's units: first | count << 16 (segments are in operand order)
-            const uint64_t u0 = uint64_t(t) * kSegTaskUnits, u1 = std::min<uint64_t>(units, u0 + kSegTaskUnits);
-            uint32_t first = 0, last = 0;
-            for (uint32_t k = 0; k < op.nseg; ++k) {
-              const Segment& sg = P->segs[op.seg0 + k];
-              if (sg.dst + sg.n <= u0) first = k + 1;
-              if (sg.dst < u1) last = k;
-            }
-            const uint32_t aux = first | ((last - first + 1) << 16);
+            const uint32_t aux = seg_aux(op, t);
             for (uint32_t s = 0; s < B; ++s) per_level[op.level].push_back(Task{i, s, 1, t, aux});
           }
           break;
@@ -2382,10 +2457,15 @@ void Compiler::build_tasks() {
   P->tasks.clear();
   P->level_off.assign(1, 0);
   for (auto& v : per_level) {
-    for (Task& t : v) prefetch_hint(P->ops[t.op], t);
+    for (Task& t : v)
+      if (!(P->ops[t.op].flags2 & FX_CHAINHEAD)) prefetch_hint(P->ops[t.op], t);
     P->tasks.insert(P->tasks.end(), v.begin(), v.end());
     P->level_off.push_back(static_cast<uint32_t>(P->tasks.size()));
   }
+  // chain templates after the last level; head tasks point at them
+  const uint32_t base = static_cast<uint32_t>(P->tasks.size());
+  P->tasks.insert(P->tasks.end(), templates.begin(), templates.end());
+  for (auto& h : heads) P->tasks[P->level_off[h.first] + h.second].tile += base;
 }
 
 // The operand bytes a task reads first, for the executor to pull into L2

@@ -2061,6 +2061,9 @@ __device__ __forceinline__ bool grid_barrier(const ExecArgs& A, uint32_t target,
 // next task's op record into L1 (op records never change during a launch)
 // and its hinted operand bytes into L2, and the record of the task after it
 // into L1.
+__device__ void run_op(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem, TcShared* tc,
+                       uint32_t next_ti);
+
 __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t next_ti, uint32_t next2_ti,
                          TcShared* tc) {
   if (htid() == 32 && next_ti != 0xFFFFFFFFu) {
@@ -2073,6 +2076,25 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
 
   const Task& t = A.tasks[ti];   // read in place (L1), not copied to local memory
   const DevOp& op = A.ops[t.op];
+  if (op.flags2 & FX_CHAINHEAD) {
+    // a chain: the templates' tasks in order for this sequence; generic
+    // stores of one step are fenced against the next step's bulk copies
+    for (uint32_t k = 0; k < t.aux; ++k) {
+      Task tt = A.tasks[t.tile + k];
+      tt.seq0 = t.seq0;
+      run_op(A, A.ops[tt.op], tt, smem, tc, 0xFFFFFFFFu);
+      sm100::fence_proxy_async();
+      hsync();
+    }
+    return;
+  }
+  run_op(A, op, t, smem, tc, next_ti);
+  hsync();
+}
+
+// The op of one task (or one chain step) on the calling half.
+__device__ void run_op(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem, TcShared* tc,
+                       uint32_t next_ti) {
   switch (op.kind) {
     case K_GATHER: op_gather(A, op, t); break;
     case K_DYN_LOAD:
@@ -2120,7 +2142,6 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
       if (htid() == 0) raise_fault(A, DF_BAD_OP, t.op, t.seq0);
       break;
   }
-  hsync();
 }
 
 // Shared memory of one half: max(MATMUL tiles, row buffers + pairwise scratch,

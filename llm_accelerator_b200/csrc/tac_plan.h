@@ -102,6 +102,11 @@ constexpr uint32_t FX_PVY = 8;         // the P.V op of an FX_PV pair: same leve
 constexpr uint32_t FX_SMSKIP = 16;     // FX_PV op whose softmax rows only its P.V op reads: not stored
 constexpr uint32_t FX_PVPF = 32;       // FX_PV op that stages its P.V op's FP16 B (V) in shared memory once
                                        // its own operand tiles are quantised; the P.V op skips that load
+constexpr uint32_t FX_CHAINED = 64;    // per-sequence row op that runs in the task of the op before it (same
+                                       // level), after every tile of that op for the sequence
+constexpr uint32_t FX_CHAINHEAD = 128; // first op of such a chain: its tasks (one per sequence) hold, in tile
+                                       // and aux, the first and count of the chain's task templates, stored
+                                       // after the last level's tasks (seq0 taken from the head's task)
 
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 

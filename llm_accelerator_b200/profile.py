@@ -44,6 +44,8 @@ def op_label(op) -> str:
             tags.append("pv")
         k += (f"[{op['M']}x{op['K']}x{op['N']}{'s' if int(op['b']) & SHARED else 'p'}]" +
               ("+" + "+".join(tags) if tags else ""))
+    elif int(op["flags2"]) & 128:
+        k += f"[{op['M']}x{op['N']}]+chain"
     elif k not in ("GATHER", "DYN_STORE", "DYN_LOAD", "DYN_STORE_MULTI", "TRANSPOSE", "SREG_LOAD", "SREG_FINAL"):
         k += f"[{op['M']}x{op['N']}]" + ("seg" if f & 32 else "") + ("+quant" if int(op["flags2"]) & 2 else "")
         if k.startswith("VADD_CHAIN"):
@@ -78,7 +80,7 @@ def profile_decode(recipe: str, batch: int, steps: int = 3, device: int = 0, pos
 
 def summarize(level_ns, task_cycles, ops, tasks, lv, halves: int, mhz: float, top: int = 25) -> str:
     per = collections.defaultdict(list)
-    for i, t in enumerate(tasks):
+    for i, t in enumerate(tasks[:int(lv[-1])]):   # chain templates (after the last level) are not tasks
         per[op_label(ops[int(t["op"])])].append(task_cycles[i])
     lines = [f"{'op: kind[M x K x N] or [M x N], fusions':56s} {'tasks':>7s} {'median':>9s} {'p90':>9s} "
              f"{'sum/halves':>11s}"]

@@ -116,11 +116,17 @@ def run_plan(m: PlanMachine, ops, segs, lv, params=None, reverse: bool = False, 
         order = np.argsort(ops["level"], kind="stable")
     for i in order:
         op = ops[i]
-        if op["flags2"] & 8:   # FX_PVY: runs inside its QK^T op's task
+        if op["flags2"] & (8 | 64):   # FX_PVY: runs inside its QK^T op's task; FX_CHAINED: after its chain head
             continue
         _run_op(m, op, segs, params)
         if poison:
             _poison_dead_rows(m, op, segs)
+        j = i + 1
+        while j < len(ops) and ops[j]["flags2"] & 64:   # FX_CHAINED ops follow their head in op order
+            _run_op(m, ops[j], segs, params)
+            if poison:
+                _poison_dead_rows(m, ops[j], segs)
+            j += 1
         if op["flags2"] & 4:   # FX_PV: the P.V op right after the softmax rows
             _run_op(m, ops[int(op["seg0"])], segs, params)
             if op["flags2"] & 16:   # FX_SMSKIP: the rows are not stored; nothing else may read them

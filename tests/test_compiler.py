@@ -349,7 +349,8 @@ def test_pc_past_end_and_halt_counts():
 @pytest.mark.parametrize("batch", [1, 3, 5, 8])
 def test_tasks_cover_every_sequence_and_element_once(batch):
     """Element-wise tasks either take one chunk of one sequence or pack whole
-    sequences; across an op's tasks every (sequence, element) appears once."""
+    sequences; across an op's tasks every (sequence, element) appears once,
+    counting the tasks a chain head runs for its sequence."""
     b = load_bundle("tiny_l2_d128")
     region = bytes(b.instruction_region())
     p = compile_program(batch, 16 << 20, b.temp_base // 16 * 16, region, b.decode_pc, 10_000_000, L.Regs(), True,
@@ -359,7 +360,17 @@ def test_tasks_cover_every_sequence_and_element_once(batch):
     ew_kinds = set(range(7, 18)) | {19, 27}
     task_elems = lambda kind: 4096 if kind in (19, 27) else (2 * EW_TASK if kind == 16 else EW_TASK)  # noqa: E731
     seen = {}
-    for t in tasks:
+    run = []   # the tasks the executor runs: leveled tasks, chain heads expanded into their templates
+    for t in tasks[:int(lv[-1])]:
+        if int(ops[t["op"]]["flags2"]) & 128:   # FX_CHAINHEAD: templates tile .. tile + aux, this sequence
+            for k in range(int(t["aux"])):
+                tt = tasks[int(t["tile"]) + k].copy()
+                assert int(tt["nseq"]) == 1
+                tt["seq0"] = t["seq0"]
+                run.append(tt)
+        else:
+            run.append(t)
+    for t in run:
         op = ops[t["op"]]
         if int(op["kind"]) not in ew_kinds:
             continue
@@ -425,10 +436,12 @@ def test_segment_list_tasks_name_the_segments_they_read():
                         10_000_000, L.Regs(), True, _sites(b, "decode"))
     ops, segs, tasks, lv = p.dump()
     seen = 0
-    for t in tasks:
+    for i, t in enumerate(tasks):
         op = ops[int(t["op"])]
         if not int(op["flags"]) & 32 or int(op["kind"]) == PE.K["MAX_ABS"]:
             continue
+        if i < int(lv[-1]) and int(op["flags2"]) & 128:
+            continue   # a chain head's task points at the chain's templates (after the last level)
         units = int(op["M"]) * int(op["N"]) // 8
         u0 = int(t["tile"]) * 512
         u1 = min(units, u0 + 512)
