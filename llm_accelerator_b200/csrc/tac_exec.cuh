@@ -876,6 +876,128 @@ __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& 
 }
 
 // ---------------------------------------------------------------------------------
+// One query row of an attention pair: an FX_PV QK^T op and its P.V op, both
+// narrowed to row 0 (a decode step).  The scores, the masked softmax and P.V
+// run on CUDA cores with the wide path's arithmetic element for element: the
+// QUANT rule on Q, K, P and V, exact int32 dot products (dp4a), the F_DQ
+// dequantisation of scores and output, softmax_row_f16.  Keys past the row's
+// last visible one get P = 0 there and are skipped here.
+// ---------------------------------------------------------------------------------
+constexpr uint32_t kAttnRowVOff = 8192;   // V rows of op_attn_row, after its scores and scratch
+
+__device__ __forceinline__ bool attn_row_ok(const ExecArgs& A, const DevOp& x) {
+  constexpr uint16_t need = F_WIDE | F_QA | F_QB | F_BT | F_DQ | F_SM | F_NOI32 | F_NODQ;
+  if (x.M != 1 || (x.flags & need) != need || (x.flags & F_ACCUMULATE) || !(x.flags2 & FX_SMSKIP)) return false;
+  if (x.K % 8 || x.K > 128 || x.N % 8 || x.N > 1024) return false;
+  const DevOp& y = A.ops[x.seg0];
+  constexpr uint16_t yneed = F_WIDE | F_QB | F_DQ | F_NOI32;
+  return y.M == 1 && (y.flags & yneed) == yneed && !(y.flags & (F_BT | F_ACCUMULATE | F_NODQ)) && y.K == x.N &&
+         y.N % 8 == 0 && y.N <= 64 && kAttnRowVOff + x.N * y.N * 2 <= kWideMmSmem;
+}
+
+__device__ __noinline__ void op_attn_row(const ExecArgs& A, const DevOp& x, const Task& t, uint8_t* smem,
+                                         TcShared* tc) {
+  const DevOp& y = A.ops[x.seg0];
+  const uint32_t seq = t.seq0, Kd = x.K, N = x.N, Ny = y.N;
+  const int warp = htid() >> 5, lane = htid() & 31;
+  uint32_t qrb = x.attn_qrb, vkl = x.attn_vkl;
+  if (x.flags & F_ATTN_DYN) {
+    const uint64_t pv = A.params[uint64_t(seq) * A.n_params + x.param];
+    qrb = pv & 0xFFFF;
+    vkl = (pv >> 16) & 0xFFFF;
+  }
+  const bool masked = (x.flags & F_SMMASK) != 0;
+  const int64_t lt = masked ? (int64_t(qrb) < int64_t(vkl) - 1 ? int64_t(qrb) : int64_t(vkl) - 1) : int64_t(N) - 1;
+  const uint32_t nvis = lt < 0 ? 0u : min(N, uint32_t(lt) + 1);
+  int32_t* q8w = reinterpret_cast<int32_t*>(smem);                 // Q quantised, 4 per word (Kd <= 128)
+  float* rb = reinterpret_cast<float*>(smem + 128);                // the dequantised scores (N <= 1024)
+  int8_t* p8 = reinterpret_cast<int8_t*>(smem + 128 + 4096);       // P quantised for P.V
+  int32_t* part = reinterpret_cast<int32_t*>(smem + 128 + 4096 + 1024);   // P.V partial sums
+  uint32_t* pw = reinterpret_cast<uint32_t*>(smem + 128 + 4096 + 1024 + kThreads * 4);   // warp 0's scratch
+  const uint8_t* vg = pptr(A, y.b, seq);
+  // the visible keys' V rows land in shared memory while the scores and the
+  // softmax are computed
+  uint16_t* vs = reinterpret_cast<uint16_t*>(smem + kAttnRowVOff);
+  const uint32_t vbytes = nvis * Ny * 2;
+  const uint32_t par = tc->phase_stage;
+  hsync();   // every thread has the parity before it flips
+  if (htid() == 0 && vbytes) {
+    tc->phase_stage = par ^ 1u;
+    sm100::fence_proxy_async();
+    sm100::mbar_arrive_expect_tx(&tc->stage, vbytes);
+    sm100::bulk_g2s(vs, vg, vbytes, &tc->stage);
+  }
+  if (htid() < Kd / 4) {
+    const float sq = h2f(sreg_bits(A, x.s[0], seq));
+    const uint2 qv = __ldcg(reinterpret_cast<const uint2*>(pptr(A, x.a, seq)) + htid());
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint16_t h = static_cast<uint16_t>((j < 2 ? qv.x : qv.y) >> (16 * (j & 1)));
+      w |= uint32_t(uint8_t(sat8(__fmul_rn(h2f(h), sq)))) << (8 * j);
+    }
+    q8w[htid()] = static_cast<int32_t>(w);
+  }
+  hsync();
+  {
+    // scores: one key per thread, its FP16 row quantised and dotted with Q
+    const float sk = h2f(sreg_bits(A, x.s[1], seq));
+    const uint8_t* kg = pptr(A, x.b, seq);
+    const uint16_t* scx = reinterpret_cast<const uint16_t*>(pptr(A, x.c, seq));
+    for (uint32_t j = htid(); j < nvis; j += kThreads) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kg + uint64_t(j) * Kd * 2);
+      uint4 kv[16];
+#pragma unroll
+      for (uint32_t g = 0; g < 16; ++g)
+        if (g < Kd / 8) kv[g] = __ldcg(kr + g);
+      const float sc = h2f(scx[j]);
+      int32_t acc = 0;
+#pragma unroll
+      for (uint32_t g = 0; g < 16; ++g) {
+        if (g >= Kd / 8) break;
+        int8_t q[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[e] = sat8(__fmul_rn(h2f(h_at(kv[g], e)), sk));
+        const uint2 pk = pack_b(q);
+        acc = __dp4a(static_cast<int32_t>(pk.x), q8w[2 * g], acc);
+        acc = __dp4a(static_cast<int32_t>(pk.y), q8w[2 * g + 1], acc);
+      }
+      rb[j] = h2f(f2h(__fmul_rn(__int2float_rn(acc), sc)));
+    }
+  }
+  hsync();
+  if (warp == 0)
+    softmax_row_f16(rb, N, masked, masked ? lt : int64_t(N) - 1, nullptr, pw, lane, p8,
+                    h2f(sreg_bits(A, y.s[0], seq)));
+  hsync();
+  {
+    // P.V: column n, keys kq, kq + nq, ... of the visible ones
+    const uint32_t nq = kThreads / Ny, n = htid() % Ny, kq = htid() / Ny;
+    const float sv = h2f(sreg_bits(A, y.s[1], seq));
+    if (vbytes && !sm100::mbar_wait(&tc->stage, par, nullptr, 0)) {
+      sm100::mbar_wait(&tc->stage, par, nullptr, 0);   // bounded: let the copy land, then fault
+      if (htid() == 0) raise_fault(A, DF_STAGE_TIMEOUT, t.op, seq);
+      return;
+    }
+    int32_t acc = 0;
+    if (kq < nq) {
+#pragma unroll 4
+      for (uint32_t j = kq; j < nvis; j += nq)
+        acc += int32_t(p8[j]) * int32_t(sat8(__fmul_rn(h2f(vs[j * Ny + n]), sv)));
+    }
+    part[htid()] = acc;
+    hsync();
+    if (htid() < Ny) {
+      int32_t sum = 0;
+      for (uint32_t k = 0; k < nq; ++k) sum += part[k * Ny + htid()];   // int32 sums are exact in any order
+      const uint16_t* scy = reinterpret_cast<const uint16_t*>(pptr(A, y.c, seq));
+      uint16_t* out = reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(y.dconst), seq));
+      out[htid()] = f2h(__fmul_rn(__int2float_rn(sum), h2f(scy[htid()])));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
 // MATMUL with shared weights on the 5th-generation tensor cores (ops flagged
 // F_TC).  A task is up to 128 rows (the M rows of up to 128/M sequences) x 64
 // columns.  Per 128-byte K block, TMA brings A as one [128/M sequences][M
@@ -2105,6 +2227,7 @@ __device__ void run_op(const ExecArgs& A, const DevOp& op, const Task& t, uint8_
     case K_SREG_FINAL: op_sreg_final(A, op, t); break;
     case K_MATMUL:
       if (op.flags & F_TC) op_matmul_tc(A, op, t, smem, tc, t.op, next_ti);
+      else if ((op.flags & F_WIDE) && (op.flags2 & FX_PV) && attn_row_ok(A, op)) op_attn_row(A, op, t, smem, tc);
       else if (op.flags & F_WIDE) {
         const uint32_t nk = op_matmul_wide(A, op, t, smem, tc, false, false);
         if ((op.flags2 & FX_PV) && nk != 0xFFFFFFFFu) {   // the P.V op, its A tile from the softmax above
