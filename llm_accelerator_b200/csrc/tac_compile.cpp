@@ -2312,7 +2312,15 @@ void Compiler::build_tasks() {
   for (auto& op : P->ops) {
     if (op.kind == K_MATMUL && tc_eligible(op.a, op.b, op.M, op.N, op.K)) {
       op.flags |= F_TC;
-      if (op.N >= 128) op.flags |= F_TC128;
+      // a task's A rows (its sequences' rows) rounded up to 8: when every K
+      // chunk fits in shared memory at once, 64-column tasks load them all
+      const uint32_t rows = (std::min<uint32_t>(128 / op.M, B) * op.M + 7) & ~7u;
+      if (!(op.flags & F_ACCUMULATE) && tc_resident_fits(rows, op.K)) {
+        op.flags2 |= FX_TCRES;
+        op.q_rows = rows;
+      } else if (op.N >= 128) {
+        op.flags |= F_TC128;
+      }
       op.seg0 = P->n_tc++;
       op.nseg = 0;
     }

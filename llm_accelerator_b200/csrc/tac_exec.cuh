@@ -1133,7 +1133,7 @@ __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, co
   // every sequence) and each row's activation scale go to shared memory from
   // warps 3 and 4, idle while the K loop runs.
   uint8_t* epi = (op.flags2 & FX_DQS) && (op.c & kSharedBit) && (op.nbytes & kSharedBit)
-                     ? base + nst * stage_bytes : nullptr;
+                     ? base + kTcStageRegion : nullptr;
   if (epi && warp == 3) {
     const uint32_t nv = (ncols + 7) / 8;   // 16-byte vectors of each row
     for (uint32_t i = lane; i < 2 * nv; i += 32) {
@@ -1150,7 +1150,42 @@ __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, co
   uint32_t flip = 0;
   for (uint32_t st = 0; st < nst; ++st)
     if (((nchunks + nst - 1 - st) / nst) & 1u) flip |= 1u << st;
-  if (htid() == 32) {
+  const bool res = (op.flags2 & FX_TCRES) != 0;
+  if (res) {
+    // every K chunk resident at once: A boxes of q_rows rows back to back,
+    // then the B boxes; chunks [0, h) complete on full[0], the rest on
+    // full[1], so the first MMAs overlap the second half's transfer; one
+    // commit on empty[0] when all MMAs are done
+    const uint32_t abytes = op.q_rows * 128, h = (nchunks + 1) / 2;
+    uint8_t* bbase = base + nchunks * abytes;
+    if (htid() == 32) {
+      sm100::fence_proxy_async();   // A was written by generic stores in earlier levels
+      sm100::mbar_arrive_expect_tx(&tc->full[0], h * (abytes + 8192));
+      if (nchunks > h) sm100::mbar_arrive_expect_tx(&tc->full[1], (nchunks - h) * (abytes + 8192));
+      for (uint32_t c = 0; c < nchunks; ++c) {
+        uint64_t* bar = &tc->full[c < h ? 0 : 1];
+        sm100::tma_load_3d(base + c * abytes, ma, int32_t(c * 128), 0, int32_t(t.seq0), bar);
+        sm100::tma_load_2d(bbase + c * 8192, mb, int32_t(n0), int32_t(c * 128), bar);
+      }
+    } else if (htid() == 0) {
+      bool ok = true;
+      for (uint32_t c = 0; c < nchunks; ++c) {
+        if ((c == 0 || c == h) && !sm100::mbar_wait(&tc->full[c < h ? 0 : 1], (pf0 >> (c < h ? 0 : 1)) & 1u, nullptr, 0))
+          ok = false;
+        sm100::tc_fence_after();
+        const uint32_t a_addr = sm100::smem_u32(base + c * abytes), b_addr = sm100::smem_u32(bbase + c * 8192);
+        const uint32_t kc = K - c * 128 < 128 ? K - c * 128 : 128;
+        for (uint32_t ks = 0; ks * 32 < kc; ++ks)
+          sm100::mma_i8(tc->tmem, sm100::smem_desc_sw128(a_addr + ks * 32, 16, 1024), desc_sw64(b_addr + ks * 2048, 16, 512),
+                        kTcIdesc, (c | ks) != 0);
+      }
+      sm100::mma_commit(&tc->empty[0]);
+      if (!sm100::mbar_wait(&tc->empty[0], pe0 & 1u, nullptr, 0)) ok = false;
+      if (!ok) raise_fault(A, DF_MMA_TIMEOUT, opi, t.seq0);
+    } else if (htid() == 64 && next_ti != 0xFFFFFFFFu) {
+      prefetch_task_weights(A, A.tasks[next_ti]);
+    }
+  } else if (htid() == 32) {
     // producer (warp 1): TMA loads; a stage is refilled once the MMAs of the
     // chunk before it in that stage have completed
     const uint32_t bytes = (128 / M) * M * 128 + tn * 128;
@@ -1188,14 +1223,14 @@ __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, co
     for (uint32_t c = nchunks > nst ? nchunks - nst : 0; c < nchunks; ++c)
       if (!sm100::mbar_wait(&tc->empty[c % nst], parity(pe0, c), nullptr, 0)) ok = false;
     if (!ok) raise_fault(A, DF_MMA_TIMEOUT, opi, t.seq0);
-  } else if (htid() == 64 && next_ti != 0xFFFFFFFFu) {
+  } else if (htid() == 64 && next_ti != 0xFFFFFFFFu && !res) {
     prefetch_task_weights(A, A.tasks[next_ti]);   // warp 2 is idle during the K loop
   }
   hsync();
   sm100::tc_fence_after();
   if (htid() == 0) {   // every thread has read the parities at the start (before the hsync above)
-    tc->phase_full = pf0 ^ flip;
-    tc->phase_empty = pe0 ^ flip;
+    tc->phase_full = pf0 ^ (res ? (nchunks > (nchunks + 1) / 2 ? 3u : 1u) : flip);
+    tc->phase_empty = pe0 ^ (res ? 1u : flip);
   }
   // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31; with 64 columns it
   // takes columns 32 (w / 4) .. +31, with 128 columns two such slices
@@ -1931,55 +1966,83 @@ __device__ __forceinline__ bool ln_small_ok(const DevOp& op) {
   return op.kind == K_LAYERNORM_F16 && op.M <= 2 && op.N % 8 == 0 && op.N <= kRowCap && pw_balanced(op.N, nl, L);
 }
 
-__device__ __noinline__ void op_ln_small(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
-  const uint32_t warp = htid() >> 5, lane = htid() & 31, seq = t.seq0, N = op.N;
+// NumPy's pairwise sum of x[0..N) (or of (x - mean)^2), for a balanced tree
+// of nl <= 8 leaves of L elements, by every warp of the half: warp w sums
+// leaf w (lanes 0..7 one accumulator chain each, combined by xor shuffles),
+// the leaf sums combine level by level.  `part` holds 8 floats; every thread
+// returns the sum.  Contains one hsync.
+__device__ __forceinline__ float ln_pairwise(const float* x, uint32_t nl, uint32_t L, bool sq, float mean,
+                                             float* part) {
+  const uint32_t warp = htid() >> 5, lane = htid() & 31;
+  float v = 0.f;
+  if (warp < nl && lane < 8) {
+    const float* q = x + warp * L + lane;
+    float r;
+    if (sq) {
+      const float d0 = __fsub_rn(q[0], mean);
+      r = __fmul_rn(d0, d0);
+      for (uint32_t i = 8; i < L; i += 8) {
+        const float d = __fsub_rn(q[i], mean);
+        r = __fadd_rn(r, __fmul_rn(d, d));
+      }
+    } else {
+      r = q[0];
+      for (uint32_t i = 8; i < L; i += 8) r = __fadd_rn(r, q[i]);
+    }
+    v = r;
+  }
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  if (lane == 0 && warp < nl) part[warp] = v;
+  hsync();
+  float t8[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) t8[k] = part[k < int(nl) ? k : 0];
+  for (uint32_t w = nl; w > 1; w >>= 1)
+#pragma unroll
+    for (uint32_t k = 0; k < 4; ++k)
+      if (k < w / 2) t8[k] = __fadd_rn(t8[2 * k], t8[2 * k + 1]);
+  return t8[0];
+}
+
+// mean and denominator sqrt(var + eps) of the row in x (float32, N
+// elements, balanced tree), as NumPy's mean and var compute them.  Uses
+// part[0..16); contains two hsyncs.
+__device__ __forceinline__ void ln_stats(const float* x, uint32_t N, float* part, float& mean, float& denom) {
   uint32_t nl, L;
   pw_balanced(N, nl, L);
+  mean = div_count(ln_pairwise(x, nl, L, false, 0.f, part), N);
+  const float var = div_count(ln_pairwise(x, nl, L, true, mean, part + 8), N);
+  denom = __fsqrt_rn(__fadd_rn(var, 1e-5f));
+}
+
+// The LayerNorm output of 4 elements (x as floats, gamma and beta as FP16
+// pairs in uint2), row_one's arithmetic.
+__device__ __forceinline__ uint2 ln_out4(const float (&xs)[4], float mean, float denom, uint2 gv, uint2 bv) {
+  const uint16_t* g16 = reinterpret_cast<const uint16_t*>(&gv);
+  const uint16_t* b16 = reinterpret_cast<const uint16_t*>(&bv);
+  uint16_t h[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float y = __fdiv_rn(__fsub_rn(xs[j], mean), denom);
+    h[j] = f2h(__fadd_rn(__fmul_rn(y, h2f(g16[j])), h2f(b16[j])));
+  }
+  return make_uint2(uint32_t(h[0]) | (uint32_t(h[1]) << 16), uint32_t(h[2]) | (uint32_t(h[3]) << 16));
+}
+
+__device__ __noinline__ void op_ln_small(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
+  const uint32_t seq = t.seq0, N = op.N;
   float* x = reinterpret_cast<float*>(smem);   // the row as float32
   float* part = x + kRowCap;                   // leaf sums: [0, 8) the row, [8, 16) the squares
   const uint8_t* gb = pptr(A, op.b, seq);
   const uint8_t* be = (op.flags & F_SPLIT) ? pptr(A, op.c, seq) : gb + uint64_t(N) * 2;
-  const float eps = 1e-5f;
-  const uint32_t n4 = N / 4;   // output groups of 4 elements
-  const bool has4 = htid() < n4;
+  const bool has4 = htid() < N / 4;   // output groups of 4 elements
   uint2 gv = make_uint2(0, 0), bv = make_uint2(0, 0);
   if (has4) {   // gamma and beta of this thread's outputs, in flight during the sums
     gv = __ldcg(reinterpret_cast<const uint2*>(gb) + htid());
     bv = __ldcg(reinterpret_cast<const uint2*>(be) + htid());
   }
-  auto leaf_sums = [&](bool sq, float mean, float* out) {
-    float v = 0.f;
-    if (warp < nl && lane < 8) {
-      const float* q = x + warp * L + lane;
-      float r;
-      if (sq) {
-        const float d0 = __fsub_rn(q[0], mean);
-        r = __fmul_rn(d0, d0);
-        for (uint32_t i = 8; i < L; i += 8) {
-          const float d = __fsub_rn(q[i], mean);
-          r = __fadd_rn(r, __fmul_rn(d, d));
-        }
-      } else {
-        r = q[0];
-        for (uint32_t i = 8; i < L; i += 8) r = __fadd_rn(r, q[i]);
-      }
-      v = r;
-    }
-    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
-    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
-    v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
-    if (lane == 0 && warp < nl) out[warp] = v;
-  };
-  auto tree = [&](const float* leaf) {
-    float s[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) s[k] = leaf[k < int(nl) ? k : 0];
-    for (uint32_t w = nl; w > 1; w >>= 1)
-#pragma unroll
-      for (uint32_t k = 0; k < 4; ++k)
-        if (k < w / 2) s[k] = __fadd_rn(s[2 * k], s[2 * k + 1]);
-    return s[0];
-  };
   for (uint32_t r = 0; r < op.M; ++r) {
     if (r) hsync();   // the previous row's readers are done with x and part
     const uint4* src = reinterpret_cast<const uint4*>(pptr(A, op.a, seq) + uint64_t(r) * N * 2);
@@ -1989,29 +2052,143 @@ __device__ __noinline__ void op_ln_small(const ExecArgs& A, const DevOp& op, con
       for (int j = 0; j < 8; ++j) x[g * 8 + j] = h2f(h_at(v, j));
     }
     hsync();
-    leaf_sums(false, 0.f, part);
-    hsync();
-    const float mean = div_count(tree(part), N);
-    leaf_sums(true, mean, part + 8);
-    hsync();
-    const float var = div_count(tree(part + 8), N);
-    const float denom = __fsqrt_rn(__fadd_rn(var, eps));
+    float mean, denom;
+    ln_stats(x, N, part, mean, denom);
     if (has4) {
       const float4 xv = *reinterpret_cast<const float4*>(x + htid() * 4);
       const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-      const uint16_t* g16 = reinterpret_cast<const uint16_t*>(&gv);
-      const uint16_t* b16 = reinterpret_cast<const uint16_t*>(&bv);
-      uint16_t h[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float y = __fdiv_rn(__fsub_rn(xs[j], mean), denom);
-        h[j] = f2h(__fadd_rn(__fmul_rn(y, h2f(g16[j])), h2f(b16[j])));
-      }
-      uint2 o;
-      o.x = uint32_t(h[0]) | (uint32_t(h[1]) << 16);
-      o.y = uint32_t(h[2]) | (uint32_t(h[3]) << 16);
-      *reinterpret_cast<uint2*>(pptr(A, op.d, seq) + (uint64_t(r) * N + htid() * 4) * 2) = o;
+      *reinterpret_cast<uint2*>(pptr(A, op.d, seq) + (uint64_t(r) * N + htid() * 4) * 2) = ln_out4(xs, mean, denom, gv, bv);
     }
+  }
+}
+
+// A chain VADD -> LAYERNORM -> MAX_ABS + QUANT over one live row (a decode
+// step's residual add, LayerNorm and activation quantisation), in one pass
+// with the row kept in shared memory and registers: the sum is stored for
+// later ops, the LayerNorm output is stored and reduced, the MAX_ABS
+// operand's other rows (the padding the program reloads) are reduced from
+// memory as they arrive, and row 0 is quantised.  Each step's arithmetic is
+// its op's own (ew VADD, op_ln_small, op_max_abs).
+__device__ __forceinline__ bool chain_vln_ok(const ExecArgs& A, const Task& t) {
+  if (t.aux != 3) return false;
+  const Task* tp = A.tasks + t.tile;
+  const DevOp& v = A.ops[tp[0].op];
+  const DevOp& l = A.ops[tp[1].op];
+  const DevOp& m = A.ops[tp[2].op];
+  const uint32_t N = v.N, ru = N / 8;
+  if (v.kind != K_VADD_F16 || l.kind != K_LAYERNORM_F16 || m.kind != K_MAX_ABS || !(m.flags2 & FX_MAXQ) ||
+      !(m.flags & F_SEGA) || v.M != 1 || l.M != 1 || l.N != N || m.N != N || N % 8 || N > 4 * kThreads ||
+      !ln_small_ok(l) || l.a != v.d || m.nseg > 8 || (m.q_rows ? m.q_rows : m.M) != 1 || (v.flags & ~F_SEGA) ||
+      (l.flags & ~F_SPLIT))
+    return false;
+  const Segment s0 = A.segs[m.seg0];
+  if (s0.dst != 0 || s0.src != l.d || s0.n != ru) return false;
+  for (uint32_t k = 1; k < m.nseg; ++k) {   // the other rows read neither result of the chain
+    const Segment sk = A.segs[m.seg0 + k];
+    if (!(sk.src & kSharedBit) && ((sk.src < l.d + ru && l.d < sk.src + sk.n) || (sk.src < v.d + ru && v.d < sk.src + sk.n)))
+      return false;
+  }
+  return true;
+}
+
+__device__ __noinline__ void op_chain_vln(const ExecArgs& A, const Task& t, uint8_t* smem) {
+  const Task* tp = A.tasks + t.tile;
+  const DevOp& v = A.ops[tp[0].op];
+  const DevOp& l = A.ops[tp[1].op];
+  const DevOp& m = A.ops[tp[2].op];
+  const uint32_t seq = t.seq0, N = v.N, ru = N / 8;
+  const uint32_t warp = htid() >> 5, lane = htid() & 31;
+  float* x = reinterpret_cast<float*>(smem + 8192);    // the summed row as float32
+  float* part = reinterpret_cast<float*>(smem + 8192 + kRowCap * 4);   // 16 leaf sums
+  uint32_t* red = reinterpret_cast<uint32_t*>(part + 16);              // per-warp maxima, then the scale
+  // 1. loads in flight together: the VADD operands' units of row 0, gamma and
+  //    beta of this thread's 4 outputs, the MAX_ABS operand's other rows
+  const uint32_t nseg_a = (v.flags & F_SEGA) ? seg_stage(A, v, Task{tp[0].op, seq, 1, 0, 0}, smem) : 0u;
+  uint4 va = make_uint4(0, 0, 0, 0), vb = make_uint4(0, 0, 0, 0);
+  if (htid() < ru) {
+    va = __ldcg((v.flags & F_SEGA) ? seg_unit(A, nseg_a, smem, seq, htid())
+                                   : reinterpret_cast<const uint4*>(pptr(A, v.a, seq)) + htid());
+    vb = __ldcg(reinterpret_cast<const uint4*>(pptr(A, v.b, seq)) + htid());
+  }
+  const bool has4 = htid() < N / 4;
+  const uint8_t* gb = pptr(A, l.b, seq);
+  const uint8_t* be = (l.flags & F_SPLIT) ? pptr(A, l.c, seq) : gb + uint64_t(N) * 2;
+  uint2 gv = make_uint2(0, 0), bv = make_uint2(0, 0);
+  if (has4) {
+    gv = __ldcg(reinterpret_cast<const uint2*>(gb) + htid());
+    bv = __ldcg(reinterpret_cast<const uint2*>(be) + htid());
+  }
+  // |x| of FP16 values compared as bit patterns (monotone for non-NaN); any NaN wins
+  auto absmax8 = [](uint4 w, uint32_t mx) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t h = h_at(w, j) & 0x7FFFu;
+      if (h > 0x7C00u) h = 0xFFFFu;
+      mx = h > mx ? h : mx;
+    }
+    return mx;
+  };
+  uint32_t mx = 0;
+  for (uint32_t k = 1; k < m.nseg; ++k) {
+    const Segment sk = A.segs[m.seg0 + k];
+    const uint4* src = reinterpret_cast<const uint4*>(pptr(A, sk.src, seq));
+    for (uint64_t u = htid(); u < sk.n; u += kThreads) mx = absmax8(__ldcg(src + u), mx);
+  }
+  // 2. VADD: f16(a + b), stored for later ops and kept as float32
+  if (htid() < ru) {
+    uint16_t h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      h[j] = f2h(__fadd_rn(h2f(h_at(va, j)), h2f(h_at(vb, j))));
+      x[htid() * 8 + j] = h2f(h[j]);
+    }
+    reinterpret_cast<uint4*>(pptr(A, v.d, seq))[htid()] = pack_h(h);
+  }
+  hsync();
+  // 3. LayerNorm of the row
+  float mean, denom;
+  ln_stats(x, N, part, mean, denom);
+  uint2 yv = make_uint2(0, 0);
+  if (has4) {
+    const float4 xv = *reinterpret_cast<const float4*>(x + htid() * 4);
+    const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+    yv = ln_out4(xs, mean, denom, gv, bv);
+    reinterpret_cast<uint2*>(pptr(A, l.d, seq))[htid()] = yv;
+    mx = absmax8(make_uint4(yv.x, yv.y, 0, 0), mx);
+  }
+  // 4. MAX_ABS over every row: scales, then QUANT of row 0
+  for (int o = 16; o; o >>= 1) {
+    const uint32_t w = __shfl_xor_sync(0xffffffffu, mx, o);
+    mx = w > mx ? w : mx;
+  }
+  if (lane == 0) red[warp] = mx;
+  hsync();
+  if (htid() == 0) {
+    for (int w = 1; w < kWarps; ++w) mx = red[w] > mx ? red[w] : mx;
+    uint16_t inv, fwd;
+    if (mx == 0xFFFFu) {
+      inv = fwd = 0x7E00u;
+    } else {
+      double d = static_cast<double>(h2f(static_cast<uint16_t>(mx)));
+      d = d > 0.001953125 ? d : 0.001953125;         // 2^-9
+      d = d < 4159504.0 ? d : 4159504.0;             // 65504 * 127 / 2
+      inv = d2h(127.0 / d);
+      fwd = d2h(d / 127.0);
+    }
+    A.sregs[uint64_t(seq) * A.sreg_stride + m.out_slot] = inv;
+    A.sregs[uint64_t(seq) * A.sreg_stride + m.out_slot + 1] = fwd;
+    red[kWarps] = inv;
+  }
+  hsync();
+  if (has4) {
+    const float s0 = h2f(static_cast<uint16_t>(red[kWarps]));
+    uint32_t q = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint16_t h = static_cast<uint16_t>((j < 2 ? yv.x : yv.y) >> (16 * (j & 1)));
+      q |= uint32_t(uint8_t(sat8(__fmul_rn(h2f(h), s0)))) << (8 * j);
+    }
+    reinterpret_cast<uint32_t*>(pptr(A, m.d, seq))[htid()] = q;
   }
 }
 
@@ -2199,6 +2376,11 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
   const Task& t = A.tasks[ti];   // read in place (L1), not copied to local memory
   const DevOp& op = A.ops[t.op];
   if (op.flags2 & FX_CHAINHEAD) {
+    if (chain_vln_ok(A, t)) {   // VADD -> LAYERNORM -> MAX_ABS + QUANT of one row, in one pass
+      op_chain_vln(A, t, smem);
+      hsync();
+      return;
+    }
     // a chain: the templates' tasks in order for this sequence; generic
     // stores of one step are fenced against the next step's bulk copies
     for (uint32_t k = 0; k < t.aux; ++k) {
@@ -2270,8 +2452,9 @@ __device__ void run_op(const ExecArgs& A, const DevOp& op, const Task& t, uint8_
 // Shared memory of one half: max(MATMUL tiles, row buffers + pairwise scratch,
 // tcgen05 stages); the two halves' regions are followed by their TcShared slots.
 constexpr size_t kRowSmem = kWarps * kRowCap * 4 + kWarps * 3 * kPwMaxLeaves * 4;
-constexpr size_t kTcSmem = (kTcStages * kTcStage > 2 * kTcStage128 ? kTcStages * kTcStage : 2 * kTcStage128) +
-                           1024 + kTcEpiBytes;   // + alignment of the swizzled stages, + the epilogue's vectors
+static_assert(kTcStages * kTcStage <= kTcStageRegion && 2 * kTcStage128 <= kTcStageRegion,
+              "tcgen05 stages outgrow their region");
+constexpr size_t kTcSmem = kTcStageRegion + 1024 + kTcEpiBytes;   // + alignment of the swizzled stages, + the epilogue's vectors
 constexpr size_t kExecOpSmem0 = kRowSmem > kMmSmem ? kRowSmem : kMmSmem;
 constexpr size_t kExecOpSmem = kExecOpSmem0 > kTcSmem ? kExecOpSmem0 : kTcSmem;
 constexpr size_t kExecSmem = kHalves * kExecOpSmem + kHalves * 128;

@@ -107,6 +107,9 @@ constexpr uint32_t FX_CHAINED = 64;    // per-sequence row op that runs in the t
 constexpr uint32_t FX_CHAINHEAD = 128; // first op of such a chain: its tasks (one per sequence) hold, in tile
                                        // and aux, the first and count of the chain's task templates, stored
                                        // after the last level's tasks (seq0 taken from the head's task)
+constexpr uint32_t FX_TCRES = 256;     // tcgen05 MATMUL (64-column tasks) whose every K chunk fits in shared
+                                       // memory at once: A boxes of q_rows rows packed back to back, then B;
+                                       // no stage is reused
 
                                        // [seg0, seg0 + nseg) (Segment.dst = offset in the operand, units)
 
@@ -134,7 +137,8 @@ struct DevOp {
   uint32_t m_decl;         // row-wise op narrowed to the rows some later op reads: the instruction's
                            // tile rows (M then holds the rows computed); 0 = not narrowed
   uint32_t q_rows;         // FX_MAXQ MAX_ABS: rows of the QUANT result stored (0 = all M); the
-                           // reduction still reads every row
+                           // reduction still reads every row.  FX_TCRES MATMUL: rows of a task's A
+                           // box (its sequences' rows rounded up to 8)
 };
 static_assert(sizeof(DevOp) == 128, "DevOp is a 128-byte record");
 
@@ -173,6 +177,16 @@ constexpr uint64_t kEwTaskElems = 8192;
 // a divisor of 128 (a MATMUL narrowed to the rows some op reads), N and K
 // 16-multiples.
 TAC_HD constexpr bool tc_rows_ok(uint32_t M) { return M > 0 && M < 128 && (M % 16 == 0 || 128 % M == 0); }
+// Shared memory of the tcgen05 stages (after the 1024-byte alignment) and
+// the resident layout: every K chunk's A box (rows x 128 B) then every B box
+// (128 K rows x 64 columns); the MMA of the last chunk reads 128 A rows from
+// its box on, which must stay inside the stage region.
+constexpr uint32_t kTcStageRegion = 73728;
+TAC_HD constexpr bool tc_resident_fits(uint32_t rows, uint32_t K) {
+  const uint32_t nchunks = (K + 127) / 128;
+  return rows % 8 == 0 && rows <= 128 && nchunks * (rows * 128 + 8192) <= kTcStageRegion &&
+         (nchunks - 1) * rows * 128 + 16384 <= kTcStageRegion;
+}
 TAC_HD constexpr bool tc_eligible(uint64_t a, uint64_t b, uint32_t M, uint32_t N, uint32_t K) {
   return (b & kSharedBit) && !(a & kSharedBit) && tc_rows_ok(M) && N > 0 && N % 16 == 0 && K > 0 && K % 16 == 0;
 }
