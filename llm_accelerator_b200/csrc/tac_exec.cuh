@@ -875,6 +875,71 @@ __device__ __noinline__ uint32_t op_matmul_wide(const ExecArgs& A, const DevOp& 
   return nk;
 }
 
+// NumPy's pairwise sum of x[0..N) (or of (x - mean)^2), for a balanced tree
+// of nl <= 8 leaves of L elements, by every warp of the half: warp w sums
+// leaf w (lanes 0..7 one accumulator chain each, combined by xor shuffles),
+// the leaf sums combine level by level.  `part` holds 8 floats; every thread
+// returns the sum.  Contains one hsync.
+__device__ __forceinline__ float ln_pairwise(const float* x, uint32_t nl, uint32_t L, bool sq, float mean,
+                                             float* part) {
+  const uint32_t warp = htid() >> 5, lane = htid() & 31;
+  float v = 0.f;
+  if (warp < nl && lane < 8) {
+    const float* q = x + warp * L + lane;
+    float r;
+    if (sq) {
+      const float d0 = __fsub_rn(q[0], mean);
+      r = __fmul_rn(d0, d0);
+      for (uint32_t i = 8; i < L; i += 8) {
+        const float d = __fsub_rn(q[i], mean);
+        r = __fadd_rn(r, __fmul_rn(d, d));
+      }
+    } else {
+      r = q[0];
+      for (uint32_t i = 8; i < L; i += 8) r = __fadd_rn(r, q[i]);
+    }
+    v = r;
+  }
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  if (lane == 0 && warp < nl) part[warp] = v;
+  hsync();
+  float t8[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) t8[k] = part[k < int(nl) ? k : 0];
+  for (uint32_t w = nl; w > 1; w >>= 1)
+#pragma unroll
+    for (uint32_t k = 0; k < 4; ++k)
+      if (k < w / 2) t8[k] = __fadd_rn(t8[2 * k], t8[2 * k + 1]);
+  return t8[0];
+}
+
+// mean and denominator sqrt(var + eps) of the row in x (float32, N
+// elements, balanced tree), as NumPy's mean and var compute them.  Uses
+// part[0..16); contains two hsyncs.
+__device__ __forceinline__ void ln_stats(const float* x, uint32_t N, float* part, float& mean, float& denom) {
+  uint32_t nl, L;
+  pw_balanced(N, nl, L);
+  mean = div_count(ln_pairwise(x, nl, L, false, 0.f, part), N);
+  const float var = div_count(ln_pairwise(x, nl, L, true, mean, part + 8), N);
+  denom = __fsqrt_rn(__fadd_rn(var, 1e-5f));
+}
+
+// The LayerNorm output of 4 elements (x as floats, gamma and beta as FP16
+// pairs in uint2), row_one's arithmetic.
+__device__ __forceinline__ uint2 ln_out4(const float (&xs)[4], float mean, float denom, uint2 gv, uint2 bv) {
+  const uint16_t* g16 = reinterpret_cast<const uint16_t*>(&gv);
+  const uint16_t* b16 = reinterpret_cast<const uint16_t*>(&bv);
+  uint16_t h[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float y = __fdiv_rn(__fsub_rn(xs[j], mean), denom);
+    h[j] = f2h(__fadd_rn(__fmul_rn(y, h2f(g16[j])), h2f(b16[j])));
+  }
+  return make_uint2(uint32_t(h[0]) | (uint32_t(h[1]) << 16), uint32_t(h[2]) | (uint32_t(h[3]) << 16));
+}
+
 // ---------------------------------------------------------------------------------
 // One query row of an attention pair: an FX_PV QK^T op and its P.V op, both
 // narrowed to row 0 (a decode step).  The scores, the masked softmax and P.V
@@ -899,7 +964,7 @@ __device__ __noinline__ void op_attn_row(const ExecArgs& A, const DevOp& x, cons
                                          TcShared* tc) {
   const DevOp& y = A.ops[x.seg0];
   const uint32_t seq = t.seq0, Kd = x.K, N = x.N, Ny = y.N;
-  const int warp = htid() >> 5, lane = htid() & 31;
+  const uint32_t warp = htid() >> 5, lane = htid() & 31;
   uint32_t qrb = x.attn_qrb, vkl = x.attn_vkl;
   if (x.flags & F_ATTN_DYN) {
     const uint64_t pv = A.params[uint64_t(seq) * A.n_params + x.param];
@@ -910,25 +975,43 @@ __device__ __noinline__ void op_attn_row(const ExecArgs& A, const DevOp& x, cons
   const int64_t lt = masked ? (int64_t(qrb) < int64_t(vkl) - 1 ? int64_t(qrb) : int64_t(vkl) - 1) : int64_t(N) - 1;
   const uint32_t nvis = lt < 0 ? 0u : min(N, uint32_t(lt) + 1);
   int32_t* q8w = reinterpret_cast<int32_t*>(smem);                 // Q quantised, 4 per word (Kd <= 128)
-  float* rb = reinterpret_cast<float*>(smem + 128);                // the dequantised scores (N <= 1024)
+  float* rb = reinterpret_cast<float*>(smem + 128);                // scores, then exp values (N <= 1024)
   int8_t* p8 = reinterpret_cast<int8_t*>(smem + 128 + 4096);       // P quantised for P.V
   int32_t* part = reinterpret_cast<int32_t*>(smem + 128 + 4096 + 1024);   // P.V partial sums
-  uint32_t* pw = reinterpret_cast<uint32_t*>(smem + 128 + 4096 + 1024 + kThreads * 4);   // warp 0's scratch
+  float* red = reinterpret_cast<float*>(smem + 128 + 4096 + 1024 + kThreads * 4);   // 16 floats, then par
+  uint32_t* pw = reinterpret_cast<uint32_t*>(red + 32);            // warp 0's pairwise scratch
+  uint16_t* vs = reinterpret_cast<uint16_t*>(smem + kAttnRowVOff); // the visible keys' V rows
   const uint8_t* vg = pptr(A, y.b, seq);
-  // the visible keys' V rows land in shared memory while the scores and the
-  // softmax are computed
-  uint16_t* vs = reinterpret_cast<uint16_t*>(smem + kAttnRowVOff);
   const uint32_t vbytes = nvis * Ny * 2;
-  const uint32_t par = tc->phase_stage;
-  hsync();   // every thread has the parity before it flips
-  if (htid() == 0 && vbytes) {
-    tc->phase_stage = par ^ 1u;
-    sm100::fence_proxy_async();
-    sm100::mbar_arrive_expect_tx(&tc->stage, vbytes);
-    sm100::bulk_g2s(vs, vg, vbytes, &tc->stage);
+  // 1. every load in flight together: V by one bulk copy into shared memory,
+  //    this thread's key row of K, its score scale, Q, the registers, the
+  //    output scale of its column
+  if (htid() == 0) {
+    const uint32_t par = tc->phase_stage;
+    reinterpret_cast<uint32_t*>(red)[16] = par;
+    if (vbytes) {
+      tc->phase_stage = par ^ 1u;
+      sm100::fence_proxy_async();
+      sm100::mbar_arrive_expect_tx(&tc->stage, vbytes);
+      sm100::bulk_g2s(vs, vg, vbytes, &tc->stage);
+    }
   }
+  const uint32_t j0 = htid();   // this thread's key (nvis <= kThreads here; more keys loop below)
+  uint4 kv[16];
+  const uint8_t* kg = pptr(A, x.b, seq);
+  if (j0 < nvis) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kg + uint64_t(j0) * Kd * 2);
+#pragma unroll
+    for (uint32_t g = 0; g < 16; ++g)
+      if (g < Kd / 8) kv[g] = __ldcg(kr + g);
+  }
+  const uint16_t* scx = reinterpret_cast<const uint16_t*>(pptr(A, x.c, seq));
+  const uint16_t sxb = j0 < nvis ? scx[j0] : uint16_t(0);
+  const uint16_t sqb = sreg_bits(A, x.s[0], seq), skb = sreg_bits(A, x.s[1], seq);
+  const uint16_t svb = sreg_bits(A, y.s[1], seq), qsb = sreg_bits(A, y.s[0], seq);
+  const uint16_t syb = htid() < Ny ? reinterpret_cast<const uint16_t*>(pptr(A, y.c, seq))[htid()] : uint16_t(0);
   if (htid() < Kd / 4) {
-    const float sq = h2f(sreg_bits(A, x.s[0], seq));
+    const float sq = h2f(sqb);
     const uint2 qv = __ldcg(reinterpret_cast<const uint2*>(pptr(A, x.a, seq)) + htid());
     uint32_t w = 0;
 #pragma unroll
@@ -939,61 +1022,83 @@ __device__ __noinline__ void op_attn_row(const ExecArgs& A, const DevOp& x, cons
     q8w[htid()] = static_cast<int32_t>(w);
   }
   hsync();
-  {
-    // scores: one key per thread, its FP16 row quantised and dotted with Q
-    const float sk = h2f(sreg_bits(A, x.s[1], seq));
-    const uint8_t* kg = pptr(A, x.b, seq);
-    const uint16_t* scx = reinterpret_cast<const uint16_t*>(pptr(A, x.c, seq));
-    for (uint32_t j = htid(); j < nvis; j += kThreads) {
-      const uint4* kr = reinterpret_cast<const uint4*>(kg + uint64_t(j) * Kd * 2);
-      uint4 kv[16];
+  // 2. scores: the key row quantised (QUANT's rule) and dotted with Q, the
+  //    int32 dot dequantised to FP16 (F_DQ)
+  const float sk = h2f(skb);
+  auto score = [&](const uint4* kvp, uint16_t scb) {
+    int32_t acc = 0;
 #pragma unroll
-      for (uint32_t g = 0; g < 16; ++g)
-        if (g < Kd / 8) kv[g] = __ldcg(kr + g);
-      const float sc = h2f(scx[j]);
-      int32_t acc = 0;
+    for (uint32_t g = 0; g < 16; ++g) {
+      if (g >= Kd / 8) break;
+      int8_t q[8];
 #pragma unroll
-      for (uint32_t g = 0; g < 16; ++g) {
-        if (g >= Kd / 8) break;
-        int8_t q[8];
+      for (int e = 0; e < 8; ++e) q[e] = sat8(__fmul_rn(h2f(h_at(kvp[g], e)), sk));
+      const uint2 pk = pack_b(q);
+      acc = __dp4a(static_cast<int32_t>(pk.x), q8w[2 * g], acc);
+      acc = __dp4a(static_cast<int32_t>(pk.y), q8w[2 * g + 1], acc);
+    }
+    return h2f(f2h(__fmul_rn(__int2float_rn(acc), h2f(scb))));
+  };
+  if (j0 < nvis) rb[j0] = score(kv, sxb);
+  for (uint32_t j = j0 + kThreads; j < nvis; j += kThreads) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kg + uint64_t(j) * Kd * 2);
+    uint4 kw[16];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) q[e] = sat8(__fmul_rn(h2f(h_at(kv[g], e)), sk));
-        const uint2 pk = pack_b(q);
-        acc = __dp4a(static_cast<int32_t>(pk.x), q8w[2 * g], acc);
-        acc = __dp4a(static_cast<int32_t>(pk.y), q8w[2 * g + 1], acc);
+    for (uint32_t g = 0; g < 16; ++g)
+      if (g < Kd / 8) kw[g] = __ldcg(kr + g);
+    rb[j] = score(kw, scx[j]);
+  }
+  hsync();
+  // 3. the masked softmax row, softmax_row_f16's arithmetic: max over the
+  //    visible columns, exp in float64 rounded once, NumPy's pairwise sum,
+  //    f16(e / sum) quantised with the P.V op's register
+  const float qs = h2f(qsb);
+  uint32_t nl = 0, L = 0;
+  if (!pw_balanced(N, nl, L) || nvis == 0) {
+    if (warp == 0) softmax_row_f16(rb, N, masked, masked ? lt : int64_t(N) - 1, nullptr, pw, lane, p8, qs);
+  } else {
+    float mx = -INFINITY;
+    for (uint32_t j = htid(); j < nvis; j += kThreads) mx = fmaxf(mx, rb[j]);
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    hsync();
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, red[w]);
+    for (uint32_t j = htid(); j < N; j += kThreads) rb[j] = j < nvis ? exp_f32(__fsub_rn(rb[j], mx)) : 0.f;
+    hsync();
+    const float denom = ln_pairwise(rb, nl, L, false, 0.f, red + 8);
+    for (uint32_t j = htid(); j < N; j += kThreads) {
+      int8_t q8 = 0;
+      if (j < nvis) {
+        const float e = rb[j];
+        const uint16_t h = f2h(!masked ? __fdiv_rn(e, denom) : (denom > 0.f ? __fdiv_rn(e, denom) : 0.f));
+        q8 = sat8(__fmul_rn(h2f(h), qs));
       }
-      rb[j] = h2f(f2h(__fmul_rn(__int2float_rn(acc), sc)));
+      p8[j] = q8;
     }
   }
   hsync();
-  if (warp == 0)
-    softmax_row_f16(rb, N, masked, masked ? lt : int64_t(N) - 1, nullptr, pw, lane, p8,
-                    h2f(sreg_bits(A, y.s[0], seq)));
-  hsync();
-  {
-    // P.V: column n, keys kq, kq + nq, ... of the visible ones
-    const uint32_t nq = kThreads / Ny, n = htid() % Ny, kq = htid() / Ny;
-    const float sv = h2f(sreg_bits(A, y.s[1], seq));
-    if (vbytes && !sm100::mbar_wait(&tc->stage, par, nullptr, 0)) {
-      sm100::mbar_wait(&tc->stage, par, nullptr, 0);   // bounded: let the copy land, then fault
-      if (htid() == 0) raise_fault(A, DF_STAGE_TIMEOUT, t.op, seq);
-      return;
-    }
-    int32_t acc = 0;
-    if (kq < nq) {
+  // 4. P.V: column n, keys kq, kq + nq, ... of the visible ones, V from shared memory
+  const uint32_t par = reinterpret_cast<const uint32_t*>(red)[16];
+  const uint32_t nq = kThreads / Ny, n = htid() % Ny, kq = htid() / Ny;
+  const float sv = h2f(svb);
+  if (vbytes && !sm100::mbar_wait(&tc->stage, par, nullptr, 0)) {
+    sm100::mbar_wait(&tc->stage, par, nullptr, 0);   // bounded: let the copy land, then fault
+    if (htid() == 0) raise_fault(A, DF_STAGE_TIMEOUT, t.op, seq);
+    return;
+  }
+  int32_t acc = 0;
+  if (kq < nq) {
 #pragma unroll 4
-      for (uint32_t j = kq; j < nvis; j += nq)
-        acc += int32_t(p8[j]) * int32_t(sat8(__fmul_rn(h2f(vs[j * Ny + n]), sv)));
-    }
-    part[htid()] = acc;
-    hsync();
-    if (htid() < Ny) {
-      int32_t sum = 0;
-      for (uint32_t k = 0; k < nq; ++k) sum += part[k * Ny + htid()];   // int32 sums are exact in any order
-      const uint16_t* scy = reinterpret_cast<const uint16_t*>(pptr(A, y.c, seq));
-      uint16_t* out = reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(y.dconst), seq));
-      out[htid()] = f2h(__fmul_rn(__int2float_rn(sum), h2f(scy[htid()])));
-    }
+    for (uint32_t j = kq; j < nvis; j += nq) acc += int32_t(p8[j]) * int32_t(sat8(__fmul_rn(h2f(vs[j * Ny + n]), sv)));
+  }
+  part[htid()] = acc;
+  hsync();
+  if (htid() < Ny) {
+    int32_t sum = 0;
+    for (uint32_t k = 0; k < nq; ++k) sum += part[k * Ny + htid()];   // int32 sums are exact in any order
+    uint16_t* out = reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(y.dconst), seq));
+    out[htid()] = f2h(__fmul_rn(__int2float_rn(sum), h2f(syb)));
   }
 }
 
@@ -1964,71 +2069,6 @@ __device__ __forceinline__ void row_one(const ExecArgs& A, const DevOp& op, uint
 __device__ __forceinline__ bool ln_small_ok(const DevOp& op) {
   uint32_t nl, L;
   return op.kind == K_LAYERNORM_F16 && op.M <= 2 && op.N % 8 == 0 && op.N <= kRowCap && pw_balanced(op.N, nl, L);
-}
-
-// NumPy's pairwise sum of x[0..N) (or of (x - mean)^2), for a balanced tree
-// of nl <= 8 leaves of L elements, by every warp of the half: warp w sums
-// leaf w (lanes 0..7 one accumulator chain each, combined by xor shuffles),
-// the leaf sums combine level by level.  `part` holds 8 floats; every thread
-// returns the sum.  Contains one hsync.
-__device__ __forceinline__ float ln_pairwise(const float* x, uint32_t nl, uint32_t L, bool sq, float mean,
-                                             float* part) {
-  const uint32_t warp = htid() >> 5, lane = htid() & 31;
-  float v = 0.f;
-  if (warp < nl && lane < 8) {
-    const float* q = x + warp * L + lane;
-    float r;
-    if (sq) {
-      const float d0 = __fsub_rn(q[0], mean);
-      r = __fmul_rn(d0, d0);
-      for (uint32_t i = 8; i < L; i += 8) {
-        const float d = __fsub_rn(q[i], mean);
-        r = __fadd_rn(r, __fmul_rn(d, d));
-      }
-    } else {
-      r = q[0];
-      for (uint32_t i = 8; i < L; i += 8) r = __fadd_rn(r, q[i]);
-    }
-    v = r;
-  }
-  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
-  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
-  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
-  if (lane == 0 && warp < nl) part[warp] = v;
-  hsync();
-  float t8[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) t8[k] = part[k < int(nl) ? k : 0];
-  for (uint32_t w = nl; w > 1; w >>= 1)
-#pragma unroll
-    for (uint32_t k = 0; k < 4; ++k)
-      if (k < w / 2) t8[k] = __fadd_rn(t8[2 * k], t8[2 * k + 1]);
-  return t8[0];
-}
-
-// mean and denominator sqrt(var + eps) of the row in x (float32, N
-// elements, balanced tree), as NumPy's mean and var compute them.  Uses
-// part[0..16); contains two hsyncs.
-__device__ __forceinline__ void ln_stats(const float* x, uint32_t N, float* part, float& mean, float& denom) {
-  uint32_t nl, L;
-  pw_balanced(N, nl, L);
-  mean = div_count(ln_pairwise(x, nl, L, false, 0.f, part), N);
-  const float var = div_count(ln_pairwise(x, nl, L, true, mean, part + 8), N);
-  denom = __fsqrt_rn(__fadd_rn(var, 1e-5f));
-}
-
-// The LayerNorm output of 4 elements (x as floats, gamma and beta as FP16
-// pairs in uint2), row_one's arithmetic.
-__device__ __forceinline__ uint2 ln_out4(const float (&xs)[4], float mean, float denom, uint2 gv, uint2 bv) {
-  const uint16_t* g16 = reinterpret_cast<const uint16_t*>(&gv);
-  const uint16_t* b16 = reinterpret_cast<const uint16_t*>(&bv);
-  uint16_t h[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float y = __fdiv_rn(__fsub_rn(xs[j], mean), denom);
-    h[j] = f2h(__fadd_rn(__fmul_rn(y, h2f(g16[j])), h2f(b16[j])));
-  }
-  return make_uint2(uint32_t(h[0]) | (uint32_t(h[1]) << 16), uint32_t(h[2]) | (uint32_t(h[3]) << 16));
 }
 
 __device__ __noinline__ void op_ln_small(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
