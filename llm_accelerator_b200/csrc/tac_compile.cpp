@@ -613,6 +613,127 @@ class Compiler {
     return true;
   }
 
+  // A MAX_ABS (with or without a segment list) whose operand runs lie in the
+  // output of a GELU op reads that GELU's input instead, through segments
+  // flagged kSegGelu (FX_GELUSEG): the executor applies the GELU to each value
+  // and rounds it to FP16, which is the value the GELU op stores.  The GELU's
+  // input must be immutable (arena or shared); its output then has one reader
+  // fewer and, in the decode streams, none, so the GELU op and its level go.
+  // Refused when the segment list would outgrow kMaxSegRuns.
+  void gelu_into_maxabs(DevOp& op, Access& acc, uint64_t units) {
+    if (gelu_out_.empty() || units == 0) return;
+    struct Run { uint64_t src, dst, n; bool gelu; };
+    std::vector<Run> in;
+    if (op.flags & F_SEGA)
+      for (uint32_t k = 0; k < op.nseg; ++k) in.push_back({P->segs[op.seg0 + k].src, P->segs[op.seg0 + k].dst,
+                                                            P->segs[op.seg0 + k].n, false});
+    else
+      in.push_back({op.a, 0, units, false});
+    std::vector<Run> out;
+    bool any = false;
+    for (const Run& r : in) {
+      auto it = gelu_out_.upper_bound(r.src);
+      if (it == gelu_out_.begin() || cls(r.src) != PC_ARENA) { out.push_back(r); continue; }
+      --it;
+      const DevOp& g = P->ops[it->second];
+      const uint64_t gu = uint64_t(g.M) * g.N * 2 / kUnit;
+      if (r.src < g.d || r.src + r.n > g.d + gu) { out.push_back(r); continue; }
+      // GELU output unit o is GELU operand unit o: map [o, o + n) through the GELU's input
+      uint64_t o = r.src - g.d, left = r.n, dst = r.dst;
+      bool ok = true;
+      std::vector<Run> pieces;
+      while (left && ok) {
+        uint64_t src = 0, run = 0;
+        if (g.flags & F_SEGA) {
+          ok = false;
+          for (uint32_t k = 0; k < g.nseg; ++k) {
+            const Segment& gs = P->segs[g.seg0 + k];
+            if (gs.dst <= o && o < gs.dst + gs.n) {
+              src = gs.src + (o - gs.dst);
+              run = std::min(left, gs.dst + gs.n - o);
+              ok = true;
+              break;
+            }
+          }
+        } else {
+          src = g.a + o;
+          run = left;
+        }
+        if (!ok || (cls(src) != PC_ARENA && cls(src) != PC_SHARED)) { ok = false; break; }
+        pieces.push_back({src, dst, run, true});
+        o += run;
+        dst += run;
+        left -= run;
+      }
+      if (!ok) { out.push_back(r); continue; }
+      out.insert(out.end(), pieces.begin(), pieces.end());
+      any = true;
+    }
+    if (!any || out.size() > kMaxSegRuns) return;
+    // the op's segments are the last ones written (src_segments) or none yet
+    if (op.flags & F_SEGA) P->segs.resize(op.seg0);
+    op.seg0 = static_cast<uint32_t>(P->segs.size());
+    acc.reads.erase(std::remove_if(acc.reads.begin(), acc.reads.end(),
+                                   [&](const std::pair<uint64_t, uint64_t>& rd) {
+                                     for (const Run& r : in)
+                                       if (rd.first == r.src) return true;
+                                     return false;
+                                   }),
+                    acc.reads.end());
+    for (const Run& r : out) {
+      P->segs.push_back(Segment{r.src, r.dst | (r.gelu ? kSegGelu : 0ull), r.n});
+      acc.reads.push_back({r.src, r.n});
+    }
+    op.nseg = static_cast<uint32_t>(out.size());
+    op.a = 0;
+    op.flags |= F_SEGA;
+    op.flags2 |= FX_GELUSEG;
+  }
+
+  // A STORE through a runtime register of the first r rows of a tcgen05
+  // MATMUL's FX_DQS FP16 result (a decode step's K / V append), whose other
+  // hazards are all settled by that MATMUL's level: the MATMUL's epilogue
+  // writes those rows to the runtime address as well (FX_DSTORE), at its own
+  // level, and the store op is not emitted.  The write is committed at that
+  // level with the store's runtime-address bookkeeping (equalities it relies
+  // on become run-time checks, as for any op).
+  bool absorb_store(const DevOp& st, const Access& acc) {
+    if (st.param < 0 || st.dconst < 0 || st.dconst >= (int64_t(1) << 32)) return false;
+    auto it = dqs_out_.find(st.a);
+    if (it == dqs_out_.end()) return false;
+    DevOp& mm = P->ops[it->second];
+    const uint64_t row = uint64_t(mm.N) * 2;
+    if ((mm.flags2 & FX_DSTORE) || !(mm.flags2 & FX_DQS) || row == 0 || st.nbytes % row || st.nbytes / row == 0 ||
+        st.nbytes / row > mm.M || !tc_eligible(mm.a, mm.b, mm.M, mm.N, mm.K) || (mm.flags & F_ACCUMULATE))
+      return false;
+    Access probe = acc;
+    probe.reads.clear();
+    for (auto& r : acc.reads)
+      if (!(r.first >= st.a && r.first + r.second <= st.a + st.nbytes / kUnit)) probe.reads.push_back(r);
+    pending_same_.clear();
+    if (level_for(probe) > int32_t(mm.level)) return false;
+    commit(acc, int32_t(mm.level));
+    for (int prm : pending_same_) {   // equalities the level relied on
+      const int g = site_group_[prm];
+      if (prm == g || same_checked_[prm]) continue;
+      same_checked_[prm] = 1;
+      RtCheck c{};
+      c.kind = CHK_SAME;
+      c.param = static_cast<uint32_t>(prm);
+      c.pc = pc_;
+      c.lo = static_cast<uint64_t>(g);
+      P->checks.push_back(c);
+    }
+    ++home_writes_;
+    mm.flags2 |= FX_DSTORE;
+    mm.param = st.param;
+    mm.attn_qrb = static_cast<uint32_t>(st.dconst);
+    mm.attn_vkl = static_cast<uint32_t>(st.nbytes / row);
+    pure_before_store_[it->second] = op_pure_[it->second];
+    op_pure_[it->second] = 0;   // a DRAM write: kept whatever reads its arena results
+    return true;
+  }
+
   // QUANT of exactly the units a MAX_ABS just reduced, with that MAX_ABS's
   // inverse scale: the MAX_ABS op writes the int8 result as well (FX_MAXQ).
   // The input units must be immutable (arena or shared), so the values the
@@ -680,6 +801,7 @@ class Compiler {
     mm.nbytes = mb[nh];
     mm.s[0] = sreg;
     mm.dconst = static_cast<int64_t>(out);
+    dqs_out_[out] = idx;
     for (auto& w : acc.writes)
       if (cls(w.first) == PC_ARENA) op_arena_writes_[idx].push_back(w);
     for (auto& r : acc.reads)
@@ -970,6 +1092,9 @@ class Compiler {
     uint64_t elems = 0;
   };
   std::unordered_map<uint32_t, MaxAbsOf> maxabs_by_slot_;
+  std::map<uint64_t, uint32_t> gelu_out_;   // GELU op output extent start -> op index
+  std::unordered_map<uint64_t, uint32_t> dqs_out_;   // FX_DQS FP16 result extent -> tcgen05 MATMUL index
+  std::unordered_map<uint32_t, uint8_t> pure_before_store_;   // FX_DSTORE MATMUL -> op_pure_ before the store
   // output extent of the latest VADD of each open chain -> op index; operand lists of the chains
   std::unordered_map<uint64_t, uint32_t> vadd_tail_;
   // softmax output extent of a wide QK^T + softmax op -> op index; QK^T op -> its P.V op
@@ -1175,6 +1300,7 @@ int Compiler::h_store(const Insn& x) {                      // dma.py:47-64
   acc.dyn_write = true;
   acc.dyn_c0 = op.dconst;
   acc.dyn_c1 = op.dconst + int64_t(n);
+  if (absorb_store(op, acc)) return 0;
   emit(op, acc);
   return 0;
 }
@@ -1527,6 +1653,7 @@ int Compiler::h_rtype(const Insn& x) {
       TRY(span(x.src1_buf, x.src1_off, M * N * 2));
       op.kind = K_MAX_ABS;
       if (!src_segments(s1, M * N * 2, acc, op)) op.a = src(s1, M * N * 2, acc);
+      gelu_into_maxabs(op, acc, M * N * 2 / kUnit);
       op.out_slot = new_slot();
       new_slot();
       acc.slot_writes.push_back(op.out_slot);
@@ -1624,6 +1751,9 @@ int Compiler::h_rtype(const Insn& x) {
   if (op.kind == K_VADD_F16 && !(op.flags & F_SEGA) && !P->ops.empty() && P->ops.back().kind == K_VADD_F16 &&
       P->ops.back().d == op.d && cls(op.d) == PC_ARENA)
     vadd_tail_[op.d] = static_cast<uint32_t>(P->ops.size() - 1);
+  if (op.kind == K_GELU_F16 && P->ops.size() == n_before + 1 && (op.flags & ~F_SEGA) == 0 &&
+      cls(P->ops.back().d) == PC_ARENA)
+    gelu_out_[P->ops.back().d] = static_cast<uint32_t>(n_before);
   if (op.kind == K_MAX_ABS) {   // remember the input of the MAX_ABS just emitted
     if (!P->ops.empty() && P->ops.back().kind == K_MAX_ABS && P->ops.back().out_slot == op.out_slot) {
       MaxAbsOf& m = maxabs_by_slot_[op.out_slot];
@@ -1796,7 +1926,7 @@ static bool row_wise(const DevOp& op0, uint32_t& in_es) {
     case K_MATMUL:
       in_es = 1;
       return tc_eligible(op.a, op.b, op.M, op.N, op.K) && (op.flags & ~F_NOI32) == 0 &&
-             (op.flags2 & ~FX_DQS) == 0 && (!(op.flags & F_NOI32) || (op.flags2 & FX_DQS));
+             (op.flags2 & ~(FX_DQS | FX_DSTORE)) == 0 && (!(op.flags & F_NOI32) || (op.flags2 & FX_DQS));
     default: return false;
   }
 }
@@ -1993,7 +2123,10 @@ void Compiler::drop_dead_walk(std::vector<uint8_t>& keep, const std::vector<uint
       }
     }
     uint32_t in_es = 0;
-    if (op_pure_[i] && row_wise(op, in_es) && (uint64_t(op.K) * in_es) % kUnit == 0 &&
+    // an absorbed store is the only effect of an FX_DSTORE MATMUL besides its arena results
+    const bool store_only = (op.flags2 & FX_DSTORE) && pure_before_store_.count(static_cast<uint32_t>(i)) &&
+                            pure_before_store_[static_cast<uint32_t>(i)];
+    if ((op_pure_[i] || store_only) && row_wise(op, in_es) && (uint64_t(op.K) * in_es) % kUnit == 0 &&
         (uint64_t(op.N) * in_es) % kUnit == 0 && op.N % kUnit == 0) {
       const std::vector<Segment>* chain = op.kind == K_VADD_CHAIN ? &chains_[op.param] : nullptr;
       const auto outs = row_outputs(op, chain);
@@ -2004,6 +2137,7 @@ void Compiler::drop_dead_walk(std::vector<uint8_t>& keep, const std::vector<uint
       };
       uint32_t m = op.M;
       while (m > 1 && !row_read(m - 1)) --m;
+      if (op.flags2 & FX_DSTORE) m = std::max(m, op.attn_vkl);   // the rows the store writes out
       if (op.kind == K_MATMUL)   // 128 / m sequences share one tensor-core tile
         while (!tc_rows_ok(m) && m < op.M) ++m;
       if (m < op.M) {
@@ -2499,9 +2633,10 @@ void Compiler::prefetch_hint(const DevOp& op, Task& t) const {
     const uint64_t u0 = op.kind == K_MAX_ABS ? 0 : uint64_t(t.tile) * kSegTaskUnits;
     for (uint32_t k = 0; k < op.nseg; ++k) {
       const Segment& sg = P->segs[op.seg0 + k];
-      if (sg.dst <= u0 && u0 < sg.dst + sg.n) {
-        phys = sg.src + (u0 - sg.dst);
-        units = std::min<uint64_t>(sg.dst + sg.n - u0, op.kind == K_MAX_ABS ? sg.n : kSegTaskUnits);
+      const uint64_t sd = sg.dst & ~kSegGelu;
+      if (sd <= u0 && u0 < sd + sg.n) {
+        phys = sg.src + (u0 - sd);
+        units = std::min<uint64_t>(sd + sg.n - u0, op.kind == K_MAX_ABS ? sg.n : kSegTaskUnits);
         break;
       }
     }

@@ -1163,6 +1163,14 @@ __device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp
                                   : reinterpret_cast<const uint16_t*>(pptr(A, op.nbytes, seq)) + col0;
       uint16_t* O = reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(op.dconst), seq)) +
                     uint64_t(row) * N + col0;
+      // FX_DSTORE: the absorbed store of the first attn_vkl rows to the runtime address
+      uint16_t* Ost = nullptr;
+      if ((op.flags2 & FX_DSTORE) && row < op.attn_vkl) {
+        const uint64_t addr = A.params[uint64_t(seq) * A.n_params + op.param] + op.attn_qrb +
+                              (uint64_t(row) * N + col0) * 2;
+        if ((addr & 15) || addr + nc * 2 > A.dram_bytes || addr < A.shared_bytes) raise_fault(A, DF_DYN_ADDRESS, t.op, seq);
+        else Ost = reinterpret_cast<uint16_t*>(dram_ptr(A, addr, seq));
+      }
 #pragma unroll
       for (uint32_t j = 0; j < 32; j += 8) {
         if (j < nc) {
@@ -1176,6 +1184,7 @@ __device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp
             hh[k] = f2h(__fadd_rn(x, h2f(h_at(b8, k))));
           }
           *reinterpret_cast<uint4*>(O + j) = pack_h(hh);
+          if (Ost) *reinterpret_cast<uint4*>(Ost + j) = pack_h(hh);
         }
       }
       if (op.flags & F_NOI32) return;
@@ -1747,14 +1756,28 @@ constexpr uint32_t kMaxQStage = 8192;   // MAX_ABS + QUANT: the reduced input, 1
 __device__ __forceinline__ uint32_t seg_stage(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
   uint32_t* ofs = reinterpret_cast<uint32_t*>(smem + kSegTableOff);
   uint64_t* src = reinterpret_cast<uint64_t*>(smem + kSegTableOff + kMaxSegRuns * 4);
+  uint8_t* gelu = smem + kSegTableOff + kMaxSegRuns * 12;   // kSegGelu flag of each segment
   const uint32_t first = t.aux ? (t.aux & 0xFFFFu) : 0u, count = t.aux ? (t.aux >> 16) : op.nseg;
   for (uint32_t k = htid(); k < count; k += kThreads) {
     const Segment sg = A.segs[op.seg0 + first + k];
-    ofs[k] = static_cast<uint32_t>(sg.dst);
+    ofs[k] = static_cast<uint32_t>(sg.dst);   // the offset (the flag bit lies above 32 bits)
     src[k] = sg.src;
+    gelu[k] = (sg.dst & kSegGelu) ? 1 : 0;
   }
   hsync();
   return count;
+}
+
+// The staged segment (index) holding operand unit u (nseg segments staged).
+__device__ __forceinline__ uint32_t seg_index(uint32_t nseg, const uint8_t* smem, uint32_t u) {
+  const uint32_t* ofs = reinterpret_cast<const uint32_t*>(smem + kSegTableOff);
+  uint32_t lo = 0, hi = nseg;   // last k with ofs[k] <= u
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (ofs[mid] <= u) lo = mid;
+    else hi = mid;
+  }
+  return lo;
 }
 
 // Address of operand unit u (segments staged by seg_stage; nseg of them).
@@ -1762,12 +1785,7 @@ __device__ __forceinline__ const uint4* seg_unit(const ExecArgs& A, uint32_t nse
                                                  uint32_t seq, uint32_t u) {
   const uint32_t* ofs = reinterpret_cast<const uint32_t*>(smem + kSegTableOff);
   const uint64_t* src = reinterpret_cast<const uint64_t*>(smem + kSegTableOff + kMaxSegRuns * 4);
-  uint32_t lo = 0, hi = nseg;   // last k with ofs[k] <= u
-  while (hi - lo > 1) {
-    const uint32_t mid = (lo + hi) >> 1;
-    if (ofs[mid] <= u) lo = mid;
-    else hi = mid;
-  }
+  const uint32_t lo = seg_index(nseg, smem, u);
   return reinterpret_cast<const uint4*>(pptr(A, src[lo], seq)) + (u - ofs[lo]);
 }
 
@@ -1839,6 +1857,20 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
     for (int k = 0; k < 8; ++k) {
       const uint64_t g = g0 + uint64_t(k) * kThreads;
       v[k] = g < ng ? __ldcg(seg ? seg_unit(A, nseg, smem, seq, uint32_t(g)) : xv + g) : make_uint4(0, 0, 0, 0);
+    }
+    if (op.flags2 & FX_GELUSEG) {
+      // segments that read a GELU's input: the value the GELU op would have stored
+      const uint8_t* gelu = smem + kSegTableOff + kMaxSegRuns * 12;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint64_t g = g0 + uint64_t(k) * kThreads;
+        if (g < ng && gelu[seg_index(nseg, smem, uint32_t(g))]) {
+          uint16_t h[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) h[j] = f2h(gelu_f32(h2f(h_at(v[k], j))));
+          v[k] = pack_h(h);
+        }
+      }
     }
     if (maxq) {
 #pragma unroll
@@ -2117,6 +2149,7 @@ __device__ __forceinline__ bool chain_vln_ok(const ExecArgs& A, const Task& t) {
   const DevOp& m = A.ops[tp[2].op];
   const uint32_t N = v.N, ru = N / 8;
   if (v.kind != K_VADD_F16 || l.kind != K_LAYERNORM_F16 || m.kind != K_MAX_ABS || !(m.flags2 & FX_MAXQ) ||
+      (m.flags2 & FX_GELUSEG) ||
       !(m.flags & F_SEGA) || v.M != 1 || l.M != 1 || l.N != N || m.N != N || N % 8 || N > 4 * kThreads ||
       !ln_small_ok(l) || l.a != v.d || m.nseg > 8 || (m.q_rows ? m.q_rows : m.M) != 1 || (v.flags & ~F_SEGA) ||
       (l.flags & ~F_SPLIT))
@@ -2504,7 +2537,7 @@ static_assert(kWideMmSmem <= kExecOpSmem, "wide MATMUL exceeds the op shared mem
 static_assert(kWarps == int(kExecWarps) && kPwScratchBytes == kWarps * 3 * kPwMaxLeaves * 4,
               "FX_PV layout constants disagree with the executor");
 static_assert(kSegTableOff + kMaxSegRuns * 12 <= kExecOpSmem, "segment table exceeds the op shared memory");
-static_assert(kSegTableOff + kMaxSegRuns * 12 <= kMaxQStage && kMaxQStage + 16384 * 2 <= kExecOpSmem,
+static_assert(kSegTableOff + kMaxSegRuns * 13 <= kMaxQStage && kMaxQStage + 16384 * 2 <= kExecOpSmem,
               "MAX_ABS staging overlaps the segment table or exceeds the op shared memory");
 static_assert(kExecOpSmem % 1024 == 0 || kTcSmem <= kExecOpSmem, "half regions must keep the stage alignment slack");
 static_assert(kExecSmem <= 227 * 1024, "executor shared memory exceeds one CTA's limit");

@@ -107,6 +107,13 @@ constexpr uint32_t FX_CHAINED = 64;    // per-sequence row op that runs in the t
 constexpr uint32_t FX_CHAINHEAD = 128; // first op of such a chain: its tasks (one per sequence) hold, in tile
                                        // and aux, the first and count of the chain's task templates, stored
                                        // after the last level's tasks (seq0 taken from the head's task)
+constexpr uint32_t FX_GELUSEG = 512;   // F_SEGA MAX_ABS some of whose segments (dst | kSegGelu) read a GELU's
+                                       // input: the value is f16(gelu(x)) of the unit read, as the GELU op
+                                       // would have stored it
+constexpr uint64_t kSegGelu = 1ull << 62;   // Segment.dst flag of such a segment (dst & ~kSegGelu is the offset)
+constexpr uint32_t FX_DSTORE = 1024;   // FX_DQS tcgen05 MATMUL that also stores the first attn_vkl rows of its
+                                       // FP16 result to writable DRAM at params[param] + attn_qrb (a STORE
+                                       // through a runtime register, e.g. a KV-cache append, absorbed)
 constexpr uint32_t FX_TCRES = 256;     // tcgen05 MATMUL (64-column tasks) whose every K chunk fits in shared
                                        // memory at once: A boxes of q_rows rows packed back to back, then B;
                                        // no stage is reused

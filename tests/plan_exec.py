@@ -15,6 +15,7 @@ from oracle import golden as G
 SRAM_UNITS = 8192 + 16384 + 4096
 SHARED = 1 << 63
 CONST = 1 << 31
+SEG_GELU = 1 << 62   # kSegGelu
 K = dict(GATHER=1, DYN_LOAD=2, DYN_STORE=3, SREG_LOAD=4, SREG_FINAL=5, MATMUL=6, REQUANT=7, REQUANT_PC=8,
          SCALE_MUL_I32=9, SCALE_MUL_I8=10, VADD_I8=11, VADD_I32=12, DEQUANT_ADD=13, DEQUANT_ACCUM=14,
          DEQUANT_SCALED=15, QUANT=16, VADD_F16=17, LAYERNORM_F16=18, GELU_F16=19, SOFTMAX_F16=20,
@@ -68,10 +69,15 @@ def _seg_read(m: PlanMachine, op, segs, nbytes: int) -> np.ndarray:
     """Operand a of an F_SEGA op: the runs of its segment list, in order."""
     out = np.zeros(nbytes, np.uint8)
     for sg in segs[int(op["seg0"]):int(op["seg0"]) + int(op["nseg"])]:
-        o, n = int(sg["dst"]) * 16, int(sg["n"]) * 16
+        dst = int(sg["dst"])
+        o, n = (dst & ~SEG_GELU) * 16, int(sg["n"]) * 16
         n = min(n, nbytes - o)   # an op narrowed to its first rows reads the runs below them
         if n > 0:
-            out[o:o + n] = m.mem(int(sg["src"]), n)
+            v = m.mem(int(sg["src"]), n)
+            if dst & SEG_GELU:   # a GELU's input: the value the GELU op stores (FX_GELUSEG MAX_ABS)
+                x = v.view(np.float16).astype(np.float32)
+                v = G._gelu_tanh(x).astype(np.float32).astype(np.float16).view(np.uint8)
+            out[o:o + n] = v
     return out
 
 
@@ -221,7 +227,12 @@ def _run_op(m: PlanMachine, op, segs, params):
         if op["flags2"] & 1:   # FX_DQS: DEQUANT_ACCUM_FP32_SCALED's FP16 result as well
             r = (acc.astype(np.float32) * _f16(m, c, N).reshape(1, N) * np.float32(m.sreg(s[0]))
                  + _f16(m, int(op["nbytes"]), N).reshape(1, N))
-            m.mem(int(op["dconst"]), M * N * 2)[:] = r.astype(np.float32).astype(np.float16).view(np.uint8).ravel()
+            out16 = r.astype(np.float32).astype(np.float16).view(np.uint8).ravel()
+            m.mem(int(op["dconst"]), M * N * 2)[:] = out16
+            if op["flags2"] & 1024:   # FX_DSTORE: the first attn_vkl rows to the runtime address too
+                rows = int(op["attn_vkl"])
+                addr = int(params[int(op["param"])]) + int(op["attn_qrb"])
+                m.dram_mem(addr, rows * N * 2)[:] = out16[:rows * N * 2]
         if op["flags"] & 2048:   # F_DQ: DEQUANT_ACCUM's FP16 result as well
             out = (acc.astype(np.float32) * _f16(m, c, N).reshape(1, N)).astype(np.float16)
             if not op["flags"] & 32768:   # F_NODQ
