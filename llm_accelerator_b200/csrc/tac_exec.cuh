@@ -2205,7 +2205,16 @@ __device__ __noinline__ void op_chain_vln(const ExecArgs& A, const Task& t, uint
   for (uint32_t k = 1; k < m.nseg; ++k) {
     const Segment sk = A.segs[m.seg0 + k];
     const uint4* src = reinterpret_cast<const uint4*>(pptr(A, sk.src, seq));
-    for (uint64_t u = htid(); u < sk.n; u += kThreads) mx = absmax8(__ldcg(src + u), mx);
+    for (uint64_t u0 = htid(); u0 < sk.n; u0 += 8 * kThreads) {   // eight loads in flight per thread
+      uint4 w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint64_t u = u0 + uint64_t(j) * kThreads;
+        w[j] = u < sk.n ? __ldcg(src + u) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx = absmax8(w[j], mx);
+    }
   }
   // 2. VADD: f16(a + b), stored for later ops and kept as float32
   if (htid() < ru) {
