@@ -20,6 +20,7 @@
 #include <unordered_map>
 #include <new>
 #include <string>
+#include <tuple>
 
 #include "tac_program.h"
 
@@ -2491,7 +2492,13 @@ void Compiler::build_tasks() {
       out.push_back(Task{opi, 0, 1, t, (op.kind != K_MAX_ABS && (op.flags & F_SEGA)) ? seg_aux(op, t) : 0u});
   };
   std::vector<Task> templates;
-  std::vector<std::pair<size_t, uint32_t>> heads;   // (level, index in per_level) of chain head tasks
+  std::vector<std::pair<size_t, uint32_t>> heads;   // (level, index in per_level) of chain / group head tasks
+  std::map<uint32_t, std::vector<uint32_t>> attn_pairs;   // level -> its row-attention QK^T ops
+  auto attn_groupable = [&](const DevOp& x) {
+    if (!(x.flags2 & FX_PV) || x.M != 1) return false;
+    const DevOp& y = P->ops[x.seg0];
+    return attn_row_shape_ok(x.M, x.K, x.N, x.flags, x.flags2, y.M, y.K, y.N, y.flags);
+  };
   for (uint32_t i = 0; i < P->ops.size(); ++i) {
     const DevOp& op = P->ops[i];
     const uint64_t MN = uint64_t(op.M) * op.N;
@@ -2533,6 +2540,10 @@ void Compiler::build_tasks() {
         const bool shared_b = (op.b & kSharedBit) != 0;
         if ((op.flags & F_WIDE) || (!(op.flags & F_TC) && !shared_b && wide_mm_ok(op.M, op.N, op.K, false, false))) {
           P->ops[i].flags |= F_WIDE;   // one task per sequence, every column
+          if (attn_groupable(P->ops[i])) {
+            attn_pairs[op.level].push_back(i);   // tasks below, per pair or per head group
+            break;
+          }
           per_seq(i, 1);
           break;
         }
@@ -2596,11 +2607,63 @@ void Compiler::build_tasks() {
       }
     }
   }
+  // Row-attention pairs of a level: when a task per pair and sequence would
+  // take more than one round over the executor's halves, pairs of one shape
+  // go in head groups (FX_ATTNGRP) of g pairs of a sequence, the least g
+  // that fits one round (at most kAttnGroupMax when none does): a group task
+  // overlaps each pair's copies with the pair before it.
+  for (auto& lp : attn_pairs) {
+    std::map<std::tuple<uint32_t, uint32_t, uint32_t>, std::vector<uint32_t>> by_shape;
+    for (uint32_t i : lp.second) {
+      const DevOp& x = P->ops[i];
+      by_shape[std::make_tuple(x.K, x.N, P->ops[x.seg0].N)].push_back(i);
+    }
+    for (auto& sh : by_shape) {
+      const std::vector<uint32_t>& xs = sh.second;
+      const uint32_t n = static_cast<uint32_t>(xs.size()), gmax = std::min(n, kAttnGroupMax);
+      uint32_t g = 1;
+      if (uint64_t(B) * n > kTargetHalves) {
+        g = gmax;
+        for (uint32_t c = 2; c <= gmax; ++c)
+          if (uint64_t(B) * ((n + c - 1) / c) <= kTargetHalves) {
+            g = c;
+            break;
+          }
+      }
+      for (uint32_t k0 = 0; k0 < n; k0 += g) {
+        if (g == 1) {
+          per_seq(xs[k0], 1);
+          continue;
+        }
+        const uint32_t first = static_cast<uint32_t>(templates.size()), cnt = std::min(g, n - k0);
+        for (uint32_t k = k0; k < k0 + cnt; ++k) templates.push_back(Task{xs[k], 0, 1, 0, 0});
+        P->ops[xs[k0]].flags2 |= FX_ATTNGRP;
+        for (uint32_t s = 0; s < B; ++s) {
+          heads.push_back({lp.first, static_cast<uint32_t>(per_level[lp.first].size())});
+          per_level[lp.first].push_back(Task{xs[k0], s, 1, first, cnt});
+        }
+      }
+    }
+  }
   P->tasks.clear();
   P->level_off.assign(1, 0);
   for (auto& v : per_level) {
-    for (Task& t : v)
-      if (!(P->ops[t.op].flags2 & FX_CHAINHEAD)) prefetch_hint(P->ops[t.op], t);
+    for (Task& t : v) {
+      const DevOp& op = P->ops[t.op];
+      if (!(op.flags2 & FX_CHAINHEAD)) {
+        prefetch_hint(op, t);
+        continue;
+      }
+      // a chain head: the first LayerNorm's gamma (and beta, when they are
+      // one vector) of its chain, read-only and ready before the level
+      for (uint32_t j = t.op; j < P->ops.size() && (j == t.op || (P->ops[j].flags2 & FX_CHAINED)); ++j)
+        if (P->ops[j].kind == K_LAYERNORM_F16) {
+          const DevOp& l = P->ops[j];
+          t.pf_phys = l.b;
+          t.pf_units = static_cast<uint32_t>(uint64_t(l.N) * 2 * ((l.flags & F_SPLIT) ? 1 : 2) / kUnit);
+          break;
+        }
+    }
     P->tasks.insert(P->tasks.end(), v.begin(), v.end());
     P->level_off.push_back(static_cast<uint32_t>(P->tasks.size()));
   }

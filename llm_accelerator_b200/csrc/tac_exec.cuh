@@ -517,10 +517,12 @@ struct TcShared {
   uint64_t full[kTcStages];    // TMA bytes of a stage landed
   uint64_t empty[kTcStages];   // the MMAs reading a stage completed
   uint64_t stage;              // bulk-copied element-wise operands landed
+  uint64_t stage2;             // row attention: its V rows landed
   uint32_t tmem;
   uint32_t phase_full;         // bit s: parity of the next phase of full[s]
   uint32_t phase_empty;
   uint32_t phase_stage;        // parity of the next phase of `stage`
+  uint32_t phase_stage2;       // parity of the next phase of `stage2`
   uint32_t pv_phase;           // FX_PVPF: parity of the `stage` phase that brings V
 };
 
@@ -941,164 +943,338 @@ __device__ __forceinline__ uint2 ln_out4(const float (&xs)[4], float mean, float
 }
 
 // ---------------------------------------------------------------------------------
-// One query row of an attention pair: an FX_PV QK^T op and its P.V op, both
-// narrowed to row 0 (a decode step).  The scores, the masked softmax and P.V
-// run on CUDA cores with the wide path's arithmetic element for element: the
-// QUANT rule on Q, K, P and V, exact int32 dot products (dp4a), the F_DQ
-// dequantisation of scores and output, softmax_row_f16.  Keys past the row's
-// last visible one get P = 0 there and are skipped here.
+// Row attention: one query row of an attention pair, an FX_PV QK^T op and its
+// P.V op, both narrowed to row 0 (a decode step).  The scores, the masked
+// softmax and P.V run on CUDA cores with the wide path's arithmetic element
+// for element: the QUANT rule on Q, K, P and V, exact int32 dot products
+// (dp4a), the F_DQ dequantisation of scores and output, softmax_row_f16.
+// Keys past the row's last visible one get P = 0 there and are skipped here.
+// A task runs one pair, or the pairs of a head group (FX_ATTNGRP) of one
+// sequence one after another.  The visible K and V rows arrive by bulk copy
+// into shared memory; in a group the next pair's K rows are copied once this
+// pair's scores are out and its V rows once this pair's P.V is done.
 // ---------------------------------------------------------------------------------
-constexpr uint32_t kAttnRowVOff = 8192;   // V rows of op_attn_row, after its scores and scratch
-
 __device__ __forceinline__ bool attn_row_ok(const ExecArgs& A, const DevOp& x) {
-  constexpr uint16_t need = F_WIDE | F_QA | F_QB | F_BT | F_DQ | F_SM | F_NOI32 | F_NODQ;
-  if (x.M != 1 || (x.flags & need) != need || (x.flags & F_ACCUMULATE) || !(x.flags2 & FX_SMSKIP)) return false;
-  if (x.K % 8 || x.K > 128 || x.N % 8 || x.N > 1024) return false;
+  if (x.M != 1 || !(x.flags2 & FX_PV)) return false;
   const DevOp& y = A.ops[x.seg0];
-  constexpr uint16_t yneed = F_WIDE | F_QB | F_DQ | F_NOI32;
-  return y.M == 1 && (y.flags & yneed) == yneed && !(y.flags & (F_BT | F_ACCUMULATE | F_NODQ)) && y.K == x.N &&
-         y.N % 8 == 0 && y.N <= 64 && kAttnRowVOff + x.N * y.N * 2 <= kWideMmSmem;
+  return attn_row_shape_ok(x.M, x.K, x.N, x.flags, x.flags2, y.M, y.K, y.N, y.flags);
 }
 
-__device__ __noinline__ void op_attn_row(const ExecArgs& A, const DevOp& x, const Task& t, uint8_t* smem,
-                                         TcShared* tc) {
-  const DevOp& y = A.ops[x.seg0];
-  const uint32_t seq = t.seq0, Kd = x.K, N = x.N, Ny = y.N;
-  const uint32_t warp = htid() >> 5, lane = htid() & 31;
+// L2 prefetch of a task's hinted operand bytes.  L2 is the point of
+// coherence, so a prefetch can never expose a stale value.
+__device__ __forceinline__ void prefetch_task_operand(const ExecArgs& A, const Task& t) {
+  if (!t.pf_units) return;
+  const uint8_t* p = pptr(A, t.pf_phys, t.seq0);
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(t.pf_units * 16u) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_l2_bytes(const void* p, uint32_t bytes) {
+  if (bytes) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// The last key a query row sees: its row in the KV window (F_SMMASK),
+// bounded by the window's valid length; every key when unmasked.
+__device__ __forceinline__ int64_t attn_row_last(const ExecArgs& A, const DevOp& x, uint32_t seq) {
   uint32_t qrb = x.attn_qrb, vkl = x.attn_vkl;
   if (x.flags & F_ATTN_DYN) {
     const uint64_t pv = A.params[uint64_t(seq) * A.n_params + x.param];
     qrb = pv & 0xFFFF;
     vkl = (pv >> 16) & 0xFFFF;
   }
-  const bool masked = (x.flags & F_SMMASK) != 0;
-  const int64_t lt = masked ? (int64_t(qrb) < int64_t(vkl) - 1 ? int64_t(qrb) : int64_t(vkl) - 1) : int64_t(N) - 1;
-  const uint32_t nvis = lt < 0 ? 0u : min(N, uint32_t(lt) + 1);
-  int32_t* q8w = reinterpret_cast<int32_t*>(smem);                 // Q quantised, 4 per word (Kd <= 128)
+  if (!(x.flags & F_SMMASK)) return int64_t(x.N) - 1;
+  return int64_t(qrb) < int64_t(vkl) - 1 ? int64_t(qrb) : int64_t(vkl) - 1;
+}
+
+// An attention pair resolved for one sequence: its operand addresses, scale
+// registers and visible keys.  A task resolves each of its pairs once, into
+// shared memory, so that loading a pair's rows waits on no chain of record
+// reads.
+struct __align__(16) AttnDesc {
+  const uint8_t* k;     // K rows [N][Kd], FP16
+  const uint8_t* v;     // V rows [N][Ny], FP16
+  const uint16_t* sx;   // score scales [N]
+  const uint16_t* sy;   // output scales [Ny]
+  const uint8_t* q;     // the query row [Kd], FP16
+  uint16_t* out;        // the output row [Ny], FP16
+  int32_t lt;           // last visible key, within [-1, N - 1]
+  uint32_t nvis;        // visible keys (lt + 1)
+  uint16_t kd, n, ny, masked;
+  uint16_t sqb, skb, svb, qsb;   // Q's, K's, V's and P's quantisation registers
+};
+static_assert(sizeof(AttnDesc) == 80, "AttnDesc is an 80-byte record");
+
+__device__ __forceinline__ AttnDesc attn_desc(const ExecArgs& A, const DevOp& x, uint32_t seq) {
+  const DevOp& y = A.ops[x.seg0];
+  const int64_t lt = attn_row_last(A, x, seq);
+  AttnDesc d;
+  d.k = pptr(A, x.b, seq);
+  d.v = pptr(A, y.b, seq);
+  d.sx = reinterpret_cast<const uint16_t*>(pptr(A, x.c, seq));
+  d.sy = reinterpret_cast<const uint16_t*>(pptr(A, y.c, seq));
+  d.q = pptr(A, x.a, seq);
+  d.out = reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(y.dconst), seq));
+  // a last key at or past N - 1 sees every key, below 0 none: the same rows
+  d.lt = lt < 0 ? -1 : int32_t(lt < int64_t(x.N) - 1 ? lt : int64_t(x.N) - 1);
+  d.nvis = uint32_t(d.lt + 1);
+  d.kd = static_cast<uint16_t>(x.K);
+  d.n = static_cast<uint16_t>(x.N);
+  d.ny = static_cast<uint16_t>(y.N);
+  d.masked = (x.flags & F_SMMASK) != 0;
+  d.sqb = sreg_bits(A, x.s[0], seq);
+  d.skb = sreg_bits(A, x.s[1], seq);
+  d.svb = sreg_bits(A, y.s[1], seq);
+  d.qsb = sreg_bits(A, y.s[0], seq);
+  return d;
+}
+
+// L2 prefetch of what task ti reads first: for a row-attention task its
+// (first) pair's visible K and V rows, scales and query row, whose extent
+// the static hint cannot know; for any other task its hint.  Resolving the
+// pair also pulls its records, position word and registers into this SM's
+// L1 for the task.
+__device__ void prefetch_next_attn(const ExecArgs& A, uint32_t ti) {
+  const Task tn = A.tasks[ti];
+  const DevOp& x = A.ops[tn.op];
+  if (!(x.kind == K_MATMUL && (x.flags & F_WIDE) && attn_row_ok(A, x))) {
+    prefetch_task_operand(A, tn);
+    return;
+  }
+  const AttnDesc d = attn_desc(A, x, tn.seq0);
+  prefetch_l2_bytes(d.k, d.nvis * d.kd * 2u);
+  prefetch_l2_bytes(d.v, d.nvis * d.ny * 2u);
+  prefetch_l2_bytes(d.sx, d.n * 2u);
+  prefetch_l2_bytes(d.sy, d.ny * 2u);
+  prefetch_l2_bytes(d.q, d.kd * 2u);
+}
+
+// An op the dispatcher may run as row attention (attn_row_ok decides), judged
+// from its own record.
+__device__ __forceinline__ bool attn_row_candidate(const DevOp& x) {
+  return x.kind == K_MATMUL && (x.flags & F_WIDE) && !(x.flags & F_TC) && (x.flags2 & FX_PV);
+}
+
+// One pair's per-thread operands: this thread's key's score scale, its word
+// of Q (threads < K / 4) and its column's output scale (threads < N of P.V).
+struct AttnLoads {
+  uint2 qv;
+  uint16_t sxb, syb;
+};
+
+__device__ __forceinline__ void attn_load(const AttnDesc& d, AttnLoads& L) {
+  L.sxb = htid() < d.nvis ? d.sx[htid()] : uint16_t(0);
+  L.syb = htid() < d.ny ? d.sy[htid()] : uint16_t(0);
+  if (htid() < d.kd / 4u) L.qv = __ldcg(reinterpret_cast<const uint2*>(d.q) + htid());
+}
+
+// Thread 0: the first `rows` rows of K or V (rb bytes each) by one bulk copy
+// into dst, completing a phase of bar (none for no rows).
+__device__ __forceinline__ void attn_issue_rows(const uint8_t* src, uint32_t rows, uint32_t rb, void* dst,
+                                                uint64_t* bar) {
+  const uint32_t bytes = rows * rb;
+  if (!bytes) return;
+  sm100::fence_proxy_async();
+  sm100::mbar_arrive_expect_tx(bar, bytes);
+  sm100::bulk_g2s(dst, src, bytes, bar);
+}
+
+// Shared memory of row attention: Q words at 0, scores / exp values at 128,
+// P at 4224, P.V partial sums at 5248, cross-warp reductions at 6272, warp
+// 0's pairwise scratch from 6400, the task's resolved pairs at kAttnTabOff;
+// from kAttnRowVOff the first visible K rows (as many as fit beside the
+// window's V rows), then the visible V rows.
+constexpr uint32_t kAttnTabOff = 7168;
+static_assert(128 + 4096 + 1024 + kThreads * 4 + 128 + 3 * kPwMaxLeaves * 4 <= kAttnTabOff &&
+                  kAttnTabOff + sizeof(AttnDesc) * kAttnGroupMax <= kAttnRowVOff,
+              "row attention scratch overlaps its pair table or K rows");
+
+__device__ __noinline__ void op_attn_rows(const ExecArgs& A, const Task& t, uint32_t npairs, bool grouped,
+                                          uint8_t* smem, TcShared* tc, uint32_t next_ti) {
+  const uint32_t seq = t.seq0;
+  const uint32_t warp = htid() >> 5, lane = htid() & 31;
+  int32_t* q8w = reinterpret_cast<int32_t*>(smem);                 // Q quantised, 4 per word (K <= 128)
   float* rb = reinterpret_cast<float*>(smem + 128);                // scores, then exp values (N <= 1024)
   int8_t* p8 = reinterpret_cast<int8_t*>(smem + 128 + 4096);       // P quantised for P.V
   int32_t* part = reinterpret_cast<int32_t*>(smem + 128 + 4096 + 1024);   // P.V partial sums
-  float* red = reinterpret_cast<float*>(smem + 128 + 4096 + 1024 + kThreads * 4);   // 16 floats, then par
+  float* red = reinterpret_cast<float*>(smem + 128 + 4096 + 1024 + kThreads * 4);   // 16 floats
   uint32_t* pw = reinterpret_cast<uint32_t*>(red + 32);            // warp 0's pairwise scratch
-  uint16_t* vs = reinterpret_cast<uint16_t*>(smem + kAttnRowVOff); // the visible keys' V rows
-  const uint8_t* vg = pptr(A, y.b, seq);
-  const uint32_t vbytes = nvis * Ny * 2;
-  // 1. every load in flight together: V by one bulk copy into shared memory,
-  //    this thread's key row of K, its score scale, Q, the registers, the
-  //    output scale of its column
-  if (htid() == 0) {
-    const uint32_t par = tc->phase_stage;
-    reinterpret_cast<uint32_t*>(red)[16] = par;
-    if (vbytes) {
-      tc->phase_stage = par ^ 1u;
-      sm100::fence_proxy_async();
-      sm100::mbar_arrive_expect_tx(&tc->stage, vbytes);
-      sm100::bulk_g2s(vs, vg, vbytes, &tc->stage);
+  AttnDesc* tab = reinterpret_cast<AttnDesc*>(smem + kAttnTabOff);
+  const DevOp& x0 = A.ops[t.op];
+  // the first kr K rows at kAttnRowVOff (every pair of a group has the
+  // head's shape), V rows after them; keys from kr on are read from global
+  // memory.  `stage` brings K, `stage2` V, one phase a pair.
+  const uint32_t vwin = x0.N * A.ops[x0.seg0].N * 2;
+  const uint32_t kr = min(x0.N, (kWideMmSmem - kAttnRowVOff - vwin) / (x0.K * 2));
+  uint16_t* ks = reinterpret_cast<uint16_t*>(smem + kAttnRowVOff);
+  uint16_t* vs = reinterpret_cast<uint16_t*>(smem + kAttnRowVOff + kr * x0.K * 2);
+  uint32_t kpar = tc->phase_stage, vpar = tc->phase_stage2;   // read before thread 0 stores the final ones
+  // the task's pairs resolved once, lane h of the last warp for pair h (a
+  // group's first pair is its head op); every thread also resolves the first
+  // pair for itself: thread 0 starts its copies, every thread its loads
+  if (warp == kWarps - 1 && lane < npairs) {
+    const uint32_t xi = lane == 0 ? t.op : A.tasks[t.tile + lane].op;
+    const DevOp& xh = A.ops[xi];
+    const bool ok = lane == 0 || (attn_row_ok(A, xh) && xh.K == x0.K && xh.N == x0.N &&
+                                  A.ops[xh.seg0].N == A.ops[x0.seg0].N);
+    AttnDesc d = attn_desc(A, xh, seq);
+    if (!ok) {
+      raise_fault(A, DF_BAD_OP, xi, seq);
+      d.lt = -1;
+      d.nvis = 0;
     }
+    tab[lane] = d;
   }
-  const uint32_t j0 = htid();   // this thread's key (nvis <= kThreads here; more keys loop below)
-  uint4 kv[16];
-  const uint8_t* kg = pptr(A, x.b, seq);
-  if (j0 < nvis) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kg + uint64_t(j0) * Kd * 2);
-#pragma unroll
-    for (uint32_t g = 0; g < 16; ++g)
-      if (g < Kd / 8) kv[g] = __ldcg(kr + g);
-  }
-  const uint16_t* scx = reinterpret_cast<const uint16_t*>(pptr(A, x.c, seq));
-  const uint16_t sxb = j0 < nvis ? scx[j0] : uint16_t(0);
-  const uint16_t sqb = sreg_bits(A, x.s[0], seq), skb = sreg_bits(A, x.s[1], seq);
-  const uint16_t svb = sreg_bits(A, y.s[1], seq), qsb = sreg_bits(A, y.s[0], seq);
-  const uint16_t syb = htid() < Ny ? reinterpret_cast<const uint16_t*>(pptr(A, y.c, seq))[htid()] : uint16_t(0);
-  if (htid() < Kd / 4) {
-    const float sq = h2f(sqb);
-    const uint2 qv = __ldcg(reinterpret_cast<const uint2*>(pptr(A, x.a, seq)) + htid());
-    uint32_t w = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint16_t h = static_cast<uint16_t>((j < 2 ? qv.x : qv.y) >> (16 * (j & 1)));
-      w |= uint32_t(uint8_t(sat8(__fmul_rn(h2f(h), sq)))) << (8 * j);
+  AttnLoads L;
+  {
+    const AttnDesc d0 = attn_desc(A, x0, seq);
+    if (htid() == 0) {
+      attn_issue_rows(d0.k, min(d0.nvis, kr), d0.kd * 2u, ks, &tc->stage);
+      attn_issue_rows(d0.v, d0.nvis, d0.ny * 2u, vs, &tc->stage2);
     }
-    q8w[htid()] = static_cast<int32_t>(w);
+    attn_load(d0, L);
   }
+  if (warp == kWarps - 2 && lane == 31 && next_ti != 0xFFFFFFFFu) prefetch_next_attn(A, next_ti);
   hsync();
-  // 2. scores: the key row quantised (QUANT's rule) and dotted with Q, the
-  //    int32 dot dequantised to FP16 (F_DQ)
-  const float sk = h2f(skb);
-  auto score = [&](const uint4* kvp, uint16_t scb) {
-    int32_t acc = 0;
+  for (uint32_t h = 0; h < npairs; ++h) {
+    const AttnDesc& D = tab[h];
+    const uint32_t Kd = D.kd, N = D.n, Ny = D.ny, nvis = D.nvis;
+    const bool masked = D.masked != 0;
+    const int64_t lt = D.lt;
+    // 1. Q quantised with its register (QUANT's rule), four values a word
+    if (htid() < Kd / 4) {
+      const float sq = h2f(D.sqb);
+      uint32_t w = 0;
 #pragma unroll
-    for (uint32_t g = 0; g < 16; ++g) {
-      if (g >= Kd / 8) break;
+      for (int j = 0; j < 4; ++j) {
+        const uint16_t hv = static_cast<uint16_t>((j < 2 ? L.qv.x : L.qv.y) >> (16 * (j & 1)));
+        w |= uint32_t(uint8_t(sat8(__fmul_rn(h2f(hv), sq)))) << (8 * j);
+      }
+      q8w[htid()] = static_cast<int32_t>(w);
+    }
+    hsync();
+    if (min(nvis, kr)) {
+      if (!sm100::mbar_wait(&tc->stage, kpar, nullptr, 0)) {
+        // bounded: let the K and V copies land, then fault
+        sm100::mbar_wait(&tc->stage, kpar, nullptr, 0);
+        sm100::mbar_wait(&tc->stage2, vpar, nullptr, 0);
+        if (htid() == 0) raise_fault(A, DF_STAGE_TIMEOUT, t.op, seq);
+        return;
+      }
+      kpar ^= 1u;
+    }
+    // 2. scores: each key row quantised (QUANT's rule) and dotted with Q, the
+    //    int32 dot dequantised to FP16 (F_DQ).  A row in shared memory is
+    //    read from its word (j mod K/8) on, so the rows of a quarter warp
+    //    fall in different banks; the int32 sum is exact in any order.
+    const float sk = h2f(D.skb);
+    const uint32_t nw = Kd / 8;
+    auto dot_word = [&](const uint4& w, uint32_t g, int32_t acc) {
       int8_t q[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) q[e] = sat8(__fmul_rn(h2f(h_at(kvp[g], e)), sk));
+      for (int e = 0; e < 8; ++e) q[e] = sat8(__fmul_rn(h2f(h_at(w, e)), sk));
       const uint2 pk = pack_b(q);
       acc = __dp4a(static_cast<int32_t>(pk.x), q8w[2 * g], acc);
-      acc = __dp4a(static_cast<int32_t>(pk.y), q8w[2 * g + 1], acc);
-    }
-    return h2f(f2h(__fmul_rn(__int2float_rn(acc), h2f(scb))));
-  };
-  if (j0 < nvis) rb[j0] = score(kv, sxb);
-  for (uint32_t j = j0 + kThreads; j < nvis; j += kThreads) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kg + uint64_t(j) * Kd * 2);
-    uint4 kw[16];
+      return __dp4a(static_cast<int32_t>(pk.y), q8w[2 * g + 1], acc);
+    };
+    auto score = [&](uint32_t j, uint16_t scb) {
+      int32_t acc = 0;
+      if (j < kr) {
+        const uint4* row = reinterpret_cast<const uint4*>(ks + j * Kd);
+        uint32_t g = j % nw;
+        for (uint32_t i = 0; i < nw; ++i) {
+          acc = dot_word(row[g], g, acc);
+          g = g + 1 == nw ? 0u : g + 1;
+        }
+      } else {   // past the staged rows: the row from global memory, every word in flight
+        const uint4* row = reinterpret_cast<const uint4*>(D.k + uint64_t(j) * Kd * 2);
+        uint4 kw[16];
 #pragma unroll
-    for (uint32_t g = 0; g < 16; ++g)
-      if (g < Kd / 8) kw[g] = __ldcg(kr + g);
-    rb[j] = score(kw, scx[j]);
-  }
-  hsync();
-  // 3. the masked softmax row, softmax_row_f16's arithmetic: max over the
-  //    visible columns, exp in float64 rounded once, NumPy's pairwise sum,
-  //    f16(e / sum) quantised with the P.V op's register
-  const float qs = h2f(qsb);
-  uint32_t nl = 0, L = 0;
-  if (!pw_balanced(N, nl, L) || nvis == 0) {
-    if (warp == 0) softmax_row_f16(rb, N, masked, masked ? lt : int64_t(N) - 1, nullptr, pw, lane, p8, qs);
-  } else {
-    float mx = -INFINITY;
-    for (uint32_t j = htid(); j < nvis; j += kThreads) mx = fmaxf(mx, rb[j]);
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[warp] = mx;
-    hsync();
+        for (uint32_t g = 0; g < 16; ++g)
+          if (g < nw) kw[g] = __ldcg(row + g);
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, red[w]);
-    for (uint32_t j = htid(); j < N; j += kThreads) rb[j] = j < nvis ? exp_f32(__fsub_rn(rb[j], mx)) : 0.f;
-    hsync();
-    const float denom = ln_pairwise(rb, nl, L, false, 0.f, red + 8);
-    for (uint32_t j = htid(); j < N; j += kThreads) {
-      int8_t q8 = 0;
-      if (j < nvis) {
-        const float e = rb[j];
-        const uint16_t h = f2h(!masked ? __fdiv_rn(e, denom) : (denom > 0.f ? __fdiv_rn(e, denom) : 0.f));
-        q8 = sat8(__fmul_rn(h2f(h), qs));
+        for (uint32_t g = 0; g < 16; ++g)
+          if (g < nw) acc = dot_word(kw[g], g, acc);
       }
-      p8[j] = q8;
+      return h2f(f2h(__fmul_rn(__int2float_rn(acc), h2f(scb))));
+    };
+    const uint32_t j0 = htid();
+    if (j0 < nvis) rb[j0] = score(j0, L.sxb);
+    for (uint32_t j = j0 + kThreads; j < nvis; j += kThreads) rb[j] = score(j, D.sx[j]);   // keys past kThreads
+    const uint16_t syb = L.syb;
+    if (h + 1 < npairs) attn_load(tab[h + 1], L);   // the next pair's small operands
+    hsync();
+    // the K rows are read: the next pair's land there
+    if (h + 1 < npairs && htid() == 0)
+      attn_issue_rows(tab[h + 1].k, min(tab[h + 1].nvis, kr), Kd * 2u, ks, &tc->stage);
+    // 3. the masked softmax row, softmax_row_f16's arithmetic: max over the
+    //    visible columns, exp in float64 rounded once, NumPy's pairwise sum,
+    //    f16(e / sum) quantised with the P.V op's register
+    const float qs = h2f(D.qsb);
+    uint32_t nl = 0, Lv = 0;
+    if (!pw_balanced(N, nl, Lv) || nvis == 0) {
+      if (warp == 0) softmax_row_f16(rb, N, masked, masked ? lt : int64_t(N) - 1, nullptr, pw, lane, p8, qs);
+    } else {
+      float mx = -INFINITY;
+      for (uint32_t j = htid(); j < nvis; j += kThreads) mx = fmaxf(mx, rb[j]);
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) red[warp] = mx;
+      hsync();
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, red[w]);
+      for (uint32_t j = htid(); j < N; j += kThreads) rb[j] = j < nvis ? exp_f32(__fsub_rn(rb[j], mx)) : 0.f;
+      hsync();
+      const float denom = ln_pairwise(rb, nl, Lv, false, 0.f, red + 8);
+      for (uint32_t j = htid(); j < N; j += kThreads) {
+        int8_t q8 = 0;
+        if (j < nvis) {
+          const float e = rb[j];
+          const uint16_t hq = f2h(!masked ? __fdiv_rn(e, denom) : (denom > 0.f ? __fdiv_rn(e, denom) : 0.f));
+          q8 = sat8(__fmul_rn(h2f(hq), qs));
+        }
+        p8[j] = q8;
+      }
     }
+    hsync();
+    // 4. P.V: column n, four keys per dp4a (P's bytes of keys j..j+3, zero
+    //    past the visible ones, against V's quantised column entries; rows
+    //    past the copy hold whatever is there and meet P = 0, a NaN
+    //    quantises to 0)
+    const uint32_t nq = kThreads / Ny, n = htid() % Ny, kq = htid() / Ny;
+    if (nvis) {
+      if (!sm100::mbar_wait(&tc->stage2, vpar, nullptr, 0)) {
+        sm100::mbar_wait(&tc->stage2, vpar, nullptr, 0);   // bounded: let the copies land, then fault
+        if (h + 1 < npairs && min(tab[h + 1].nvis, kr)) sm100::mbar_wait(&tc->stage, kpar, nullptr, 0);
+        if (htid() == 0) raise_fault(A, DF_STAGE_TIMEOUT, t.op, seq);
+        return;
+      }
+      vpar ^= 1u;
+    }
+    const float sv = h2f(D.svb);
+    int32_t acc = 0;
+    if (kq < nq) {
+      const uint32_t nv4 = (nvis + 3) & ~3u;
+#pragma unroll 2
+      for (uint32_t j = 4 * kq; j < nv4; j += 4 * nq) {
+        const int32_t pw4 = *reinterpret_cast<const int32_t*>(p8 + j);
+        uint32_t vw = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          vw |= uint32_t(uint8_t(sat8(__fmul_rn(h2f(vs[(j + e) * Ny + n]), sv)))) << (8 * e);
+        acc = __dp4a(pw4, static_cast<int32_t>(vw), acc);
+      }
+    }
+    part[htid()] = acc;
+    hsync();
+    if (htid() < Ny) {
+      int32_t sum = 0;
+      for (uint32_t k = 0; k < nq; ++k) sum += part[k * Ny + htid()];   // int32 sums are exact in any order
+      D.out[htid()] = f2h(__fmul_rn(__int2float_rn(sum), h2f(syb)));
+    }
+    // the V rows are read: the next pair's land there
+    if (h + 1 < npairs && htid() == 0) attn_issue_rows(tab[h + 1].v, tab[h + 1].nvis, Ny * 2u, vs, &tc->stage2);
   }
-  hsync();
-  // 4. P.V: column n, keys kq, kq + nq, ... of the visible ones, V from shared memory
-  const uint32_t par = reinterpret_cast<const uint32_t*>(red)[16];
-  const uint32_t nq = kThreads / Ny, n = htid() % Ny, kq = htid() / Ny;
-  const float sv = h2f(svb);
-  if (vbytes && !sm100::mbar_wait(&tc->stage, par, nullptr, 0)) {
-    sm100::mbar_wait(&tc->stage, par, nullptr, 0);   // bounded: let the copy land, then fault
-    if (htid() == 0) raise_fault(A, DF_STAGE_TIMEOUT, t.op, seq);
-    return;
-  }
-  int32_t acc = 0;
-  if (kq < nq) {
-#pragma unroll 4
-    for (uint32_t j = kq; j < nvis; j += nq) acc += int32_t(p8[j]) * int32_t(sat8(__fmul_rn(h2f(vs[j * Ny + n]), sv)));
-  }
-  part[htid()] = acc;
-  hsync();
-  if (htid() < Ny) {
-    int32_t sum = 0;
-    for (uint32_t k = 0; k < nq; ++k) sum += part[k * Ny + htid()];   // int32 sums are exact in any order
-    uint16_t* out = reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(y.dconst), seq));
-    out[htid()] = f2h(__fmul_rn(__int2float_rn(sum), h2f(syb)));
+  if (htid() == 0) {
+    tc->phase_stage = kpar;
+    tc->phase_stage2 = vpar;
   }
 }
 
@@ -2389,14 +2565,6 @@ __device__ __forceinline__ void prefetch_l1(const void* p) {
   asm volatile("prefetch.global.L1 [%0];\n" ::"l"(p));
 }
 
-// L2 prefetch of a task's hinted operand bytes.  L2 is the point of
-// coherence, so a prefetch can never expose a stale value.
-__device__ __forceinline__ void prefetch_task_operand(const ExecArgs& A, const Task& t) {
-  if (!t.pf_units) return;
-  const uint8_t* p = pptr(A, t.pf_phys, t.seq0);
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(t.pf_units * 16u) : "memory");
-}
-
 // Grid-wide barrier between levels.  The arrival counter only grows during a
 // launch (the host zeroes it before each launch): a CTA arrives with a release
 // add and waits, with acquire loads, until all gridDim.x CTAs of this level
@@ -2447,16 +2615,23 @@ __device__ void run_op(const ExecArgs& A, const DevOp& op, const Task& t, uint8_
 
 __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t next_ti, uint32_t next2_ti,
                          TcShared* tc) {
+  const Task& t = A.tasks[ti];   // read in place (L1), not copied to local memory
+  const DevOp& op = A.ops[t.op];
   if (htid() == 32 && next_ti != 0xFFFFFFFFu) {
     const Task tn = A.tasks[next_ti];
     prefetch_l1(A.ops + tn.op);
     prefetch_l1(reinterpret_cast<const uint8_t*>(A.ops + tn.op) + sizeof(DevOp) - 1);
-    prefetch_task_operand(A, tn);
+    if (!attn_row_candidate(op)) prefetch_task_operand(A, tn);   // else the attention op prefetches it
     if (next2_ti != 0xFFFFFFFFu) prefetch_l1(A.tasks + next2_ti);
   }
-
-  const Task& t = A.tasks[ti];   // read in place (L1), not copied to local memory
-  const DevOp& op = A.ops[t.op];
+  if (op.flags2 & FX_ATTNGRP) {   // a head group: its attention pairs of this sequence in one task
+    if (attn_row_ok(A, op) && t.aux >= 1 && t.aux <= kAttnGroupMax)
+      op_attn_rows(A, t, t.aux, true, smem, tc, next_ti);
+    else if (htid() == 0)
+      raise_fault(A, DF_BAD_OP, t.op, t.seq0);
+    hsync();
+    return;
+  }
   if (op.flags2 & FX_CHAINHEAD) {
     if (chain_vln_ok(A, t)) {   // VADD -> LAYERNORM -> MAX_ABS + QUANT of one row, in one pass
       op_chain_vln(A, t, smem);
@@ -2491,8 +2666,9 @@ __device__ void run_op(const ExecArgs& A, const DevOp& op, const Task& t, uint8_
     case K_SREG_FINAL: op_sreg_final(A, op, t); break;
     case K_MATMUL:
       if (op.flags & F_TC) op_matmul_tc(A, op, t, smem, tc, t.op, next_ti);
-      else if ((op.flags & F_WIDE) && (op.flags2 & FX_PV) && attn_row_ok(A, op)) op_attn_row(A, op, t, smem, tc);
+      else if ((op.flags & F_WIDE) && attn_row_ok(A, op)) op_attn_rows(A, t, 1, false, smem, tc, next_ti);
       else if (op.flags & F_WIDE) {
+        if (attn_row_candidate(op) && htid() == 32 && next_ti != 0xFFFFFFFFu) prefetch_task_operand(A, A.tasks[next_ti]);
         const uint32_t nk = op_matmul_wide(A, op, t, smem, tc, false, false);
         if ((op.flags2 & FX_PV) && nk != 0xFFFFFFFFu) {   // the P.V op, its A tile from the softmax above
           hsync();
@@ -2565,9 +2741,11 @@ __global__ void __launch_bounds__(kCtaThreads, 1) exec_kernel(const __grid_const
         sm100::mbar_init(&tcs[h].empty[st], 1);
       }
       sm100::mbar_init(&tcs[h].stage, 1);
+      sm100::mbar_init(&tcs[h].stage2, 1);
       tcs[h].phase_full = 0;
       tcs[h].phase_empty = 0;
       tcs[h].phase_stage = 0;
+      tcs[h].phase_stage2 = 0;
     }
     sm100::mbar_fence_init();
   }

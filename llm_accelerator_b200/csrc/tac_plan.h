@@ -114,6 +114,10 @@ constexpr uint64_t kSegGelu = 1ull << 62;   // Segment.dst flag of such a segmen
 constexpr uint32_t FX_DSTORE = 1024;   // FX_DQS tcgen05 MATMUL that also stores the first attn_vkl rows of its
                                        // FP16 result to writable DRAM at params[param] + attn_qrb (a STORE
                                        // through a runtime register, e.g. a KV-cache append, absorbed)
+constexpr uint32_t FX_ATTNGRP = 2048;  // FX_PV op heading a group of attention pairs of one sequence (the
+                                       // heads of a layer) run as row attention in one task, the next pair's
+                                       // copies overlapped: its tasks hold, in tile and aux, the first and
+                                       // count of the group's task templates (after the last level's tasks)
 constexpr uint32_t FX_TCRES = 256;     // tcgen05 MATMUL (64-column tasks) whose every K chunk fits in shared
                                        // memory at once: A boxes of q_rows rows packed back to back, then B;
                                        // no stage is reused
@@ -251,6 +255,25 @@ TAC_HD constexpr uint32_t pv_scratch_end(uint32_t M, uint32_t N) {
   return pv_a_bytes(M, N) + M * N * 2 + 2 * kExecWarps * N * 4 + kPwScratchBytes;
 }
 TAC_HD constexpr bool pv_ok(uint32_t M, uint32_t N) { return pv_scratch_end(M, N) <= kWideMmSmem - 512; }
+// Row attention: one query row of an FX_PV pair (QK^T op x, P.V op y) on
+// CUDA cores.  Q, the scores, P and the scratch sit below kAttnRowVOff, the
+// visible K rows (as many as fit) and V rows above it; in a head group
+// (FX_ATTNGRP) the next pair's rows land there while this pair computes.
+// Groups are sized for one round over kTargetHalves executor halves (148 SMs
+// x 2).
+constexpr uint32_t kAttnRowVOff = 8192;
+constexpr uint32_t kTargetHalves = 296;
+constexpr uint32_t kAttnGroupMax = 8;   // pairs of one head group
+TAC_HD constexpr bool attn_row_shape_ok(uint32_t xM, uint32_t xK, uint32_t xN, uint32_t xflags, uint32_t xflags2,
+                                        uint32_t yM, uint32_t yK, uint32_t yN, uint32_t yflags) {
+  return xM == 1 && (xflags & (F_WIDE | F_QA | F_QB | F_BT | F_DQ | F_SM | F_NOI32 | F_NODQ)) ==
+                        uint32_t(F_WIDE | F_QA | F_QB | F_BT | F_DQ | F_SM | F_NOI32 | F_NODQ) &&
+         !(xflags & F_ACCUMULATE) && (xflags2 & FX_PV) && (xflags2 & FX_SMSKIP) && xK % 8 == 0 && xK <= 128 &&
+         xN % 8 == 0 && xN <= 1024 && yM == 1 &&
+         (yflags & (F_WIDE | F_QB | F_DQ | F_NOI32)) == uint32_t(F_WIDE | F_QB | F_DQ | F_NOI32) &&
+         !(yflags & (F_BT | F_ACCUMULATE | F_NODQ)) && yK == xN && yN % 8 == 0 && yN <= 64 &&
+         kAttnRowVOff + xN * yN * 2 <= kWideMmSmem;
+}
 TAC_HD constexpr bool pvpf_ok(uint32_t M, uint32_t N, uint32_t K, uint32_t n_pv, bool bt_pv) {
   return pv_scratch_end(M, N) <= wide_mm_bh_off(M, n_pv, N, bt_pv) &&
          ((M + 15) / 16) * 16 * (((K + 31) & ~31u) + 16) + ((N + 7) / 8) * 8 * (((K + 31) & ~31u) + 16) <=

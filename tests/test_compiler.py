@@ -453,3 +453,62 @@ def test_segment_list_tasks_name_the_segments_they_read():
         assert all(int(a["dst"]) + int(a["n"]) == int(c["dst"]) for a, c in zip(sl[:-1], sl[1:]))
         seen += 1
     assert seen > 0
+
+
+class _NoEngine:
+    """Stands in for the GPU engine while BatchedRunner compiles its plans."""
+
+    def __init__(self, *args, **kwargs):
+        pass
+
+    def write_dram(self, *args, **kwargs):
+        pass
+
+
+FX_PV, FX_ATTNGRP, HALVES = 4, 2048, 296
+
+
+@pytest.mark.parametrize("batch,group", [(8, 1), (80, 2), (150, 4), (300, 4)])
+def test_attention_head_groups_cover_every_pair_once(monkeypatch, batch, group):
+    """Row-attention pairs (FX_PV QK^T ops of one query row) of a level run
+    once per sequence: in a task of their own, or as templates of a head
+    group (FX_ATTNGRP) task of one sequence.  A group holds pairs of one
+    shape, its head op first; groups take the least size that fits the
+    level's pairs into one round over the executor's 296 halves (all of a
+    level's pairs per sequence, up to 8, when none does)."""
+    from llm_accelerator_b200 import runner as R
+    monkeypatch.setattr(R, "Engine", _NoEngine)
+    r = R.BatchedRunner(load_bundle("tiny_l2_d128"), batch)
+    ops, segs, tasks, lv = r.plans["decode"].dump()
+    n_leveled = int(lv[-1])
+    row_pairs = [i for i, op in enumerate(ops)
+                 if int(op["flags2"]) & FX_PV and int(op["M"]) == 1 and int(op["flags"]) & 64]
+    assert row_pairs
+    runs = {}
+    sizes = set()
+    for L_ in range(len(lv) - 1):
+        level = tasks[int(lv[L_]):int(lv[L_ + 1])]
+        attn_tasks = 0
+        for t in level:
+            op = ops[int(t["op"])]
+            if int(op["flags2"]) & FX_ATTNGRP:
+                first, count = int(t["tile"]), int(t["aux"])
+                assert n_leveled <= first and first + count <= len(tasks) and 1 <= count <= 8
+                temps = tasks[first:first + count]
+                assert int(temps[0]["op"]) == int(t["op"])
+                assert len({(int(ops[o]["K"]), int(ops[o]["N"]), int(ops[int(ops[o]["seg0"])]["N"]))
+                            for o in temps["op"]}) == 1
+                assert all(int(ops[o]["level"]) == int(op["level"]) for o in temps["op"])
+                for o in temps["op"]:
+                    runs[(int(o), int(t["seq0"]))] = runs.get((int(o), int(t["seq0"])), 0) + 1
+                sizes.add(count)
+                attn_tasks += 1
+            elif int(t["op"]) in row_pairs:
+                runs[(int(t["op"]), int(t["seq0"]))] = runs.get((int(t["op"]), int(t["seq0"])), 0) + 1
+                attn_tasks += 1
+        if batch <= HALVES:
+            assert attn_tasks <= HALVES
+    assert runs == {(o, s): 1 for o in row_pairs for s in range(batch)}
+    assert max(sizes, default=1) == group
+    heads = {int(o) for o in np.nonzero(ops["flags2"] & FX_ATTNGRP)[0]}
+    assert all(int(ops[o]["flags2"]) & FX_PV for o in heads)

@@ -201,6 +201,35 @@ def test_batched_runner_matches_single_sequence_runs(path):
         np.testing.assert_array_equal(batched[s].view(np.uint16), single.view(np.uint16))
 
 
+@pytest.mark.parametrize("B", [80, 150])
+def test_batched_runner_head_groups_match_single_sequence_runs(B):
+    """At batches whose attention pairs run in head groups (2 pairs a task at
+    80 sequences, 4 at 150), sampled sequences of the batch reproduce their
+    single-sequence runs bit for bit, one of them at a ragged position."""
+    from llm_accelerator_b200.runner import BatchedRunner, HostRunner
+    b = load_bundle("tiny_l2_d128")
+    steps, vocab = 4, 512
+    rng = np.random.default_rng(B)
+    prompts = rng.integers(0, vocab, (B, steps))
+    br = BatchedRunner(b, B)
+    ops, _, tasks, lv = br.plans["decode"].dump()
+    assert (ops[tasks[:int(lv[-1])]["op"]]["flags2"] & 2048).any(), "no head-group tasks in the plan"
+    br.step("prefill", prompts[:, 0], np.zeros(B, int))
+    for pos in range(1, steps):
+        br.step("decode", prompts[:, pos], np.full(B, pos))
+    # the last token once more: at its own position for every sequence but
+    # sequence 1, which takes it at the position before
+    br.step("decode", prompts[:, steps - 1], np.where(np.arange(B) == 1, steps - 2, steps - 1))
+    for s in (0, 1, B // 2, B - 1):
+        r = HostRunner(load_bundle("tiny_l2_d128"), simulator=_sim(), logits_dtype=np.float16)
+        r.run_prefill([int(prompts[s, 0])])
+        last = steps - 2 if s == 1 else steps - 1
+        for pos in range(1, last + 1 if s != 1 else last):
+            r.run_decode_step(int(prompts[s, pos]), pos)
+        want = r.run_decode_step(int(prompts[s, steps - 1]), last)
+        np.testing.assert_array_equal(br.logits("decode", s).view(np.uint16), want.view(np.uint16))
+
+
 def test_batched_runner_ragged_positions():
     """Sequences at different positions in one step (per-sequence runtime words):
     sequence 1 re-runs position 1 while sequences 0 and 2 move to position 2."""
