@@ -2494,6 +2494,7 @@ void Compiler::build_tasks() {
   std::vector<Task> templates;
   std::vector<std::pair<size_t, uint32_t>> heads;   // (level, index in per_level) of chain / group head tasks
   std::map<uint32_t, std::vector<uint32_t>> attn_pairs;   // level -> its row-attention QK^T ops
+  std::map<uint32_t, std::vector<uint32_t>> max_ops;      // level -> its pairable MAX_ABS + QUANT ops
   auto attn_groupable = [&](const DevOp& x) {
     if (!(x.flags2 & FX_PV) || x.M != 1) return false;
     const DevOp& y = P->ops[x.seg0];
@@ -2566,6 +2567,12 @@ void Compiler::build_tasks() {
         break;
       }
       case K_MAX_ABS:
+        if (max_pair_ok(op.M, op.N, op.nseg, op.flags, op.flags2)) {
+          max_ops[op.level].push_back(i);   // tasks below, per op or per pair
+          break;
+        }
+        per_seq(i, 1);
+        break;
       case K_DYN_LOAD:
       case K_DYN_STORE:
       case K_DYN_STORE_MULTI:
@@ -2641,6 +2648,31 @@ void Compiler::build_tasks() {
         for (uint32_t s = 0; s < B; ++s) {
           heads.push_back({lp.first, static_cast<uint32_t>(per_level[lp.first].size())});
           per_level[lp.first].push_back(Task{xs[k0], s, 1, first, cnt});
+        }
+      }
+    }
+  }
+  // MAX_ABS + QUANT ops of a level: when a task per op and sequence would
+  // take more than one round over the executor's halves, ops of one shape go
+  // in pairs (FX_MAXGRP), one task per pair and sequence.
+  for (auto& lm : max_ops) {
+    std::map<std::pair<uint32_t, uint32_t>, std::vector<uint32_t>> by_shape;
+    for (uint32_t i : lm.second) by_shape[{P->ops[i].M, P->ops[i].N}].push_back(i);
+    for (auto& sh : by_shape) {
+      const std::vector<uint32_t>& xs = sh.second;
+      const bool pair = uint64_t(B) * xs.size() > kTargetHalves;
+      for (size_t k0 = 0; k0 < xs.size(); k0 += pair ? 2 : 1) {
+        if (!pair || k0 + 1 == xs.size()) {
+          per_seq(xs[k0], 1);
+          continue;
+        }
+        const uint32_t first = static_cast<uint32_t>(templates.size());
+        templates.push_back(Task{xs[k0], 0, 1, 0, 0});
+        templates.push_back(Task{xs[k0 + 1], 0, 1, 0, 0});
+        P->ops[xs[k0]].flags2 |= FX_MAXGRP;
+        for (uint32_t s = 0; s < B; ++s) {
+          heads.push_back({lm.first, static_cast<uint32_t>(per_level[lm.first].size())});
+          per_level[lm.first].push_back(Task{xs[k0], s, 1, first, 2});
         }
       }
     }

@@ -2014,6 +2014,21 @@ __device__ __noinline__ void op_seg_ew(const ExecArgs& A, const DevOp& op, const
   }
 }
 
+// The scale pair MAX_ABS derives from max |x| (m: its FP16 bit pattern,
+// 0xFFFF for a NaN): inverse 127 / max and forward max / 127, max clamped to
+// [2^-9, 65504 * 127 / 2], both rounded once from float64.
+__device__ __forceinline__ void max_abs_scales(uint32_t m, uint16_t& inv, uint16_t& fwd) {
+  if (m == 0xFFFFu) {
+    inv = fwd = 0x7E00u;
+    return;
+  }
+  double mx = static_cast<double>(h2f(static_cast<uint16_t>(m)));
+  mx = mx > 0.001953125 ? mx : 0.001953125;         // 2^-9
+  mx = mx < 4159504.0 ? mx : 4159504.0;             // 65504 * 127 / 2
+  inv = d2h(127.0 / mx);
+  fwd = d2h(mx / 127.0);
+}
+
 __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, const Task& t, uint8_t* smem) {
   const uint32_t seq = t.seq0;
   const uint64_t MN = uint64_t(op.M) * op.N;
@@ -2074,15 +2089,7 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
   if (htid() == 0) {
     for (int w = 1; w < kWarps; ++w) m = red[w] > m ? red[w] : m;
     uint16_t inv, fwd;
-    if (m == 0xFFFFu) {
-      inv = fwd = 0x7E00u;
-    } else {
-      double mx = static_cast<double>(h2f(static_cast<uint16_t>(m)));
-      mx = mx > 0.001953125 ? mx : 0.001953125;         // 2^-9
-      mx = mx < 4159504.0 ? mx : 4159504.0;             // 65504 * 127 / 2
-      inv = d2h(127.0 / mx);
-      fwd = d2h(mx / 127.0);
-    }
+    max_abs_scales(m, inv, fwd);
     A.sregs[uint64_t(seq) * A.sreg_stride + op.out_slot] = inv;
     A.sregs[uint64_t(seq) * A.sreg_stride + op.out_slot + 1] = fwd;
     red[kWarps] = inv;
@@ -2102,6 +2109,108 @@ __device__ __noinline__ void op_max_abs(const ExecArgs& A, const DevOp& op, cons
       }
       *reinterpret_cast<uint2*>(out + g * 8) = pack_b(q8);
     }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// A pair of MAX_ABS + QUANT ops (FX_MAXGRP: two ops of one level and shape,
+// segment-list input, FX_MAXQ) of one sequence in one task: each op on half
+// the threads (128) with a shared-memory region of its own, op_max_abs's
+// arithmetic.  Both halves pass the same barriers.
+// ---------------------------------------------------------------------------------
+constexpr uint32_t kMaxGrpRegion = 24576;   // per op: reductions, segment table, the kept input
+constexpr uint32_t kMaxGrpSegs = 64;        // segment table at 64
+constexpr uint32_t kMaxGrpKeep = 4096;      // the kept input (kMaxGrpElems FP16)
+static_assert(kMaxGrpSegs + kMaxSegRuns * 13 <= kMaxGrpKeep && kMaxGrpKeep + kMaxGrpElems * 2 <= kMaxGrpRegion,
+              "MAX_ABS pair region layout");
+
+__device__ __noinline__ void op_max_abs_pair(const ExecArgs& A, const Task& t, uint8_t* smem) {
+  const uint32_t seq = t.seq0;
+  const uint32_t g = htid() >> 7, gt = htid() & 127, gw = gt >> 5, lane = htid() & 31;
+  const uint32_t opi = g == 0 ? t.op : A.tasks[t.tile + 1].op;
+  const DevOp& op = A.ops[opi];
+  uint8_t* base = smem + g * kMaxGrpRegion;
+  uint32_t* red = reinterpret_cast<uint32_t*>(base);
+  uint32_t* ofs = reinterpret_cast<uint32_t*>(base + kMaxGrpSegs);
+  uint64_t* src = reinterpret_cast<uint64_t*>(base + kMaxGrpSegs + kMaxSegRuns * 4);
+  uint8_t* gel = base + kMaxGrpSegs + kMaxSegRuns * 12;
+  uint4* keep = reinterpret_cast<uint4*>(base + kMaxGrpKeep);
+  const uint32_t nseg = op.nseg;
+  for (uint32_t k = gt; k < nseg; k += 128) {
+    const Segment sg = A.segs[op.seg0 + k];
+    ofs[k] = static_cast<uint32_t>(sg.dst);   // the offset (the flag bit lies above 32 bits)
+    src[k] = sg.src;
+    gel[k] = (sg.dst & kSegGelu) ? 1 : 0;
+  }
+  hsync();
+  auto seg_of = [&](uint32_t u) {   // last segment k with ofs[k] <= u
+    uint32_t lo = 0, hi = nseg;
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (ofs[mid] <= u) lo = mid;
+      else hi = mid;
+    }
+    return lo;
+  };
+  const uint32_t ng = op.M * op.N / 8;
+  uint32_t m = 0;
+  for (uint32_t g0 = gt; g0 < ng; g0 += 128 * 8) {
+    uint4 v[8];
+    uint32_t si[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t u = g0 + k * 128;
+      si[k] = 0;
+      v[k] = make_uint4(0, 0, 0, 0);
+      if (u < ng) {
+        si[k] = seg_of(u);
+        v[k] = __ldcg(reinterpret_cast<const uint4*>(pptr(A, src[si[k]], seq)) + (u - ofs[si[k]]));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t u = g0 + k * 128;
+      if (u >= ng) continue;
+      if (gel[si[k]]) {   // a GELU's input: the value the GELU op would have stored
+        uint16_t h[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = f2h(gelu_f32(h2f(h_at(v[k], j))));
+        v[k] = pack_h(h);
+      }
+      keep[u] = v[k];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t h = h_at(v[k], j) & 0x7FFFu;
+        if (h > 0x7C00u) h = 0xFFFFu;  // NaN
+        m = h > m ? h : m;
+      }
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const uint32_t w = __shfl_xor_sync(0xffffffffu, m, o);
+    m = w > m ? w : m;
+  }
+  if (lane == 0) red[gw] = m;
+  hsync();
+  if (gt == 0) {
+    for (int w = 1; w < 4; ++w) m = red[w] > m ? red[w] : m;
+    uint16_t inv, fwd;
+    max_abs_scales(m, inv, fwd);
+    A.sregs[uint64_t(seq) * A.sreg_stride + op.out_slot] = inv;
+    A.sregs[uint64_t(seq) * A.sreg_stride + op.out_slot + 1] = fwd;
+    red[4] = inv;
+  }
+  hsync();
+  // QUANT's rule with the inverse scale just derived: rint(x * inv), NaN -> 0, clipped to int8
+  const float s0 = h2f(static_cast<uint16_t>(red[4]));
+  int8_t* out = reinterpret_cast<int8_t*>(pptr(A, op.d, seq));
+  const uint32_t nq = op.q_rows ? op.q_rows * op.N / 8 : ng;   // rows of the result some op reads
+  for (uint32_t u = gt; u < nq; u += 128) {
+    const uint4 x8 = keep[u];
+    int8_t q8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q8[j] = sat8(__fmul_rn(h2f(h_at(x8, j)), s0));
+    *reinterpret_cast<uint2*>(out + uint64_t(u) * 8) = pack_b(q8);
   }
 }
 
@@ -2632,6 +2741,12 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
     hsync();
     return;
   }
+  if (op.flags2 & FX_MAXGRP) {   // a pair of MAX_ABS + QUANT ops of this sequence
+    if (t.aux == 2 && max_pair_ok(op.M, op.N, op.nseg, op.flags, op.flags2)) op_max_abs_pair(A, t, smem);
+    else if (htid() == 0) raise_fault(A, DF_BAD_OP, t.op, t.seq0);
+    hsync();
+    return;
+  }
   if (op.flags2 & FX_CHAINHEAD) {
     if (chain_vln_ok(A, t)) {   // VADD -> LAYERNORM -> MAX_ABS + QUANT of one row, in one pass
       op_chain_vln(A, t, smem);
@@ -2722,6 +2837,7 @@ static_assert(kWideMmSmem <= kExecOpSmem, "wide MATMUL exceeds the op shared mem
 static_assert(kWarps == int(kExecWarps) && kPwScratchBytes == kWarps * 3 * kPwMaxLeaves * 4,
               "FX_PV layout constants disagree with the executor");
 static_assert(kSegTableOff + kMaxSegRuns * 12 <= kExecOpSmem, "segment table exceeds the op shared memory");
+static_assert(2 * kMaxGrpRegion <= kExecOpSmem, "MAX_ABS pair regions exceed the op shared memory");
 static_assert(kSegTableOff + kMaxSegRuns * 13 <= kMaxQStage && kMaxQStage + 16384 * 2 <= kExecOpSmem,
               "MAX_ABS staging overlaps the segment table or exceeds the op shared memory");
 static_assert(kExecOpSmem % 1024 == 0 || kTcSmem <= kExecOpSmem, "half regions must keep the stage alignment slack");

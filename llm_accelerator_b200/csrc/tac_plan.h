@@ -118,6 +118,10 @@ constexpr uint32_t FX_ATTNGRP = 2048;  // FX_PV op heading a group of attention 
                                        // heads of a layer) run as row attention in one task, the next pair's
                                        // copies overlapped: its tasks hold, in tile and aux, the first and
                                        // count of the group's task templates (after the last level's tasks)
+constexpr uint32_t FX_MAXGRP = 4096;   // F_SEGA FX_MAXQ MAX_ABS heading a pair of such ops of one level and
+                                       // shape run in one task per sequence, each on half the threads: its
+                                       // tasks hold, in tile and aux, the first and count (2) of the pair's
+                                       // task templates (after the last level's tasks)
 constexpr uint32_t FX_TCRES = 256;     // tcgen05 MATMUL (64-column tasks) whose every K chunk fits in shared
                                        // memory at once: A boxes of q_rows rows packed back to back, then B;
                                        // no stage is reused
@@ -127,6 +131,9 @@ constexpr uint32_t FX_TCRES = 256;     // tcgen05 MATMUL (64-column tasks) whose
 // Most runs an operand read through a segment list may have (longer lists are gathered).
 constexpr uint32_t kMaxSegRuns = 256;
 constexpr uint32_t kSegTaskUnits = 512;   // operand units (4096 FP16 elements) of one QUANT / VADD_F16 task
+// MAX_ABS pairs (FX_MAXGRP): ops of at most kMaxGrpElems FP16 elements read
+// through at most kMaxSegRuns segments, each on half the threads of a task.
+constexpr uint32_t kMaxGrpElems = 8192;
                                           // whose first operand is a segment list
 
 struct DevOp {
@@ -187,6 +194,10 @@ constexpr uint64_t kEwTaskElems = 8192;
 // than 128 rows (128 / M sequences fill one 128-row tile): a 16-multiple, or
 // a divisor of 128 (a MATMUL narrowed to the rows some op reads), N and K
 // 16-multiples.
+TAC_HD constexpr bool max_pair_ok(uint32_t M, uint32_t N, uint32_t nseg, uint32_t flags, uint32_t flags2) {
+  return (flags & F_SEGA) && (flags2 & FX_MAXQ) && M * N <= kMaxGrpElems && (M * N) % 8 == 0 && nseg >= 1 &&
+         nseg <= kMaxSegRuns;
+}
 TAC_HD constexpr bool tc_rows_ok(uint32_t M) { return M > 0 && M < 128 && (M % 16 == 0 || 128 % M == 0); }
 // Shared memory of the tcgen05 stages (after the 1024-byte alignment) and
 // the resident layout: every K chunk's A box (rows x 128 B) then every B box

@@ -2,6 +2,7 @@
 
     python -m llm_accelerator_b200.profile [--recipe tests/golden/recipe_gpt2_medium.npz]
                                            [--batch 64] [--steps 3] [--position 130] [--mhz 1965]
+                                           [--levels LO:HI]
 
 Runs a prefill and teacher-forced decode steps of a GPT-2 recipe through
 BatchedRunner up to --position (the bench's timed steps follow a 128-token
@@ -50,6 +51,8 @@ def op_label(op) -> str:
         k += f"[{op['M']}x{op['N']}]" + ("seg" if f & 32 else "") + ("+quant" if int(op["flags2"]) & 2 else "")
         if k.startswith("VADD_CHAIN"):
             k += f"x{int(op['nseg'])}"
+    if int(op["flags2"]) & (2048 | 4096):   # a head group / MAX_ABS pair: one task runs several ops
+        k += "+group"
     return k
 
 
@@ -100,6 +103,20 @@ def summarize(level_ns, task_cycles, ops, tasks, lv, halves: int, mhz: float, to
     return "\n".join(lines)
 
 
+def level_table(level_ns, task_cycles, ops, tasks, lv, halves: int, mhz: float, lo: int, hi: int) -> str:
+    """Levels lo..hi-1 one per line: the level's time (globaltimer), its task
+    count, its busiest half's task time and its ops' labels."""
+    lines = [f"{'level':>5s} {'time':>9s} {'tasks':>6s} {'busiest':>9s}  ops"]
+    for L in range(max(0, lo), min(hi, len(level_ns))):
+        c = task_cycles[lv[L]:lv[L + 1]]
+        h = np.zeros(halves)
+        np.add.at(h, np.arange(len(c)) % halves, c)
+        labels = collections.Counter(op_label(ops[int(t["op"])]) for t in tasks[lv[L]:lv[L + 1]])
+        lines.append(f"{L:5d} {level_ns[L] / 1e3:7.2f}us {len(c):6d} {h.max() / mhz:7.2f}us  "
+                     + ", ".join(f"{k} x{n}" for k, n in labels.items()))
+    return "\n".join(lines)
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     root = Path(__file__).resolve().parent.parent
@@ -109,8 +126,13 @@ def main(argv=None) -> None:
     ap.add_argument("--position", type=int, default=130, help="KV position of the first profiled step")
     ap.add_argument("--mhz", type=float, default=1965.0, help="SM clock that converts task cycles to time")
     ap.add_argument("--top", type=int, default=25)
+    ap.add_argument("--levels", default="", help="LO:HI: also list levels LO..HI-1 one per line")
     a = ap.parse_args(argv)
-    print(summarize(*profile_decode(a.recipe, a.batch, a.steps, position=a.position), mhz=a.mhz, top=a.top))
+    prof = profile_decode(a.recipe, a.batch, a.steps, position=a.position)
+    print(summarize(*prof, mhz=a.mhz, top=a.top))
+    if a.levels:
+        lo, hi = (int(v) for v in a.levels.split(":"))
+        print(level_table(*prof, mhz=a.mhz, lo=lo, hi=hi))
 
 
 if __name__ == "__main__":

@@ -512,3 +512,45 @@ def test_attention_head_groups_cover_every_pair_once(monkeypatch, batch, group):
     assert max(sizes, default=1) == group
     heads = {int(o) for o in np.nonzero(ops["flags2"] & FX_ATTNGRP)[0]}
     assert all(int(ops[o]["flags2"]) & FX_PV for o in heads)
+
+
+def test_gpt2_medium_batch64_groups_run_every_op_once(monkeypatch):
+    """At batch 64 the GPT-2 medium decode plan runs its attention pairs in
+    head groups of four and its GELU MAX_ABS + QUANT ops in pairs
+    (FX_MAXGRP, one task per pair and sequence, the second op a template);
+    every such op runs exactly once per sequence, and each of those levels
+    takes one round over the executor's 296 halves."""
+    from llm_accelerator_b200 import runner as R
+    from llm_accelerator_b200.recipe import load_recipe
+    monkeypatch.setattr(R, "Engine", _NoEngine)
+    B = 64
+    r = R.BatchedRunner(load_recipe(GOLDEN / "recipe_gpt2_medium.npz"), B)
+    ops, segs, tasks, lv = r.plans["decode"].dump()
+    FX_MAXQ, FX_CHAINED, FX_MAXGRP, F_SEGA = 2, 64, 4096, 32
+    grouped = [i for i, op in enumerate(ops)
+               if (int(op["flags2"]) & FX_PV and int(op["M"]) == 1 and int(op["flags"]) & 64) or
+               (int(op["kind"]) == PE.K["MAX_ABS"] and int(op["flags"]) & F_SEGA and int(op["flags2"]) & FX_MAXQ
+                and not int(op["flags2"]) & FX_CHAINED)]
+    runs, sizes = {}, {FX_ATTNGRP: set(), FX_MAXGRP: set()}
+    for L_ in range(len(lv) - 1):
+        level = tasks[int(lv[L_]):int(lv[L_ + 1])]
+        n_group_tasks = 0
+        for t in level:
+            op = ops[int(t["op"])]
+            f2 = int(op["flags2"])
+            if f2 & (FX_ATTNGRP | FX_MAXGRP):
+                temps = tasks[int(t["tile"]):int(t["tile"]) + int(t["aux"])]
+                assert int(temps[0]["op"]) == int(t["op"])
+                sizes[f2 & (FX_ATTNGRP | FX_MAXGRP)].add(int(t["aux"]))
+                members = [int(o) for o in temps["op"]]
+                n_group_tasks += 1
+            elif int(t["op"]) in grouped:
+                members = [int(t["op"])]
+            else:
+                continue
+            for o in members:
+                assert int(ops[o]["level"]) == int(op["level"])
+                runs[(o, int(t["seq0"]))] = runs.get((o, int(t["seq0"])), 0) + 1
+        assert n_group_tasks <= HALVES
+    assert runs == {(o, s): 1 for o in grouped for s in range(B)}
+    assert sizes == {FX_ATTNGRP: {4}, FX_MAXGRP: {2}}
