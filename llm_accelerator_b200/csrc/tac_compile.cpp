@@ -2709,7 +2709,8 @@ void Compiler::build_tasks() {
 // while the task before it runs.  A hint never exceeds what the task itself
 // reads; ops without a cheap contiguous estimate get none.
 void Compiler::prefetch_hint(const DevOp& op, Task& t) const {
-  constexpr uint64_t kMaxUnits = 4096;   // 64 KB
+  constexpr uint64_t kMaxUnits = 4096;     // 64 KB
+  constexpr uint64_t kMaxTcUnits = 16384;  // 256 KB of tcgen05 weights
   uint64_t phys = 0, units = 0;
   const uint64_t MN = uint64_t(op.M) * op.N;
   auto elem_bytes = [&](uint32_t kind) -> uint64_t {
@@ -2748,7 +2749,15 @@ void Compiler::prefetch_hint(const DevOp& op, Task& t) const {
         units = op.nbytes / kUnit;
         break;
       case K_MATMUL:
-        if (op.flags & F_TC) break;
+        if (op.flags & F_TC) {
+          // the first column tile's task hints the whole shared weight matrix
+          // [K][N] (every tile's slice), up to kMaxTcUnits
+          if (t.tile == 0 && (op.b & kSharedBit)) {
+            t.pf_phys = op.b;
+            t.pf_units = static_cast<uint32_t>(std::min<uint64_t>(uint64_t(op.K) * op.N / kUnit, kMaxTcUnits));
+          }
+          return;
+        }
         if (!(op.b & kSharedBit)) {   // per-sequence B: the whole matrix (FP16 when quantised on load)
           phys = op.b;
           units = uint64_t(op.K) * op.N * ((op.flags & F_QB) ? 2 : 1) / kUnit;

@@ -2877,10 +2877,14 @@ __global__ void __launch_bounds__(kCtaThreads, 1) exec_kernel(const __grid_const
   const uint32_t vid = hidx() * gridDim.x + blockIdx.x, vgrid = gridDim.x * kHalves;
   for (uint32_t L = 0; L < A.n_levels; ++L) {
     const uint32_t t0 = A.level_off[L], t1 = A.level_off[L + 1];
+    // the half's first task of the next level follows its last task of this
+    // one: its prefetches start a task early
+    const uint32_t tn0 = L + 1 < A.n_levels && A.level_off[L + 1] + vid < A.level_off[L + 2]
+                             ? A.level_off[L + 1] + vid : 0xFFFFFFFFu;
     for (uint32_t ti = t0 + vid; ti < t1; ti += vgrid) {
       const long long c0 = A.task_prof ? clock64() : 0;
-      run_task(A, ti, smem, ti + vgrid < t1 ? ti + vgrid : 0xFFFFFFFFu,
-               ti + 2 * vgrid < t1 ? ti + 2 * vgrid : 0xFFFFFFFFu, tc);
+      run_task(A, ti, smem, ti + vgrid < t1 ? ti + vgrid : tn0,
+               ti + 2 * vgrid < t1 ? ti + 2 * vgrid : (ti + vgrid < t1 ? tn0 : 0xFFFFFFFFu), tc);
       if (A.task_prof && htid() == 0) A.task_prof[ti] = static_cast<uint32_t>(clock64() - c0);
     }
     if (L + 1 < A.n_levels) {

@@ -230,7 +230,8 @@ def _check_prefetch_hints(p, dram_bytes, shared_bytes):
     end = off + units
     assert np.all(end[shared] <= np.uint64(shared_bytes // 16))
     assert np.all(end[~shared] <= np.uint64(block_units))
-    assert np.all(units <= 4096)
+    tc = (ops[hinted["op"]]["flags"] & 8) != 0   # tcgen05 tasks hint their whole weight matrix, up to 256 KB
+    assert np.all(units[~tc] <= 4096) and np.all(units[tc] <= 16384)
     # a per-sequence MATMUL operand B: the hint covers at most B's bytes (FP16 under F_QB)
     for t in hinted:
         op = ops[int(t["op"])]
