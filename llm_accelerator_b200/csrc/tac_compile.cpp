@@ -2556,7 +2556,8 @@ void Compiler::build_tasks() {
           const uint32_t nt = (op.flags & F_TC128) ? (op.N + 127) / 128 : ntile;
           for (uint32_t s = 0; s < B; s += spt)
             for (uint32_t t = 0; t < nt; ++t)
-              per_level[op.level].push_back(Task{i, s, std::min(spt, B - s), t, 0});
+              per_level[op.level].push_back(Task{i, s, std::min(spt, B - s), t,
+                                                 (op.flags & F_TC) ? (kTaskTcMap | op.seg0) : 0u});
         }
         break;
       }

@@ -2674,14 +2674,50 @@ __device__ __forceinline__ void prefetch_l1(const void* p) {
   asm volatile("prefetch.global.L1 [%0];\n" ::"l"(p));
 }
 
+// Brings the plan records task ti reads first into this SM's L1 by loading
+// them with one warp (the values are discarded): the task record and its op
+// record; for a chain, head-group or MAX_ABS-pair task its templates and
+// their ops; for an attention pair the P.V op; for a segment-list op its
+// first segments.  Done while the half waits at the grid barrier, so the
+// task starts on L1 hits rather than a chain of L2 round trips.
+__device__ __forceinline__ uint32_t touch_op(const ExecArgs& A, uint32_t opi, uint32_t sub) {
+  // one word of each 32-byte sector of the 128-byte record (sub = sector)
+  return reinterpret_cast<const uint32_t*>(A.ops + opi)[sub * 8];
+}
+
+__device__ void warm_task(const ExecArgs& A, uint32_t ti, uint32_t lane) {
+  const Task t = A.tasks[ti];
+  uint32_t sink = lane < 4 ? touch_op(A, t.op, lane) : 0u;
+  const DevOp& op = A.ops[t.op];
+  const uint32_t f2 = op.flags2;
+  if (f2 & (FX_CHAINHEAD | FX_ATTNGRP | FX_MAXGRP)) {
+    // lanes 4k .. 4k+3: template k's op record, then its P.V op or first segments
+    const uint32_t k = lane >> 2, sub = lane & 3;
+    if (k < t.aux && k < 8) {
+      const uint32_t xo = A.tasks[t.tile + k].op;
+      sink ^= touch_op(A, xo, sub);
+      const DevOp& x = A.ops[xo];
+      if (x.flags2 & FX_PV) sink ^= touch_op(A, x.seg0, sub);
+      if ((x.flags & F_SEGA) && sub < x.nseg) sink ^= static_cast<uint32_t>(A.segs[x.seg0 + sub].src);
+    }
+  } else {
+    if ((f2 & FX_PV) && lane < 4) sink ^= touch_op(A, op.seg0, lane);
+    const uint32_t first = t.aux & 0xFFFFu;   // a segment-list task's first segment (0 for MAX_ABS)
+    if ((op.flags & F_SEGA) && lane < 16 && first + lane < op.nseg)
+      sink ^= static_cast<uint32_t>(A.segs[op.seg0 + first + lane].src);
+  }
+  asm volatile("" ::"r"(sink));   // keeps the loads
+}
+
 // Grid-wide barrier between levels.  The arrival counter only grows during a
 // launch (the host zeroes it before each launch): a CTA arrives with a release
 // add and waits, with acquire loads, until all gridDim.x CTAs of this level
 // have arrived (target = (level + 1) * gridDim.x).  The same poll watches the
 // fault word, so a fault anywhere stops every CTA at its next barrier.  The
 // wait is bounded: running out raises DF_BARRIER_TIMEOUT.  Meanwhile warp 1 of
-// each half pulls that half's first task of the next level and its op record
-// into L1.
+// each half loads the records that half's first task of the next level reads
+// first into L1 (warm_task), and its lane 0 prefetches the task's tensor
+// maps and hinted operand bytes.
 __device__ __forceinline__ bool grid_barrier(const ExecArgs& A, uint32_t target, uint32_t next_level) {
   __syncthreads();
   __shared__ uint32_t ok;
@@ -2700,12 +2736,17 @@ __device__ __forceinline__ bool grid_barrier(const ExecArgs& A, uint32_t target,
       if (spins > 256) __nanosleep(32);
     }
     ok = st == 0;
-  } else if (htid() == 32 && next_level < A.n_levels) {
+  } else if ((htid() >> 5) == 1 && next_level < A.n_levels) {
     const uint32_t ti = A.level_off[next_level] + hidx() * gridDim.x + blockIdx.x;
-    if (ti < A.level_off[next_level + 1]) {
+    if (ti < A.level_off[next_level + 1]) warm_task(A, ti, htid() & 31);
+    if (htid() == 32 && ti < A.level_off[next_level + 1]) {
       const Task tn = A.tasks[ti];
       prefetch_l1(A.ops + tn.op);
       prefetch_l1(reinterpret_cast<const uint8_t*>(A.ops + tn.op) + sizeof(DevOp) - 1);
+      if (tn.aux & kTaskTcMap) {
+        sm100::prefetch_tmap(A.tmaps + 2 * (tn.aux & ~kTaskTcMap));
+        sm100::prefetch_tmap(A.tmaps + 2 * (tn.aux & ~kTaskTcMap) + 1);
+      }
       prefetch_task_operand(A, tn);
       const uint32_t t2 = ti + gridDim.x * kHalves;
       if (t2 < A.level_off[next_level + 1]) prefetch_l1(A.tasks + t2);
@@ -2715,7 +2756,7 @@ __device__ __forceinline__ bool grid_barrier(const ExecArgs& A, uint32_t target,
   return ok != 0;
 }
 
-// Runs one task on the calling half.  Meanwhile lane 0 of warp 1 pulls the
+// Runs one task on the calling half.  Meanwhile lane 0 of the last warp pulls the
 // next task's op record into L1 (op records never change during a launch)
 // and its hinted operand bytes into L2, and the record of the task after it
 // into L1.
@@ -2726,10 +2767,16 @@ __device__ void run_task(const ExecArgs& A, uint32_t ti, uint8_t* smem, uint32_t
                          TcShared* tc) {
   const Task& t = A.tasks[ti];   // read in place (L1), not copied to local memory
   const DevOp& op = A.ops[t.op];
-  if (htid() == 32 && next_ti != 0xFFFFFFFFu) {
+  // the last warp (not the tcgen05 producer or MMA thread, whose first
+  // copies would wait behind this task-record load) prefetches for the next task
+  if (htid() == kThreads - 32 && next_ti != 0xFFFFFFFFu) {
     const Task tn = A.tasks[next_ti];
     prefetch_l1(A.ops + tn.op);
     prefetch_l1(reinterpret_cast<const uint8_t*>(A.ops + tn.op) + sizeof(DevOp) - 1);
+    if (tn.aux & kTaskTcMap) {   // a tcgen05 task: its tensor maps into the descriptor cache
+      sm100::prefetch_tmap(A.tmaps + 2 * (tn.aux & ~kTaskTcMap));
+      sm100::prefetch_tmap(A.tmaps + 2 * (tn.aux & ~kTaskTcMap) + 1);
+    }
     if (!attn_row_candidate(op)) prefetch_task_operand(A, tn);   // else the attention op prefetches it
     if (next2_ti != 0xFFFFFFFFu) prefetch_l1(A.tasks + next2_ti);
   }

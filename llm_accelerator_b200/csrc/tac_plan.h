@@ -176,6 +176,9 @@ struct Task {
   uint64_t pf_phys;    // prefetch hint: their physical start (sequence seq0)
 };
 static_assert(sizeof(Task) == 32, "Task is a 32-byte record");
+// Task.aux of a tcgen05 MATMUL task: this bit | the op's tensor-map pair index
+// (seg0), so a prefetcher holding only the task record reaches its maps.
+constexpr uint32_t kTaskTcMap = 1u << 31;
 
 // Gathers split their segments into pieces of at most this many units, and a
 // gather task copies a run of whole segments of about this size.
