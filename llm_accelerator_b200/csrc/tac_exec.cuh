@@ -1087,6 +1087,28 @@ static_assert(128 + 4096 + 1024 + kThreads * 4 + 128 + 3 * kPwMaxLeaves * 4 <= k
                   kAttnTabOff + sizeof(AttnDesc) * kAttnGroupMax <= kAttnRowVOff,
               "row attention scratch overlaps its pair table or K rows");
 
+// The int32 dot of a key row read from global memory (every word in flight)
+// with the quantised Q words, the row quantised with sk (QUANT's rule): the
+// keys row attention could not stage in shared memory, kept out of line.
+__device__ __noinline__ int32_t attn_dot_global(const uint4* row, const int32_t* q8w, uint32_t nw, float sk) {
+  uint4 kw[16];
+#pragma unroll
+  for (uint32_t g = 0; g < 16; ++g)
+    if (g < nw) kw[g] = __ldcg(row + g);
+  int32_t acc = 0;
+#pragma unroll
+  for (uint32_t g = 0; g < 16; ++g) {
+    if (g >= nw) break;
+    int8_t q[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q[e] = sat8(__fmul_rn(h2f(h_at(kw[g], e)), sk));
+    const uint2 pk = pack_b(q);
+    acc = __dp4a(static_cast<int32_t>(pk.x), q8w[2 * g], acc);
+    acc = __dp4a(static_cast<int32_t>(pk.y), q8w[2 * g + 1], acc);
+  }
+  return acc;
+}
+
 __device__ __noinline__ void op_attn_rows(const ExecArgs& A, const Task& t, uint32_t npairs, bool grouped,
                                           uint8_t* smem, TcShared* tc, uint32_t next_ti) {
   const uint32_t seq = t.seq0;
@@ -1184,15 +1206,8 @@ __device__ __noinline__ void op_attn_rows(const ExecArgs& A, const Task& t, uint
           acc = dot_word(row[g], g, acc);
           g = g + 1 == nw ? 0u : g + 1;
         }
-      } else {   // past the staged rows: the row from global memory, every word in flight
-        const uint4* row = reinterpret_cast<const uint4*>(D.k + uint64_t(j) * Kd * 2);
-        uint4 kw[16];
-#pragma unroll
-        for (uint32_t g = 0; g < 16; ++g)
-          if (g < nw) kw[g] = __ldcg(row + g);
-#pragma unroll
-        for (uint32_t g = 0; g < 16; ++g)
-          if (g < nw) acc = dot_word(kw[g], g, acc);
+      } else {   // past the staged rows: the row from global memory
+        acc = attn_dot_global(reinterpret_cast<const uint4*>(D.k + uint64_t(j) * Kd * 2), q8w, nw, sk);
       }
       return h2f(f2h(__fmul_rn(__int2float_rn(acc), h2f(scb))));
     };
