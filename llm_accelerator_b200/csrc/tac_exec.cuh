@@ -1308,7 +1308,6 @@ constexpr uint32_t kTcAStage = 128 * 128;
 constexpr uint32_t kTcBStage = 128 * 64;                // 64 columns x 128 K rows
 constexpr uint32_t kTcStage = kTcAStage + kTcBStage;    // a multiple of 1024
 constexpr uint32_t kTcStage128 = kTcAStage + 128 * 128; // 128-column stage
-constexpr uint32_t kTcTileRowDst = 128 * (128 * 2 + 16); // epilogue tile rows, then their store addresses
 constexpr uint32_t kTcCols = 128;                       // TMEM columns per half
 constexpr uint32_t kTcIdesc = sm100::idesc_i8(128, 64, 1);
 constexpr uint32_t kTcIdesc128 = sm100::idesc_i8(128, 128, 1);
@@ -1329,15 +1328,9 @@ __device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr, uint32_t lbo, uint
 // and the activation-scale register of each of the 128 rows.
 constexpr uint32_t kTcEpiBytes = 768;
 
-// One warp's slice of the epilogue: TMEM lanes 32 q .. +31 (rows), columns
-// 32 h .. +31 of the tile.  With a shared-memory tile (FX_DQS + F_NOI32
-// only) the FP16 rows go there, pitch bytes apart, and each row's absorbed
-// store address (FX_DSTORE, else 0) to rowdst; tc_store_tile writes them out.
 __device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp& op, const Task& t, TcShared* tc,
                                                   uint32_t q, uint32_t lane, uint32_t h, uint32_t n0,
-                                                  uint32_t ncols, uint32_t rows, const uint8_t* epi,
-                                                  uint8_t* tile = nullptr, uint32_t pitch = 0,
-                                                  uint64_t* rowdst = nullptr) {
+                                                  uint32_t ncols, uint32_t rows, const uint8_t* epi) {
   const uint32_t M = op.M, N = op.N;
   uint32_t v[32];
   __syncwarp();
@@ -1381,15 +1374,10 @@ __device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp
             x = __fmul_rn(x, s0);
             hh[k] = f2h(__fadd_rn(x, h2f(h_at(b8, k))));
           }
-          if (tile) {
-            *reinterpret_cast<uint4*>(tile + r * pitch + (h * 32 + j) * 2) = pack_h(hh);
-          } else {
-            *reinterpret_cast<uint4*>(O + j) = pack_h(hh);
-            if (Ost) *reinterpret_cast<uint4*>(Ost + j) = pack_h(hh);
-          }
+          *reinterpret_cast<uint4*>(O + j) = pack_h(hh);
+          if (Ost) *reinterpret_cast<uint4*>(Ost + j) = pack_h(hh);
         }
       }
-      if (tile && h == 0) rowdst[r] = reinterpret_cast<uint64_t>(Ost);   // the row's column n0 (or 0)
       if (op.flags & F_NOI32) return;
     }
     const int32_t* C = (op.flags & F_ACCUMULATE)
@@ -1409,23 +1397,6 @@ __device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp
         *reinterpret_cast<int4*>(D + j) = val;
       }
     }
-  }
-}
-
-// Writes a staged FP16 tile out (tc_epilogue_slice with a tile): the whole
-// half, consecutive threads on consecutive 16-byte words of a row, so one
-// store instruction covers a few rows (sequences) instead of one per lane.
-__device__ __noinline__ void tc_store_tile(const ExecArgs& A, const DevOp& op, const Task& t, const uint8_t* tile,
-                                              uint32_t pitch, const uint64_t* rowdst, uint32_t n0, uint32_t ncols,
-                                              uint32_t rows) {
-  const uint32_t M = op.M, N = op.N, upr = ncols / 8;
-  for (uint32_t u = htid(); u < rows * upr; u += kThreads) {
-    const uint32_t r = u / upr, c = u - r * upr;
-    const uint4 w = *reinterpret_cast<const uint4*>(tile + r * pitch + c * 16);
-    const uint32_t seq = t.seq0 + r / M, row = r % M;
-    uint16_t* O = reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(op.dconst), seq)) + uint64_t(row) * N + n0;
-    *reinterpret_cast<uint4*>(O + c * 8) = w;
-    if (rowdst[r]) *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(rowdst[r]) + c * 8) = w;
   }
 }
 
@@ -1568,19 +1539,7 @@ __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, co
   }
   // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31; with 64 columns it
   // takes columns 32 (w / 4) .. +31, with 128 columns two such slices
-  // With the DEQUANT_SCALED vectors staged and no int32 result the FP16 rows
-  // go through shared memory (the stage region, free once the MMAs are done)
-  // and the whole half writes them out row by row.
-  const bool via_tile = epi && (op.flags & F_NOI32) && ncols % 8 == 0;
-  uint8_t* tile = via_tile ? base : nullptr;
-  const uint32_t pitch = tn * 2 + 16;   // rows 16 bytes apart in bank order
-  uint64_t* rowdst = reinterpret_cast<uint64_t*>(base + kTcTileRowDst);
-  for (uint32_t hh = warp >> 2; hh * 32 < tn; hh += 2)
-    tc_epilogue_slice(A, op, t, tc, q, lane, hh, n0, ncols, rows, epi, tile, pitch, rowdst);
-  if (via_tile) {
-    hsync();
-    tc_store_tile(A, op, t, tile, pitch, rowdst, n0, ncols, rows);
-  }
+  for (uint32_t hh = warp >> 2; hh * 32 < tn; hh += 2) tc_epilogue_slice(A, op, t, tc, q, lane, hh, n0, ncols, rows, epi);
   // the next tcgen05 MATMUL overwrites the accumulator only after every warp read it
   sm100::tc_fence_before();
   hsync();
@@ -2941,7 +2900,6 @@ static_assert(kWarps == int(kExecWarps) && kPwScratchBytes == kWarps * 3 * kPwMa
               "FX_PV layout constants disagree with the executor");
 static_assert(kSegTableOff + kMaxSegRuns * 12 <= kExecOpSmem, "segment table exceeds the op shared memory");
 static_assert(2 * kMaxGrpRegion <= kExecOpSmem, "MAX_ABS pair regions exceed the op shared memory");
-static_assert(kTcTileRowDst + 128 * 8 <= kTcStageRegion, "tcgen05 epilogue tile exceeds the stage region");
 static_assert(kSegTableOff + kMaxSegRuns * 13 <= kMaxQStage && kMaxQStage + 16384 * 2 <= kExecOpSmem,
               "MAX_ABS staging overlaps the segment table or exceeds the op shared memory");
 static_assert(kExecOpSmem % 1024 == 0 || kTcSmem <= kExecOpSmem, "half regions must keep the stage alignment slack");
