@@ -1400,6 +1400,61 @@ __device__ __forceinline__ void tc_epilogue_slice(const ExecArgs& A, const DevOp
   }
 }
 
+// The FX_DQS + F_NOI32 slice with its vectors staged and all 32 columns
+// valid: each lane computes its row's 32 FP16 results into the warp's own
+// 2.5 KB of shared memory (scr), and after a warp barrier each store
+// instruction writes 8 rows' 64 bytes (4 lanes a row) instead of 32 rows'
+// 16 bytes, the rows being different sequences.
+__device__ __forceinline__ void tc_epilogue_slice_t(const ExecArgs& A, const DevOp& op, const Task& t, TcShared* tc,
+                                                    uint32_t q, uint32_t lane, uint32_t h, uint32_t n0,
+                                                    uint32_t rows, const uint8_t* epi, uint8_t* scr) {
+  const uint32_t M = op.M, N = op.N;
+  uint32_t v[32];
+  __syncwarp();
+  sm100::tmem_ld32(tc->tmem + ((q * 32) << 16) + h * 32, v);
+  const uint32_t r = q * 32 + lane, col0 = n0 + h * 32;
+  uint64_t ost = 0;   // this row's absorbed store address (FX_DSTORE), else 0
+  if (r < rows) {
+    const uint32_t seq = t.seq0 + r / M, row = r % M;
+    const float s0 = h2f(reinterpret_cast<const uint16_t*>(epi + 512)[r]);
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(epi) + h * 32;
+    const uint16_t* bi = reinterpret_cast<const uint16_t*>(epi + 256) + h * 32;
+    if ((op.flags2 & FX_DSTORE) && row < op.attn_vkl) {
+      const uint64_t addr = A.params[uint64_t(seq) * A.n_params + op.param] + op.attn_qrb +
+                            (uint64_t(row) * N + col0) * 2;
+      if ((addr & 15) || addr + 64 > A.dram_bytes || addr < A.shared_bytes) raise_fault(A, DF_DYN_ADDRESS, t.op, seq);
+      else ost = reinterpret_cast<uint64_t>(dram_ptr(A, addr, seq));
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < 32; j += 8) {
+      const uint4 s8 = *reinterpret_cast<const uint4*>(sc + j);
+      const uint4 b8 = *reinterpret_cast<const uint4*>(bi + j);
+      uint16_t hh[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float x = __fmul_rn(__int2float_rn(int(v[j + k])), h2f(h_at(s8, k)));
+        x = __fmul_rn(x, s0);
+        hh[k] = f2h(__fadd_rn(x, h2f(h_at(b8, k))));
+      }
+      *reinterpret_cast<uint4*>(scr + lane * 80 + j * 2) = pack_h(hh);
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (uint32_t i = 0; i < 4; ++i) {
+    const uint32_t rr = 8 * i + (lane >> 2), c = lane & 3, rg = q * 32 + rr;   // the row and 16-byte word
+    const uint64_t o2 = __shfl_sync(0xffffffffu, ost, rr);
+    if (rg < rows) {
+      const uint4 w = *reinterpret_cast<const uint4*>(scr + rr * 80 + c * 16);
+      const uint32_t seq = t.seq0 + rg / M, row = rg % M;
+      uint16_t* O = reinterpret_cast<uint16_t*>(pptr(A, static_cast<uint64_t>(op.dconst), seq)) + uint64_t(row) * N + col0;
+      *reinterpret_cast<uint4*>(O + c * 8) = w;
+      if (o2) *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(o2) + c * 8) = w;
+    }
+  }
+  __syncwarp();   // the scratch is free for the warp's next slice
+}
+
 // The weight tiles a tcgen05 MATMUL task streams (its B column slice over
 // every K chunk), pulled into L2 by TMA prefetches, and its tensor maps into
 // the descriptor cache; other tasks need nothing here.
@@ -1539,7 +1594,14 @@ __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, co
   }
   // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31; with 64 columns it
   // takes columns 32 (w / 4) .. +31, with 128 columns two such slices
-  for (uint32_t hh = warp >> 2; hh * 32 < tn; hh += 2) tc_epilogue_slice(A, op, t, tc, q, lane, hh, n0, ncols, rows, epi);
+  // (with the DEQUANT_SCALED vectors staged and no int32 result, through the
+  // warp's own scratch in the stage region, free once the MMAs are done)
+  for (uint32_t hh = warp >> 2; hh * 32 < tn; hh += 2) {
+    if (epi && (op.flags & F_NOI32) && hh * 32 + 32 <= ncols)
+      tc_epilogue_slice_t(A, op, t, tc, q, lane, hh, n0, rows, epi, base + warp * 2560);
+    else
+      tc_epilogue_slice(A, op, t, tc, q, lane, hh, n0, ncols, rows, epi);
+  }
   // the next tcgen05 MATMUL overwrites the accumulator only after every warp read it
   sm100::tc_fence_before();
   hsync();
