@@ -2453,8 +2453,11 @@ void Compiler::build_tasks() {
       if (!(op.flags & F_ACCUMULATE) && tc_resident_fits(rows, op.K)) {
         op.flags2 |= FX_TCRES;
         op.q_rows = rows;
-      } else if (op.N >= 128) {
-        op.flags |= F_TC128;
+      } else {
+        if (op.N >= 128) op.flags |= F_TC128;
+        // a K loop through the stage ring is latency-bound: past kTcSplitRows
+        // rows a task takes kTcSplitRows of them (q_rows), twice the tasks
+        if (rows > kTcSplitRows && op.M <= kTcSplitRows && kTcSplitRows % op.M == 0) op.q_rows = kTcSplitRows;
       }
       op.seg0 = P->n_tc++;
       op.nseg = 0;
@@ -2552,7 +2555,7 @@ void Compiler::build_tasks() {
           const uint32_t mchunks = (op.M + 127) / 128;
           per_seq(i, ntile * mchunks);
         } else {
-          const uint32_t spt = std::max<uint32_t>(1, 128 / op.M);
+          const uint32_t spt = ((op.flags & F_TC) && op.q_rows) ? op.q_rows / op.M : std::max<uint32_t>(1, 128 / op.M);
           const uint32_t nt = (op.flags & F_TC128) ? (op.N + 127) / 128 : ntile;
           for (uint32_t s = 0; s < B; s += spt)
             for (uint32_t t = 0; t < nt; ++t)

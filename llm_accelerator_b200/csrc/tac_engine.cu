@@ -151,8 +151,8 @@ int ensure_maps(tac_engine* e, tac_program* p, tac_fault* f) {
     const uint8_t* b = static_cast<const uint8_t*>(e->d_shared) + ((op.b & ~kSharedBit) << 4);
     const cuuint64_t adims[3] = {op.K, op.M, cuuint64_t(e->batch)};
     const cuuint64_t astr[2] = {op.K, e->seq_stride};
-    // resident tasks load their sequences' rows only (q_rows, a multiple of 8)
-    const cuuint32_t abox[3] = {128, op.M, (op.flags2 & FX_TCRES) ? op.q_rows / op.M : 128 / op.M};
+    // resident and split tasks load their sequences' rows only (q_rows, a multiple of 8)
+    const cuuint32_t abox[3] = {128, op.M, op.q_rows ? op.q_rows / op.M : 128 / op.M};
     const bool wide = (op.flags & F_TC128) != 0;   // 128-column tiles: 128-byte swizzle, else 64
     const cuuint64_t bdims[2] = {op.N, op.K};
     const cuuint64_t bstr[1] = {op.N};

@@ -1548,7 +1548,7 @@ __device__ __noinline__ void op_matmul_tc(const ExecArgs& A, const DevOp& op, co
   } else if (htid() == 32) {
     // producer (warp 1): TMA loads; a stage is refilled once the MMAs of the
     // chunk before it in that stage have completed
-    const uint32_t bytes = (128 / M) * M * 128 + tn * 128;
+    const uint32_t bytes = (op.q_rows ? op.q_rows : (128 / M) * M) * 128 + tn * 128;   // the A box's rows
     bool ok = true;
     sm100::fence_proxy_async();   // A was written by generic stores in earlier levels
     for (uint32_t c = 0; c < nchunks; ++c) {

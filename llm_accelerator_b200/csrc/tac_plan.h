@@ -207,6 +207,7 @@ TAC_HD constexpr bool tc_rows_ok(uint32_t M) { return M > 0 && M < 128 && (M % 1
 // (128 K rows x 64 columns); the MMA of the last chunk reads 128 A rows from
 // its box on, which must stay inside the stage region.
 constexpr uint32_t kTcStageRegion = 73728;
+constexpr uint32_t kTcSplitRows = 32;   // rows of a ring-fed (non-resident) tcgen05 task with more sequences
 TAC_HD constexpr bool tc_resident_fits(uint32_t rows, uint32_t K) {
   const uint32_t nchunks = (K + 127) / 128;
   return rows % 8 == 0 && rows <= 128 && nchunks * (rows * 128 + 8192) <= kTcStageRegion &&
